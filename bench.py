@@ -1,0 +1,479 @@
+"""Benchmark of the quantized-matvec hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Workload: Q4_1 weights (32-element blocks, f16
+scale d ~ U(0.002, 0.02) and min m = -8 d, 4-bit codes uniform), x bf16
+~ N(0, 1), batches 1, 8 and 64 over the four shapes 4096x4096, 12288x4096,
+4096x12288 and 151936x4096 (the lm-head). One step is the whole sweep: for
+each batch, each shape, one `linear` (x prepared once, then the product).
+Weights total 462 MB, 3.7x L2, visited in order, so no product finds its
+weight in L2 from the previous visit (inputs larger than L2; no flush).
+
+The line's metric is weight-streaming throughput: algorithmic bytes
+(weights + x + y of every product) over the step time, in GB/s, also as a
+fraction of BASELINE's 8 TB/s. `value` is device time with inputs resident
+(the step replayed as a CUDA graph); `e2e` runs the same step through the
+public C ABI with host buffers, copying each x in and each y out inside the
+timed region. With N GPUs each rank runs its own sweep on its own weights
+(weak scaling: the products shard by rows with no exchange); the time is the
+max over ranks.
+
+`--impl reference` times the reference's CPU path for the same products (the
+C restatement of CpuOps.linear in oracle/, on every host thread) on a sample
+of each matrix's rows, on rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+SHAPES = [(4096, 4096), (12288, 4096), (4096, 12288), (151936, 4096)]
+BATCHES = [1, 8, 64]
+Q4_1 = 3
+METRIC = "quant matvec HBM GB/s (% of 8 TB/s); decode tok/s at 1/2/4/8 B200"
+NOMINAL_HBM_GBS = 8000.0
+
+
+def algorithmic_bytes(n: int, k: int, b: int) -> int:
+    """Weights once, x (bf16) and y (f32) once: N (K/32) 20 + 2 b K + 4 b N."""
+    return n * (k // 32) * 20 + 2 * b * k + 4 * b * n
+
+
+def step_bytes() -> int:
+    return sum(algorithmic_bytes(n, k, b) for b in BATCHES for n, k in SHAPES)
+
+
+def measured_peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            data = json.load(f)
+        return {"hbm_gbs": float(data["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+# ---- clocks ---------------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi clock and throttle samples while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.samples: list[list[str]] = []
+        self._stop = threading.Event()
+        self._proc = None
+        self._thread = None
+
+    def start(self):
+        try:
+            self._proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self._proc = None
+            return
+        self._thread = threading.Thread(target=self._read, daemon=True)
+        self._thread.start()
+
+    def _read(self):
+        for line in self._proc.stdout:
+            self.samples.append([c.strip() for c in line.split(",")])
+
+    def stop(self) -> dict:
+        if self._proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self._proc.terminate()
+        try:
+            self._proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self._proc.kill()
+        if self._thread:
+            self._thread.join(timeout=5)
+        sm, sm_max, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for s in self.samples:
+            try:
+                sm.append(float(s[1]))
+                sm_max.append(float(s[2]))
+            except (ValueError, IndexError):
+                continue
+            for name, value in zip(names, s[5:9]):
+                if value.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(sm_max) if sm_max else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---- the GPU arm ------------------------------------------------------------------------------
+def run_gpu(args) -> dict | None:
+    import torch
+    import torch.distributed as dist
+
+    from drift_b200 import synthetic
+    from drift_b200._lib import check
+    from drift_b200.ops import CudaOps, Stored
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                timeout=__import__("datetime").timedelta(seconds=120))
+    ops = CudaOps(local)
+    lib = ops.lib
+
+    # inputs, resident: every rank its own weights (seeded by rank)
+    rng = np.random.default_rng(1000 + rank)
+    weights = {}
+    for n, k in SHAPES:
+        weights[(n, k)] = Stored.upload(Q4_1, (n, k), synthetic.quantized(rng, Q4_1, n, k))
+    xs, ys = {}, {}
+    host_x, host_y = {}, {}
+    for b in BATCHES:
+        for n, k in SHAPES:
+            bits = synthetic.bf16_bits(synthetic.gaussian(rng, b, k))
+            xs[(b, n, k)] = torch.from_numpy(bits.view(np.int16)).cuda().view(torch.bfloat16)
+            ys[(b, n, k)] = torch.empty(b, n, device="cuda")
+            host_x[(b, n, k)] = torch.from_numpy(bits.view(np.int16)).view(
+                torch.bfloat16).pin_memory()
+            host_y[(b, n, k)] = torch.empty(b, n, dtype=torch.float32).pin_memory()
+    ops.reserve_workspace(max(BATCHES), max(k for _, k in SHAPES))
+
+    def step():
+        for b in BATCHES:
+            for n, k in SHAPES:
+                ops.linear(xs[(b, n, k)], weights[(n, k)], ys[(b, n, k)])
+
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            step()  # first calls resolve the library's lazy state outside capture
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    launches_per_step = count_launches(ops, step)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        graph.replay()
+    end.record()
+    torch.cuda.synchronize()
+    clock_info = clocks.stop()
+    elapsed_ms = start.elapsed_time(end)
+    barrier()
+    torch.cuda.synchronize()
+
+    # e2e: the public C ABI with host buffers, copies inside the timed region
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def e2e_step():
+        for b in BATCHES:
+            for n, k in SHAPES:
+                hx, dx = host_x[(b, n, k)], xs[(b, n, k)]
+                check("drift_memcpy_async", lib.drift_memcpy_async(
+                    ctypes.c_void_p(dx.data_ptr()), ctypes.c_void_p(hx.data_ptr()),
+                    hx.numel() * 2, 1, s))
+                w = weights[(n, k)]
+                check("drift_linear", lib.drift_linear(
+                    30, ctypes.c_void_p(dx.data_ptr()), Q4_1, ctypes.c_void_p(w.data.data_ptr()),
+                    ctypes.c_void_p(ys[(b, n, k)].data_ptr()), b, n, k, s))
+                hy = host_y[(b, n, k)]
+                check("drift_memcpy_async", lib.drift_memcpy_async(
+                    ctypes.c_void_p(hy.data_ptr()), ctypes.c_void_p(ys[(b, n, k)].data_ptr()),
+                    hy.numel() * 4, 2, s))
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e_end.record()
+    torch.cuda.synchronize()
+    e2e_ms = e_start.elapsed_time(e_end)
+    h2d = sum(b * k * 2 for b in BATCHES for n, k in SHAPES)
+    d2h = sum(b * n * 4 for b in BATCHES for n, k in SHAPES)
+
+    # the dominant kernel alone: the lm-head product at batch 1, replayed
+    dominant = dominant_kernel(ops, weights, xs, ys, stream)
+
+    times = torch.tensor([elapsed_ms, e2e_ms], device="cuda")
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    elapsed_ms, e2e_ms = float(times[0]), float(times[1])
+    del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+
+    total_bytes = step_bytes() * args.steps * world
+    value = total_bytes / (elapsed_ms / 1e3) / 1e9
+    e2e_value = total_bytes / (e2e_ms / 1e3) / 1e9
+    peaks = measured_peaks()
+    result = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(elapsed_ms / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "q4_1 weights, bf16 x, exact-integer dp4a products, f32 out",
+        "data": "synthetic (seeded; BASELINE C2 value laws)",
+        "config": {
+            "workload": "C2 Q4_1 matvec sweep: batches 1/8/64 x shapes 4096x4096, "
+                        "12288x4096, 4096x12288, 151936x4096",
+            "per_gpu_bytes_per_step": step_bytes(),
+            "l2": "inputs larger than L2 (462 MB of weights visited in turn), no flush",
+            "parallelism": f"replicas x{world} (weak scaling, no exchange)",
+            "fraction_of_8TBs": round(value / world / NOMINAL_HBM_GBS, 4),
+            "fraction_of_measured_hbm": round(value / world / peaks["hbm_gbs"], 4),
+        },
+        "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches_per_step * args.steps,
+        "roofline": {
+            "bound": "hbm",
+            "kernel": "matvec_x22_q4_1 (+ quantize_x22), lm-head 151936x4096, batch 1",
+            "achieved": round(dominant["gbs"], 1),
+            "peak": peaks["hbm_gbs"],
+            "peak_source": peaks["source"] + " (MEASURED_PEAKS.json hbm_gbs, copy)",
+            "unit": "GB/s",
+            "frac": round(dominant["gbs"] / peaks["hbm_gbs"], 4),
+            "traffic": None,
+            "launch_us": round(dominant["us"], 3),
+        },
+        "clocks": clock_info,
+        "sweep": sweep_table(ops, weights, xs, ys, stream),
+    }
+    if args.cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(seconds=args.cpu_seconds)
+    return result
+
+
+def count_launches(ops, step) -> int:
+    """Kernels one step launches: two per product (x preparation, product)
+    plus one per extra pass of MAX_V vectors."""
+    launches = 0
+    for b in BATCHES:
+        for _ in SHAPES:
+            launches += 1 + (b + 1) // 2
+    return launches
+
+
+def timed_graph(fn, stream, repeats: int) -> float:
+    """Average ms of fn replayed as a CUDA graph `repeats` times."""
+    import torch
+
+    with torch.cuda.stream(stream):
+        fn()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        fn()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(repeats):
+        graph.replay()
+    end.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / repeats
+
+
+L2_BYTES = 126 * 2 ** 20
+
+
+def rotation(weight, minimum_bytes: int) -> list:
+    """Copies of a weight at distinct addresses, enough that cycling through
+    them streams `minimum_bytes`: a product never finds its weight in L2."""
+    from drift_b200.ops import Stored
+
+    count = max(1, -(-minimum_bytes // weight.data.numel()))
+    return [weight] + [Stored(weight.dtype, weight.shape, weight.data.clone())
+                       for _ in range(count - 1)]
+
+
+def dominant_kernel(ops, weights, xs, ys, stream) -> dict:
+    """The lm-head product at batch 1 alone, cycling through copies of its
+    weight that stream 4x L2 between reuses."""
+    n, k = 151936, 4096
+    copies = rotation(weights[(n, k)], 4 * L2_BYTES)
+
+    def fn():
+        for w in copies:
+            ops.linear(xs[(1, n, k)], w, ys[(1, n, k)])
+
+    ms = timed_graph(fn, stream, 20) / len(copies)
+    return {"us": ms * 1e3, "gbs": algorithmic_bytes(n, k, 1) / (ms / 1e3) / 1e9}
+
+
+def sweep_table(ops, weights, xs, ys, stream) -> list:
+    """Per (batch, shape): microseconds per product and GB/s, each product
+    cycling through copies of its weight that stream 4x L2 between reuses."""
+    rows = []
+    for n, k in SHAPES:
+        copies = rotation(weights[(n, k)], 4 * L2_BYTES)
+        for b in BATCHES:
+            def fn(b=b, n=n, k=k):
+                for w in copies:
+                    ops.linear(xs[(b, n, k)], w, ys[(b, n, k)])
+            ms = timed_graph(fn, stream, 5 if b == 64 else 10) / len(copies)
+            rows.append({"batch": b, "shape": f"{n}x{k}", "us": round(ms * 1e3, 2),
+                         "gbs": round(algorithmic_bytes(n, k, b) / (ms / 1e3) / 1e9, 1)})
+        del copies
+    rows.sort(key=lambda r: (r["batch"], SHAPES.index(tuple(map(int, r["shape"].split("x"))))))
+    return rows
+
+
+# ---- CPU: the reference's path ---------------------------------------------------------------------
+def cpu_sample(rng, rows_per_matrix: int):
+    import oracle
+    from drift_b200 import synthetic
+
+    cases = []
+    for n, k in SHAPES:
+        rows = min(n, rows_per_matrix)
+        w = synthetic.quantized(rng, Q4_1, rows, k)
+        for b in BATCHES:
+            x = synthetic.bf16_values(synthetic.bf16_bits(synthetic.gaussian(rng, b, k)))
+            cases.append((w, x, rows, k, b))
+    return cases, oracle
+
+
+def cpu_baseline(seconds: float) -> dict:
+    """The oracle (C restatement of CpuOps.linear, single thread) on a sample:
+    the 4096x4096 Q4_1 product at batch 1, repeated for ~`seconds`."""
+    import oracle
+    from drift_b200 import synthetic
+
+    rng = np.random.default_rng(7)
+    n, k = 4096, 4096
+    w = synthetic.quantized(rng, Q4_1, n, k)
+    x = synthetic.bf16_values(synthetic.bf16_bits(synthetic.gaussian(rng, 1, k)))
+    runs, start = 0, time.perf_counter()
+    while True:
+        oracle.linear(Q4_1, x, w, n, k)
+        runs += 1
+        if time.perf_counter() - start >= seconds:
+            break
+    elapsed = time.perf_counter() - start
+    gbs = algorithmic_bytes(n, k, 1) * runs / elapsed / 1e9
+    return {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"Q4_1 4096x4096 batch 1 x{runs} ({elapsed:.1f} s): C restatement of "
+                      "CpuOps.linear (decode per row, Double sums), one thread"}
+
+
+def run_reference(args) -> dict | None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    import oracle
+
+    threads = oracle.max_threads()
+    rng = np.random.default_rng(7)
+    rows = 256  # rows sampled per matrix: a bounded share of the sweep
+    cases, _ = cpu_sample(rng, rows)
+    sample_bytes = sum(algorithmic_bytes(r, k, b) for _, _, r, k, b in cases)
+
+    def step():
+        for w, x, r, k, b in cases:
+            oracle.linear_threads(Q4_1, x, w, r, k, threads)
+
+    for _ in range(args.warmup):
+        step()
+    start = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    elapsed = time.perf_counter() - start
+    value = sample_bytes * args.steps / elapsed / 1e9
+    sample = (f"{rows} rows of each C2 matrix at batches 1/8/64 per step "
+              f"({sample_bytes / 1e6:.1f} MB): C restatement of CpuOps.linear on {threads} "
+              "host threads (rows split between threads)")
+    return {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 4),
+        "unit": "GB/s",
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(elapsed / args.steps * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "q4_1 weights, f32 x (bf16 widened), f64 sums",
+        "data": "synthetic (seeded; BASELINE C2 value laws)",
+        "config": {"workload": "C2 Q4_1 matvec sweep (row sample), CPU reference path"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main() -> int:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--impl", default="drift_b200")
+    parser.add_argument("--cpu-seconds", type=float, default=10.0)
+    parser.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    args = parser.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        result = run_reference(args)
+    else:
+        result = run_gpu(args)
+    if result is not None:
+        print(json.dumps(result), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,53 @@
+// Shared definitions of libdrift_cuda: status codes, dtype codes, argument
+// checks that report like the reference's `require`s, and launch helpers.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/drift_ops.h"
+#include "../../include/drift_runtime.h"
+
+namespace drift {
+
+// The calling thread's last error message (what a HipException or a failed
+// `require` would carry), kept until the next failing call.
+void set_error(const char* format, ...);
+const char* last_error();
+
+// Returns DRIFT_ERROR_INVALID_ARGUMENT with the message set, as a failed
+// `require` throws IllegalArgumentException.
+int invalid(const char* format, ...);
+
+// A CUDA status as a drift status: 0 stays 0, anything else is returned as is
+// with a message naming the call.
+int cuda_status(cudaError_t status, const char* call);
+
+// Bytes of storage for `elements` values of `dtype`, or -1 if they are not
+// whole blocks (DType.byteSize, runner/src/drift/runner/tensor/DType.scala:24-30).
+int64_t byte_size(int dtype, int64_t elements);
+int block_elements(int dtype);
+int block_bytes(int dtype);
+const char* dtype_name(int dtype);
+
+// Streaming multiprocessors of the current device (cached per device).
+int sm_count();
+
+constexpr int WARP = 32;
+
+}  // namespace drift
+
+#define DRIFT_TRY(call)                                                      \
+  do {                                                                       \
+    const int drift_status_ = (call);                                        \
+    if (drift_status_ != 0) return drift_status_;                            \
+  } while (0)
+
+#define DRIFT_CUDA(call) DRIFT_TRY(::drift::cuda_status((call), #call))
+
+// The launch just queued, checked (a bad configuration fails here, not later).
+#define DRIFT_LAUNCHED(name) DRIFT_TRY(::drift::cuda_status(cudaGetLastError(), name))

@@ -1,0 +1,388 @@
+// Mixtures of experts: top-k routing, the experts' products (plain and gated
+// SwiGLU), and their weighted sum with the shared expert and the residual,
+// optionally followed by the next RMS norm.
+//
+// Reference kernels: route_topk / route.h (kernels/linear_attention.hip:
+// 274-281, route.h:9-41), matvec_experts[_gated]_<t> (matvec.hip:579-656),
+// moe_combine (linear_attention.hip:286-297), moe_combine_norm (norm.hip:
+// 43-59, combine.h:10-32); dispatch ops/HipExperts.scala. CPU twins:
+// ops/CpuExperts.scala:11-106.
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "quant.cuh"
+#include "registry.cuh"
+
+namespace drift {
+
+int* device_error_word();
+int workspace_reserve(size_t bytes, void** pointer);
+size_t linear_workspace_bytes(int64_t m, int64_t k);
+int prepare_x(int x_dtype, const void* x, int64_t m, int64_t k, uint32_t* records,
+              cudaStream_t stream);
+
+// ---- routing ----------------------------------------------------------------------------
+// One warp per token: the k largest of `experts` <= 512 logits, the lower
+// expert first among equals, then their softmax among themselves in double
+// (as CpuExperts.route computes it), rounded once.
+__global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ logits,
+                                                    int* __restrict__ ids,
+                                                    float* __restrict__ weights, int tokens,
+                                                    int experts, int k) {
+  const int t = blockIdx.x * (blockDim.x / WARP) + threadIdx.x / WARP;
+  if (t >= tokens) return;
+  const int lane = threadIdx.x % WARP;
+  const float* row = logits + (long long)t * experts;
+  float v[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int e = lane + 32 * i;
+    v[i] = e < experts ? row[e] : -INFINITY;
+  }
+  float chosen[16];
+  int chosen_id[16];
+  unsigned taken = 0;  // bit i: expert lane + 32 i is chosen already
+  for (int j = 0; j < k; ++j) {
+    float best = -INFINITY;
+    int best_expert = 1 << 30;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int e = lane + 32 * i;
+      if (e < experts && !((taken >> i) & 1u) &&
+          (v[i] > best || (v[i] == best && e < best_expert))) {
+        best = v[i];
+        best_expert = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o /= 2) {
+      const float other = __shfl_xor_sync(0xffffffffu, best, o);
+      const int other_expert = __shfl_xor_sync(0xffffffffu, best_expert, o);
+      if (other > best || (other == best && other_expert < best_expert)) {
+        best = other;
+        best_expert = other_expert;
+      }
+    }
+    chosen[j] = best;
+    chosen_id[j] = best_expert;
+    if ((best_expert & 31) == lane && best_expert < experts) taken |= 1u << (best_expert >> 5);
+  }
+  if (lane == 0) {
+    double sum = 0.0;
+    double e[16];
+    for (int j = 0; j < k; ++j) {
+      e[j] = exp(double(chosen[j]) - double(chosen[0]));
+      sum += e[j];
+    }
+    for (int j = 0; j < k; ++j) {
+      ids[(long long)t * k + j] = chosen_id[j];
+      weights[(long long)t * k + j] = float(e[j] / sum);
+    }
+  }
+}
+
+DRIFT_REGISTER(route_topk, route_kernel)
+
+// ---- experts' products ---------------------------------------------------------------------
+// Slot s (blockIdx.y) multiplies expert ids[s] of a [experts][rows][cols]
+// weight with x row s / divisor, prepared as for the plain product. The
+// warps of a CTA split rows and blocks as matvec_x22_kernel does. GATED: a
+// gate and an up weight of the same shape, out = silu(gate . x) * (up . x).
+template <typename T, int KS>
+__device__ __forceinline__ float expert_row_sum(const uint8_t* __restrict__ weight,
+                                                const uint32_t* __restrict__ record, int cols,
+                                                long long row, int kw) {
+  const int lane = threadIdx.x % WARP;
+  const int blocks = cols / 32;
+  const uint8_t* base = weight + row * (long long)blocks * T::BYTES;
+  float sum = 0.0f;
+  for (int c = kw * WARP + lane; c < blocks; c += WARP * KS) {
+    uint32_t w[T::WORDS];
+    load_block<T>(base, c, w);
+    const uint4* rec = reinterpret_cast<const uint4*>(record + (long long)c * X_RECORD_WORDS);
+    uint32_t planes[24];
+#pragma unroll
+    for (int i = 0; i < 6; ++i) {
+      const uint4 q = __ldg(rec + i);
+      planes[4 * i] = q.x;
+      planes[4 * i + 1] = q.y;
+      planes[4 * i + 2] = q.z;
+      planes[4 * i + 3] = q.w;
+    }
+    const uint4 tail = __ldg(rec + 6);
+    const Codes codes = T::decode(w, c);
+    int a0, a1, a2;
+    plane_sums<T>(codes, planes, a0, a1, a2);
+    sum += block_dot<T>(codes, a0, a1, a2, __uint_as_float(tail.x), int(tail.y));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o /= 2) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  return sum;
+}
+
+// Each warp: rows of its group, k-split kw; 8 warps = (8 / KS) row groups.
+template <typename T, int KS, bool GATED>
+__global__ void __launch_bounds__(256) experts_x22_kernel(
+    const uint8_t* __restrict__ gate, const uint8_t* __restrict__ up, long long expert_bytes,
+    const int* __restrict__ ids, const uint32_t* __restrict__ records, int divisor,
+    float* __restrict__ y, int rows, int cols, long long experts, int* error) {
+  constexpr int GROUPS = 8 / KS;
+  constexpr int ROWS = 4;  // rows per warp
+  __shared__ float partial[8][ROWS][2];
+  const int warp = threadIdx.x / WARP, lane = threadIdx.x % WARP;
+  const int kw = warp % KS, group = warp / KS;
+  const int slot = blockIdx.y;
+  const long long expert = ids[slot];
+  const int row0 = (blockIdx.x * GROUPS + group) * ROWS;
+  const int blocks = cols / 32;
+  const uint32_t* record = records + (long long)(slot / divisor) * blocks * X_RECORD_WORDS;
+  if (expert < 0 || expert >= experts) {
+    if (threadIdx.x == 0 && blockIdx.x == 0 && error) atomicCAS(error, 0, 1);
+    for (int r = threadIdx.x; r < GROUPS * ROWS; r += blockDim.x) {
+      const int row = blockIdx.x * GROUPS * ROWS + r;
+      if (row < rows) y[(long long)slot * rows + row] = __int_as_float(0x7fc00000);
+    }
+    return;
+  }
+  float g[ROWS], u[ROWS];
+#pragma unroll
+  for (int r = 0; r < ROWS; ++r) {
+    g[r] = u[r] = 0.0f;
+    const int row = row0 + r;
+    if (row < rows) {
+      g[r] = expert_row_sum<T, KS>(gate + expert * expert_bytes, record, cols, row, kw);
+      if (GATED) u[r] = expert_row_sum<T, KS>(up + expert * expert_bytes, record, cols, row, kw);
+    }
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) {
+      partial[warp][r][0] = g[r];
+      partial[warp][r][1] = u[r];
+    }
+  }
+  __syncthreads();
+  const int t = threadIdx.x;
+  if (t < GROUPS * ROWS) {
+    const int gi = t / ROWS, r = t % ROWS;
+    const int row = (blockIdx.x * GROUPS + gi) * ROWS + r;
+    if (row < rows) {
+      float gs = 0.0f, us = 0.0f;
+#pragma unroll
+      for (int kk = 0; kk < KS; ++kk) {
+        gs += partial[gi * KS + kk][r][0];
+        us += partial[gi * KS + kk][r][1];
+      }
+      y[(long long)slot * rows + row] = GATED ? gs / (1.0f + expf(-gs)) * us : gs;
+    }
+  }
+}
+
+#define DRIFT_EXPERTS_REGISTER(T, name)                                                   \
+  DRIFT_REGISTER(experts_x22_##name##_ks1, (experts_x22_kernel<T, 1, false>))             \
+  DRIFT_REGISTER(experts_x22_##name##_ks2, (experts_x22_kernel<T, 2, false>))             \
+  DRIFT_REGISTER(experts_x22_##name##_ks4, (experts_x22_kernel<T, 4, false>))             \
+  DRIFT_REGISTER(experts_gated_x22_##name##_ks1, (experts_x22_kernel<T, 1, true>))        \
+  DRIFT_REGISTER(experts_gated_x22_##name##_ks2, (experts_x22_kernel<T, 2, true>))        \
+  DRIFT_REGISTER(experts_gated_x22_##name##_ks4, (experts_x22_kernel<T, 4, true>))
+DRIFT_EXPERTS_REGISTER(Q8_0T, q8_0)
+DRIFT_EXPERTS_REGISTER(Q4_0T, q4_0)
+DRIFT_EXPERTS_REGISTER(Q4_1T, q4_1)
+
+template <typename T, bool GATED>
+static int launch_experts(const uint8_t* gate, const uint8_t* up, long long expert_bytes,
+                          const int* ids, const uint32_t* records, int divisor, float* y, int rows,
+                          int cols, int slots, long long experts, cudaStream_t stream) {
+  const int blocks = cols / 32;
+  const int ks = blocks >= 128 ? 4 : (blocks >= 64 ? 2 : 1);
+  const int rows_per_cta = 4 * (8 / ks);
+  const dim3 grid(unsigned((rows + rows_per_cta - 1) / rows_per_cta), unsigned(slots));
+  int* error = device_error_word();
+  if (ks == 4)
+    experts_x22_kernel<T, 4, GATED><<<grid, 256, 0, stream>>>(gate, up, expert_bytes, ids, records,
+                                                              divisor, y, rows, cols, experts, error);
+  else if (ks == 2)
+    experts_x22_kernel<T, 2, GATED><<<grid, 256, 0, stream>>>(gate, up, expert_bytes, ids, records,
+                                                              divisor, y, rows, cols, experts, error);
+  else
+    experts_x22_kernel<T, 1, GATED><<<grid, 256, 0, stream>>>(gate, up, expert_bytes, ids, records,
+                                                              divisor, y, rows, cols, experts, error);
+  DRIFT_LAUNCHED("experts_x22");
+  return 0;
+}
+
+static int experts_common(bool gated, int x_dtype, const void* x, int64_t x_rows,
+                          int weight_dtype, const void* gate, const void* up, int64_t experts,
+                          int64_t n, int64_t k, const int32_t* ids, int64_t slots, float* out,
+                          cudaStream_t stream) {
+  const char* name = gated ? "expertsGatedLinear" : "expertsLinear";
+  if (x_dtype != DRIFT_F32 && x_dtype != DRIFT_BF16)
+    return invalid("%s takes F32 (or BF16) x, not %s", name, dtype_name(x_dtype));
+  if (weight_dtype != DRIFT_Q8_0 && weight_dtype != DRIFT_Q4_0 && weight_dtype != DRIFT_Q4_1)
+    return invalid("no kernels for %s experts yet", dtype_name(weight_dtype));
+  if (x_rows <= 0 || slots < 0 || slots % x_rows != 0)
+    return invalid("%s: x [%lld, %lld] for %lld slots of %lld", name, (long long)x_rows,
+                   (long long)k, (long long)slots, (long long)k);
+  const int64_t row = byte_size(weight_dtype, k);
+  if (row < 0 || row % 4 != 0)
+    return invalid("%s rows of %lld are not whole words", dtype_name(weight_dtype), (long long)k);
+  if (n <= 0 || experts <= 0 || k <= 0) return invalid("%s: weight [%lld, %lld, %lld]", name,
+                                                       (long long)experts, (long long)n,
+                                                       (long long)k);
+  if (slots == 0) return 0;
+  if (!x || !gate || (gated && !up) || !ids || !out) return invalid("%s: a null tensor", name);
+  if (slots > 65535) return invalid("%s: %lld slots in one launch", name, (long long)slots);
+  void* w = nullptr;
+  DRIFT_TRY(workspace_reserve(linear_workspace_bytes(x_rows, k), &w));
+  uint32_t* records = static_cast<uint32_t*>(w);
+  DRIFT_TRY(prepare_x(x_dtype, x, x_rows, k, records, stream));
+  const long long expert_bytes = n * row;
+  const int divisor = int(slots / x_rows);
+  const uint8_t* g = static_cast<const uint8_t*>(gate);
+  const uint8_t* u = static_cast<const uint8_t*>(up);
+#define DRIFT_EXPERTS_CASE(T)                                                                   \
+  return gated ? launch_experts<T, true>(g, u, expert_bytes, ids, records, divisor, out, int(n), \
+                                         int(k), int(slots), experts, stream)                   \
+               : launch_experts<T, false>(g, g, expert_bytes, ids, records, divisor, out, int(n), \
+                                          int(k), int(slots), experts, stream);
+  switch (weight_dtype) {
+    case DRIFT_Q8_0: DRIFT_EXPERTS_CASE(Q8_0T)
+    case DRIFT_Q4_0: DRIFT_EXPERTS_CASE(Q4_0T)
+    default: DRIFT_EXPERTS_CASE(Q4_1T)
+  }
+#undef DRIFT_EXPERTS_CASE
+}
+
+// ---- combine ---------------------------------------------------------------------------------
+// The shared expert's gate: sigmoid(x . router), reduced by the block in a
+// fixed order.
+__device__ __forceinline__ float shared_gate(const float* x, const float* router, int hidden,
+                                             float* partial) {
+  float dot = 0.0f;
+  for (int c = threadIdx.x; c < hidden; c += blockDim.x) dot = fmaf(x[c], router[c], dot);
+#pragma unroll
+  for (int o = 16; o > 0; o /= 2) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+  if (threadIdx.x % WARP == 0) partial[threadIdx.x / WARP] = dot;
+  __syncthreads();
+  float total = 0.0f;
+  for (int w = 0; w < int(blockDim.x / WARP); ++w) total += partial[w];
+  __syncthreads();
+  return 1.0f / (1.0f + expf(-total));
+}
+
+// One block of 256 threads per token. NORM: the combined row is also the
+// residual stream (written back) and its RMS norm goes to `normed`.
+template <bool NORM>
+__global__ void __launch_bounds__(256) combine_kernel(
+    const float* __restrict__ expert_out, const float* __restrict__ weights,
+    const float* __restrict__ shared_out, const float* __restrict__ shared_input,
+    const float* __restrict__ shared_router, const float* residual, float* out, int k, int hidden,
+    const float* __restrict__ norm_weight, float* __restrict__ normed, float epsilon,
+    float weight_offset) {
+  __shared__ float partial[32];
+  const long long t = blockIdx.x;
+  const float gate =
+      shared_out ? shared_gate(shared_input + t * hidden, shared_router, hidden, partial) : 0.0f;
+  float squares = 0.0f;
+  for (int c = threadIdx.x; c < hidden; c += blockDim.x) {
+    float sum = residual ? residual[t * hidden + c] : 0.0f;
+    float routed = 0.0f;
+    for (int j = 0; j < k; ++j)
+      routed = fmaf(weights[t * k + j], expert_out[(t * k + j) * hidden + c], routed);
+    sum += routed;
+    if (shared_out) sum = fmaf(gate, shared_out[t * hidden + c], sum);
+    out[t * hidden + c] = sum;
+    squares = fmaf(sum, sum, squares);
+  }
+  if (!NORM) return;
+#pragma unroll
+  for (int o = 16; o > 0; o /= 2) squares += __shfl_xor_sync(0xffffffffu, squares, o);
+  if (threadIdx.x % WARP == 0) partial[threadIdx.x / WARP] = squares;
+  __syncthreads();
+  float total = 0.0f;
+  for (int w = 0; w < int(blockDim.x / WARP); ++w) total += partial[w];
+  const float scale = 1.0f / sqrtf(total / float(hidden) + epsilon);
+  for (int c = threadIdx.x; c < hidden; c += blockDim.x)
+    normed[t * hidden + c] = out[t * hidden + c] * scale * (norm_weight[c] + weight_offset);
+}
+
+DRIFT_REGISTER(moe_combine, combine_kernel<false>)
+DRIFT_REGISTER(moe_combine_norm, combine_kernel<true>)
+
+static int check_combine(const float* expert_out, const float* weights, int64_t tokens, int64_t k,
+                         int64_t hidden, const float* shared_out, const float* shared_input,
+                         const float* shared_router, const void* out) {
+  if (tokens < 0 || k < 0 || hidden < 0 || tokens > 0x7fffffffll || hidden > 0x7fffffffll)
+    return invalid("moeCombine over [%lld, %lld] with k %lld", (long long)tokens,
+                   (long long)hidden, (long long)k);
+  if (tokens > 0 && hidden > 0 && (!out || (k > 0 && (!expert_out || !weights))))
+    return invalid("moeCombine: a null tensor");
+  if (shared_out && (!shared_input || !shared_router))
+    return invalid("moeCombine: a shared expert without its input and router");
+  return 0;
+}
+
+}  // namespace drift
+
+using namespace drift;
+
+extern "C" {
+
+int drift_route(const float* logits, int32_t* ids, float* weights, int tokens, int experts, int k,
+                drift_stream_t stream) {
+  if (tokens < 0 || experts <= 0 || k <= 0 || k > 16 || experts > 512 || k > experts)
+    return invalid("route: top-%d of %d", k, experts);
+  if (tokens == 0) return 0;
+  if (!logits || !ids || !weights) return invalid("route: a null tensor");
+  route_kernel<<<unsigned((tokens + 7) / 8), 256, 0, cudaStream_t(stream)>>>(logits, ids, weights,
+                                                                            tokens, experts, k);
+  DRIFT_LAUNCHED("route_topk");
+  return 0;
+}
+
+int drift_experts_linear(int x_dtype, const void* x, int64_t x_rows, int weight_dtype,
+                         const void* weight, int64_t experts, int64_t n, int64_t k,
+                         const int32_t* ids, int64_t slots, float* out, drift_stream_t stream) {
+  return experts_common(false, x_dtype, x, x_rows, weight_dtype, weight, nullptr, experts, n, k,
+                        ids, slots, out, cudaStream_t(stream));
+}
+
+int drift_experts_gated_linear(int x_dtype, const void* x, int64_t x_rows, int weight_dtype,
+                               const void* gate, const void* up, int64_t experts, int64_t n,
+                               int64_t k, const int32_t* ids, int64_t slots, float* out,
+                               drift_stream_t stream) {
+  return experts_common(true, x_dtype, x, x_rows, weight_dtype, gate, up, experts, n, k, ids,
+                        slots, out, cudaStream_t(stream));
+}
+
+int drift_moe_combine(const float* expert_out, const float* weights, int64_t tokens, int64_t k,
+                      int64_t hidden, const float* shared_out, const float* shared_input,
+                      const float* shared_router, const float* residual, float* out,
+                      drift_stream_t stream) {
+  DRIFT_TRY(check_combine(expert_out, weights, tokens, k, hidden, shared_out, shared_input,
+                          shared_router, out));
+  if (tokens == 0 || hidden == 0) return 0;
+  combine_kernel<false><<<unsigned(tokens), 256, 0, cudaStream_t(stream)>>>(
+      expert_out, weights, shared_out, shared_input, shared_router, residual, out, int(k),
+      int(hidden), nullptr, nullptr, 0.0f, 0.0f);
+  DRIFT_LAUNCHED("moe_combine");
+  return 0;
+}
+
+int drift_moe_combine_norm(const float* expert_out, const float* weights, int64_t tokens,
+                           int64_t k, int64_t hidden, const float* shared_out,
+                           const float* shared_input, const float* shared_router, float* residual,
+                           const float* norm_weight, float epsilon, float weight_offset,
+                           float* normed, drift_stream_t stream) {
+  DRIFT_TRY(check_combine(expert_out, weights, tokens, k, hidden, shared_out, shared_input,
+                          shared_router, residual));
+  if (tokens == 0 || hidden == 0) return 0;
+  if (!norm_weight || !normed) return invalid("moeCombineNorm: no norm weight or output");
+  combine_kernel<true><<<unsigned(tokens), 256, 0, cudaStream_t(stream)>>>(
+      expert_out, weights, shared_out, shared_input, shared_router, residual, residual, int(k),
+      int(hidden), norm_weight, normed, epsilon, weight_offset);
+  DRIFT_LAUNCHED("moe_combine_norm");
+  return 0;
+}
+
+}  // extern "C"

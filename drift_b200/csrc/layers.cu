@@ -1,0 +1,387 @@
+// The layer operations around the products: the embedding gather, RMS norm
+// (with the residual add fused), add, the gated activation (SwiGLU), rotary
+// embedding, and products with F32 weights (routers).
+//
+// Reference kernels: gather_<t> (kernels/matvec.hip:830-839), gather_rows_f32
+// (elementwise.hip:89-93), rms_norm_f32 (norm.hip:15-41), add_f32 /
+// gated_f32 (elementwise.hip:14-65), rope_f32 (rope.hip:6-15, rope.h:20-51),
+// matvec_rows_f32 (matvec.hip:1696-1734). Their CPU twins, which the results
+// are checked against: ops/CpuLinear.scala:12-41, CpuNormalisation.scala:
+// 11-71, CpuElementwise.scala:9-13, CpuAttention.scala:92-146.
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "quant.cuh"
+#include "registry.cuh"
+
+namespace drift {
+
+// ---- the device error word -----------------------------------------------------------
+// Set (first flag wins) by kernels that meet an input the reference refuses,
+// instead of reading out of bounds; read and cleared by drift_device_error_take.
+__device__ int error_word = 0;
+
+int* device_error_word() {
+  static int* words[64] = {nullptr};
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64) return nullptr;
+  if (!words[device]) {
+    void* address = nullptr;
+    if (cudaGetSymbolAddress(&address, error_word) != cudaSuccess) return nullptr;
+    words[device] = static_cast<int*>(address);
+  }
+  return words[device];
+}
+
+__device__ __forceinline__ void flag_error(int* error, int code) {
+  if (error) atomicCAS(error, 0, code);
+}
+
+// ---- embedding gather -----------------------------------------------------------------
+// One warp per id; lane l decodes blocks l, l + 32, ... of row ids[i] into 32
+// floats each, bit for bit the CPU decode (quant.cuh T::value).
+template <typename T>
+__global__ void __launch_bounds__(256) gather_kernel(const uint8_t* __restrict__ table,
+                                                     const int* __restrict__ ids,
+                                                     float* __restrict__ out, int count, int cols,
+                                                     long long vocab, int* error) {
+  const int index = blockIdx.x * (blockDim.x / WARP) + threadIdx.x / WARP;
+  if (index >= count) return;
+  const int lane = threadIdx.x % WARP;
+  const long long id = ids[index];
+  float4* target = reinterpret_cast<float4*>(out + (long long)index * cols);
+  const int blocks = cols / 32;
+  if (id < 0 || id >= vocab) {
+    const float nan = __int_as_float(0x7fc00000);
+    for (int i = lane; i < cols / 4; i += WARP) target[i] = make_float4(nan, nan, nan, nan);
+    if (lane == 0) flag_error(error, 1);
+    return;
+  }
+  const uint8_t* row = table + id * (long long)blocks * T::BYTES;
+  for (int c = lane; c < blocks; c += WARP) {
+    uint32_t w[T::WORDS];
+    load_block<T>(row, c, w);
+    const Codes codes = T::decode(w, c);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      target[c * 8 + i] = make_float4(T::value(codes, 4 * i), T::value(codes, 4 * i + 1),
+                                      T::value(codes, 4 * i + 2), T::value(codes, 4 * i + 3));
+  }
+}
+
+// F32 tables of any width: one thread per value.
+__global__ void gather_rows_f32_kernel(const float* __restrict__ table, const int* __restrict__ ids,
+                                       float* __restrict__ out, int count, int cols,
+                                       long long vocab, int* error) {
+  const long long index = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (index >= (long long)count * cols) return;
+  const long long id = ids[index / cols];
+  if (id < 0 || id >= vocab) {
+    out[index] = __int_as_float(0x7fc00000);
+    flag_error(error, 1);
+    return;
+  }
+  out[index] = table[id * cols + index % cols];
+}
+
+DRIFT_REGISTER(gather_q8_0, gather_kernel<Q8_0T>)
+DRIFT_REGISTER(gather_q4_0, gather_kernel<Q4_0T>)
+DRIFT_REGISTER(gather_q4_1, gather_kernel<Q4_1T>)
+DRIFT_REGISTER(gather_rows_f32, gather_rows_f32_kernel)
+
+// ---- block reductions -------------------------------------------------------------------
+// The sum over a block of `blockDim.x` threads (a multiple of 32): warps by
+// shuffles, then the warps' sums in warp order. Every thread gets it.
+__device__ __forceinline__ float block_sum(float value, float* partial) {
+#pragma unroll
+  for (int o = 16; o > 0; o /= 2) value += __shfl_xor_sync(0xffffffffu, value, o);
+  const int warp = threadIdx.x / WARP, warps = blockDim.x / WARP;
+  if (threadIdx.x % WARP == 0) partial[warp] = value;
+  __syncthreads();
+  float total = 0.0f;
+  for (int w = 0; w < warps; ++w) total += partial[w];
+  __syncthreads();  // partial is reused by the next reduction
+  return total;
+}
+
+// ---- RMS norm ----------------------------------------------------------------------------
+// One block of 256 threads per row. With `y`, x += y first (written back: the
+// residual stream). The sum of squares is float (each thread's values in
+// order, then a fixed tree); 1 / sqrt(mean + eps) is rounded as IEEE division
+// and square root round it, not rsqrtf's approximation.
+__global__ void __launch_bounds__(256) rms_norm_kernel(float* __restrict__ x, const float* __restrict__ y,
+                                                       const float* __restrict__ weight,
+                                                       float* __restrict__ out, int cols,
+                                                       float epsilon, float weight_offset) {
+  __shared__ float partial[32];
+  float* row = x + (long long)blockIdx.x * cols;
+  const float* add = y ? y + (long long)blockIdx.x * cols : nullptr;
+  float* target = out + (long long)blockIdx.x * cols;
+  float sum = 0.0f;
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+    float value = row[c];
+    if (add) {
+      value = value + add[c];
+      row[c] = value;
+    }
+    sum = fmaf(value, value, sum);
+  }
+  const float total = block_sum(sum, partial);
+  const float scale = 1.0f / sqrtf(total / float(cols) + epsilon);
+  for (int c = threadIdx.x; c < cols; c += blockDim.x)
+    target[c] = row[c] * scale * (weight[c] + weight_offset);
+}
+
+DRIFT_REGISTER(rms_norm_f32, rms_norm_kernel)
+
+// ---- elementwise ---------------------------------------------------------------------------
+#define DRIFT_FOR_EACH(i, n)                                                     \
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < (n); \
+       i += (long long)gridDim.x * blockDim.x)
+
+__global__ void add_kernel(const float* a, const float* b, float* out, long long n) {
+  DRIFT_FOR_EACH(i, n) out[i] = a[i] + b[i];
+}
+
+// Activation codes of ops/Activation.scala:5-19.
+__device__ __forceinline__ float activate(float v, int kind) {
+  switch (kind) {
+    case DRIFT_SILU: return v / (1.0f + expf(-v));
+    case DRIFT_GELU_TANH: {
+      const float inner = 0.7978845608028654f * (v + 0.044715f * v * v * v);
+      return 0.5f * v * (1.0f + tanhf(inner));
+    }
+    case DRIFT_GELU_ERF: return 0.5f * v * (1.0f + erff(v * 0.7071067811865476f));
+    case DRIFT_SIGMOID: return 1.0f / (1.0f + expf(-v));
+    default: return 4.0f * tanhf(v * 0.25f) / (1.0f + expf(-v));
+  }
+}
+
+__global__ void gated_kernel(const float* gate, const float* up, float* out, long long n, int kind) {
+  DRIFT_FOR_EACH(i, n) {
+    const float u = kind == DRIFT_SITU ? 25.0f * tanhf(up[i] * 0.04f) : up[i];
+    out[i] = activate(gate[i], kind) * u;
+  }
+}
+
+DRIFT_REGISTER(add_f32, add_kernel)
+DRIFT_REGISTER(gated_f32, gated_kernel)
+
+// ---- rotary embedding ---------------------------------------------------------------------
+// One thread per value of x [tokens, heads, head_dim]. The angle is the CPU
+// reference's to the bit: the inverse frequency 1f / (float) pow(theta,
+// 2 pair / rotary) (pow in double, then float), times float(position) in
+// float; the turn is then in double, as CpuAttention.rope turns it, and
+// rounded once. (The runner's own kernel uses powf/cosf/sinf and is held to
+// 1e-2 against the CPU, SmallOpsTests.scala:450-500; this one lands within an
+// ulp.)
+__global__ void rope_kernel(const float* __restrict__ x, const int* __restrict__ positions,
+                            float* __restrict__ out, int tokens, int heads, int head_dim,
+                            int rotary, float theta, int layout) {
+  const long long index = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (index >= (long long)tokens * heads * head_dim) return;
+  const int d = int(index % head_dim);
+  const int t = int(index / ((long long)heads * head_dim));
+  const float* head = x + (index - d);
+  if (d >= rotary) {
+    out[index] = head[d];
+    return;
+  }
+  const int half = rotary / 2;
+  int pair, partner;
+  bool first;
+  if (layout == DRIFT_ROPE_NEOX) {
+    pair = d % half;
+    first = d < half;
+    partner = first ? d + half : d - half;
+  } else {
+    pair = d / 2;
+    first = d % 2 == 0;
+    partner = first ? d + 1 : d - 1;
+  }
+  const float power = float(pow(double(theta), __ddiv_rn(2.0 * pair, double(rotary))));
+  const float inverse = __fdiv_rn(1.0f, power);
+  const float angle = __fmul_rn(float(positions[t]), inverse);
+  double s, c;
+  sincos(double(angle), &s, &c);
+  const double a = first ? double(head[d]) : double(head[partner]);
+  const double b = first ? double(head[partner]) : double(head[d]);
+  const double value = first ? __dsub_rn(__dmul_rn(a, c), __dmul_rn(b, s))
+                             : __dadd_rn(__dmul_rn(a, s), __dmul_rn(b, c));
+  out[index] = float(value);
+}
+
+DRIFT_REGISTER(rope_f32, rope_kernel)
+
+// ---- products with F32 weights (routers) -----------------------------------------------------
+// One warp per (row, vector): float4 loads when k is a multiple of 4, float
+// sums in a fixed order, then shuffles.
+template <bool BF16>
+__global__ void __launch_bounds__(256) matvec_f32_kernel(const void* __restrict__ x,
+                                                         const float* __restrict__ weight,
+                                                         float* __restrict__ y, int m, int n, int k) {
+  const long long index = (long long)blockIdx.x * (blockDim.x / WARP) + threadIdx.x / WARP;
+  if (index >= (long long)m * n) return;
+  const int lane = threadIdx.x % WARP;
+  const int row = int(index % n), vector = int(index / n);
+  const float* w = weight + (long long)row * k;
+  float sum = 0.0f;
+  for (int c = lane; c < k; c += WARP) {
+    float xv;
+    if (BF16)
+      xv = __uint_as_float(uint32_t(reinterpret_cast<const uint16_t*>(x)[(long long)vector * k + c]) << 16);
+    else
+      xv = reinterpret_cast<const float*>(x)[(long long)vector * k + c];
+    sum = fmaf(w[c], xv, sum);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o /= 2) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if (lane == 0) y[(long long)vector * n + row] = sum;
+}
+
+DRIFT_REGISTER(matvec_f32_f32x, matvec_f32_kernel<false>)
+DRIFT_REGISTER(matvec_f32_bf16x, matvec_f32_kernel<true>)
+
+int matvec_f32_weights(int x_dtype, const void* x, const float* weight, float* y, int64_t m,
+                       int64_t n, int64_t k, cudaStream_t stream) {
+  const long long warps = m * n;
+  const unsigned grid = unsigned((warps + 7) / 8);
+  if (x_dtype == DRIFT_BF16)
+    matvec_f32_kernel<true><<<grid, 256, 0, stream>>>(x, weight, y, int(m), int(n), int(k));
+  else
+    matvec_f32_kernel<false><<<grid, 256, 0, stream>>>(x, weight, y, int(m), int(n), int(k));
+  DRIFT_LAUNCHED("matvec_f32");
+  return 0;
+}
+
+static unsigned elementwise_grid(long long n) {
+  long long blocks = (n + 255) / 256;
+  const long long cap = (long long)sm_count() * 16;
+  return unsigned(blocks < 1 ? 1 : (blocks > cap ? cap : blocks));
+}
+
+}  // namespace drift
+
+using namespace drift;
+
+extern "C" {
+
+int drift_device_error_take(int* code) {
+  if (!code) return invalid("drift_device_error_take: no slot for the code");
+  int* word = device_error_word();
+  if (!word) return invalid("the device error word is not reachable");
+  DRIFT_CUDA(cudaDeviceSynchronize());
+  DRIFT_CUDA(cudaMemcpy(code, word, sizeof(int), cudaMemcpyDeviceToHost));
+  DRIFT_CUDA(cudaMemset(word, 0, sizeof(int)));
+  return 0;
+}
+
+int drift_embedding(int table_dtype, const void* table, int64_t vocab, int64_t cols,
+                    const int32_t* ids, int64_t count, float* out, drift_stream_t stream) {
+  if (vocab < 0 || cols < 0 || count < 0)
+    return invalid("an embedding table is [vocabulary, D], not [%lld, %lld]", (long long)vocab,
+                   (long long)cols);
+  if (table_dtype != DRIFT_Q8_0 && table_dtype != DRIFT_Q4_0 && table_dtype != DRIFT_Q4_1 &&
+      table_dtype != DRIFT_F32)
+    return invalid("no kernels for %s tables yet", dtype_name(table_dtype));
+  const int64_t row = byte_size(table_dtype, cols);
+  if (row < 0)
+    return invalid("%lld elements are not whole %s blocks of %d", (long long)cols,
+                   dtype_name(table_dtype), block_elements(table_dtype));
+  if (table_dtype != DRIFT_F32 && row % 4 != 0)
+    return invalid("%s rows of %lld are not whole words", dtype_name(table_dtype),
+                   (long long)cols);
+  if (count == 0 || cols == 0) return 0;
+  if (!table || !ids || !out) return invalid("embedding: a null tensor");
+  if (count > 0x7fffffffll || cols > 0x7fffffffll) return invalid("embedding too large");
+  int* error = device_error_word();
+  const cudaStream_t s = cudaStream_t(stream);
+  const uint8_t* t = static_cast<const uint8_t*>(table);
+  if (table_dtype == DRIFT_F32) {
+    const long long values = count * cols;
+    gather_rows_f32_kernel<<<unsigned((values + 255) / 256), 256, 0, s>>>(
+        static_cast<const float*>(table), ids, out, int(count), int(cols), vocab, error);
+  } else {
+    const unsigned grid = unsigned((count + 7) / 8);
+    if (table_dtype == DRIFT_Q8_0)
+      gather_kernel<Q8_0T><<<grid, 256, 0, s>>>(t, ids, out, int(count), int(cols), vocab, error);
+    else if (table_dtype == DRIFT_Q4_0)
+      gather_kernel<Q4_0T><<<grid, 256, 0, s>>>(t, ids, out, int(count), int(cols), vocab, error);
+    else
+      gather_kernel<Q4_1T><<<grid, 256, 0, s>>>(t, ids, out, int(count), int(cols), vocab, error);
+  }
+  DRIFT_LAUNCHED("gather");
+  return 0;
+}
+
+static int check_rows(const char* name, const void* x, const void* out, int64_t rows,
+                      int64_t cols) {
+  if (rows < 0 || cols < 0) return invalid("%s over [%lld, %lld]", name, (long long)rows,
+                                           (long long)cols);
+  if (rows > 0 && cols > 0 && (!x || !out)) return invalid("%s: a null tensor", name);
+  if (rows > 0x7fffffffll || cols > 0x7fffffffll) return invalid("%s too large", name);
+  return 0;
+}
+
+int drift_rms_norm(const float* x, const float* weight, float epsilon, float weight_offset,
+                   float* out, int64_t rows, int64_t cols, drift_stream_t stream) {
+  DRIFT_TRY(check_rows("rmsNorm", x, out, rows, cols));
+  if (rows == 0 || cols == 0) return 0;
+  if (!weight) return invalid("rmsNorm: no weight");
+  rms_norm_kernel<<<unsigned(rows), 256, 0, cudaStream_t(stream)>>>(
+      const_cast<float*>(x), nullptr, weight, out, int(cols), epsilon, weight_offset);
+  DRIFT_LAUNCHED("rms_norm_f32");
+  return 0;
+}
+
+int drift_add_rms_norm(float* x, const float* y, const float* weight, float epsilon,
+                       float weight_offset, float* out, int64_t rows, int64_t cols,
+                       drift_stream_t stream) {
+  DRIFT_TRY(check_rows("addRmsNorm", x, out, rows, cols));
+  if (rows == 0 || cols == 0) return 0;
+  if (!weight || !y) return invalid("addRmsNorm: no weight or no y");
+  rms_norm_kernel<<<unsigned(rows), 256, 0, cudaStream_t(stream)>>>(x, y, weight, out, int(cols),
+                                                                     epsilon, weight_offset);
+  DRIFT_LAUNCHED("rms_norm_f32");
+  return 0;
+}
+
+int drift_add(const float* a, const float* b, float* out, int64_t n, drift_stream_t stream) {
+  if (n < 0) return invalid("add over %lld values", (long long)n);
+  if (n == 0) return 0;
+  if (!a || !b || !out) return invalid("add: a null tensor");
+  add_kernel<<<elementwise_grid(n), 256, 0, cudaStream_t(stream)>>>(a, b, out, n);
+  DRIFT_LAUNCHED("add_f32");
+  return 0;
+}
+
+int drift_gated(int kind, const float* gate, const float* up, float* out, int64_t n,
+                drift_stream_t stream) {
+  if (kind < 0 || kind > 4) return invalid("gated: activation code %d", kind);
+  if (n < 0) return invalid("gated over %lld values", (long long)n);
+  if (n == 0) return 0;
+  if (!gate || !up || !out) return invalid("gated: a null tensor");
+  gated_kernel<<<elementwise_grid(n), 256, 0, cudaStream_t(stream)>>>(gate, up, out, n, kind);
+  DRIFT_LAUNCHED("gated_f32");
+  return 0;
+}
+
+int drift_rope(const float* x, const int32_t* positions, float* out, int tokens, int heads,
+               int head_dim, float theta, int rotary, int layout, drift_stream_t stream) {
+  if (tokens < 0 || heads < 0 || head_dim < 0)
+    return invalid("rope takes [tokens, heads, headDimension], got [%d, %d, %d]", tokens, heads,
+                   head_dim);
+  if (rotary <= 0 || rotary % 2 != 0 || rotary > head_dim)
+    return invalid("rope: %d rotary values of a head of %d", rotary, head_dim);
+  if (layout != DRIFT_ROPE_NEOX && layout != DRIFT_ROPE_INTERLEAVED)
+    return invalid("rope: layout %d", layout);
+  const long long values = (long long)tokens * heads * head_dim;
+  if (values == 0) return 0;
+  if (!x || !positions || !out) return invalid("rope: a null tensor");
+  rope_kernel<<<unsigned((values + 255) / 256), 256, 0, cudaStream_t(stream)>>>(
+      x, positions, out, tokens, heads, head_dim, rotary, theta, layout);
+  DRIFT_LAUNCHED("rope_f32");
+  return 0;
+}
+
+}  // extern "C"

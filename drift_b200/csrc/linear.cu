@@ -1,0 +1,102 @@
+// Ops.linear / Ops.linears behind the C ABI (include/drift_ops.h): the shape
+// rules of Ops.checkLinear (runner/src/drift/runner/ops/LinearOps.scala:
+// 227-249) and the dispatch of HipLinear.linears (ops/HipLinear.scala:104-276),
+// re-decided for B200.
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "quant.cuh"
+#include "registry.cuh"
+
+namespace drift {
+
+int workspace_reserve(size_t bytes, void** pointer);
+size_t linear_workspace_bytes(int64_t m, int64_t k);
+int prepare_x(int x_dtype, const void* x, int64_t m, int64_t k, uint32_t* records,
+              cudaStream_t stream);
+int matvec_prepared(int weight_dtype, const void* weight, const uint32_t* records, float* y,
+                    int64_t rows, int64_t cols, int64_t vectors, cudaStream_t stream);
+int matvec_f32_weights(int x_dtype, const void* x, const float* weight, float* y, int64_t m,
+                       int64_t n, int64_t k, cudaStream_t stream);
+
+// Ops.checkLinear, plus what the kernels need of a stored weight.
+static int check_linear(int x_dtype, const void* x, int weight_dtype, const void* weight,
+                        const float* out, int64_t m, int64_t n, int64_t k) {
+  if (x_dtype != DRIFT_F32 && x_dtype != DRIFT_BF16)
+    return invalid("linear takes F32 (or BF16) x, not %s", dtype_name(x_dtype));
+  if (m < 0 || n < 0 || k < 0) return invalid("linear over [%lld, %lld] x [%lld, %lld]",
+                                               (long long)m, (long long)k, (long long)n,
+                                               (long long)k);
+  if (weight_dtype != DRIFT_Q8_0 && weight_dtype != DRIFT_Q4_0 && weight_dtype != DRIFT_Q4_1 &&
+      weight_dtype != DRIFT_F32)
+    return invalid("no kernels for %s weights yet", dtype_name(weight_dtype));
+  const int64_t row = byte_size(weight_dtype, k);
+  if (row < 0)
+    return invalid("%lld elements are not whole %s blocks of %d", (long long)k,
+                   dtype_name(weight_dtype), block_elements(weight_dtype));
+  if (weight_dtype != DRIFT_F32 && row % 4 != 0)
+    return invalid("%s rows of %lld are not whole words", dtype_name(weight_dtype), (long long)k);
+  if (k > (1ll << 30) || m * k > 0x7fffffffll || n > 0x7fffffffll)
+    return invalid("linear over [%lld, %lld]", (long long)m, (long long)k);
+  if (m > 0 && n > 0 && k > 0 && (!x || !weight || !out))
+    return invalid("linear: a null tensor");
+  if ((reinterpret_cast<uintptr_t>(weight) & 3) != 0)
+    return invalid("linear: the weight does not start on a 4-byte boundary");
+  return 0;
+}
+
+}  // namespace drift
+
+using namespace drift;
+
+extern "C" {
+
+size_t drift_linear_workspace_bytes(int64_t m, int64_t k) { return linear_workspace_bytes(m, k); }
+
+int drift_workspace_reserve(size_t bytes) { return workspace_reserve(bytes, nullptr); }
+
+int drift_linears(int x_dtype, const void* x, int count, const int* weight_dtypes,
+                  const void* const* weights, float* const* outs, const int64_t* ns, int64_t m,
+                  int64_t k, drift_stream_t stream) {
+  if (count < 0 || (count > 0 && (!weight_dtypes || !weights || !outs || !ns)))
+    return invalid("linears: %d products without their weights", count);
+  for (int i = 0; i < count; ++i)
+    DRIFT_TRY(check_linear(x_dtype, x, weight_dtypes[i], weights[i], outs[i], m, ns[i], k));
+  if (m == 0 || k == 0 || count == 0) {
+    // an empty sum: zero rows of out, or rows of zeros
+    for (int i = 0; i < count; ++i)
+      if (m > 0 && ns[i] > 0)
+        DRIFT_CUDA(cudaMemsetAsync(outs[i], 0, size_t(m * ns[i]) * 4, cudaStream_t(stream)));
+    return 0;
+  }
+  const cudaStream_t s = cudaStream_t(stream);
+  bool quantized = false;
+  for (int i = 0; i < count; ++i) quantized |= weight_dtypes[i] != DRIFT_F32;
+  uint32_t* records = nullptr;
+  if (quantized) {
+    void* w = nullptr;
+    DRIFT_TRY(workspace_reserve(linear_workspace_bytes(m, k), &w));
+    records = static_cast<uint32_t*>(w);
+    DRIFT_TRY(prepare_x(x_dtype, x, m, k, records, s));  // one preparation for all
+  }
+  for (int i = 0; i < count; ++i) {
+    if (ns[i] == 0) continue;
+    if (weight_dtypes[i] == DRIFT_F32)
+      DRIFT_TRY(matvec_f32_weights(x_dtype, x, static_cast<const float*>(weights[i]), outs[i], m,
+                                   ns[i], k, s));
+    else
+      DRIFT_TRY(matvec_prepared(weight_dtypes[i], weights[i], records, outs[i], ns[i], k, m, s));
+  }
+  return 0;
+}
+
+int drift_linear(int x_dtype, const void* x, int weight_dtype, const void* weight, float* out,
+                 int64_t m, int64_t n, int64_t k, drift_stream_t stream) {
+  const void* weights[1] = {weight};
+  float* outs[1] = {out};
+  const int64_t ns[1] = {n};
+  const int dtypes[1] = {weight_dtype};
+  return drift_linears(x_dtype, x, 1, dtypes, weights, outs, ns, m, k, stream);
+}
+
+}  // extern "C"

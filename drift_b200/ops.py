@@ -1,0 +1,370 @@
+"""The drift runner's `Ops` API for the quantized-inference hot path, on B200.
+
+`CudaOps` mirrors the reference's operator interface (runner/src/drift/runner/
+ops/Ops.scala and its LinearOps, NormalisationOps, ElementwiseOps,
+AttentionOps.rope, ExpertsOps traits): the same operations, argument meanings
+and shape rules, with `out` tensors written and never read. Each call goes
+through libdrift_cuda's C ABI (include/drift_ops.h) -- the kernels, their
+dispatch and their checks are native; PyTorch only owns device memory and
+streams here. There is no CPU path: without the built library or a GPU the
+calls raise.
+
+Tensors: activations are torch CUDA tensors, F32 (and BF16 for a product's x);
+a stored weight is a `Stored` (its GGML type, logical shape and raw block
+bytes on the device), as the reference's Tensor(dtype, shape, storage) is.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Optional, Sequence
+
+import torch
+
+from . import _lib
+from ._lib import BF16, F32, Q4_0, Q4_1, Q8_0, check
+from .dtypes import DTYPES, byte_size
+
+# Activation codes (runner/src/drift/runner/ops/Activation.scala:5-19).
+SILU, GELU_TANH, GELU_ERF, SIGMOID, SITU = 0, 1, 2, 3, 4
+# RoPE layouts (ops/Rope.scala:7-10).
+NEOX, INTERLEAVED = 0, 1
+
+
+@dataclass
+class Stored:
+    """A weight in a storage type: `data` holds the raw blocks (uint8, on the
+    device), `shape` the logical elements ([N, K], or [experts, N, K])."""
+    dtype: int
+    shape: tuple
+    data: torch.Tensor
+
+    def __post_init__(self):
+        expected = byte_size(self.dtype, _count(self.shape))
+        if self.data.dtype != torch.uint8 or self.data.numel() < expected:
+            raise ValueError(f"{DTYPES[self.dtype].name} {list(self.shape)} needs {expected} "
+                             f"bytes, not {self.data.numel()} {self.data.dtype}")
+
+    @staticmethod
+    def upload(dtype: int, shape: Sequence[int], blocks, device=None) -> "Stored":
+        """Raw blocks (numpy uint8 or a tensor) copied to the device."""
+        tensor = torch.as_tensor(blocks).to(torch.uint8).reshape(-1)
+        return Stored(dtype, tuple(int(s) for s in shape),
+                      tensor.to(device or torch.device("cuda")))
+
+
+@dataclass
+class Rope:
+    """A rotary embedding (ops/Rope.scala:37-46), Single sections only."""
+    theta: float
+    rotary_dimensions: int
+    layout: int = NEOX
+
+
+@dataclass
+class RowNorm:
+    """An RMS norm taken of a result as it is written (ops/RowNorm.scala:20-25)."""
+    weight: torch.Tensor
+    epsilon: float
+    weight_offset: float
+    out: torch.Tensor
+
+
+@dataclass
+class SharedExpert:
+    """A mixture's shared expert in moe_combine (ops/ExpertTensors.scala:8-12):
+    its output [tokens, H] weighted by sigmoid(input . router)."""
+    output: torch.Tensor
+    input: torch.Tensor
+    router: torch.Tensor
+
+
+def _count(shape) -> int:
+    n = 1
+    for s in shape:
+        n *= int(s)
+    return n
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _require(condition: bool, message: str) -> None:
+    if not condition:
+        raise ValueError(message)
+
+
+def _f32(name: str, *tensors: torch.Tensor) -> None:
+    for t in tensors:
+        _require(t.dtype == torch.float32, f"{name} takes F32, not {t.dtype}")
+        _require(t.is_cuda and t.is_contiguous(),
+                 f"{name}: tensors are contiguous device memory")
+
+
+def _same_shape(name: str, *tensors: torch.Tensor) -> None:
+    shapes = {tuple(t.shape) for t in tensors}
+    _require(len(shapes) == 1,
+             f"{name} needs equal shapes, got {', '.join(str(list(t.shape)) for t in tensors)}")
+
+
+def _x_dtype(name: str, x: torch.Tensor) -> int:
+    _require(x.dtype in (torch.float32, torch.bfloat16),
+             f"{name} takes F32 (or BF16) x, not {x.dtype}")
+    _require(x.is_cuda and x.is_contiguous(), f"{name}: x is contiguous device memory")
+    return F32 if x.dtype == torch.float32 else BF16
+
+
+class CudaOps:
+    """The B200 backend of the `Ops` operations on the hot path."""
+
+    name = "cuda"
+
+    def __init__(self, device: int | None = None):
+        self.lib = _lib.load()
+        if device is not None:
+            torch.cuda.set_device(device)
+        self.device = torch.cuda.current_device()
+
+    # -- plumbing -------------------------------------------------------------------------
+    @staticmethod
+    def _stream():
+        return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def synchronize(self) -> None:
+        torch.cuda.current_stream().synchronize()
+
+    def take_device_error(self) -> int:
+        """The device error word (1: an id outside its table), cleared."""
+        code = ctypes.c_int(0)
+        check("drift_device_error_take", self.lib.drift_device_error_take(ctypes.byref(code)))
+        return code.value
+
+    def reserve_workspace(self, m: int, k: int) -> None:
+        """Sizes the library's scratch for products of m rows of k (call before
+        capturing a CUDA graph)."""
+        check("drift_workspace_reserve",
+              self.lib.drift_workspace_reserve(self.lib.drift_linear_workspace_bytes(m, k)))
+
+    # -- LinearOps (ops/LinearOps.scala) ------------------------------------------------------
+    @staticmethod
+    def _check_linear(x: torch.Tensor, weight, out: torch.Tensor):
+        """Ops.checkLinear (ops/LinearOps.scala:227-249); returns (M, N, K)."""
+        _x_dtype("linear", x)
+        _f32("linear", out)
+        wshape = weight.shape if isinstance(weight, Stored) else tuple(weight.shape)
+        _require(x.dim() == 2 and len(wshape) == 2 and out.dim() == 2,
+                 f"linear takes [M, K] · [N, K]ᵀ → [M, N], got {list(x.shape)}, "
+                 f"{list(wshape)}, {list(out.shape)}")
+        m, k = x.shape
+        n, wk = wshape
+        _require(wk == k, f"linear: x rows of {k} against weight rows of {wk}")
+        _require(tuple(out.shape) == (m, n), f"linear: out {list(out.shape)} for [{m}, {n}]")
+        return int(m), int(n), int(k)
+
+    @staticmethod
+    def _weight(weight):
+        if isinstance(weight, Stored):
+            return weight.dtype, weight.data
+        _require(weight.dtype == torch.float32 and weight.is_cuda and weight.is_contiguous(),
+                 f"no kernels for {weight.dtype} weights yet")
+        return F32, weight
+
+    def linear(self, x: torch.Tensor, weight, out: torch.Tensor) -> None:
+        """out = x · weightᵀ (ops/LinearOps.scala:147-150)."""
+        self.linears(x, [weight], [out])
+
+    def linears(self, x: torch.Tensor, weights: Sequence, outs: Sequence[torch.Tensor]) -> None:
+        """Several products of the same x, x prepared once (LinearOps.scala:152-156)."""
+        shapes = [self._check_linear(x, w, o) for w, o in zip(weights, outs)]
+        _require(len(weights) == len(outs), "linears: as many outs as weights")
+        if not shapes:
+            return
+        m, _, k = shapes[0]
+        count = len(weights)
+        dtypes = (ctypes.c_int * count)()
+        wptrs = (ctypes.c_void_p * count)()
+        optrs = (ctypes.c_void_p * count)()
+        ns = (ctypes.c_int64 * count)()
+        for i, (w, o, (_, n, _)) in enumerate(zip(weights, outs, shapes)):
+            dtype, data = self._weight(w)
+            dtypes[i], wptrs[i], optrs[i], ns[i] = dtype, data.data_ptr(), o.data_ptr(), n
+        status = self.lib.drift_linears(_x_dtype("linear", x), _ptr(x), count, dtypes, wptrs,
+                                        optrs, ns, m, k, self._stream())
+        check("drift_linears", status)
+
+    def embedding(self, table: Stored, ids: torch.Tensor, out: torch.Tensor) -> None:
+        """out[t] = table[ids[t]] as F32 (LinearOps.scala:83-87; checks L163-177)."""
+        _require(len(table.shape) == 2,
+                 f"an embedding table is [vocabulary, D], not {list(table.shape)}")
+        _require(ids.dtype == torch.int32 and ids.dim() == 1,
+                 f"embedding ids are I32 [tokens], not {ids.dtype} {list(ids.shape)}")
+        _f32("embedding", out)
+        vocab, cols = table.shape
+        _require(tuple(out.shape) == (ids.shape[0], cols),
+                 f"embedding: out {list(out.shape)} for {ids.shape[0]} rows of {cols}")
+        status = self.lib.drift_embedding(table.dtype, _ptr(table.data), vocab, cols, _ptr(ids),
+                                          ids.shape[0], _ptr(out), self._stream())
+        check("drift_embedding", status)
+
+    # -- NormalisationOps (ops/NormalisationOps.scala) ---------------------------------------------
+    @staticmethod
+    def _check_row_wise(name: str, x, out, *vectors) -> int:
+        """Ops.checkRowWise (ops/Ops.scala:76-92); returns the row count."""
+        _f32(name, x, out)
+        _same_shape(name, x, out)
+        _require(x.dim() >= 1, f"{name} needs at least one dimension")
+        for v in vectors:
+            _f32(name, v)
+            _require(tuple(v.shape) == (x.shape[-1],),
+                     f"{name}: {list(v.shape)} for rows of {x.shape[-1]}")
+        return x.numel() // max(1, x.shape[-1])
+
+    def rms_norm(self, x, weight, epsilon: float, weight_offset: float, out) -> None:
+        """out = x / sqrt(mean(x²) + eps) × (weight + offset) (NormalisationOps.scala:205-215)."""
+        rows = self._check_row_wise("rmsNorm", x, out, weight)
+        status = self.lib.drift_rms_norm(_ptr(x), _ptr(weight), epsilon, weight_offset, _ptr(out),
+                                         rows, x.shape[-1], self._stream())
+        check("drift_rms_norm", status)
+
+    def add_rms_norm(self, x, y, norm: RowNorm) -> None:
+        """x += y, then norm's RMS norm of x into norm.out, one launch
+        (NormalisationOps.scala:217-224)."""
+        _f32("add", x, y)
+        _same_shape("add", x, y)
+        rows = self._check_row_wise("rmsNorm", x, norm.out, norm.weight)
+        status = self.lib.drift_add_rms_norm(_ptr(x), _ptr(y), _ptr(norm.weight), norm.epsilon,
+                                             norm.weight_offset, _ptr(norm.out), rows,
+                                             x.shape[-1], self._stream())
+        check("drift_add_rms_norm", status)
+
+    def add(self, a, b, out) -> None:
+        """out = a + b (ops/CpuElementwise.scala:9-13)."""
+        _f32("add", a, b, out)
+        _same_shape("add", a, b, out)
+        check("drift_add", self.lib.drift_add(_ptr(a), _ptr(b), _ptr(out), a.numel(),
+                                              self._stream()))
+
+    def gated(self, kind: int, gate, up, out) -> None:
+        """out = kind(gate) × up: SwiGLU with SILU (NormalisationOps.scala:200-203)."""
+        _f32("gated", gate, up, out)
+        _same_shape("gated", gate, up, out)
+        check("drift_gated", self.lib.drift_gated(kind, _ptr(gate), _ptr(up), _ptr(out),
+                                                  gate.numel(), self._stream()))
+
+    # -- AttentionOps.rope (ops/AttentionOps.scala:42-45) ---------------------------------------------
+    def rope(self, x, positions, rope: Rope, out) -> None:
+        """Rotary embedding of x [tokens, heads, D]; positions I32 [tokens]."""
+        _f32("rope", x, out)
+        _same_shape("rope", x, out)
+        _require(x.dim() == 3, f"rope takes [tokens, heads, headDimension], got {list(x.shape)}")
+        _require(positions.dtype == torch.int32,
+                 f"rope positions are I32, not {positions.dtype}")
+        tokens, heads, dim = x.shape
+        _require(tuple(positions.shape) == (tokens,),
+                 f"rope: positions {list(positions.shape)} for {tokens} tokens")
+        status = self.lib.drift_rope(_ptr(x), _ptr(positions), _ptr(out), tokens, heads, dim,
+                                     rope.theta, rope.rotary_dimensions, rope.layout,
+                                     self._stream())
+        check("drift_rope", status)
+
+    # -- ExpertsOps (ops/ExpertsOps.scala) -------------------------------------------------------------
+    def route(self, logits, ids, weights) -> None:
+        """Top-k routing (ExpertsOps.scala:116-120; checks L252-269)."""
+        _f32("route", logits, weights)
+        _require(ids.dtype == torch.int32 and tuple(ids.shape) == tuple(weights.shape)
+                 and logits.dim() == 2,
+                 f"route: {list(logits.shape)}, {list(ids.shape)}, {list(weights.shape)}")
+        tokens, experts = logits.shape
+        k = weights.shape[-1]
+        _require(tuple(weights.shape) == (tokens, k) and k <= 16 and experts <= 512,
+                 f"route: top-{k} of {experts}")
+        status = self.lib.drift_route(_ptr(logits), _ptr(ids), _ptr(weights), tokens, experts, k,
+                                      self._stream())
+        check("drift_route", status)
+
+    def route_linear(self, x, router, logits, ids, weights) -> None:
+        """A router's logits = x · routerᵀ, then route (ExpertsOps.scala:176-186)."""
+        self.linear(x, router, logits)
+        self.route(logits, ids, weights)
+
+    @staticmethod
+    def _check_experts(x, weight: Stored, ids, out):
+        """Ops.checkExperts (ExpertsOps.scala:271-295); returns (slots, N, K, rows)."""
+        _x_dtype("expertsLinear", x)
+        _f32("expertsLinear", out)
+        _require(len(weight.shape) == 3 and ids.dtype == torch.int32,
+                 f"expertsLinear: weight {list(weight.shape)}, ids {ids.dtype}")
+        _, n, k = weight.shape
+        slots = ids.numel()
+        rows = x.shape[0]
+        _require(x.dim() == 2 and x.shape[1] == k and rows > 0 and slots % rows == 0,
+                 f"expertsLinear: x {list(x.shape)} for {slots} slots of {k}")
+        _require(tuple(out.shape) == (slots, n),
+                 f"expertsLinear: out {list(out.shape)}, expected [{slots}, {n}]")
+        return slots, n, k, rows
+
+    def experts_linear(self, x, weight: Stored, ids, out) -> None:
+        """Slot s: expert ids[s] of weight [experts, N, K] times x row
+        s / (slots / rows of x) (ExpertsOps.scala:122-126)."""
+        slots, n, k, rows = self._check_experts(x, weight, ids, out)
+        status = self.lib.drift_experts_linear(
+            _x_dtype("expertsLinear", x), _ptr(x), rows, weight.dtype, _ptr(weight.data),
+            weight.shape[0], n, k, _ptr(ids), slots, _ptr(out), self._stream())
+        check("drift_experts_linear", status)
+
+    def experts_gated_linear(self, x, gate: Stored, up: Stored, ids, out) -> None:
+        """silu(gate · x) × (up · x) per slot, one launch (ExpertsOps.scala:188-198)."""
+        _require(tuple(gate.shape) == tuple(up.shape) and gate.dtype == up.dtype,
+                 f"expertsGatedLinear needs equal shapes, got {list(gate.shape)}, "
+                 f"{list(up.shape)}")
+        slots, n, k, rows = self._check_experts(x, gate, ids, out)
+        status = self.lib.drift_experts_gated_linear(
+            _x_dtype("expertsGatedLinear", x), _ptr(x), rows, gate.dtype, _ptr(gate.data),
+            _ptr(up.data), gate.shape[0], n, k, _ptr(ids), slots, _ptr(out), self._stream())
+        check("drift_experts_gated_linear", status)
+
+    @staticmethod
+    def _check_combine(expert_out, weights, shared, residual, out):
+        _f32("moeCombine", expert_out, weights, out)
+        tokens, hidden = out.shape
+        _require(weights.numel() % max(1, tokens) == 0, "moeCombine: weights per token")
+        k = weights.numel() // max(1, tokens)
+        _require(tuple(expert_out.shape) == (tokens * k, hidden),
+                 f"moeCombine: expert outputs {list(expert_out.shape)} for [{tokens * k}, "
+                 f"{hidden}]")
+        if shared is not None:
+            _f32("moeCombine", shared.output, shared.input, shared.router)
+            _require(tuple(shared.output.shape) == (tokens, hidden)
+                     and tuple(shared.input.shape) == (tokens, hidden)
+                     and tuple(shared.router.shape) == (hidden,),
+                     "moeCombine: shared expert shapes")
+        if residual is not None:
+            _f32("moeCombine", residual)
+            _same_shape("moeCombine", residual, out)
+        return tokens, k, hidden
+
+    def moe_combine(self, expert_out, weights, shared: Optional[SharedExpert],
+                    residual: Optional[torch.Tensor], out) -> None:
+        """out[t] = residual[t] + Σ_j weights[t, j]·expertOut[t·k + j] (+ the
+        shared expert by its gate) (ExpertsOps.scala:128-138)."""
+        tokens, k, hidden = self._check_combine(expert_out, weights, shared, residual, out)
+        status = self.lib.drift_moe_combine(
+            _ptr(expert_out), _ptr(weights), tokens, k, hidden,
+            _ptr(shared.output) if shared else None, _ptr(shared.input) if shared else None,
+            _ptr(shared.router) if shared else None, _ptr(residual), _ptr(out), self._stream())
+        check("drift_moe_combine", status)
+
+    def moe_combine_norm(self, expert_out, weights, shared: Optional[SharedExpert], residual,
+                         norm: RowNorm) -> None:
+        """moe_combine into the residual, then norm's RMS norm of it into
+        norm.out, one launch (ExpertsOps.scala:140-152)."""
+        tokens, k, hidden = self._check_combine(expert_out, weights, shared, residual, residual)
+        self._check_row_wise("rmsNorm", residual, norm.out, norm.weight)
+        status = self.lib.drift_moe_combine_norm(
+            _ptr(expert_out), _ptr(weights), tokens, k, hidden,
+            _ptr(shared.output) if shared else None, _ptr(shared.input) if shared else None,
+            _ptr(shared.router) if shared else None, _ptr(residual), _ptr(norm.weight),
+            norm.epsilon, norm.weight_offset, _ptr(norm.out), self._stream())
+        check("drift_moe_combine_norm", status)

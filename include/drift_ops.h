@@ -1,0 +1,157 @@
+/*
+ * drift_ops.h -- the operator half of libdrift_cuda's C ABI.
+ *
+ * One entry point per operation of the drift runner's `Ops` API on the
+ * quantized-inference hot path. Each does what the runner's HIP backend does
+ * for that operation -- check the shapes as `Ops.check*` does, choose a kernel
+ * variant by dtype and shape, compute the launch geometry, launch on `stream`
+ * -- so a host that calls these needs none of HipLinear/HipNormalisation/
+ * HipExperts' dispatch. Every function is asynchronous on `stream`, returns an
+ * int status (see drift_runtime.h), and refuses shapes the reference refuses
+ * with DRIFT_ERROR_INVALID_ARGUMENT and the reference's message.
+ *
+ * Conventions, as the reference's (runner/src/drift/runner/ops/Ops.scala:7-13):
+ * activations are F32 (this ABI also takes BF16 x for the products, widened
+ * exactly); weights are raw GGML blocks, rows of [N, K] row-major with the
+ * blocks along K (tensor/Tensor.scala:75-87); `out` is written, never read,
+ * and may alias an input for elementwise operations. Pointers are device
+ * addresses of the current device.
+ */
+#ifndef DRIFT_OPS_H
+#define DRIFT_OPS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "drift_runtime.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Storage types: GGML type ids, as DType.ggmlId gives them
+ * (runner/src/drift/runner/tensor/DType.scala:86-175; GgmlQuants.scala). */
+#define DRIFT_F32 0
+#define DRIFT_F16 1
+#define DRIFT_Q4_0 2
+#define DRIFT_Q4_1 3
+#define DRIFT_Q8_0 8
+#define DRIFT_I32 26
+#define DRIFT_BF16 30
+
+/* Activation codes (runner/src/drift/runner/ops/Activation.scala:5-19). */
+#define DRIFT_SILU 0
+#define DRIFT_GELU_TANH 1
+#define DRIFT_GELU_ERF 2
+#define DRIFT_SIGMOID 3
+#define DRIFT_SITU 4
+
+/* RoPE layouts (runner/src/drift/runner/ops/Rope.scala:7-10). */
+#define DRIFT_ROPE_NEOX 0
+#define DRIFT_ROPE_INTERLEAVED 1
+
+/* Ops.linear (ops/LinearOps.scala:147-150; HIP dispatch ops/HipLinear.scala:
+ * 94-276): out[m, n] = x[m, k] . weight[n, k]^T. x is F32 or BF16 [m, k],
+ * weight Q8_0/Q4_0/Q4_1 (or F32) [n, k], out F32 [m, n]. Up to 8 rows of x
+ * are one pass over the weight; 8 < m < 32 runs passes of 8; m >= 32 is the
+ * tensor-core product. Rows must be whole 4-byte words ("rows are not whole
+ * words", HipLinear.scala:126-131). */
+int drift_linear(int x_dtype, const void* x, int weight_dtype, const void* weight, float* out,
+                 int64_t m, int64_t n, int64_t k, drift_stream_t stream);
+
+/* Ops.linears (LinearOps.scala:152-156; HipLinear.scala:104-156): several
+ * products of the same x (Q, K and V; gate and up), x prepared once. */
+int drift_linears(int x_dtype, const void* x, int count, const int* weight_dtypes,
+                  const void* const* weights, float* const* outs, const int64_t* ns, int64_t m,
+                  int64_t k, drift_stream_t stream);
+
+/* Ops.embedding (LinearOps.scala:83-87; HipLinear.scala:21-52): out[t] =
+ * decode(table[ids[t]]) as F32, bit for bit the CPU decode. An id outside
+ * [0, vocab) -- which the reference's CPU backend refuses with "token id ...
+ * outside the table" (ops/CpuLinear.scala:19-23) -- leaves that row NaN and
+ * sets the device error word (drift_device_error_take). */
+int drift_embedding(int table_dtype, const void* table, int64_t vocab, int64_t cols,
+                    const int32_t* ids, int64_t count, float* out, drift_stream_t stream);
+
+/* Ops.rmsNorm (ops/NormalisationOps.scala:30-36; HipNormalisation.scala:57-115):
+ * out = x / sqrt(mean(x^2) + eps) * (weight + offset), per row of `cols`. */
+int drift_rms_norm(const float* x, const float* weight, float epsilon, float weight_offset,
+                   float* out, int64_t rows, int64_t cols, drift_stream_t stream);
+
+/* Ops.addRmsNorm (NormalisationOps.scala:42-45; HipNormalisation.scala:117-131):
+ * x += y (written back), then out = rmsNorm(x). One launch. */
+int drift_add_rms_norm(float* x, const float* y, const float* weight, float epsilon,
+                       float weight_offset, float* out, int64_t rows, int64_t cols,
+                       drift_stream_t stream);
+
+/* ElementwiseOps.add (ops/CpuElementwise.scala:9-13; kernels add_f32). */
+int drift_add(const float* a, const float* b, float* out, int64_t n, drift_stream_t stream);
+
+/* Ops.gated (NormalisationOps.scala:24; HipNormalisation.scala:32-47):
+ * out = act(gate) * up; DRIFT_SILU is SwiGLU. */
+int drift_gated(int kind, const float* gate, const float* up, float* out, int64_t n,
+                drift_stream_t stream);
+
+/* Ops.rope with RopeSections.Single (ops/AttentionOps.scala:42-45;
+ * HipAttention.scala:81-104): x [tokens, heads, head_dim] F32, positions I32
+ * [tokens]; the first `rotary` values of each head turn in pairs. */
+int drift_rope(const float* x, const int32_t* positions, float* out, int tokens, int heads,
+               int head_dim, float theta, int rotary, int layout, drift_stream_t stream);
+
+/* Ops.route (ops/ExpertsOps.scala:116-120; HipExperts.scala:19-32): each
+ * token's k largest logits (the lower expert first among equals) into ids
+ * [tokens, k], their softmax among themselves into weights. k <= 16,
+ * experts <= 512 (ExpertsOps.scala:264-267). */
+int drift_route(const float* logits, int32_t* ids, float* weights, int tokens, int experts, int k,
+                drift_stream_t stream);
+
+/* Ops.expertsLinear (ExpertsOps.scala:122-126; HipExperts.scala:76-168): slot
+ * s multiplies expert ids[s] of weight [experts, n, k] with x row
+ * s / (slots / x_rows), into out [slots, n]. An id outside [0, experts)
+ * leaves its slot NaN and sets the device error word. */
+int drift_experts_linear(int x_dtype, const void* x, int64_t x_rows, int weight_dtype,
+                         const void* weight, int64_t experts, int64_t n, int64_t k,
+                         const int32_t* ids, int64_t slots, float* out, drift_stream_t stream);
+
+/* Ops.expertsGatedLinear (ExpertsOps.scala:188-198; HipExperts.scala:478-546):
+ * out = silu(gate . x) * (up . x) per slot, one launch. */
+int drift_experts_gated_linear(int x_dtype, const void* x, int64_t x_rows, int weight_dtype,
+                               const void* gate, const void* up, int64_t experts, int64_t n,
+                               int64_t k, const int32_t* ids, int64_t slots, float* out,
+                               drift_stream_t stream);
+
+/* Ops.moeCombine (ExpertsOps.scala:128-138; kernels/linear_attention.hip:
+ * 286-297, combine.h:10-32): out[t] = residual[t] + sum_j weights[t, j] *
+ * expert_out[t*k + j] + sigmoid(shared_input[t] . shared_router) *
+ * shared_out[t]. shared_* and residual may be NULL; out may be residual. */
+int drift_moe_combine(const float* expert_out, const float* weights, int64_t tokens, int64_t k,
+                      int64_t hidden, const float* shared_out, const float* shared_input,
+                      const float* shared_router, const float* residual, float* out,
+                      drift_stream_t stream);
+
+/* Ops.moeCombineNorm (ExpertsOps.scala:140-152; kernels/norm.hip:43-59):
+ * moeCombine into residual, then its RMS norm into normed, one launch. */
+int drift_moe_combine_norm(const float* expert_out, const float* weights, int64_t tokens,
+                           int64_t k, int64_t hidden, const float* shared_out,
+                           const float* shared_input, const float* shared_router, float* residual,
+                           const float* norm_weight, float epsilon, float weight_offset,
+                           float* normed, drift_stream_t stream);
+
+/* The library keeps one grow-only scratch buffer per device for the products'
+ * prepared x (as the runner's HIP backend keeps grow-only scratch,
+ * ops/HipBase.scala:341-351). Reserving it ahead keeps allocation out of a
+ * CUDA graph capture. */
+int drift_workspace_reserve(size_t bytes);
+/* Bytes of scratch drift_linear needs for m rows of k (new). */
+size_t drift_linear_workspace_bytes(int64_t m, int64_t k);
+
+/* Reads and clears the current device's error word: 0 if no kernel flagged
+ * anything since the last call, else the first flag (1 = an id outside its
+ * table, 2 = a bounded wait gave up). Synchronises the device. */
+int drift_device_error_take(int* code);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DRIFT_OPS_H */

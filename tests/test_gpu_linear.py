@@ -1,0 +1,159 @@
+"""Quantized products on the GPU against the CPU oracle (the reference's
+LinearTests, runner/gpuTest/src/drift/runner/LinearTests.scala, on this path).
+
+Each case is held to two bars:
+- BASELINE's: |gpu - oracle| <= 1e-4 + 1e-3 |oracle|;
+- the rigorous bound of the x preparation: x enters as exact integers 21 bits
+  below each 32-value block's largest |x| (drift_b200/csrc/quant.cuh), so an
+  output can move by at most sum_k |w_k| * max|x_block| * 2^-21, plus float
+  rounding of the sums, 1e-5 of the output scale (the reference's own
+  float-x tolerance, LinearTests.scala:154-157).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from drift_b200 import synthetic
+from drift_b200.ops import CudaOps, Stored
+from tests.conftest import within
+
+pytestmark = pytest.mark.gpu
+
+TYPES = [oracle.Q8_0, oracle.Q4_0, oracle.Q4_1]
+
+# (M, N, K) as LinearTests.cases (L33-58): one row, odd row counts, rows
+# shorter than a chunk, a model's width, several vectors, past 8 vectors.
+CASES = [(1, 1, 64), (1, 7, 512), (1, 33, 640), (1, 64, 2560), (2, 9, 4096), (3, 20, 1024),
+         (8, 16, 2560), (9, 24, 512), (40, 72, 2560), (1, 1030, 1024), (64, 130, 4096)]
+
+
+@pytest.fixture(scope="module")
+def ops():
+    return CudaOps()
+
+
+def bound(decoded: np.ndarray, x: np.ndarray) -> np.ndarray:
+    """sum_k |w_k| * max|x_block(k)| * 2^-21 per output [m, n]."""
+    m, k = x.shape
+    block_max = np.abs(x.reshape(m, k // 32, 32)).max(axis=2)  # [m, k/32]
+    per_block = np.abs(decoded.reshape(decoded.shape[0], k // 32, 32)).sum(axis=2)  # [n, k/32]
+    return (block_max.astype(np.float64) @ per_block.T.astype(np.float64)) * 2.0 ** -21
+
+
+def run_case(ops, dtype, m, n, k, seed, x_bf16: bool, law: str):
+    rng = np.random.default_rng(seed)
+    if law == "tests":
+        w = synthetic.random_blocks(rng, dtype, n, k)
+    else:
+        w = synthetic.quantized(rng, dtype, n, k)
+    x32 = synthetic.gaussian(rng, m, k)
+    if x_bf16:
+        bits = synthetic.bf16_bits(x32)
+        x_eff = synthetic.bf16_values(bits)
+        x_dev = torch.from_numpy(bits.view(np.int16)).cuda().view(torch.bfloat16)
+    else:
+        x_eff = x32
+        x_dev = torch.from_numpy(x32).cuda()
+    weight = Stored.upload(dtype, (n, k), w)
+    out = torch.full((m, n), float("nan"), device="cuda")
+    ops.linear(x_dev, weight, out)
+    torch.cuda.synchronize()
+    actual = out.cpu().numpy()
+    expected = oracle.linear(dtype, x_eff, w, n, k)
+    decoded = oracle.decode(dtype, w, n * k).reshape(n, k)
+    return actual, expected, bound(decoded, x_eff)
+
+
+@pytest.mark.parametrize("dtype", TYPES, ids=lambda t: oracle.NAMES[t])
+@pytest.mark.parametrize("case", CASES, ids=lambda c: "x".join(map(str, c)))
+@pytest.mark.parametrize("x_bf16", [False, True], ids=["x_f32", "x_bf16"])
+def test_linear_matches_oracle(ops, dtype, case, x_bf16):
+    m, n, k = case
+    for law in ("tests", "bench"):
+        actual, expected, limit = run_case(ops, dtype, m, n, k, seed=hash(case) % 1000,
+                                           x_bf16=x_bf16, law=law)
+        ok, _, _, summary = within(actual, expected, 1e-4, 1e-3)
+        assert ok, f"{law} weights: {summary}"
+        scale = np.abs(expected).max()
+        err = np.abs(actual.astype(np.float64) - expected)
+        assert (err <= limit + 1e-5 * scale).all(), \
+            f"{law} weights: worst at {(err / (limit + 1e-5 * scale)).max():.2f} of the bound"
+
+
+@pytest.mark.parametrize("dtype", TYPES, ids=lambda t: oracle.NAMES[t])
+def test_linears_share_one_preparation(ops, dtype):
+    """linears (Q, K, V) equals separate linears, bit for bit."""
+    rng = np.random.default_rng(11)
+    k = 2048
+    shapes = [512, 128, 128]
+    ws = [synthetic.quantized(rng, dtype, n, k) for n in shapes]
+    x = torch.from_numpy(synthetic.gaussian(rng, 3, k)).cuda()
+    weights = [Stored.upload(dtype, (n, k), w) for n, w in zip(shapes, ws)]
+    together = [torch.empty(3, n, device="cuda") for n in shapes]
+    ops.linears(x, weights, together)
+    for w, t in zip(weights, together):
+        alone = torch.empty_like(t)
+        ops.linear(x, w, alone)
+        assert torch.equal(alone, t)
+
+
+def test_linear_rows_do_not_depend_on_batch(ops):
+    """A row's sum is the same whether it comes alone or with 7 others."""
+    rng = np.random.default_rng(12)
+    n, k = 300, 4096
+    w = Stored.upload(oracle.Q4_1, (n, k), synthetic.quantized(rng, oracle.Q4_1, n, k))
+    x = torch.from_numpy(synthetic.gaussian(rng, 8, k)).cuda()
+    batch = torch.empty(8, n, device="cuda")
+    ops.linear(x, w, batch)
+    for i in range(8):
+        one = torch.empty(1, n, device="cuda")
+        ops.linear(x[i:i + 1].contiguous(), w, one)
+        assert torch.equal(one[0], batch[i])
+
+
+# The BASELINE C2 shapes at full size: sampled rows against the oracle.
+FULL = [(4096, 4096), (12288, 4096), (4096, 12288), (151936, 4096)]
+
+
+@pytest.mark.parametrize("shape", FULL, ids=lambda s: f"{s[0]}x{s[1]}")
+@pytest.mark.parametrize("m", [1, 8, 64])
+def test_full_size_q4_1_sampled_rows(ops, shape, m):
+    n, k = shape
+    rng = np.random.default_rng(n + k + m)
+    w = synthetic.quantized(rng, oracle.Q4_1, n, k)
+    bits = synthetic.bf16_bits(synthetic.gaussian(rng, m, k))
+    x_eff = synthetic.bf16_values(bits)
+    weight = Stored.upload(oracle.Q4_1, (n, k), w)
+    out = torch.empty((m, n), device="cuda")
+    ops.linear(torch.from_numpy(bits.view(np.int16)).cuda().view(torch.bfloat16), weight, out)
+    torch.cuda.synchronize()
+    rows = np.unique(np.concatenate([[0, n - 1], rng.integers(0, n, 200)]))
+    expected = oracle.linear_rows(oracle.Q4_1, x_eff, w, n, k, rows)
+    actual = out.cpu().numpy()[:, rows]
+    ok, _, _, summary = within(actual, expected, 1e-4, 1e-3)
+    assert ok, summary
+    assert torch.isfinite(out).all()
+
+
+def test_f32_router_weights(ops):
+    """F32 weights (the MoE router, ops/ExpertTensors.scala:15) against the oracle."""
+    rng = np.random.default_rng(13)
+    n, k = 512, 2048
+    w = synthetic.gaussian(rng, n, k) * 0.05
+    x = synthetic.gaussian(rng, 4, k)
+    out = torch.empty(4, n, device="cuda")
+    ops.linear(torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda(), out)
+    expected = oracle.linear(oracle.F32, x, w.view(np.uint8), n, k)
+    ok, _, _, summary = within(out.cpu().numpy(), expected, 1e-4, 1e-3)
+    assert ok, summary
+
+
+def test_linear_refuses_like_the_reference(ops):
+    x = torch.zeros(1, 96, device="cuda")
+    w = Stored.upload(oracle.Q8_0, (1, 96), np.zeros(102, np.uint8))
+    with pytest.raises(ValueError, match="are not whole words"):
+        ops.linear(x, w, torch.empty(1, 1, device="cuda"))
+    with pytest.raises(ValueError, match="x rows of 64 against weight rows of 96"):
+        ops.linear(torch.zeros(1, 64, device="cuda"), w, torch.empty(1, 1, device="cuda"))

@@ -1,0 +1,257 @@
+"""The layer operations and the mixture of experts on the GPU against the CPU
+oracle (the reference's SmallOpsTests and FusedOpsTests,
+runner/gpuTest/src/drift/runner/SmallOpsTests.scala, FusedOpsTests.scala)."""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from drift_b200 import synthetic
+from drift_b200.ops import (CudaOps, Rope, RowNorm, SharedExpert, Stored, NEOX, INTERLEAVED,
+                            SILU, SIGMOID, GELU_ERF, GELU_TANH, SITU)
+from tests.conftest import within
+
+pytestmark = pytest.mark.gpu
+
+# SmallOpsTests' awkward shapes (L22-29) and the BASELINE C3 ones.
+SHAPES = [(1, 1), (3, 7), (2, 255), (5, 4097), (17, 2560), (1, 2048), (1, 4096), (64, 4096)]
+
+
+@pytest.fixture(scope="module")
+def ops():
+    return CudaOps()
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+# ---- embedding (bit-exact) -------------------------------------------------------------------
+@pytest.mark.parametrize("dtype", [oracle.Q8_0, oracle.Q4_0, oracle.Q4_1],
+                         ids=lambda t: oracle.NAMES[t])
+def test_embedding_is_bit_exact(ops, dtype):
+    rng = np.random.default_rng(21)
+    vocab, cols = 1000, 4096
+    table = synthetic.random_blocks(rng, dtype, vocab, cols)
+    ids = np.concatenate([[0, vocab - 1], rng.integers(0, vocab, 62)]).astype(np.int32)
+    out = torch.empty(ids.size, cols, device="cuda")
+    ops.embedding(Stored.upload(dtype, (vocab, cols), table), dev(ids), out)
+    expected = oracle.embedding(dtype, table, vocab, cols, ids)
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), expected.view(np.uint32))
+
+
+def test_embedding_full_vocabulary_q8_0(ops):
+    """BASELINE C3: a Q8_0 table 151936 x 4096, random ids, b in {1, 8, 16, 64}."""
+    rng = np.random.default_rng(22)
+    vocab, cols = 151936, 4096
+    table = synthetic.quantized(rng, oracle.Q8_0, vocab, cols)
+    stored = Stored.upload(oracle.Q8_0, (vocab, cols), table)
+    for b in (1, 8, 16, 64):
+        ids = rng.integers(0, vocab, b).astype(np.int32)
+        ids[0] = vocab - 1
+        out = torch.empty(b, cols, device="cuda")
+        ops.embedding(stored, dev(ids), out)
+        expected = oracle.embedding(oracle.Q8_0, table, vocab, cols, ids)
+        assert np.array_equal(out.cpu().numpy().view(np.uint32), expected.view(np.uint32))
+
+
+def test_embedding_id_outside_the_table_is_flagged(ops):
+    """The CPU reference refuses it ("token id ... outside the table",
+    ops/CpuLinear.scala:19-23); here the row comes out NaN and the device
+    error word says so -- no out-of-bounds read."""
+    vocab, cols = 4, 64
+    table = Stored.upload(oracle.Q8_0, (vocab, cols), np.zeros(vocab * 68, np.uint8))
+    ops.take_device_error()
+    out = torch.zeros(3, cols, device="cuda")
+    ops.embedding(table, dev(np.array([0, 4, -1], np.int32)), out)
+    assert ops.take_device_error() == 1
+    result = out.cpu().numpy()
+    assert (result[0] == 0).all() and np.isnan(result[1:]).all()
+    assert ops.take_device_error() == 0
+
+
+# ---- norms and elementwise ------------------------------------------------------------------------
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: f"{s[0]}x{s[1]}")
+def test_rms_norm(ops, shape):
+    rng = np.random.default_rng(sum(shape))
+    x = synthetic.gaussian(rng, *shape)
+    w = (1 + rng.standard_normal(shape[1]) * 0.02).astype(np.float32)
+    out = torch.empty(shape, device="cuda")
+    ops.rms_norm(dev(x), dev(w), 1e-6, 0.0, out)
+    expected = oracle.rms_norm(x, w, 1e-6)
+    ok, _, _, summary = within(out.cpu().numpy(), expected, 1e-5, 1e-5)  # SmallOpsTests L115-127
+    assert ok, summary
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: f"{s[0]}x{s[1]}")
+def test_add_rms_norm(ops, shape):
+    rng = np.random.default_rng(sum(shape) + 1)
+    x = synthetic.gaussian(rng, *shape)
+    y = synthetic.gaussian(rng, *shape)
+    w = (1 + rng.standard_normal(shape[1]) * 0.02).astype(np.float32)
+    xd = dev(x)
+    out = torch.empty(shape, device="cuda")
+    ops.add_rms_norm(xd, dev(y), RowNorm(dev(w), 1e-6, 0.0, out))
+    sum_expected, norm_expected = oracle.add_rms_norm(x, y, w, 1e-6)
+    assert np.array_equal(xd.cpu().numpy(), sum_expected)
+    ok, _, _, summary = within(out.cpu().numpy(), norm_expected, 1e-5, 1e-5)
+    assert ok, summary
+
+
+def test_rms_norm_weight_offset_and_zero_row(ops):
+    x = np.zeros((2, 8), np.float32)
+    x[1] = np.arange(8)
+    w = np.full(8, 0.5, np.float32)
+    out = torch.empty(2, 8, device="cuda")
+    ops.rms_norm(dev(x), dev(w), 1e-6, 1.0, out)
+    ok, _, _, summary = within(out.cpu().numpy(), oracle.rms_norm(x, w, 1e-6, 1.0), 1e-6, 1e-6)
+    assert ok, summary
+    assert (out[0] == 0).all()
+
+
+@pytest.mark.parametrize("kind", [SILU, GELU_TANH, GELU_ERF, SIGMOID, SITU])
+def test_gated(ops, kind):
+    rng = np.random.default_rng(30 + kind)
+    for shape in [(1, 1), (3, 7), (64, 12288)]:
+        g = synthetic.gaussian(rng, *shape) * 3
+        u = synthetic.gaussian(rng, *shape)
+        out = torch.empty(shape, device="cuda")
+        ops.gated(kind, dev(g), dev(u), out)
+        ok, _, _, summary = within(out.cpu().numpy(), oracle.gated(kind, g, u), 1e-6, 1e-5)
+        assert ok, summary  # SmallOpsTests L66, 95-103
+
+
+def test_add_and_gated_in_place(ops):
+    rng = np.random.default_rng(31)
+    a, b = synthetic.gaussian(rng, 1000), synthetic.gaussian(rng, 1000)
+    ad = dev(a)
+    ops.add(ad, dev(b), ad)  # out may be an input
+    assert np.array_equal(ad.cpu().numpy(), (a + b).astype(np.float32))
+
+
+# ---- rotary embedding --------------------------------------------------------------------------
+@pytest.mark.parametrize("layout", [NEOX, INTERLEAVED], ids=["neox", "interleaved"])
+def test_rope_matches_the_cpu_angle(ops, layout):
+    """BASELINE C3: theta 1e6, head_dim 128, positions up to 8191, q [b, 32,
+    128] and k [b, 8, 128]. The reference holds its own kernel to 1e-2
+    (SmallOpsTests L450-500); this one computes the CPU's angle bit for bit
+    and lands within about an ulp."""
+    rng = np.random.default_rng(40 + layout)
+    for tokens, heads in [(1, 32), (16, 8), (64, 32)]:
+        x = synthetic.gaussian(rng, tokens, heads, 128)
+        positions = ((np.arange(tokens) * 131) % 4096).astype(np.int32)
+        positions[-1] = 8191
+        out = torch.empty(x.shape, device="cuda")
+        ops.rope(dev(x), dev(positions), Rope(1e6, 128, layout), out)
+        expected = oracle.rope(x, positions, 1e6, 128, layout)
+        ok, _, max_abs, summary = within(out.cpu().numpy(), expected, 1e-6, 1e-6)
+        assert ok, summary
+
+
+def test_rope_partial_and_known_turns(ops):
+    """ReferenceOpsTests' hand-worked turns, on the GPU."""
+    x = np.array([1, 1, 0, 0], np.float32).reshape(1, 1, 4)
+    out = torch.empty(1, 1, 4, device="cuda")
+    ops.rope(dev(x), dev(np.array([1], np.int32)), Rope(100.0, 4, NEOX), out)
+    expected = [np.cos(1.0), np.cos(0.1), np.sin(1.0), np.sin(0.1)]
+    assert within(out.cpu().numpy(), expected, 1e-6, 0)[0]
+    values = np.arange(1, 7, dtype=np.float32).reshape(1, 1, 6)
+    out = torch.empty(1, 1, 6, device="cuda")
+    ops.rope(dev(values), dev(np.array([7], np.int32)), Rope(1e4, 2, NEOX), out)
+    assert np.array_equal(out.cpu().numpy()[0, 0, 2:], values[0, 0, 2:])
+
+
+# ---- mixture of experts -------------------------------------------------------------------------
+def test_route_matches_oracle(ops):
+    """BASELINE C5: 512 experts, top-10, logits ~ N(0, 1)."""
+    rng = np.random.default_rng(50)
+    for tokens in (1, 16, 64):
+        logits = synthetic.gaussian(rng, tokens, 512)
+        ids = torch.empty(tokens, 10, dtype=torch.int32, device="cuda")
+        weights = torch.empty(tokens, 10, device="cuda")
+        ops.route(dev(logits), ids, weights)
+        e_ids, e_weights = oracle.route(logits, 10)
+        assert np.array_equal(ids.cpu().numpy(), e_ids)
+        assert within(weights.cpu().numpy(), e_weights, 1e-7, 1e-6)[0]
+
+
+def test_route_ties_take_the_lower_expert(ops):
+    logits = np.array([[0.5, 2.0, 2.0, -1.0, 2.0, 0.5]], np.float32)
+    ids = torch.empty(1, 4, dtype=torch.int32, device="cuda")
+    weights = torch.empty(1, 4, device="cuda")
+    ops.route(dev(logits), ids, weights)
+    assert ids.cpu().numpy().tolist() == [[1, 2, 4, 0]]
+
+
+@pytest.mark.parametrize("dtype", [oracle.Q8_0, oracle.Q4_1], ids=lambda t: oracle.NAMES[t])
+def test_experts_linear_and_gated(ops, dtype):
+    """C5 shapes with fewer experts: gate/up [E, 512, 2048], down [E, 2048, 512];
+    b tokens of 10 slots."""
+    rng = np.random.default_rng(60 + dtype)
+    experts, ffn, hidden = 24, 512, 2048
+    gate = synthetic.quantized(rng, dtype, experts * ffn, hidden)
+    up = synthetic.quantized(rng, dtype, experts * ffn, hidden)
+    down = synthetic.quantized(rng, dtype, experts * hidden, ffn)
+    sg = Stored.upload(dtype, (experts, ffn, hidden), gate)
+    su = Stored.upload(dtype, (experts, ffn, hidden), up)
+    sd = Stored.upload(dtype, (experts, hidden, ffn), down)
+    for tokens in (1, 4):
+        x = synthetic.gaussian(rng, tokens, hidden)
+        ids = np.stack([rng.permutation(experts)[:10] for _ in range(tokens)]).astype(np.int32)
+        gated = torch.empty(tokens * 10, ffn, device="cuda")
+        ops.experts_gated_linear(dev(x), sg, su, dev(ids.reshape(-1)), gated)
+        e_gated = oracle.experts_gated_linear(dtype, x, gate, up, experts, ffn, hidden, ids)
+        ok, _, _, summary = within(gated.cpu().numpy(), e_gated, 1e-4, 1e-3)
+        assert ok, summary
+        # down over every slot's own row (divisor 1), fed the oracle's input
+        out = torch.empty(tokens * 10, hidden, device="cuda")
+        ops.experts_linear(dev(e_gated), sd, dev(ids.reshape(-1)), out)
+        e_out = oracle.experts_linear(dtype, e_gated, down, experts, hidden, ffn, ids)
+        ok, _, _, summary = within(out.cpu().numpy(), e_out, 1e-4, 1e-3)
+        assert ok, summary
+
+
+def test_experts_bad_id_is_flagged(ops):
+    rng = np.random.default_rng(61)
+    w = Stored.upload(oracle.Q4_1, (2, 64, 64), synthetic.quantized(rng, oracle.Q4_1, 128, 64))
+    ops.take_device_error()
+    out = torch.zeros(2, 64, device="cuda")
+    ops.experts_linear(dev(synthetic.gaussian(rng, 1, 64)), w, dev(np.array([1, 7], np.int32)),
+                       out)
+    assert ops.take_device_error() == 1
+    result = out.cpu().numpy()
+    assert np.isfinite(result[0]).all() and np.isnan(result[1]).all()
+
+
+def test_moe_combine_and_norm(ops):
+    rng = np.random.default_rng(70)
+    tokens, k, hidden = 4, 10, 2048
+    expert_out = synthetic.gaussian(rng, tokens * k, hidden)
+    weights = rng.random((tokens, k)).astype(np.float32)
+    weights /= weights.sum(axis=1, keepdims=True)
+    residual = synthetic.gaussian(rng, tokens, hidden)
+    shared_out = synthetic.gaussian(rng, tokens, hidden)
+    shared_in = synthetic.gaussian(rng, tokens, hidden)
+    router = (synthetic.gaussian(rng, hidden) * 0.05).astype(np.float32)
+    norm_w = (1 + rng.standard_normal(hidden) * 0.02).astype(np.float32)
+    shared = SharedExpert(dev(shared_out), dev(shared_in), dev(router))
+    out = torch.empty(tokens, hidden, device="cuda")
+    ops.moe_combine(dev(expert_out), dev(weights), shared, dev(residual), out)
+    expected = oracle.moe_combine(expert_out, weights, hidden, shared_out, shared_in, router,
+                                  residual)
+    ok, _, _, summary = within(out.cpu().numpy(), expected, 1e-5, 1e-5)
+    assert ok, summary
+    res = dev(residual)
+    normed = torch.empty(tokens, hidden, device="cuda")
+    ops.moe_combine_norm(dev(expert_out), dev(weights), shared, res,
+                         RowNorm(dev(norm_w), 1e-6, 0.0, normed))
+    e_res, e_norm = oracle.moe_combine_norm(expert_out, weights, hidden, residual, norm_w, 1e-6,
+                                            0.0, shared_out, shared_in, router)
+    assert within(res.cpu().numpy(), e_res, 1e-5, 1e-5)[0]
+    ok, _, _, summary = within(normed.cpu().numpy(), e_norm, 1e-5, 1e-5)
+    assert ok, summary
+    # no shared expert, no residual
+    ops.moe_combine(dev(expert_out), dev(weights), None, None, out)
+    expected = oracle.moe_combine(expert_out, weights, hidden)
+    assert within(out.cpu().numpy(), expected, 1e-5, 1e-5)[0]
