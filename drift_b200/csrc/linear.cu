@@ -18,6 +18,14 @@ int matvec_prepared(int weight_dtype, const void* weight, const uint32_t* record
                     int64_t rows, int64_t cols, int64_t vectors, cudaStream_t stream);
 int matvec_f32_weights(int x_dtype, const void* x, const float* weight, float* y, int64_t m,
                        int64_t n, int64_t k, cudaStream_t stream);
+bool tc_supports(int weight_dtype, const void* weight, int64_t k);
+int linear_tc(int x_dtype, const void* x, int weight_dtype, const void* weight, float* y,
+              int64_t m, int64_t n, int64_t k, cudaStream_t stream);
+
+// From this many rows of x a product is a tensor-core product, as the
+// runner's GemmMinimumRows (ops/HipLinear.scala:14-19); below, the weight is
+// streamed once for all rows of x (up to 8 per pass in the reference).
+constexpr int64_t GEMM_MINIMUM_ROWS = 32;
 
 // Ops.checkLinear, plus what the kernels need of a stored weight.
 static int check_linear(int x_dtype, const void* x, int weight_dtype, const void* weight,
@@ -71,7 +79,9 @@ int drift_linears(int x_dtype, const void* x, int count, const int* weight_dtype
   }
   const cudaStream_t s = cudaStream_t(stream);
   bool quantized = false;
-  for (int i = 0; i < count; ++i) quantized |= weight_dtypes[i] != DRIFT_F32;
+  for (int i = 0; i < count; ++i)
+    quantized |= weight_dtypes[i] != DRIFT_F32 &&
+                 !(m >= GEMM_MINIMUM_ROWS && tc_supports(weight_dtypes[i], weights[i], k));
   uint32_t* records = nullptr;
   if (quantized) {
     void* w = nullptr;
@@ -84,6 +94,8 @@ int drift_linears(int x_dtype, const void* x, int count, const int* weight_dtype
     if (weight_dtypes[i] == DRIFT_F32)
       DRIFT_TRY(matvec_f32_weights(x_dtype, x, static_cast<const float*>(weights[i]), outs[i], m,
                                    ns[i], k, s));
+    else if (m >= GEMM_MINIMUM_ROWS && tc_supports(weight_dtypes[i], weights[i], k))
+      DRIFT_TRY(linear_tc(x_dtype, x, weight_dtypes[i], weights[i], outs[i], m, ns[i], k, s));
     else
       DRIFT_TRY(matvec_prepared(weight_dtypes[i], weights[i], records, outs[i], ns[i], k, m, s));
   }

@@ -1,13 +1,18 @@
 """Quantized products on the GPU against the CPU oracle (the reference's
 LinearTests, runner/gpuTest/src/drift/runner/LinearTests.scala, on this path).
 
-Each case is held to two bars:
+Up to 31 rows of x (the reference's matrix-vector path, float x) each case is
+held to two bars:
 - BASELINE's: |gpu - oracle| <= 1e-4 + 1e-3 |oracle|;
 - the rigorous bound of the x preparation: x enters as exact integers 21 bits
   below each 32-value block's largest |x| (drift_b200/csrc/quant.cuh), so an
   output can move by at most sum_k |w_k| * max|x_block| * 2^-21, plus float
   rounding of the sums, 1e-5 of the output scale (the reference's own
   float-x tolerance, LinearTests.scala:154-157).
+From 32 rows on, a product is the reference's GEMM path (weights dequantized to
+F16, x rounded to F16, F32 accumulation: ops/HipLinear.scala:389-469), here on
+the tcgen05 tensor cores, and is held to the reference's own bound for it
+(LinearTests.scala:139-147): |gpu - oracle| <= (2 sum|w x| + |y|) 2^-11 1.01.
 """
 
 import numpy as np
@@ -42,6 +47,12 @@ def bound(decoded: np.ndarray, x: np.ndarray) -> np.ndarray:
     return (block_max.astype(np.float64) @ per_block.T.astype(np.float64)) * 2.0 ** -21
 
 
+def gemm_bound(decoded: np.ndarray, x: np.ndarray, expected: np.ndarray) -> np.ndarray:
+    """(2 sum_k |w_k x_k| + |y|) 2^-11 1.01 per output [m, n]."""
+    sums = np.abs(x.astype(np.float64)) @ np.abs(decoded.astype(np.float64)).T
+    return (2 * sums + np.abs(expected)) * 2.0 ** -11 * 1.01
+
+
 def run_case(ops, dtype, m, n, k, seed, x_bf16: bool, law: str):
     rng = np.random.default_rng(seed)
     if law == "tests":
@@ -74,6 +85,18 @@ def test_linear_matches_oracle(ops, dtype, case, x_bf16):
     for law in ("tests", "bench"):
         actual, expected, limit = run_case(ops, dtype, m, n, k, seed=hash(case) % 1000,
                                            x_bf16=x_bf16, law=law)
+        if m >= 32:
+            rng = np.random.default_rng(hash(case) % 1000)
+            w = (synthetic.random_blocks if law == "tests" else synthetic.quantized)(
+                rng, dtype, n, k)
+            x32 = synthetic.gaussian(rng, m, k)
+            x_eff = synthetic.bf16_values(synthetic.bf16_bits(x32)) if x_bf16 else x32
+            decoded = oracle.decode(dtype, w, n * k).reshape(n, k)
+            err = np.abs(actual.astype(np.float64) - expected)
+            bound = gemm_bound(decoded, x_eff, expected)
+            assert (err <= bound).all(), \
+                f"{law} weights: worst at {(err / bound).max():.2f} of the GEMM bound"
+            continue
         ok, _, _, summary = within(actual, expected, 1e-4, 1e-3)
         assert ok, f"{law} weights: {summary}"
         scale = np.abs(expected).max()
@@ -132,8 +155,15 @@ def test_full_size_q4_1_sampled_rows(ops, shape, m):
     rows = np.unique(np.concatenate([[0, n - 1], rng.integers(0, n, 200)]))
     expected = oracle.linear_rows(oracle.Q4_1, x_eff, w, n, k, rows)
     actual = out.cpu().numpy()[:, rows]
-    ok, _, _, summary = within(actual, expected, 1e-4, 1e-3)
-    assert ok, summary
+    if m >= 32:
+        decoded = np.stack([oracle.decode(oracle.Q4_1, w[r * (k // 32) * 20:(r + 1) * (k // 32) * 20], k)
+                            for r in rows])
+        err = np.abs(actual.astype(np.float64) - expected)
+        bound = gemm_bound(decoded, x_eff, expected)
+        assert (err <= bound).all(), f"worst at {(err / bound).max():.2f} of the GEMM bound"
+    else:
+        ok, _, _, summary = within(actual, expected, 1e-4, 1e-3)
+        assert ok, summary
     assert torch.isfinite(out).all()
 
 
