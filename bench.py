@@ -68,7 +68,10 @@ def measured_peaks() -> dict:
 
 # ---- clocks ---------------------------------------------------------------------------------
 class ClockSampler:
-    """nvidia-smi clock and throttle samples while the timed region runs."""
+    """nvidia-smi clock and throttle samples (every 20 ms, each stamped on
+    arrival) from before the timed region to after it; the summary keeps the
+    samples inside the region, or the nearest ones when it is shorter than
+    the sampling period."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -76,30 +79,38 @@ class ClockSampler:
 
     def __init__(self, device: int):
         self.device = device
-        self.samples: list[list[str]] = []
-        self._stop = threading.Event()
+        self.samples: list[tuple[float, list[str]]] = []
         self._proc = None
         self._thread = None
+        self.window = (0.0, 0.0)
 
     def start(self):
         try:
             self._proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "--format=csv,noheader,nounits", "-lms", "20"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True, bufsize=1)
         except (FileNotFoundError, OSError):
             self._proc = None
             return
         self._thread = threading.Thread(target=self._read, daemon=True)
         self._thread.start()
+        # let the first samples arrive before the timed region starts
+        deadline = time.time() + 3.0
+        while not self.samples and time.time() < deadline:
+            time.sleep(0.02)
 
     def _read(self):
         for line in self._proc.stdout:
-            self.samples.append([c.strip() for c in line.split(",")])
+            self.samples.append((time.time(), [c.strip() for c in line.split(",")]))
+
+    def mark(self, begin: float, end: float):
+        self.window = (begin, end)
 
     def stop(self) -> dict:
         if self._proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.1)
         self._proc.terminate()
         try:
             self._proc.wait(timeout=5)
@@ -107,12 +118,18 @@ class ClockSampler:
             self._proc.kill()
         if self._thread:
             self._thread.join(timeout=5)
-        sm, sm_max, reasons = [], [], set()
+        begin, end = self.window
+        inside = [s for t, s in self.samples if begin - 0.025 <= t <= end + 0.025]
+        if not inside and self.samples:
+            middle = (begin + end) / 2
+            inside = [min(self.samples, key=lambda ts: abs(ts[0] - middle))[1]]
+        sm, sm_max, power, reasons = [], [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for s in self.samples:
+        for s in inside:
             try:
                 sm.append(float(s[1]))
                 sm_max.append(float(s[2]))
+                power.append(float(s[3]))
             except (ValueError, IndexError):
                 continue
             for name, value in zip(names, s[5:9]):
@@ -120,7 +137,9 @@ class ClockSampler:
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(sm_max) if sm_max else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "power_w_max": max(power) if power else None,
+                "reasons": sorted(reasons), "samples": len(sm),
+                "timed_region_s": round(end - begin, 4)}
 
 
 # ---- the GPU arm ------------------------------------------------------------------------------
@@ -187,11 +206,13 @@ def run_gpu(args) -> dict | None:
     clocks = ClockSampler(local)
     clocks.start()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    wall_begin = time.time()
     start.record()
     for _ in range(args.steps):
         graph.replay()
     end.record()
     torch.cuda.synchronize()
+    clocks.mark(wall_begin, time.time())
     clock_info = clocks.stop()
     elapsed_ms = start.elapsed_time(end)
     barrier()
@@ -459,7 +480,7 @@ def run_reference(args) -> dict | None:
 def main() -> int:
     parser = argparse.ArgumentParser()
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--steps", type=int, default=100)
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", default="drift_b200")
     parser.add_argument("--cpu-seconds", type=float, default=10.0)

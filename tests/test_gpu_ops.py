@@ -196,12 +196,26 @@ def test_experts_linear_and_gated(ops, dtype):
     sg = Stored.upload(dtype, (experts, ffn, hidden), gate)
     su = Stored.upload(dtype, (experts, ffn, hidden), up)
     sd = Stored.upload(dtype, (experts, hidden, ffn), down)
+    # x scaled so the gate pre-activations are O(1), as a normed layer input
+    # makes them: at the raw law's scale (sigma ~ 36 for Q8_0 at K = 2048)
+    # silu'(g) * up amplifies any float32 rounding of g near g = 0 past 1e-4
+    w_rms = np.sqrt(np.mean(oracle.decode(dtype, gate[:ffn * hidden // 32 * synthetic.BLOCK_BYTES[dtype]],
+                                          ffn * hidden) ** 2))
+    x_scale = 1.0 / (np.sqrt(hidden) * w_rms)
     for tokens in (1, 4):
         x = synthetic.gaussian(rng, tokens, hidden)
         ids = np.stack([rng.permutation(experts)[:10] for _ in range(tokens)]).astype(np.int32)
+        # the plain products at the raw scale: fp32-accumulated outputs
+        g_out = torch.empty(tokens * 10, ffn, device="cuda")
+        ops.experts_linear(dev(x), sg, dev(ids.reshape(-1)), g_out)
+        e_g = oracle.experts_linear(dtype, x, gate, experts, ffn, hidden, ids)
+        ok, _, _, summary = within(g_out.cpu().numpy(), e_g, 1e-4, 1e-3)
+        assert ok, summary
+        # the gated product (one launch) at a unit pre-activation scale
+        xs = (x * x_scale).astype(np.float32)
         gated = torch.empty(tokens * 10, ffn, device="cuda")
-        ops.experts_gated_linear(dev(x), sg, su, dev(ids.reshape(-1)), gated)
-        e_gated = oracle.experts_gated_linear(dtype, x, gate, up, experts, ffn, hidden, ids)
+        ops.experts_gated_linear(dev(xs), sg, su, dev(ids.reshape(-1)), gated)
+        e_gated = oracle.experts_gated_linear(dtype, xs, gate, up, experts, ffn, hidden, ids)
         ok, _, _, summary = within(gated.cpu().numpy(), e_gated, 1e-4, 1e-3)
         assert ok, summary
         # down over every slot's own row (divisor 1), fed unit-scale activations
