@@ -206,6 +206,201 @@ __global__ void __launch_bounds__(256) matvec_x22_kernel(const uint8_t* __restri
   }
 }
 
+// ---- 3 to 8 vectors: the same exact sums on the integer tensor cores -------------------------
+// mma.sync m16n8k32 (8-bit in, 32-bit integer accumulate) meets a 16-row x
+// 32-column tile of codes with the byte planes of 8 vectors: three MMAs per
+// 32-block (planes 0, 1 unsigned, plane 2 signed), then the same float
+// epilogue per block and output as block_dot. The fragment layouts line up
+// with GGML's blocks: thread (g = lane / 4, t = lane % 4) holds columns
+// 4t..4t+3 and 16+4t..16+4t+3 of rows g and g+8 -- word t of a Q4 block's
+// nibbles, masked low and high -- and the same columns of vector g's planes.
+template <bool SIGNED_A, bool SIGNED_B>
+__device__ __forceinline__ void mma_i8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                       uint32_t b1) {
+  if (SIGNED_A && SIGNED_B)
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  else if (SIGNED_A)
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  else if (SIGNED_B)
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  else
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// A row's part of block `c` as this thread's fragment needs it: the codes of
+// values 4t..4t+3 (lo) and 16+4t..16+4t+3 (hi), and the block's d and m.
+template <typename T>
+__device__ __forceinline__ void fragment_row(const uint8_t* __restrict__ row, int c, int t,
+                                             uint32_t& lo, uint32_t& hi, float& d, float& m) {
+  const int start = c * T::BYTES;
+  const uint32_t* words = reinterpret_cast<const uint32_t*>(row + (start & ~3));
+  const int off = start & 3;  // 0, or 2 for the 2-byte aligned Q8_0 / Q4_0 blocks
+  if (T::DTYPE == DRIFT_Q4_1) {
+    const uint32_t head = __ldg(words);
+    const uint32_t w = __ldg(words + 1 + t);
+    d = half_bits_to_float(head);
+    m = half_bits_to_float(head >> 16);
+    lo = w & 0x0F0F0F0Fu;
+    hi = (w >> 4) & 0x0F0F0F0Fu;
+  } else if (T::DTYPE == DRIFT_Q4_0) {
+    // nibbles start 2 bytes in: word t of them spans aligned words t, t+1
+    // (off 0, shift 16) or is aligned word t+1 (off 2)
+    const uint32_t head = __ldg(words);
+    const uint32_t w0 = __ldg(words + t + (off >> 1)), w1 = __ldg(words + t + 1);
+    const uint32_t w = off ? w1 : __funnelshift_r(w0, w1, 16);
+    d = half_bits_to_float(off ? (head >> 16) : head);
+    m = 0.0f;
+    lo = w & 0x0F0F0F0Fu;
+    hi = (w >> 4) & 0x0F0F0F0Fu;
+  } else {
+    const uint32_t head = __ldg(words);
+    const uint32_t a0 = __ldg(words + t + (off >> 1)), a1 = __ldg(words + t + 1);
+    const uint32_t b0 = __ldg(words + t + 4 + (off >> 1)), b1 = __ldg(words + t + 5);
+    lo = off ? a1 : __funnelshift_r(a0, a1, 16);
+    hi = off ? b1 : __funnelshift_r(b0, b1, 16);
+    d = half_bits_to_float(off ? (head >> 16) : head);
+    m = 0.0f;
+  }
+}
+
+// One output's share of a block: the three plane sums joined, scaled.
+template <typename T>
+__device__ __forceinline__ float mma_block_value(int p0, int p1, int p2, float d, float m, float s,
+                                                 int sum_x) {
+  if (T::DTYPE == DRIFT_Q8_0) {
+    return s * d * fmaf(256.0f, float(p1 + (p2 << 8)), float(p0));
+  } else if (T::DTYPE == DRIFT_Q4_0) {
+    return s * d * float(p0 + (p1 << 8) + (p2 << 16) - 8 * sum_x);
+  } else {
+    return s * fmaf(d, float(p0 + (p1 << 8) + (p2 << 16)), m * float(sum_x));
+  }
+}
+
+// Grid: ceil(rows / (16 MT (8 / KS))) CTAs of 256 threads. Warp (group, kw)
+// takes rows [16 MT group, +16 MT) of the CTA's and the kw-th contiguous
+// share of the blocks; vectors <= 8 x records at `records`.
+template <typename T, int MT, int KS>
+__global__ void __launch_bounds__(256) matvec_mma_kernel(const uint8_t* __restrict__ weight,
+                                                         const uint32_t* __restrict__ records,
+                                                         float* __restrict__ y, int rows, int cols,
+                                                         int vectors) {
+  constexpr int GROUPS = 8 / KS;
+  constexpr int ROWS = 16 * MT;
+  __shared__ float partial[KS][GROUPS][ROWS][8];
+  const int warp = threadIdx.x / WARP, lane = threadIdx.x % WARP;
+  const int kw = warp % KS, group = warp / KS;
+  const int g = lane / 4, t = lane % 4;
+  const int blocks = cols / 32;
+  const long long row_bytes = (long long)blocks * T::BYTES;
+  const int row0 = (blockIdx.x * GROUPS + group) * ROWS;
+  const int first = int((long long)blocks * kw / KS), end = int((long long)blocks * (kw + 1) / KS);
+
+  float acc[MT][4];
+#pragma unroll
+  for (int i = 0; i < MT; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+
+  // rows of this thread's fragments, clamped to the matrix (their results
+  // are dropped)
+  const uint8_t* row_ptr[MT][2];
+#pragma unroll
+  for (int i = 0; i < MT; ++i)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      int r = row0 + 16 * i + g + 8 * h;
+      r = r < rows ? r : rows - 1;
+      row_ptr[i][h] = weight + (long long)r * row_bytes;
+    }
+  const bool have_vector = g < vectors;
+  const uint32_t* rec_g = records + (long long)g * blocks * X_RECORD_WORDS;
+  const uint32_t* rec_v0 = records + (long long)(2 * t) * blocks * X_RECORD_WORDS;
+  const uint32_t* rec_v1 = records + (long long)(2 * t + 1) * blocks * X_RECORD_WORDS;
+  const bool have_v0 = 2 * t < vectors, have_v1 = 2 * t + 1 < vectors;
+
+  if (row0 < rows) {
+    for (int c = first; c < end; ++c) {
+      uint32_t b[3][2] = {{0, 0}, {0, 0}, {0, 0}};
+      if (have_vector) {
+        const uint32_t* r = rec_g + (long long)c * X_RECORD_WORDS;
+#pragma unroll
+        for (int p = 0; p < 3; ++p) {
+          b[p][0] = __ldg(r + 8 * p + t);
+          b[p][1] = __ldg(r + 8 * p + 4 + t);
+        }
+      }
+      float s0 = 0.0f, s1 = 0.0f;
+      int x0 = 0, x1 = 0;
+      if (have_v0) {
+        const uint2 v = __ldg(reinterpret_cast<const uint2*>(rec_v0 + (long long)c * X_RECORD_WORDS + 24));
+        s0 = __uint_as_float(v.x);
+        x0 = int(v.y);
+      }
+      if (have_v1) {
+        const uint2 v = __ldg(reinterpret_cast<const uint2*>(rec_v1 + (long long)c * X_RECORD_WORDS + 24));
+        s1 = __uint_as_float(v.x);
+        x1 = int(v.y);
+      }
+#pragma unroll
+      for (int i = 0; i < MT; ++i) {
+        uint32_t lo0, hi0, lo1, hi1;
+        float d0, m0, d1, m1;
+        fragment_row<T>(row_ptr[i][0], c, t, lo0, hi0, d0, m0);
+        fragment_row<T>(row_ptr[i][1], c, t, lo1, hi1, d1, m1);
+        const uint32_t a[4] = {lo0, lo1, hi0, hi1};
+        int p[3][4];
+#pragma unroll
+        for (int q = 0; q < 3; ++q) {
+          p[q][0] = p[q][1] = p[q][2] = p[q][3] = 0;
+          if (q < 2)
+            mma_i8<T::SIGNED, false>(p[q], a, b[q][0], b[q][1]);
+          else
+            mma_i8<T::SIGNED, true>(p[q], a, b[q][0], b[q][1]);
+        }
+        // outputs (row g, vector 2t), (g, 2t+1), (g+8, 2t), (g+8, 2t+1)
+        acc[i][0] += mma_block_value<T>(p[0][0], p[1][0], p[2][0], d0, m0, s0, x0);
+        acc[i][1] += mma_block_value<T>(p[0][1], p[1][1], p[2][1], d0, m0, s1, x1);
+        acc[i][2] += mma_block_value<T>(p[0][2], p[1][2], p[2][2], d1, m1, s0, x0);
+        acc[i][3] += mma_block_value<T>(p[0][3], p[1][3], p[2][3], d1, m1, s1, x1);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < MT; ++i) {
+    partial[kw][group][16 * i + g][2 * t] = acc[i][0];
+    partial[kw][group][16 * i + g][2 * t + 1] = acc[i][1];
+    partial[kw][group][16 * i + g + 8][2 * t] = acc[i][2];
+    partial[kw][group][16 * i + g + 8][2 * t + 1] = acc[i][3];
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < GROUPS * ROWS * 8; e += blockDim.x) {
+    const int gi = e / (ROWS * 8), r = (e / 8) % ROWS, v = e % 8;
+    const int row = (blockIdx.x * GROUPS + gi) * ROWS + r;
+    if (row < rows && v < vectors) {
+      float total = 0.0f;
+#pragma unroll
+      for (int k = 0; k < KS; ++k) total += partial[k][gi][r][v];
+      y[(long long)v * rows + row] = total;
+    }
+  }
+}
+
 // ---- by-name kernels ------------------------------------------------------------------
 // Every instantiation, for hosts that launch by name (drift_module_get_function
 // with a NULL module): matvec_x22_<type>_v<V>_ks<KS>, 256 threads, grid
@@ -217,6 +412,14 @@ __global__ void __launch_bounds__(256) matvec_x22_kernel(const uint8_t* __restri
   DRIFT_REGISTER(matvec_x22_##name##_v2_ks1, (matvec_x22_kernel<T, 2, 1>))    \
   DRIFT_REGISTER(matvec_x22_##name##_v2_ks2, (matvec_x22_kernel<T, 2, 2>))    \
   DRIFT_REGISTER(matvec_x22_##name##_v2_ks4, (matvec_x22_kernel<T, 2, 4>))
+#define DRIFT_MMA_REGISTER(T, name)                                               \
+  DRIFT_REGISTER(matvec_mma_##name##_mt2_ks1, (matvec_mma_kernel<T, 2, 1>))       \
+  DRIFT_REGISTER(matvec_mma_##name##_mt2_ks2, (matvec_mma_kernel<T, 2, 2>))       \
+  DRIFT_REGISTER(matvec_mma_##name##_mt2_ks4, (matvec_mma_kernel<T, 2, 4>))       \
+  DRIFT_REGISTER(matvec_mma_##name##_mt1_ks8, (matvec_mma_kernel<T, 1, 8>))
+DRIFT_MMA_REGISTER(Q8_0T, q8_0)
+DRIFT_MMA_REGISTER(Q4_0T, q4_0)
+DRIFT_MMA_REGISTER(Q4_1T, q4_1)
 DRIFT_MATVEC_REGISTER(Q8_0T, q8_0)
 DRIFT_MATVEC_REGISTER(Q4_0T, q4_0)
 DRIFT_MATVEC_REGISTER(Q4_1T, q4_1)
@@ -285,10 +488,49 @@ static int launch_matvec_v(const uint8_t* weight, const uint32_t* records, float
 }
 
 template <typename T>
+static int launch_mma(const uint8_t* weight, const uint32_t* records, float* y, int rows, int cols,
+                      int vectors, cudaStream_t stream) {
+  const int blocks = cols / 32;
+  // enough warps for every SM: split the blocks between more warps when the
+  // matrix has few rows
+  const long long groups32 = (rows + 31) / 32;
+  int ks = 1;
+  while (ks < 4 && groups32 * ks < 8LL * sm_count() && blocks / (ks * 2) >= 8) ks *= 2;
+  if (rows <= 2048 && blocks >= 64) {
+    const unsigned grid = unsigned((rows + 16 - 1) / 16);  // MT 1, 8 k-splits, 16 rows per CTA
+    matvec_mma_kernel<T, 1, 8><<<grid, 256, 0, stream>>>(weight, records, y, rows, cols, vectors);
+  } else if (ks == 4) {
+    const unsigned grid = unsigned((rows + 64 - 1) / 64);
+    matvec_mma_kernel<T, 2, 4><<<grid, 256, 0, stream>>>(weight, records, y, rows, cols, vectors);
+  } else if (ks == 2) {
+    const unsigned grid = unsigned((rows + 128 - 1) / 128);
+    matvec_mma_kernel<T, 2, 2><<<grid, 256, 0, stream>>>(weight, records, y, rows, cols, vectors);
+  } else {
+    const unsigned grid = unsigned((rows + 256 - 1) / 256);
+    matvec_mma_kernel<T, 2, 1><<<grid, 256, 0, stream>>>(weight, records, y, rows, cols, vectors);
+  }
+  DRIFT_LAUNCHED("matvec_mma");
+  return 0;
+}
+
+template <typename T>
 static int launch_matvec(const uint8_t* weight, const uint32_t* records, float* y, int rows,
                          int cols, int vectors, cudaStream_t stream) {
-  // vectors in passes of MAX_V over the weight
   const int blocks = cols / 32;
+  // passes of up to 8 vectors on the integer tensor cores: one kernel for
+  // every batch, whose block order depends on the matrix only, so a row sums
+  // to the same bits alone or beside 7 others (the runner's guarantee that a
+  // verification's tokens get a decode step's logits, ops/HipLinear.scala:
+  // 197-201)
+  if (vectors >= 1) {
+    for (int first = 0; first < vectors; first += 8) {
+      const int count = vectors - first < 8 ? vectors - first : 8;
+      DRIFT_TRY(launch_mma<T>(weight, records + (long long)first * blocks * X_RECORD_WORDS,
+                              y + (long long)first * rows, rows, cols, count, stream));
+    }
+    return 0;
+  }
+  // (the dp4a kernels above stay for by-name callers)
   for (int first = 0; first < vectors; first += MAX_V) {
     const int count = vectors - first < MAX_V ? vectors - first : MAX_V;
     const uint32_t* rec = records + (long long)first * blocks * X_RECORD_WORDS;
