@@ -19,6 +19,7 @@
 #include <cuda_runtime.h>
 
 #include "common.cuh"
+#include "mma_i8.cuh"
 #include "quant.cuh"
 #include "registry.cuh"
 
@@ -203,92 +204,6 @@ __global__ void __launch_bounds__(256) matvec_x22_kernel(const uint8_t* __restri
       for (int k = 0; k < KS; ++k) total += partial[g * KS + k][r][v];
       y[(long long)v * rows + row] = total;
     }
-  }
-}
-
-// ---- 3 to 8 vectors: the same exact sums on the integer tensor cores -------------------------
-// mma.sync m16n8k32 (8-bit in, 32-bit integer accumulate) meets a 16-row x
-// 32-column tile of codes with the byte planes of 8 vectors: three MMAs per
-// 32-block (planes 0, 1 unsigned, plane 2 signed), then the same float
-// epilogue per block and output as block_dot. The fragment layouts line up
-// with GGML's blocks: thread (g = lane / 4, t = lane % 4) holds columns
-// 4t..4t+3 and 16+4t..16+4t+3 of rows g and g+8 -- word t of a Q4 block's
-// nibbles, masked low and high -- and the same columns of vector g's planes.
-template <bool SIGNED_A, bool SIGNED_B>
-__device__ __forceinline__ void mma_i8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0,
-                                       uint32_t b1) {
-  if (SIGNED_A && SIGNED_B)
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-  else if (SIGNED_A)
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-  else if (SIGNED_B)
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-  else
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// A row's part of block `c` as this thread's fragment needs it: the codes of
-// values 4t..4t+3 (lo) and 16+4t..16+4t+3 (hi), and the block's d and m.
-template <typename T>
-__device__ __forceinline__ void fragment_row(const uint8_t* __restrict__ row, int c, int t,
-                                             uint32_t& lo, uint32_t& hi, float& d, float& m) {
-  const int start = c * T::BYTES;
-  const uint32_t* words = reinterpret_cast<const uint32_t*>(row + (start & ~3));
-  const int off = start & 3;  // 0, or 2 for the 2-byte aligned Q8_0 / Q4_0 blocks
-  if (T::DTYPE == DRIFT_Q4_1) {
-    const uint32_t head = __ldg(words);
-    const uint32_t w = __ldg(words + 1 + t);
-    d = half_bits_to_float(head);
-    m = half_bits_to_float(head >> 16);
-    lo = w & 0x0F0F0F0Fu;
-    hi = (w >> 4) & 0x0F0F0F0Fu;
-  } else if (T::DTYPE == DRIFT_Q4_0) {
-    // nibbles start 2 bytes in: word t of them spans aligned words t, t+1
-    // (off 0, shift 16) or is aligned word t+1 (off 2)
-    const uint32_t head = __ldg(words);
-    const uint32_t w0 = __ldg(words + t + (off >> 1)), w1 = __ldg(words + t + 1);
-    const uint32_t w = off ? w1 : __funnelshift_r(w0, w1, 16);
-    d = half_bits_to_float(off ? (head >> 16) : head);
-    m = 0.0f;
-    lo = w & 0x0F0F0F0Fu;
-    hi = (w >> 4) & 0x0F0F0F0Fu;
-  } else {
-    const uint32_t head = __ldg(words);
-    const uint32_t a0 = __ldg(words + t + (off >> 1)), a1 = __ldg(words + t + 1);
-    const uint32_t b0 = __ldg(words + t + 4 + (off >> 1)), b1 = __ldg(words + t + 5);
-    lo = off ? a1 : __funnelshift_r(a0, a1, 16);
-    hi = off ? b1 : __funnelshift_r(b0, b1, 16);
-    d = half_bits_to_float(off ? (head >> 16) : head);
-    m = 0.0f;
-  }
-}
-
-// One output's share of a block: the three plane sums joined, scaled.
-template <typename T>
-__device__ __forceinline__ float mma_block_value(int p0, int p1, int p2, float d, float m, float s,
-                                                 int sum_x) {
-  if (T::DTYPE == DRIFT_Q8_0) {
-    return s * d * fmaf(256.0f, float(p1 + (p2 << 8)), float(p0));
-  } else if (T::DTYPE == DRIFT_Q4_0) {
-    return s * d * float(p0 + (p1 << 8) + (p2 << 16) - 8 * sum_x);
-  } else {
-    return s * fmaf(d, float(p0 + (p1 << 8) + (p2 << 16)), m * float(sum_x));
   }
 }
 
@@ -543,9 +458,24 @@ static int launch_matvec(const uint8_t* weight, const uint32_t* records, float* 
   return 0;
 }
 
+bool ring_supports(int weight_dtype, const void* weight, int64_t k);
+int matvec_ring(int weight_dtype, const void* weight, const uint32_t* records, float* y,
+                int64_t rows, int64_t cols, int64_t vectors, cudaStream_t stream);
+
 // The quantized product of prepared x; `vectors` rows of x, y [vectors, rows].
+// Weights whose rows are whole 16-byte units stream through shared memory
+// (matvec_ring.cu); the rest are read straight from global memory.
 int matvec_prepared(int weight_dtype, const void* weight, const uint32_t* records, float* y,
                     int64_t rows, int64_t cols, int64_t vectors, cudaStream_t stream) {
+  if (ring_supports(weight_dtype, weight, cols)) {
+    const int64_t blocks = cols / 32;
+    for (int64_t first = 0; first < vectors; first += 8) {
+      const int64_t count = vectors - first < 8 ? vectors - first : 8;
+      DRIFT_TRY(matvec_ring(weight_dtype, weight, records + first * blocks * X_RECORD_WORDS,
+                            y + first * rows, rows, cols, count, stream));
+    }
+    return 0;
+  }
   const uint8_t* w = static_cast<const uint8_t*>(weight);
   switch (weight_dtype) {
     case DRIFT_Q8_0: return launch_matvec<Q8_0T>(w, records, y, int(rows), int(cols), int(vectors), stream);
