@@ -31,6 +31,7 @@
 #include "quant.cuh"
 #include "registry.cuh"
 #include "tc_common.cuh"
+#include "tma_host.cuh"
 
 namespace drift {
 
@@ -373,24 +374,6 @@ DRIFT_REGISTER(linear_tc_q4_0, linear_tc_kernel<Q4_0T>)
 DRIFT_REGISTER(linear_tc_q4_1, linear_tc_kernel<Q4_1T>)
 
 // ---- host ---------------------------------------------------------------------------------------
-typedef CUresult (*EncodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiled encode_tiled() {
-  static EncodeTiled fn = nullptr;
-  if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiled>(p);
-  }
-  return fn;
-}
-
 template <typename T>
 static int launch_tc(int x_dtype, const void* x, const void* weight, float* y, int64_t m,
                      int64_t n, int64_t k, cudaStream_t stream) {
@@ -411,32 +394,10 @@ static int launch_tc(int x_dtype, const void* x, const void* weight, float* y, i
                                                                             int(padded), int(k));
     DRIFT_LAUNCHED("tc_prepare_x");
   }
-  EncodeTiled encode = encode_tiled();
-  if (!encode) return invalid("cuTensorMapEncodeTiled is not available from the driver");
   const int64_t row_bytes = k / 32 * T::BYTES;
   CUtensorMap wmap, xmap;
-  {
-    const cuuint64_t dims[2] = {cuuint64_t(row_bytes / 4), cuuint64_t(n)};
-    const cuuint64_t strides[1] = {cuuint64_t(row_bytes)};
-    const cuuint32_t box[2] = {cuuint32_t(Unpack<T>::RAW_WORDS), cuuint32_t(TILE_ROWS)};
-    const cuuint32_t element[2] = {1, 1};
-    const CUresult r = encode(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(weight),
-                              dims, strides, box, element, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return invalid("weight tensor map refused (CUresult %d)", int(r));
-  }
-  {
-    const cuuint64_t dims[2] = {cuuint64_t(k), cuuint64_t(padded)};
-    const cuuint64_t strides[1] = {cuuint64_t(k * 2)};
-    const cuuint32_t box[2] = {cuuint32_t(STEP), cuuint32_t(TILE_VECTORS)};
-    const cuuint32_t element[2] = {1, 1};
-    const CUresult r = encode(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xh, dims, strides, box,
-                              element, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return invalid("x tensor map refused (CUresult %d)", int(r));
-  }
+  DRIFT_TRY(encode_word_rows(&wmap, weight, row_bytes / 4, n, Unpack<T>::RAW_WORDS, TILE_ROWS));
+  DRIFT_TRY(encode_f16_sw128(&xmap, xh, k, padded, TILE_VECTORS));
   static bool configured[3] = {false, false, false};
   const int which = T::DTYPE == DRIFT_Q8_0 ? 0 : (T::DTYPE == DRIFT_Q4_0 ? 1 : 2);
   if (!configured[which]) {
@@ -462,7 +423,7 @@ bool tc_supports(int weight_dtype, const void* weight, int64_t k) {
     return false;
   const int64_t row = byte_size(weight_dtype, k);
   return row > 0 && row % 16 == 0 && (reinterpret_cast<uintptr_t>(weight) & 15) == 0 &&
-         encode_tiled() != nullptr;
+         tensor_maps_available();
 }
 
 int linear_tc(int x_dtype, const void* x, int weight_dtype, const void* weight, float* y,

@@ -14,8 +14,11 @@ int workspace_reserve(size_t bytes, void** pointer);
 size_t linear_workspace_bytes(int64_t m, int64_t k);
 int prepare_x(int x_dtype, const void* x, int64_t m, int64_t k, uint32_t* records,
               cudaStream_t stream);
-int matvec_prepared(int weight_dtype, const void* weight, const uint32_t* records, float* y,
+int matvec_prepared(int weight_dtype, const void* weight, const uint8_t* records, float* y,
                     int64_t rows, int64_t cols, int64_t vectors, cudaStream_t stream);
+size_t mma_workspace_bytes(int64_t m, int64_t k);
+int prepare_x_mma(int x_dtype, const void* x, int64_t m, int64_t k, uint8_t* records,
+                  cudaStream_t stream);
 int matvec_f32_weights(int x_dtype, const void* x, const float* weight, float* y, int64_t m,
                        int64_t n, int64_t k, cudaStream_t stream);
 bool tc_supports(int weight_dtype, const void* weight, int64_t k);
@@ -59,7 +62,12 @@ using namespace drift;
 
 extern "C" {
 
-size_t drift_linear_workspace_bytes(int64_t m, int64_t k) { return linear_workspace_bytes(m, k); }
+size_t drift_linear_workspace_bytes(int64_t m, int64_t k) {
+  // the largest of the products' scratch: x records (either layout), or F16 x
+  const size_t a = linear_workspace_bytes(m, k), b = mma_workspace_bytes(m, k);
+  const size_t c = size_t((m + 63) / 64 * 64) * size_t(k) * 2;
+  return a > b ? (a > c ? a : c) : (b > c ? b : c);
+}
 
 int drift_workspace_reserve(size_t bytes) { return workspace_reserve(bytes, nullptr); }
 
@@ -82,12 +90,12 @@ int drift_linears(int x_dtype, const void* x, int count, const int* weight_dtype
   for (int i = 0; i < count; ++i)
     quantized |= weight_dtypes[i] != DRIFT_F32 &&
                  !(m >= GEMM_MINIMUM_ROWS && tc_supports(weight_dtypes[i], weights[i], k));
-  uint32_t* records = nullptr;
+  uint8_t* records = nullptr;
   if (quantized) {
     void* w = nullptr;
-    DRIFT_TRY(workspace_reserve(linear_workspace_bytes(m, k), &w));
-    records = static_cast<uint32_t*>(w);
-    DRIFT_TRY(prepare_x(x_dtype, x, m, k, records, s));  // one preparation for all
+    DRIFT_TRY(workspace_reserve(mma_workspace_bytes(m, k), &w));
+    records = static_cast<uint8_t*>(w);
+    DRIFT_TRY(prepare_x_mma(x_dtype, x, m, k, records, s));  // one preparation for all
   }
   for (int i = 0; i < count; ++i) {
     if (ns[i] == 0) continue;

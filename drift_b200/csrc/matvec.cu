@@ -90,6 +90,58 @@ extern "C" __global__ void __launch_bounds__(256)
   quantize_x22_block<true>(x, records, block);
 }
 
+// The same preparation into the MMA layout (mma_i8.cuh): block `block` of
+// vector v (pass v / 8, slot g = v % 8).
+template <bool BF16>
+__global__ void __launch_bounds__(256) quantize_x22_mma_kernel(const void* x, uint8_t* records,
+                                                              int vectors, int blocks) {
+  const long long index = (long long)blockIdx.x * (blockDim.x / WARP) + threadIdx.x / WARP;
+  const int passes = (vectors + 7) / 8;
+  if (index >= (long long)passes * 8 * blocks) return;
+  const int lane = threadIdx.x % WARP;
+  const int block = int(index % blocks);
+  const int v = int(index / blocks);  // pass * 8 + slot
+  const int pass = v / 8, g = v % 8;
+  float value = 0.0f;
+  if (v < vectors) {
+    const long long at = ((long long)v * blocks + block) * 32 + lane;
+    value = BF16 ? __uint_as_float(uint32_t(reinterpret_cast<const uint16_t*>(x)[at]) << 16)
+                 : reinterpret_cast<const float*>(x)[at];
+  }
+  float amax = fabsf(value);
+  bool finite = isfinite(value);
+#pragma unroll
+  for (int o = 16; o > 0; o /= 2) {
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    finite = __all_sync(0xffffffffu, finite);
+  }
+  int X = 0;
+  float s = 0.0f;
+  if (!finite) {
+    s = __int_as_float(0x7fc00000);
+  } else if (amax > 0.0f) {
+    const int e = ilogbf(amax) + 1;
+    s = ldexpf(1.0f, e - X_BITS);
+    X = __float2int_rn(ldexpf(value, X_BITS - e));
+  }
+  uint8_t* record = records + ((long long)pass * blocks + block) * MMA_RECORD_BYTES;
+  // value j = lane sits in word w = j / 4 (byte j % 4) of each plane; word w
+  // belongs to lane (g, w % 4) as its half w / 4
+  const int w = lane / 4;
+  const int at = (4 * g + (w % 4)) * 8 + (w / 4) * 4 + (lane % 4);
+  record[at] = uint8_t(X & 0xff);
+  record[256 + at] = uint8_t((X >> 8) & 0xff);
+  record[512 + at] = uint8_t((X >> 16) & 0xff);
+  int sum = X;
+#pragma unroll
+  for (int o = 16; o > 0; o /= 2) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if (lane == 0) {
+    reinterpret_cast<float*>(record + 768)[g] = s;
+    reinterpret_cast<int*>(record + 800)[g] = sum;
+    reinterpret_cast<float*>(record + 832)[g] = float(sum);
+  }
+}
+
 // ---- the product -----------------------------------------------------------------
 constexpr int ROWS_PER_GROUP = 8;
 constexpr int MAX_V = 2;
@@ -209,10 +261,10 @@ __global__ void __launch_bounds__(256) matvec_x22_kernel(const uint8_t* __restri
 
 // Grid: ceil(rows / (16 MT (8 / KS))) CTAs of 256 threads. Warp (group, kw)
 // takes rows [16 MT group, +16 MT) of the CTA's and the kw-th contiguous
-// share of the blocks; vectors <= 8 x records at `records`.
+// share of the blocks; up to 8 vectors, x records in the MMA layout.
 template <typename T, int MT, int KS>
 __global__ void __launch_bounds__(256) matvec_mma_kernel(const uint8_t* __restrict__ weight,
-                                                         const uint32_t* __restrict__ records,
+                                                         const uint8_t* __restrict__ records,
                                                          float* __restrict__ y, int rows, int cols,
                                                          int vectors) {
   constexpr int GROUPS = 8 / KS;
@@ -232,8 +284,6 @@ __global__ void __launch_bounds__(256) matvec_mma_kernel(const uint8_t* __restri
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
 
-  // rows of this thread's fragments, clamped to the matrix (their results
-  // are dropped)
   const uint8_t* row_ptr[MT][2];
 #pragma unroll
   for (int i = 0; i < MT; ++i)
@@ -244,34 +294,20 @@ __global__ void __launch_bounds__(256) matvec_mma_kernel(const uint8_t* __restri
       row_ptr[i][h] = weight + (long long)r * row_bytes;
     }
   const bool have_vector = g < vectors;
-  const uint32_t* rec_g = records + (long long)g * blocks * X_RECORD_WORDS;
-  const uint32_t* rec_v0 = records + (long long)(2 * t) * blocks * X_RECORD_WORDS;
-  const uint32_t* rec_v1 = records + (long long)(2 * t + 1) * blocks * X_RECORD_WORDS;
-  const bool have_v0 = 2 * t < vectors, have_v1 = 2 * t + 1 < vectors;
 
   if (row0 < rows) {
     for (int c = first; c < end; ++c) {
-      uint32_t b[3][2] = {{0, 0}, {0, 0}, {0, 0}};
+      const uint8_t* rec = records + (long long)c * MMA_RECORD_BYTES;
+      uint2 planes[3] = {make_uint2(0, 0), make_uint2(0, 0), make_uint2(0, 0)};
       if (have_vector) {
-        const uint32_t* r = rec_g + (long long)c * X_RECORD_WORDS;
 #pragma unroll
-        for (int p = 0; p < 3; ++p) {
-          b[p][0] = __ldg(r + 8 * p + t);
-          b[p][1] = __ldg(r + 8 * p + 4 + t);
-        }
+        for (int p = 0; p < 3; ++p) planes[p] = __ldg(reinterpret_cast<const uint2*>(rec) + p * 32 + lane);
       }
-      float s0 = 0.0f, s1 = 0.0f;
-      int x0 = 0, x1 = 0;
-      if (have_v0) {
-        const uint2 v = __ldg(reinterpret_cast<const uint2*>(rec_v0 + (long long)c * X_RECORD_WORDS + 24));
-        s0 = __uint_as_float(v.x);
-        x0 = int(v.y);
-      }
-      if (have_v1) {
-        const uint2 v = __ldg(reinterpret_cast<const uint2*>(rec_v1 + (long long)c * X_RECORD_WORDS + 24));
-        s1 = __uint_as_float(v.x);
-        x1 = int(v.y);
-      }
+      const float2 s = __ldg(reinterpret_cast<const float2*>(rec + 768) + t);
+      int2 sum = make_int2(0, 0);
+      float2 fsum = make_float2(0.0f, 0.0f);
+      if (T::DTYPE == DRIFT_Q4_0) sum = __ldg(reinterpret_cast<const int2*>(rec + 800) + t);
+      if (T::DTYPE == DRIFT_Q4_1) fsum = __ldg(reinterpret_cast<const float2*>(rec + 832) + t);
 #pragma unroll
       for (int i = 0; i < MT; ++i) {
         uint32_t lo0, hi0, lo1, hi1;
@@ -279,20 +315,14 @@ __global__ void __launch_bounds__(256) matvec_mma_kernel(const uint8_t* __restri
         fragment_row<T>(row_ptr[i][0], c, t, lo0, hi0, d0, m0);
         fragment_row<T>(row_ptr[i][1], c, t, lo1, hi1, d1, m1);
         const uint32_t a[4] = {lo0, lo1, hi0, hi1};
-        int p[3][4];
-#pragma unroll
-        for (int q = 0; q < 3; ++q) {
-          p[q][0] = p[q][1] = p[q][2] = p[q][3] = 0;
-          if (q < 2)
-            mma_i8<T::SIGNED, false>(p[q], a, b[q][0], b[q][1]);
-          else
-            mma_i8<T::SIGNED, true>(p[q], a, b[q][0], b[q][1]);
-        }
-        // outputs (row g, vector 2t), (g, 2t+1), (g+8, 2t), (g+8, 2t+1)
-        acc[i][0] += mma_block_value<T>(p[0][0], p[1][0], p[2][0], d0, m0, s0, x0);
-        acc[i][1] += mma_block_value<T>(p[0][1], p[1][1], p[2][1], d0, m0, s1, x1);
-        acc[i][2] += mma_block_value<T>(p[0][2], p[1][2], p[2][2], d1, m1, s0, x0);
-        acc[i][3] += mma_block_value<T>(p[0][3], p[1][3], p[2][3], d1, m1, s1, x1);
+        int p0[4], p1[4], p2[4];
+        mma_i8_zero<T::SIGNED, false>(p0, a, planes[0].x, planes[0].y);
+        mma_i8_zero<T::SIGNED, false>(p1, a, planes[1].x, planes[1].y);
+        mma_i8_zero<T::SIGNED, true>(p2, a, planes[2].x, planes[2].y);
+        acc[i][0] = fmaf(s.x, mma_block_value<T>(p0[0], p1[0], p2[0], d0, m0, sum.x, fsum.x), acc[i][0]);
+        acc[i][1] = fmaf(s.y, mma_block_value<T>(p0[1], p1[1], p2[1], d0, m0, sum.y, fsum.y), acc[i][1]);
+        acc[i][2] = fmaf(s.x, mma_block_value<T>(p0[2], p1[2], p2[2], d1, m1, sum.x, fsum.x), acc[i][2]);
+        acc[i][3] = fmaf(s.y, mma_block_value<T>(p0[3], p1[3], p2[3], d1, m1, sum.y, fsum.y), acc[i][3]);
       }
     }
   }
@@ -370,6 +400,24 @@ size_t linear_workspace_bytes(int64_t m, int64_t k) {
   return size_t(m) * size_t(k / 32) * X_RECORD_BYTES;
 }
 
+size_t mma_workspace_bytes(int64_t m, int64_t k) {
+  return size_t((m + 7) / 8) * size_t(k / 32) * MMA_RECORD_BYTES;
+}
+
+int prepare_x_mma(int x_dtype, const void* x, int64_t m, int64_t k, uint8_t* records,
+                  cudaStream_t stream) {
+  const long long blocks = k / 32;
+  const long long warps = (m + 7) / 8 * 8 * blocks;
+  if (warps == 0) return 0;
+  const unsigned grid = unsigned((warps + 7) / 8);
+  if (x_dtype == DRIFT_BF16)
+    quantize_x22_mma_kernel<true><<<grid, 256, 0, stream>>>(x, records, int(m), int(blocks));
+  else
+    quantize_x22_mma_kernel<false><<<grid, 256, 0, stream>>>(x, records, int(m), int(blocks));
+  DRIFT_LAUNCHED("quantize_x22_mma");
+  return 0;
+}
+
 int prepare_x(int x_dtype, const void* x, int64_t m, int64_t k, uint32_t* records,
               cudaStream_t stream) {
   const long long blocks = m * (k / 32);
@@ -403,7 +451,7 @@ static int launch_matvec_v(const uint8_t* weight, const uint32_t* records, float
 }
 
 template <typename T>
-static int launch_mma(const uint8_t* weight, const uint32_t* records, float* y, int rows, int cols,
+static int launch_mma(const uint8_t* weight, const uint8_t* records, float* y, int rows, int cols,
                       int vectors, cudaStream_t stream) {
   const int blocks = cols / 32;
   // enough warps for every SM: split the blocks between more warps when the
@@ -428,50 +476,36 @@ static int launch_mma(const uint8_t* weight, const uint32_t* records, float* y, 
   return 0;
 }
 
+// Passes of up to 8 vectors, each one launch of a single kernel whose block
+// order depends on the matrix only: a row sums to the same bits alone or
+// beside 7 others (the runner's guarantee that a verification's tokens get a
+// decode step's logits, ops/HipLinear.scala:197-201).
 template <typename T>
-static int launch_matvec(const uint8_t* weight, const uint32_t* records, float* y, int rows,
+static int launch_matvec(const uint8_t* weight, const uint8_t* records, float* y, int rows,
                          int cols, int vectors, cudaStream_t stream) {
-  const int blocks = cols / 32;
-  // passes of up to 8 vectors on the integer tensor cores: one kernel for
-  // every batch, whose block order depends on the matrix only, so a row sums
-  // to the same bits alone or beside 7 others (the runner's guarantee that a
-  // verification's tokens get a decode step's logits, ops/HipLinear.scala:
-  // 197-201)
-  if (vectors >= 1) {
-    for (int first = 0; first < vectors; first += 8) {
-      const int count = vectors - first < 8 ? vectors - first : 8;
-      DRIFT_TRY(launch_mma<T>(weight, records + (long long)first * blocks * X_RECORD_WORDS,
-                              y + (long long)first * rows, rows, cols, count, stream));
-    }
-    return 0;
-  }
-  // (the dp4a kernels above stay for by-name callers)
-  for (int first = 0; first < vectors; first += MAX_V) {
-    const int count = vectors - first < MAX_V ? vectors - first : MAX_V;
-    const uint32_t* rec = records + (long long)first * blocks * X_RECORD_WORDS;
-    float* out = y + (long long)first * rows;
-    if (count == 1)
-      DRIFT_TRY((launch_matvec_v<T, 1>(weight, rec, out, rows, cols, 1, stream)));
-    else
-      DRIFT_TRY((launch_matvec_v<T, 2>(weight, rec, out, rows, cols, count, stream)));
+  const long long blocks = cols / 32;
+  for (int first = 0; first < vectors; first += 8) {
+    const int count = vectors - first < 8 ? vectors - first : 8;
+    DRIFT_TRY(launch_mma<T>(weight, records + (first / 8) * blocks * MMA_RECORD_BYTES,
+                            y + (long long)first * rows, rows, cols, count, stream));
   }
   return 0;
 }
 
 bool ring_supports(int weight_dtype, const void* weight, int64_t k);
-int matvec_ring(int weight_dtype, const void* weight, const uint32_t* records, float* y,
+int matvec_ring(int weight_dtype, const void* weight, const uint8_t* records, float* y,
                 int64_t rows, int64_t cols, int64_t vectors, cudaStream_t stream);
 
 // The quantized product of prepared x; `vectors` rows of x, y [vectors, rows].
 // Weights whose rows are whole 16-byte units stream through shared memory
 // (matvec_ring.cu); the rest are read straight from global memory.
-int matvec_prepared(int weight_dtype, const void* weight, const uint32_t* records, float* y,
+int matvec_prepared(int weight_dtype, const void* weight, const uint8_t* records, float* y,
                     int64_t rows, int64_t cols, int64_t vectors, cudaStream_t stream) {
   if (ring_supports(weight_dtype, weight, cols)) {
     const int64_t blocks = cols / 32;
     for (int64_t first = 0; first < vectors; first += 8) {
       const int64_t count = vectors - first < 8 ? vectors - first : 8;
-      DRIFT_TRY(matvec_ring(weight_dtype, weight, records + first * blocks * X_RECORD_WORDS,
+      DRIFT_TRY(matvec_ring(weight_dtype, weight, records + (first / 8) * blocks * MMA_RECORD_BYTES,
                             y + first * rows, rows, cols, count, stream));
     }
     return 0;

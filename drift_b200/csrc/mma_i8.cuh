@@ -46,6 +46,51 @@ __device__ __forceinline__ void mma_i8(int (&d)[4], const uint32_t (&a)[4], uint
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// ---- x for the integer tensor cores --------------------------------------------------
+// The prepared x of up to 8 vectors (a pass), one 896-byte record per block,
+// laid out as the m16n8k32 B fragments are held: lane (g, t) of a warp reads
+// one 8-byte word per plane, in lane order, so a warp's plane load is one
+// coalesced 256-byte access.
+//   bytes   0..767  plane p (0..2): uint2 [32 lanes]; lane 4g + t holds words t
+//                   and 4 + t of vector g's plane p (values 4t..4t+3 and
+//                   16+4t..16+4t+3), zero for vectors past the pass
+//   bytes 768..799  s of vectors 0..7 (float)
+//   bytes 800..831  sum_j X_j of vectors 0..7 (int)
+//   bytes 832..863  the same sums as float
+constexpr int MMA_RECORD_BYTES = 896;
+constexpr int MMA_RECORD_WORDS = MMA_RECORD_BYTES / 4;
+
+// The same product with a zero accumulator (no registers to clear first).
+template <bool SIGNED_A, bool SIGNED_B>
+__device__ __forceinline__ void mma_i8_zero(int (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                            uint32_t b1) {
+  const int zero = 0;
+  if (SIGNED_A && SIGNED_B)
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(zero));
+  else if (SIGNED_A)
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(zero));
+  else if (SIGNED_B)
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(zero));
+  else
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(zero));
+}
+
 // A row's part of block `c` as this thread's fragment needs it: the codes of
 // values 4t..4t+3 (lo) and 16+4t..16+4t+3 (hi), and the block's d and m.
 // LOAD reads a word: __ldg for global memory, a plain load for shared.
@@ -90,16 +135,18 @@ __device__ __forceinline__ void fragment_row(const uint8_t* __restrict__ row, in
   }
 }
 
-// One output's share of a block: the three plane sums joined, scaled.
+// One output's share of a block before the x scale s: the three plane sums
+// joined (exactly for the Q4 types, |sum| < 2^31; in float for Q8_0) and
+// scaled by the block's d (and m). The caller adds s times it.
 template <typename T>
-__device__ __forceinline__ float mma_block_value(int p0, int p1, int p2, float d, float m, float s,
-                                                 int sum_x) {
+__device__ __forceinline__ float mma_block_value(int p0, int p1, int p2, float d, float m,
+                                                 int sum_x, float sum_x_float) {
   if (T::DTYPE == DRIFT_Q8_0) {
-    return s * d * fmaf(256.0f, float(p1 + (p2 << 8)), float(p0));
+    return d * fmaf(256.0f, float(p1 + (p2 << 8)), float(p0));
   } else if (T::DTYPE == DRIFT_Q4_0) {
-    return s * d * float(p0 + (p1 << 8) + (p2 << 16) - 8 * sum_x);
+    return d * float(p0 + (p1 << 8) + (p2 << 16) - 8 * sum_x);
   } else {
-    return s * fmaf(d, float(p0 + (p1 << 8) + (p2 << 16)), m * float(sum_x));
+    return fmaf(d, float(p0 + (p1 << 8) + (p2 << 16)), m * sum_x_float);
   }
 }
 
