@@ -31,7 +31,7 @@ int linear_tc(int x_dtype, const void* x, int weight_dtype, const void* weight, 
 constexpr int64_t GEMM_MINIMUM_ROWS = 32;
 
 // Ops.checkLinear, plus what the kernels need of a stored weight.
-static int check_linear(int x_dtype, const void* x, int weight_dtype, const void* weight,
+int check_linear(int x_dtype, const void* x, int weight_dtype, const void* weight,
                         const float* out, int64_t m, int64_t n, int64_t k) {
   if (x_dtype != DRIFT_F32 && x_dtype != DRIFT_BF16)
     return invalid("linear takes F32 (or BF16) x, not %s", dtype_name(x_dtype));

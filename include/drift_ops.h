@@ -145,6 +145,23 @@ int drift_workspace_reserve(size_t bytes);
 /* Bytes of scratch drift_linear needs for m rows of k (new). */
 size_t drift_linear_workspace_bytes(int64_t m, int64_t k);
 
+/* drift_linear, for 1 to 31 rows of x, allocating no device memory. No
+ * counterpart in the reference: it exists for hosts that cannot allocate on
+ * the call path -- a server whose device memory is all reserved up front, so
+ * an allocation mid-step could fail; an FFM host that owns every device
+ * buffer through its own allocator and budget; a latency-bound loop that must
+ * not let cudaMalloc or cudaFree synchronize the device.
+ * Its scratch (the prepared x) is a fixed 1 MiB array in the library's device
+ * image: (ceil(m / 8)) * (k / 32) * 896 bytes must fit, i.e. 8 rows of up to
+ * 37,440 columns or 31 rows of up to 9,344; larger sizes, and m >= 32, are
+ * refused with DRIFT_ERROR_INVALID_ARGUMENT. The first call on a device looks
+ * up the array's device address (cudaGetSymbolAddress): make it before any
+ * stream capture. Every call shares the array, so calls whose kernels overlap
+ * on the GPU (other streams, other threads) race; calls in one stream do not.
+ * Each call writes all the scratch it reads, so no state carries over. */
+int drift_linear_static(int x_dtype, const void* x, int weight_dtype, const void* weight,
+                        float* out, int64_t m, int64_t n, int64_t k, drift_stream_t stream);
+
 /* Reads and clears the current device's error word: 0 if no kernel flagged
  * anything since the last call, else the first flag (1 = an id outside its
  * table, 2 = a bounded wait gave up). Synchronises the device. */
