@@ -189,10 +189,11 @@ def run_gpu(args) -> dict | None:
         for _ in range(2):
             step()  # first calls resolve the library's lazy state outside capture
     torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
+    graph = torch.cuda.CUDAGraph(keep_graph=True)
     with torch.cuda.graph(graph, stream=stream):
         step()
-    launches_per_step = count_launches(ops, step)
+    launches_per_step = count_launches(graph)
+    graph.instantiate()
 
     def barrier():
         if world > 1:
@@ -281,7 +282,7 @@ def run_gpu(args) -> dict | None:
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "q4_1 weights, bf16 x, exact-integer dp4a products, f32 out",
+        "dtype": "q4_1 weights, bf16 x; int8 planes (dp4a, mma.sync s8) and f16 tcgen05 products, f32 out",
         "data": "synthetic (seeded; BASELINE C2 value laws)",
         "config": {
             "workload": "C2 Q4_1 matvec sweep: batches 1/8/64 x shapes 4096x4096, "
@@ -297,7 +298,7 @@ def run_gpu(args) -> dict | None:
         "gpu_launches": launches_per_step * args.steps,
         "roofline": {
             "bound": "hbm",
-            "kernel": "matvec_x22_q4_1 (+ quantize_x22), lm-head 151936x4096, batch 1",
+            "kernel": "matvec_ring_q4_1 (+ quantize_x22_mma), lm-head 151936x4096, batch 1",
             "achieved": round(dominant["gbs"], 1),
             "peak": peaks["hbm_gbs"],
             "peak_source": peaks["source"] + " (MEASURED_PEAKS.json hbm_gbs, copy)",
@@ -314,14 +315,21 @@ def run_gpu(args) -> dict | None:
     return result
 
 
-def count_launches(ops, step) -> int:
-    """Kernels one step launches: two per product (x preparation, product)
-    plus one per extra pass of MAX_V vectors."""
-    launches = 0
-    for b in BATCHES:
-        for _ in SHAPES:
-            launches += 1 + (b + 1) // 2
-    return launches
+def count_launches(graph) -> int:
+    """Kernel nodes in the captured step: the launches one step makes (all of
+    them the library's own; the step calls nothing else)."""
+    from cuda.bindings import runtime
+
+    handle = runtime.cudaGraph_t(init_value=graph.raw_cuda_graph())
+    err, nodes, count = runtime.cudaGraphGetNodes(handle, 0)
+    err, nodes, count = runtime.cudaGraphGetNodes(handle, count)
+    if err != runtime.cudaError_t.cudaSuccess:
+        raise RuntimeError(f"cudaGraphGetNodes: {err}")
+    kernels = 0
+    for node in nodes[:count]:
+        err, kind = runtime.cudaGraphNodeGetType(node)
+        kernels += kind == runtime.cudaGraphNodeType.cudaGraphNodeTypeKernel
+    return kernels
 
 
 def timed_graph(fn, stream, repeats: int) -> float:

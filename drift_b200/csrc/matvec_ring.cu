@@ -45,9 +45,14 @@ struct Ring {
   static constexpr int PITCH = SEG;
 };
 
-template <typename T, int MT, int KS, int S, int WARPS>
+// Every tile is 32 rows: one row per lane in the dp4a modes, two 16-row MMA
+// tiles in the MMA mode, so all modes share one schedule -- and one order of
+// summation -- per matrix.
+constexpr int ROWS = 32;
+constexpr int MODE_DP4A_1 = 1, MODE_DP4A_2 = 2, MODE_MMA = 8;
+
+template <typename T, int KS, int S, int WARPS>
 struct RingLayout {
-  static constexpr int ROWS = 16 * MT;
   static constexpr int STAGE = ROWS * Ring<T>::PITCH;
   static constexpr int RING = WARPS * S * STAGE;
   static constexpr int BARS = RING;                            // WARPS x S mbarriers
@@ -56,21 +61,17 @@ struct RingLayout {
   static constexpr int BYTES = COUNTER + 16 + 1024;  // + room to align the base to 1024
 };
 
-// The products of one 8-block segment held in a stage: acc[i][.] gains the
-// blocks' values for rows (16 i + g, 16 i + g + 8) and vectors (2t, 2t + 1),
-// each as acc = fmaf(s, value, acc). V1: one vector, whose outputs are the
-// first and third of each thread (t = 0); the others are not computed.
-template <typename T, int MT, bool V1>
-__device__ __forceinline__ void segment_products(const uint8_t* stage, int first_block, int count,
-                                                 const uint8_t* __restrict__ records, int vectors,
-                                                 float (&acc)[MT][4]) {
+// ---- MMA mode: 3-8 vectors ---------------------------------------------------------------
+// acc[i][.] gains the segment's blocks for rows (16 i + g, 16 i + g + 8) and
+// vectors (2t, 2t + 1), each as acc = fmaf(s, value, acc).
+template <typename T>
+__device__ __forceinline__ void segment_mma(const uint8_t* stage, int first_block, int count,
+                                            const uint8_t* __restrict__ records, int vectors,
+                                            float (&acc)[2][4]) {
   const int lane = threadIdx.x % WARP, g = lane / 4, t = lane % 4;
   const bool have_vector = g < vectors;
-  const bool have_v1 = !V1;
   const uint8_t* rec0 = records + (long long)first_block * MMA_RECORD_BYTES;
-  const uint8_t* rows_lo[MT];
-#pragma unroll
-  for (int i = 0; i < MT; ++i) rows_lo[i] = stage + (16 * i + g) * Ring<T>::PITCH;
+  const uint8_t* rows_lo[2] = {stage + g * Ring<T>::PITCH, stage + (16 + g) * Ring<T>::PITCH};
 #pragma unroll
   for (int b = 0; b < SEG_BLOCKS; ++b) {
     if (b < count) {
@@ -86,7 +87,7 @@ __device__ __forceinline__ void segment_products(const uint8_t* stage, int first
       if (T::DTYPE == DRIFT_Q4_0) sum = __ldg(reinterpret_cast<const int2*>(rec + 800) + t);
       if (T::DTYPE == DRIFT_Q4_1) fsum = __ldg(reinterpret_cast<const float2*>(rec + 832) + t);
 #pragma unroll
-      for (int i = 0; i < MT; ++i) {
+      for (int i = 0; i < 2; ++i) {
         uint32_t lo0, hi0, lo1, hi1;
         float d0, m0, d1, m1;
         fragment_row<T, SharedWords>(rows_lo[i], b, t, lo0, hi0, d0, m0);
@@ -97,25 +98,84 @@ __device__ __forceinline__ void segment_products(const uint8_t* stage, int first
         mma_i8_zero<T::SIGNED, false>(p1, a, planes[1].x, planes[1].y);
         mma_i8_zero<T::SIGNED, true>(p2, a, planes[2].x, planes[2].y);
         acc[i][0] = fmaf(s.x, mma_block_value<T>(p0[0], p1[0], p2[0], d0, m0, sum.x, fsum.x), acc[i][0]);
+        acc[i][1] = fmaf(s.y, mma_block_value<T>(p0[1], p1[1], p2[1], d0, m0, sum.y, fsum.y), acc[i][1]);
         acc[i][2] = fmaf(s.x, mma_block_value<T>(p0[2], p1[2], p2[2], d1, m1, sum.x, fsum.x), acc[i][2]);
-        if (have_v1) {
-          acc[i][1] = fmaf(s.y, mma_block_value<T>(p0[1], p1[1], p2[1], d0, m0, sum.y, fsum.y), acc[i][1]);
-          acc[i][3] = fmaf(s.y, mma_block_value<T>(p0[3], p1[3], p2[3], d1, m1, sum.y, fsum.y), acc[i][3]);
-        }
+        acc[i][3] = fmaf(s.y, mma_block_value<T>(p0[3], p1[3], p2[3], d1, m1, sum.y, fsum.y), acc[i][3]);
       }
     }
   }
 }
 
-// Grid (tiles schedule): at most one CTA per SM; `tiles` = ceil(rows / ROWS).
+// ---- dp4a modes: 1 or 2 vectors ------------------------------------------------------------
+// Lane r takes row r of the tile: its 8 blocks come out of shared memory in
+// 16-byte reads, each block's codes meet x's planes (the same for every lane:
+// broadcast loads) in 24 dp4a, and acc[v] = fmaf(s, value, acc[v]) with the
+// same value and the same order as the MMA mode -- the plane sums are exact
+// integers either way -- so a row's result does not depend on the mode.
+template <typename T, int V>
+__device__ __forceinline__ void segment_dp4a(const uint8_t* stage, int first_block, int count,
+                                             const uint8_t* __restrict__ records, float (&acc)[4]) {
+  constexpr int SEG = Ring<T>::SEG;
+  constexpr int WORDS = SEG / 4;
+  const int lane = threadIdx.x % WARP;
+  uint32_t row[WORDS];
+  const uint4* src = reinterpret_cast<const uint4*>(stage + lane * Ring<T>::PITCH);
+#pragma unroll
+  for (int i = 0; i < SEG / 16; ++i) {
+    const uint4 q = src[i];
+    row[4 * i] = q.x;
+    row[4 * i + 1] = q.y;
+    row[4 * i + 2] = q.z;
+    row[4 * i + 3] = q.w;
+  }
+  const uint8_t* rec0 = records + (long long)first_block * MMA_RECORD_BYTES;
+#pragma unroll
+  for (int b = 0; b < SEG_BLOCKS; ++b) {
+    if (b < count) {
+      const int word = (b * T::BYTES) / 4;
+      uint32_t w[T::WORDS];
+#pragma unroll
+      for (int i = 0; i < T::WORDS; ++i) w[i] = (word + i < WORDS) ? row[word + i] : 0u;
+      const Codes codes = T::decode(w, b);
+      const uint8_t* rec = rec0 + b * MMA_RECORD_BYTES;
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        uint32_t planes[24];
+#pragma unroll
+        for (int p = 0; p < 3; ++p) {
+          const uint4* q = reinterpret_cast<const uint4*>(rec + 256 * p + 32 * v);
+          const uint4 q0 = __ldg(q), q1 = __ldg(q + 1);
+          planes[8 * p + 0] = q0.x;
+          planes[8 * p + 4] = q0.y;
+          planes[8 * p + 1] = q0.z;
+          planes[8 * p + 5] = q0.w;
+          planes[8 * p + 2] = q1.x;
+          planes[8 * p + 6] = q1.y;
+          planes[8 * p + 3] = q1.z;
+          planes[8 * p + 7] = q1.w;
+        }
+        const float s = __ldg(reinterpret_cast<const float*>(rec + 768) + v);
+        int sum = 0;
+        float fsum = 0.0f;
+        if (T::DTYPE == DRIFT_Q4_0) sum = __ldg(reinterpret_cast<const int*>(rec + 800) + v);
+        if (T::DTYPE == DRIFT_Q4_1) fsum = __ldg(reinterpret_cast<const float*>(rec + 832) + v);
+        int a0, a1, a2;
+        plane_sums<T>(codes, planes, a0, a1, a2);
+        acc[v] = fmaf(s, mma_block_value<T>(a0, a1, a2, codes.d, codes.m, sum, fsum), acc[v]);
+      }
+    }
+  }
+}
+
+// Grid (tiles schedule, KS = 1): at most one CTA per SM.
 // Grid (split schedule): ceil(tiles / (WARPS / KS)) CTAs, one unit each.
-template <typename T, int MT, int KS, int S, int WARPS, bool V1>
+template <typename T, int KS, int S, int WARPS, int MODE>
 __global__ void __launch_bounds__(WARPS * 32, 1)
     matvec_ring_kernel(const __grid_constant__ CUtensorMap wmap,
                        const uint8_t* __restrict__ records, float* __restrict__ y, int rows,
                        int cols, int vectors, int* error) {
-  using L = RingLayout<T, MT, KS, S, WARPS>;
-  constexpr int ROWS = L::ROWS, GROUPS = WARPS / KS;
+  using L = RingLayout<T, KS, S, WARPS>;
+  constexpr int GROUPS = WARPS / KS;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -127,7 +187,6 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   volatile int* abort = counter + 1;
 
   const int blocks = cols / 32;
-  const long long row_bytes = (long long)blocks * T::BYTES;
   const int segments = (blocks + SEG_BLOCKS - 1) / SEG_BLOCKS;
   const int tiles = (rows + ROWS - 1) / ROWS;
   const int kw = warp % KS, slot = warp / KS;
@@ -166,8 +225,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     return true;
   };
   // job j: segment seg0 + j % nseg of tile claimed[j / nseg], one 2-D tensor
-  // copy of ROWS rows x SEG bytes (rows past the matrix, and columns past a
-  // row, arrive as zeros)
+  // copy of 32 rows x SEG bytes (rows past the matrix, and columns past a row,
+  // arrive as zeros)
   auto issue = [&](int j) {
     const int tile = claimed[(j / nseg) % 8];
     const int segment = seg0 + j % nseg;
@@ -189,22 +248,24 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     }
     issue(issued++);
   }
-  float acc[MT][4];
+  float acc[2][4];
 #pragma unroll
-  for (int i = 0; i < MT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
+  for (int i = 0; i < 2; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
   while (consumed < issued) {
     const int j = consumed;
     const int segment = seg0 + j % nseg;
     if (j % nseg == 0) {
 #pragma unroll
-      for (int i = 0; i < MT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
+      for (int i = 0; i < 2; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
     }
     if (ok) ok = tc::mbar_wait_warp(&bars[j % S], (j / S) & 1, abort, error);
     if (ok) {
       const int first = segment * SEG_BLOCKS;
       const int count = blocks - first < SEG_BLOCKS ? blocks - first : SEG_BLOCKS;
-      segment_products<T, MT, V1>(ring + (j % S) * L::STAGE, first, count, records, vectors,
-                                  acc);
+      if constexpr (MODE == MODE_MMA)
+        segment_mma<T>(ring + (j % S) * L::STAGE, first, count, records, vectors, acc);
+      else
+        segment_dp4a<T, MODE>(ring + (j % S) * L::STAGE, first, count, records, acc[0]);
     }
     __syncwarp();
     ++consumed;
@@ -215,12 +276,12 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       else
         issue(issued++);
     }
-    if (j % nseg == nseg - 1) {
+    if (KS == 1 && j % nseg == nseg - 1) {
+      // whole rows: write them
       const int tile = claimed[(j / nseg) % 8];
-      if (KS == 1) {
-        // whole rows: write them
+      if constexpr (MODE == MODE_MMA) {
 #pragma unroll
-        for (int i = 0; i < MT; ++i) {
+        for (int i = 0; i < 2; ++i) {
           const int r0 = tile * ROWS + 16 * i + g, r1 = r0 + 8;
           if (r0 < rows) {
             if (2 * t < vectors) y[(long long)(2 * t) * rows + r0] = acc[i][0];
@@ -231,23 +292,31 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
             if (2 * t + 1 < vectors) y[(long long)(2 * t + 1) * rows + r1] = acc[i][3];
           }
         }
+      } else {
+        const int row = tile * ROWS + lane;
+        if (row < rows) {
+#pragma unroll
+          for (int v = 0; v < MODE; ++v)
+            if (v < vectors) y[(long long)v * rows + row] = acc[0][v];
+        }
       }
     }
   }
   if (KS > 1) {
     // this warp's share of its unit's tile, then the shares in order
     float* partial = reinterpret_cast<float*>(smem + L::PARTIAL);
-    if (nseg == 0) {
-#pragma unroll
-      for (int i = 0; i < MT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
-    }
     float* mine = partial + ((kw * GROUPS + slot) * ROWS) * 8;
+    if constexpr (MODE == MODE_MMA) {
 #pragma unroll
-    for (int i = 0; i < MT; ++i) {
-      mine[(16 * i + g) * 8 + 2 * t] = acc[i][0];
-      mine[(16 * i + g) * 8 + 2 * t + 1] = acc[i][1];
-      mine[(16 * i + g + 8) * 8 + 2 * t] = acc[i][2];
-      mine[(16 * i + g + 8) * 8 + 2 * t + 1] = acc[i][3];
+      for (int i = 0; i < 2; ++i) {
+        mine[(16 * i + g) * 8 + 2 * t] = acc[i][0];
+        mine[(16 * i + g) * 8 + 2 * t + 1] = acc[i][1];
+        mine[(16 * i + g + 8) * 8 + 2 * t] = acc[i][2];
+        mine[(16 * i + g + 8) * 8 + 2 * t + 1] = acc[i][3];
+      }
+    } else {
+#pragma unroll
+      for (int v = 0; v < MODE; ++v) mine[lane * 8 + v] = acc[0][v];
     }
     __syncthreads();
     for (int e = threadIdx.x; e < GROUPS * ROWS * 8; e += blockDim.x) {
@@ -268,35 +337,39 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   }
 }
 
-template <typename T, int MT, int KS, int S, int WARPS>
-int launch_ring(const uint8_t* weight, const uint8_t* records, float* y, int rows, int cols,
+template <typename T, int KS, int S, int WARPS, int MODE>
+int launch_mode(const CUtensorMap& wmap, const uint8_t* records, float* y, int rows, int cols,
                 int vectors, cudaStream_t stream) {
-  using L = RingLayout<T, MT, KS, S, WARPS>;
-  CUtensorMap wmap;
-  DRIFT_TRY(encode_word_rows(&wmap, weight, int64_t(cols / 32) * T::BYTES / 4, rows,
-                             Ring<T>::SEG / 4, L::ROWS));
+  using L = RingLayout<T, KS, S, WARPS>;
   static bool configured = false;
   if (!configured) {
-    DRIFT_CUDA(cudaFuncSetAttribute(matvec_ring_kernel<T, MT, KS, S, WARPS, true>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES));
-    DRIFT_CUDA(cudaFuncSetAttribute(matvec_ring_kernel<T, MT, KS, S, WARPS, false>,
+    DRIFT_CUDA(cudaFuncSetAttribute(matvec_ring_kernel<T, KS, S, WARPS, MODE>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES));
     configured = true;
   }
-  const int tiles = (rows + L::ROWS - 1) / L::ROWS;
+  const int tiles = (rows + ROWS - 1) / ROWS;
   unsigned grid;
   if (KS == 1)
     grid = unsigned(tiles < sm_count() ? tiles : sm_count());
   else
     grid = unsigned((tiles + (WARPS / KS) - 1) / (WARPS / KS));
-  if (vectors == 1)
-    matvec_ring_kernel<T, MT, KS, S, WARPS, true><<<grid, WARPS * 32, L::BYTES, stream>>>(
-        wmap, records, y, rows, cols, vectors, device_error_word());
-  else
-    matvec_ring_kernel<T, MT, KS, S, WARPS, false><<<grid, WARPS * 32, L::BYTES, stream>>>(
-        wmap, records, y, rows, cols, vectors, device_error_word());
+  matvec_ring_kernel<T, KS, S, WARPS, MODE><<<grid, WARPS * 32, L::BYTES, stream>>>(
+      wmap, records, y, rows, cols, vectors, device_error_word());
   DRIFT_LAUNCHED("matvec_ring");
   return 0;
+}
+
+template <typename T, int KS, int S, int WARPS>
+int launch_ring(const uint8_t* weight, const uint8_t* records, float* y, int rows, int cols,
+                int vectors, cudaStream_t stream) {
+  CUtensorMap wmap;
+  DRIFT_TRY(encode_word_rows(&wmap, weight, int64_t(cols / 32) * T::BYTES / 4, rows,
+                             Ring<T>::SEG / 4, ROWS));
+  if (vectors == 1)
+    return launch_mode<T, KS, S, WARPS, MODE_DP4A_1>(wmap, records, y, rows, cols, vectors, stream);
+  if (vectors == 2)
+    return launch_mode<T, KS, S, WARPS, MODE_DP4A_2>(wmap, records, y, rows, cols, vectors, stream);
+  return launch_mode<T, KS, S, WARPS, MODE_MMA>(wmap, records, y, rows, cols, vectors, stream);
 }
 
 // The configuration of a matrix: the same for every number of vectors, so a
@@ -306,37 +379,35 @@ int ring_dispatch(const uint8_t* weight, const uint8_t* records, float* y, int r
                   int vectors, cudaStream_t stream) {
   const int blocks = cols / 32;
   const int segments = (blocks + SEG_BLOCKS - 1) / SEG_BLOCKS;
-  const long long tiles16 = (rows + 15) / 16;
+  const long long tiles = (rows + ROWS - 1) / ROWS;
   const int sms = sm_count();
-  constexpr bool big = T::DTYPE == DRIFT_Q8_0;  // 272-byte segments
-  // Many rows: whole tiles per warp, 16 warps per SM (32 rows each when the
-  // segments are small enough: x records read once for both halves).
-  if ((rows + 31) / 32 >= 16LL * sms) {
-    if (big) return launch_ring<T, 1, 1, 3, 16>(weight, records, y, rows, cols, vectors, stream);
-    return launch_ring<T, 2, 1, 2, 16>(weight, records, y, rows, cols, vectors, stream);
-  }
-  if (tiles16 >= 16LL * sms)
-    return launch_ring<T, 1, 1, 3, 16>(weight, records, y, rows, cols, vectors, stream);
-  // Few rows: split each tile's segments between warps so every SM works.
-  int ks = 1;
-  while (ks < 8 && ks * 2 <= segments && tiles16 * ks * 2 <= 16LL * sms) ks *= 2;
-  if (ks < 2) ks = 2;
+  constexpr int WIDE = T::DTYPE == DRIFT_Q8_0 ? 12 : 16;  // warps per CTA (272-byte segments: 12)
+  // Many rows: whole tiles per warp, tiles claimed within the CTA's range.
+  if (tiles >= 2LL * WIDE * sms)
+    return launch_ring<T, 1, 2, WIDE>(weight, records, y, rows, cols, vectors, stream);
+  // Fewer rows: split each tile's segments between warps so every SM works.
+  int ks = 2;
+  while (ks < 8 && ks * 2 <= segments && tiles * ks < 8LL * sms) ks *= 2;
   switch (ks) {
-    case 8: return launch_ring<T, 1, 8, 3, 8>(weight, records, y, rows, cols, vectors, stream);
-    case 4: return launch_ring<T, 1, 4, 4, 8>(weight, records, y, rows, cols, vectors, stream);
-    default: return launch_ring<T, 1, 2, 4, 8>(weight, records, y, rows, cols, vectors, stream);
+    case 8: return launch_ring<T, 8, 3, 8>(weight, records, y, rows, cols, vectors, stream);
+    case 4: return launch_ring<T, 4, 3, 8>(weight, records, y, rows, cols, vectors, stream);
+    default: return launch_ring<T, 2, 3, 8>(weight, records, y, rows, cols, vectors, stream);
   }
 }
 
-#define DRIFT_RING_REGISTER(T, name)                                                          \
-  DRIFT_REGISTER(matvec_ring_##name##_mt2_w16, (matvec_ring_kernel<T, 2, 1, 2, 16, false>))   \
-  DRIFT_REGISTER(matvec_ring_##name##_mt1_w16, (matvec_ring_kernel<T, 1, 1, 3, 16, false>))   \
-  DRIFT_REGISTER(matvec_ring_##name##_ks2, (matvec_ring_kernel<T, 1, 2, 4, 8, false>))        \
-  DRIFT_REGISTER(matvec_ring_##name##_ks4, (matvec_ring_kernel<T, 1, 4, 4, 8, false>))        \
-  DRIFT_REGISTER(matvec_ring_##name##_ks8, (matvec_ring_kernel<T, 1, 8, 3, 8, false>))
-DRIFT_RING_REGISTER(Q8_0T, q8_0)
-DRIFT_RING_REGISTER(Q4_0T, q4_0)
-DRIFT_RING_REGISTER(Q4_1T, q4_1)
+#define DRIFT_RING_REGISTER(T, name, wide)                                                      \
+  DRIFT_REGISTER(matvec_ring_##name##_tiles_dp4a1, (matvec_ring_kernel<T, 1, 2, wide, 1>))     \
+  DRIFT_REGISTER(matvec_ring_##name##_tiles_dp4a2, (matvec_ring_kernel<T, 1, 2, wide, 2>))     \
+  DRIFT_REGISTER(matvec_ring_##name##_tiles_mma, (matvec_ring_kernel<T, 1, 2, wide, 8>))       \
+  DRIFT_REGISTER(matvec_ring_##name##_ks2_dp4a1, (matvec_ring_kernel<T, 2, 3, 8, 1>))          \
+  DRIFT_REGISTER(matvec_ring_##name##_ks4_dp4a1, (matvec_ring_kernel<T, 4, 3, 8, 1>))          \
+  DRIFT_REGISTER(matvec_ring_##name##_ks8_dp4a1, (matvec_ring_kernel<T, 8, 3, 8, 1>))          \
+  DRIFT_REGISTER(matvec_ring_##name##_ks2_mma, (matvec_ring_kernel<T, 2, 3, 8, 8>))            \
+  DRIFT_REGISTER(matvec_ring_##name##_ks4_mma, (matvec_ring_kernel<T, 4, 3, 8, 8>))            \
+  DRIFT_REGISTER(matvec_ring_##name##_ks8_mma, (matvec_ring_kernel<T, 8, 3, 8, 8>))
+DRIFT_RING_REGISTER(Q8_0T, q8_0, 12)
+DRIFT_RING_REGISTER(Q4_0T, q4_0, 16)
+DRIFT_RING_REGISTER(Q4_1T, q4_1, 16)
 
 }  // namespace
 
