@@ -485,6 +485,27 @@ def run_reference(args) -> dict | None:
     }
 
 
+def run_case(spec: str, repeat: int, dtype: int = Q4_1) -> None:
+    """`--case B,N,K`: one product, `repeat` times, nothing timed -- the small
+    fixed workload the ncu captures run."""
+    import torch
+
+    from drift_b200 import synthetic
+    from drift_b200.ops import CudaOps, Stored
+
+    b, n, k = (int(v) for v in spec.split(","))
+    ops = CudaOps(0)
+    rng = np.random.default_rng(7)
+    weight = Stored.upload(dtype, (n, k), synthetic.quantized(rng, dtype, n, k))
+    bits = synthetic.bf16_bits(synthetic.gaussian(rng, b, k))
+    x = torch.from_numpy(bits.view(np.int16)).cuda().view(torch.bfloat16)
+    y = torch.empty(b, n, device="cuda")
+    for _ in range(repeat):
+        ops.linear(x, weight, y)
+    torch.cuda.synchronize()
+    print(f"case {b}x{n}x{k} dtype {dtype}: {repeat} products, y[0,:4] = {y[0, :4].tolist()}")
+
+
 def main() -> int:
     parser = argparse.ArgumentParser()
     parser.add_argument("--gpus", type=int, default=1)
@@ -493,8 +514,14 @@ def main() -> int:
     parser.add_argument("--impl", default="drift_b200")
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    parser.add_argument("--case", help="B,N,K: run one product --repeat times (profiling)")
+    parser.add_argument("--case-dtype", type=int, default=Q4_1)
+    parser.add_argument("--repeat", type=int, default=3)
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.case:
+        run_case(args.case, args.repeat, args.case_dtype)
+        return 0
     if args.impl == "reference":
         result = run_reference(args)
     else:

@@ -37,41 +37,151 @@ int* device_error_word();
 namespace {
 
 constexpr int SEG_BLOCKS = 8;
+// Every tile is 64 rows: two rows per lane in the dp4a modes, four 16-row MMA
+// tiles in the MMA mode, so all modes share one schedule -- and one order of
+// summation -- per matrix.
+constexpr int ROWS = 64;
+constexpr int MODE_DP4A_1 = 1, MODE_DP4A_2 = 2, MODE_MMA = 8;
 
 template <typename T>
 struct Ring {
-  static constexpr int SEG = SEG_BLOCKS * T::BYTES;
-  // rows sit densely in a stage, as one 2-D tensor copy lays them out
-  static constexpr int PITCH = SEG;
+  static constexpr int SEG = SEG_BLOCKS * T::BYTES;  // 160 (Q4_1), 144 (Q4_0), 272 (Q8_0)
+  // The width each copy brings per row. Q4_1 takes 16 bytes past its segment
+  // (the next segment's first bytes, or zeros past the row) so a row sits 176
+  // bytes -- 44 words -- from the next: lanes reading one column of eight
+  // consecutive rows then hit eight distinct 4-bank groups, where a 160-byte
+  // pitch would put rows r and r + 4 on the same banks.
+  static constexpr int PITCH = T::DTYPE == DRIFT_Q4_1 ? 176 : SEG;
+  static constexpr int STAGE = ROWS * PITCH;
 };
 
-// Every tile is 32 rows: one row per lane in the dp4a modes, two 16-row MMA
-// tiles in the MMA mode, so all modes share one schedule -- and one order of
-// summation -- per matrix.
-constexpr int ROWS = 32;
-constexpr int MODE_DP4A_1 = 1, MODE_DP4A_2 = 2, MODE_MMA = 8;
-
-template <typename T, int KS, int S, int WARPS>
-struct RingLayout {
-  static constexpr int STAGE = ROWS * Ring<T>::PITCH;
-  static constexpr int RING = WARPS * S * STAGE;
-  static constexpr int BARS = RING;                            // WARPS x S mbarriers
-  static constexpr int PARTIAL = BARS + WARPS * S * 8;         // [KS][WARPS/KS][ROWS][8] floats
-  static constexpr int COUNTER = PARTIAL + (KS > 1 ? WARPS * ROWS * 8 * 4 : 0);
-  static constexpr int BYTES = COUNTER + 16 + 1024;  // + room to align the base to 1024
+// Warps per CTA and stages per warp, by type: about 180-210 KB of ring.
+template <typename T>
+struct RingShape {
+  static constexpr int WARPS = T::DTYPE == DRIFT_Q8_0 ? 6 : 8;
+  static constexpr int S = 2;
+  static constexpr int BARS = WARPS * S * Ring<T>::STAGE;
+  static constexpr int BYTES = BARS + WARPS * S * 8 + 16 + 1024;  // + room to align to 1024
 };
 
-// ---- MMA mode: 3-8 vectors ---------------------------------------------------------------
+// words [OFF, END) of a row in shared memory (16-byte aligned), by the widest
+// aligned loads
+template <int OFF, int END>
+__device__ __forceinline__ void lds_span(const uint8_t* row, uint32_t* w) {
+  if constexpr (OFF < END) {
+    if constexpr (OFF % 16 == 0 && OFF + 16 <= END) {
+      const uint4 q = *reinterpret_cast<const uint4*>(row + OFF);
+      w[0] = q.x;
+      w[1] = q.y;
+      w[2] = q.z;
+      w[3] = q.w;
+      lds_span<OFF + 16, END>(row, w + 4);
+    } else {
+      const uint2 q = *reinterpret_cast<const uint2*>(row + OFF);
+      w[0] = q.x;
+      w[1] = q.y;
+      lds_span<OFF + 8, END>(row, w + 2);
+    }
+  }
+}
+
+// One vector's x for one block, as the dp4a modes use it.
+struct XBlock {
+  uint32_t planes[24];
+  float s, fsum;
+  int sum;
+};
+
+template <typename T>
+__device__ __forceinline__ void load_x(const uint8_t* rec, int v, XBlock& x) {
+#pragma unroll
+  for (int p = 0; p < 3; ++p) {
+    // plane p, vector v: words (0, 4, 1, 5) then (2, 6, 3, 7) of the 8
+    const uint4* q = reinterpret_cast<const uint4*>(rec + 256 * p + 32 * v);
+    const uint4 q0 = __ldg(q), q1 = __ldg(q + 1);
+    x.planes[8 * p + 0] = q0.x;
+    x.planes[8 * p + 4] = q0.y;
+    x.planes[8 * p + 1] = q0.z;
+    x.planes[8 * p + 5] = q0.w;
+    x.planes[8 * p + 2] = q1.x;
+    x.planes[8 * p + 6] = q1.y;
+    x.planes[8 * p + 3] = q1.z;
+    x.planes[8 * p + 7] = q1.w;
+  }
+  x.s = __ldg(reinterpret_cast<const float*>(rec + 768) + v);
+  x.sum = T::DTYPE == DRIFT_Q4_0 ? __ldg(reinterpret_cast<const int*>(rec + 800) + v) : 0;
+  x.fsum = T::DTYPE == DRIFT_Q4_1 ? __ldg(reinterpret_cast<const float*>(rec + 832) + v) : 0.0f;
+}
+
+// ---- dp4a modes: 1 or 2 vectors --------------------------------------------------------------
+// Lane l takes rows l and l + 32 of the tile. A half segment (4 blocks) of
+// each row comes out of shared memory in 16-byte reads; each block's codes
+// meet x's planes -- the same for every lane, broadcast loads shared by the
+// two rows -- in 24 dp4a, and acc = fmaf(s, value, acc) with the same value
+// and order as the MMA mode: the plane sums are exact integers either way, so
+// a row's result does not depend on the mode.
+template <typename T, int V, int HALF>
+__device__ __forceinline__ void half_dp4a(const uint8_t* row0, const uint8_t* row1,
+                                          const uint8_t* rec0, int count, float (&acc)[2][4]) {
+  constexpr int B0 = HALF * 4;
+  constexpr int START = B0 * T::BYTES, END = (B0 + 4) * T::BYTES;
+  uint32_t w0[(END - START) / 4], w1[(END - START) / 4];
+  lds_span<START, END>(row0, w0);
+  lds_span<START, END>(row1, w1);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int b = B0 + i;
+    if (b < count) {
+      const int word = (b * T::BYTES) / 4 - START / 4;
+      uint32_t a[T::WORDS], c[T::WORDS];
+#pragma unroll
+      for (int j = 0; j < T::WORDS; ++j) {
+        a[j] = w0[word + j];
+        c[j] = w1[word + j];
+      }
+      const Codes r0 = T::decode(a, b), r1 = T::decode(c, b);
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        XBlock x;
+        load_x<T>(rec0 + b * MMA_RECORD_BYTES, v, x);
+        int p0, p1, p2;
+        plane_sums<T>(r0, x.planes, p0, p1, p2);
+        acc[0][v] = fmaf(x.s, mma_block_value<T>(p0, p1, p2, r0.d, r0.m, x.sum, x.fsum), acc[0][v]);
+        plane_sums<T>(r1, x.planes, p0, p1, p2);
+        acc[1][v] = fmaf(x.s, mma_block_value<T>(p0, p1, p2, r1.d, r1.m, x.sum, x.fsum), acc[1][v]);
+      }
+    }
+  }
+}
+
+template <typename T, int V>
+__device__ __forceinline__ void segment_dp4a(const uint8_t* stage, int first_block, int count,
+                                             const uint8_t* __restrict__ records,
+                                             float (&acc)[2][4]) {
+  const int lane = threadIdx.x % WARP;
+  const uint8_t* row0 = stage + lane * Ring<T>::PITCH;
+  const uint8_t* row1 = row0 + 32 * Ring<T>::PITCH;
+  const uint8_t* rec0 = records + (long long)first_block * MMA_RECORD_BYTES;
+  if (count == SEG_BLOCKS) {
+    half_dp4a<T, V, 0>(row0, row1, rec0, SEG_BLOCKS, acc);
+    half_dp4a<T, V, 1>(row0, row1, rec0, SEG_BLOCKS, acc);
+  } else {
+    half_dp4a<T, V, 0>(row0, row1, rec0, count, acc);
+    if (count > 4) half_dp4a<T, V, 1>(row0, row1, rec0, count, acc);
+  }
+}
+
+// ---- MMA mode: 3-8 vectors -------------------------------------------------------------------
 // acc[i][.] gains the segment's blocks for rows (16 i + g, 16 i + g + 8) and
 // vectors (2t, 2t + 1), each as acc = fmaf(s, value, acc).
 template <typename T>
 __device__ __forceinline__ void segment_mma(const uint8_t* stage, int first_block, int count,
                                             const uint8_t* __restrict__ records, int vectors,
-                                            float (&acc)[2][4]) {
+                                            float (&acc)[4][4]) {
   const int lane = threadIdx.x % WARP, g = lane / 4, t = lane % 4;
   const bool have_vector = g < vectors;
   const uint8_t* rec0 = records + (long long)first_block * MMA_RECORD_BYTES;
-  const uint8_t* rows_lo[2] = {stage + g * Ring<T>::PITCH, stage + (16 + g) * Ring<T>::PITCH};
+  const uint8_t* row_g = stage + g * Ring<T>::PITCH;
 #pragma unroll
   for (int b = 0; b < SEG_BLOCKS; ++b) {
     if (b < count) {
@@ -87,11 +197,11 @@ __device__ __forceinline__ void segment_mma(const uint8_t* stage, int first_bloc
       if (T::DTYPE == DRIFT_Q4_0) sum = __ldg(reinterpret_cast<const int2*>(rec + 800) + t);
       if (T::DTYPE == DRIFT_Q4_1) fsum = __ldg(reinterpret_cast<const float2*>(rec + 832) + t);
 #pragma unroll
-      for (int i = 0; i < 2; ++i) {
+      for (int i = 0; i < 4; ++i) {
         uint32_t lo0, hi0, lo1, hi1;
         float d0, m0, d1, m1;
-        fragment_row<T, SharedWords>(rows_lo[i], b, t, lo0, hi0, d0, m0);
-        fragment_row<T, SharedWords>(rows_lo[i] + 8 * Ring<T>::PITCH, b, t, lo1, hi1, d1, m1);
+        fragment_row<T, SharedWords>(row_g + 16 * i * Ring<T>::PITCH, b, t, lo0, hi0, d0, m0);
+        fragment_row<T, SharedWords>(row_g + (16 * i + 8) * Ring<T>::PITCH, b, t, lo1, hi1, d1, m1);
         const uint32_t a[4] = {lo0, lo1, hi0, hi1};
         int p0[4], p1[4], p2[4];
         mma_i8_zero<T::SIGNED, false>(p0, a, planes[0].x, planes[0].y);
@@ -106,134 +216,105 @@ __device__ __forceinline__ void segment_mma(const uint8_t* stage, int first_bloc
   }
 }
 
-// ---- dp4a modes: 1 or 2 vectors ------------------------------------------------------------
-// Lane r takes row r of the tile: its 8 blocks come out of shared memory in
-// 16-byte reads, each block's codes meet x's planes (the same for every lane:
-// broadcast loads) in 24 dp4a, and acc[v] = fmaf(s, value, acc[v]) with the
-// same value and the same order as the MMA mode -- the plane sums are exact
-// integers either way -- so a row's result does not depend on the mode.
-template <typename T, int V>
-__device__ __forceinline__ void segment_dp4a(const uint8_t* stage, int first_block, int count,
-                                             const uint8_t* __restrict__ records, float (&acc)[4]) {
-  constexpr int SEG = Ring<T>::SEG;
-  constexpr int WORDS = SEG / 4;
-  const int lane = threadIdx.x % WARP;
-  uint32_t row[WORDS];
-  const uint4* src = reinterpret_cast<const uint4*>(stage + lane * Ring<T>::PITCH);
+// The accumulators of a warp: dp4a modes acc[r][v] for rows lane + 32 r;
+// MMA mode acc[i][e] for the fragment of rows 16 i + g (+8), vectors 2t (+1).
+template <int MODE>
+struct Acc {
+  float a[MODE == MODE_MMA ? 4 : 2][4];
+  __device__ void zero() {
 #pragma unroll
-  for (int i = 0; i < SEG / 16; ++i) {
-    const uint4 q = src[i];
-    row[4 * i] = q.x;
-    row[4 * i + 1] = q.y;
-    row[4 * i + 2] = q.z;
-    row[4 * i + 3] = q.w;
+    for (int i = 0; i < (MODE == MODE_MMA ? 4 : 2); ++i) a[i][0] = a[i][1] = a[i][2] = a[i][3] = 0.0f;
   }
-  const uint8_t* rec0 = records + (long long)first_block * MMA_RECORD_BYTES;
+  // call f(row within the tile, vector, value) for each output this lane holds
+  template <typename F>
+  __device__ void each(F f) const {
+    const int lane = threadIdx.x % WARP, g = lane / 4, t = lane % 4;
+    if constexpr (MODE == MODE_MMA) {
 #pragma unroll
-  for (int b = 0; b < SEG_BLOCKS; ++b) {
-    if (b < count) {
-      const int word = (b * T::BYTES) / 4;
-      uint32_t w[T::WORDS];
-#pragma unroll
-      for (int i = 0; i < T::WORDS; ++i) w[i] = (word + i < WORDS) ? row[word + i] : 0u;
-      const Codes codes = T::decode(w, b);
-      const uint8_t* rec = rec0 + b * MMA_RECORD_BYTES;
-#pragma unroll
-      for (int v = 0; v < V; ++v) {
-        uint32_t planes[24];
-#pragma unroll
-        for (int p = 0; p < 3; ++p) {
-          const uint4* q = reinterpret_cast<const uint4*>(rec + 256 * p + 32 * v);
-          const uint4 q0 = __ldg(q), q1 = __ldg(q + 1);
-          planes[8 * p + 0] = q0.x;
-          planes[8 * p + 4] = q0.y;
-          planes[8 * p + 1] = q0.z;
-          planes[8 * p + 5] = q0.w;
-          planes[8 * p + 2] = q1.x;
-          planes[8 * p + 6] = q1.y;
-          planes[8 * p + 3] = q1.z;
-          planes[8 * p + 7] = q1.w;
-        }
-        const float s = __ldg(reinterpret_cast<const float*>(rec + 768) + v);
-        int sum = 0;
-        float fsum = 0.0f;
-        if (T::DTYPE == DRIFT_Q4_0) sum = __ldg(reinterpret_cast<const int*>(rec + 800) + v);
-        if (T::DTYPE == DRIFT_Q4_1) fsum = __ldg(reinterpret_cast<const float*>(rec + 832) + v);
-        int a0, a1, a2;
-        plane_sums<T>(codes, planes, a0, a1, a2);
-        acc[v] = fmaf(s, mma_block_value<T>(a0, a1, a2, codes.d, codes.m, sum, fsum), acc[v]);
+      for (int i = 0; i < 4; ++i) {
+        f(16 * i + g, 2 * t, a[i][0]);
+        f(16 * i + g, 2 * t + 1, a[i][1]);
+        f(16 * i + g + 8, 2 * t, a[i][2]);
+        f(16 * i + g + 8, 2 * t + 1, a[i][3]);
       }
+    } else {
+#pragma unroll
+      for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int v = 0; v < MODE; ++v) f(lane + 32 * r, v, a[r][v]);
     }
   }
-}
+};
 
-// Grid (tiles schedule, KS = 1): at most one CTA per SM.
-// Grid (split schedule): ceil(tiles / (WARPS / KS)) CTAs, one unit each.
-template <typename T, int KS, int S, int WARPS, int MODE>
-__global__ void __launch_bounds__(WARPS * 32, 1)
+// The CTA's schedule. CTA c owns tiles [t0, t0 + count), an even share of the
+// matrix's. Its W warps take them in rounds -- warp w sums tile t0 + f W + w
+// whole in round f -- and the (count mod W) tiles left over are split by
+// segments, P = W / left warps to a tile, whose partial sums meet in shared
+// memory in a fixed order. All of it follows from rows, cols and the grid,
+// never from the number of vectors.
+struct Schedule {
+  int t0, rounds, left, parts, segments, warps;
+  __device__ Schedule(int tiles, int segs, int w) : segments(segs), warps(w) {
+    t0 = int((long long)tiles * blockIdx.x / gridDim.x);
+    const int t1 = int((long long)tiles * (blockIdx.x + 1) / gridDim.x);
+    rounds = (t1 - t0) / w;
+    left = (t1 - t0) % w;
+    parts = left ? w / left : 1;
+  }
+  __device__ bool shares(int w) const { return w < left * parts; }
+  __device__ int share_tile(int w) const { return t0 + rounds * warps + w / parts; }
+  __device__ int share_begin(int w) const { return int((long long)segments * (w % parts) / parts); }
+  __device__ int share_end(int w) const { return int((long long)segments * (w % parts + 1) / parts); }
+  // job j of warp w: (tile, segment)
+  __device__ void job(int w, int j, int& tile, int& segment) const {
+    const int whole = rounds * segments;
+    if (j < whole) {
+      tile = t0 + (j / segments) * warps + w;
+      segment = j % segments;
+    } else {
+      tile = share_tile(w);
+      segment = share_begin(w) + (j - whole);
+    }
+  }
+  __device__ int jobs(int w) const {
+    return rounds * segments + (shares(w) ? share_end(w) - share_begin(w) : 0);
+  }
+};
+
+template <typename T, int MODE>
+__global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
     matvec_ring_kernel(const __grid_constant__ CUtensorMap wmap,
                        const uint8_t* __restrict__ records, float* __restrict__ y, int rows,
                        int cols, int vectors, int* error) {
-  using L = RingLayout<T, KS, S, WARPS>;
-  constexpr int GROUPS = WARPS / KS;
+  using Shape = RingShape<T>;
+  constexpr int W = Shape::WARPS, S = Shape::S, STAGE = Ring<T>::STAGE;
+  constexpr int VSLOTS = MODE == MODE_MMA ? 8 : MODE;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   const int warp = threadIdx.x / WARP, lane = threadIdx.x % WARP;
-  const int g = lane / 4, t = lane % 4;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BARS) + warp * S;
-  uint8_t* ring = smem + warp * S * L::STAGE;
-  int* counter = reinterpret_cast<int*>(smem + L::COUNTER);
-  volatile int* abort = counter + 1;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Shape::BARS) + warp * S;
+  volatile int* abort = reinterpret_cast<int*>(smem + Shape::BARS + W * S * 8);
+  uint8_t* ring = smem + warp * S * STAGE;
 
   const int blocks = cols / 32;
   const int segments = (blocks + SEG_BLOCKS - 1) / SEG_BLOCKS;
-  const int tiles = (rows + ROWS - 1) / ROWS;
-  const int kw = warp % KS, slot = warp / KS;
-  const int seg0 = int((long long)segments * kw / KS), seg1 = int((long long)segments * (kw + 1) / KS);
-  const int nseg = seg1 - seg0;  // segments per tile for this warp
+  const Schedule plan((rows + ROWS - 1) / ROWS, segments, W);
+  const int jobs = plan.jobs(warp);
 
-  // the CTA's tiles: a contiguous range (tiles schedule) or its unit's
-  const int range0 = KS == 1 ? int((long long)tiles * blockIdx.x / gridDim.x) : 0;
-  const int range1 = KS == 1 ? int((long long)tiles * (blockIdx.x + 1) / gridDim.x) : 0;
-  if (threadIdx.x == 0) {
-    *counter = range0;
-    *abort = 0;
-  }
+  if (threadIdx.x == 0) *abort = 0;
   if (lane < S) tc::mbar_init(&bars[lane], 1);
   tc::fence_barrier_init();
   __syncthreads();
 
-  // this warp's claimed tiles, in order (a short queue: at most S segments ahead)
-  int claimed[8];
-  int claimed_count = 0;
-  bool more = nseg > 0;
-  auto claim = [&]() -> bool {
-    int tile;
-    if (KS == 1) {
-      int next = 0;
-      if (lane == 0) next = atomicAdd(counter, 1);
-      tile = __shfl_sync(0xffffffffu, next, 0);
-      if (tile >= range1) return false;
-    } else {
-      if (claimed_count > 0) return false;  // one unit per CTA
-      tile = blockIdx.x * GROUPS + slot;
-      if (tile >= tiles) return false;
-    }
-    claimed[claimed_count % 8] = tile;
-    ++claimed_count;
-    return true;
-  };
-  // job j: segment seg0 + j % nseg of tile claimed[j / nseg], one 2-D tensor
-  // copy of 32 rows x SEG bytes (rows past the matrix, and columns past a row,
-  // arrive as zeros)
+  // job j: one 2-D tensor copy of 64 rows x PITCH bytes (rows past the
+  // matrix, and columns past a row, arrive as zeros)
   auto issue = [&](int j) {
-    const int tile = claimed[(j / nseg) % 8];
-    const int segment = seg0 + j % nseg;
-    uint64_t* bar = &bars[j % S];
+    int tile, segment;
+    plan.job(warp, j, tile, segment);
     if (lane == 0) {
-      tc::mbar_expect_tx(bar, uint32_t(L::STAGE));
-      tc::tma_load_2d(ring + (j % S) * L::STAGE, &wmap, bar, segment * (Ring<T>::SEG / 4),
+      tc::mbar_expect_tx(&bars[j % S], uint32_t(STAGE));
+      tc::tma_load_2d(ring + (j % S) * STAGE, &wmap, &bars[j % S], segment * (Ring<T>::SEG / 4),
                       tile * ROWS);
     }
     __syncwarp();
@@ -241,173 +322,101 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
 
   int issued = 0, consumed = 0;
   bool ok = true;
-  while (more && issued < S) {
-    if (issued / nseg == claimed_count && !claim()) {
-      more = false;
-      break;
-    }
-    issue(issued++);
-  }
-  float acc[2][4];
-#pragma unroll
-  for (int i = 0; i < 2; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
+  while (issued < jobs && issued < S) issue(issued++);
+  Acc<MODE> acc;
+  acc.zero();
+  const int whole = plan.rounds * segments;
   while (consumed < issued) {
     const int j = consumed;
-    const int segment = seg0 + j % nseg;
-    if (j % nseg == 0) {
-#pragma unroll
-      for (int i = 0; i < 2; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
-    }
+    int tile, segment;
+    plan.job(warp, j, tile, segment);
     if (ok) ok = tc::mbar_wait_warp(&bars[j % S], (j / S) & 1, abort, error);
     if (ok) {
       const int first = segment * SEG_BLOCKS;
       const int count = blocks - first < SEG_BLOCKS ? blocks - first : SEG_BLOCKS;
       if constexpr (MODE == MODE_MMA)
-        segment_mma<T>(ring + (j % S) * L::STAGE, first, count, records, vectors, acc);
+        segment_mma<T>(ring + (j % S) * STAGE, first, count, records, vectors, acc.a);
       else
-        segment_dp4a<T, MODE>(ring + (j % S) * L::STAGE, first, count, records, acc[0]);
+        segment_dp4a<T, MODE>(ring + (j % S) * STAGE, first, count, records, acc.a);
     }
     __syncwarp();
     ++consumed;
-    // refill the freed stage
-    if (ok && more) {
-      if (issued / nseg == claimed_count && !claim())
-        more = false;
-      else
-        issue(issued++);
-    }
-    if (KS == 1 && j % nseg == nseg - 1) {
-      // whole rows: write them
-      const int tile = claimed[(j / nseg) % 8];
-      if constexpr (MODE == MODE_MMA) {
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          const int r0 = tile * ROWS + 16 * i + g, r1 = r0 + 8;
-          if (r0 < rows) {
-            if (2 * t < vectors) y[(long long)(2 * t) * rows + r0] = acc[i][0];
-            if (2 * t + 1 < vectors) y[(long long)(2 * t + 1) * rows + r0] = acc[i][1];
-          }
-          if (r1 < rows) {
-            if (2 * t < vectors) y[(long long)(2 * t) * rows + r1] = acc[i][2];
-            if (2 * t + 1 < vectors) y[(long long)(2 * t + 1) * rows + r1] = acc[i][3];
-          }
-        }
-      } else {
-        const int row = tile * ROWS + lane;
-        if (row < rows) {
-#pragma unroll
-          for (int v = 0; v < MODE; ++v)
-            if (v < vectors) y[(long long)v * rows + row] = acc[0][v];
-        }
-      }
+    if (ok && issued < jobs) issue(issued++);  // refill the freed stage
+    if (j < whole && segment == segments - 1) {
+      // a whole tile: write its rows, start the next
+      acc.each([&](int r, int v, float value) {
+        const int row = tile * ROWS + r;
+        if (row < rows && v < vectors) y[(long long)v * rows + row] = value;
+      });
+      acc.zero();
     }
   }
-  if (KS > 1) {
-    // this warp's share of its unit's tile, then the shares in order
-    float* partial = reinterpret_cast<float*>(smem + L::PARTIAL);
-    float* mine = partial + ((kw * GROUPS + slot) * ROWS) * 8;
-    if constexpr (MODE == MODE_MMA) {
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        mine[(16 * i + g) * 8 + 2 * t] = acc[i][0];
-        mine[(16 * i + g) * 8 + 2 * t + 1] = acc[i][1];
-        mine[(16 * i + g + 8) * 8 + 2 * t] = acc[i][2];
-        mine[(16 * i + g + 8) * 8 + 2 * t + 1] = acc[i][3];
-      }
-    } else {
-#pragma unroll
-      for (int v = 0; v < MODE; ++v) mine[lane * 8 + v] = acc[0][v];
-    }
+  if (!ok) {
+    // let the copies already issued land before the ring is reused or left
+    volatile int never = 0;
+    for (int j = consumed; j < issued; ++j) tc::mbar_wait(&bars[j % S], (j / S) & 1, &never, nullptr);
+  }
+  if (plan.left > 0) {
+    // the leftover tiles: shares in shared memory (the drained rings), then
+    // summed in share order
     __syncthreads();
-    for (int e = threadIdx.x; e < GROUPS * ROWS * 8; e += blockDim.x) {
-      const int gi = e / (ROWS * 8), r = (e / 8) % ROWS, v = e % 8;
-      const int row = (blockIdx.x * GROUPS + gi) * ROWS + r;
+    float* partial = reinterpret_cast<float*>(smem);  // [W][ROWS][VSLOTS]
+    if (plan.shares(warp))
+      acc.each([&](int r, int v, float value) {
+        if (v < VSLOTS) partial[(warp * ROWS + r) * VSLOTS + v] = value;
+      });
+    __syncthreads();
+    for (int e = threadIdx.x; e < plan.left * ROWS * VSLOTS; e += blockDim.x) {
+      const int l = e / (ROWS * VSLOTS), r = (e / VSLOTS) % ROWS, v = e % VSLOTS;
+      const int row = (plan.t0 + plan.rounds * W + l) * ROWS + r;
       if (row < rows && v < vectors) {
         float total = 0.0f;
-#pragma unroll
-        for (int k = 0; k < KS; ++k) total += partial[((k * GROUPS + gi) * ROWS + r) * 8 + v];
+        for (int p = 0; p < plan.parts; ++p)
+          total += partial[(((l * plan.parts) + p) * ROWS + r) * VSLOTS + v];
         y[(long long)v * rows + row] = total;
       }
     }
   }
-  if (!ok) {
-    // let the copies already issued land before the CTA leaves
-    volatile int never = 0;
-    for (int j = consumed; j < issued; ++j) tc::mbar_wait(&bars[j % S], (j / S) & 1, &never, nullptr);
-  }
 }
 
-template <typename T, int KS, int S, int WARPS, int MODE>
+template <typename T, int MODE>
 int launch_mode(const CUtensorMap& wmap, const uint8_t* records, float* y, int rows, int cols,
                 int vectors, cudaStream_t stream) {
-  using L = RingLayout<T, KS, S, WARPS>;
+  using Shape = RingShape<T>;
   static bool configured = false;
   if (!configured) {
-    DRIFT_CUDA(cudaFuncSetAttribute(matvec_ring_kernel<T, KS, S, WARPS, MODE>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES));
+    DRIFT_CUDA(cudaFuncSetAttribute(matvec_ring_kernel<T, MODE>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, Shape::BYTES));
     configured = true;
   }
   const int tiles = (rows + ROWS - 1) / ROWS;
-  unsigned grid;
-  if (KS == 1)
-    grid = unsigned(tiles < sm_count() ? tiles : sm_count());
-  else
-    grid = unsigned((tiles + (WARPS / KS) - 1) / (WARPS / KS));
-  matvec_ring_kernel<T, KS, S, WARPS, MODE><<<grid, WARPS * 32, L::BYTES, stream>>>(
+  const unsigned grid = unsigned(tiles < sm_count() ? tiles : sm_count());
+  matvec_ring_kernel<T, MODE><<<grid, Shape::WARPS * 32, Shape::BYTES, stream>>>(
       wmap, records, y, rows, cols, vectors, device_error_word());
   DRIFT_LAUNCHED("matvec_ring");
   return 0;
 }
 
-template <typename T, int KS, int S, int WARPS>
-int launch_ring(const uint8_t* weight, const uint8_t* records, float* y, int rows, int cols,
-                int vectors, cudaStream_t stream) {
-  CUtensorMap wmap;
-  DRIFT_TRY(encode_word_rows(&wmap, weight, int64_t(cols / 32) * T::BYTES / 4, rows,
-                             Ring<T>::SEG / 4, ROWS));
-  if (vectors == 1)
-    return launch_mode<T, KS, S, WARPS, MODE_DP4A_1>(wmap, records, y, rows, cols, vectors, stream);
-  if (vectors == 2)
-    return launch_mode<T, KS, S, WARPS, MODE_DP4A_2>(wmap, records, y, rows, cols, vectors, stream);
-  return launch_mode<T, KS, S, WARPS, MODE_MMA>(wmap, records, y, rows, cols, vectors, stream);
-}
-
-// The configuration of a matrix: the same for every number of vectors, so a
+// One configuration per matrix type, whatever the number of vectors, so a
 // row's blocks are summed in the same order whatever the batch.
 template <typename T>
 int ring_dispatch(const uint8_t* weight, const uint8_t* records, float* y, int rows, int cols,
                   int vectors, cudaStream_t stream) {
-  const int blocks = cols / 32;
-  const int segments = (blocks + SEG_BLOCKS - 1) / SEG_BLOCKS;
-  const long long tiles = (rows + ROWS - 1) / ROWS;
-  const int sms = sm_count();
-  constexpr int WIDE = T::DTYPE == DRIFT_Q8_0 ? 12 : 16;  // warps per CTA (272-byte segments: 12)
-  // Many rows: whole tiles per warp, tiles claimed within the CTA's range.
-  if (tiles >= 2LL * WIDE * sms)
-    return launch_ring<T, 1, 2, WIDE>(weight, records, y, rows, cols, vectors, stream);
-  // Fewer rows: split each tile's segments between warps so every SM works.
-  int ks = 2;
-  while (ks < 8 && ks * 2 <= segments && tiles * ks < 8LL * sms) ks *= 2;
-  switch (ks) {
-    case 8: return launch_ring<T, 8, 3, 8>(weight, records, y, rows, cols, vectors, stream);
-    case 4: return launch_ring<T, 4, 3, 8>(weight, records, y, rows, cols, vectors, stream);
-    default: return launch_ring<T, 2, 3, 8>(weight, records, y, rows, cols, vectors, stream);
-  }
+  CUtensorMap wmap;
+  DRIFT_TRY(encode_word_rows(&wmap, weight, int64_t(cols / 32) * T::BYTES / 4, rows,
+                             Ring<T>::PITCH / 4, ROWS));
+  if (vectors == 1) return launch_mode<T, MODE_DP4A_1>(wmap, records, y, rows, cols, vectors, stream);
+  if (vectors == 2) return launch_mode<T, MODE_DP4A_2>(wmap, records, y, rows, cols, vectors, stream);
+  return launch_mode<T, MODE_MMA>(wmap, records, y, rows, cols, vectors, stream);
 }
 
-#define DRIFT_RING_REGISTER(T, name, wide)                                                      \
-  DRIFT_REGISTER(matvec_ring_##name##_tiles_dp4a1, (matvec_ring_kernel<T, 1, 2, wide, 1>))     \
-  DRIFT_REGISTER(matvec_ring_##name##_tiles_dp4a2, (matvec_ring_kernel<T, 1, 2, wide, 2>))     \
-  DRIFT_REGISTER(matvec_ring_##name##_tiles_mma, (matvec_ring_kernel<T, 1, 2, wide, 8>))       \
-  DRIFT_REGISTER(matvec_ring_##name##_ks2_dp4a1, (matvec_ring_kernel<T, 2, 3, 8, 1>))          \
-  DRIFT_REGISTER(matvec_ring_##name##_ks4_dp4a1, (matvec_ring_kernel<T, 4, 3, 8, 1>))          \
-  DRIFT_REGISTER(matvec_ring_##name##_ks8_dp4a1, (matvec_ring_kernel<T, 8, 3, 8, 1>))          \
-  DRIFT_REGISTER(matvec_ring_##name##_ks2_mma, (matvec_ring_kernel<T, 2, 3, 8, 8>))            \
-  DRIFT_REGISTER(matvec_ring_##name##_ks4_mma, (matvec_ring_kernel<T, 4, 3, 8, 8>))            \
-  DRIFT_REGISTER(matvec_ring_##name##_ks8_mma, (matvec_ring_kernel<T, 8, 3, 8, 8>))
-DRIFT_RING_REGISTER(Q8_0T, q8_0, 12)
-DRIFT_RING_REGISTER(Q4_0T, q4_0, 16)
-DRIFT_RING_REGISTER(Q4_1T, q4_1, 16)
+#define DRIFT_RING_REGISTER(T, name)                                              \
+  DRIFT_REGISTER(matvec_ring_##name##_dp4a1, (matvec_ring_kernel<T, MODE_DP4A_1>)) \
+  DRIFT_REGISTER(matvec_ring_##name##_dp4a2, (matvec_ring_kernel<T, MODE_DP4A_2>)) \
+  DRIFT_REGISTER(matvec_ring_##name##_mma, (matvec_ring_kernel<T, MODE_MMA>))
+DRIFT_RING_REGISTER(Q8_0T, q8_0)
+DRIFT_RING_REGISTER(Q4_0T, q4_0)
+DRIFT_RING_REGISTER(Q4_1T, q4_1)
 
 }  // namespace
 
