@@ -117,22 +117,33 @@ __device__ __forceinline__ void load_x(const uint8_t* rec, int v, XBlock& x) {
 // Lane l takes rows l and l + 32 of the tile. A half segment (4 blocks) of
 // each row comes out of shared memory in 16-byte reads; each block's codes
 // meet x's planes -- the same for every lane, broadcast loads shared by the
-// two rows -- in 24 dp4a, and acc = fmaf(s, value, acc) with the same value
-// and order as the MMA mode: the plane sums are exact integers either way, so
-// a row's result does not depend on the mode.
-template <typename T, int V, int HALF>
-__device__ __forceinline__ void half_dp4a(const uint8_t* row0, const uint8_t* row1,
-                                          const uint8_t* rec0, int count, float (&acc)[2][4]) {
-  constexpr int B0 = HALF * 4;
-  constexpr int START = B0 * T::BYTES, END = (B0 + 4) * T::BYTES;
-  uint32_t w0[(END - START) / 4], w1[(END - START) / 4];
-  lds_span<START, END>(row0, w0);
-  lds_span<START, END>(row1, w1);
+// two rows, fetched one block ahead -- in 24 dp4a, and acc = fmaf(s, value,
+// acc) with the same value and order as the MMA mode: the plane sums are
+// exact integers either way, so a row's result does not depend on the mode.
+template <typename T, int V, bool FULL>
+__device__ __forceinline__ void segment_dp4a_blocks(const uint8_t* row0, const uint8_t* row1,
+                                                    const uint8_t* rec0, int count,
+                                                    float (&acc)[2][4]) {
+  constexpr int HALF = 4 * T::BYTES;  // bytes of 4 blocks: 80, 72 or 136
+  uint32_t w0[HALF / 4], w1[HALF / 4];
+  XBlock x[2][V];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int b = B0 + i;
-    if (b < count) {
-      const int word = (b * T::BYTES) / 4 - START / 4;
+  for (int v = 0; v < V; ++v) load_x<T>(rec0, v, x[0][v]);
+#pragma unroll
+  for (int b = 0; b < SEG_BLOCKS; ++b) {
+    if (FULL || b < count) {
+      if (b == 0) {
+        lds_span<0, HALF>(row0, w0);
+        lds_span<0, HALF>(row1, w1);
+      } else if (b == 4) {
+        lds_span<HALF, 2 * HALF>(row0, w0);
+        lds_span<HALF, 2 * HALF>(row1, w1);
+      }
+      if (b + 1 < SEG_BLOCKS && (FULL || b + 1 < count)) {
+#pragma unroll
+        for (int v = 0; v < V; ++v) load_x<T>(rec0 + (b + 1) * MMA_RECORD_BYTES, v, x[(b + 1) & 1][v]);
+      }
+      const int word = (b * T::BYTES) / 4 - (b >= 4 ? HALF / 4 : 0);
       uint32_t a[T::WORDS], c[T::WORDS];
 #pragma unroll
       for (int j = 0; j < T::WORDS; ++j) {
@@ -142,13 +153,12 @@ __device__ __forceinline__ void half_dp4a(const uint8_t* row0, const uint8_t* ro
       const Codes r0 = T::decode(a, b), r1 = T::decode(c, b);
 #pragma unroll
       for (int v = 0; v < V; ++v) {
-        XBlock x;
-        load_x<T>(rec0 + b * MMA_RECORD_BYTES, v, x);
+        const XBlock& xv = x[b & 1][v];
         int p0, p1, p2;
-        plane_sums<T>(r0, x.planes, p0, p1, p2);
-        acc[0][v] = fmaf(x.s, mma_block_value<T>(p0, p1, p2, r0.d, r0.m, x.sum, x.fsum), acc[0][v]);
-        plane_sums<T>(r1, x.planes, p0, p1, p2);
-        acc[1][v] = fmaf(x.s, mma_block_value<T>(p0, p1, p2, r1.d, r1.m, x.sum, x.fsum), acc[1][v]);
+        plane_sums<T>(r0, xv.planes, p0, p1, p2);
+        acc[0][v] = fmaf(xv.s, mma_block_value<T>(p0, p1, p2, r0.d, r0.m, xv.sum, xv.fsum), acc[0][v]);
+        plane_sums<T>(r1, xv.planes, p0, p1, p2);
+        acc[1][v] = fmaf(xv.s, mma_block_value<T>(p0, p1, p2, r1.d, r1.m, xv.sum, xv.fsum), acc[1][v]);
       }
     }
   }
@@ -162,40 +172,50 @@ __device__ __forceinline__ void segment_dp4a(const uint8_t* stage, int first_blo
   const uint8_t* row0 = stage + lane * Ring<T>::PITCH;
   const uint8_t* row1 = row0 + 32 * Ring<T>::PITCH;
   const uint8_t* rec0 = records + (long long)first_block * MMA_RECORD_BYTES;
-  if (count == SEG_BLOCKS) {
-    half_dp4a<T, V, 0>(row0, row1, rec0, SEG_BLOCKS, acc);
-    half_dp4a<T, V, 1>(row0, row1, rec0, SEG_BLOCKS, acc);
-  } else {
-    half_dp4a<T, V, 0>(row0, row1, rec0, count, acc);
-    if (count > 4) half_dp4a<T, V, 1>(row0, row1, rec0, count, acc);
-  }
+  if (count == SEG_BLOCKS)
+    segment_dp4a_blocks<T, V, true>(row0, row1, rec0, SEG_BLOCKS, acc);
+  else
+    segment_dp4a_blocks<T, V, false>(row0, row1, rec0, count, acc);
 }
 
 // ---- MMA mode: 3-8 vectors -------------------------------------------------------------------
-// acc[i][.] gains the segment's blocks for rows (16 i + g, 16 i + g + 8) and
-// vectors (2t, 2t + 1), each as acc = fmaf(s, value, acc).
+// x's fragment of one block for the MMA mode: lane (g, t) holds vector g's
+// plane words (t, t + 4) and s, sum for vectors 2t, 2t + 1.
+struct XFragment {
+  uint2 planes[3];
+  float2 s, fsum;
+  int2 sum;
+};
+
 template <typename T>
-__device__ __forceinline__ void segment_mma(const uint8_t* stage, int first_block, int count,
-                                            const uint8_t* __restrict__ records, int vectors,
-                                            float (&acc)[4][4]) {
-  const int lane = threadIdx.x % WARP, g = lane / 4, t = lane % 4;
-  const bool have_vector = g < vectors;
-  const uint8_t* rec0 = records + (long long)first_block * MMA_RECORD_BYTES;
-  const uint8_t* row_g = stage + g * Ring<T>::PITCH;
+__device__ __forceinline__ void load_fragment(const uint8_t* rec, bool have_vector, XFragment& x) {
+  const int lane = threadIdx.x % WARP, t = lane % 4;
+#pragma unroll
+  for (int p = 0; p < 3; ++p)
+    x.planes[p] = have_vector ? __ldg(reinterpret_cast<const uint2*>(rec) + p * 32 + lane)
+                              : make_uint2(0, 0);
+  x.s = __ldg(reinterpret_cast<const float2*>(rec + 768) + t);
+  x.sum = T::DTYPE == DRIFT_Q4_0 ? __ldg(reinterpret_cast<const int2*>(rec + 800) + t) : make_int2(0, 0);
+  x.fsum = T::DTYPE == DRIFT_Q4_1 ? __ldg(reinterpret_cast<const float2*>(rec + 832) + t)
+                                  : make_float2(0.0f, 0.0f);
+}
+
+// acc[i][.] gains the segment's blocks for rows (16 i + g, 16 i + g + 8) and
+// vectors (2t, 2t + 1), each as acc = fmaf(s, value, acc); x is fetched one
+// block ahead.
+template <typename T, bool FULL>
+__device__ __forceinline__ void segment_mma_blocks(const uint8_t* row_g, const uint8_t* rec0,
+                                                   int count, bool have_vector,
+                                                   float (&acc)[4][4]) {
+  const int t = threadIdx.x % 4;
+  XFragment x[2];
+  load_fragment<T>(rec0, have_vector, x[0]);
 #pragma unroll
   for (int b = 0; b < SEG_BLOCKS; ++b) {
-    if (b < count) {
-      const uint8_t* rec = rec0 + b * MMA_RECORD_BYTES;
-      uint2 planes[3] = {make_uint2(0, 0), make_uint2(0, 0), make_uint2(0, 0)};
-      if (have_vector) {
-#pragma unroll
-        for (int p = 0; p < 3; ++p) planes[p] = __ldg(reinterpret_cast<const uint2*>(rec) + p * 32 + lane);
-      }
-      const float2 s = __ldg(reinterpret_cast<const float2*>(rec + 768) + t);
-      int2 sum = make_int2(0, 0);
-      float2 fsum = make_float2(0.0f, 0.0f);
-      if (T::DTYPE == DRIFT_Q4_0) sum = __ldg(reinterpret_cast<const int2*>(rec + 800) + t);
-      if (T::DTYPE == DRIFT_Q4_1) fsum = __ldg(reinterpret_cast<const float2*>(rec + 832) + t);
+    if (FULL || b < count) {
+      if (b + 1 < SEG_BLOCKS && (FULL || b + 1 < count))
+        load_fragment<T>(rec0 + (b + 1) * MMA_RECORD_BYTES, have_vector, x[(b + 1) & 1]);
+      const XFragment& xb = x[b & 1];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         uint32_t lo0, hi0, lo1, hi1;
@@ -204,16 +224,29 @@ __device__ __forceinline__ void segment_mma(const uint8_t* stage, int first_bloc
         fragment_row<T, SharedWords>(row_g + (16 * i + 8) * Ring<T>::PITCH, b, t, lo1, hi1, d1, m1);
         const uint32_t a[4] = {lo0, lo1, hi0, hi1};
         int p0[4], p1[4], p2[4];
-        mma_i8_zero<T::SIGNED, false>(p0, a, planes[0].x, planes[0].y);
-        mma_i8_zero<T::SIGNED, false>(p1, a, planes[1].x, planes[1].y);
-        mma_i8_zero<T::SIGNED, true>(p2, a, planes[2].x, planes[2].y);
-        acc[i][0] = fmaf(s.x, mma_block_value<T>(p0[0], p1[0], p2[0], d0, m0, sum.x, fsum.x), acc[i][0]);
-        acc[i][1] = fmaf(s.y, mma_block_value<T>(p0[1], p1[1], p2[1], d0, m0, sum.y, fsum.y), acc[i][1]);
-        acc[i][2] = fmaf(s.x, mma_block_value<T>(p0[2], p1[2], p2[2], d1, m1, sum.x, fsum.x), acc[i][2]);
-        acc[i][3] = fmaf(s.y, mma_block_value<T>(p0[3], p1[3], p2[3], d1, m1, sum.y, fsum.y), acc[i][3]);
+        mma_i8_zero<T::SIGNED, false>(p0, a, xb.planes[0].x, xb.planes[0].y);
+        mma_i8_zero<T::SIGNED, false>(p1, a, xb.planes[1].x, xb.planes[1].y);
+        mma_i8_zero<T::SIGNED, true>(p2, a, xb.planes[2].x, xb.planes[2].y);
+        acc[i][0] = fmaf(xb.s.x, mma_block_value<T>(p0[0], p1[0], p2[0], d0, m0, xb.sum.x, xb.fsum.x), acc[i][0]);
+        acc[i][1] = fmaf(xb.s.y, mma_block_value<T>(p0[1], p1[1], p2[1], d0, m0, xb.sum.y, xb.fsum.y), acc[i][1]);
+        acc[i][2] = fmaf(xb.s.x, mma_block_value<T>(p0[2], p1[2], p2[2], d1, m1, xb.sum.x, xb.fsum.x), acc[i][2]);
+        acc[i][3] = fmaf(xb.s.y, mma_block_value<T>(p0[3], p1[3], p2[3], d1, m1, xb.sum.y, xb.fsum.y), acc[i][3]);
       }
     }
   }
+}
+
+template <typename T>
+__device__ __forceinline__ void segment_mma(const uint8_t* stage, int first_block, int count,
+                                            const uint8_t* __restrict__ records, int vectors,
+                                            float (&acc)[4][4]) {
+  const int lane = threadIdx.x % WARP, g = lane / 4;
+  const uint8_t* rec0 = records + (long long)first_block * MMA_RECORD_BYTES;
+  const uint8_t* row_g = stage + g * Ring<T>::PITCH;
+  if (count == SEG_BLOCKS)
+    segment_mma_blocks<T, true>(row_g, rec0, SEG_BLOCKS, g < vectors, acc);
+  else
+    segment_mma_blocks<T, false>(row_g, rec0, count, g < vectors, acc);
 }
 
 // The accumulators of a warp: dp4a modes acc[r][v] for rows lane + 32 r;
