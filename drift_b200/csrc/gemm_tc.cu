@@ -3,21 +3,27 @@
 // F16 and multiplied by hipBLAS with F32 compute, ops/HipLinear.scala:
 // 389-469, kernels/matvec.hip:801-810), fused into one persistent kernel.
 //
-// One CTA per SM, 10 warps, a tile of 128 weight rows x 64 vectors at a time:
-//  - warp 8 (TMA): streams each 256-column chunk of the tile's raw GGML blocks
-//    (a 2-D tensor copy, 128 rows) and the matching four 64-column tiles of x
-//    (F16, 128-byte swizzled, the UMMA canonical K-major layout) into a
-//    3-stage shared-memory ring;
-//  - warps 0-7 (dequant, two warpgroups taking alternate 64-column steps):
-//    each thread turns its row's two blocks into 64 F16 weights -- d * q + m
-//    rounded once, as the reference's dequantize_<t> does -- and stores them
-//    straight into tensor memory (tcgen05.st), which is where the MMA reads
-//    A from: the dequantized tile never touches shared memory;
-//  - warp 9 (MMA): one thread issues tcgen05.mma kind::f16 with A in TMEM, B
-//    in shared memory and the F32 accumulator in TMEM (128 x 64), committing
-//    to mbarriers that free the A buffers and ring stages.
-// After the last step of a tile, the dequant warps read the accumulator back
-// (tcgen05.ld) and store F32 out. Every wait is bounded (tc_common.cuh).
+// One CTA per SM, 18 warps, units of 128 weight rows x 64 vectors (x a
+// K-range of the columns, when a matrix has too few rows to fill the SMs):
+//  - warp 16 (TMA): streams each 256-column chunk of the unit's raw GGML
+//    blocks (a 2-D tensor copy, 128 rows) and the matching four 64-column
+//    tiles of x (F16, 128-byte swizzled, the UMMA canonical K-major layout)
+//    into a 3-stage shared-memory ring;
+//  - warps 0-15 (dequant, four warpgroups, warpgroup g taking 64-column step g
+//    of every chunk): each thread turns its row's two blocks into 64 F16
+//    weights -- d * q + m rounded once, as the reference's dequantize_<t>
+//    does -- and stores them straight into tensor memory (tcgen05.st), into
+//    its warpgroup's own A buffer, which is where the MMA reads A from: the
+//    dequantized tile never touches shared memory;
+//  - warp 17 (MMA): one thread issues tcgen05.mma kind::f16 with A in TMEM, B
+//    in shared memory and the F32 accumulator in TMEM (128 x 64, two of them
+//    so a unit's epilogue overlaps the next unit's products), committing to
+//    mbarriers that free the A buffers and ring stages.
+// One chunk into the next unit, the dequant warps read the last unit's
+// accumulator back (tcgen05.ld) and store F32 out -- or, for a unit that
+// holds a K-range, store it as a partial sum; the last of a tile's K-ranges
+// to finish adds the partials in K order, so the result does not depend on
+// which CTA finishes first. Every wait is bounded (tc_common.cuh).
 //
 // The weights' values within a 32-block come out of the unpacking in a
 // permuted order (pairs of nibbles that one LOP3 makes into an F16x2), so x
@@ -36,7 +42,6 @@
 namespace drift {
 
 int* device_error_word();
-int workspace_reserve(size_t bytes, void** pointer);
 
 namespace {
 
@@ -45,7 +50,6 @@ constexpr int TILE_VECTORS = 64;
 constexpr int CHUNK = 256;  // columns per ring stage
 constexpr int STEP = 64;    // columns per MMA step (one 128-byte swizzle atom of F16)
 constexpr int STAGES = 3;
-constexpr int THREADS = 320;
 constexpr int B_STAGE_BYTES = 4 * TILE_VECTORS * 128;  // four [64 vectors x 64 F16] tiles
 
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
@@ -83,6 +87,9 @@ __host__ __device__ constexpr int perm_q4(int p) {
 template <>
 struct Unpack<Q4_1T> {
   static constexpr int RAW_WORDS = 40;  // 8 blocks of 20 bytes
+  // a chunk's row as copied: 16 bytes past the chunk, so rows sit 44 words
+  // apart and 16-byte reads of one column of 8 rows hit 8 distinct bank groups
+  static constexpr int PITCH_WORDS = 44;
   __device__ static void block(const uint32_t* w, uint32_t* out) {
     const __half2 d = u2h(__byte_perm(w[0], 0, 0x1010));
     const __half2 m = u2h(__byte_perm(w[0], 0, 0x3232));
@@ -96,17 +103,14 @@ struct Unpack<Q4_1T> {
       out[4 * i + 3] = h2u(__hfma2(hi1, d, m));
     }
   }
-  __device__ static void step(const uint32_t* row, int sub, uint32_t (&out)[32]) {
-    const uint2* p = reinterpret_cast<const uint2*>(row + 10 * sub);  // 8-byte aligned
-    uint32_t w[10];
-#pragma unroll
-    for (int i = 0; i < 5; ++i) {
-      const uint2 v = p[i];
-      w[2 * i] = v.x;
-      w[2 * i + 1] = v.y;
-    }
-    block(w, out);
-    block(w + 5, out + 16);
+  // step SUB: bytes [40 SUB, 40 SUB + 40) of the row's chunk
+  template <int SUB>
+  __device__ static void step(const uint8_t* row, uint32_t (&out)[32]) {
+    constexpr int A = 40 * SUB, C0 = A & ~15, C1 = (A + 40 + 15) & ~15;
+    uint32_t w[(C1 - C0) / 4];
+    lds_span<C0, C1>(row, w);
+    block(w + (A - C0) / 4, out);
+    block(w + (A - C0) / 4 + 5, out + 16);
   }
   __host__ __device__ static constexpr int perm(int p) { return perm_q4(p); }
 };
@@ -114,6 +118,7 @@ struct Unpack<Q4_1T> {
 template <>
 struct Unpack<Q4_0T> {
   static constexpr int RAW_WORDS = 36;  // 8 blocks of 18 bytes
+  static constexpr int PITCH_WORDS = 36;  // 36 words apart: 16-byte reads are conflict-free
   // d: the block's f16 scale bits; q: its four nibble words
   __device__ static void block(uint32_t d_bits, const uint32_t* q, uint32_t* out) {
     const __half2 d = u2h(__byte_perm(d_bits, 0, 0x1010));
@@ -128,16 +133,18 @@ struct Unpack<Q4_0T> {
       out[4 * i + 3] = h2u(__hmul2(__hsub2(hi1, eight), d));
     }
   }
-  __device__ static void step(const uint32_t* row, int sub, uint32_t (&out)[32]) {
-    const uint32_t* p = row + 9 * sub;  // 36 bytes: block 0 at byte 0, block 1 at byte 18
-    uint32_t w[9];
-#pragma unroll
-    for (int i = 0; i < 9; ++i) w[i] = p[i];
+  // step SUB: bytes [36 SUB, 36 SUB + 36): block 0 at byte 0, block 1 at 18
+  template <int SUB>
+  __device__ static void step(const uint8_t* row, uint32_t (&out)[32]) {
+    constexpr int A = 36 * SUB, C0 = A & ~15, C1 = (A + 36 + 15) & ~15;
+    uint32_t w[(C1 - C0) / 4];
+    lds_span<C0, C1>(row, w);
+    const uint32_t* p = w + (A - C0) / 4;
     uint32_t q[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) q[i] = __funnelshift_r(w[i], w[i + 1], 16);
-    block(w[0], q, out);
-    block(w[4] >> 16, w + 5, out + 16);
+    for (int i = 0; i < 4; ++i) q[i] = __funnelshift_r(p[i], p[i + 1], 16);
+    block(p[0], q, out);
+    block(p[4] >> 16, p + 5, out + 16);
   }
   __host__ __device__ static constexpr int perm(int p) { return perm_q4(p); }
 };
@@ -145,6 +152,7 @@ struct Unpack<Q4_0T> {
 template <>
 struct Unpack<Q8_0T> {
   static constexpr int RAW_WORDS = 68;  // 8 blocks of 34 bytes
+  static constexpr int PITCH_WORDS = 68;
   // Signed codes c0..c3 of a word become (c0, c2), (c1, c3): bytes biased by
   // 128 under the magic exponent of 1024, less 1152.
   __device__ static void block(uint32_t d_bits, const uint32_t* q, uint32_t* out) {
@@ -159,16 +167,18 @@ struct Unpack<Q8_0T> {
       out[2 * i + 1] = h2u(__hmul2(p1, d));
     }
   }
-  __device__ static void step(const uint32_t* row, int sub, uint32_t (&out)[32]) {
-    const uint32_t* p = row + 17 * sub;  // 68 bytes: block 0 at byte 0, block 1 at byte 34
-    uint32_t w[17];
-#pragma unroll
-    for (int i = 0; i < 17; ++i) w[i] = p[i];
+  // step SUB: bytes [68 SUB, 68 SUB + 68): block 0 at byte 0, block 1 at 34
+  template <int SUB>
+  __device__ static void step(const uint8_t* row, uint32_t (&out)[32]) {
+    constexpr int A = 68 * SUB, C0 = A & ~15, C1 = (A + 68 + 15) & ~15;
+    uint32_t w[(C1 - C0) / 4];
+    lds_span<C0, C1>(row, w);
+    const uint32_t* p = w + (A - C0) / 4;
     uint32_t q[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) q[i] = __funnelshift_r(w[i], w[i + 1], 16);
-    block(w[0], q, out);
-    block(w[8] >> 16, w + 9, out + 16);
+    for (int i = 0; i < 8; ++i) q[i] = __funnelshift_r(p[i], p[i + 1], 16);
+    block(p[0], q, out);
+    block(p[8] >> 16, p + 9, out + 16);
   }
   // p = 4 i + 2 t + h -> 4 i + t + 2 h
   __host__ __device__ static constexpr int perm(int p) {
@@ -181,7 +191,11 @@ struct Unpack<Q8_0T> {
 // zero for v >= vectors. x is F32 or BF16 [vectors][k].
 template <typename T, bool BF16>
 __global__ void tc_prepare_x_kernel(const void* __restrict__ x, __half* __restrict__ out,
-                                    int vectors, int padded, int cols) {
+                                    int vectors, int padded, int cols, int* counters,
+                                    int count) {
+  // the split product's arrival counters start at zero
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += gridDim.x * blockDim.x)
+    counters[i] = 0;
   const long long total = (long long)padded * cols;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
@@ -199,21 +213,67 @@ __global__ void tc_prepare_x_kernel(const void* __restrict__ x, __half* __restri
 }
 
 // ---- the product ------------------------------------------------------------------------------
+constexpr int DEQUANT_WARPS = 16;
+constexpr int TMA_WARP = 16, MMA_WARP = 17;
+constexpr int TC_THREADS = 32 * (DEQUANT_WARPS + 2);
+// TMEM columns: accumulators 0-63 and 64-127, A buffer of warpgroup g at 128 + 32 g
+constexpr uint32_t TMEM_COLUMNS = 256;
+
 template <typename T>
 struct TcLayout {
-  static constexpr int RAW_BYTES = TILE_ROWS * Unpack<T>::RAW_WORDS * 4;
+  static constexpr int RAW_BYTES = TILE_ROWS * Unpack<T>::PITCH_WORDS * 4;
   static constexpr int RAW_PADDED = (RAW_BYTES + 1023) / 1024 * 1024;
   static constexpr int STAGE_BYTES = B_STAGE_BYTES + RAW_PADDED;
   static constexpr int BARRIER_OFFSET = STAGES * STAGE_BYTES;
-  // + full[S], empty[S], a_full[2], a_empty[2], acc_full, acc_empty, tmem slot, abort
+  // full[S], empty[S], a_full[4], a_empty[4], acc_full[2], acc_empty[2], tmem slot, abort
   static constexpr int SMEM_BYTES = BARRIER_OFFSET + 256 + 1024;  // + alignment slack
 };
 
+// What a CTA's units are: unit u is K-range u % splits of tile u / splits,
+// tile = pass * row_tiles + row tile.
+struct TcPlan {
+  int row_tiles, tiles, splits, chunks;
+  __device__ int units() const { return tiles * splits; }
+  __device__ int chunk_begin(int u) const { return int((long long)chunks * (u % splits) / splits); }
+  __device__ int chunk_end(int u) const { return int((long long)chunks * (u % splits + 1) / splits); }
+};
+
+// Scratch of the split products: partial sums [tile][split][64 vectors][128
+// rows] and one arrival counter per (tile, dequant warp), zeroed by
+// tc_prepare_x.
+struct TcScratch {
+  float* partial;
+  int* arrivals;
+};
+
+// 16 consecutive 32-bit columns of this thread's lane, to registers.
+__device__ __forceinline__ void tmem_load_16(uint32_t address, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15])
+      : "r"(address)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
 template <typename T>
-__global__ void __launch_bounds__(THREADS, 1)
+__device__ __forceinline__ void dequant_step(int group, const uint8_t* row, uint32_t (&a)[32]) {
+  switch (group) {
+    case 0: Unpack<T>::template step<0>(row, a); break;
+    case 1: Unpack<T>::template step<1>(row, a); break;
+    case 2: Unpack<T>::template step<2>(row, a); break;
+    default: Unpack<T>::template step<3>(row, a); break;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(TC_THREADS, 1)
     linear_tc_kernel(const __grid_constant__ CUtensorMap wmap,
                      const __grid_constant__ CUtensorMap xmap, float* __restrict__ y, int rows,
-                     int cols, int vectors, int row_tiles, int tiles, int* error) {
+                     int vectors, TcPlan plan, TcScratch scratch, int* error) {
   using L = TcLayout<T>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -222,46 +282,49 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
   uint64_t* a_full = bars + 2 * STAGES;
-  uint64_t* a_empty = a_full + 2;
-  uint64_t* acc_full = a_empty + 2;
-  uint64_t* acc_empty = acc_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
+  uint64_t* a_empty = a_full + 4;
+  uint64_t* acc_full = a_empty + 4;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int chunks = (cols + CHUNK - 1) / CHUNK;
+  const int units = plan.units();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       tc::mbar_init(&full[s], 1);
-      tc::mbar_init(&empty[s], 9);  // 8 dequant warps + the MMA's commit
+      tc::mbar_init(&empty[s], DEQUANT_WARPS + 1);  // the dequant warps + the MMA's commit
+    }
+    for (int g = 0; g < 4; ++g) {
+      tc::mbar_init(&a_full[g], 4);  // the four warps of a warpgroup
+      tc::mbar_init(&a_empty[g], 1);
     }
     for (int b = 0; b < 2; ++b) {
-      tc::mbar_init(&a_full[b], 4);  // the four warps of a warpgroup
-      tc::mbar_init(&a_empty[b], 1);
+      tc::mbar_init(&acc_full[b], 1);
+      tc::mbar_init(&acc_empty[b], DEQUANT_WARPS);
     }
-    tc::mbar_init(acc_full, 1);
-    tc::mbar_init(acc_empty, 8);
     *abort = 0;
     tc::fence_barrier_init();
   }
-  if (warp == 8 && lane == 0) {
+  if (warp == TMA_WARP && lane == 0) {
     tc::prefetch_tensor_map(&wmap);
     tc::prefetch_tensor_map(&xmap);
   }
-  if (warp == 0) tc::tmem_alloc(tmem_slot, 128);
+  if (warp == 0) tc::tmem_alloc(tmem_slot, TMEM_COLUMNS);
   __syncthreads();
   tc::fence_after_sync();
-  const uint32_t tmem = *tmem_slot;  // columns 0..63: accumulator; 64..127: two A buffers
+  const uint32_t tmem = *tmem_slot;
 
-  if (warp == 8) {
+  if (warp == TMA_WARP) {
     // ---- TMA producer ----
     if (lane == 0) {
       int gc = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
-        const int rt = tile % row_tiles, pass = tile / row_tiles;
-        for (int c = 0; c < chunks; ++c, ++gc) {
+      for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
+        const int tile = u / plan.splits;
+        const int rt = tile % plan.row_tiles, pass = tile / plan.row_tiles;
+        for (int c = plan.chunk_begin(u); c < plan.chunk_end(u); ++c, ++gc) {
           const int s = gc % STAGES;
           if (gc >= STAGES && !(ok = tc::mbar_wait(&empty[s], ((gc / STAGES) - 1) & 1, abort, error)))
             break;
@@ -283,89 +346,132 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == MMA_WARP) {
     // ---- MMA issuer ----
     if (lane == 0) {
       const uint32_t idesc = tc::instr_desc_f16(TILE_ROWS, TILE_VECTORS);
-      int gs = 0, gc = 0, local = 0;
+      int gc = 0, local = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x, ++local) {
-        if (local > 0 && !(ok = tc::mbar_wait(acc_empty, (local - 1) & 1, abort, error))) break;
-        for (int c = 0; ok && c < chunks; ++c, ++gc) {
+      for (int u = blockIdx.x; ok && u < units; u += gridDim.x, ++local) {
+        const int b = local & 1;
+        if (local >= 2 && !(ok = tc::mbar_wait(&acc_empty[b], ((local >> 1) - 1) & 1, abort, error)))
+          break;
+        tc::fence_after_sync();
+        const uint32_t acc = tmem + 64 * b;
+        const int c0 = plan.chunk_begin(u);
+        for (int c = c0; ok && c < plan.chunk_end(u); ++c, ++gc) {
           const int s = gc % STAGES;
           if (!(ok = tc::mbar_wait(&full[s], (gc / STAGES) & 1, abort, error))) break;
           const uint32_t b_base = tc::smem_u32(smem + s * L::STAGE_BYTES);
-          for (int sub = 0; sub < 4; ++sub, ++gs) {
-            const int buf = gs & 1;
-            if (!(ok = tc::mbar_wait(&a_full[buf], (gs >> 1) & 1, abort, error))) break;
+          for (int g = 0; g < 4; ++g) {
+            if (!(ok = tc::mbar_wait(&a_full[g], gc & 1, abort, error))) break;
             tc::fence_after_sync();
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              const uint64_t b_desc =
-                  tc::smem_desc_sw128(b_base + sub * TILE_VECTORS * 128 + j * 32);
-              tc::mma_f16_ts(tmem, tmem + 64 + buf * 32 + j * 8, b_desc, idesc,
-                             (c | sub | j) != 0);
+              const uint64_t b_desc = tc::smem_desc_sw128(b_base + g * TILE_VECTORS * 128 + j * 32);
+              tc::mma_f16_ts(acc, tmem + 128 + 32 * g + 8 * j, b_desc, idesc,
+                             (c != c0) | g | j);
             }
-            tc::mma_commit(&a_empty[buf]);
-            if (sub == 3) tc::mma_commit(&empty[s]);
+            tc::mma_commit(&a_empty[g]);
           }
+          if (ok) tc::mma_commit(&empty[s]);
         }
-        if (ok) tc::mma_commit(acc_full);
+        if (ok) tc::mma_commit(&acc_full[b]);
       }
     }
   } else {
-    // ---- dequant warpgroups, then the epilogue ----
+    // ---- dequant warpgroups, and the epilogues ----
     const int group = warp / 4, quarter = warp % 4;
     const int row_in_tile = quarter * 32 + lane;
     const uint32_t lane_base = uint32_t(quarter * 32) << 16;
-    int gs = 0, gc = 0, local = 0;
+    int gc = 0, local = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x, ++local) {
-      const int rt = tile % row_tiles, pass = tile / row_tiles;
-      for (int c = 0; ok && c < chunks; ++c, ++gc) {
-        const int s = gc % STAGES;
-        if (!(ok = tc::mbar_wait_warp(&full[s], (gc / STAGES) & 1, abort, error))) break;
-        const uint32_t* raw_row = reinterpret_cast<const uint32_t*>(
-            smem + s * L::STAGE_BYTES + B_STAGE_BYTES + row_in_tile * Unpack<T>::RAW_WORDS * 4);
-        for (int sub = 0; sub < 4; ++sub, ++gs) {
-          if ((gs & 1) != group) continue;
-          if (gs >= 2 && !(ok = tc::mbar_wait_warp(&a_empty[group], ((gs >> 1) - 1) & 1, abort, error)))
-            break;
-          tc::fence_after_sync();
-          uint32_t a[32];
-          Unpack<T>::step(raw_row, sub, a);
-          tc::tmem_store_32(tmem + lane_base + 64 + group * 32, a);
-          tc::tmem_store_wait();
-          tc::fence_before_sync();
-          __syncwarp();
-          if (lane == 0) tc::mbar_arrive(&a_full[group]);
-        }
-        __syncwarp();
-        if (ok && lane == 0) tc::mbar_arrive(&empty[s]);
-      }
-      if (!ok) break;
-      // epilogue: this warp's 32 rows x 32 of the tile's 64 vectors
-      if (!(ok = tc::mbar_wait_warp(acc_full, local & 1, abort, error))) break;
+    // the epilogue of the CTA's unit number `l` (its u), one chunk into the next
+    auto epilogue = [&](int u, int l) -> bool {
+      const int b = l & 1;
+      if (!tc::mbar_wait_warp(&acc_full[b], (l >> 1) & 1, abort, error)) return false;
       tc::fence_after_sync();
-      uint32_t acc[32];
-      tc::tmem_load_32(tmem + lane_base + group * 32, acc);
-      const int row = rt * TILE_ROWS + row_in_tile;
-      if (row < rows) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int v = pass * TILE_VECTORS + group * 32 + i;
-          if (v < vectors) y[(long long)v * rows + row] = __uint_as_float(acc[i]);
-        }
-      }
+      uint32_t acc[16];
+      tmem_load_16(tmem + lane_base + 64 * b + 16 * group, acc);
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(acc_empty);
+      if (lane == 0) tc::mbar_arrive(&acc_empty[b]);
+      const int tile = u / plan.splits;
+      const int rt = tile % plan.row_tiles, pass = tile / plan.row_tiles;
+      const int row = rt * TILE_ROWS + row_in_tile;
+      const int v0 = pass * TILE_VECTORS + 16 * group;
+      if (plan.splits == 1) {
+        if (row < rows) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (v0 + i < vectors) y[(long long)(v0 + i) * rows + row] = __uint_as_float(acc[i]);
+        }
+        return true;
+      }
+      // A K-range: leave this warp's slice of the partial sum (32 rows x 16
+      // vectors); the warp that brings a slice's last range adds the ranges
+      // in K order. Slices are counted apart, so no warp waits for another.
+      const int split = u % plan.splits;
+      const int slot = warp;  // the slice: rows of `quarter`, vectors of `group`
+      float* mine = scratch.partial + ((long long)tile * plan.splits + split) * TILE_VECTORS * TILE_ROWS;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) mine[(16 * group + i) * TILE_ROWS + row_in_tile] = __uint_as_float(acc[i]);
+      __threadfence();
+      __syncwarp();
+      int arrived = 0;
+      if (lane == 0) arrived = atomicAdd(&scratch.arrivals[tile * DEQUANT_WARPS + slot], 1);
+      arrived = __shfl_sync(0xffffffffu, arrived, 0);
+      if (arrived == plan.splits - 1) {
+        __threadfence();
+        if (row < rows) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float total = 0.0f;
+            for (int k = 0; k < plan.splits; ++k) {
+              const float* part = scratch.partial +
+                                  ((long long)tile * plan.splits + k) * TILE_VECTORS * TILE_ROWS;
+              total += k == split ? __uint_as_float(acc[i])
+                                  : __ldcg(part + (16 * group + i) * TILE_ROWS + row_in_tile);
+            }
+            if (v0 + i < vectors) y[(long long)(v0 + i) * rows + row] = total;
+          }
+        }
+      }
+      return true;
+    };
+    int pending = -1, pending_local = 0;
+    for (int u = blockIdx.x; ok && u < units; u += gridDim.x, ++local) {
+      for (int c = plan.chunk_begin(u); ok && c < plan.chunk_end(u); ++c, ++gc) {
+        const int s = gc % STAGES;
+        if (!(ok = tc::mbar_wait_warp(&full[s], (gc / STAGES) & 1, abort, error))) break;
+        if (gc >= 1 && !(ok = tc::mbar_wait_warp(&a_empty[group], (gc - 1) & 1, abort, error))) break;
+        tc::fence_after_sync();
+        const uint8_t* raw_row =
+            smem + s * L::STAGE_BYTES + B_STAGE_BYTES + row_in_tile * Unpack<T>::PITCH_WORDS * 4;
+        uint32_t a[32];
+        dequant_step<T>(group, raw_row, a);
+        tc::tmem_store_32(tmem + lane_base + 128 + 32 * group, a);
+        tc::tmem_store_wait();
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) {
+          tc::mbar_arrive(&a_full[group]);
+          tc::mbar_arrive(&empty[s]);
+        }
+        if (pending >= 0) {
+          ok = epilogue(pending, pending_local);
+          pending = -1;
+        }
+      }
+      pending = u;
+      pending_local = local;
     }
+    if (ok && pending >= 0) ok = epilogue(pending, pending_local);
   }
   __syncthreads();
   if (warp == 0) {
     tc::fence_after_sync();
-    tc::tmem_dealloc(tmem, 128);
+    tc::tmem_dealloc(tmem, TMEM_COLUMNS);
   }
 }
 
@@ -374,29 +480,57 @@ DRIFT_REGISTER(linear_tc_q4_0, linear_tc_kernel<Q4_0T>)
 DRIFT_REGISTER(linear_tc_q4_1, linear_tc_kernel<Q4_1T>)
 
 // ---- host ---------------------------------------------------------------------------------------
+// How many K-ranges a tile splits into: the fewest chunk-times per SM, a
+// split unit paying about two chunks for its partial sums, and at most
+// 4 units per SM in all when split (the scratch is sized for that).
+static int choose_splits(long long tiles, int chunks, int sms) {
+  int best = 1;
+  long long best_cost = ((tiles + sms - 1) / sms) * chunks;
+  for (int splits = 2; splits <= 8 && splits <= chunks; ++splits) {
+    const long long units = tiles * splits;
+    if (units > 4LL * sms) break;
+    const long long cost = ((units + sms - 1) / sms) * ((chunks + splits - 1) / splits + 2);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = splits;
+    }
+  }
+  return best;
+}
+
 template <typename T>
 static int launch_tc(int x_dtype, const void* x, const void* weight, float* y, int64_t m,
-                     int64_t n, int64_t k, cudaStream_t stream) {
+                     int64_t n, int64_t k, uint8_t* workspace, cudaStream_t stream) {
   using L = TcLayout<T>;
+  const int sms = sm_count();
   const int64_t padded = (m + TILE_VECTORS - 1) / TILE_VECTORS * TILE_VECTORS;
-  void* ws = nullptr;
-  DRIFT_TRY(workspace_reserve(size_t(padded * k * 2), &ws));
-  __half* xh = static_cast<__half*>(ws);
+  TcPlan plan;
+  plan.row_tiles = int((n + TILE_ROWS - 1) / TILE_ROWS);
+  plan.tiles = plan.row_tiles * int(padded / TILE_VECTORS);
+  plan.chunks = int((k + CHUNK - 1) / CHUNK);
+  plan.splits = choose_splits(plan.tiles, plan.chunks, sms);
+  __half* xh = reinterpret_cast<__half*>(workspace);
+  TcScratch scratch;
+  scratch.partial = reinterpret_cast<float*>(workspace + size_t(padded * k * 2));
+  scratch.arrivals = reinterpret_cast<int*>(
+      reinterpret_cast<uint8_t*>(scratch.partial) +
+      (plan.splits > 1 ? size_t(plan.tiles) * plan.splits * TILE_VECTORS * TILE_ROWS * 4 : 0));
   {
     const long long total = padded * k;
     long long blocks = (total + 255) / 256;
-    if (blocks > (long long)sm_count() * 32) blocks = (long long)sm_count() * 32;
+    if (blocks > (long long)sms * 32) blocks = (long long)sms * 32;
+    const int counters = plan.splits > 1 ? plan.tiles * DEQUANT_WARPS : 0;
     if (x_dtype == DRIFT_BF16)
-      tc_prepare_x_kernel<T, true><<<unsigned(blocks), 256, 0, stream>>>(x, xh, int(m),
-                                                                           int(padded), int(k));
+      tc_prepare_x_kernel<T, true><<<unsigned(blocks), 256, 0, stream>>>(
+          x, xh, int(m), int(padded), int(k), scratch.arrivals, counters);
     else
-      tc_prepare_x_kernel<T, false><<<unsigned(blocks), 256, 0, stream>>>(x, xh, int(m),
-                                                                            int(padded), int(k));
+      tc_prepare_x_kernel<T, false><<<unsigned(blocks), 256, 0, stream>>>(
+          x, xh, int(m), int(padded), int(k), scratch.arrivals, counters);
     DRIFT_LAUNCHED("tc_prepare_x");
   }
   const int64_t row_bytes = k / 32 * T::BYTES;
   CUtensorMap wmap, xmap;
-  DRIFT_TRY(encode_word_rows(&wmap, weight, row_bytes / 4, n, Unpack<T>::RAW_WORDS, TILE_ROWS));
+  DRIFT_TRY(encode_word_rows(&wmap, weight, row_bytes / 4, n, Unpack<T>::PITCH_WORDS, TILE_ROWS));
   DRIFT_TRY(encode_f16_sw128(&xmap, xh, k, padded, TILE_VECTORS));
   static bool configured[3] = {false, false, false};
   const int which = T::DTYPE == DRIFT_Q8_0 ? 0 : (T::DTYPE == DRIFT_Q4_0 ? 1 : 2);
@@ -405,16 +539,25 @@ static int launch_tc(int x_dtype, const void* x, const void* weight, float* y, i
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES));
     configured[which] = true;
   }
-  const int row_tiles = int((n + TILE_ROWS - 1) / TILE_ROWS);
-  const int tiles = row_tiles * int(padded / TILE_VECTORS);
-  const int grid = tiles < sm_count() ? tiles : sm_count();
-  linear_tc_kernel<T><<<grid, THREADS, L::SMEM_BYTES, stream>>>(
-      wmap, xmap, y, int(n), int(k), int(m), row_tiles, tiles, device_error_word());
+  const long long units = (long long)plan.tiles * plan.splits;
+  const int grid = units < sms ? int(units) : sms;
+  linear_tc_kernel<T><<<grid, TC_THREADS, L::SMEM_BYTES, stream>>>(
+      wmap, xmap, y, int(n), int(m), plan, scratch, device_error_word());
   DRIFT_LAUNCHED("linear_tc");
   return 0;
 }
 
 }  // namespace
+
+// Bytes of scratch a tensor-core product of m rows of k (new) needs at most:
+// the F16 x, and for split products the partial sums (at most 4 units per SM)
+// and the counters.
+size_t tc_workspace_bytes(int64_t m, int64_t k) {
+  const size_t padded = size_t((m + TILE_VECTORS - 1) / TILE_VECTORS * TILE_VECTORS);
+  const size_t units = size_t(4) * size_t(sm_count());  // split tiles are at most half that
+  return padded * size_t(k) * 2 + units * TILE_VECTORS * TILE_ROWS * 4 +
+         units * DEQUANT_WARPS * 4 + 256;
+}
 
 // Whether the tensor-core path takes a product: rows in whole 16-byte units
 // and a 16-byte aligned weight (what the tensor copies need).
@@ -426,12 +569,13 @@ bool tc_supports(int weight_dtype, const void* weight, int64_t k) {
          tensor_maps_available();
 }
 
+// `workspace`: tc_workspace_bytes(m, k) bytes of device scratch.
 int linear_tc(int x_dtype, const void* x, int weight_dtype, const void* weight, float* y,
-              int64_t m, int64_t n, int64_t k, cudaStream_t stream) {
+              int64_t m, int64_t n, int64_t k, uint8_t* workspace, cudaStream_t stream) {
   switch (weight_dtype) {
-    case DRIFT_Q8_0: return launch_tc<Q8_0T>(x_dtype, x, weight, y, m, n, k, stream);
-    case DRIFT_Q4_0: return launch_tc<Q4_0T>(x_dtype, x, weight, y, m, n, k, stream);
-    default: return launch_tc<Q4_1T>(x_dtype, x, weight, y, m, n, k, stream);
+    case DRIFT_Q8_0: return launch_tc<Q8_0T>(x_dtype, x, weight, y, m, n, k, workspace, stream);
+    case DRIFT_Q4_0: return launch_tc<Q4_0T>(x_dtype, x, weight, y, m, n, k, workspace, stream);
+    default: return launch_tc<Q4_1T>(x_dtype, x, weight, y, m, n, k, workspace, stream);
   }
 }
 

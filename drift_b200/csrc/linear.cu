@@ -22,8 +22,9 @@ int prepare_x_mma(int x_dtype, const void* x, int64_t m, int64_t k, uint8_t* rec
 int matvec_f32_weights(int x_dtype, const void* x, const float* weight, float* y, int64_t m,
                        int64_t n, int64_t k, cudaStream_t stream);
 bool tc_supports(int weight_dtype, const void* weight, int64_t k);
+size_t tc_workspace_bytes(int64_t m, int64_t k);
 int linear_tc(int x_dtype, const void* x, int weight_dtype, const void* weight, float* y,
-              int64_t m, int64_t n, int64_t k, cudaStream_t stream);
+              int64_t m, int64_t n, int64_t k, uint8_t* workspace, cudaStream_t stream);
 
 // From this many rows of x a product is a tensor-core product, as the
 // runner's GemmMinimumRows (ops/HipLinear.scala:14-19); below, the weight is
@@ -62,11 +63,17 @@ using namespace drift;
 
 extern "C" {
 
+// Scratch of one drift_linears call: the x records of the streamed products,
+// then (from GEMM_MINIMUM_ROWS rows) the tensor-core products' own region, so
+// a list that mixes the two never has one overwrite the other's x.
+static size_t records_region(int64_t m, int64_t k) {
+  return (mma_workspace_bytes(m, k) + 255) & ~size_t(255);
+}
+
 size_t drift_linear_workspace_bytes(int64_t m, int64_t k) {
-  // the largest of the products' scratch: x records (either layout), or F16 x
-  const size_t a = linear_workspace_bytes(m, k), b = mma_workspace_bytes(m, k);
-  const size_t c = size_t((m + 63) / 64 * 64) * size_t(k) * 2;
-  return a > b ? (a > c ? a : c) : (b > c ? b : c);
+  const size_t a = linear_workspace_bytes(m, k);  // the experts' x records
+  const size_t b = records_region(m, k) + (m >= GEMM_MINIMUM_ROWS ? tc_workspace_bytes(m, k) : 0);
+  return a > b ? a : b;
 }
 
 int drift_workspace_reserve(size_t bytes) { return workspace_reserve(bytes, nullptr); }
@@ -86,24 +93,28 @@ int drift_linears(int x_dtype, const void* x, int count, const int* weight_dtype
     return 0;
   }
   const cudaStream_t s = cudaStream_t(stream);
-  bool quantized = false;
-  for (int i = 0; i < count; ++i)
-    quantized |= weight_dtypes[i] != DRIFT_F32 &&
-                 !(m >= GEMM_MINIMUM_ROWS && tc_supports(weight_dtypes[i], weights[i], k));
-  uint8_t* records = nullptr;
-  if (quantized) {
-    void* w = nullptr;
-    DRIFT_TRY(workspace_reserve(mma_workspace_bytes(m, k), &w));
-    records = static_cast<uint8_t*>(w);
-    DRIFT_TRY(prepare_x_mma(x_dtype, x, m, k, records, s));  // one preparation for all
+  bool quantized = false, tensor_cores = false;
+  for (int i = 0; i < count; ++i) {
+    const bool tc = weight_dtypes[i] != DRIFT_F32 && m >= GEMM_MINIMUM_ROWS &&
+                    tc_supports(weight_dtypes[i], weights[i], k);
+    tensor_cores |= tc;
+    quantized |= weight_dtypes[i] != DRIFT_F32 && !tc;
   }
+  const size_t records_bytes = quantized ? records_region(m, k) : 0;
+  void* w = nullptr;
+  if (quantized || tensor_cores)
+    DRIFT_TRY(workspace_reserve(records_bytes + (tensor_cores ? tc_workspace_bytes(m, k) : 0), &w));
+  uint8_t* records = static_cast<uint8_t*>(w);
+  uint8_t* tc_region = static_cast<uint8_t*>(w) + records_bytes;
+  if (quantized) DRIFT_TRY(prepare_x_mma(x_dtype, x, m, k, records, s));  // one preparation for all
   for (int i = 0; i < count; ++i) {
     if (ns[i] == 0) continue;
     if (weight_dtypes[i] == DRIFT_F32)
       DRIFT_TRY(matvec_f32_weights(x_dtype, x, static_cast<const float*>(weights[i]), outs[i], m,
                                    ns[i], k, s));
     else if (m >= GEMM_MINIMUM_ROWS && tc_supports(weight_dtypes[i], weights[i], k))
-      DRIFT_TRY(linear_tc(x_dtype, x, weight_dtypes[i], weights[i], outs[i], m, ns[i], k, s));
+      DRIFT_TRY(linear_tc(x_dtype, x, weight_dtypes[i], weights[i], outs[i], m, ns[i], k,
+                          tc_region, s));
     else
       DRIFT_TRY(matvec_prepared(weight_dtypes[i], weights[i], records, outs[i], ns[i], k, m, s));
   }

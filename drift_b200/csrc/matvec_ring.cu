@@ -64,27 +64,6 @@ struct RingShape {
   static constexpr int BYTES = BARS + WARPS * S * 8 + 16 + 1024;  // + room to align to 1024
 };
 
-// words [OFF, END) of a row in shared memory (16-byte aligned), by the widest
-// aligned loads
-template <int OFF, int END>
-__device__ __forceinline__ void lds_span(const uint8_t* row, uint32_t* w) {
-  if constexpr (OFF < END) {
-    if constexpr (OFF % 16 == 0 && OFF + 16 <= END) {
-      const uint4 q = *reinterpret_cast<const uint4*>(row + OFF);
-      w[0] = q.x;
-      w[1] = q.y;
-      w[2] = q.z;
-      w[3] = q.w;
-      lds_span<OFF + 16, END>(row, w + 4);
-    } else {
-      const uint2 q = *reinterpret_cast<const uint2*>(row + OFF);
-      w[0] = q.x;
-      w[1] = q.y;
-      lds_span<OFF + 8, END>(row, w + 2);
-    }
-  }
-}
-
 // One vector's x for one block, as the dp4a modes use it.
 struct XBlock {
   uint32_t planes[24];

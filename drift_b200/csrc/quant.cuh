@@ -163,6 +163,27 @@ struct Q4_1T {
   }
 };
 
+// Bytes [OFF, END) of a 16-byte aligned row in shared memory, as words, by the
+// widest aligned loads (OFF and END multiples of 8).
+template <int OFF, int END>
+__device__ __forceinline__ void lds_span(const uint8_t* row, uint32_t* w) {
+  if constexpr (OFF < END) {
+    if constexpr (OFF % 16 == 0 && OFF + 16 <= END) {
+      const uint4 q = *reinterpret_cast<const uint4*>(row + OFF);
+      w[0] = q.x;
+      w[1] = q.y;
+      w[2] = q.z;
+      w[3] = q.w;
+      lds_span<OFF + 16, END>(row, w + 4);
+    } else {
+      const uint2 q = *reinterpret_cast<const uint2*>(row + OFF);
+      w[0] = q.x;
+      w[1] = q.y;
+      lds_span<OFF + 8, END>(row, w + 2);
+    }
+  }
+}
+
 // The aligned words covering block `block` of a row that starts at `row`
 // (4-byte aligned).
 template <typename T>
