@@ -49,8 +49,6 @@ constexpr int TILE_ROWS = 128;
 constexpr int TILE_VECTORS = 64;
 constexpr int CHUNK = 256;  // columns per ring stage
 constexpr int STEP = 64;    // columns per MMA step (one 128-byte swizzle atom of F16)
-constexpr int STAGES = 3;
-constexpr int B_STAGE_BYTES = 4 * TILE_VECTORS * 128;  // four [64 vectors x 64 F16] tiles
 
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
@@ -187,46 +185,66 @@ struct Unpack<Q8_0T> {
 };
 
 // ---- x, staged for the tensor cores -------------------------------------------------------
-// out[v][k] (F16, [vectors_padded][k]): x[v][32 b + perm(p)] at k = 32 b + p,
-// zero for v >= vectors. x is F32 or BF16 [vectors][k].
+// The F16 x as the MMA reads it, laid out so that ONE contiguous bulk copy
+// brings a chunk's four [64 vectors x 64 columns] tiles: tile (pass, chunk,
+// step) is 8 KB at ((pass * chunks + chunk) * 4 + step) * 8 KB, each in the
+// 128-byte swizzled K-major layout (the 16-byte unit u of row r at u ^ (r % 8))
+// that a swizzled tensor copy would have made. Column 32 b + p of a tile row
+// holds x[v][32 b + perm(p)]; vectors past m and columns past k are zeros.
+constexpr int X_TILE_BYTES = TILE_VECTORS * 128;
+constexpr int X_CHUNK_BYTES = 4 * X_TILE_BYTES;
+
 template <typename T, bool BF16>
 __global__ void tc_prepare_x_kernel(const void* __restrict__ x, __half* __restrict__ out,
-                                    int vectors, int padded, int cols, int* counters,
-                                    int count) {
+                                    int vectors, int cols, int chunks, long long total,
+                                    int* counters, int count) {
   // the split product's arrival counters start at zero
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += gridDim.x * blockDim.x)
     counters[i] = 0;
-  const long long total = (long long)padded * cols;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int v = int(i / cols), k = int(i % cols);
+  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (long long)gridDim.x * blockDim.x) {
+    const long long tile = e / (X_TILE_BYTES / 2);
+    const int swizzled = int(e % (X_TILE_BYTES / 2)) * 2;  // byte offset in the tile
+    const int plain = swizzled ^ (((swizzled >> 7) & 7) << 4);
+    const int row = plain / 128, column = (plain % 128) / 2;
+    const int step = int(tile % 4), chunk = int((tile / 4) % chunks), pass = int(tile / (4LL * chunks));
+    const int v = pass * TILE_VECTORS + row;
+    const int k = chunk * CHUNK + step * STEP + column;
     float value = 0.0f;
-    if (v < vectors) {
+    if (v < vectors && k < cols) {
       const long long source = (long long)v * cols + (k & ~31) + Unpack<T>::perm(k & 31);
       if (BF16)
         value = __uint_as_float(uint32_t(reinterpret_cast<const uint16_t*>(x)[source]) << 16);
       else
         value = reinterpret_cast<const float*>(x)[source];
     }
-    out[i] = __float2half_rn(value);
+    out[e] = __float2half_rn(value);
   }
 }
 
 // ---- the product ------------------------------------------------------------------------------
 constexpr int DEQUANT_WARPS = 16;
-constexpr int TMA_WARP = 16, MMA_WARP = 17;
-constexpr int TC_THREADS = 32 * (DEQUANT_WARPS + 2);
-// TMEM columns: accumulators 0-63 and 64-127, A buffer of warpgroup g at 128 + 32 g
-constexpr uint32_t TMEM_COLUMNS = 256;
+constexpr int W_WARP = 16, MMA_WARP = 17, X_WARP = 18;
+constexpr int TC_THREADS = 32 * (DEQUANT_WARPS + 3);
+// TMEM columns: accumulators 0-63 and 64-127; warpgroup g's two A buffers at
+// 128 + 64 g and 160 + 64 g (it fills one while the MMA reads the other)
+constexpr uint32_t TMEM_COLUMNS = 512;
 
+// Two rings: raw weights (freed by the dequant warps, so they run ahead of
+// the MMA) and x (freed by the MMA's commit).
 template <typename T>
 struct TcLayout {
+  static constexpr int W_STAGES = T::DTYPE == DRIFT_Q8_0 ? 3 : 5;
+  static constexpr int X_STAGES = 3;
   static constexpr int RAW_BYTES = TILE_ROWS * Unpack<T>::PITCH_WORDS * 4;
   static constexpr int RAW_PADDED = (RAW_BYTES + 1023) / 1024 * 1024;
-  static constexpr int STAGE_BYTES = B_STAGE_BYTES + RAW_PADDED;
-  static constexpr int BARRIER_OFFSET = STAGES * STAGE_BYTES;
-  // full[S], empty[S], a_full[4], a_empty[4], acc_full[2], acc_empty[2], tmem slot, abort
-  static constexpr int SMEM_BYTES = BARRIER_OFFSET + 256 + 1024;  // + alignment slack
+  static constexpr int X_OFFSET = W_STAGES * RAW_PADDED;
+  static constexpr int BARRIER_OFFSET = X_OFFSET + X_STAGES * X_CHUNK_BYTES;
+  // w_full, w_empty [W], x_full, x_empty [X], a_full, a_empty, acc_full,
+  // acc_empty [2], tmem slot, abort
+  static constexpr int SMEM_BYTES = BARRIER_OFFSET + 512 + 1024;  // + alignment slack
+  static_assert((2 * W_STAGES + 2 * X_STAGES + 8) * 8 + 8 <= 512, "barrier area");
+  static_assert(SMEM_BYTES <= 232448, "shared memory");
 };
 
 // What a CTA's units are: unit u is K-range u % splits of tile u / splits,
@@ -271,19 +289,22 @@ __device__ __forceinline__ void dequant_step(int group, const uint8_t* row, uint
 
 template <typename T>
 __global__ void __launch_bounds__(TC_THREADS, 1)
-    linear_tc_kernel(const __grid_constant__ CUtensorMap wmap,
-                     const __grid_constant__ CUtensorMap xmap, float* __restrict__ y, int rows,
-                     int vectors, TcPlan plan, TcScratch scratch, int* error) {
+    linear_tc_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __restrict__ xs,
+                     float* __restrict__ y, int rows, int vectors, TcPlan plan,
+                     TcScratch scratch, int* error) {
   using L = TcLayout<T>;
+  constexpr int WS = L::W_STAGES, XS = L::X_STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BARRIER_OFFSET);
-  uint64_t* full = bars;
-  uint64_t* empty = bars + STAGES;
-  uint64_t* a_full = bars + 2 * STAGES;
-  uint64_t* a_empty = a_full + 4;
-  uint64_t* acc_full = a_empty + 4;
+  uint64_t* w_full = bars;
+  uint64_t* w_empty = w_full + WS;
+  uint64_t* x_full = w_empty + WS;
+  uint64_t* x_empty = x_full + XS;
+  uint64_t* a_full = x_empty + XS;  // [2]: chunk parity
+  uint64_t* a_empty = a_full + 2;
+  uint64_t* acc_full = a_empty + 2;
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -292,13 +313,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const int units = plan.units();
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      tc::mbar_init(&full[s], 1);
-      tc::mbar_init(&empty[s], DEQUANT_WARPS + 1);  // the dequant warps + the MMA's commit
+    for (int s = 0; s < WS; ++s) {
+      tc::mbar_init(&w_full[s], 1);
+      tc::mbar_init(&w_empty[s], DEQUANT_WARPS);
     }
-    for (int g = 0; g < 4; ++g) {
-      tc::mbar_init(&a_full[g], 4);  // the four warps of a warpgroup
-      tc::mbar_init(&a_empty[g], 1);
+    for (int s = 0; s < XS; ++s) {
+      tc::mbar_init(&x_full[s], 1);
+      tc::mbar_init(&x_empty[s], 1);  // the MMA's commit
+    }
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&a_full[i], DEQUANT_WARPS);  // a chunk's A, all four steps
+      tc::mbar_init(&a_empty[i], 1);             // the MMA's commit
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(&acc_full[b], 1);
@@ -307,42 +332,44 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     *abort = 0;
     tc::fence_barrier_init();
   }
-  if (warp == TMA_WARP && lane == 0) {
-    tc::prefetch_tensor_map(&wmap);
-    tc::prefetch_tensor_map(&xmap);
-  }
+  if (warp == W_WARP && lane == 0) tc::prefetch_tensor_map(&wmap);
   if (warp == 0) tc::tmem_alloc(tmem_slot, TMEM_COLUMNS);
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == TMA_WARP) {
-    // ---- TMA producer ----
+  if (warp == W_WARP || warp == X_WARP) {
+    // ---- producers: raw weights (2-D tensor copy of 128 rows), x (one bulk copy) ----
     if (lane == 0) {
+      const bool weights = warp == W_WARP;
+      const int S = weights ? WS : XS;
+      uint64_t* full = weights ? w_full : x_full;
+      uint64_t* empty = weights ? w_empty : x_empty;
       int gc = 0;
       bool ok = true;
       for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
         const int tile = u / plan.splits;
         const int rt = tile % plan.row_tiles, pass = tile / plan.row_tiles;
         for (int c = plan.chunk_begin(u); c < plan.chunk_end(u); ++c, ++gc) {
-          const int s = gc % STAGES;
-          if (gc >= STAGES && !(ok = tc::mbar_wait(&empty[s], ((gc / STAGES) - 1) & 1, abort, error)))
-            break;
-          uint8_t* stage = smem + s * L::STAGE_BYTES;
-          tc::mbar_expect_tx(&full[s], B_STAGE_BYTES + L::RAW_BYTES);
-          tc::tma_load_2d(stage + B_STAGE_BYTES, &wmap, &full[s], c * Unpack<T>::RAW_WORDS,
-                          rt * TILE_ROWS);
-#pragma unroll
-          for (int sub = 0; sub < 4; ++sub)
-            tc::tma_load_2d(stage + sub * TILE_VECTORS * 128, &xmap, &full[s],
-                            (c * 4 + sub) * STEP, pass * TILE_VECTORS);
+          const int s = gc % S;
+          if (gc >= S && !(ok = tc::mbar_wait(&empty[s], ((gc / S) - 1) & 1, abort, error))) break;
+          if (weights) {
+            tc::mbar_expect_tx(&full[s], L::RAW_BYTES);
+            tc::tma_load_2d(smem + s * L::RAW_PADDED, &wmap, &full[s], c * Unpack<T>::RAW_WORDS,
+                            rt * TILE_ROWS);
+          } else {
+            tc::mbar_expect_tx(&full[s], X_CHUNK_BYTES);
+            tc::bulk_load(smem + L::X_OFFSET + s * X_CHUNK_BYTES,
+                          xs + ((long long)pass * plan.chunks + c) * X_CHUNK_BYTES, X_CHUNK_BYTES,
+                          &full[s]);
+          }
         }
       }
       if (!ok) {
         // let the copies already issued land before the CTA leaves
-        for (int j = gc - STAGES < 0 ? 0 : gc - STAGES; j < gc; ++j) {
+        for (int j = gc - S < 0 ? 0 : gc - S; j < gc; ++j) {
           volatile int never = 0;
-          tc::mbar_wait(&full[j % STAGES], (j / STAGES) & 1, &never, nullptr);
+          tc::mbar_wait(&full[j % S], (j / S) & 1, &never, nullptr);
         }
       }
     }
@@ -360,21 +387,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const uint32_t acc = tmem + 64 * b;
         const int c0 = plan.chunk_begin(u);
         for (int c = c0; ok && c < plan.chunk_end(u); ++c, ++gc) {
-          const int s = gc % STAGES;
-          if (!(ok = tc::mbar_wait(&full[s], (gc / STAGES) & 1, abort, error))) break;
-          const uint32_t b_base = tc::smem_u32(smem + s * L::STAGE_BYTES);
-          for (int g = 0; g < 4; ++g) {
-            if (!(ok = tc::mbar_wait(&a_full[g], gc & 1, abort, error))) break;
-            tc::fence_after_sync();
+          const int s = gc % XS;
+          if (!(ok = tc::mbar_wait(&x_full[s], (gc / XS) & 1, abort, error))) break;
+          if (!(ok = tc::mbar_wait(&a_full[gc & 1], (gc >> 1) & 1, abort, error))) break;
+          tc::fence_after_sync();
+          // one chunk: 16 MMAs back to back (the tensor core's queue stays full
+          // while this thread waits for the next chunk), then one commit per ring
+          const uint32_t b_base = tc::smem_u32(smem + L::X_OFFSET + s * X_CHUNK_BYTES);
+          const uint64_t b_desc = tc::smem_desc_sw128(b_base);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint64_t b_desc = tc::smem_desc_sw128(b_base + g * TILE_VECTORS * 128 + j * 32);
-              tc::mma_f16_ts(acc, tmem + 128 + 32 * g + 8 * j, b_desc, idesc,
+          for (int g = 0; g < 4; ++g) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              tc::mma_f16_ts(acc, tmem + 128 + 32 * (2 * g + (gc & 1)) + 8 * j,
+                             b_desc + uint64_t((g * X_TILE_BYTES + j * 32) >> 4), idesc,
                              (c != c0) | g | j);
-            }
-            tc::mma_commit(&a_empty[g]);
           }
-          if (ok) tc::mma_commit(&empty[s]);
+          tc::mma_commit(&a_empty[gc & 1]);
+          tc::mma_commit(&x_empty[s]);
         }
         if (ok) tc::mma_commit(&acc_full[b]);
       }
@@ -412,14 +442,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       // vectors); the warp that brings a slice's last range adds the ranges
       // in K order. Slices are counted apart, so no warp waits for another.
       const int split = u % plan.splits;
-      const int slot = warp;  // the slice: rows of `quarter`, vectors of `group`
       float* mine = scratch.partial + ((long long)tile * plan.splits + split) * TILE_VECTORS * TILE_ROWS;
 #pragma unroll
       for (int i = 0; i < 16; ++i) mine[(16 * group + i) * TILE_ROWS + row_in_tile] = __uint_as_float(acc[i]);
       __threadfence();
       __syncwarp();
       int arrived = 0;
-      if (lane == 0) arrived = atomicAdd(&scratch.arrivals[tile * DEQUANT_WARPS + slot], 1);
+      if (lane == 0) arrived = atomicAdd(&scratch.arrivals[tile * DEQUANT_WARPS + warp], 1);
       arrived = __shfl_sync(0xffffffffu, arrived, 0);
       if (arrived == plan.splits - 1) {
         __threadfence();
@@ -442,22 +471,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     int pending = -1, pending_local = 0;
     for (int u = blockIdx.x; ok && u < units; u += gridDim.x, ++local) {
       for (int c = plan.chunk_begin(u); ok && c < plan.chunk_end(u); ++c, ++gc) {
-        const int s = gc % STAGES;
-        if (!(ok = tc::mbar_wait_warp(&full[s], (gc / STAGES) & 1, abort, error))) break;
-        if (gc >= 1 && !(ok = tc::mbar_wait_warp(&a_empty[group], (gc - 1) & 1, abort, error))) break;
+        const int s = gc % WS;
+        if (!(ok = tc::mbar_wait_warp(&w_full[s], (gc / WS) & 1, abort, error))) break;
+        const int buf = 2 * group + (gc & 1);
+        if (gc >= 2 && !(ok = tc::mbar_wait_warp(&a_empty[gc & 1], ((gc >> 1) - 1) & 1, abort, error)))
+          break;
         tc::fence_after_sync();
-        const uint8_t* raw_row =
-            smem + s * L::STAGE_BYTES + B_STAGE_BYTES + row_in_tile * Unpack<T>::PITCH_WORDS * 4;
+        const uint8_t* raw_row = smem + s * L::RAW_PADDED + row_in_tile * Unpack<T>::PITCH_WORDS * 4;
         uint32_t a[32];
         dequant_step<T>(group, raw_row, a);
-        tc::tmem_store_32(tmem + lane_base + 128 + 32 * group, a);
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&w_empty[s]);  // the raw weights are in registers
+        tc::tmem_store_32(tmem + lane_base + 128 + 32 * buf, a);
         tc::tmem_store_wait();
         tc::fence_before_sync();
         __syncwarp();
-        if (lane == 0) {
-          tc::mbar_arrive(&a_full[group]);
-          tc::mbar_arrive(&empty[s]);
-        }
+        if (lane == 0) tc::mbar_arrive(&a_full[gc & 1]);
         if (pending >= 0) {
           ok = epilogue(pending, pending_local);
           pending = -1;
@@ -509,29 +538,29 @@ static int launch_tc(int x_dtype, const void* x, const void* weight, float* y, i
   plan.tiles = plan.row_tiles * int(padded / TILE_VECTORS);
   plan.chunks = int((k + CHUNK - 1) / CHUNK);
   plan.splits = choose_splits(plan.tiles, plan.chunks, sms);
-  __half* xh = reinterpret_cast<__half*>(workspace);
+  const size_t x_bytes = size_t(padded / TILE_VECTORS) * plan.chunks * X_CHUNK_BYTES;
+  __half* xs = reinterpret_cast<__half*>(workspace);
   TcScratch scratch;
-  scratch.partial = reinterpret_cast<float*>(workspace + size_t(padded * k * 2));
+  scratch.partial = reinterpret_cast<float*>(workspace + x_bytes);
   scratch.arrivals = reinterpret_cast<int*>(
       reinterpret_cast<uint8_t*>(scratch.partial) +
       (plan.splits > 1 ? size_t(plan.tiles) * plan.splits * TILE_VECTORS * TILE_ROWS * 4 : 0));
   {
-    const long long total = padded * k;
+    const long long total = (long long)(x_bytes / 2);
     long long blocks = (total + 255) / 256;
     if (blocks > (long long)sms * 32) blocks = (long long)sms * 32;
     const int counters = plan.splits > 1 ? plan.tiles * DEQUANT_WARPS : 0;
     if (x_dtype == DRIFT_BF16)
       tc_prepare_x_kernel<T, true><<<unsigned(blocks), 256, 0, stream>>>(
-          x, xh, int(m), int(padded), int(k), scratch.arrivals, counters);
+          x, xs, int(m), int(k), plan.chunks, total, scratch.arrivals, counters);
     else
       tc_prepare_x_kernel<T, false><<<unsigned(blocks), 256, 0, stream>>>(
-          x, xh, int(m), int(padded), int(k), scratch.arrivals, counters);
+          x, xs, int(m), int(k), plan.chunks, total, scratch.arrivals, counters);
     DRIFT_LAUNCHED("tc_prepare_x");
   }
   const int64_t row_bytes = k / 32 * T::BYTES;
-  CUtensorMap wmap, xmap;
+  CUtensorMap wmap;
   DRIFT_TRY(encode_word_rows(&wmap, weight, row_bytes / 4, n, Unpack<T>::PITCH_WORDS, TILE_ROWS));
-  DRIFT_TRY(encode_f16_sw128(&xmap, xh, k, padded, TILE_VECTORS));
   static bool configured[3] = {false, false, false};
   const int which = T::DTYPE == DRIFT_Q8_0 ? 0 : (T::DTYPE == DRIFT_Q4_0 ? 1 : 2);
   if (!configured[which]) {
@@ -542,7 +571,8 @@ static int launch_tc(int x_dtype, const void* x, const void* weight, float* y, i
   const long long units = (long long)plan.tiles * plan.splits;
   const int grid = units < sms ? int(units) : sms;
   linear_tc_kernel<T><<<grid, TC_THREADS, L::SMEM_BYTES, stream>>>(
-      wmap, xmap, y, int(n), int(m), plan, scratch, device_error_word());
+      wmap, reinterpret_cast<const uint8_t*>(xs), y, int(n), int(m), plan, scratch,
+      device_error_word());
   DRIFT_LAUNCHED("linear_tc");
   return 0;
 }
@@ -550,12 +580,13 @@ static int launch_tc(int x_dtype, const void* x, const void* weight, float* y, i
 }  // namespace
 
 // Bytes of scratch a tensor-core product of m rows of k (new) needs at most:
-// the F16 x, and for split products the partial sums (at most 4 units per SM)
+// the F16 x (whole chunks), and for split products the partial sums (at most 4 units per SM)
 // and the counters.
 size_t tc_workspace_bytes(int64_t m, int64_t k) {
-  const size_t padded = size_t((m + TILE_VECTORS - 1) / TILE_VECTORS * TILE_VECTORS);
+  const size_t passes = size_t((m + TILE_VECTORS - 1) / TILE_VECTORS);
+  const size_t chunks = size_t((k + CHUNK - 1) / CHUNK);
   const size_t units = size_t(4) * size_t(sm_count());  // split tiles are at most half that
-  return padded * size_t(k) * 2 + units * TILE_VECTORS * TILE_ROWS * 4 +
+  return passes * chunks * X_CHUNK_BYTES + units * TILE_VECTORS * TILE_ROWS * 4 +
          units * DEQUANT_WARPS * 4 + 256;
 }
 
