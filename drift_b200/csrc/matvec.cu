@@ -125,20 +125,19 @@ __global__ void __launch_bounds__(256) quantize_x22_mma_kernel(const void* x, ui
     X = __float2int_rn(ldexpf(value, X_BITS - e));
   }
   uint8_t* record = records + ((long long)pass * blocks + block) * MMA_RECORD_BYTES;
-  // value j = lane sits in word w = j / 4 (byte j % 4) of each plane; word w
-  // belongs to lane (g, w % 4) as its half w / 4
+  // value j = lane sits in byte j % 4 of word j / 4 of each plane
   const int w = lane / 4;
-  const int at = (4 * g + (w % 4)) * 8 + (w / 4) * 4 + (lane % 4);
-  record[at] = uint8_t(X & 0xff);
-  record[256 + at] = uint8_t((X >> 8) & 0xff);
-  record[512 + at] = uint8_t((X >> 16) & 0xff);
+  record[mma_plane_byte(g, 0, w) + lane % 4] = uint8_t(X & 0xff);
+  record[mma_plane_byte(g, 1, w) + lane % 4] = uint8_t((X >> 8) & 0xff);
+  record[mma_plane_byte(g, 2, w) + lane % 4] = uint8_t((X >> 16) & 0xff);
   int sum = X;
 #pragma unroll
   for (int o = 16; o > 0; o /= 2) sum += __shfl_xor_sync(0xffffffffu, sum, o);
   if (lane == 0) {
-    reinterpret_cast<float*>(record + 768)[g] = s;
-    reinterpret_cast<int*>(record + 800)[g] = sum;
-    reinterpret_cast<float*>(record + 832)[g] = float(sum);
+    uint8_t* scales = record + mma_scale_byte(g);
+    reinterpret_cast<float*>(scales)[0] = s;
+    reinterpret_cast<int*>(scales)[1] = sum;
+    reinterpret_cast<float*>(scales)[2] = float(sum);
   }
 }
 
@@ -298,16 +297,12 @@ __global__ void __launch_bounds__(256) matvec_mma_kernel(const uint8_t* __restri
   if (row0 < rows) {
     for (int c = first; c < end; ++c) {
       const uint8_t* rec = records + (long long)c * MMA_RECORD_BYTES;
-      uint2 planes[3] = {make_uint2(0, 0), make_uint2(0, 0), make_uint2(0, 0)};
-      if (have_vector) {
-#pragma unroll
-        for (int p = 0; p < 3; ++p) planes[p] = __ldg(reinterpret_cast<const uint2*>(rec) + p * 32 + lane);
-      }
-      const float2 s = __ldg(reinterpret_cast<const float2*>(rec + 768) + t);
-      int2 sum = make_int2(0, 0);
-      float2 fsum = make_float2(0.0f, 0.0f);
-      if (T::DTYPE == DRIFT_Q4_0) sum = __ldg(reinterpret_cast<const int2*>(rec + 800) + t);
-      if (T::DTYPE == DRIFT_Q4_1) fsum = __ldg(reinterpret_cast<const float2*>(rec + 832) + t);
+      XFragment xf;
+      load_fragment<T>(rec, have_vector, xf);
+      const uint2* planes = xf.planes;
+      const float2 s = xf.s;
+      const int2 sum = xf.sum;
+      const float2 fsum = xf.fsum;
 #pragma unroll
       for (int i = 0; i < MT; ++i) {
         uint32_t lo0, hi0, lo1, hi1;

@@ -73,11 +73,12 @@ struct XBlock {
 
 template <typename T>
 __device__ __forceinline__ void load_x(const uint8_t* rec, int v, XBlock& x) {
+  // vector v's slot: 96 bytes of planes, then s, sum, fsum -- one 128-byte line
+  const uint4* q = reinterpret_cast<const uint4*>(rec + MMA_SLOT_BYTES * v);
 #pragma unroll
   for (int p = 0; p < 3; ++p) {
-    // plane p, vector v: words (0, 4, 1, 5) then (2, 6, 3, 7) of the 8
-    const uint4* q = reinterpret_cast<const uint4*>(rec + 256 * p + 32 * v);
-    const uint4 q0 = __ldg(q), q1 = __ldg(q + 1);
+    // plane p: words (0, 4, 1, 5) then (2, 6, 3, 7)
+    const uint4 q0 = __ldg(q + 2 * p), q1 = __ldg(q + 2 * p + 1);
     x.planes[8 * p + 0] = q0.x;
     x.planes[8 * p + 4] = q0.y;
     x.planes[8 * p + 1] = q0.z;
@@ -87,9 +88,10 @@ __device__ __forceinline__ void load_x(const uint8_t* rec, int v, XBlock& x) {
     x.planes[8 * p + 3] = q1.z;
     x.planes[8 * p + 7] = q1.w;
   }
-  x.s = __ldg(reinterpret_cast<const float*>(rec + 768) + v);
-  x.sum = T::DTYPE == DRIFT_Q4_0 ? __ldg(reinterpret_cast<const int*>(rec + 800) + v) : 0;
-  x.fsum = T::DTYPE == DRIFT_Q4_1 ? __ldg(reinterpret_cast<const float*>(rec + 832) + v) : 0.0f;
+  const uint4 scales = __ldg(q + 6);
+  x.s = __uint_as_float(scales.x);
+  x.sum = T::DTYPE == DRIFT_Q4_0 ? int(scales.y) : 0;
+  x.fsum = T::DTYPE == DRIFT_Q4_1 ? __uint_as_float(scales.z) : 0.0f;
 }
 
 // ---- dp4a modes: 1 or 2 vectors --------------------------------------------------------------
@@ -158,27 +160,6 @@ __device__ __forceinline__ void segment_dp4a(const uint8_t* stage, int first_blo
 }
 
 // ---- MMA mode: 3-8 vectors -------------------------------------------------------------------
-// x's fragment of one block for the MMA mode: lane (g, t) holds vector g's
-// plane words (t, t + 4) and s, sum for vectors 2t, 2t + 1.
-struct XFragment {
-  uint2 planes[3];
-  float2 s, fsum;
-  int2 sum;
-};
-
-template <typename T>
-__device__ __forceinline__ void load_fragment(const uint8_t* rec, bool have_vector, XFragment& x) {
-  const int lane = threadIdx.x % WARP, t = lane % 4;
-#pragma unroll
-  for (int p = 0; p < 3; ++p)
-    x.planes[p] = have_vector ? __ldg(reinterpret_cast<const uint2*>(rec) + p * 32 + lane)
-                              : make_uint2(0, 0);
-  x.s = __ldg(reinterpret_cast<const float2*>(rec + 768) + t);
-  x.sum = T::DTYPE == DRIFT_Q4_0 ? __ldg(reinterpret_cast<const int2*>(rec + 800) + t) : make_int2(0, 0);
-  x.fsum = T::DTYPE == DRIFT_Q4_1 ? __ldg(reinterpret_cast<const float2*>(rec + 832) + t)
-                                  : make_float2(0.0f, 0.0f);
-}
-
 // acc[i][.] gains the segment's blocks for rows (16 i + g, 16 i + g + 8) and
 // vectors (2t, 2t + 1), each as acc = fmaf(s, value, acc); x is fetched one
 // block ahead.

@@ -47,17 +47,22 @@ __device__ __forceinline__ void mma_i8(int (&d)[4], const uint32_t (&a)[4], uint
 }
 
 // ---- x for the integer tensor cores --------------------------------------------------
-// The prepared x of up to 8 vectors (a pass), one 896-byte record per block,
-// laid out as the m16n8k32 B fragments are held: lane (g, t) of a warp reads
-// one 8-byte word per plane, in lane order, so a warp's plane load is one
-// coalesced 256-byte access.
-//   bytes   0..767  plane p (0..2): uint2 [32 lanes]; lane 4g + t holds words t
-//                   and 4 + t of vector g's plane p (values 4t..4t+3 and
-//                   16+4t..16+4t+3), zero for vectors past the pass
-//   bytes 768..799  s of vectors 0..7 (float)
-//   bytes 800..831  sum_j X_j of vectors 0..7 (int)
-//   bytes 832..863  the same sums as float
-constexpr int MMA_RECORD_BYTES = 896;
+// The prepared x of up to 8 vectors (a pass), one 896-byte record per block:
+// eight 112-byte slots, slot v holding vector v's part of the block (zeros for
+// vectors past the pass), so one vector's x for a block is one 128-byte line
+// -- what the one- and two-vector products read, for every block of a row:
+//   slot bytes  0..95   plane p (0..2) at 32 p: its 8 words in the order
+//                       0, 4, 1, 5, 2, 6, 3, 7, so the m16n8k32 B fragment of
+//                       lane (g, t) -- words t and 4 + t, values 4t..4t+3 and
+//                       16+4t..16+4t+3 -- is the 8 bytes at 8 t
+//   slot bytes 96..107  s (float), sum_j X_j (int), the same sum as float
+constexpr int MMA_SLOT_BYTES = 112;
+constexpr int MMA_RECORD_BYTES = 8 * MMA_SLOT_BYTES;
+// byte of plane p, word w (0..7) of vector v's slot
+__host__ __device__ constexpr int mma_plane_byte(int v, int p, int w) {
+  return MMA_SLOT_BYTES * v + 32 * p + 8 * (w % 4) + 4 * (w / 4);
+}
+__host__ __device__ constexpr int mma_scale_byte(int v) { return MMA_SLOT_BYTES * v + 96; }
 constexpr int MMA_RECORD_WORDS = MMA_RECORD_BYTES / 4;
 
 // The same product with a zero accumulator (no registers to clear first).
@@ -133,6 +138,33 @@ __device__ __forceinline__ void fragment_row(const uint8_t* __restrict__ row, in
     d = half_bits_to_float(off ? (head >> 16) : head);
     m = 0.0f;
   }
+}
+
+// x's fragment of one block for the m16n8k32 products: lane (g, t) holds
+// vector g's plane words (t, t + 4) and s, sum for vectors 2t, 2t + 1.
+struct XFragment {
+  uint2 planes[3];
+  float2 s, fsum;
+  int2 sum;
+};
+
+template <typename T>
+__device__ __forceinline__ void load_fragment(const uint8_t* rec, bool have_vector, XFragment& x) {
+  const int lane = threadIdx.x % 32, g = lane / 4, t = lane % 4;
+#pragma unroll
+  for (int p = 0; p < 3; ++p)
+    x.planes[p] = have_vector
+                      ? __ldg(reinterpret_cast<const uint2*>(rec + mma_plane_byte(g, p, t)))
+                      : make_uint2(0, 0);
+  const uint8_t* s0 = rec + mma_scale_byte(2 * t);
+  const uint8_t* s1 = rec + mma_scale_byte(2 * t + 1);
+  x.s = make_float2(__ldg(reinterpret_cast<const float*>(s0)), __ldg(reinterpret_cast<const float*>(s1)));
+  x.sum = T::DTYPE == DRIFT_Q4_0
+              ? make_int2(__ldg(reinterpret_cast<const int*>(s0) + 1), __ldg(reinterpret_cast<const int*>(s1) + 1))
+              : make_int2(0, 0);
+  x.fsum = T::DTYPE == DRIFT_Q4_1 ? make_float2(__ldg(reinterpret_cast<const float*>(s0) + 2),
+                                                __ldg(reinterpret_cast<const float*>(s1) + 2))
+                                  : make_float2(0.0f, 0.0f);
 }
 
 // One output's share of a block before the x scale s: the three plane sums
