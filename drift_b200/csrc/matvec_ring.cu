@@ -316,6 +316,15 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
   int issued = 0, consumed = 0;
   bool ok = true;
   while (issued < jobs && issued < S) issue(issued++);
+  if constexpr (MODE != MODE_MMA) {
+    // While the first copies fly: bring this launch's x -- the line or two of
+    // each record that the vectors' slots occupy -- into L1, where every row
+    // of every tile reads it, instead of each warp missing it on first touch.
+    constexpr int LINES = MODE == MODE_DP4A_1 ? 1 : 2;
+    for (int i = threadIdx.x; i < blocks * LINES; i += blockDim.x)
+      asm volatile("prefetch.global.L1 [%0];" ::"l"(records + (long long)(i / LINES) * MMA_RECORD_BYTES +
+                                                    128 * (i % LINES)));
+  }
   Acc<MODE> acc;
   acc.zero();
   const int whole = plan.rounds * segments;
