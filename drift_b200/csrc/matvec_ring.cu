@@ -23,6 +23,8 @@
 // vectors.
 #include <cuda_runtime.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "mma_i8.cuh"
 #include "quant.cuh"
@@ -61,8 +63,10 @@ struct RingShape {
   static constexpr int WARPS = T::DTYPE == DRIFT_Q8_0 ? 6 : 8;
   static constexpr int S = 2;
   static constexpr int BARS = WARPS * S * Ring<T>::STAGE;
-  static constexpr int BYTES = BARS + WARPS * S * 8 + 16 + 1024;  // + room to align to 1024
+  static constexpr int X_OFFSET = BARS + WARPS * S * 8 + 16;  // x staged for the dp4a modes
+  static constexpr int BYTES = X_OFFSET + 1024;  // + room to align to 1024; + x when staged
 };
+constexpr int MAX_SMEM = 232448;
 
 // One vector's x for one block, as the dp4a modes use it.
 struct XBlock {
@@ -71,14 +75,25 @@ struct XBlock {
   int sum;
 };
 
-template <typename T>
+// Where the dp4a modes read x from: the records in global memory (896 bytes
+// apart, read through L1) or their slots copied into shared memory.
+struct XGlobal {
+  static constexpr bool SHARED = false;
+  __device__ static uint4 at(const uint8_t* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+};
+struct XShared {
+  static constexpr bool SHARED = true;
+  __device__ static uint4 at(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+};
+
+template <typename T, typename SRC>
 __device__ __forceinline__ void load_x(const uint8_t* rec, int v, XBlock& x) {
   // vector v's slot: 96 bytes of planes, then s, sum, fsum -- one 128-byte line
-  const uint4* q = reinterpret_cast<const uint4*>(rec + MMA_SLOT_BYTES * v);
+  const uint8_t* slot = rec + MMA_SLOT_BYTES * v;
 #pragma unroll
   for (int p = 0; p < 3; ++p) {
     // plane p: words (0, 4, 1, 5) then (2, 6, 3, 7)
-    const uint4 q0 = __ldg(q + 2 * p), q1 = __ldg(q + 2 * p + 1);
+    const uint4 q0 = SRC::at(slot + 32 * p), q1 = SRC::at(slot + 32 * p + 16);
     x.planes[8 * p + 0] = q0.x;
     x.planes[8 * p + 4] = q0.y;
     x.planes[8 * p + 1] = q0.z;
@@ -88,7 +103,7 @@ __device__ __forceinline__ void load_x(const uint8_t* rec, int v, XBlock& x) {
     x.planes[8 * p + 3] = q1.z;
     x.planes[8 * p + 7] = q1.w;
   }
-  const uint4 scales = __ldg(q + 6);
+  const uint4 scales = SRC::at(slot + 96);
   x.s = __uint_as_float(scales.x);
   x.sum = T::DTYPE == DRIFT_Q4_0 ? int(scales.y) : 0;
   x.fsum = T::DTYPE == DRIFT_Q4_1 ? __uint_as_float(scales.z) : 0.0f;
@@ -101,7 +116,7 @@ __device__ __forceinline__ void load_x(const uint8_t* rec, int v, XBlock& x) {
 // two rows, fetched one block ahead -- in 24 dp4a, and acc = fmaf(s, value,
 // acc) with the same value and order as the MMA mode: the plane sums are
 // exact integers either way, so a row's result does not depend on the mode.
-template <typename T, int V, bool FULL>
+template <typename T, int V, typename SRC, int STRIDE, bool FULL>
 __device__ __forceinline__ void segment_dp4a_blocks(const uint8_t* row0, const uint8_t* row1,
                                                     const uint8_t* rec0, int count,
                                                     float (&acc)[2][4]) {
@@ -109,7 +124,7 @@ __device__ __forceinline__ void segment_dp4a_blocks(const uint8_t* row0, const u
   uint32_t w0[HALF / 4], w1[HALF / 4];
   XBlock x[2][V];
 #pragma unroll
-  for (int v = 0; v < V; ++v) load_x<T>(rec0, v, x[0][v]);
+  for (int v = 0; v < V; ++v) load_x<T, SRC>(rec0, v, x[0][v]);
 #pragma unroll
   for (int b = 0; b < SEG_BLOCKS; ++b) {
     if (FULL || b < count) {
@@ -122,7 +137,7 @@ __device__ __forceinline__ void segment_dp4a_blocks(const uint8_t* row0, const u
       }
       if (b + 1 < SEG_BLOCKS && (FULL || b + 1 < count)) {
 #pragma unroll
-        for (int v = 0; v < V; ++v) load_x<T>(rec0 + (b + 1) * MMA_RECORD_BYTES, v, x[(b + 1) & 1][v]);
+        for (int v = 0; v < V; ++v) load_x<T, SRC>(rec0 + (b + 1) * STRIDE, v, x[(b + 1) & 1][v]);
       }
       const int word = (b * T::BYTES) / 4 - (b >= 4 ? HALF / 4 : 0);
       uint32_t a[T::WORDS], c[T::WORDS];
@@ -145,18 +160,21 @@ __device__ __forceinline__ void segment_dp4a_blocks(const uint8_t* row0, const u
   }
 }
 
-template <typename T, int V>
+// `x`: the records in global memory, or (XSMEM) their first V slots copied
+// to shared memory, 112 V bytes a block.
+template <typename T, int V, bool XSMEM>
 __device__ __forceinline__ void segment_dp4a(const uint8_t* stage, int first_block, int count,
-                                             const uint8_t* __restrict__ records,
-                                             float (&acc)[2][4]) {
+                                             const uint8_t* x, float (&acc)[2][4]) {
   const int lane = threadIdx.x % WARP;
   const uint8_t* row0 = stage + lane * Ring<T>::PITCH;
   const uint8_t* row1 = row0 + 32 * Ring<T>::PITCH;
-  const uint8_t* rec0 = records + (long long)first_block * MMA_RECORD_BYTES;
+  using SRC = typename std::conditional<XSMEM, XShared, XGlobal>::type;
+  constexpr int STRIDE = XSMEM ? MMA_SLOT_BYTES * V : MMA_RECORD_BYTES;
+  const uint8_t* rec0 = x + (long long)first_block * STRIDE;
   if (count == SEG_BLOCKS)
-    segment_dp4a_blocks<T, V, true>(row0, row1, rec0, SEG_BLOCKS, acc);
+    segment_dp4a_blocks<T, V, SRC, STRIDE, true>(row0, row1, rec0, SEG_BLOCKS, acc);
   else
-    segment_dp4a_blocks<T, V, false>(row0, row1, rec0, count, acc);
+    segment_dp4a_blocks<T, V, SRC, STRIDE, false>(row0, row1, rec0, count, acc);
 }
 
 // ---- MMA mode: 3-8 vectors -------------------------------------------------------------------
@@ -274,7 +292,7 @@ struct Schedule {
   }
 };
 
-template <typename T, int MODE>
+template <typename T, int MODE, bool XSMEM>
 __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
     matvec_ring_kernel(const __grid_constant__ CUtensorMap wmap,
                        const uint8_t* __restrict__ records, float* __restrict__ y, int rows,
@@ -316,10 +334,24 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
   int issued = 0, consumed = 0;
   bool ok = true;
   while (issued < jobs && issued < S) issue(issued++);
-  if constexpr (MODE != MODE_MMA) {
-    // While the first copies fly: bring this launch's x -- the line or two of
-    // each record that the vectors' slots occupy -- into L1, where every row
-    // of every tile reads it, instead of each warp missing it on first touch.
+  const uint8_t* x = records;
+  if constexpr (XSMEM) {
+    // While the first copies fly: the vectors' slots of every block's record,
+    // 112 V bytes a block, into shared memory, where every row of every tile
+    // reads them.
+    static_assert(MODE != MODE_MMA, "the MMA mode reads x from global memory");
+    constexpr int SLOT = MMA_SLOT_BYTES * MODE;
+    uint8_t* xs = smem + Shape::X_OFFSET;
+    for (int i = threadIdx.x; i < blocks * (SLOT / 16); i += blockDim.x) {
+      const int block = i / (SLOT / 16), part = i % (SLOT / 16);
+      *reinterpret_cast<uint4*>(xs + block * SLOT + 16 * part) = __ldg(
+          reinterpret_cast<const uint4*>(records + (long long)block * MMA_RECORD_BYTES + 16 * part));
+    }
+    __syncthreads();
+    x = xs;
+  } else if constexpr (MODE != MODE_MMA) {
+    // x stays in global memory: bring the line or two of each record that the
+    // vectors' slots occupy into L1 before the first rows need them.
     constexpr int LINES = MODE == MODE_DP4A_1 ? 1 : 2;
     for (int i = threadIdx.x; i < blocks * LINES; i += blockDim.x)
       asm volatile("prefetch.global.L1 [%0];" ::"l"(records + (long long)(i / LINES) * MMA_RECORD_BYTES +
@@ -339,7 +371,7 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
       if constexpr (MODE == MODE_MMA)
         segment_mma<T>(ring + (j % S) * STAGE, first, count, records, vectors, acc.a);
       else
-        segment_dp4a<T, MODE>(ring + (j % S) * STAGE, first, count, records, acc.a);
+        segment_dp4a<T, MODE, XSMEM>(ring + (j % S) * STAGE, first, count, x, acc.a);
     }
     __syncwarp();
     ++consumed;
@@ -381,22 +413,37 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
   }
 }
 
-template <typename T, int MODE>
+template <typename T, int MODE, bool XSMEM>
 int launch_mode(const CUtensorMap& wmap, const uint8_t* records, float* y, int rows, int cols,
-                int vectors, cudaStream_t stream) {
+                int vectors, int smem, cudaStream_t stream) {
   using Shape = RingShape<T>;
   static bool configured = false;
   if (!configured) {
-    DRIFT_CUDA(cudaFuncSetAttribute(matvec_ring_kernel<T, MODE>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, Shape::BYTES));
+    DRIFT_CUDA(cudaFuncSetAttribute(matvec_ring_kernel<T, MODE, XSMEM>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_SMEM));
     configured = true;
   }
   const int tiles = (rows + ROWS - 1) / ROWS;
   const unsigned grid = unsigned(tiles < sm_count() ? tiles : sm_count());
-  matvec_ring_kernel<T, MODE><<<grid, Shape::WARPS * 32, Shape::BYTES, stream>>>(
+  matvec_ring_kernel<T, MODE, XSMEM><<<grid, Shape::WARPS * 32, smem, stream>>>(
       wmap, records, y, rows, cols, vectors, device_error_word());
   DRIFT_LAUNCHED("matvec_ring");
   return 0;
+}
+
+// The 1-2 vector products stage x in shared memory when it fits beside the
+// ring (112 bytes a block a vector: up to 14,500 columns for one Q4 vector)
+// and every CTA has tiles enough to repay the copy (a small matrix is over
+// before the staged x would pay for itself).
+template <typename T, int MODE>
+int launch_dp4a(const CUtensorMap& wmap, const uint8_t* records, float* y, int rows, int cols,
+                int vectors, cudaStream_t stream) {
+  const long long staged = RingShape<T>::BYTES + (long long)(cols / 32) * MMA_SLOT_BYTES * MODE;
+  const long long tiles = (rows + ROWS - 1) / ROWS;
+  if (staged <= MAX_SMEM && tiles >= 4LL * sm_count())
+    return launch_mode<T, MODE, true>(wmap, records, y, rows, cols, vectors, int(staged), stream);
+  return launch_mode<T, MODE, false>(wmap, records, y, rows, cols, vectors, RingShape<T>::BYTES,
+                                     stream);
 }
 
 // One configuration per matrix type, whatever the number of vectors, so a
@@ -407,15 +454,18 @@ int ring_dispatch(const uint8_t* weight, const uint8_t* records, float* y, int r
   CUtensorMap wmap;
   DRIFT_TRY(encode_word_rows(&wmap, weight, int64_t(cols / 32) * T::BYTES / 4, rows,
                              Ring<T>::PITCH / 4, ROWS));
-  if (vectors == 1) return launch_mode<T, MODE_DP4A_1>(wmap, records, y, rows, cols, vectors, stream);
-  if (vectors == 2) return launch_mode<T, MODE_DP4A_2>(wmap, records, y, rows, cols, vectors, stream);
-  return launch_mode<T, MODE_MMA>(wmap, records, y, rows, cols, vectors, stream);
+  if (vectors == 1) return launch_dp4a<T, MODE_DP4A_1>(wmap, records, y, rows, cols, vectors, stream);
+  if (vectors == 2) return launch_dp4a<T, MODE_DP4A_2>(wmap, records, y, rows, cols, vectors, stream);
+  return launch_mode<T, MODE_MMA, false>(wmap, records, y, rows, cols, vectors, RingShape<T>::BYTES,
+                                         stream);
 }
 
-#define DRIFT_RING_REGISTER(T, name)                                              \
-  DRIFT_REGISTER(matvec_ring_##name##_dp4a1, (matvec_ring_kernel<T, MODE_DP4A_1>)) \
-  DRIFT_REGISTER(matvec_ring_##name##_dp4a2, (matvec_ring_kernel<T, MODE_DP4A_2>)) \
-  DRIFT_REGISTER(matvec_ring_##name##_mma, (matvec_ring_kernel<T, MODE_MMA>))
+#define DRIFT_RING_REGISTER(T, name)                                                        \
+  DRIFT_REGISTER(matvec_ring_##name##_dp4a1, (matvec_ring_kernel<T, MODE_DP4A_1, false>))    \
+  DRIFT_REGISTER(matvec_ring_##name##_dp4a1_xs, (matvec_ring_kernel<T, MODE_DP4A_1, true>))  \
+  DRIFT_REGISTER(matvec_ring_##name##_dp4a2, (matvec_ring_kernel<T, MODE_DP4A_2, false>))    \
+  DRIFT_REGISTER(matvec_ring_##name##_dp4a2_xs, (matvec_ring_kernel<T, MODE_DP4A_2, true>))  \
+  DRIFT_REGISTER(matvec_ring_##name##_mma, (matvec_ring_kernel<T, MODE_MMA, false>))
 DRIFT_RING_REGISTER(Q8_0T, q8_0)
 DRIFT_RING_REGISTER(Q4_0T, q4_0)
 DRIFT_RING_REGISTER(Q4_1T, q4_1)
