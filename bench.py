@@ -304,7 +304,8 @@ def run_gpu(args) -> dict | None:
             "peak_source": peaks["source"] + " (MEASURED_PEAKS.json hbm_gbs, copy)",
             "unit": "GB/s",
             "frac": round(dominant["gbs"] / peaks["hbm_gbs"], 4),
-            "traffic": None,
+            "traffic": profiled_traffic(),
+            "traffic_source": "profiles/matvec_ring_q4_1_lmhead.md (ncu dram read + write, one launch)",
             "launch_us": round(dominant["us"], 3),
         },
         "clocks": clock_info,
@@ -313,6 +314,19 @@ def run_gpu(args) -> dict | None:
     if args.cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(seconds=args.cpu_seconds)
     return result
+
+
+def profiled_traffic() -> int | None:
+    """DRAM bytes (read + write) of one lm-head batch-1 launch of the ring
+    kernel, as the committed ncu summary records them."""
+    path = os.path.join(ROOT, "profiles", "matvec_ring_q4_1_lmhead.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_b1:"):
+                return int(line.split(":")[1])
+    except OSError:
+        pass
+    return None
 
 
 def count_launches(graph) -> int:
