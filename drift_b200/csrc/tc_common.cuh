@@ -44,15 +44,38 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// The same test, letting the thread sleep until the phase completes or
+// `ns` nanoseconds pass (a waiting warp then takes no issue slots).
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return done != 0;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
 // Waits for the phase of `bar` with the given parity to complete, at most
-// about a second; on giving up, flags `abort` (shared) and the device error
-// word (code 2) and returns false. A kernel never spins forever.
+// about a second by the global timer; on giving up, flags `abort` (shared)
+// and the device error word (code 2) and returns false. A kernel never spins
+// forever, and a waiting thread sleeps in slices of 20 us rather than spin.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                                           int* error) {
-  for (uint32_t i = 0; i < (1u << 22); ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = global_ns();
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity, 20000)) return true;
     if (*abort) return false;
-    if (i > 4096) __nanosleep(256);
+    if (global_ns() - start > 1000000000ull) break;
   }
   *abort = 1;
   if (error) atomicCAS(error, 0, 2);
