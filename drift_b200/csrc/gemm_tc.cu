@@ -374,39 +374,42 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
     }
   } else if (warp == MMA_WARP) {
-    // ---- MMA issuer ----
-    if (lane == 0) {
+    // ---- MMA issuer: the whole warp, one elected lane issuing ----
+    {
       const uint32_t idesc = tc::instr_desc_f16(TILE_ROWS, TILE_VECTORS);
       int gc = 0, local = 0;
       bool ok = true;
       for (int u = blockIdx.x; ok && u < units; u += gridDim.x, ++local) {
         const int b = local & 1;
-        if (local >= 2 && !(ok = tc::mbar_wait(&acc_empty[b], ((local >> 1) - 1) & 1, abort, error)))
+        if (local >= 2 &&
+            !(ok = tc::mbar_wait_warp(&acc_empty[b], ((local >> 1) - 1) & 1, abort, error)))
           break;
         tc::fence_after_sync();
         const uint32_t acc = tmem + 64 * b;
         const int c0 = plan.chunk_begin(u);
         for (int c = c0; ok && c < plan.chunk_end(u); ++c, ++gc) {
           const int s = gc % XS;
-          if (!(ok = tc::mbar_wait(&x_full[s], (gc / XS) & 1, abort, error))) break;
-          if (!(ok = tc::mbar_wait(&a_full[gc & 1], (gc >> 1) & 1, abort, error))) break;
+          if (!(ok = tc::mbar_wait_warp(&x_full[s], (gc / XS) & 1, abort, error))) break;
+          if (!(ok = tc::mbar_wait_warp(&a_full[gc & 1], (gc >> 1) & 1, abort, error))) break;
           tc::fence_after_sync();
           // one chunk: 16 MMAs back to back (the tensor core's queue stays full
-          // while this thread waits for the next chunk), then one commit per ring
-          const uint32_t b_base = tc::smem_u32(smem + L::X_OFFSET + s * X_CHUNK_BYTES);
-          const uint64_t b_desc = tc::smem_desc_sw128(b_base);
+          // while the warp waits for the next chunk), then one commit per ring
+          const uint64_t b_desc =
+              tc::smem_desc_sw128(tc::smem_u32(smem + L::X_OFFSET + s * X_CHUNK_BYTES));
+          const uint32_t a_base = tmem + 128 + 32 * (gc & 1);
+          const uint32_t first = c != c0;
 #pragma unroll
           for (int g = 0; g < 4; ++g) {
 #pragma unroll
             for (int j = 0; j < 4; ++j)
-              tc::mma_f16_ts(acc, tmem + 128 + 32 * (2 * g + (gc & 1)) + 8 * j,
-                             b_desc + uint64_t((g * X_TILE_BYTES + j * 32) >> 4), idesc,
-                             (c != c0) | g | j);
+              tc::mma_f16_ts_warp(acc, a_base + 64 * g + 8 * j,
+                                  b_desc + uint64_t((g * X_TILE_BYTES + j * 32) >> 4), idesc,
+                                  (g | j) ? 1u : first);
           }
-          tc::mma_commit(&a_empty[gc & 1]);
-          tc::mma_commit(&x_empty[s]);
+          tc::mma_commit_warp(&a_empty[gc & 1]);
+          tc::mma_commit_warp(&x_empty[s]);
         }
-        if (ok) tc::mma_commit(&acc_full[b]);
+        if (ok) tc::mma_commit_warp(&acc_full[b]);
       }
     }
   } else {
