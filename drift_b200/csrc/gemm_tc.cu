@@ -226,8 +226,9 @@ __global__ void tc_prepare_x_kernel(const void* __restrict__ x, __half* __restri
 constexpr int DEQUANT_WARPS = 16;
 constexpr int W_WARP = 16, MMA_WARP = 17, X_WARP = 18;
 constexpr int TC_THREADS = 32 * (DEQUANT_WARPS + 3);
-// TMEM columns: accumulators 0-63 and 64-127; warpgroup g's two A buffers at
-// 128 + 64 g and 160 + 64 g (it fills one while the MMA reads the other)
+// TMEM columns: accumulators 0-63 and 64-127; three sets of A buffers (chunk
+// number mod 3), warpgroup g's at 128 + 128 set + 32 g: the dequant warps
+// fill one set while the MMA reads another
 constexpr uint32_t TMEM_COLUMNS = 512;
 
 // Two rings: raw weights (freed by the dequant warps, so they run ahead of
@@ -243,7 +244,7 @@ struct TcLayout {
   // w_full, w_empty [W], x_full, x_empty [X], a_full, a_empty, acc_full,
   // acc_empty [2], tmem slot, abort
   static constexpr int SMEM_BYTES = BARRIER_OFFSET + 512 + 1024;  // + alignment slack
-  static_assert((2 * W_STAGES + 2 * X_STAGES + 8) * 8 + 8 <= 512, "barrier area");
+  static_assert((2 * W_STAGES + 2 * X_STAGES + 10) * 8 + 8 <= 512, "barrier area");
   static_assert(SMEM_BYTES <= 232448, "shared memory");
 };
 
@@ -302,9 +303,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint64_t* w_empty = w_full + WS;
   uint64_t* x_full = w_empty + WS;
   uint64_t* x_empty = x_full + XS;
-  uint64_t* a_full = x_empty + XS;  // [2]: chunk parity
-  uint64_t* a_empty = a_full + 2;
-  uint64_t* acc_full = a_empty + 2;
+  uint64_t* a_full = x_empty + XS;  // [3]: chunk number mod 3
+  uint64_t* a_empty = a_full + 3;
+  uint64_t* acc_full = a_empty + 3;
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -321,7 +322,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       tc::mbar_init(&x_full[s], 1);
       tc::mbar_init(&x_empty[s], 1);  // the MMA's commit
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < 3; ++i) {
       tc::mbar_init(&a_full[i], DEQUANT_WARPS);  // a chunk's A, all four steps
       tc::mbar_init(&a_empty[i], 1);             // the MMA's commit
     }
@@ -390,23 +391,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         for (int c = c0; ok && c < plan.chunk_end(u); ++c, ++gc) {
           const int s = gc % XS;
           if (!(ok = tc::mbar_wait_warp(&x_full[s], (gc / XS) & 1, abort, error))) break;
-          if (!(ok = tc::mbar_wait_warp(&a_full[gc & 1], (gc >> 1) & 1, abort, error))) break;
+          if (!(ok = tc::mbar_wait_warp(&a_full[gc % 3], (gc / 3) & 1, abort, error))) break;
           tc::fence_after_sync();
           // one chunk: 16 MMAs back to back (the tensor core's queue stays full
           // while the warp waits for the next chunk), then one commit per ring
           const uint64_t b_desc =
               tc::smem_desc_sw128(tc::smem_u32(smem + L::X_OFFSET + s * X_CHUNK_BYTES));
-          const uint32_t a_base = tmem + 128 + 32 * (gc & 1);
+          const uint32_t a_base = tmem + 128 + 128 * (gc % 3);
           const uint32_t first = c != c0;
 #pragma unroll
           for (int g = 0; g < 4; ++g) {
 #pragma unroll
             for (int j = 0; j < 4; ++j)
-              tc::mma_f16_ts_warp(acc, a_base + 64 * g + 8 * j,
+              tc::mma_f16_ts_warp(acc, a_base + 32 * g + 8 * j,
                                   b_desc + uint64_t((g * X_TILE_BYTES + j * 32) >> 4), idesc,
                                   (g | j) ? 1u : first);
           }
-          tc::mma_commit_warp(&a_empty[gc & 1]);
+          tc::mma_commit_warp(&a_empty[gc % 3]);
           tc::mma_commit_warp(&x_empty[s]);
         }
         if (ok) tc::mma_commit_warp(&acc_full[b]);
@@ -476,8 +477,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       for (int c = plan.chunk_begin(u); ok && c < plan.chunk_end(u); ++c, ++gc) {
         const int s = gc % WS;
         if (!(ok = tc::mbar_wait_warp(&w_full[s], (gc / WS) & 1, abort, error))) break;
-        const int buf = 2 * group + (gc & 1);
-        if (gc >= 2 && !(ok = tc::mbar_wait_warp(&a_empty[gc & 1], ((gc >> 1) - 1) & 1, abort, error)))
+        if (gc >= 3 && !(ok = tc::mbar_wait_warp(&a_empty[gc % 3], ((gc / 3) - 1) & 1, abort, error)))
           break;
         tc::fence_after_sync();
         const uint8_t* raw_row = smem + s * L::RAW_PADDED + row_in_tile * Unpack<T>::PITCH_WORDS * 4;
@@ -485,11 +485,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         dequant_step<T>(group, raw_row, a);
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&w_empty[s]);  // the raw weights are in registers
-        tc::tmem_store_32(tmem + lane_base + 128 + 32 * buf, a);
+        tc::tmem_store_32(tmem + lane_base + 128 + 128 * (gc % 3) + 32 * group, a);
         tc::tmem_store_wait();
         tc::fence_before_sync();
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&a_full[gc & 1]);
+        if (lane == 0) tc::mbar_arrive(&a_full[gc % 3]);
         if (pending >= 0) {
           ok = epilogue(pending, pending_local);
           pending = -1;
