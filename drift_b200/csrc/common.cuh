@@ -49,5 +49,34 @@ constexpr int WARP = 32;
 
 #define DRIFT_CUDA(call) DRIFT_TRY(::drift::cuda_status((call), #call))
 
+// ---- programmatic dependent launch ------------------------------------------
+// The products launch with programmatic stream serialization: a kernel may
+// start while the kernel before it in the stream finishes, and does what
+// depends on nothing -- barrier set-up, the first weight copies (weights are
+// never written by the kernels of this library) -- before pdl_wait(), which
+// returns once the previous kernel has completed and its writes are visible.
+// Every global read of data another kernel writes, and every global write,
+// comes after pdl_wait(). pdl_trigger() lets the next such kernel start.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... Params, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t config = {};
+  config.gridDim = grid;
+  config.blockDim = block;
+  config.dynamicSmemBytes = smem;
+  config.stream = stream;
+  cudaLaunchAttribute attribute[1];
+  attribute[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attribute[0].val.programmaticStreamSerializationAllowed = 1;
+  config.attrs = attribute;
+  config.numAttrs = 1;
+  return cudaLaunchKernelEx(&config, kernel, static_cast<Params>(args)...);
+}
+
 // The launch just queued, checked (a bad configuration fails here, not later).
 #define DRIFT_LAUNCHED(name) DRIFT_TRY(::drift::cuda_status(cudaGetLastError(), name))

@@ -198,6 +198,8 @@ template <typename T, bool BF16>
 __global__ void tc_prepare_x_kernel(const void* __restrict__ x, __half* __restrict__ out,
                                     int vectors, int cols, int chunks, long long total,
                                     int* counters, int count) {
+  pdl_trigger();  // the product may launch and start on its weights
+  pdl_wait();
   // the split product's arrival counters start at zero
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += gridDim.x * blockDim.x)
     counters[i] = 0;
@@ -338,6 +340,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
+  pdl_trigger();
+  // Only the weight producer may run ahead of the previous kernel: everything
+  // else reads x or writes out, scratch and counters.
+  if (warp != W_WARP) pdl_wait();
 
   if (warp == W_WARP || warp == X_WARP) {
     // ---- producers: raw weights (2-D tensor copy of 128 rows), x (one bulk copy) ----
@@ -554,12 +560,11 @@ static int launch_tc(int x_dtype, const void* x, const void* weight, float* y, i
     if (blocks > (long long)sms * 32) blocks = (long long)sms * 32;
     const int counters = plan.splits > 1 ? plan.tiles * DEQUANT_WARPS : 0;
     if (x_dtype == DRIFT_BF16)
-      tc_prepare_x_kernel<T, true><<<unsigned(blocks), 256, 0, stream>>>(
-          x, xs, int(m), int(k), plan.chunks, total, scratch.arrivals, counters);
+      DRIFT_CUDA(launch_pdl(tc_prepare_x_kernel<T, true>, unsigned(blocks), 256, 0, stream, x, xs,
+                            int(m), int(k), plan.chunks, total, scratch.arrivals, counters));
     else
-      tc_prepare_x_kernel<T, false><<<unsigned(blocks), 256, 0, stream>>>(
-          x, xs, int(m), int(k), plan.chunks, total, scratch.arrivals, counters);
-    DRIFT_LAUNCHED("tc_prepare_x");
+      DRIFT_CUDA(launch_pdl(tc_prepare_x_kernel<T, false>, unsigned(blocks), 256, 0, stream, x, xs,
+                            int(m), int(k), plan.chunks, total, scratch.arrivals, counters));
   }
   const int64_t row_bytes = k / 32 * T::BYTES;
   CUtensorMap wmap;
@@ -573,10 +578,9 @@ static int launch_tc(int x_dtype, const void* x, const void* weight, float* y, i
   }
   const long long units = (long long)plan.tiles * plan.splits;
   const int grid = units < sms ? int(units) : sms;
-  linear_tc_kernel<T><<<grid, TC_THREADS, L::SMEM_BYTES, stream>>>(
-      wmap, reinterpret_cast<const uint8_t*>(xs), y, int(n), int(m), plan, scratch,
-      device_error_word());
-  DRIFT_LAUNCHED("linear_tc");
+  DRIFT_CUDA(launch_pdl(linear_tc_kernel<T>, grid, TC_THREADS, L::SMEM_BYTES, stream, wmap,
+                        reinterpret_cast<const uint8_t*>(xs), y, int(n), int(m), plan, scratch,
+                        device_error_word()));
   return 0;
 }
 

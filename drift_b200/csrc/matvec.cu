@@ -95,6 +95,8 @@ extern "C" __global__ void __launch_bounds__(256)
 template <bool BF16>
 __global__ void __launch_bounds__(256) quantize_x22_mma_kernel(const void* x, uint8_t* records,
                                                               int vectors, int blocks) {
+  pdl_trigger();  // the product may launch and start on its weights
+  pdl_wait();     // x, and the records the previous product reads, are ours now
   const long long index = (long long)blockIdx.x * (blockDim.x / WARP) + threadIdx.x / WARP;
   const int passes = (vectors + 7) / 8;
   if (index >= (long long)passes * 8 * blocks) return;
@@ -406,10 +408,11 @@ int prepare_x_mma(int x_dtype, const void* x, int64_t m, int64_t k, uint8_t* rec
   if (warps == 0) return 0;
   const unsigned grid = unsigned((warps + 7) / 8);
   if (x_dtype == DRIFT_BF16)
-    quantize_x22_mma_kernel<true><<<grid, 256, 0, stream>>>(x, records, int(m), int(blocks));
+    DRIFT_CUDA(launch_pdl(quantize_x22_mma_kernel<true>, grid, 256, 0, stream, x, records, int(m),
+                          int(blocks)));
   else
-    quantize_x22_mma_kernel<false><<<grid, 256, 0, stream>>>(x, records, int(m), int(blocks));
-  DRIFT_LAUNCHED("quantize_x22_mma");
+    DRIFT_CUDA(launch_pdl(quantize_x22_mma_kernel<false>, grid, 256, 0, stream, x, records, int(m),
+                          int(blocks)));
   return 0;
 }
 

@@ -334,6 +334,8 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
   int issued = 0, consumed = 0;
   bool ok = true;
   while (issued < jobs && issued < S) issue(issued++);
+  pdl_trigger();
+  pdl_wait();  // the weights' first copies are in flight; x is now ready
   const uint8_t* x = records;
   if constexpr (XSMEM) {
     // While the first copies fly: the vectors' slots of every block's record,
@@ -425,9 +427,8 @@ int launch_mode(const CUtensorMap& wmap, const uint8_t* records, float* y, int r
   }
   const int tiles = (rows + ROWS - 1) / ROWS;
   const unsigned grid = unsigned(tiles < sm_count() ? tiles : sm_count());
-  matvec_ring_kernel<T, MODE, XSMEM><<<grid, Shape::WARPS * 32, smem, stream>>>(
-      wmap, records, y, rows, cols, vectors, device_error_word());
-  DRIFT_LAUNCHED("matvec_ring");
+  DRIFT_CUDA(launch_pdl(matvec_ring_kernel<T, MODE, XSMEM>, grid, Shape::WARPS * 32, smem, stream,
+                        wmap, records, y, rows, cols, vectors, device_error_word()));
   return 0;
 }
 
