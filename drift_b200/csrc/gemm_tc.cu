@@ -3,27 +3,31 @@
 // F16 and multiplied by hipBLAS with F32 compute, ops/HipLinear.scala:
 // 389-469, kernels/matvec.hip:801-810), fused into one persistent kernel.
 //
-// One CTA per SM, 18 warps, units of 128 weight rows x 64 vectors (x a
+// One CTA per SM, 19 warps, units of 128 weight rows x 64 vectors (x a
 // K-range of the columns, when a matrix has too few rows to fill the SMs):
-//  - warp 16 (TMA): streams each 256-column chunk of the unit's raw GGML
-//    blocks (a 2-D tensor copy, 128 rows) and the matching four 64-column
-//    tiles of x (F16, 128-byte swizzled, the UMMA canonical K-major layout)
-//    into a 3-stage shared-memory ring;
+//  - warp 16 (weights): streams each 256-column chunk of the unit's raw GGML
+//    blocks (a 2-D tensor copy, 128 rows) into a 5-stage ring (3 for Q8_0),
+//    freed as soon as the dequant warps hold a stage in registers;
+//  - warp 18 (x): one bulk copy per chunk of the four 64-column x tiles (F16,
+//    pre-swizzled by tc_prepare_x into the UMMA canonical K-major layout)
+//    into a 3-stage ring, freed by the MMA's commit;
 //  - warps 0-15 (dequant, four warpgroups, warpgroup g taking 64-column step g
 //    of every chunk): each thread turns its row's two blocks into 64 F16
 //    weights -- d * q + m rounded once, as the reference's dequantize_<t>
 //    does -- and stores them straight into tensor memory (tcgen05.st), into
-//    its warpgroup's own A buffer, which is where the MMA reads A from: the
+//    one of three sets of A buffers, which is where the MMA reads A from: the
 //    dequantized tile never touches shared memory;
-//  - warp 17 (MMA): one thread issues tcgen05.mma kind::f16 with A in TMEM, B
-//    in shared memory and the F32 accumulator in TMEM (128 x 64, two of them
-//    so a unit's epilogue overlaps the next unit's products), committing to
-//    mbarriers that free the A buffers and ring stages.
+//  - warp 17 (MMA): the whole warp waits, one elected lane issues the chunk's
+//    16 tcgen05.mma kind::f16 back to back (A in TMEM, B in shared memory,
+//    the F32 accumulator in TMEM: 128 x 64, two of them so a unit's epilogue
+//    overlaps the next unit's products) and commits once per ring.
 // One chunk into the next unit, the dequant warps read the last unit's
 // accumulator back (tcgen05.ld) and store F32 out -- or, for a unit that
 // holds a K-range, store it as a partial sum; the last of a tile's K-ranges
 // to finish adds the partials in K order, so the result does not depend on
-// which CTA finishes first. Every wait is bounded (tc_common.cuh).
+// which CTA finishes first. Every wait is bounded (tc_common.cuh). The kernel
+// is launched as a programmatic dependent of the x preparation: it sets up
+// and starts the weight copies while that kernel finishes.
 //
 // The weights' values within a 32-block come out of the unpacking in a
 // permuted order (pairs of nibbles that one LOP3 makes into an F16x2), so x
@@ -225,8 +229,12 @@ __global__ void tc_prepare_x_kernel(const void* __restrict__ x, __half* __restri
 }
 
 // ---- the product ------------------------------------------------------------------------------
+// Dequant warps: GROUPS warpgroups (one warp per TMEM lane quarter each),
+// warpgroup g taking the STEPS 64-column steps g * STEPS.. of every chunk.
 constexpr int DEQUANT_WARPS = 16;
-constexpr int W_WARP = 16, MMA_WARP = 17, X_WARP = 18;
+constexpr int GROUPS = DEQUANT_WARPS / 4, STEPS = 4 / GROUPS;
+constexpr int VCOLS = TILE_VECTORS / GROUPS;  // accumulator columns a dequant warp reads back
+constexpr int W_WARP = DEQUANT_WARPS, MMA_WARP = DEQUANT_WARPS + 1, X_WARP = DEQUANT_WARPS + 2;
 constexpr int TC_THREADS = 32 * (DEQUANT_WARPS + 3);
 // TMEM columns: accumulators 0-63 and 64-127; three sets of A buffers (chunk
 // number mod 3), warpgroup g's at 128 + 128 set + 32 g: the dequant warps
@@ -278,6 +286,13 @@ __device__ __forceinline__ void tmem_load_16(uint32_t address, uint32_t (&v)[16]
       : "r"(address)
       : "memory");
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_load_cols(uint32_t address, uint32_t (&v)[16]) {
+  tmem_load_16(address, v);
+}
+__device__ __forceinline__ void tmem_load_cols(uint32_t address, uint32_t (&v)[32]) {
+  tc::tmem_load_32(address, v);
 }
 
 template <typename T>
@@ -431,30 +446,30 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int b = l & 1;
       if (!tc::mbar_wait_warp(&acc_full[b], (l >> 1) & 1, abort, error)) return false;
       tc::fence_after_sync();
-      uint32_t acc[16];
-      tmem_load_16(tmem + lane_base + 64 * b + 16 * group, acc);
+      uint32_t acc[VCOLS];
+      tmem_load_cols(tmem + lane_base + 64 * b + VCOLS * group, acc);
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&acc_empty[b]);
       const int tile = u / plan.splits;
       const int rt = tile % plan.row_tiles, pass = tile / plan.row_tiles;
       const int row = rt * TILE_ROWS + row_in_tile;
-      const int v0 = pass * TILE_VECTORS + 16 * group;
+      const int v0 = pass * TILE_VECTORS + VCOLS * group;
       if (plan.splits == 1) {
         if (row < rows) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
+          for (int i = 0; i < VCOLS; ++i)
             if (v0 + i < vectors) y[(long long)(v0 + i) * rows + row] = __uint_as_float(acc[i]);
         }
         return true;
       }
-      // A K-range: leave this warp's slice of the partial sum (32 rows x 16
+      // A K-range: leave this warp's slice of the partial sum (32 rows x VCOLS
       // vectors); the warp that brings a slice's last range adds the ranges
       // in K order. Slices are counted apart, so no warp waits for another.
       const int split = u % plan.splits;
       float* mine = scratch.partial + ((long long)tile * plan.splits + split) * TILE_VECTORS * TILE_ROWS;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) mine[(16 * group + i) * TILE_ROWS + row_in_tile] = __uint_as_float(acc[i]);
+      for (int i = 0; i < VCOLS; ++i) mine[(VCOLS * group + i) * TILE_ROWS + row_in_tile] = __uint_as_float(acc[i]);
       __threadfence();
       __syncwarp();
       int arrived = 0;
@@ -464,13 +479,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         __threadfence();
         if (row < rows) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
+          for (int i = 0; i < VCOLS; ++i) {
             float total = 0.0f;
             for (int k = 0; k < plan.splits; ++k) {
               const float* part = scratch.partial +
                                   ((long long)tile * plan.splits + k) * TILE_VECTORS * TILE_ROWS;
               total += k == split ? __uint_as_float(acc[i])
-                                  : __ldcg(part + (16 * group + i) * TILE_ROWS + row_in_tile);
+                                  : __ldcg(part + (VCOLS * group + i) * TILE_ROWS + row_in_tile);
             }
             if (v0 + i < vectors) y[(long long)(v0 + i) * rows + row] = total;
           }
@@ -487,11 +502,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           break;
         tc::fence_after_sync();
         const uint8_t* raw_row = smem + s * L::RAW_PADDED + row_in_tile * Unpack<T>::PITCH_WORDS * 4;
-        uint32_t a[32];
-        dequant_step<T>(group, raw_row, a);
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&w_empty[s]);  // the raw weights are in registers
-        tc::tmem_store_32(tmem + lane_base + 128 + 128 * (gc % 3) + 32 * group, a);
+        uint32_t a[STEPS][32];
+#pragma unroll
+        for (int st = 0; st < STEPS; ++st) {
+          dequant_step<T>(group * STEPS + st, raw_row, a[st]);
+          if (st == STEPS - 1) {
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&w_empty[s]);  // the raw weights are in registers
+          }
+          tc::tmem_store_32(tmem + lane_base + 128 + 128 * (gc % 3) + 32 * (group * STEPS + st), a[st]);
+        }
         tc::tmem_store_wait();
         tc::fence_before_sync();
         __syncwarp();
