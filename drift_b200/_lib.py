@@ -81,6 +81,9 @@ SIGNATURES = {
     "drift_linear_workspace_bytes": (_sz, [_i64, _i64]),
     "drift_device_error_take": (_i32, [ctypes.POINTER(ctypes.c_int)]),
     "drift_linear_static": (_i32, [_i32, _p, _i32, _p, _p, _i64, _i64, _i64, _p]),
+    "drift_cache_write": (_i32, [_p, _p, _i32, _i32, _i32, _p, _p, _i32, _i32, _p, _i32, _i32, _p]),
+    "drift_attention": (_i32, [_p, _i32, _i32, _p, _p, _i32, _i32, _i32, _i32, _p, _i32, _i32, _i32,
+                               _f32, _i32, _i32, _f32, _p, _p, _p]),
 }
 
 

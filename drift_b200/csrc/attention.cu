@@ -1,0 +1,358 @@
+// Ops.cacheWrite and Ops.attention for the decode step (ops/AttentionOps.scala:
+// 58-64, 113-121), over the reference's paged F16 cache (ops/KvCache.scala:
+// 12-23; element indices ops/CpuAttention.scala:163-179): keys [pages][page
+// offset][kvHeads][D], values [pages][kvHeads][D][page offset] -- a key row is
+// D contiguous halves, a value column (one d, consecutive positions) is
+// contiguous within a page.
+//
+// attention is split-K ("flash decoding"): a CTA takes one key head, the
+// query heads that share it (q_heads / kv_heads of them) and 128 consecutive
+// keys -- a thread per key for the scores, a thread per dimension for the
+// weighted values -- and leaves, per query head, the largest score, the sum
+// of exp(score - largest) and the unnormalised weighted sum. A second kernel
+// joins the splits (and the sink, if any) per query head. Scores and sums in
+// F32 (the CPU reference accumulates in Double; BASELINE's tolerance applies).
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "registry.cuh"
+
+namespace drift {
+
+int workspace_reserve(size_t bytes, void** pointer);
+
+namespace {
+
+constexpr int ATT_THREADS = 128;
+constexpr int KEYS = 128;       // keys a split takes
+constexpr int MAX_GROUP = 16;   // query heads per key head
+
+__device__ __forceinline__ int64_t key_index(const int* table, int page_size, int kv_heads, int dim,
+                                             int position, int head) {
+  const int64_t page = table[position / page_size];
+  return ((page * page_size + position % page_size) * kv_heads + head) * dim;
+}
+
+__device__ __forceinline__ int64_t value_index(const int* table, int page_size, int kv_heads,
+                                               int dim, int position, int head, int d) {
+  const int64_t page = table[position / page_size];
+  return ((page * kv_heads + head) * dim + d) * page_size + position % page_size;
+}
+
+// One F32 value of k and v per thread, rounded to F16 to nearest even (as
+// Float.floatToFloat16).
+__global__ void cache_write_kernel(const float* __restrict__ k, const float* __restrict__ v,
+                                   __half* keys, __half* values, const int* __restrict__ table,
+                                   int page_size, int kv_heads, int dim, int tokens, int start) {
+  const long long total = (long long)tokens * kv_heads * dim;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int d = int(i % dim), h = int((i / dim) % kv_heads), t = int(i / ((long long)dim * kv_heads));
+    const int position = start + t;
+    keys[key_index(table, page_size, kv_heads, dim, position, h) + d] = __float2half_rn(k[i]);
+    values[value_index(table, page_size, kv_heads, dim, position, h, d)] = __float2half_rn(v[i]);
+  }
+}
+
+struct AttentionArgs {
+  const float* q;
+  const __half* keys;
+  const __half* values;
+  const int* table;
+  float* part_o;   // [tokens][q_heads][splits][D]
+  float* part_ml;  // [tokens][q_heads][splits][2]
+  int page_size, kv_heads, q_heads, query_start, key_count, tokens, splits;
+  float scale;
+  int causal, window, has_softcap;
+  float softcap;
+};
+
+// The visible keys of the query at `position`: [lo, hi).
+__device__ __forceinline__ void visible(const AttentionArgs& a, int position, int& lo, int& hi) {
+  hi = a.key_count;
+  if (a.causal && position + 1 < hi) hi = position + 1;
+  lo = 0;
+  if (a.window > 0 && position - a.window + 1 > lo) lo = position - a.window + 1;
+}
+
+template <int D>
+__global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttentionArgs a) {
+  static_assert(D % 8 == 0 && D <= 2 * ATT_THREADS, "head width");
+  constexpr int DIMS = (D + ATT_THREADS - 1) / ATT_THREADS;  // dimensions per thread
+  __shared__ float qs[MAX_GROUP][D];
+  __shared__ float ws[MAX_GROUP][KEYS];
+  __shared__ float reduce[MAX_GROUP][ATT_THREADS / 32];
+  const int split = blockIdx.x, head = blockIdx.y, t = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
+  const int group = a.q_heads / a.kv_heads;
+  const int position = a.query_start + t;
+  int lo, hi;
+  visible(a, position, lo, hi);
+  const int k0 = split * KEYS;
+  const int first = k0 > lo ? k0 : lo, last = k0 + KEYS < hi ? k0 + KEYS : hi;  // [first, last)
+
+  for (int i = tid; i < group * D; i += ATT_THREADS)
+    qs[i / D][i % D] = a.q[((long long)t * a.q_heads + head * group + i / D) * D + i % D];
+  __syncthreads();
+
+  // scores: a thread per key
+  const int key = k0 + tid;
+  const bool seen = key >= first && key < last;
+  float score[MAX_GROUP];
+#pragma unroll
+  for (int g = 0; g < MAX_GROUP; ++g) score[g] = 0.0f;
+  if (seen) {
+    const uint4* row = reinterpret_cast<const uint4*>(
+        a.keys + key_index(a.table, a.page_size, a.kv_heads, D, key, head));
+#pragma unroll 4
+    for (int c = 0; c < D / 8; ++c) {
+      const uint4 raw = row[c];
+      const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+      float kv[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(h2[i]);
+        kv[2 * i] = f.x;
+        kv[2 * i + 1] = f.y;
+      }
+#pragma unroll
+      for (int g = 0; g < MAX_GROUP; ++g) {
+        if (g < group) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) score[g] = fmaf(qs[g][8 * c + i], kv[i], score[g]);
+        }
+      }
+    }
+  }
+  float largest[MAX_GROUP];
+#pragma unroll
+  for (int g = 0; g < MAX_GROUP; ++g) {
+    float s = score[g] * a.scale;
+    if (a.has_softcap) s = a.softcap * tanhf(s / a.softcap);
+    score[g] = seen ? s : -INFINITY;
+    float m = score[g];
+#pragma unroll
+    for (int o = 16; o > 0; o /= 2) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0 && g < group) reduce[g][warp] = m;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < MAX_GROUP; ++g) {
+    float m = -INFINITY;
+    if (g < group) {
+#pragma unroll
+      for (int w = 0; w < ATT_THREADS / 32; ++w) m = fmaxf(m, reduce[g][w]);
+    }
+    largest[g] = m;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < MAX_GROUP; ++g) {
+    const float w = seen && g < group ? expf(score[g] - largest[g]) : 0.0f;
+    if (g < group) ws[g][tid] = w;
+    float s = w;
+#pragma unroll
+    for (int o = 16; o > 0; o /= 2) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0 && g < group) reduce[g][warp] = s;
+  }
+  __syncthreads();
+
+  // weighted values: a thread per dimension (two for D = 256)
+  float acc[MAX_GROUP][DIMS];
+#pragma unroll
+  for (int g = 0; g < MAX_GROUP; ++g)
+#pragma unroll
+    for (int j = 0; j < DIMS; ++j) acc[g][j] = 0.0f;
+#pragma unroll
+  for (int j = 0; j < DIMS; ++j) {
+    const int d = tid + j * ATT_THREADS;
+    if (d >= D) continue;
+    int p = first;
+    // eight keys at a time where they share a page and start on an 8-key
+    // boundary (a 16-byte run of one value column)
+    while (p < last) {
+      if (p % 8 == 0 && p + 8 <= last && (p % a.page_size) + 8 <= a.page_size) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(
+            a.values + value_index(a.table, a.page_size, a.kv_heads, D, p, head, d));
+        const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __half22float2(h2[i]);
+#pragma unroll
+          for (int g = 0; g < MAX_GROUP; ++g) {
+            if (g < group) {
+              acc[g][j] = fmaf(ws[g][p - k0 + 2 * i], f.x, acc[g][j]);
+              acc[g][j] = fmaf(ws[g][p - k0 + 2 * i + 1], f.y, acc[g][j]);
+            }
+          }
+        }
+        p += 8;
+      } else {
+        const float f = __half2float(
+            a.values[value_index(a.table, a.page_size, a.kv_heads, D, p, head, d)]);
+#pragma unroll
+        for (int g = 0; g < MAX_GROUP; ++g)
+          if (g < group) acc[g][j] = fmaf(ws[g][p - k0], f, acc[g][j]);
+        ++p;
+      }
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < MAX_GROUP; ++g) {
+    if (g >= group) break;
+    const long long at = ((long long)t * a.q_heads + head * group + g) * a.splits + split;
+#pragma unroll
+    for (int j = 0; j < DIMS; ++j) {
+      const int d = tid + j * ATT_THREADS;
+      if (d < D) a.part_o[at * D + d] = acc[g][j];
+    }
+    if (tid == 0) {
+      float total = 0.0f;
+#pragma unroll
+      for (int w = 0; w < ATT_THREADS / 32; ++w) total += reduce[g][w];
+      a.part_ml[at * 2] = largest[g];
+      a.part_ml[at * 2 + 1] = total;
+    }
+  }
+}
+
+// Joins a query head's splits: out = sum_s o_s e^(m_s - M) / (sum_s l_s
+// e^(m_s - M) + e^(sink - M)), M the largest of the m_s and the sink.
+template <int D>
+__global__ void __launch_bounds__(ATT_THREADS) attention_join_kernel(const AttentionArgs a,
+                                                                     const float* sinks,
+                                                                     float* out) {
+  const int head = blockIdx.x, t = blockIdx.y;
+  const long long base = ((long long)t * a.q_heads + head) * a.splits;
+  float largest = -INFINITY;
+  for (int s = 0; s < a.splits; ++s)
+    if (a.part_ml[(base + s) * 2 + 1] > 0.0f) largest = fmaxf(largest, a.part_ml[(base + s) * 2]);
+  const bool sink = sinks != nullptr;
+  if (sink) largest = fmaxf(largest, sinks[head]);
+  float total = sink ? expf(sinks[head] - largest) : 0.0f;
+  for (int s = 0; s < a.splits; ++s) {
+    const float l = a.part_ml[(base + s) * 2 + 1];
+    if (l > 0.0f) total += l * expf(a.part_ml[(base + s) * 2] - largest);
+  }
+  for (int d = threadIdx.x; d < D; d += ATT_THREADS) {
+    float sum = 0.0f;
+    for (int s = 0; s < a.splits; ++s) {
+      const float l = a.part_ml[(base + s) * 2 + 1];
+      if (l > 0.0f) sum += a.part_o[(base + s) * D + d] * expf(a.part_ml[(base + s) * 2] - largest);
+    }
+    out[((long long)t * a.q_heads + head) * D + d] = total > 0.0f ? sum / total : 0.0f;
+  }
+}
+
+#define DRIFT_ATTENTION_REGISTER(D)                                                   \
+  DRIFT_REGISTER(attention_split_d##D, attention_split_kernel<D>)                     \
+  DRIFT_REGISTER(attention_join_d##D, attention_join_kernel<D>)
+DRIFT_ATTENTION_REGISTER(64)
+DRIFT_ATTENTION_REGISTER(80)
+DRIFT_ATTENTION_REGISTER(128)
+DRIFT_ATTENTION_REGISTER(256)
+DRIFT_REGISTER(cache_write_f16, cache_write_kernel)
+
+template <int D>
+int launch_attention(const AttentionArgs& a, const float* sinks, float* out, cudaStream_t stream) {
+  attention_split_kernel<D><<<dim3(a.splits, a.kv_heads, a.tokens), ATT_THREADS, 0, stream>>>(a);
+  DRIFT_LAUNCHED("attention_split");
+  attention_join_kernel<D><<<dim3(a.q_heads, a.tokens), ATT_THREADS, 0, stream>>>(a, sinks, out);
+  DRIFT_LAUNCHED("attention_join");
+  return 0;
+}
+
+int check_cache(int pages, int page_size, int kv_heads, int head_dim, const int32_t* page_table,
+                int table_pages, long long positions, const char* call) {
+  if (page_size <= 0 || page_size % 16 != 0)
+    return invalid("pages of %d tokens: not a multiple of 16", page_size);
+  if (head_dim != 64 && head_dim != 80 && head_dim != 128 && head_dim != 256)
+    return invalid("%s: heads of %d (kernels take 64, 80, 128, 256)", call, head_dim);
+  if (pages <= 0 || kv_heads <= 0) return invalid("%s: an empty cache", call);
+  if (!page_table || table_pages <= 0 || (long long)table_pages * page_size < positions)
+    return invalid("a page table of %d pages for %lld positions", table_pages, positions);
+  return 0;
+}
+
+}  // namespace
+}  // namespace drift
+
+using namespace drift;
+
+extern "C" {
+
+int drift_cache_write(const float* k, const float* v, int tokens, int kv_heads, int head_dim,
+                      void* keys, void* values, int pages, int page_size,
+                      const int32_t* page_table, int table_pages, int start,
+                      drift_stream_t stream) {
+  if (tokens < 0 || start < 0) return invalid("cacheWrite: %d tokens at %d", tokens, start);
+  DRIFT_TRY(check_cache(pages, page_size, kv_heads, head_dim, page_table, table_pages,
+                        (long long)start + tokens, "cacheWrite"));
+  if (tokens == 0) return 0;
+  if (!k || !v || !keys || !values) return invalid("cacheWrite: a null tensor");
+  if ((reinterpret_cast<uintptr_t>(keys) | reinterpret_cast<uintptr_t>(values)) & 15)
+    return invalid("cacheWrite: the cache does not start on a 16-byte boundary");
+  const long long total = (long long)tokens * kv_heads * head_dim;
+  long long grid = (total + 255) / 256;
+  if (grid > 4096) grid = 4096;
+  cache_write_kernel<<<unsigned(grid), 256, 0, cudaStream_t(stream)>>>(
+      k, v, static_cast<__half*>(keys), static_cast<__half*>(values), page_table, page_size,
+      kv_heads, head_dim, tokens, start);
+  DRIFT_LAUNCHED("cache_write");
+  return 0;
+}
+
+int drift_attention(const float* q, int tokens, int q_heads, const void* keys, const void* values,
+                    int pages, int page_size, int kv_heads, int head_dim,
+                    const int32_t* page_table, int table_pages, int query_start, int key_count,
+                    float scale, int causal, int window, float softcap, const float* sinks,
+                    float* out, drift_stream_t stream) {
+  if (tokens < 0 || q_heads <= 0) return invalid("attention: %d tokens of %d heads", tokens, q_heads);
+  DRIFT_TRY(check_cache(pages, page_size, kv_heads, head_dim, page_table, table_pages, key_count,
+                        "attention"));
+  if (q_heads % kv_heads != 0)
+    return invalid("attention: %d query heads over %d key heads", q_heads, kv_heads);
+  if (q_heads / kv_heads > MAX_GROUP)
+    return invalid("attention: %d query heads per key head (at most %d)", q_heads / kv_heads,
+                   MAX_GROUP);
+  if (query_start < 0 || key_count < 0 ||
+      (query_start + tokens > key_count && (causal || window > 0)))
+    return invalid("attention: queries at %d..%d past %d keys", query_start,
+                   query_start + tokens - 1, key_count);
+  if (tokens == 0) return 0;
+  if (!q || !keys || !values || !out) return invalid("attention: a null tensor");
+  if ((reinterpret_cast<uintptr_t>(keys) | reinterpret_cast<uintptr_t>(values)) & 15)
+    return invalid("attention: the cache does not start on a 16-byte boundary");
+  AttentionArgs a;
+  a.q = q;
+  a.keys = static_cast<const __half*>(keys);
+  a.values = static_cast<const __half*>(values);
+  a.table = page_table;
+  a.page_size = page_size;
+  a.kv_heads = kv_heads;
+  a.q_heads = q_heads;
+  a.query_start = query_start;
+  a.key_count = key_count;
+  a.tokens = tokens;
+  a.splits = key_count > 0 ? (key_count + KEYS - 1) / KEYS : 1;
+  a.scale = scale;
+  a.causal = causal;
+  a.window = window;
+  a.has_softcap = softcap > 0.0f;
+  a.softcap = softcap;
+  const size_t parts = size_t(tokens) * q_heads * a.splits;
+  void* ws = nullptr;
+  DRIFT_TRY(workspace_reserve(parts * (head_dim + 2) * sizeof(float), &ws));
+  a.part_o = static_cast<float*>(ws);
+  a.part_ml = a.part_o + parts * head_dim;
+  const cudaStream_t s = cudaStream_t(stream);
+  switch (head_dim) {
+    case 64: return launch_attention<64>(a, sinks, out, s);
+    case 80: return launch_attention<80>(a, sinks, out, s);
+    case 128: return launch_attention<128>(a, sinks, out, s);
+    default: return launch_attention<256>(a, sinks, out, s);
+  }
+}
+
+}  // extern "C"

@@ -63,6 +63,47 @@ class Rope:
 
 
 @dataclass
+class KvCache:
+    """The reference's paged F16 key/value cache (ops/KvCache.scala:12-23):
+    keys [pages, page_size, kv_heads, D], values [pages, kv_heads, D,
+    page_size]; page_size a multiple of 16."""
+    keys: torch.Tensor
+    values: torch.Tensor
+    page_size: int
+
+    @property
+    def pages(self) -> int:
+        return int(self.keys.shape[0])
+
+    @property
+    def kv_heads(self) -> int:
+        return int(self.keys.shape[2])
+
+    @property
+    def head_dim(self) -> int:
+        return int(self.keys.shape[3])
+
+    @staticmethod
+    def allocate(pages: int, page_size: int, kv_heads: int, head_dim: int,
+                 device=None) -> "KvCache":
+        device = device or torch.device("cuda")
+        return KvCache(torch.zeros(pages, page_size, kv_heads, head_dim, dtype=torch.float16,
+                                   device=device),
+                       torch.zeros(pages, kv_heads, head_dim, page_size, dtype=torch.float16,
+                                   device=device), page_size)
+
+
+@dataclass
+class Attention:
+    """An attention's parameters (ops/Attention.scala:11-17)."""
+    scale: float
+    causal: bool = True
+    window: Optional[int] = None
+    softcap: Optional[float] = None
+    sinks: Optional[torch.Tensor] = None
+
+
+@dataclass
 class RowNorm:
     """An RMS norm taken of a result as it is written (ops/RowNorm.scala:20-25)."""
     weight: torch.Tensor
@@ -268,6 +309,46 @@ class CudaOps:
                                      rope.theta, rope.rotary_dimensions, rope.layout,
                                      self._stream())
         check("drift_rope", status)
+
+    def cache_write(self, k, v, cache: KvCache, page_table, start: int) -> None:
+        """k, v [tokens, kv_heads, D] into the cache at positions start..
+        (AttentionOps.scala:58-64; checks L225-257)."""
+        _f32("cacheWrite", k, v)
+        _require(k.shape == v.shape and k.dim() == 3 and
+                 tuple(k.shape[1:]) == (cache.kv_heads, cache.head_dim),
+                 f"cacheWrite: {list(k.shape)} into a cache of {cache.kv_heads} heads of "
+                 f"{cache.head_dim}")
+        _require(page_table.dtype == torch.int32 and page_table.dim() == 1,
+                 f"a page table is I32 [pages], not {page_table.dtype} {list(page_table.shape)}")
+        status = self.lib.drift_cache_write(
+            _ptr(k), _ptr(v), int(k.shape[0]), cache.kv_heads, cache.head_dim, _ptr(cache.keys),
+            _ptr(cache.values), cache.pages, cache.page_size, _ptr(page_table),
+            int(page_table.numel()), start, self._stream())
+        check("drift_cache_write", status)
+
+    def attention(self, q, cache: KvCache, page_table, query_start: int, key_count: int,
+                  attention: Attention, out) -> None:
+        """Attention of q [tokens, q_heads, D] over the cache's first key_count
+        positions (AttentionOps.scala:113-121; checks L259-294)."""
+        _f32("attention", q, out)
+        _same_shape("attention", q, out)
+        _require(q.dim() == 3 and q.shape[2] == cache.head_dim,
+                 f"attention: queries {list(q.shape)} against heads of {cache.head_dim}")
+        _require(page_table.dtype == torch.int32 and page_table.dim() == 1,
+                 f"a page table is I32 [pages], not {page_table.dtype} {list(page_table.shape)}")
+        tokens, q_heads, _ = q.shape
+        sinks = attention.sinks
+        if sinks is not None:
+            _f32("attention sinks", sinks)
+            _require(tuple(sinks.shape) == (q_heads,),
+                     f"attention: sinks {list(sinks.shape)} for {q_heads} heads")
+        status = self.lib.drift_attention(
+            _ptr(q), tokens, q_heads, _ptr(cache.keys), _ptr(cache.values), cache.pages,
+            cache.page_size, cache.kv_heads, cache.head_dim, _ptr(page_table),
+            int(page_table.numel()), query_start, key_count, attention.scale,
+            int(attention.causal), int(attention.window or 0), float(attention.softcap or 0.0),
+            _ptr(sinks), _ptr(out), self._stream())
+        check("drift_attention", status)
 
     # -- ExpertsOps (ops/ExpertsOps.scala) -------------------------------------------------------------
     def route(self, logits, ids, weights) -> None:

@@ -137,6 +137,32 @@ int drift_moe_combine_norm(const float* expert_out, const float* weights, int64_
                            const float* norm_weight, float epsilon, float weight_offset,
                            float* normed, drift_stream_t stream);
 
+/* Ops.cacheWrite (ops/AttentionOps.scala:58-64; CPU ops/CpuAttention.scala:
+ * 181-210): k, v [tokens, kv_heads, head_dim] F32, rounded to F16 (nearest
+ * even), into the paged cache at positions start.. . The cache is the
+ * reference's KvCache (ops/KvCache.scala:12-23): keys [pages][page_size]
+ * [kv_heads][head_dim] and values [pages][kv_heads][head_dim][page_size], F16,
+ * page_size a multiple of 16; page_table I32 [table_pages] maps position /
+ * page_size to a page. Cache pointers 16-byte aligned. */
+int drift_cache_write(const float* k, const float* v, int tokens, int kv_heads, int head_dim,
+                      void* keys, void* values, int pages, int page_size,
+                      const int32_t* page_table, int table_pages, int start,
+                      drift_stream_t stream);
+
+/* Ops.attention (ops/AttentionOps.scala:113-121; CPU ops/CpuAttention.scala:
+ * 215-288): for each token t and query head h, softmax over the visible keys
+ * (key < key_count; key <= query_start + t when causal; key > query_start +
+ * t - window when window > 0) of scale * q . k (softcapped as softcap *
+ * tanh(score / softcap) when softcap > 0; sinks F32 [q_heads] or NULL join the
+ * softmax's denominator), times the values. q and out F32 [tokens, q_heads,
+ * head_dim]; head_dim 64, 80, 128 or 256; q_heads a multiple of kv_heads, at
+ * most 16 query heads per key head. */
+int drift_attention(const float* q, int tokens, int q_heads, const void* keys, const void* values,
+                    int pages, int page_size, int kv_heads, int head_dim,
+                    const int32_t* page_table, int table_pages, int query_start, int key_count,
+                    float scale, int causal, int window, float softcap, const float* sinks,
+                    float* out, drift_stream_t stream);
+
 /* The library keeps one grow-only scratch buffer per device for the products'
  * prepared x (as the runner's HIP backend keeps grow-only scratch,
  * ops/HipBase.scala:341-351). Reserving it ahead keeps allocation out of a

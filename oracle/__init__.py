@@ -53,6 +53,10 @@ def lib() -> ctypes.CDLL:
         p, i64, i32, f32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float
         sigs = {
             "oracle_f16_to_f32": (f32, [ctypes.c_uint16]),
+            "oracle_f32_to_f16": (ctypes.c_uint16, [f32]),
+            "oracle_cache_write": (None, [p, p, i32, i32, i32, p, p, i32, p, i32]),
+            "oracle_attention": (None, [p, i32, i32, p, p, i32, i32, i32, p, i32, i32, f32, i32, i32,
+                                        i32, f32, p, p]),
             "oracle_f32_to_bf16": (ctypes.c_uint16, [f32]),
             "oracle_decode": (i32, [i32, p, i64, p]),
             "oracle_linear": (i32, [i32, p, p, p, i64, i64, i64]),
@@ -276,3 +280,44 @@ def moe_combine_norm(expert_out, weights, hidden: int, residual, norm_weight, ep
                                   _p(si), _p(sr), _p(residual), _p(_f32(norm_weight)), epsilon,
                                   weight_offset, _p(normed))
     return residual, normed
+
+
+def f32_to_f16(values) -> np.ndarray:
+    """Float.floatToFloat16 (round to nearest even) of each value, as bits."""
+    flat = _f32(values).reshape(-1)
+    out = np.empty(flat.size, dtype=np.uint16)
+    fn = lib().oracle_f32_to_f16
+    for i, v in enumerate(flat):
+        out[i] = fn(float(v))
+    return out.reshape(np.shape(values))
+
+
+def cache_write(k, v, keys: np.ndarray, values: np.ndarray, page_size: int, page_table,
+                start: int) -> None:
+    """CpuAttention.cacheWrite: k, v [tokens, kvHeads, D] into the F16 cache
+    (uint16 bits; keys [pages, page, kvHeads, D], values [pages, kvHeads, D,
+    page]) in place."""
+    k, v = _f32(k), _f32(v)
+    tokens, kv_heads, dim = k.shape
+    table = np.ascontiguousarray(page_table, dtype=np.int32)
+    assert keys.dtype == np.uint16 and values.dtype == np.uint16
+    assert keys.flags.c_contiguous and values.flags.c_contiguous
+    lib().oracle_cache_write(_p(k), _p(v), tokens, kv_heads, dim, _p(keys), _p(values), page_size,
+                             _p(table), start)
+
+
+def attention(q, keys: np.ndarray, values: np.ndarray, page_size: int, kv_heads: int,
+              page_table, query_start: int, key_count: int, scale: float, causal: bool = True,
+              window: int = 0, softcap: float | None = None, sinks=None) -> np.ndarray:
+    """CpuAttention.attention: q [tokens, qHeads, D] F32 over the F16 cache."""
+    q = _f32(q)
+    tokens, q_heads, dim = q.shape
+    table = np.ascontiguousarray(page_table, dtype=np.int32)
+    keys = np.ascontiguousarray(keys, dtype=np.uint16)
+    values = np.ascontiguousarray(values, dtype=np.uint16)
+    sinks_arr = None if sinks is None else _f32(sinks)
+    out = np.empty_like(q)
+    lib().oracle_attention(_p(q), tokens, q_heads, _p(keys), _p(values), page_size, kv_heads, dim,
+                           _p(table), query_start, key_count, scale, int(causal), window,
+                           int(softcap is not None), float(softcap or 0.0), _p(sinks_arr), _p(out))
+    return out

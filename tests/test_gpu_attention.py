@@ -1,0 +1,115 @@
+"""Ops.cacheWrite and Ops.attention on the GPU against the oracle (the
+reference's CpuAttention.cacheWrite/attention, ops/CpuAttention.scala:
+181-288), over the reference's paged F16 cache layout.
+
+cacheWrite is bit-exact (F32 to F16, nearest even). attention is held to
+BASELINE's 1e-4 absolute + 1e-3 relative: the GPU sums in F32 where the CPU
+sums in Double.
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from drift_b200.ops import Attention, CudaOps, KvCache
+from tests.conftest import within
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ops():
+    return CudaOps()
+
+
+def filled_cache(rng, pages, page_size, kv_heads, dim, positions, table):
+    """A cache whose first `positions` positions hold N(0, 1) keys and values,
+    written by the oracle (numpy copies) and uploaded."""
+    keys = np.zeros((pages, page_size, kv_heads, dim), dtype=np.uint16)
+    values = np.zeros((pages, kv_heads, dim, page_size), dtype=np.uint16)
+    k = rng.standard_normal((positions, kv_heads, dim)).astype(np.float32)
+    v = rng.standard_normal((positions, kv_heads, dim)).astype(np.float32)
+    oracle.cache_write(k, v, keys, values, page_size, table, 0)
+    cache = KvCache(torch.from_numpy(keys.view(np.float16)).cuda(),
+                    torch.from_numpy(values.view(np.float16)).cuda(), page_size)
+    return keys, values, cache
+
+
+@pytest.mark.parametrize("tokens,start,page_size,dim", [(1, 0, 16, 128), (1, 37, 16, 128),
+                                                         (5, 30, 32, 64), (3, 100, 16, 256)])
+def test_cache_write_is_bit_exact(ops, tokens, start, page_size, dim):
+    rng = np.random.default_rng(tokens + start)
+    kv_heads, pages = 4, 16
+    table = rng.permutation(pages).astype(np.int32)
+    keys = np.zeros((pages, page_size, kv_heads, dim), dtype=np.uint16)
+    values = np.zeros((pages, kv_heads, dim, page_size), dtype=np.uint16)
+    k = (rng.standard_normal((tokens, kv_heads, dim)) * 10).astype(np.float32)
+    v = (rng.standard_normal((tokens, kv_heads, dim)) * 1e-3).astype(np.float32)
+    cache = KvCache(torch.zeros(pages, page_size, kv_heads, dim, dtype=torch.float16).cuda(),
+                    torch.zeros(pages, kv_heads, dim, page_size, dtype=torch.float16).cuda(),
+                    page_size)
+    ops.cache_write(torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda(), cache,
+                    torch.from_numpy(table).cuda(), start)
+    oracle.cache_write(k, v, keys, values, page_size, table, start)
+    np.testing.assert_array_equal(cache.keys.cpu().numpy().view(np.uint16), keys)
+    np.testing.assert_array_equal(cache.values.cpu().numpy().view(np.uint16), values)
+
+
+# (tokens, q_heads, kv_heads, dim, keys, page_size, causal, window, softcap, sinks)
+CASES = [
+    (1, 32, 8, 128, 1, 16, True, 0, None, False),       # first decode step
+    (1, 32, 8, 128, 17, 16, True, 0, None, False),      # a partial page
+    (1, 32, 8, 128, 300, 16, True, 0, None, False),     # several splits
+    (1, 32, 8, 128, 4096, 16, True, 0, None, False),    # C4's context
+    (1, 16, 2, 256, 1000, 32, True, 0, None, False),    # C5's full attention (group 8)
+    (1, 8, 8, 64, 129, 16, True, 0, None, False),
+    (1, 10, 2, 80, 200, 16, True, 0, None, False),      # the 80-wide kernel
+    (7, 32, 8, 128, 250, 16, True, 0, None, False),     # a prefill chunk, causal
+    (4, 8, 2, 128, 300, 16, True, 64, None, False),     # sliding window
+    (2, 8, 2, 128, 150, 16, True, 0, 30.0, True),       # softcap and sinks
+    (3, 8, 4, 64, 40, 16, False, 0, None, False),       # not causal
+]
+
+
+@pytest.mark.parametrize("case", CASES, ids=[f"t{c[0]}h{c[1]}/{c[2]}d{c[3]}k{c[4]}" for c in CASES])
+def test_attention_matches_the_oracle(ops, case):
+    tokens, q_heads, kv_heads, dim, key_count, page_size, causal, window, softcap, sinks = case
+    rng = np.random.default_rng(key_count * 7 + dim)
+    table_pages = (key_count + page_size - 1) // page_size + 1
+    pages = table_pages + 3
+    table = rng.permutation(pages)[:table_pages].astype(np.int32)
+    keys, values, cache = filled_cache(rng, pages, page_size, kv_heads, dim, key_count, table)
+    q = rng.standard_normal((tokens, q_heads, dim)).astype(np.float32)
+    sink_values = rng.standard_normal(q_heads).astype(np.float32) if sinks else None
+    query_start = key_count - tokens if causal else 0
+    scale = 1.0 / math.sqrt(dim)
+    expected = oracle.attention(q, keys, values, page_size, kv_heads, table, query_start,
+                                key_count, scale, causal, window, softcap, sink_values)
+    out = torch.empty(tokens, q_heads, dim, device="cuda")
+    ops.attention(torch.from_numpy(q).cuda(), cache, torch.from_numpy(table).cuda(), query_start,
+                  key_count,
+                  Attention(scale, causal, window or None, softcap,
+                            None if sink_values is None else torch.from_numpy(sink_values).cuda()),
+                  out)
+    ok, _, _, summary = within(out.cpu().numpy(), expected, 1e-4, 1e-3)
+    assert ok, summary
+
+
+def test_attention_refuses_what_the_reference_refuses(ops):
+    cache = KvCache.allocate(4, 16, 2, 128)
+    table = torch.arange(4, dtype=torch.int32, device="cuda")
+    q = torch.zeros(1, 6, 128, device="cuda")
+    out = torch.empty_like(q)
+    with pytest.raises(ValueError, match="query heads over"):
+        ops.attention(q[:, :5], cache, table, 0, 1, Attention(1.0), out[:, :5])
+    with pytest.raises(ValueError, match="past"):
+        ops.attention(q, cache, table, 10, 5, Attention(1.0), out)
+    with pytest.raises(ValueError, match="page table"):
+        ops.attention(q, cache, table[:1], 0, 40, Attention(1.0), out)
+    bad = KvCache(torch.zeros(4, 8, 2, 128, dtype=torch.float16, device="cuda"),
+                  torch.zeros(4, 2, 128, 8, dtype=torch.float16, device="cuda"), 8)
+    with pytest.raises(ValueError, match="multiple of 16"):
+        ops.attention(q, bad, table, 0, 1, Attention(1.0), out)
