@@ -255,6 +255,13 @@ def run_gpu(args) -> dict | None:
 
     # the dominant kernel alone: the lm-head product at batch 1, replayed
     dominant = dominant_kernel(ops, weights, xs, ys, stream)
+    sweep = sweep_table(ops, weights, xs, ys, stream) if rank == 0 else None
+    del weights, xs, ys, host_x, host_y
+    torch.cuda.empty_cache()
+
+    # BASELINE C4: the dense decoder's decode step, tensor-parallel over the
+    # job's GPUs (one NCCL group), tok/s at each batch
+    decode = run_decode(args, ops, rank, world, stream) if args.decode else None
 
     times = torch.tensor([elapsed_ms, e2e_ms], device="cuda")
     if world > 1:
@@ -309,11 +316,68 @@ def run_gpu(args) -> dict | None:
             "launch_us": round(dominant["us"], 3),
         },
         "clocks": clock_info,
-        "sweep": sweep_table(ops, weights, xs, ys, stream),
+        "sweep": sweep,
+        "decode": decode,
     }
     if args.cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(seconds=args.cpu_seconds)
     return result
+
+
+DECODE_CONTEXT = 4096
+
+
+def run_decode(args, ops, rank: int, world: int, stream) -> dict:
+    """Decode tok/s of BASELINE C4 (36 layers, hidden 4096, 32 q / 8 kv heads
+    of 128, FFN 12288, vocabulary 151936; random-init Q4_1 weights, Q8_0
+    embedding; F16 KV caches prefilled with N(0, 1) to 4095 positions): one
+    step at position 4095 (4096 keys) captured as a CUDA graph, replayed,
+    timed with CUDA events, the slowest rank's time."""
+    import torch
+    import torch.distributed as dist
+
+    from drift_b200.decoder import DenseConfig, DenseDecoder, DenseWeights
+    from drift_b200.tensor_parallel import max_over_ranks
+
+    config = DenseConfig()
+    group = dist.group.WORLD if world > 1 else None
+    weights = DenseWeights.random(config, rank=rank, world=world)
+    peaks = measured_peaks()
+    out = {"config": "C4 dense decode, TP over the job's GPUs", "tp": world,
+           "context": DECODE_CONTEXT, "weights": "random-init Q4_1 (C2 law), Q8_0 embedding",
+           "kv_cache": "F16 paged (the reference's KvCache), prefilled N(0,1)"}
+    steps = max(5, min(args.steps, 30))
+    for batch in args.decode_batches:
+        decoder = DenseDecoder(ops, config, weights, batch, DECODE_CONTEXT, group=group)
+        decoder.prefill_random(DECODE_CONTEXT - 1)
+        decoder.capture([DECODE_CONTEXT - 1] * batch, stream)
+        for _ in range(3):
+            decoder.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(steps):
+                decoder.replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+        ms = max_over_ranks(start.elapsed_time(end) / steps, device="cuda")
+        kv_bytes = (2 * config.layers * (config.kv_heads // world) * config.head_dim * 2
+                    * DECODE_CONTEXT * batch)
+        per_rank = weights.nbytes() + kv_bytes
+        out[f"b{batch}"] = {
+            "tok_s": round(batch / (ms / 1e3), 1),
+            "ms_per_step": round(ms, 4),
+            "bytes_per_step_per_gpu": per_rank,
+            "fraction_of_measured_hbm": round(per_rank / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
+            "steps": steps,
+        }
+        decoder.release()
+        del decoder
+        torch.cuda.empty_cache()
+    return out
 
 
 def profiled_traffic() -> int | None:
@@ -528,11 +592,15 @@ def main() -> int:
     parser.add_argument("--impl", default="drift_b200")
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    parser.add_argument("--no-decode", dest="decode", action="store_false",
+                        help="skip the C4 decode tok/s measurement")
+    parser.add_argument("--decode-batches", default="1,16")
     parser.add_argument("--case", help="B,N,K: run one product --repeat times (profiling)")
     parser.add_argument("--case-dtype", type=int, default=Q4_1)
     parser.add_argument("--repeat", type=int, default=3)
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)
+    args.decode_batches = [int(b) for b in str(args.decode_batches).split(",") if b]
     if args.case:
         run_case(args.case, args.repeat, args.case_dtype)
         return 0

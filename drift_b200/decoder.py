@@ -1,0 +1,252 @@
+"""The dense decoder's decode step on this library's ops: the op order of the
+runner's DenseDecoder.run (runner/src/drift/runner/models/DenseDecoder.scala:
+778-939), for a batch of sequences, on one GPU or tensor-parallel across the
+GPUs of one box (drift_b200/tensor_parallel.py).
+
+Per token and layer: RMSNorm; q, k, v products (one x preparation); per-head
+q/k RMSNorm (Qwen3); RoPE of q and k; the new k, v into each sequence's paged
+F16 cache; attention over the cache; o product; residual add + RMSNorm; gate
+and up products; SwiGLU; down product; residual add. Then the final RMSNorm
+and the lm-head product. With tensor parallelism a rank holds its share of
+the query and key heads and of the FFN rows (column-split q/k/v/gate/up),
+the matching columns of o and down (row-split, one all-reduce each), and its
+share of the vocabulary rows of the lm-head; the embedding and the norms are
+replicated.
+
+This is the harness BASELINE's decode tok/s is measured on: weights are
+random-init (the benchmark laws), the caches prefilled with N(0, 1) keys and
+values; a step is captured once as a CUDA graph and replayed.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Optional
+
+import numpy as np
+import torch
+
+from . import synthetic
+from ._lib import Q4_1, Q8_0
+from .ops import SILU, Attention, CudaOps, KvCache, Rope, RowNorm, Stored
+from .tensor_parallel import row_range
+
+
+@dataclass(frozen=True)
+class DenseConfig:
+    """A dense decoder's shape (BASELINE C4: Qwen3-8B-like)."""
+    layers: int = 36
+    hidden: int = 4096
+    q_heads: int = 32
+    kv_heads: int = 8
+    head_dim: int = 128
+    ffn: int = 12288
+    vocab: int = 151936
+    epsilon: float = 1e-6
+    theta: float = 1e6
+    qk_norm: bool = True
+    page_size: int = 16
+
+
+@dataclass
+class DenseLayer:
+    attention_norm: torch.Tensor
+    q: Stored
+    k: Stored
+    v: Stored
+    q_norm: Optional[torch.Tensor]
+    k_norm: Optional[torch.Tensor]
+    o: Stored
+    mlp_norm: torch.Tensor
+    gate: Stored
+    up: Stored
+    down: Stored
+
+
+@dataclass
+class DenseWeights:
+    """One rank's weights: its heads and FFN rows of the column-split
+    products, the matching columns of o and down, its vocabulary rows of the
+    lm-head; the embedding and norms whole."""
+    embedding: Stored
+    layers: list
+    final_norm: torch.Tensor
+    lm_head: Stored
+    rank: int = 0
+    world: int = 1
+
+    @staticmethod
+    def random(config: DenseConfig, dtype: int = Q4_1, embedding_dtype: int = Q8_0,
+               seed: int = 0, rank: int = 0, world: int = 1) -> "DenseWeights":
+        """Random-init weights by the benchmark laws, drawn on the device: this
+        rank's shards only (different ranks draw different numbers -- a
+        timing harness, not a model)."""
+        c = config
+        g = torch.Generator(device="cuda")
+        g.manual_seed(seed * 1000 + rank)
+        q_heads, kv_heads = c.q_heads // world, c.kv_heads // world
+        ffn = row_range(c.ffn, rank, world)
+        ffn_rows = ffn[1] - ffn[0]
+        vocab = row_range(c.vocab, rank, world)
+
+        def stored(t, n, k):
+            return Stored(t, (n, k), synthetic.quantized_device(t, n, k, g))
+
+        def norm(width):
+            return 1.0 + 0.02 * torch.randn(width, generator=g, device="cuda")
+
+        layers = []
+        for _ in range(c.layers):
+            layers.append(DenseLayer(
+                attention_norm=norm(c.hidden),
+                q=stored(dtype, q_heads * c.head_dim, c.hidden),
+                k=stored(dtype, kv_heads * c.head_dim, c.hidden),
+                v=stored(dtype, kv_heads * c.head_dim, c.hidden),
+                q_norm=norm(c.head_dim) if c.qk_norm else None,
+                k_norm=norm(c.head_dim) if c.qk_norm else None,
+                o=stored(dtype, c.hidden, q_heads * c.head_dim),
+                mlp_norm=norm(c.hidden),
+                gate=stored(dtype, ffn_rows, c.hidden),
+                up=stored(dtype, ffn_rows, c.hidden),
+                down=stored(dtype, c.hidden, ffn_rows)))
+        return DenseWeights(stored(embedding_dtype, c.vocab, c.hidden), layers, norm(c.hidden),
+                            stored(dtype, vocab[1] - vocab[0], c.hidden), rank, world)
+
+    def nbytes(self) -> int:
+        """Bytes of weights one decode step streams on this rank (all but the
+        embedding, of which a step reads only the batch's rows)."""
+        total = self.final_norm.numel() * 4 + self.lm_head.data.numel()
+        for layer in self.layers:
+            for w in (layer.q, layer.k, layer.v, layer.o, layer.gate, layer.up, layer.down):
+                total += w.data.numel()
+            total += (layer.attention_norm.numel() + layer.mlp_norm.numel()) * 4
+        return total
+
+
+class DenseDecoder:
+    """Decode steps for `batch` sequences of up to `context` positions each,
+    on this rank's weights. `group`: the tensor-parallel process group (NCCL),
+    or None for one GPU."""
+
+    def __init__(self, ops: CudaOps, config: DenseConfig, weights: DenseWeights, batch: int,
+                 context: int, group=None):
+        c = self.config = config
+        self.ops, self.weights, self.batch, self.context, self.group = ops, weights, batch, context, group
+        world = weights.world
+        self.q_heads, self.kv_heads = c.q_heads // world, c.kv_heads // world
+        self.ffn = weights.layers[0].gate.shape[0] if weights.layers else 0
+        self.vocab_rows = weights.lm_head.shape[0]
+        pages_per_sequence = (context + c.page_size - 1) // c.page_size
+        self.pages_per_sequence = pages_per_sequence
+        pages = pages_per_sequence * batch
+        self.caches = [KvCache.allocate(pages, c.page_size, self.kv_heads, c.head_dim)
+                       for _ in weights.layers]
+        self.tables = [torch.arange(i * pages_per_sequence, (i + 1) * pages_per_sequence,
+                                    dtype=torch.int32, device="cuda") for i in range(batch)]
+        self.rope = Rope(c.theta, c.head_dim)
+        self.attention = Attention(1.0 / math.sqrt(c.head_dim))
+        b, hd = batch, c.head_dim
+        f32 = dict(dtype=torch.float32, device="cuda")
+        self.ids = torch.zeros(b, dtype=torch.int32, device="cuda")
+        self.positions = torch.zeros(b, dtype=torch.int32, device="cuda")
+        self.x = torch.zeros(b, c.hidden, **f32)
+        self.normed = torch.zeros(b, c.hidden, **f32)
+        self.q = torch.zeros(b, self.q_heads * hd, **f32)
+        self.k = torch.zeros(b, self.kv_heads * hd, **f32)
+        self.v = torch.zeros(b, self.kv_heads * hd, **f32)
+        self.q_turned = torch.zeros(b, self.q_heads, hd, **f32)
+        self.k_turned = torch.zeros(b, self.kv_heads, hd, **f32)
+        self.attended = torch.zeros(b, self.q_heads, hd, **f32)
+        self.projected = torch.zeros(b, c.hidden, **f32)
+        self.gate = torch.zeros(b, self.ffn, **f32)
+        self.up = torch.zeros(b, self.ffn, **f32)
+        self.logits = torch.zeros(b, self.vocab_rows, **f32)
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self._positions_host: list[int] = [0] * b
+
+    def prefill_random(self, positions: int, seed: int = 1) -> None:
+        """Every sequence's cache holds `positions` positions of N(0, 1) keys
+        and values (BASELINE C4's prefilled cache), as F16."""
+        g = torch.Generator(device="cuda")
+        g.manual_seed(seed)
+        used = (positions + self.config.page_size - 1) // self.config.page_size
+        for cache in self.caches:
+            for i in range(self.batch):
+                pages = slice(i * self.pages_per_sequence, i * self.pages_per_sequence + used)
+                cache.keys[pages].normal_(generator=g)
+                cache.values[pages].normal_(generator=g)
+
+    def _all_reduce(self, t: torch.Tensor) -> None:
+        if self.group is not None:
+            torch.distributed.all_reduce(t, group=self.group)
+
+    def step(self, positions: list[int]) -> torch.Tensor:
+        """One decode step: self.ids at `positions` (one per sequence, written
+        to self.positions by the caller or here) -> self.logits [batch, this
+        rank's vocabulary rows]."""
+        ops, c, w = self.ops, self.config, self.weights
+        b, hd = self.batch, c.head_dim
+        ops.embedding(w.embedding, self.ids, self.x)
+        ops.rms_norm(self.x, w.layers[0].attention_norm, c.epsilon, 0.0, self.normed)
+        for index, (layer, cache) in enumerate(zip(w.layers, self.caches)):
+            ops.linears(self.normed, [layer.q, layer.k, layer.v], [self.q, self.k, self.v])
+            q = self.q.view(b, self.q_heads, hd)
+            k = self.k.view(b, self.kv_heads, hd)
+            if c.qk_norm:
+                ops.rms_norm(q, layer.q_norm, c.epsilon, 0.0, q)
+                ops.rms_norm(k, layer.k_norm, c.epsilon, 0.0, k)
+            ops.rope(q, self.positions, self.rope, self.q_turned)
+            ops.rope(k, self.positions, self.rope, self.k_turned)
+            v = self.v.view(b, self.kv_heads, hd)
+            for i in range(b):
+                p = positions[i]
+                ops.cache_write(self.k_turned[i:i + 1], v[i:i + 1], cache, self.tables[i], p)
+                ops.attention(self.q_turned[i:i + 1], cache, self.tables[i], p, p + 1,
+                              self.attention, self.attended[i:i + 1])
+            ops.linear(self.attended.view(b, self.q_heads * hd), layer.o, self.projected)
+            self._all_reduce(self.projected)
+            ops.add_rms_norm(self.x, self.projected,
+                             RowNorm(layer.mlp_norm, c.epsilon, 0.0, self.normed))
+            ops.linears(self.normed, [layer.gate, layer.up], [self.gate, self.up])
+            ops.gated(SILU, self.gate, self.up, self.gate)
+            ops.linear(self.gate, layer.down, self.projected)
+            self._all_reduce(self.projected)
+            following = w.layers[index + 1].attention_norm if index + 1 < len(w.layers) else w.final_norm
+            ops.add_rms_norm(self.x, self.projected, RowNorm(following, c.epsilon, 0.0, self.normed))
+        ops.linear(self.normed, w.lm_head, self.logits)
+        return self.logits
+
+    def reserve(self) -> None:
+        """Sizes the library's scratch for every product and attention of a
+        step, so a capture allocates nothing."""
+        c = self.config
+        widest = max(c.hidden, self.q_heads * c.head_dim, self.ffn)
+        self.ops.reserve_workspace(self.batch, widest)
+        splits = (self.context + 127) // 128
+        attention_bytes = self.q_heads * splits * (c.head_dim + 2) * 4
+        lib = self.ops.lib
+        from ._lib import check
+        check("drift_workspace_reserve", lib.drift_workspace_reserve(
+            max(attention_bytes, lib.drift_linear_workspace_bytes(self.batch, widest))))
+
+    def capture(self, positions: list[int], stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Records one step at `positions` as a CUDA graph (replayed by
+        `replay`): the positions are fixed in the graph's launches."""
+        self.positions.copy_(torch.tensor(positions, dtype=torch.int32))
+        self.reserve()
+        stream = stream or torch.cuda.Stream()
+        with torch.cuda.stream(stream):
+            self.step(positions)  # first calls resolve lazy state outside the capture
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=stream):
+            self.step(positions)
+        torch.cuda.synchronize()
+
+    def replay(self) -> None:
+        self.graph.replay()
+
+    def release(self) -> None:
+        """Drops the graph (it must go before an NCCL group is destroyed)."""
+        self.graph = None

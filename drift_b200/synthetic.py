@@ -71,3 +71,32 @@ def bf16_bits(values: np.ndarray) -> np.ndarray:
 def bf16_values(bits: np.ndarray) -> np.ndarray:
     """BF16 bits widened exactly to F32."""
     return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def quantized_device(dtype: int, n: int, k: int, generator=None, device=None):
+    """The `quantized` law drawn on the device (torch): for model-sized
+    random-init weights, where drawing gigabytes on the host would dominate a
+    run. Not the same bytes as `quantized` for a seed."""
+    import torch
+
+    device = device or torch.device("cuda")
+    blocks = n * (k // 32)
+    size = BLOCK_BYTES[dtype]
+    out = torch.empty(blocks, size, dtype=torch.uint8, device=device)
+    d = (torch.rand(blocks, generator=generator, device=device) * 0.018 + 0.002).half()
+    out[:, 0:2] = d.view(torch.uint8).view(blocks, 2)
+    if dtype == Q8_0:
+        codes = torch.randint(-127, 128, (blocks, 32), generator=generator, device=device,
+                              dtype=torch.int16).to(torch.int8)
+        out[:, 2:34] = codes.view(torch.uint8)
+    elif dtype == Q4_1:
+        m = (-8.0 * d.float()).half()
+        out[:, 2:4] = m.view(torch.uint8).view(blocks, 2)
+        out[:, 4:20] = torch.randint(0, 256, (blocks, 16), generator=generator, device=device,
+                                     dtype=torch.uint8)
+    elif dtype == Q4_0:
+        out[:, 2:18] = torch.randint(0, 256, (blocks, 16), generator=generator, device=device,
+                                     dtype=torch.uint8)
+    else:
+        raise ValueError(f"no synthetic law for type {dtype}")
+    return out.reshape(-1)
