@@ -584,6 +584,26 @@ def run_case(spec: str, repeat: int, dtype: int = Q4_1) -> None:
     print(f"case {b}x{n}x{k} dtype {dtype}: {repeat} products, y[0,:4] = {y[0, :4].tolist()}")
 
 
+def run_decode_case(batch: int, layers: int, steps: int) -> None:
+    """`--decode-case B`: eager decode steps of C4 (with `--decode-layers`
+    layers), nothing timed -- the workload of a launch-list capture."""
+    import torch
+
+    from drift_b200.decoder import DenseConfig, DenseDecoder, DenseWeights
+    from drift_b200.ops import CudaOps
+
+    config = DenseConfig(layers=layers)
+    ops = CudaOps(0)
+    decoder = DenseDecoder(ops, config, DenseWeights.random(config), batch, DECODE_CONTEXT)
+    decoder.prefill_random(DECODE_CONTEXT - 1)
+    positions = [DECODE_CONTEXT - 1] * batch
+    decoder.positions.copy_(torch.tensor(positions, dtype=torch.int32))
+    for _ in range(steps):
+        decoder.step(positions)
+    torch.cuda.synchronize()
+    print(f"decode case: batch {batch}, {layers} layers, {steps} steps")
+
+
 def main() -> int:
     parser = argparse.ArgumentParser()
     parser.add_argument("--gpus", type=int, default=1)
@@ -595,12 +615,17 @@ def main() -> int:
     parser.add_argument("--no-decode", dest="decode", action="store_false",
                         help="skip the C4 decode tok/s measurement")
     parser.add_argument("--decode-batches", default="1,16")
+    parser.add_argument("--decode-case", type=int, help="B: eager C4 decode steps (profiling)")
+    parser.add_argument("--decode-layers", type=int, default=36)
     parser.add_argument("--case", help="B,N,K: run one product --repeat times (profiling)")
     parser.add_argument("--case-dtype", type=int, default=Q4_1)
     parser.add_argument("--repeat", type=int, default=3)
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)
     args.decode_batches = [int(b) for b in str(args.decode_batches).split(",") if b]
+    if args.decode_case:
+        run_decode_case(args.decode_case, args.decode_layers, args.repeat)
+        return 0
     if args.case:
         run_case(args.case, args.repeat, args.case_dtype)
         return 0

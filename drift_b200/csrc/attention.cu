@@ -26,7 +26,7 @@ namespace {
 
 constexpr int ATT_THREADS = 128;
 constexpr int KEYS = 128;       // keys a split takes
-constexpr int MAX_GROUP = 16;   // query heads per key head
+constexpr int MAX_GROUP = 16;   // query heads per key head, at most
 
 __device__ __forceinline__ int64_t key_index(const int* table, int page_size, int kv_heads, int dim,
                                              int position, int head) {
@@ -76,51 +76,72 @@ __device__ __forceinline__ void visible(const AttentionArgs& a, int position, in
   if (a.window > 0 && position - a.window + 1 > lo) lo = position - a.window + 1;
 }
 
-template <int D>
+// G: query heads per key head, a template so that the unrolled loops hold
+// exactly the heads there are (a kernel unrolled for 16 heads but running 4
+// spends its time waiting on the instruction cache).
+template <int D, int G>
 __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttentionArgs a) {
   static_assert(D % 8 == 0 && D <= 2 * ATT_THREADS, "head width");
   constexpr int DIMS = (D + ATT_THREADS - 1) / ATT_THREADS;  // dimensions per thread
+  constexpr int MAX_GROUP = G;
   __shared__ float qs[MAX_GROUP][D];
   __shared__ float ws[MAX_GROUP][KEYS];
   __shared__ float reduce[MAX_GROUP][ATT_THREADS / 32];
   const int split = blockIdx.x, head = blockIdx.y, t = blockIdx.z;
   const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
-  const int group = a.q_heads / a.kv_heads;
+  const int group = a.q_heads / a.kv_heads;  // <= G
   const int position = a.query_start + t;
   int lo, hi;
   visible(a, position, lo, hi);
   const int k0 = split * KEYS;
   const int first = k0 > lo ? k0 : lo, last = k0 + KEYS < hi ? k0 + KEYS : hi;  // [first, last)
 
+  // the chunk's pages, looked up once
+  __shared__ int pages[KEYS / 16 + 2];
+  const int page0 = k0 / a.page_size;
+  if (tid < KEYS / 16 + 2) {
+    const int p = page0 + tid;
+    pages[tid] = (long long)p * a.page_size < a.key_count ? a.table[p] : 0;
+  }
   for (int i = tid; i < group * D; i += ATT_THREADS)
     qs[i / D][i % D] = a.q[((long long)t * a.q_heads + head * group + i / D) * D + i % D];
   __syncthreads();
 
-  // scores: a thread per key
+  // scores: a thread per key, the key row read in slices of 64 values with
+  // every load of a slice issued before its first use
   const int key = k0 + tid;
   const bool seen = key >= first && key < last;
   float score[MAX_GROUP];
 #pragma unroll
   for (int g = 0; g < MAX_GROUP; ++g) score[g] = 0.0f;
   if (seen) {
+    const long long page = pages[key / a.page_size - page0];
     const uint4* row = reinterpret_cast<const uint4*>(
-        a.keys + key_index(a.table, a.page_size, a.kv_heads, D, key, head));
-#pragma unroll 4
-    for (int c = 0; c < D / 8; ++c) {
-      const uint4 raw = row[c];
-      const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
-      float kv[8];
+        a.keys + ((page * a.page_size + key % a.page_size) * a.kv_heads + head) * D);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __half22float2(h2[i]);
-        kv[2 * i] = f.x;
-        kv[2 * i + 1] = f.y;
-      }
+    for (int slice = 0; slice < (D + 63) / 64; ++slice) {
+      constexpr int PER = D < 64 ? D / 8 : 8;
+      uint4 raw[PER];
 #pragma unroll
-      for (int g = 0; g < MAX_GROUP; ++g) {
-        if (g < group) {
+      for (int c = 0; c < PER; ++c) raw[c] = slice * 8 + c < D / 8 ? row[slice * 8 + c] : make_uint4(0, 0, 0, 0);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) score[g] = fmaf(qs[g][8 * c + i], kv[i], score[g]);
+      for (int c = 0; c < PER; ++c) {
+        if (slice * 8 + c >= D / 8) break;
+        const __half2* h2 = reinterpret_cast<const __half2*>(&raw[c]);
+        float kv[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __half22float2(h2[i]);
+          kv[2 * i] = f.x;
+          kv[2 * i + 1] = f.y;
+        }
+#pragma unroll
+        for (int g = 0; g < MAX_GROUP; ++g) {
+          if (g < group) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              score[g] = fmaf(qs[g][8 * (slice * 8 + c) + i], kv[i], score[g]);
+          }
         }
       }
     }
@@ -164,10 +185,37 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const Atte
   for (int g = 0; g < MAX_GROUP; ++g)
 #pragma unroll
     for (int j = 0; j < DIMS; ++j) acc[g][j] = 0.0f;
+  const bool whole = first == k0 && last == k0 + KEYS;  // a full chunk: 16 runs of 8 keys
 #pragma unroll
   for (int j = 0; j < DIMS; ++j) {
     const int d = tid + j * ATT_THREADS;
     if (d >= D) continue;
+    if (whole) {
+      uint4 raw[KEYS / 8];
+#pragma unroll
+      for (int r = 0; r < KEYS / 8; ++r) {
+        const int p = k0 + 8 * r;
+        const long long page = pages[p / a.page_size - page0];
+        raw[r] = *reinterpret_cast<const uint4*>(
+            a.values + ((page * a.kv_heads + head) * D + d) * a.page_size + p % a.page_size);
+      }
+#pragma unroll
+      for (int r = 0; r < KEYS / 8; ++r) {
+        const __half2* h2 = reinterpret_cast<const __half2*>(&raw[r]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __half22float2(h2[i]);
+#pragma unroll
+          for (int g = 0; g < MAX_GROUP; ++g) {
+            if (g < group) {
+              acc[g][j] = fmaf(ws[g][8 * r + 2 * i], f.x, acc[g][j]);
+              acc[g][j] = fmaf(ws[g][8 * r + 2 * i + 1], f.y, acc[g][j]);
+            }
+          }
+        }
+      }
+      continue;
+    }
     int p = first;
     // eight keys at a time where they share a page and start on an 8-key
     // boundary (a 16-byte run of one value column)
@@ -223,30 +271,40 @@ template <int D>
 __global__ void __launch_bounds__(ATT_THREADS) attention_join_kernel(const AttentionArgs a,
                                                                      const float* sinks,
                                                                      float* out) {
+  extern __shared__ float factor[];  // [splits]: e^(m_s - M), 0 for an empty split
+  __shared__ float shared_total;
   const int head = blockIdx.x, t = blockIdx.y;
   const long long base = ((long long)t * a.q_heads + head) * a.splits;
-  float largest = -INFINITY;
-  for (int s = 0; s < a.splits; ++s)
-    if (a.part_ml[(base + s) * 2 + 1] > 0.0f) largest = fmaxf(largest, a.part_ml[(base + s) * 2]);
-  const bool sink = sinks != nullptr;
-  if (sink) largest = fmaxf(largest, sinks[head]);
-  float total = sink ? expf(sinks[head] - largest) : 0.0f;
-  for (int s = 0; s < a.splits; ++s) {
-    const float l = a.part_ml[(base + s) * 2 + 1];
-    if (l > 0.0f) total += l * expf(a.part_ml[(base + s) * 2] - largest);
+  if (threadIdx.x < 32) {
+    float largest = -INFINITY;
+    for (int s = threadIdx.x; s < a.splits; s += 32)
+      if (a.part_ml[(base + s) * 2 + 1] > 0.0f) largest = fmaxf(largest, a.part_ml[(base + s) * 2]);
+#pragma unroll
+    for (int o = 16; o > 0; o /= 2) largest = fmaxf(largest, __shfl_xor_sync(0xffffffffu, largest, o));
+    if (sinks) largest = fmaxf(largest, sinks[head]);
+    float total = 0.0f;
+    for (int s = threadIdx.x; s < a.splits; s += 32) {
+      const float l = a.part_ml[(base + s) * 2 + 1];
+      const float f = l > 0.0f ? expf(a.part_ml[(base + s) * 2] - largest) : 0.0f;
+      factor[s] = f;
+      total += l * f;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o /= 2) total += __shfl_xor_sync(0xffffffffu, total, o);
+    if (threadIdx.x == 0) shared_total = total + (sinks ? expf(sinks[head] - largest) : 0.0f);
   }
+  __syncthreads();
+  const float total = shared_total;
   for (int d = threadIdx.x; d < D; d += ATT_THREADS) {
     float sum = 0.0f;
-    for (int s = 0; s < a.splits; ++s) {
-      const float l = a.part_ml[(base + s) * 2 + 1];
-      if (l > 0.0f) sum += a.part_o[(base + s) * D + d] * expf(a.part_ml[(base + s) * 2] - largest);
-    }
+    for (int s = 0; s < a.splits; ++s)
+      if (factor[s] > 0.0f) sum += a.part_o[(base + s) * D + d] * factor[s];
     out[((long long)t * a.q_heads + head) * D + d] = total > 0.0f ? sum / total : 0.0f;
   }
 }
 
 #define DRIFT_ATTENTION_REGISTER(D)                                                   \
-  DRIFT_REGISTER(attention_split_d##D, attention_split_kernel<D>)                     \
+  DRIFT_REGISTER(attention_split_d##D##_g4, (attention_split_kernel<D, 4>))           \
   DRIFT_REGISTER(attention_join_d##D, attention_join_kernel<D>)
 DRIFT_ATTENTION_REGISTER(64)
 DRIFT_ATTENTION_REGISTER(80)
@@ -254,11 +312,25 @@ DRIFT_ATTENTION_REGISTER(128)
 DRIFT_ATTENTION_REGISTER(256)
 DRIFT_REGISTER(cache_write_f16, cache_write_kernel)
 
+template <int D, int G>
+int launch_split(const AttentionArgs& a, cudaStream_t stream) {
+  attention_split_kernel<D, G><<<dim3(a.splits, a.kv_heads, a.tokens), ATT_THREADS, 0, stream>>>(a);
+  DRIFT_LAUNCHED("attention_split");
+  return 0;
+}
+
 template <int D>
 int launch_attention(const AttentionArgs& a, const float* sinks, float* out, cudaStream_t stream) {
-  attention_split_kernel<D><<<dim3(a.splits, a.kv_heads, a.tokens), ATT_THREADS, 0, stream>>>(a);
-  DRIFT_LAUNCHED("attention_split");
-  attention_join_kernel<D><<<dim3(a.q_heads, a.tokens), ATT_THREADS, 0, stream>>>(a, sinks, out);
+  // the key head's query heads, padded up to the next kernel's count (the
+  // padding heads' scores are computed and dropped)
+  const int group = a.q_heads / a.kv_heads;
+  if (group <= 1) DRIFT_TRY((launch_split<D, 1>(a, stream)));
+  else if (group <= 2) DRIFT_TRY((launch_split<D, 2>(a, stream)));
+  else if (group <= 4) DRIFT_TRY((launch_split<D, 4>(a, stream)));
+  else if (group <= 8) DRIFT_TRY((launch_split<D, 8>(a, stream)));
+  else DRIFT_TRY((launch_split<D, 16>(a, stream)));
+  attention_join_kernel<D><<<dim3(a.q_heads, a.tokens), ATT_THREADS, a.splits * sizeof(float),
+                             stream>>>(a, sinks, out);
   DRIFT_LAUNCHED("attention_join");
   return 0;
 }
@@ -320,6 +392,8 @@ int drift_attention(const float* q, int tokens, int q_heads, const void* keys, c
       (query_start + tokens > key_count && (causal || window > 0)))
     return invalid("attention: queries at %d..%d past %d keys", query_start,
                    query_start + tokens - 1, key_count);
+  if (key_count > (48 * 1024 / 4 - 16) * KEYS)
+    return invalid("attention: %d keys (at most %d)", key_count, (48 * 1024 / 4 - 16) * KEYS);
   if (tokens == 0) return 0;
   if (!q || !keys || !values || !out) return invalid("attention: a null tensor");
   if ((reinterpret_cast<uintptr_t>(keys) | reinterpret_cast<uintptr_t>(values)) & 15)

@@ -108,11 +108,57 @@ __device__ __forceinline__ float block_sum(float value, float* partial) {
 // One block of 256 threads per row. With `y`, x += y first (written back: the
 // residual stream). The sum of squares is float (each thread's values in
 // order, then a fixed tree); 1 / sqrt(mean + eps) is rounded as IEEE division
-// and square root round it, not rsqrtf's approximation.
+// and square root round it, not rsqrtf's approximation. Rows of up to 256 PER
+// values are held in registers, every load issued before the first use (a
+// row is one round trip to memory, not PER of them).
+template <int PER>
 __global__ void __launch_bounds__(256) rms_norm_kernel(float* __restrict__ x, const float* __restrict__ y,
                                                        const float* __restrict__ weight,
                                                        float* __restrict__ out, int cols,
                                                        float epsilon, float weight_offset) {
+  __shared__ float partial[32];
+  float* row = x + (long long)blockIdx.x * cols;
+  const float* add = y ? y + (long long)blockIdx.x * cols : nullptr;
+  float* target = out + (long long)blockIdx.x * cols;
+  float value[PER], w[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int c = threadIdx.x + i * 256;
+    value[i] = c < cols ? row[c] : 0.0f;
+    w[i] = c < cols ? weight[c] : 0.0f;
+  }
+  if (add) {
+    float extra[PER];
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int c = threadIdx.x + i * 256;
+      extra[i] = c < cols ? add[c] : 0.0f;
+    }
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int c = threadIdx.x + i * 256;
+      value[i] = value[i] + extra[i];
+      if (c < cols) row[c] = value[i];
+    }
+  }
+  float sum = 0.0f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) sum = fmaf(value[i], value[i], sum);
+  const float total = block_sum(sum, partial);
+  const float scale = 1.0f / sqrtf(total / float(cols) + epsilon);
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int c = threadIdx.x + i * 256;
+    if (c < cols) target[c] = value[i] * scale * (w[i] + weight_offset);
+  }
+}
+
+// Rows longer than 4096: the same arithmetic, a pass over memory per 256.
+__global__ void __launch_bounds__(256) rms_norm_long_kernel(float* __restrict__ x,
+                                                            const float* __restrict__ y,
+                                                            const float* __restrict__ weight,
+                                                            float* __restrict__ out, int cols,
+                                                            float epsilon, float weight_offset) {
   __shared__ float partial[32];
   float* row = x + (long long)blockIdx.x * cols;
   const float* add = y ? y + (long long)blockIdx.x * cols : nullptr;
@@ -132,7 +178,28 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(float* __restrict__ x, co
     target[c] = row[c] * scale * (weight[c] + weight_offset);
 }
 
-DRIFT_REGISTER(rms_norm_f32, rms_norm_kernel)
+int launch_rms_norm(float* x, const float* y, const float* weight, float* out, int64_t rows,
+                    int64_t cols, float epsilon, float weight_offset, cudaStream_t stream) {
+  const unsigned grid = unsigned(rows);
+  const int c = int(cols);
+  if (cols <= 256)
+    rms_norm_kernel<1><<<grid, 256, 0, stream>>>(x, y, weight, out, c, epsilon, weight_offset);
+  else if (cols <= 512)
+    rms_norm_kernel<2><<<grid, 256, 0, stream>>>(x, y, weight, out, c, epsilon, weight_offset);
+  else if (cols <= 1024)
+    rms_norm_kernel<4><<<grid, 256, 0, stream>>>(x, y, weight, out, c, epsilon, weight_offset);
+  else if (cols <= 2048)
+    rms_norm_kernel<8><<<grid, 256, 0, stream>>>(x, y, weight, out, c, epsilon, weight_offset);
+  else if (cols <= 4096)
+    rms_norm_kernel<16><<<grid, 256, 0, stream>>>(x, y, weight, out, c, epsilon, weight_offset);
+  else
+    rms_norm_long_kernel<<<grid, 256, 0, stream>>>(x, y, weight, out, c, epsilon, weight_offset);
+  DRIFT_LAUNCHED("rms_norm_f32");
+  return 0;
+}
+
+DRIFT_REGISTER(rms_norm_f32, rms_norm_kernel<16>)
+DRIFT_REGISTER(rms_norm_long_f32, rms_norm_long_kernel)
 
 // ---- elementwise ---------------------------------------------------------------------------
 #define DRIFT_FOR_EACH(i, n)                                                     \
@@ -328,10 +395,8 @@ int drift_rms_norm(const float* x, const float* weight, float epsilon, float wei
   DRIFT_TRY(check_rows("rmsNorm", x, out, rows, cols));
   if (rows == 0 || cols == 0) return 0;
   if (!weight) return invalid("rmsNorm: no weight");
-  rms_norm_kernel<<<unsigned(rows), 256, 0, cudaStream_t(stream)>>>(
-      const_cast<float*>(x), nullptr, weight, out, int(cols), epsilon, weight_offset);
-  DRIFT_LAUNCHED("rms_norm_f32");
-  return 0;
+  return launch_rms_norm(const_cast<float*>(x), nullptr, weight, out, rows, cols, epsilon,
+                         weight_offset, cudaStream_t(stream));
 }
 
 int drift_add_rms_norm(float* x, const float* y, const float* weight, float epsilon,
@@ -340,10 +405,8 @@ int drift_add_rms_norm(float* x, const float* y, const float* weight, float epsi
   DRIFT_TRY(check_rows("addRmsNorm", x, out, rows, cols));
   if (rows == 0 || cols == 0) return 0;
   if (!weight || !y) return invalid("addRmsNorm: no weight or no y");
-  rms_norm_kernel<<<unsigned(rows), 256, 0, cudaStream_t(stream)>>>(x, y, weight, out, int(cols),
-                                                                     epsilon, weight_offset);
-  DRIFT_LAUNCHED("rms_norm_f32");
-  return 0;
+  return launch_rms_norm(x, y, weight, out, rows, cols, epsilon, weight_offset,
+                         cudaStream_t(stream));
 }
 
 int drift_add(const float* a, const float* b, float* out, int64_t n, drift_stream_t stream) {
