@@ -84,6 +84,11 @@ SIGNATURES = {
     "drift_cache_write": (_i32, [_p, _p, _i32, _i32, _i32, _p, _p, _i32, _i32, _p, _i32, _i32, _p]),
     "drift_attention": (_i32, [_p, _i32, _i32, _p, _p, _i32, _i32, _i32, _i32, _p, _i32, _i32, _i32,
                                _f32, _i32, _i32, _f32, _p, _p, _p]),
+    "drift_attention_inputs_decode": (_i32, [_p, _p, _p, _i32, _i32, _i32, _i32, _p, _p, _f32, _f32,
+                                             _p, _f32, _i32, _i32, _p, _p, _p, _i32, _i32, _p, _i32,
+                                             _p]),
+    "drift_attention_decode": (_i32, [_p, _i32, _i32, _p, _p, _i32, _i32, _i32, _i32, _p, _i32, _p,
+                                      _i32, _f32, _i32, _f32, _p, _p, _p]),
 }
 
 

@@ -17,10 +17,12 @@
 
 #include "common.cuh"
 #include "registry.cuh"
+#include "rowwise.cuh"
 
 namespace drift {
 
 int workspace_reserve(size_t bytes, void** pointer);
+int* device_error_word();
 
 namespace {
 
@@ -55,25 +57,102 @@ __global__ void cache_write_kernel(const float* __restrict__ k, const float* __r
   }
 }
 
+// One launch serves either one sequence's `tokens` queries (the reference's
+// call) or, with `positions`, a batch of sequences with one query each (a
+// decode step): row z of q is then sequence z at positions[z], seeing keys
+// 0..positions[z] through its page table row table + z * table_stride.
+// A decode step's attention inputs, fused (the rmsNorm of each query and key
+// head, the rope of both, and the cache write of keys and values that the
+// dense decoder calls one by one, models/DenseDecoder.scala:830-860): a CTA of
+// 256 threads per (head, sequence), thread d holding value d. Slots 0..q_heads
+// are query heads, turned into q_out; the rest are key heads, whose turned
+// keys and the values go into the sequence's cache at positions[z]. The norm
+// and the turn are rms_norm_kernel's and rope_kernel's arithmetic
+// (rowwise.cuh), so the results are those kernels' bits. A position outside
+// the sequence's page table sets the device error word (code 1) and writes
+// nothing.
+__global__ void __launch_bounds__(256) attention_inputs_kernel(
+    const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+    int q_heads, int kv_heads, int dim, const float* __restrict__ q_norm,
+    const float* __restrict__ k_norm, float epsilon, float weight_offset,
+    const int* __restrict__ positions, float theta, int rotary, int layout, float* __restrict__ q_out,
+    __half* keys, __half* values, int page_size, const int* __restrict__ tables, int table_stride,
+    int* error) {
+  __shared__ float partial[32];
+  __shared__ float row[256];
+  const int slot = blockIdx.x, z = blockIdx.y, d = threadIdx.x;
+  const bool query = slot < q_heads;
+  const int h = query ? slot : slot - q_heads;
+  const float* source = query ? q + ((long long)z * q_heads + h) * dim
+                              : k + ((long long)z * kv_heads + h) * dim;
+  const float* norm = query ? q_norm : k_norm;
+  float value = d < dim ? source[d] : 0.0f;
+  if (norm) {
+    const float w = d < dim ? norm[d] : 0.0f;
+    const float total = block_sum(fmaf(value, value, 0.0f), partial);
+    const float scale = 1.0f / sqrtf(total / float(dim) + epsilon);
+    value = value * scale * (w + weight_offset);
+  }
+  if (d < dim) row[d] = value;
+  __syncthreads();
+  if (d >= dim) return;
+  const int position = positions[z];
+  const float turned = rope_turn(row, d, position, theta, rotary, layout);
+  if (query) {
+    q_out[((long long)z * q_heads + h) * dim + d] = turned;
+    return;
+  }
+  if (position < 0 || position >= table_stride * page_size) {
+    if (d == 0) atomicCAS(error, 0, 1);
+    return;
+  }
+  const int* table = tables + (long long)z * table_stride;
+  keys[key_index(table, page_size, kv_heads, dim, position, h) + d] = __float2half_rn(turned);
+  values[value_index(table, page_size, kv_heads, dim, position, h, d)] =
+      __float2half_rn(v[((long long)z * kv_heads + h) * dim + d]);
+}
+
 struct AttentionArgs {
   const float* q;
   const __half* keys;
   const __half* values;
   const int* table;
-  float* part_o;   // [tokens][q_heads][splits][D]
-  float* part_ml;  // [tokens][q_heads][splits][2]
-  int page_size, kv_heads, q_heads, query_start, key_count, tokens, splits;
+  const int* positions;  // batched decode, or nullptr
+  float* part_o;   // [rows][q_heads][splits][D]
+  float* part_ml;  // [rows][q_heads][splits][2]
+  int page_size, kv_heads, q_heads, query_start, key_count, tokens, splits, table_stride;
   float scale;
   int causal, window, has_softcap;
   float softcap;
 };
 
-// The visible keys of the query at `position`: [lo, hi).
-__device__ __forceinline__ void visible(const AttentionArgs& a, int position, int& lo, int& hi) {
-  hi = a.key_count;
-  if (a.causal && position + 1 < hi) hi = position + 1;
+// Row z's page table, key count and query position.
+struct Query {
+  const int* table;
+  int key_count, position;
+  __device__ Query(const AttentionArgs& a, int z) {
+    if (a.positions) {
+      table = a.table + (long long)z * a.table_stride;
+      position = a.positions[z];
+      key_count = position + 1;
+      // a position past the page table (or the launch's key count) sees no keys
+      if (position < 0 || key_count > a.table_stride * a.page_size || key_count > a.key_count)
+        key_count = 0;
+    } else {
+      table = a.table;
+      position = a.query_start + z;
+      key_count = a.key_count;
+    }
+  }
+};
+
+// The visible keys of the query: [lo, hi).
+__device__ __forceinline__ void visible(const AttentionArgs& a, const Query& query, int& lo,
+                                        int& hi) {
+  hi = query.key_count;
+  if (a.causal && query.position + 1 < hi) hi = query.position + 1;
   lo = 0;
-  if (a.window > 0 && position - a.window + 1 > lo) lo = position - a.window + 1;
+  if (a.window > 0 && query.position - a.window + 1 > lo) lo = query.position - a.window + 1;
 }
 
 // G: query heads per key head, a template so that the unrolled loops hold
@@ -90,9 +169,9 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const Atte
   const int split = blockIdx.x, head = blockIdx.y, t = blockIdx.z;
   const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
   const int group = a.q_heads / a.kv_heads;  // <= G
-  const int position = a.query_start + t;
+  const Query query(a, t);
   int lo, hi;
-  visible(a, position, lo, hi);
+  visible(a, query, lo, hi);
   const int k0 = split * KEYS;
   const int first = k0 > lo ? k0 : lo, last = k0 + KEYS < hi ? k0 + KEYS : hi;  // [first, last)
 
@@ -101,7 +180,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const Atte
   const int page0 = k0 / a.page_size;
   if (tid < KEYS / 16 + 2) {
     const int p = page0 + tid;
-    pages[tid] = (long long)p * a.page_size < a.key_count ? a.table[p] : 0;
+    pages[tid] = (long long)p * a.page_size < query.key_count ? query.table[p] : 0;
   }
   for (int i = tid; i < group * D; i += ATT_THREADS)
     qs[i / D][i % D] = a.q[((long long)t * a.q_heads + head * group + i / D) * D + i % D];
@@ -195,7 +274,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const Atte
 #pragma unroll
       for (int r = 0; r < KEYS / 8; ++r) {
         const int p = k0 + 8 * r;
-        const long long page = pages[p / a.page_size - page0];
+        const long long page = pages[p / a.page_size - page0];  // within the chunk's pages
         raw[r] = *reinterpret_cast<const uint4*>(
             a.values + ((page * a.kv_heads + head) * D + d) * a.page_size + p % a.page_size);
       }
@@ -222,7 +301,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const Atte
     while (p < last) {
       if (p % 8 == 0 && p + 8 <= last && (p % a.page_size) + 8 <= a.page_size) {
         const uint4 raw = *reinterpret_cast<const uint4*>(
-            a.values + value_index(a.table, a.page_size, a.kv_heads, D, p, head, d));
+            a.values + value_index(query.table, a.page_size, a.kv_heads, D, p, head, d));
         const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -238,7 +317,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const Atte
         p += 8;
       } else {
         const float f = __half2float(
-            a.values[value_index(a.table, a.page_size, a.kv_heads, D, p, head, d)]);
+            a.values[value_index(query.table, a.page_size, a.kv_heads, D, p, head, d)]);
 #pragma unroll
         for (int g = 0; g < MAX_GROUP; ++g)
           if (g < group) acc[g][j] = fmaf(ws[g][p - k0], f, acc[g][j]);
@@ -311,6 +390,7 @@ DRIFT_ATTENTION_REGISTER(80)
 DRIFT_ATTENTION_REGISTER(128)
 DRIFT_ATTENTION_REGISTER(256)
 DRIFT_REGISTER(cache_write_f16, cache_write_kernel)
+DRIFT_REGISTER(attention_inputs_f32, attention_inputs_kernel)
 
 template <int D, int G>
 int launch_split(const AttentionArgs& a, cudaStream_t stream) {
@@ -403,6 +483,8 @@ int drift_attention(const float* q, int tokens, int q_heads, const void* keys, c
   a.keys = static_cast<const __half*>(keys);
   a.values = static_cast<const __half*>(values);
   a.table = page_table;
+  a.positions = nullptr;
+  a.table_stride = 0;
   a.page_size = page_size;
   a.kv_heads = kv_heads;
   a.q_heads = q_heads;
@@ -416,6 +498,80 @@ int drift_attention(const float* q, int tokens, int q_heads, const void* keys, c
   a.has_softcap = softcap > 0.0f;
   a.softcap = softcap;
   const size_t parts = size_t(tokens) * q_heads * a.splits;
+  void* ws = nullptr;
+  DRIFT_TRY(workspace_reserve(parts * (head_dim + 2) * sizeof(float), &ws));
+  a.part_o = static_cast<float*>(ws);
+  a.part_ml = a.part_o + parts * head_dim;
+  const cudaStream_t s = cudaStream_t(stream);
+  switch (head_dim) {
+    case 64: return launch_attention<64>(a, sinks, out, s);
+    case 80: return launch_attention<80>(a, sinks, out, s);
+    case 128: return launch_attention<128>(a, sinks, out, s);
+    default: return launch_attention<256>(a, sinks, out, s);
+  }
+}
+
+int drift_attention_inputs_decode(const float* q, const float* k, const float* v, int batch,
+                                  int q_heads, int kv_heads, int head_dim, const float* q_norm,
+                                  const float* k_norm, float epsilon, float weight_offset,
+                                  const int32_t* positions, float theta, int rotary, int layout,
+                                  float* q_out, void* keys, void* values, int pages,
+                                  int page_size, const int32_t* page_tables, int table_stride,
+                                  drift_stream_t stream) {
+  if (batch < 0 || q_heads <= 0) return invalid("attention inputs: %d sequences of %d heads", batch, q_heads);
+  DRIFT_TRY(check_cache(pages, page_size, kv_heads, head_dim, page_tables, table_stride, 0,
+                        "attention inputs"));
+  if (rotary < 0 || rotary > head_dim || rotary % 2)
+    return invalid("rope: %d rotary dimensions in heads of %d", rotary, head_dim);
+  if (batch == 0) return 0;
+  if (!q || !k || !v || !positions || !q_out || !keys || !values)
+    return invalid("attention inputs: a null tensor");
+  if ((reinterpret_cast<uintptr_t>(keys) | reinterpret_cast<uintptr_t>(values)) & 15)
+    return invalid("attention inputs: the cache does not start on a 16-byte boundary");
+  attention_inputs_kernel<<<dim3(q_heads + kv_heads, batch), 256, 0, cudaStream_t(stream)>>>(
+      q, k, v, q_heads, kv_heads, head_dim, q_norm, k_norm, epsilon, weight_offset, positions,
+      theta, rotary, layout, q_out, static_cast<__half*>(keys), static_cast<__half*>(values),
+      page_size, page_tables, table_stride, device_error_word());
+  DRIFT_LAUNCHED("attention_inputs");
+  return 0;
+}
+
+int drift_attention_decode(const float* q, int batch, int q_heads, const void* keys,
+                           const void* values, int pages, int page_size, int kv_heads,
+                           int head_dim, const int32_t* page_tables, int table_stride,
+                           const int32_t* positions, int max_key_count, float scale, int window,
+                           float softcap, const float* sinks, float* out, drift_stream_t stream) {
+  if (batch < 0 || q_heads <= 0) return invalid("attention: %d sequences of %d heads", batch, q_heads);
+  DRIFT_TRY(check_cache(pages, page_size, kv_heads, head_dim, page_tables, table_stride,
+                        max_key_count, "attention"));
+  if (q_heads % kv_heads != 0 || q_heads / kv_heads > MAX_GROUP)
+    return invalid("attention: %d query heads over %d key heads", q_heads, kv_heads);
+  if (max_key_count <= 0 || max_key_count > (48 * 1024 / 4 - 16) * KEYS)
+    return invalid("attention: %d keys", max_key_count);
+  if (batch == 0) return 0;
+  if (!q || !keys || !values || !positions || !out) return invalid("attention: a null tensor");
+  if ((reinterpret_cast<uintptr_t>(keys) | reinterpret_cast<uintptr_t>(values)) & 15)
+    return invalid("attention: the cache does not start on a 16-byte boundary");
+  AttentionArgs a;
+  a.q = q;
+  a.keys = static_cast<const __half*>(keys);
+  a.values = static_cast<const __half*>(values);
+  a.table = page_tables;
+  a.positions = positions;
+  a.table_stride = table_stride;
+  a.page_size = page_size;
+  a.kv_heads = kv_heads;
+  a.q_heads = q_heads;
+  a.query_start = 0;
+  a.key_count = max_key_count;
+  a.tokens = batch;
+  a.splits = (max_key_count + KEYS - 1) / KEYS;
+  a.scale = scale;
+  a.causal = 1;
+  a.window = window;
+  a.has_softcap = softcap > 0.0f;
+  a.softcap = softcap;
+  const size_t parts = size_t(batch) * q_heads * a.splits;
   void* ws = nullptr;
   DRIFT_TRY(workspace_reserve(parts * (head_dim + 2) * sizeof(float), &ws));
   a.part_o = static_cast<float*>(ws);

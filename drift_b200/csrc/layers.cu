@@ -11,6 +11,7 @@
 #include <cuda_runtime.h>
 
 #include "common.cuh"
+#include "rowwise.cuh"
 #include "quant.cuh"
 #include "registry.cuh"
 
@@ -88,21 +89,6 @@ DRIFT_REGISTER(gather_q8_0, gather_kernel<Q8_0T>)
 DRIFT_REGISTER(gather_q4_0, gather_kernel<Q4_0T>)
 DRIFT_REGISTER(gather_q4_1, gather_kernel<Q4_1T>)
 DRIFT_REGISTER(gather_rows_f32, gather_rows_f32_kernel)
-
-// ---- block reductions -------------------------------------------------------------------
-// The sum over a block of `blockDim.x` threads (a multiple of 32): warps by
-// shuffles, then the warps' sums in warp order. Every thread gets it.
-__device__ __forceinline__ float block_sum(float value, float* partial) {
-#pragma unroll
-  for (int o = 16; o > 0; o /= 2) value += __shfl_xor_sync(0xffffffffu, value, o);
-  const int warp = threadIdx.x / WARP, warps = blockDim.x / WARP;
-  if (threadIdx.x % WARP == 0) partial[warp] = value;
-  __syncthreads();
-  float total = 0.0f;
-  for (int w = 0; w < warps; ++w) total += partial[w];
-  __syncthreads();  // partial is reused by the next reduction
-  return total;
-}
 
 // ---- RMS norm ----------------------------------------------------------------------------
 // One block of 256 threads per row. With `y`, x += y first (written back: the
@@ -249,33 +235,7 @@ __global__ void rope_kernel(const float* __restrict__ x, const int* __restrict__
   if (index >= (long long)tokens * heads * head_dim) return;
   const int d = int(index % head_dim);
   const int t = int(index / ((long long)heads * head_dim));
-  const float* head = x + (index - d);
-  if (d >= rotary) {
-    out[index] = head[d];
-    return;
-  }
-  const int half = rotary / 2;
-  int pair, partner;
-  bool first;
-  if (layout == DRIFT_ROPE_NEOX) {
-    pair = d % half;
-    first = d < half;
-    partner = first ? d + half : d - half;
-  } else {
-    pair = d / 2;
-    first = d % 2 == 0;
-    partner = first ? d + 1 : d - 1;
-  }
-  const float power = float(pow(double(theta), __ddiv_rn(2.0 * pair, double(rotary))));
-  const float inverse = __fdiv_rn(1.0f, power);
-  const float angle = __fmul_rn(float(positions[t]), inverse);
-  double s, c;
-  sincos(double(angle), &s, &c);
-  const double a = first ? double(head[d]) : double(head[partner]);
-  const double b = first ? double(head[partner]) : double(head[d]);
-  const double value = first ? __dsub_rn(__dmul_rn(a, c), __dmul_rn(b, s))
-                             : __dadd_rn(__dmul_rn(a, s), __dmul_rn(b, c));
-  out[index] = float(value);
+  out[index] = rope_turn(x + (index - d), d, positions[t], theta, rotary, layout);
 }
 
 DRIFT_REGISTER(rope_f32, rope_kernel)

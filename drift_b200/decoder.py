@@ -4,10 +4,11 @@ runner's DenseDecoder.run (runner/src/drift/runner/models/DenseDecoder.scala:
 GPUs of one box (drift_b200/tensor_parallel.py).
 
 Per token and layer: RMSNorm; q, k, v products (one x preparation); per-head
-q/k RMSNorm (Qwen3); RoPE of q and k; the new k, v into each sequence's paged
-F16 cache; attention over the cache; o product; residual add + RMSNorm; gate
-and up products; SwiGLU; down product; residual add. Then the final RMSNorm
-and the lm-head product. With tensor parallelism a rank holds its share of
+q/k RMSNorm (Qwen3), RoPE of q and k and the new k, v into each sequence's
+paged F16 cache (one fused launch for the batch); attention over the caches
+(one launch for the batch); o product; residual add + RMSNorm; gate and up
+products; SwiGLU; down product; residual add. Then the final RMSNorm and the
+lm-head product. With tensor parallelism a rank holds its share of
 the query and key heads and of the FFN rows (column-split q/k/v/gate/up),
 the matching columns of o and down (row-split, one all-reduce each), and its
 share of the vocabulary rows of the lm-head; the embedding and the norms are
@@ -142,8 +143,10 @@ class DenseDecoder:
         pages = pages_per_sequence * batch
         self.caches = [KvCache.allocate(pages, c.page_size, self.kv_heads, c.head_dim)
                        for _ in weights.layers]
-        self.tables = [torch.arange(i * pages_per_sequence, (i + 1) * pages_per_sequence,
-                                    dtype=torch.int32, device="cuda") for i in range(batch)]
+        # sequence i's pages: [i P, (i + 1) P); one row of the page table each
+        self.page_tables = torch.arange(pages, dtype=torch.int32,
+                                        device="cuda").view(batch, pages_per_sequence)
+        self.tables = [self.page_tables[i] for i in range(batch)]
         self.rope = Rope(c.theta, c.head_dim)
         self.attention = Attention(1.0 / math.sqrt(c.head_dim))
         b, hd = batch, c.head_dim
@@ -181,29 +184,25 @@ class DenseDecoder:
         if self.group is not None:
             torch.distributed.all_reduce(t, group=self.group)
 
-    def step(self, positions: list[int]) -> torch.Tensor:
-        """One decode step: self.ids at `positions` (one per sequence, written
-        to self.positions by the caller or here) -> self.logits [batch, this
-        rank's vocabulary rows]."""
+    def step(self, positions: Optional[list[int]] = None) -> torch.Tensor:
+        """One decode step: self.ids at self.positions (device, one per
+        sequence, set by the caller) -> self.logits [batch, this rank's
+        vocabulary rows]. `positions` is not needed: the kernels read the
+        device copy (so a captured step replays at new positions)."""
         ops, c, w = self.ops, self.config, self.weights
         b, hd = self.batch, c.head_dim
         ops.embedding(w.embedding, self.ids, self.x)
         ops.rms_norm(self.x, w.layers[0].attention_norm, c.epsilon, 0.0, self.normed)
         for index, (layer, cache) in enumerate(zip(w.layers, self.caches)):
             ops.linears(self.normed, [layer.q, layer.k, layer.v], [self.q, self.k, self.v])
-            q = self.q.view(b, self.q_heads, hd)
-            k = self.k.view(b, self.kv_heads, hd)
-            if c.qk_norm:
-                ops.rms_norm(q, layer.q_norm, c.epsilon, 0.0, q)
-                ops.rms_norm(k, layer.k_norm, c.epsilon, 0.0, k)
-            ops.rope(q, self.positions, self.rope, self.q_turned)
-            ops.rope(k, self.positions, self.rope, self.k_turned)
-            v = self.v.view(b, self.kv_heads, hd)
-            for i in range(b):
-                p = positions[i]
-                ops.cache_write(self.k_turned[i:i + 1], v[i:i + 1], cache, self.tables[i], p)
-                ops.attention(self.q_turned[i:i + 1], cache, self.tables[i], p, p + 1,
-                              self.attention, self.attended[i:i + 1])
+            # per-head q/k norms, rope, cache write: one launch for the batch;
+            # then every sequence's attention in one launch
+            ops.attention_inputs_decode(
+                self.q.view(b, self.q_heads, hd), self.k.view(b, self.kv_heads, hd),
+                self.v.view(b, self.kv_heads, hd), layer.q_norm, layer.k_norm, c.epsilon,
+                self.positions, self.rope, self.q_turned, cache, self.page_tables)
+            ops.attention_decode(self.q_turned, cache, self.page_tables, self.positions,
+                                 self.context, self.attention, self.attended)
             ops.linear(self.attended.view(b, self.q_heads * hd), layer.o, self.projected)
             self._all_reduce(self.projected)
             ops.add_rms_norm(self.x, self.projected,
@@ -224,7 +223,7 @@ class DenseDecoder:
         widest = max(c.hidden, self.q_heads * c.head_dim, self.ffn)
         self.ops.reserve_workspace(self.batch, widest)
         splits = (self.context + 127) // 128
-        attention_bytes = self.q_heads * splits * (c.head_dim + 2) * 4
+        attention_bytes = self.batch * self.q_heads * splits * (c.head_dim + 2) * 4
         lib = self.ops.lib
         from ._lib import check
         check("drift_workspace_reserve", lib.drift_workspace_reserve(

@@ -350,6 +350,54 @@ class CudaOps:
             _ptr(sinks), _ptr(out), self._stream())
         check("drift_attention", status)
 
+    def attention_inputs_decode(self, q, k, v, q_norm, k_norm, epsilon: float, positions,
+                                rope: Rope, q_out, cache: KvCache, page_tables) -> None:
+        """A decode step's per-head q/k RMS norms, their rope and the cache
+        write of k and v, for one token per sequence, in one launch.
+        q [b, q_heads, D], k, v [b, kv_heads, D]; positions I32 [b];
+        page_tables I32 [b, pages per sequence]."""
+        _f32("attentionInputs", q, k, v, q_out)
+        _same_shape("attentionInputs", q, q_out)
+        _same_shape("attentionInputs", k, v)
+        b, q_heads, dim = q.shape
+        _require(k.dim() == 3 and k.shape[0] == b and tuple(k.shape[1:]) ==
+                 (cache.kv_heads, cache.head_dim) and dim == cache.head_dim,
+                 f"attentionInputs: {list(q.shape)}, {list(k.shape)} for a cache of "
+                 f"{cache.kv_heads} heads of {cache.head_dim}")
+        _require(positions.dtype == torch.int32 and tuple(positions.shape) == (b,),
+                 f"attentionInputs: positions {list(positions.shape)} for {b} sequences")
+        _require(page_tables.dtype == torch.int32 and page_tables.dim() == 2 and
+                 page_tables.shape[0] == b and page_tables.is_contiguous(),
+                 f"attentionInputs: page tables {list(page_tables.shape)} for {b} sequences")
+        status = self.lib.drift_attention_inputs_decode(
+            _ptr(q), _ptr(k), _ptr(v), b, q_heads, cache.kv_heads, dim, _ptr(q_norm),
+            _ptr(k_norm), epsilon, 0.0, _ptr(positions), rope.theta, rope.rotary_dimensions,
+            rope.layout, _ptr(q_out), _ptr(cache.keys), _ptr(cache.values), cache.pages,
+            cache.page_size, _ptr(page_tables), int(page_tables.shape[1]), self._stream())
+        check("drift_attention_inputs_decode", status)
+
+    def attention_decode(self, q, cache: KvCache, page_tables, positions, max_key_count: int,
+                         attention: Attention, out) -> None:
+        """Attention of one query per sequence, all sequences in one launch:
+        row z of q [b, q_heads, D] at positions[z] over its keys 0..positions[z]."""
+        _f32("attention", q, out)
+        _same_shape("attention", q, out)
+        b, q_heads, dim = q.shape
+        _require(dim == cache.head_dim,
+                 f"attention: queries {list(q.shape)} against heads of {cache.head_dim}")
+        _require(page_tables.dtype == torch.int32 and page_tables.dim() == 2 and
+                 page_tables.shape[0] == b and page_tables.is_contiguous(),
+                 f"attention: page tables {list(page_tables.shape)} for {b} sequences")
+        _require(positions.dtype == torch.int32 and tuple(positions.shape) == (b,),
+                 f"attention: positions {list(positions.shape)} for {b} sequences")
+        _require(attention.causal, "a decode step's attention is causal")
+        status = self.lib.drift_attention_decode(
+            _ptr(q), b, q_heads, _ptr(cache.keys), _ptr(cache.values), cache.pages,
+            cache.page_size, cache.kv_heads, dim, _ptr(page_tables), int(page_tables.shape[1]),
+            _ptr(positions), max_key_count, attention.scale, int(attention.window or 0),
+            float(attention.softcap or 0.0), _ptr(attention.sinks), _ptr(out), self._stream())
+        check("drift_attention_decode", status)
+
     # -- ExpertsOps (ops/ExpertsOps.scala) -------------------------------------------------------------
     def route(self, logits, ids, weights) -> None:
         """Top-k routing (ExpertsOps.scala:116-120; checks L252-269)."""

@@ -163,6 +163,37 @@ int drift_attention(const float* q, int tokens, int q_heads, const void* keys, c
                     float scale, int causal, int window, float softcap, const float* sinks,
                     float* out, drift_stream_t stream);
 
+/* A decode step's attention inputs in one launch, for `batch` sequences of
+ * one new token each (the dense decoder's per-head rmsNorm of q and k, rope of
+ * both and cacheWrite, models/DenseDecoder.scala:830-860, fused; no single
+ * counterpart in the reference's Ops API). q [batch, q_heads, head_dim], k, v
+ * [batch, kv_heads, head_dim] F32; q_norm / k_norm [head_dim] or NULL (no
+ * norm); positions I32 [batch] (device) give each token's rope position and
+ * cache slot; page_tables I32 [batch, table_stride] (device), row z mapping
+ * sequence z's positions to pages. The turned queries go to q_out; keys and
+ * values to the cache. Results are bit for bit those of drift_rms_norm,
+ * drift_rope and drift_cache_write called in turn. A position outside its
+ * page table sets the device error word (code 1). */
+int drift_attention_inputs_decode(const float* q, const float* k, const float* v, int batch,
+                                  int q_heads, int kv_heads, int head_dim, const float* q_norm,
+                                  const float* k_norm, float epsilon, float weight_offset,
+                                  const int32_t* positions, float theta, int rotary, int layout,
+                                  float* q_out, void* keys, void* values, int pages,
+                                  int page_size, const int32_t* page_tables, int table_stride,
+                                  drift_stream_t stream);
+
+/* drift_attention for a decode step of `batch` sequences in one launch: row z
+ * of q [batch, q_heads, head_dim] is sequence z's token at positions[z]
+ * (device), attending causally to its keys 0..positions[z] through page table
+ * row z; max_key_count bounds every positions[z] + 1 (a row past it, or past
+ * its table, gets zeros). Each row's result is bit for bit drift_attention's
+ * for that sequence alone. */
+int drift_attention_decode(const float* q, int batch, int q_heads, const void* keys,
+                           const void* values, int pages, int page_size, int kv_heads,
+                           int head_dim, const int32_t* page_tables, int table_stride,
+                           const int32_t* positions, int max_key_count, float scale, int window,
+                           float softcap, const float* sinks, float* out, drift_stream_t stream);
+
 /* The library keeps one grow-only scratch buffer per device for the products'
  * prepared x (as the runner's HIP backend keeps grow-only scratch,
  * ops/HipBase.scala:341-351). Reserving it ahead keeps allocation out of a

@@ -113,3 +113,68 @@ def test_attention_refuses_what_the_reference_refuses(ops):
                   torch.zeros(4, 2, 128, 8, dtype=torch.float16, device="cuda"), 8)
     with pytest.raises(ValueError, match="multiple of 16"):
         ops.attention(q, bad, table, 0, 1, Attention(1.0), out)
+
+
+@pytest.mark.parametrize("dim,q_heads,kv_heads", [(128, 32, 8), (256, 16, 2), (64, 8, 8)])
+def test_batched_decode_is_each_sequence_alone(ops, dim, q_heads, kv_heads):
+    """drift_attention_decode: every row bit for bit drift_attention of its
+    sequence at its own length (sequences of different lengths in one launch)."""
+    rng = np.random.default_rng(dim)
+    batch, page_size, per_sequence = 4, 16, 20
+    lengths = [1, 17, 130, 300]
+    pages = batch * per_sequence
+    tables = rng.permutation(pages).astype(np.int32).reshape(batch, per_sequence)
+    keys = np.zeros((pages, page_size, kv_heads, dim), dtype=np.uint16)
+    values = np.zeros((pages, kv_heads, dim, page_size), dtype=np.uint16)
+    for i, n in enumerate(lengths):
+        k = rng.standard_normal((n, kv_heads, dim)).astype(np.float32)
+        v = rng.standard_normal((n, kv_heads, dim)).astype(np.float32)
+        oracle.cache_write(k, v, keys, values, page_size, tables[i], 0)
+    cache = KvCache(torch.from_numpy(keys.view(np.float16)).cuda(),
+                    torch.from_numpy(values.view(np.float16)).cuda(), page_size)
+    q = torch.from_numpy(rng.standard_normal((batch, q_heads, dim)).astype(np.float32)).cuda()
+    table_dev = torch.from_numpy(tables).cuda()
+    positions = torch.tensor([n - 1 for n in lengths], dtype=torch.int32, device="cuda")
+    attention = Attention(1.0 / math.sqrt(dim))
+    batched = torch.empty_like(q)
+    ops.attention_decode(q, cache, table_dev, positions, per_sequence * page_size, attention,
+                         batched)
+    for i, n in enumerate(lengths):
+        alone = torch.empty(1, q_heads, dim, device="cuda")
+        ops.attention(q[i:i + 1], cache, table_dev[i], n - 1, n, attention, alone)
+        assert torch.equal(batched[i:i + 1], alone), f"sequence {i}"
+
+
+def test_fused_attention_inputs_are_the_separate_ops(ops):
+    """drift_attention_inputs_decode: the bits of rms_norm per head, rope and
+    cache_write called in turn."""
+    from drift_b200.ops import Rope
+
+    rng = np.random.default_rng(8)
+    batch, q_heads, kv_heads, dim, page_size, per_sequence = 3, 8, 2, 128, 16, 8
+    pages = batch * per_sequence
+    tables = torch.arange(pages, dtype=torch.int32, device="cuda").view(batch, per_sequence)
+    q = torch.from_numpy(rng.standard_normal((batch, q_heads, dim)).astype(np.float32)).cuda()
+    k = torch.from_numpy(rng.standard_normal((batch, kv_heads, dim)).astype(np.float32)).cuda()
+    v = torch.from_numpy(rng.standard_normal((batch, kv_heads, dim)).astype(np.float32)).cuda()
+    q_norm = torch.from_numpy((1 + 0.02 * rng.standard_normal(dim)).astype(np.float32)).cuda()
+    k_norm = torch.from_numpy((1 + 0.02 * rng.standard_normal(dim)).astype(np.float32)).cuda()
+    positions = torch.tensor([5, 60, 100], dtype=torch.int32, device="cuda")
+    rope = Rope(1e6, dim)
+    fused_cache = KvCache.allocate(pages, page_size, kv_heads, dim)
+    fused_q = torch.empty_like(q)
+    ops.attention_inputs_decode(q, k, v, q_norm, k_norm, 1e-6, positions, rope, fused_q,
+                                fused_cache, tables)
+    cache = KvCache.allocate(pages, page_size, kv_heads, dim)
+    qn, kn = torch.empty_like(q), torch.empty_like(k)
+    ops.rms_norm(q, q_norm, 1e-6, 0.0, qn)
+    ops.rms_norm(k, k_norm, 1e-6, 0.0, kn)
+    q_turned = torch.empty_like(q)
+    k_turned = torch.empty_like(k)
+    for i in range(batch):
+        ops.rope(qn[i:i + 1], positions[i:i + 1], rope, q_turned[i:i + 1])
+        ops.rope(kn[i:i + 1], positions[i:i + 1], rope, k_turned[i:i + 1])
+        ops.cache_write(k_turned[i:i + 1], v[i:i + 1], cache, tables[i], int(positions[i]))
+    assert torch.equal(fused_q, q_turned)
+    assert torch.equal(fused_cache.keys, cache.keys)
+    assert torch.equal(fused_cache.values, cache.values)
