@@ -47,6 +47,8 @@ __device__ __forceinline__ int64_t value_index(const int* table, int page_size, 
 __global__ void cache_write_kernel(const float* __restrict__ k, const float* __restrict__ v,
                                    __half* keys, __half* values, const int* __restrict__ table,
                                    int page_size, int kv_heads, int dim, int tokens, int start) {
+  pdl_trigger();  // the next kernel may launch and wait for this one
+  pdl_wait();     // what the kernels before this one wrote is visible
   const long long total = (long long)tokens * kv_heads * dim;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
@@ -78,6 +80,8 @@ __global__ void __launch_bounds__(256) attention_inputs_kernel(
     const int* __restrict__ positions, float theta, int rotary, int layout, float* __restrict__ q_out,
     __half* keys, __half* values, int page_size, const int* __restrict__ tables, int table_stride,
     int* error) {
+  pdl_trigger();  // the next kernel may launch and wait for this one
+  pdl_wait();     // what the kernels before this one wrote is visible
   __shared__ float partial[32];
   __shared__ float row[256];
   const int slot = blockIdx.x, z = blockIdx.y, d = threadIdx.x;
@@ -160,6 +164,8 @@ __device__ __forceinline__ void visible(const AttentionArgs& a, const Query& que
 // spends its time waiting on the instruction cache).
 template <int D, int G>
 __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttentionArgs a) {
+  pdl_trigger();  // the next kernel may launch and wait for this one
+  pdl_wait();     // what the kernels before this one wrote is visible
   static_assert(D % 8 == 0 && D <= 2 * ATT_THREADS, "head width");
   constexpr int DIMS = (D + ATT_THREADS - 1) / ATT_THREADS;  // dimensions per thread
   constexpr int MAX_GROUP = G;
@@ -350,6 +356,8 @@ template <int D>
 __global__ void __launch_bounds__(ATT_THREADS) attention_join_kernel(const AttentionArgs a,
                                                                      const float* sinks,
                                                                      float* out) {
+  pdl_trigger();  // the next kernel may launch and wait for this one
+  pdl_wait();     // what the kernels before this one wrote is visible
   extern __shared__ float factor[];  // [splits]: e^(m_s - M), 0 for an empty split
   __shared__ float shared_total;
   const int head = blockIdx.x, t = blockIdx.y;
@@ -394,7 +402,8 @@ DRIFT_REGISTER(attention_inputs_f32, attention_inputs_kernel)
 
 template <int D, int G>
 int launch_split(const AttentionArgs& a, cudaStream_t stream) {
-  attention_split_kernel<D, G><<<dim3(a.splits, a.kv_heads, a.tokens), ATT_THREADS, 0, stream>>>(a);
+  DRIFT_CUDA(launch_pdl(attention_split_kernel<D, G>, dim3(a.splits, a.kv_heads, a.tokens),
+                        ATT_THREADS, 0, stream, a));
   DRIFT_LAUNCHED("attention_split");
   return 0;
 }
@@ -409,8 +418,8 @@ int launch_attention(const AttentionArgs& a, const float* sinks, float* out, cud
   else if (group <= 4) DRIFT_TRY((launch_split<D, 4>(a, stream)));
   else if (group <= 8) DRIFT_TRY((launch_split<D, 8>(a, stream)));
   else DRIFT_TRY((launch_split<D, 16>(a, stream)));
-  attention_join_kernel<D><<<dim3(a.q_heads, a.tokens), ATT_THREADS, a.splits * sizeof(float),
-                             stream>>>(a, sinks, out);
+  DRIFT_CUDA(launch_pdl(attention_join_kernel<D>, dim3(a.q_heads, a.tokens), ATT_THREADS,
+                        a.splits * sizeof(float), stream, a, sinks, out));
   DRIFT_LAUNCHED("attention_join");
   return 0;
 }
@@ -448,9 +457,9 @@ int drift_cache_write(const float* k, const float* v, int tokens, int kv_heads, 
   const long long total = (long long)tokens * kv_heads * head_dim;
   long long grid = (total + 255) / 256;
   if (grid > 4096) grid = 4096;
-  cache_write_kernel<<<unsigned(grid), 256, 0, cudaStream_t(stream)>>>(
-      k, v, static_cast<__half*>(keys), static_cast<__half*>(values), page_table, page_size,
-      kv_heads, head_dim, tokens, start);
+  DRIFT_CUDA(launch_pdl(cache_write_kernel, unsigned(grid), 256, 0, cudaStream_t(stream), k, v,
+                        static_cast<__half*>(keys), static_cast<__half*>(values), page_table,
+                        page_size, kv_heads, head_dim, tokens, start));
   DRIFT_LAUNCHED("cache_write");
   return 0;
 }
@@ -528,10 +537,11 @@ int drift_attention_inputs_decode(const float* q, const float* k, const float* v
     return invalid("attention inputs: a null tensor");
   if ((reinterpret_cast<uintptr_t>(keys) | reinterpret_cast<uintptr_t>(values)) & 15)
     return invalid("attention inputs: the cache does not start on a 16-byte boundary");
-  attention_inputs_kernel<<<dim3(q_heads + kv_heads, batch), 256, 0, cudaStream_t(stream)>>>(
-      q, k, v, q_heads, kv_heads, head_dim, q_norm, k_norm, epsilon, weight_offset, positions,
-      theta, rotary, layout, q_out, static_cast<__half*>(keys), static_cast<__half*>(values),
-      page_size, page_tables, table_stride, device_error_word());
+  DRIFT_CUDA(launch_pdl(attention_inputs_kernel, dim3(q_heads + kv_heads, batch), 256, 0,
+                        cudaStream_t(stream), q, k, v, q_heads, kv_heads, head_dim, q_norm, k_norm,
+                        epsilon, weight_offset, positions, theta, rotary, layout, q_out,
+                        static_cast<__half*>(keys), static_cast<__half*>(values), page_size,
+                        page_tables, table_stride, device_error_word()));
   DRIFT_LAUNCHED("attention_inputs");
   return 0;
 }

@@ -29,6 +29,8 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
                                                     int* __restrict__ ids,
                                                     float* __restrict__ weights, int tokens,
                                                     int experts, int k) {
+  pdl_trigger();  // the next kernel may launch and wait for this one
+  pdl_wait();     // what the kernels before this one wrote is visible
   const int t = blockIdx.x * (blockDim.x / WARP) + threadIdx.x / WARP;
   if (t >= tokens) return;
   const int lane = threadIdx.x % WARP;
@@ -126,6 +128,8 @@ __global__ void __launch_bounds__(256) experts_x22_kernel(
     const uint8_t* __restrict__ gate, const uint8_t* __restrict__ up, long long expert_bytes,
     const int* __restrict__ ids, const uint32_t* __restrict__ records, int divisor,
     float* __restrict__ y, int rows, int cols, long long experts, int* error) {
+  pdl_trigger();  // the next kernel may launch and wait for this one
+  pdl_wait();     // what the kernels before this one wrote is visible
   constexpr int GROUPS = 8 / KS;
   constexpr int ROWS = 4;  // rows per warp
   __shared__ float partial[8][ROWS][2];
@@ -199,14 +203,14 @@ static int launch_experts(const uint8_t* gate, const uint8_t* up, long long expe
   const dim3 grid(unsigned((rows + rows_per_cta - 1) / rows_per_cta), unsigned(slots));
   int* error = device_error_word();
   if (ks == 4)
-    experts_x22_kernel<T, 4, GATED><<<grid, 256, 0, stream>>>(gate, up, expert_bytes, ids, records,
-                                                              divisor, y, rows, cols, experts, error);
+    DRIFT_CUDA(launch_pdl(experts_x22_kernel<T, 4, GATED>, grid, 256, 0, stream, gate, up,
+                          expert_bytes, ids, records, divisor, y, rows, cols, experts, error));
   else if (ks == 2)
-    experts_x22_kernel<T, 2, GATED><<<grid, 256, 0, stream>>>(gate, up, expert_bytes, ids, records,
-                                                              divisor, y, rows, cols, experts, error);
+    DRIFT_CUDA(launch_pdl(experts_x22_kernel<T, 2, GATED>, grid, 256, 0, stream, gate, up,
+                          expert_bytes, ids, records, divisor, y, rows, cols, experts, error));
   else
-    experts_x22_kernel<T, 1, GATED><<<grid, 256, 0, stream>>>(gate, up, expert_bytes, ids, records,
-                                                              divisor, y, rows, cols, experts, error);
+    DRIFT_CUDA(launch_pdl(experts_x22_kernel<T, 1, GATED>, grid, 256, 0, stream, gate, up,
+                          expert_bytes, ids, records, divisor, y, rows, cols, experts, error));
   DRIFT_LAUNCHED("experts_x22");
   return 0;
 }
@@ -279,6 +283,8 @@ __global__ void __launch_bounds__(256) combine_kernel(
     const float* __restrict__ shared_router, const float* residual, float* out, int k, int hidden,
     const float* __restrict__ norm_weight, float* __restrict__ normed, float epsilon,
     float weight_offset) {
+  pdl_trigger();  // the next kernel may launch and wait for this one
+  pdl_wait();     // what the kernels before this one wrote is visible
   __shared__ float partial[32];
   const long long t = blockIdx.x;
   const float gate =
@@ -334,8 +340,8 @@ int drift_route(const float* logits, int32_t* ids, float* weights, int tokens, i
     return invalid("route: top-%d of %d", k, experts);
   if (tokens == 0) return 0;
   if (!logits || !ids || !weights) return invalid("route: a null tensor");
-  route_kernel<<<unsigned((tokens + 7) / 8), 256, 0, cudaStream_t(stream)>>>(logits, ids, weights,
-                                                                            tokens, experts, k);
+  DRIFT_CUDA(launch_pdl(route_kernel, unsigned((tokens + 7) / 8), 256, 0, cudaStream_t(stream),
+                        logits, ids, weights, tokens, experts, k));
   DRIFT_LAUNCHED("route_topk");
   return 0;
 }
@@ -362,9 +368,9 @@ int drift_moe_combine(const float* expert_out, const float* weights, int64_t tok
   DRIFT_TRY(check_combine(expert_out, weights, tokens, k, hidden, shared_out, shared_input,
                           shared_router, out));
   if (tokens == 0 || hidden == 0) return 0;
-  combine_kernel<false><<<unsigned(tokens), 256, 0, cudaStream_t(stream)>>>(
-      expert_out, weights, shared_out, shared_input, shared_router, residual, out, int(k),
-      int(hidden), nullptr, nullptr, 0.0f, 0.0f);
+  DRIFT_CUDA(launch_pdl(combine_kernel<false>, unsigned(tokens), 256, 0, cudaStream_t(stream),
+                        expert_out, weights, shared_out, shared_input, shared_router, residual, out,
+                        int(k), int(hidden), nullptr, nullptr, 0.0f, 0.0f));
   DRIFT_LAUNCHED("moe_combine");
   return 0;
 }
@@ -378,9 +384,10 @@ int drift_moe_combine_norm(const float* expert_out, const float* weights, int64_
                           shared_router, residual));
   if (tokens == 0 || hidden == 0) return 0;
   if (!norm_weight || !normed) return invalid("moeCombineNorm: no norm weight or output");
-  combine_kernel<true><<<unsigned(tokens), 256, 0, cudaStream_t(stream)>>>(
-      expert_out, weights, shared_out, shared_input, shared_router, residual, residual, int(k),
-      int(hidden), norm_weight, normed, epsilon, weight_offset);
+  DRIFT_CUDA(launch_pdl(combine_kernel<true>, unsigned(tokens), 256, 0, cudaStream_t(stream),
+                        expert_out, weights, shared_out, shared_input, shared_router, residual,
+                        residual, int(k), int(hidden), norm_weight, normed, epsilon,
+                        weight_offset));
   DRIFT_LAUNCHED("moe_combine_norm");
   return 0;
 }

@@ -46,6 +46,8 @@ __global__ void __launch_bounds__(256) gather_kernel(const uint8_t* __restrict__
                                                      const int* __restrict__ ids,
                                                      float* __restrict__ out, int count, int cols,
                                                      long long vocab, int* error) {
+  pdl_trigger();  // the next kernel may launch and wait for this one
+  pdl_wait();     // what the kernels before this one wrote is visible
   const int index = blockIdx.x * (blockDim.x / WARP) + threadIdx.x / WARP;
   if (index >= count) return;
   const int lane = threadIdx.x % WARP;
@@ -74,6 +76,8 @@ __global__ void __launch_bounds__(256) gather_kernel(const uint8_t* __restrict__
 __global__ void gather_rows_f32_kernel(const float* __restrict__ table, const int* __restrict__ ids,
                                        float* __restrict__ out, int count, int cols,
                                        long long vocab, int* error) {
+  pdl_trigger();  // the next kernel may launch and wait for this one
+  pdl_wait();     // what the kernels before this one wrote is visible
   const long long index = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (index >= (long long)count * cols) return;
   const long long id = ids[index / cols];
@@ -102,6 +106,8 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(float* __restrict__ x, co
                                                        const float* __restrict__ weight,
                                                        float* __restrict__ out, int cols,
                                                        float epsilon, float weight_offset) {
+  pdl_trigger();  // the next kernel may launch and wait for this one
+  pdl_wait();     // what the kernels before this one wrote is visible
   __shared__ float partial[32];
   float* row = x + (long long)blockIdx.x * cols;
   const float* add = y ? y + (long long)blockIdx.x * cols : nullptr;
@@ -145,6 +151,8 @@ __global__ void __launch_bounds__(256) rms_norm_long_kernel(float* __restrict__ 
                                                             const float* __restrict__ weight,
                                                             float* __restrict__ out, int cols,
                                                             float epsilon, float weight_offset) {
+  pdl_trigger();  // the next kernel may launch and wait for this one
+  pdl_wait();     // what the kernels before this one wrote is visible
   __shared__ float partial[32];
   float* row = x + (long long)blockIdx.x * cols;
   const float* add = y ? y + (long long)blockIdx.x * cols : nullptr;
@@ -169,17 +177,23 @@ int launch_rms_norm(float* x, const float* y, const float* weight, float* out, i
   const unsigned grid = unsigned(rows);
   const int c = int(cols);
   if (cols <= 256)
-    rms_norm_kernel<1><<<grid, 256, 0, stream>>>(x, y, weight, out, c, epsilon, weight_offset);
+    DRIFT_CUDA(launch_pdl(rms_norm_kernel<1>, grid, 256, 0, stream, x, y, weight, out, c, epsilon,
+                          weight_offset));
   else if (cols <= 512)
-    rms_norm_kernel<2><<<grid, 256, 0, stream>>>(x, y, weight, out, c, epsilon, weight_offset);
+    DRIFT_CUDA(launch_pdl(rms_norm_kernel<2>, grid, 256, 0, stream, x, y, weight, out, c, epsilon,
+                          weight_offset));
   else if (cols <= 1024)
-    rms_norm_kernel<4><<<grid, 256, 0, stream>>>(x, y, weight, out, c, epsilon, weight_offset);
+    DRIFT_CUDA(launch_pdl(rms_norm_kernel<4>, grid, 256, 0, stream, x, y, weight, out, c, epsilon,
+                          weight_offset));
   else if (cols <= 2048)
-    rms_norm_kernel<8><<<grid, 256, 0, stream>>>(x, y, weight, out, c, epsilon, weight_offset);
+    DRIFT_CUDA(launch_pdl(rms_norm_kernel<8>, grid, 256, 0, stream, x, y, weight, out, c, epsilon,
+                          weight_offset));
   else if (cols <= 4096)
-    rms_norm_kernel<16><<<grid, 256, 0, stream>>>(x, y, weight, out, c, epsilon, weight_offset);
+    DRIFT_CUDA(launch_pdl(rms_norm_kernel<16>, grid, 256, 0, stream, x, y, weight, out, c, epsilon,
+                          weight_offset));
   else
-    rms_norm_long_kernel<<<grid, 256, 0, stream>>>(x, y, weight, out, c, epsilon, weight_offset);
+    DRIFT_CUDA(launch_pdl(rms_norm_long_kernel, grid, 256, 0, stream, x, y, weight, out, c, epsilon,
+                          weight_offset));
   DRIFT_LAUNCHED("rms_norm_f32");
   return 0;
 }
@@ -193,6 +207,8 @@ DRIFT_REGISTER(rms_norm_long_f32, rms_norm_long_kernel)
        i += (long long)gridDim.x * blockDim.x)
 
 __global__ void add_kernel(const float* a, const float* b, float* out, long long n) {
+  pdl_trigger();  // the next kernel may launch and wait for this one
+  pdl_wait();     // what the kernels before this one wrote is visible
   DRIFT_FOR_EACH(i, n) out[i] = a[i] + b[i];
 }
 
@@ -211,6 +227,8 @@ __device__ __forceinline__ float activate(float v, int kind) {
 }
 
 __global__ void gated_kernel(const float* gate, const float* up, float* out, long long n, int kind) {
+  pdl_trigger();  // the next kernel may launch and wait for this one
+  pdl_wait();     // what the kernels before this one wrote is visible
   DRIFT_FOR_EACH(i, n) {
     const float u = kind == DRIFT_SITU ? 25.0f * tanhf(up[i] * 0.04f) : up[i];
     out[i] = activate(gate[i], kind) * u;
@@ -231,6 +249,8 @@ DRIFT_REGISTER(gated_f32, gated_kernel)
 __global__ void rope_kernel(const float* __restrict__ x, const int* __restrict__ positions,
                             float* __restrict__ out, int tokens, int heads, int head_dim,
                             int rotary, float theta, int layout) {
+  pdl_trigger();  // the next kernel may launch and wait for this one
+  pdl_wait();     // what the kernels before this one wrote is visible
   const long long index = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (index >= (long long)tokens * heads * head_dim) return;
   const int d = int(index % head_dim);
@@ -247,6 +267,8 @@ template <bool BF16>
 __global__ void __launch_bounds__(256) matvec_f32_kernel(const void* __restrict__ x,
                                                          const float* __restrict__ weight,
                                                          float* __restrict__ y, int m, int n, int k) {
+  pdl_trigger();  // the next kernel may launch and wait for this one
+  pdl_wait();     // what the kernels before this one wrote is visible
   const long long index = (long long)blockIdx.x * (blockDim.x / WARP) + threadIdx.x / WARP;
   if (index >= (long long)m * n) return;
   const int lane = threadIdx.x % WARP;
@@ -274,9 +296,11 @@ int matvec_f32_weights(int x_dtype, const void* x, const float* weight, float* y
   const long long warps = m * n;
   const unsigned grid = unsigned((warps + 7) / 8);
   if (x_dtype == DRIFT_BF16)
-    matvec_f32_kernel<true><<<grid, 256, 0, stream>>>(x, weight, y, int(m), int(n), int(k));
+    DRIFT_CUDA(launch_pdl(matvec_f32_kernel<true>, grid, 256, 0, stream, x, weight, y, int(m),
+                          int(n), int(k)));
   else
-    matvec_f32_kernel<false><<<grid, 256, 0, stream>>>(x, weight, y, int(m), int(n), int(k));
+    DRIFT_CUDA(launch_pdl(matvec_f32_kernel<false>, grid, 256, 0, stream, x, weight, y, int(m),
+                          int(n), int(k)));
   DRIFT_LAUNCHED("matvec_f32");
   return 0;
 }
@@ -326,16 +350,20 @@ int drift_embedding(int table_dtype, const void* table, int64_t vocab, int64_t c
   const uint8_t* t = static_cast<const uint8_t*>(table);
   if (table_dtype == DRIFT_F32) {
     const long long values = count * cols;
-    gather_rows_f32_kernel<<<unsigned((values + 255) / 256), 256, 0, s>>>(
-        static_cast<const float*>(table), ids, out, int(count), int(cols), vocab, error);
+    DRIFT_CUDA(launch_pdl(gather_rows_f32_kernel, unsigned((values + 255) / 256), 256, 0, s,
+                          static_cast<const float*>(table), ids, out, int(count), int(cols), vocab,
+                          error));
   } else {
     const unsigned grid = unsigned((count + 7) / 8);
     if (table_dtype == DRIFT_Q8_0)
-      gather_kernel<Q8_0T><<<grid, 256, 0, s>>>(t, ids, out, int(count), int(cols), vocab, error);
+      DRIFT_CUDA(launch_pdl(gather_kernel<Q8_0T>, grid, 256, 0, s, t, ids, out, int(count),
+                            int(cols), vocab, error));
     else if (table_dtype == DRIFT_Q4_0)
-      gather_kernel<Q4_0T><<<grid, 256, 0, s>>>(t, ids, out, int(count), int(cols), vocab, error);
+      DRIFT_CUDA(launch_pdl(gather_kernel<Q4_0T>, grid, 256, 0, s, t, ids, out, int(count),
+                            int(cols), vocab, error));
     else
-      gather_kernel<Q4_1T><<<grid, 256, 0, s>>>(t, ids, out, int(count), int(cols), vocab, error);
+      DRIFT_CUDA(launch_pdl(gather_kernel<Q4_1T>, grid, 256, 0, s, t, ids, out, int(count),
+                            int(cols), vocab, error));
   }
   DRIFT_LAUNCHED("gather");
   return 0;
@@ -373,7 +401,8 @@ int drift_add(const float* a, const float* b, float* out, int64_t n, drift_strea
   if (n < 0) return invalid("add over %lld values", (long long)n);
   if (n == 0) return 0;
   if (!a || !b || !out) return invalid("add: a null tensor");
-  add_kernel<<<elementwise_grid(n), 256, 0, cudaStream_t(stream)>>>(a, b, out, n);
+  DRIFT_CUDA(launch_pdl(add_kernel, elementwise_grid(n), 256, 0, cudaStream_t(stream), a, b, out,
+                        n));
   DRIFT_LAUNCHED("add_f32");
   return 0;
 }
@@ -384,7 +413,8 @@ int drift_gated(int kind, const float* gate, const float* up, float* out, int64_
   if (n < 0) return invalid("gated over %lld values", (long long)n);
   if (n == 0) return 0;
   if (!gate || !up || !out) return invalid("gated: a null tensor");
-  gated_kernel<<<elementwise_grid(n), 256, 0, cudaStream_t(stream)>>>(gate, up, out, n, kind);
+  DRIFT_CUDA(launch_pdl(gated_kernel, elementwise_grid(n), 256, 0, cudaStream_t(stream), gate, up,
+                        out, n, kind));
   DRIFT_LAUNCHED("gated_f32");
   return 0;
 }
@@ -401,8 +431,8 @@ int drift_rope(const float* x, const int32_t* positions, float* out, int tokens,
   const long long values = (long long)tokens * heads * head_dim;
   if (values == 0) return 0;
   if (!x || !positions || !out) return invalid("rope: a null tensor");
-  rope_kernel<<<unsigned((values + 255) / 256), 256, 0, cudaStream_t(stream)>>>(
-      x, positions, out, tokens, heads, head_dim, rotary, theta, layout);
+  DRIFT_CUDA(launch_pdl(rope_kernel, unsigned((values + 255) / 256), 256, 0, cudaStream_t(stream), x,
+                        positions, out, tokens, heads, head_dim, rotary, theta, layout));
   DRIFT_LAUNCHED("rope_f32");
   return 0;
 }

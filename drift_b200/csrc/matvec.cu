@@ -71,6 +71,8 @@ __device__ __forceinline__ void quantize_x22_block(const void* x, uint32_t* reco
 template <bool BF16>
 __global__ void __launch_bounds__(256) quantize_x22_kernel(const void* x, uint32_t* records,
                                                           long long blocks) {
+  pdl_trigger();  // the next kernel may launch and wait for this one
+  pdl_wait();     // what the kernels before this one wrote is visible
   const long long block = (long long)blockIdx.x * (blockDim.x / WARP) + threadIdx.x / WARP;
   if (block >= blocks) return;
   quantize_x22_block<BF16>(x, records, block);
@@ -216,6 +218,8 @@ __global__ void __launch_bounds__(256) matvec_x22_kernel(const uint8_t* __restri
                                                          const uint32_t* __restrict__ records,
                                                          float* __restrict__ y, int rows, int cols,
                                                          int vectors) {
+  pdl_trigger();  // the next kernel may launch and wait for this one
+  pdl_wait();     // what the kernels before this one wrote is visible
   constexpr int GROUPS = 8 / KS;  // row groups per CTA
   __shared__ float partial[8][ROWS_PER_GROUP][V];
   const int warp = threadIdx.x / WARP, lane = threadIdx.x % WARP;
@@ -268,6 +272,8 @@ __global__ void __launch_bounds__(256) matvec_mma_kernel(const uint8_t* __restri
                                                          const uint8_t* __restrict__ records,
                                                          float* __restrict__ y, int rows, int cols,
                                                          int vectors) {
+  pdl_trigger();  // the next kernel may launch and wait for this one
+  pdl_wait();     // what the kernels before this one wrote is visible
   constexpr int GROUPS = 8 / KS;
   constexpr int ROWS = 16 * MT;
   __shared__ float partial[KS][GROUPS][ROWS][8];
@@ -422,9 +428,9 @@ int prepare_x(int x_dtype, const void* x, int64_t m, int64_t k, uint32_t* record
   if (blocks == 0) return 0;
   const unsigned grid = unsigned((blocks + 7) / 8);
   if (x_dtype == DRIFT_BF16)
-    quantize_x22_kernel<true><<<grid, 256, 0, stream>>>(x, records, blocks);
+    DRIFT_CUDA(launch_pdl(quantize_x22_kernel<true>, grid, 256, 0, stream, x, records, blocks));
   else
-    quantize_x22_kernel<false><<<grid, 256, 0, stream>>>(x, records, blocks);
+    DRIFT_CUDA(launch_pdl(quantize_x22_kernel<false>, grid, 256, 0, stream, x, records, blocks));
   DRIFT_LAUNCHED("quantize_x22");
   return 0;
 }
@@ -439,11 +445,14 @@ static int launch_matvec_v(const uint8_t* weight, const uint32_t* records, float
   const int rows_per_cta = ROWS_PER_GROUP * 8 / ks;
   const unsigned grid = unsigned((rows + rows_per_cta - 1) / rows_per_cta);
   if (ks == 4)
-    matvec_x22_kernel<T, V, 4><<<grid, 256, 0, stream>>>(weight, records, y, rows, cols, vectors);
+    DRIFT_CUDA(launch_pdl(matvec_x22_kernel<T, V, 4>, grid, 256, 0, stream, weight, records, y, rows,
+                          cols, vectors));
   else if (ks == 2)
-    matvec_x22_kernel<T, V, 2><<<grid, 256, 0, stream>>>(weight, records, y, rows, cols, vectors);
+    DRIFT_CUDA(launch_pdl(matvec_x22_kernel<T, V, 2>, grid, 256, 0, stream, weight, records, y, rows,
+                          cols, vectors));
   else
-    matvec_x22_kernel<T, V, 1><<<grid, 256, 0, stream>>>(weight, records, y, rows, cols, vectors);
+    DRIFT_CUDA(launch_pdl(matvec_x22_kernel<T, V, 1>, grid, 256, 0, stream, weight, records, y, rows,
+                          cols, vectors));
   DRIFT_LAUNCHED("matvec_x22");
   return 0;
 }
@@ -459,16 +468,20 @@ static int launch_mma(const uint8_t* weight, const uint8_t* records, float* y, i
   while (ks < 4 && groups32 * ks < 8LL * sm_count() && blocks / (ks * 2) >= 8) ks *= 2;
   if (rows <= 2048 && blocks >= 64) {
     const unsigned grid = unsigned((rows + 16 - 1) / 16);  // MT 1, 8 k-splits, 16 rows per CTA
-    matvec_mma_kernel<T, 1, 8><<<grid, 256, 0, stream>>>(weight, records, y, rows, cols, vectors);
+    DRIFT_CUDA(launch_pdl(matvec_mma_kernel<T, 1, 8>, grid, 256, 0, stream, weight, records, y, rows,
+                          cols, vectors));
   } else if (ks == 4) {
     const unsigned grid = unsigned((rows + 64 - 1) / 64);
-    matvec_mma_kernel<T, 2, 4><<<grid, 256, 0, stream>>>(weight, records, y, rows, cols, vectors);
+    DRIFT_CUDA(launch_pdl(matvec_mma_kernel<T, 2, 4>, grid, 256, 0, stream, weight, records, y, rows,
+                          cols, vectors));
   } else if (ks == 2) {
     const unsigned grid = unsigned((rows + 128 - 1) / 128);
-    matvec_mma_kernel<T, 2, 2><<<grid, 256, 0, stream>>>(weight, records, y, rows, cols, vectors);
+    DRIFT_CUDA(launch_pdl(matvec_mma_kernel<T, 2, 2>, grid, 256, 0, stream, weight, records, y, rows,
+                          cols, vectors));
   } else {
     const unsigned grid = unsigned((rows + 256 - 1) / 256);
-    matvec_mma_kernel<T, 2, 1><<<grid, 256, 0, stream>>>(weight, records, y, rows, cols, vectors);
+    DRIFT_CUDA(launch_pdl(matvec_mma_kernel<T, 2, 1>, grid, 256, 0, stream, weight, records, y, rows,
+                          cols, vectors));
   }
   DRIFT_LAUNCHED("matvec_mma");
   return 0;
