@@ -79,6 +79,7 @@ SIGNATURES = {
                                       _p, _p]),
     "drift_workspace_reserve": (_i32, [_sz]),
     "drift_linear_workspace_bytes": (_sz, [_i64, _i64]),
+    "drift_attention_workspace_bytes": (_sz, [_i32, _i32, _i32, _i32]),
     "drift_device_error_take": (_i32, [ctypes.POINTER(ctypes.c_int)]),
     "drift_linear_static": (_i32, [_i32, _p, _i32, _p, _p, _i64, _i64, _i64, _p]),
     "drift_cache_write": (_i32, [_p, _p, _i32, _i32, _i32, _p, _p, _i32, _i32, _p, _i32, _i32, _p]),

@@ -6,12 +6,15 @@
 // contiguous within a page.
 //
 // attention is split-K ("flash decoding"): a CTA takes one key head, the
-// query heads that share it (q_heads / kv_heads of them) and 128 consecutive
-// keys -- a thread per key for the scores, a thread per dimension for the
-// weighted values -- and leaves, per query head, the largest score, the sum
-// of exp(score - largest) and the unnormalised weighted sum. A second kernel
-// joins the splits (and the sink, if any) per query head. Scores and sums in
-// F32 (the CPU reference accumulates in Double; BASELINE's tolerance applies).
+// query heads that share it (q_heads / kv_heads of them, at most 16: one
+// 16-row tensor-core tile) and 128 consecutive keys (64 for 256-wide heads),
+// brings the keys and values into shared memory in one round of asynchronous
+// copies, forms scores and weighted values with mma.sync on F16 operands
+// (q and the weights as two F16 terms each, so the sums are F32-grade), and
+// leaves, per query head, the largest score, the sum of exp(score - largest)
+// and the unnormalised weighted sum. A second kernel joins the splits (and
+// the sink, if any) per query head. Scores and sums in F32 (the CPU
+// reference accumulates in Double; the 1e-4 + 1e-3 |e| tolerance applies).
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -26,8 +29,8 @@ int* device_error_word();
 
 namespace {
 
-constexpr int ATT_THREADS = 128;
-constexpr int KEYS = 128;       // keys a split takes
+constexpr int ATT_THREADS = 128;    // the join's threads
+constexpr int SPLIT_THREADS = 256;  // the splits' threads: 8 warps
 constexpr int MAX_GROUP = 16;   // query heads per key head, at most
 
 __device__ __forceinline__ int64_t key_index(const int* table, int page_size, int kv_heads, int dim,
@@ -159,194 +162,309 @@ __device__ __forceinline__ void visible(const AttentionArgs& a, const Query& que
   if (a.window > 0 && query.position - a.window + 1 > lo) lo = query.position - a.window + 1;
 }
 
-// G: query heads per key head, a template so that the unrolled loops hold
-// exactly the heads there are (a kernel unrolled for 16 heads but running 4
-// spends its time waiting on the instruction cache).
-template <int D, int G>
-__global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttentionArgs a) {
+// A split's tile: KEYS keys of one key head against the (up to 16) query
+// heads that share it, as 16-row tensor-core tiles (mma.sync m16n8k16, F16
+// operands, F32 sums). The keys and values are F16 in the cache, so they are
+// exact operands; q and the weights p are F32, so each goes in as two F16
+// terms, hi = f16(x) and lo = f16(x - hi), whose sum holds x to about 2^-22:
+// a score is q_hi.k + q_lo.k and an output p_hi.v + p_lo.v, F32 throughout
+// after that.
+//
+// Shared memory: the key rows ([KEYS][D] halves), the value columns
+// ([D][KEYS] halves -- the cache's own order within a page), then the q
+// fragments, later reused for the p fragments. A fragment load reads one
+// 16-byte chunk from each of eight consecutive rows, so chunk c of row r sits
+// at chunk c ^ (r mod 8) of its row: the eight reads land on distinct banks.
+// (80-wide key rows, ten chunks, are padded by a chunk instead.)
+template <int D>
+struct SplitTile {
+  static constexpr int KEYS = D > 128 ? 64 : 128;  // keys of a split
+  static constexpr int WARPS = SPLIT_THREADS / 32;
+  static constexpr int QW = KEYS / 16;             // warps that score: 16 keys each
+  static constexpr int NT = 2;                     // 8-key tiles of a warp's scores
+  static constexpr int KQ = D / 16;                // k-steps of q.k
+  static constexpr int KP = KEYS / 16;             // k-steps of p.v
+  static constexpr int ND = D / 8;                 // 8-wide dimension tiles of p.v
+  static constexpr int CH = D / 8;                 // 16-byte chunks of a key row
+  static constexpr int RUNS = KEYS / 8;            // 16-byte chunks of a value column
+  static constexpr bool KEY_SWIZZLE = CH % 8 == 0;
+  static constexpr int KPITCH = KEY_SWIZZLE ? 2 * D : 2 * D + 16;
+  static constexpr int VPITCH = 2 * KEYS;
+  static constexpr int K_BYTES = KEYS * KPITCH;
+  static constexpr int V_BYTES = D * VPITCH;
+  static constexpr int QF_BYTES = KQ * 2 * 32 * 16;
+  static constexpr int PF_BYTES = KP * 2 * 32 * 16;
+  static constexpr int BYTES = K_BYTES + V_BYTES + (QF_BYTES > PF_BYTES ? QF_BYTES : PF_BYTES);
+  // byte offsets of chunk c of key row k, and of run r of value column d
+  __device__ static int key_chunk(int k, int c) {
+    return k * KPITCH + 16 * (KEY_SWIZZLE ? c ^ (k & 7) : c);
+  }
+  __device__ static int value_chunk(int d, int r) { return d * VPITCH + 16 * (r ^ (d & 7)); }
+  static_assert(RUNS % 8 == 0, "value columns of whole 8-chunk groups");
+};
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* global) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(smem))),
+               "l"(global)
+               : "memory");
+}
+
+__device__ __forceinline__ void mma_f16(float (&c)[4], const uint4& a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
+}
+
+// The two F16 terms of a pair of F32 values, packed as (first, second).
+__device__ __forceinline__ void split_pair(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
+  const __half l0 = __float2half_rn(x0 - __half2float(h0));
+  const __half l1 = __float2half_rn(x1 - __half2float(h1));
+  const __half2 h = __halves2half2(h0, h1), l = __halves2half2(l0, l1);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+// Warp w < KEYS / 16 scores keys [16 w, 16 w + 16) of the split for all 16
+// query rows; after the softmax statistics meet in shared memory, it writes
+// those keys' weights as one A fragment of the p.v product, and then each of
+// the 8 warps takes an eighth of the dimensions of p.v over all of the
+// split's keys. Positions outside the visible range are never read from the
+// cache: their scores are -inf and their value columns zeros.
+template <int D>
+__global__ void __launch_bounds__(SPLIT_THREADS) attention_split_kernel(const AttentionArgs a) {
   pdl_trigger();  // the next kernel may launch and wait for this one
   pdl_wait();     // what the kernels before this one wrote is visible
-  static_assert(D % 8 == 0 && D <= 2 * ATT_THREADS, "head width");
-  constexpr int DIMS = (D + ATT_THREADS - 1) / ATT_THREADS;  // dimensions per thread
-  constexpr int MAX_GROUP = G;
-  __shared__ float qs[MAX_GROUP][D];
-  __shared__ float ws[MAX_GROUP][KEYS];
-  __shared__ float reduce[MAX_GROUP][ATT_THREADS / 32];
-  const int split = blockIdx.x, head = blockIdx.y, t = blockIdx.z;
-  const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
-  const int group = a.q_heads / a.kv_heads;  // <= G
-  const Query query(a, t);
+  using T = SplitTile<D>;
+  constexpr int KEYS = T::KEYS;
+  extern __shared__ __align__(16) uint8_t tile[];
+  uint8_t* ks = tile;
+  uint8_t* vs = tile + T::K_BYTES;
+  uint4* frags = reinterpret_cast<uint4*>(tile + T::K_BYTES + T::V_BYTES);  // [k-step][hi, lo][lane]
+  __shared__ float red_max[T::QW][16], red_sum[T::QW][16];
+  const int split = blockIdx.x, head = blockIdx.y, z = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32, g = lane / 4, t = lane % 4;
+  const int group = a.q_heads / a.kv_heads;  // <= 16
+  const Query query(a, z);
   int lo, hi;
   visible(a, query, lo, hi);
   const int k0 = split * KEYS;
   const int first = k0 > lo ? k0 : lo, last = k0 + KEYS < hi ? k0 + KEYS : hi;  // [first, last)
+  const int ps = a.page_size;
 
-  // the chunk's pages, looked up once
-  __shared__ int pages[KEYS / 16 + 2];
-  const int page0 = k0 / a.page_size;
-  if (tid < KEYS / 16 + 2) {
-    const int p = page0 + tid;
-    pages[tid] = (long long)p * a.page_size < query.key_count ? query.table[p] : 0;
-  }
-  for (int i = tid; i < group * D; i += ATT_THREADS)
-    qs[i / D][i % D] = a.q[((long long)t * a.q_heads + head * group + i / D) * D + i % D];
-  __syncthreads();
-
-  // scores: a thread per key, the key row read in slices of 64 values with
-  // every load of a slice issued before its first use
-  const int key = k0 + tid;
-  const bool seen = key >= first && key < last;
-  float score[MAX_GROUP];
-#pragma unroll
-  for (int g = 0; g < MAX_GROUP; ++g) score[g] = 0.0f;
-  if (seen) {
-    const long long page = pages[key / a.page_size - page0];
-    const uint4* row = reinterpret_cast<const uint4*>(
-        a.keys + ((page * a.page_size + key % a.page_size) * a.kv_heads + head) * D);
-#pragma unroll
-    for (int slice = 0; slice < (D + 63) / 64; ++slice) {
-      constexpr int PER = D < 64 ? D / 8 : 8;
-      uint4 raw[PER];
-#pragma unroll
-      for (int c = 0; c < PER; ++c) raw[c] = slice * 8 + c < D / 8 ? row[slice * 8 + c] : make_uint4(0, 0, 0, 0);
-#pragma unroll
-      for (int c = 0; c < PER; ++c) {
-        if (slice * 8 + c >= D / 8) break;
-        const __half2* h2 = reinterpret_cast<const __half2*>(&raw[c]);
-        float kv[8];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f = __half22float2(h2[i]);
-          kv[2 * i] = f.x;
-          kv[2 * i + 1] = f.y;
-        }
-#pragma unroll
-        for (int g = 0; g < MAX_GROUP; ++g) {
-          if (g < group) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              score[g] = fmaf(qs[g][8 * (slice * 8 + c) + i], kv[i], score[g]);
-          }
-        }
-      }
+  // where each visible key's row and each whole visible run of 8 value
+  // positions starts in the cache, in 16-byte units (a page is looked up
+  // once per key, not once per copy)
+  __shared__ unsigned key_at[KEYS], run_at[T::RUNS];
+  __shared__ bool run_whole[T::RUNS];
+  constexpr unsigned NONE = 0xffffffffu;
+  if (tid < KEYS) {
+    const int key = k0 + tid;
+    unsigned at = NONE;
+    if (key >= first && key < last) {
+      const long long page = query.table[key / ps];
+      at = unsigned((((page * ps + key % ps) * a.kv_heads + head) * D) / 8);
     }
+    key_at[tid] = at;
   }
-  float largest[MAX_GROUP];
-#pragma unroll
-  for (int g = 0; g < MAX_GROUP; ++g) {
-    float s = score[g] * a.scale;
-    if (a.has_softcap) s = a.softcap * tanhf(s / a.softcap);
-    score[g] = seen ? s : -INFINITY;
-    float m = score[g];
-#pragma unroll
-    for (int o = 16; o > 0; o /= 2) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0 && g < group) reduce[g][warp] = m;
+  if (tid < T::RUNS) {
+    const int key = k0 + 8 * tid;
+    const bool whole = key >= first && key + 8 <= last;
+    run_whole[tid] = whole;
+    run_at[tid] = whole ? unsigned((((long long)query.table[key / ps] * a.kv_heads + head) * D *
+                                        ps + key % ps) / 8)
+                        : NONE;
   }
-  __syncthreads();
-#pragma unroll
-  for (int g = 0; g < MAX_GROUP; ++g) {
-    float m = -INFINITY;
-    if (g < group) {
-#pragma unroll
-      for (int w = 0; w < ATT_THREADS / 32; ++w) m = fmaxf(m, reduce[g][w]);
+  // q as A fragments, hi and lo: rows past the group are zeros
+  const float* q = a.q + ((long long)z * a.q_heads + head * group) * D;
+  for (int i = tid; i < T::KQ * 32; i += SPLIT_THREADS) {
+    const int kk = i / 32, l = i % 32, row = l / 4, col = 16 * kk + 2 * (l % 4);
+    float2 v[4] = {};
+    if (row < group) {
+      v[0] = make_float2(q[row * D + col], q[row * D + col + 1]);
+      v[2] = make_float2(q[row * D + col + 8], q[row * D + col + 9]);
     }
-    largest[g] = m;
-  }
-  __syncthreads();
-#pragma unroll
-  for (int g = 0; g < MAX_GROUP; ++g) {
-    const float w = seen && g < group ? expf(score[g] - largest[g]) : 0.0f;
-    if (g < group) ws[g][tid] = w;
-    float s = w;
-#pragma unroll
-    for (int o = 16; o > 0; o /= 2) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if (lane == 0 && g < group) reduce[g][warp] = s;
+    if (row + 8 < group) {
+      v[1] = make_float2(q[(row + 8) * D + col], q[(row + 8) * D + col + 1]);
+      v[3] = make_float2(q[(row + 8) * D + col + 8], q[(row + 8) * D + col + 9]);
+    }
+    uint4 h, w;
+    split_pair(v[0].x, v[0].y, h.x, w.x);
+    split_pair(v[1].x, v[1].y, h.y, w.y);
+    split_pair(v[2].x, v[2].y, h.z, w.z);
+    split_pair(v[3].x, v[3].y, h.w, w.w);
+    frags[(kk * 2) * 32 + l] = h;
+    frags[(kk * 2 + 1) * 32 + l] = w;
   }
   __syncthreads();
 
-  // weighted values: a thread per dimension (two for D = 256)
-  float acc[MAX_GROUP][DIMS];
+  // keys (an invisible key's row is left as it is: its score is never used)
+#pragma unroll 4
+  for (int i = tid; i < KEYS * T::CH; i += SPLIT_THREADS) {
+    const int k = i / T::CH, c = i % T::CH;
+    const unsigned at = key_at[k];
+    if (at != NONE) cp_async16(ks + T::key_chunk(k, c), a.keys + 8 * ((long long)at + c));
+  }
+  // values, a 16-byte run of 8 positions of one dimension at a time (a run
+  // never crosses a page: pages are multiples of 16 positions)
+  const long long column = ps / 8;  // 16-byte units from one dimension to the next
+#pragma unroll 4
+  for (int i = tid; i < D * T::RUNS; i += SPLIT_THREADS) {
+    const int d = i / T::RUNS, r = i % T::RUNS;
+    uint8_t* to = vs + T::value_chunk(d, r);
+    if (run_whole[r]) {
+      cp_async16(to, a.values + 8 * (run_at[r] + d * column));
+    } else {
+      // a run the visible range cuts or misses: its visible positions one
+      // by one, zeros elsewhere (an invisible position's weight is 0, and
+      // 0 times whatever the cache holds there must not reach the sum)
+      const int key = k0 + 8 * r;
+      __align__(16) __half run[8];
 #pragma unroll
-  for (int g = 0; g < MAX_GROUP; ++g)
-#pragma unroll
-    for (int j = 0; j < DIMS; ++j) acc[g][j] = 0.0f;
-  const bool whole = first == k0 && last == k0 + KEYS;  // a full chunk: 16 runs of 8 keys
-#pragma unroll
-  for (int j = 0; j < DIMS; ++j) {
-    const int d = tid + j * ATT_THREADS;
-    if (d >= D) continue;
-    if (whole) {
-      uint4 raw[KEYS / 8];
-#pragma unroll
-      for (int r = 0; r < KEYS / 8; ++r) {
-        const int p = k0 + 8 * r;
-        const long long page = pages[p / a.page_size - page0];  // within the chunk's pages
-        raw[r] = *reinterpret_cast<const uint4*>(
-            a.values + ((page * a.kv_heads + head) * D + d) * a.page_size + p % a.page_size);
-      }
-#pragma unroll
-      for (int r = 0; r < KEYS / 8; ++r) {
-        const __half2* h2 = reinterpret_cast<const __half2*>(&raw[r]);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f = __half22float2(h2[i]);
-#pragma unroll
-          for (int g = 0; g < MAX_GROUP; ++g) {
-            if (g < group) {
-              acc[g][j] = fmaf(ws[g][8 * r + 2 * i], f.x, acc[g][j]);
-              acc[g][j] = fmaf(ws[g][8 * r + 2 * i + 1], f.y, acc[g][j]);
-            }
-          }
+      for (int j = 0; j < 8; ++j) {
+        const int p = key + j;
+        run[j] = __float2half_rn(0.0f);
+        if (p >= first && p < last) {
+          const long long page = query.table[p / ps];
+          run[j] = a.values[((page * a.kv_heads + head) * D + d) * ps + p % ps];
         }
       }
-      continue;
+      *reinterpret_cast<uint4*>(to) = *reinterpret_cast<const uint4*>(run);
     }
-    int p = first;
-    // eight keys at a time where they share a page and start on an 8-key
-    // boundary (a 16-byte run of one value column)
-    while (p < last) {
-      if (p % 8 == 0 && p + 8 <= last && (p % a.page_size) + 8 <= a.page_size) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(
-            a.values + value_index(query.table, a.page_size, a.kv_heads, D, p, head, d));
-        const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+  }
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_all;" ::: "memory");
+  __syncthreads();
+
+  // scores of this warp's keys: s[j] holds rows (g, g + 8), keys
+  // 16 warp + 8 j + (2t, 2t + 1)
+  const bool scoring = warp < T::QW;
+  float s[T::NT][4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f = __half22float2(h2[i]);
+  for (int j = 0; j < T::NT; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
 #pragma unroll
-          for (int g = 0; g < MAX_GROUP; ++g) {
-            if (g < group) {
-              acc[g][j] = fmaf(ws[g][p - k0 + 2 * i], f.x, acc[g][j]);
-              acc[g][j] = fmaf(ws[g][p - k0 + 2 * i + 1], f.y, acc[g][j]);
-            }
-          }
-        }
-        p += 8;
-      } else {
-        const float f = __half2float(
-            a.values[value_index(query.table, a.page_size, a.kv_heads, D, p, head, d)]);
+  for (int kk = 0; kk < T::KQ; ++kk) {
+    if (!scoring) break;
+    const uint4 qh = frags[(kk * 2) * 32 + lane], ql = frags[(kk * 2 + 1) * 32 + lane];
 #pragma unroll
-        for (int g = 0; g < MAX_GROUP; ++g)
-          if (g < group) acc[g][j] = fmaf(ws[g][p - k0], f, acc[g][j]);
-        ++p;
-      }
+    for (int j = 0; j < T::NT; ++j) {
+      const int k = 16 * warp + 8 * j + g;
+      const uint32_t b0 = *reinterpret_cast<const uint32_t*>(ks + T::key_chunk(k, 2 * kk) + 4 * t);
+      const uint32_t b1 =
+          *reinterpret_cast<const uint32_t*>(ks + T::key_chunk(k, 2 * kk + 1) + 4 * t);
+      mma_f16(s[j], qh, b0, b1);
+      mma_f16(s[j], ql, b0, b1);
+    }
+  }
+  float m_lo = -INFINITY, m_hi = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < T::NT; ++j) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int key = k0 + 16 * warp + 8 * j + 2 * t + (e & 1);
+      float v = s[j][e] * a.scale;
+      if (a.has_softcap) v = a.softcap * tanhf(v / a.softcap);
+      v = key >= first && key < last ? v : -INFINITY;
+      s[j][e] = v;
+      if (e < 2) m_lo = fmaxf(m_lo, v);
+      else m_hi = fmaxf(m_hi, v);
     }
   }
 #pragma unroll
-  for (int g = 0; g < MAX_GROUP; ++g) {
-    if (g >= group) break;
-    const long long at = ((long long)t * a.q_heads + head * group + g) * a.splits + split;
+  for (int o = 1; o < 4; o *= 2) {
+    m_lo = fmaxf(m_lo, __shfl_xor_sync(0xffffffffu, m_lo, o));
+    m_hi = fmaxf(m_hi, __shfl_xor_sync(0xffffffffu, m_hi, o));
+  }
+  if (scoring && t == 0) {
+    red_max[warp][g] = m_lo;
+    red_max[warp][g + 8] = m_hi;
+  }
+  __syncthreads();  // every warp is past its q fragments too
+  float largest_lo = -INFINITY, largest_hi = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < DIMS; ++j) {
-      const int d = tid + j * ATT_THREADS;
-      if (d < D) a.part_o[at * D + d] = acc[g][j];
-    }
-    if (tid == 0) {
-      float total = 0.0f;
+  for (int w = 0; w < T::QW; ++w) {
+    largest_lo = fmaxf(largest_lo, red_max[w][g]);
+    largest_hi = fmaxf(largest_hi, red_max[w][g + 8]);
+  }
+  float sum_lo = 0.0f, sum_hi = 0.0f;
 #pragma unroll
-      for (int w = 0; w < ATT_THREADS / 32; ++w) total += reduce[g][w];
-      a.part_ml[at * 2] = largest[g];
-      a.part_ml[at * 2 + 1] = total;
+  for (int j = 0; j < T::NT; ++j) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float m = e < 2 ? largest_lo : largest_hi;
+      const float p = s[j][e] == -INFINITY ? 0.0f : expf(s[j][e] - m);
+      s[j][e] = p;
+      if (e < 2) sum_lo += p;
+      else sum_hi += p;
     }
+  }
+#pragma unroll
+  for (int o = 1; o < 4; o *= 2) {
+    sum_lo += __shfl_xor_sync(0xffffffffu, sum_lo, o);
+    sum_hi += __shfl_xor_sync(0xffffffffu, sum_hi, o);
+  }
+  if (scoring) {
+    if (t == 0) {
+      red_sum[warp][g] = sum_lo;
+      red_sum[warp][g + 8] = sum_hi;
+    }
+    // this warp's weights as the A fragment of k-step `warp` (the score
+    // tiles 0 and 1 are exactly a 16-key A fragment, lane for lane)
+    uint4 h, w;
+    split_pair(s[0][0], s[0][1], h.x, w.x);
+    split_pair(s[0][2], s[0][3], h.y, w.y);
+    split_pair(s[1][0], s[1][1], h.z, w.z);
+    split_pair(s[1][2], s[1][3], h.w, w.w);
+    frags[(warp * 2) * 32 + lane] = h;
+    frags[(warp * 2 + 1) * 32 + lane] = w;
+  }
+  __syncthreads();
+
+  // p.v for this warp's dimension tiles [ND w / 8, ND (w + 1) / 8)
+  constexpr int MAXN = (T::ND + T::WARPS - 1) / T::WARPS;
+  const int n0 = T::ND * warp / T::WARPS, n1 = T::ND * (warp + 1) / T::WARPS;
+  float o[MAXN][4];
+#pragma unroll
+  for (int n = 0; n < MAXN; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+#pragma unroll
+  for (int kk = 0; kk < T::KP; ++kk) {
+    const uint4 ph = frags[(kk * 2) * 32 + lane], pl = frags[(kk * 2 + 1) * 32 + lane];
+#pragma unroll
+    for (int n = 0; n < MAXN; ++n) {
+      if (n0 + n < n1) {
+        const int d = 8 * (n0 + n) + g;
+        const uint32_t b0 =
+            *reinterpret_cast<const uint32_t*>(vs + T::value_chunk(d, 2 * kk) + 4 * t);
+        const uint32_t b1 =
+            *reinterpret_cast<const uint32_t*>(vs + T::value_chunk(d, 2 * kk + 1) + 4 * t);
+        mma_f16(o[n], ph, b0, b1);
+        mma_f16(o[n], pl, b0, b1);
+      }
+    }
+  }
+  const long long at0 = ((long long)z * a.q_heads + head * group) * a.splits + split;
+#pragma unroll
+  for (int n = 0; n < MAXN; ++n) {
+    if (n0 + n >= n1) break;
+    const int d = 8 * (n0 + n) + 2 * t;
+    if (g < group)
+      *reinterpret_cast<float2*>(a.part_o + (at0 + (long long)g * a.splits) * D + d) =
+          make_float2(o[n][0], o[n][1]);
+    if (g + 8 < group)
+      *reinterpret_cast<float2*>(a.part_o + (at0 + (long long)(g + 8) * a.splits) * D + d) =
+          make_float2(o[n][2], o[n][3]);
+  }
+  if (tid < group) {
+    float largest = -INFINITY, total = 0.0f;
+#pragma unroll
+    for (int w = 0; w < T::QW; ++w) {
+      largest = fmaxf(largest, red_max[w][tid]);
+      total += red_sum[w][tid];
+    }
+    a.part_ml[(at0 + (long long)tid * a.splits) * 2] = largest;
+    a.part_ml[(at0 + (long long)tid * a.splits) * 2 + 1] = total;
   }
 }
 
@@ -383,15 +501,23 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_join_kernel(const Atten
   __syncthreads();
   const float total = shared_total;
   for (int d = threadIdx.x; d < D; d += ATT_THREADS) {
+    // eight splits' loads in flight at a time, summed in split order
     float sum = 0.0f;
-    for (int s = 0; s < a.splits; ++s)
-      if (factor[s] > 0.0f) sum += a.part_o[(base + s) * D + d] * factor[s];
+    for (int s0 = 0; s0 < a.splits; s0 += 8) {
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        o[j] = s0 + j < a.splits ? a.part_o[(base + s0 + j) * D + d] : 0.0f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (s0 + j < a.splits && factor[s0 + j] > 0.0f) sum += o[j] * factor[s0 + j];
+    }
     out[((long long)t * a.q_heads + head) * D + d] = total > 0.0f ? sum / total : 0.0f;
   }
 }
 
 #define DRIFT_ATTENTION_REGISTER(D)                                                   \
-  DRIFT_REGISTER(attention_split_d##D##_g4, (attention_split_kernel<D, 4>))           \
+  DRIFT_REGISTER(attention_split_d##D, attention_split_kernel<D>)                      \
   DRIFT_REGISTER(attention_join_d##D, attention_join_kernel<D>)
 DRIFT_ATTENTION_REGISTER(64)
 DRIFT_ATTENTION_REGISTER(80)
@@ -400,29 +526,32 @@ DRIFT_ATTENTION_REGISTER(256)
 DRIFT_REGISTER(cache_write_f16, cache_write_kernel)
 DRIFT_REGISTER(attention_inputs_f32, attention_inputs_kernel)
 
-template <int D, int G>
-int launch_split(const AttentionArgs& a, cudaStream_t stream) {
-  DRIFT_CUDA(launch_pdl(attention_split_kernel<D, G>, dim3(a.splits, a.kv_heads, a.tokens),
-                        ATT_THREADS, 0, stream, a));
-  DRIFT_LAUNCHED("attention_split");
-  return 0;
-}
-
 template <int D>
 int launch_attention(const AttentionArgs& a, const float* sinks, float* out, cudaStream_t stream) {
-  // the key head's query heads, padded up to the next kernel's count (the
-  // padding heads' scores are computed and dropped)
-  const int group = a.q_heads / a.kv_heads;
-  if (group <= 1) DRIFT_TRY((launch_split<D, 1>(a, stream)));
-  else if (group <= 2) DRIFT_TRY((launch_split<D, 2>(a, stream)));
-  else if (group <= 4) DRIFT_TRY((launch_split<D, 4>(a, stream)));
-  else if (group <= 8) DRIFT_TRY((launch_split<D, 8>(a, stream)));
-  else DRIFT_TRY((launch_split<D, 16>(a, stream)));
+  static bool configured = false;
+  if (!configured) {
+    DRIFT_CUDA(cudaFuncSetAttribute(attention_split_kernel<D>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    SplitTile<D>::BYTES));
+    // all of L1 as shared memory, so that two or more splits share an SM
+    DRIFT_CUDA(cudaFuncSetAttribute(attention_split_kernel<D>,
+                                    cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+    configured = true;
+  }
+  DRIFT_CUDA(launch_pdl(attention_split_kernel<D>, dim3(a.splits, a.kv_heads, a.tokens),
+                        SPLIT_THREADS, SplitTile<D>::BYTES, stream, a));
+  DRIFT_LAUNCHED("attention_split");
   DRIFT_CUDA(launch_pdl(attention_join_kernel<D>, dim3(a.q_heads, a.tokens), ATT_THREADS,
                         a.splits * sizeof(float), stream, a, sinks, out));
   DRIFT_LAUNCHED("attention_join");
   return 0;
 }
+
+// Keys a split of attention takes, by head width.
+int keys_per_split(int head_dim) { return head_dim > 128 ? 64 : 128; }
+
+// The most splits the join takes (their factors in 48 KB of shared memory).
+constexpr int MAX_SPLITS = 48 * 1024 / 4 - 16;
 
 int check_cache(int pages, int page_size, int kv_heads, int head_dim, const int32_t* page_table,
                 int table_pages, long long positions, const char* call) {
@@ -431,6 +560,10 @@ int check_cache(int pages, int page_size, int kv_heads, int head_dim, const int3
   if (head_dim != 64 && head_dim != 80 && head_dim != 128 && head_dim != 256)
     return invalid("%s: heads of %d (kernels take 64, 80, 128, 256)", call, head_dim);
   if (pages <= 0 || kv_heads <= 0) return invalid("%s: an empty cache", call);
+  // the kernels address the cache in 16-byte units with 32-bit offsets
+  if ((long long)pages * page_size * kv_heads * head_dim / 8 >= 0xffffffffll)
+    return invalid("%s: a cache of %lld bytes per side (at most 64 GiB)", call,
+                   (long long)pages * page_size * kv_heads * head_dim * 2);
   if (!page_table || table_pages <= 0 || (long long)table_pages * page_size < positions)
     return invalid("a page table of %d pages for %lld positions", table_pages, positions);
   return 0;
@@ -481,8 +614,9 @@ int drift_attention(const float* q, int tokens, int q_heads, const void* keys, c
       (query_start + tokens > key_count && (causal || window > 0)))
     return invalid("attention: queries at %d..%d past %d keys", query_start,
                    query_start + tokens - 1, key_count);
-  if (key_count > (48 * 1024 / 4 - 16) * KEYS)
-    return invalid("attention: %d keys (at most %d)", key_count, (48 * 1024 / 4 - 16) * KEYS);
+  if ((long long)key_count > (long long)MAX_SPLITS * keys_per_split(head_dim))
+    return invalid("attention: %d keys (at most %d)", key_count,
+                   MAX_SPLITS * keys_per_split(head_dim));
   if (tokens == 0) return 0;
   if (!q || !keys || !values || !out) return invalid("attention: a null tensor");
   if ((reinterpret_cast<uintptr_t>(keys) | reinterpret_cast<uintptr_t>(values)) & 15)
@@ -500,7 +634,8 @@ int drift_attention(const float* q, int tokens, int q_heads, const void* keys, c
   a.query_start = query_start;
   a.key_count = key_count;
   a.tokens = tokens;
-  a.splits = key_count > 0 ? (key_count + KEYS - 1) / KEYS : 1;
+  const int per_split = keys_per_split(head_dim);
+  a.splits = key_count > 0 ? (key_count + per_split - 1) / per_split : 1;
   a.scale = scale;
   a.causal = causal;
   a.window = window;
@@ -546,6 +681,13 @@ int drift_attention_inputs_decode(const float* q, const float* k, const float* v
   return 0;
 }
 
+size_t drift_attention_workspace_bytes(int rows, int q_heads, int head_dim, int key_count) {
+  if (rows <= 0 || q_heads <= 0 || head_dim <= 0) return 0;
+  const int per_split = keys_per_split(head_dim);
+  const size_t splits = key_count > 0 ? size_t(key_count + per_split - 1) / per_split : 1;
+  return size_t(rows) * q_heads * splits * (head_dim + 2) * sizeof(float);
+}
+
 int drift_attention_decode(const float* q, int batch, int q_heads, const void* keys,
                            const void* values, int pages, int page_size, int kv_heads,
                            int head_dim, const int32_t* page_tables, int table_stride,
@@ -556,7 +698,8 @@ int drift_attention_decode(const float* q, int batch, int q_heads, const void* k
                         max_key_count, "attention"));
   if (q_heads % kv_heads != 0 || q_heads / kv_heads > MAX_GROUP)
     return invalid("attention: %d query heads over %d key heads", q_heads, kv_heads);
-  if (max_key_count <= 0 || max_key_count > (48 * 1024 / 4 - 16) * KEYS)
+  if (max_key_count <= 0 ||
+      (long long)max_key_count > (long long)MAX_SPLITS * keys_per_split(head_dim))
     return invalid("attention: %d keys", max_key_count);
   if (batch == 0) return 0;
   if (!q || !keys || !values || !positions || !out) return invalid("attention: a null tensor");
@@ -575,7 +718,7 @@ int drift_attention_decode(const float* q, int batch, int q_heads, const void* k
   a.query_start = 0;
   a.key_count = max_key_count;
   a.tokens = batch;
-  a.splits = (max_key_count + KEYS - 1) / KEYS;
+  a.splits = (max_key_count + keys_per_split(head_dim) - 1) / keys_per_split(head_dim);
   a.scale = scale;
   a.causal = 1;
   a.window = window;

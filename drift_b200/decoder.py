@@ -222,9 +222,9 @@ class DenseDecoder:
         c = self.config
         widest = max(c.hidden, self.q_heads * c.head_dim, self.ffn)
         self.ops.reserve_workspace(self.batch, widest)
-        splits = (self.context + 127) // 128
-        attention_bytes = self.batch * self.q_heads * splits * (c.head_dim + 2) * 4
         lib = self.ops.lib
+        attention_bytes = lib.drift_attention_workspace_bytes(self.batch, self.q_heads, c.head_dim,
+                                                              self.context)
         from ._lib import check
         check("drift_workspace_reserve", lib.drift_workspace_reserve(
             max(attention_bytes, lib.drift_linear_workspace_bytes(self.batch, widest))))

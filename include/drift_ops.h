@@ -201,6 +201,10 @@ int drift_attention_decode(const float* q, int batch, int q_heads, const void* k
 int drift_workspace_reserve(size_t bytes);
 /* Bytes of scratch drift_linear needs for m rows of k (new). */
 size_t drift_linear_workspace_bytes(int64_t m, int64_t k);
+/* Bytes of scratch drift_attention / drift_attention_decode need for `rows`
+ * query rows (tokens, or sequences) of q_heads heads over key_count keys
+ * (new: the split-K partial sums). */
+size_t drift_attention_workspace_bytes(int rows, int q_heads, int head_dim, int key_count);
 
 /* drift_linear, for 1 to 31 rows of x, allocating no device memory. No
  * counterpart in the reference: it exists for hosts that cannot allocate on
