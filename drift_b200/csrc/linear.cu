@@ -22,6 +22,11 @@ int prepare_x_mma(int x_dtype, const void* x, int64_t m, int64_t k, uint8_t* rec
 int matvec_f32_weights(int x_dtype, const void* x, const float* weight, float* y, int64_t m,
                        int64_t n, int64_t k, cudaStream_t stream);
 bool tc_supports(int weight_dtype, const void* weight, int64_t k);
+bool ring_many_fits(int weight_dtype, int count, const void* const* weights, const int64_t* rows,
+                    int64_t cols);
+int matvec_ring_many(int weight_dtype, int count, const void* const* weights,
+                     const uint8_t* records, float* const* ys, const int64_t* rows, int64_t cols,
+                     int64_t vectors, cudaStream_t stream);
 size_t tc_workspace_bytes(int64_t m, int64_t k);
 int linear_tc(int x_dtype, const void* x, int weight_dtype, const void* weight, float* y,
               int64_t m, int64_t n, int64_t k, uint8_t* workspace, cudaStream_t stream);
@@ -107,6 +112,12 @@ int drift_linears(int x_dtype, const void* x, int count, const int* weight_dtype
   uint8_t* records = static_cast<uint8_t*>(w);
   uint8_t* tc_region = static_cast<uint8_t*>(w) + records_bytes;
   if (quantized) DRIFT_TRY(prepare_x_mma(x_dtype, x, m, k, records, s));  // one preparation for all
+  // streamed products of one type that fit one balanced launch take it
+  // together (the same bits as one by one)
+  bool together = quantized && !tensor_cores && count >= 2;
+  for (int i = 1; together && i < count; ++i) together = weight_dtypes[i] == weight_dtypes[0];
+  if (together && ring_many_fits(weight_dtypes[0], count, weights, ns, k))
+    return matvec_ring_many(weight_dtypes[0], count, weights, records, outs, ns, k, m, s);
   for (int i = 0; i < count; ++i) {
     if (ns[i] == 0) continue;
     if (weight_dtypes[i] == DRIFT_F32)

@@ -65,6 +65,8 @@ struct RingShape {
   static constexpr int BARS = WARPS * S * Ring<T>::STAGE;
   static constexpr int X_OFFSET = BARS + WARPS * S * 8 + 16;  // x staged for the dp4a modes
   static constexpr int BYTES = X_OFFSET + 1024;  // + room to align to 1024; + x when staged
+  // the MMA mode keeps a tile's chain of group sums here, not in registers
+  static constexpr int CHAIN_BYTES = WARPS * 16 * WARP * 4;
 };
 constexpr int MAX_SMEM = 232448;
 
@@ -236,6 +238,33 @@ struct Acc {
 #pragma unroll
     for (int i = 0; i < (MODE == MODE_MMA ? 4 : 2); ++i) a[i][0] = a[i][1] = a[i][2] = a[i][3] = 0.0f;
   }
+  // the chain in shared memory (MMA mode), lane-major: slot (i, e) of lane l
+  // at chain[(4 i + e) 32 + l]. first: the tile's first group (the chain
+  // starts as it); returns nothing -- the last group is added by `finish`.
+  __device__ void chain_into(float* chain, bool first) const {
+    const int lane = threadIdx.x % WARP;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float* c = chain + (4 * i + e) * WARP + lane;
+        *c = first ? a[i][e] : *c + a[i][e];
+      }
+  }
+  // this (the last group's sums) after the chain so far
+  __device__ void finish(const float* chain, bool first) {
+    const int lane = threadIdx.x % WARP;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) a[i][e] = first ? a[i][e] : chain[(4 * i + e) * WARP + lane] + a[i][e];
+  }
+  __device__ void add(const Acc& o) {
+#pragma unroll
+    for (int i = 0; i < (MODE == MODE_MMA ? 4 : 2); ++i)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) a[i][e] += o.a[i][e];
+  }
   // call f(row within the tile, vector, value) for each output this lane holds
   template <typename F>
   __device__ void each(F f) const {
@@ -257,25 +286,62 @@ struct Acc {
   }
 };
 
+// A row's sum is a chain over fixed groups of its segments: min(8, segments)
+// groups, group g holding segments [segments g / G, segments (g + 1) / G);
+// a group is summed block by block from zero and the row is
+// ((group_0 + group_1) + group_2) + ... Whichever warps take which groups,
+// the bits are the same -- so the schedule (tiles per warp, splits between
+// warps and CTAs, other matrices sharing a launch, the number of vectors)
+// never shows in the result.
+struct Groups {
+  int segments, count, first_end;
+  unsigned long long ends;  // bit s: segment s ends a group (segments below 64)
+  __device__ explicit Groups(int s) : segments(s), count(s < 8 ? s : 8), ends(0) {
+    for (int g = 1; g <= count; ++g)
+      if (begin(g) - 1 < 64) ends |= 1ull << (begin(g) - 1);
+    first_end = begin(1);
+  }
+  __device__ int begin(int g) const { return segments * g / count; }
+  __device__ int of(int s) const { return ((s + 1) * count - 1) / segments; }
+  __device__ bool last(int s) const {
+    return s < 64 ? (ends >> s) & 1 : s + 1 == begin(of(s) + 1);
+  }
+  __device__ bool in_first(int s) const { return s < first_end; }
+};
+
+// Group sums of tiles split between warps: [slot][group][ROWS][slots], the
+// slot a tile's index in a balanced launch, or a CTA's leftover tile in the
+// tile schedule.
+constexpr long long PARTIAL_FLOATS = 5ll << 20;
+__device__ float group_partials[PARTIAL_FLOATS];
+
 // The CTA's schedule. CTA c owns tiles [t0, t0 + count), an even share of the
 // matrix's. Its W warps take them in rounds -- warp w sums tile t0 + f W + w
 // whole in round f -- and the (count mod W) tiles left over are split by
-// segments, P = W / left warps to a tile, whose partial sums meet in shared
-// memory in a fixed order. All of it follows from rows, cols and the grid,
-// never from the number of vectors.
+// groups, P warps to a tile (a power of two, at most W / left and the group
+// count), whose group sums meet in global memory and are chained in group
+// order. All of it follows from rows, cols and the grid, never from the
+// number of vectors.
 struct Schedule {
   int t0, rounds, left, parts, segments, warps;
-  __device__ Schedule(int tiles, int segs, int w) : segments(segs), warps(w) {
+  Groups groups;
+  __device__ Schedule(int tiles, int segs, int w) : segments(segs), warps(w), groups(segs) {
     t0 = int((long long)tiles * blockIdx.x / gridDim.x);
     const int t1 = int((long long)tiles * (blockIdx.x + 1) / gridDim.x);
     rounds = (t1 - t0) / w;
     left = (t1 - t0) % w;
-    parts = left ? w / left : 1;
+    const int most = left ? (w / left < groups.count ? w / left : groups.count) : 1;
+    parts = 1;
+    while (parts * 2 <= most) parts *= 2;
   }
   __device__ bool shares(int w) const { return w < left * parts; }
   __device__ int share_tile(int w) const { return t0 + rounds * warps + w / parts; }
-  __device__ int share_begin(int w) const { return int((long long)segments * (w % parts) / parts); }
-  __device__ int share_end(int w) const { return int((long long)segments * (w % parts + 1) / parts); }
+  __device__ int share_begin(int w) const {
+    return groups.begin(groups.count * (w % parts) / parts);
+  }
+  __device__ int share_end(int w) const {
+    return groups.begin(groups.count * (w % parts + 1) / parts);
+  }
   // job j of warp w: (tile, segment)
   __device__ void job(int w, int j, int& tile, int& segment) const {
     const int whole = rounds * segments;
@@ -359,9 +425,13 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
       asm volatile("prefetch.global.L1 [%0];" ::"l"(records + (long long)(i / LINES) * MMA_RECORD_BYTES +
                                                     128 * (i % LINES)));
   }
-  Acc<MODE> acc;
-  acc.zero();
+  Acc<MODE> part, total;  // the group being summed; the chain of the tile's groups
+  part.zero();
+  total.zero();
   const int whole = plan.rounds * segments;
+  const Groups& groups = plan.groups;
+  float* chain = reinterpret_cast<float*>(smem + Shape::X_OFFSET) + warp * 16 * WARP;
+  float* shared_sums = group_partials + (long long)blockIdx.x * W * groups.count * ROWS * VSLOTS;
   while (consumed < issued) {
     const int j = consumed;
     int tile, segment;
@@ -371,21 +441,46 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
       const int first = segment * SEG_BLOCKS;
       const int count = blocks - first < SEG_BLOCKS ? blocks - first : SEG_BLOCKS;
       if constexpr (MODE == MODE_MMA)
-        segment_mma<T>(ring + (j % S) * STAGE, first, count, records, vectors, acc.a);
+        segment_mma<T>(ring + (j % S) * STAGE, first, count, records, vectors, part.a);
       else
-        segment_dp4a<T, MODE, XSMEM>(ring + (j % S) * STAGE, first, count, x, acc.a);
+        segment_dp4a<T, MODE, XSMEM>(ring + (j % S) * STAGE, first, count, x, part.a);
     }
     __syncwarp();
     ++consumed;
     if (ok && issued < jobs) issue(issued++);  // refill the freed stage
-    if (j < whole && segment == segments - 1) {
-      // a whole tile: write its rows, start the next
-      acc.each([&](int r, int v, float value) {
-        const int row = tile * ROWS + r;
-        if (row < rows && v < vectors) y[(long long)v * rows + row] = value;
+    if (!groups.last(segment)) continue;
+    if (j < whole) {
+      const bool first_group = groups.in_first(segment);
+      if constexpr (MODE == MODE_MMA) {
+        if (segment != segments - 1) {
+          part.chain_into(chain, first_group);
+        } else {
+          part.finish(chain, first_group);
+          part.each([&](int r, int v, float value) {
+            const int row = tile * ROWS + r;
+            if (row < rows && v < vectors) y[(long long)v * rows + row] = value;
+          });
+        }
+      } else {
+        total.add(part);
+        if (segment == segments - 1) {
+          // a whole tile: write its rows, start the next
+          total.each([&](int r, int v, float value) {
+            const int row = tile * ROWS + r;
+            if (row < rows && v < vectors) y[(long long)v * rows + row] = value;
+          });
+          total.zero();
+        }
+      }
+    } else {
+      // a group of a leftover tile: its sums to memory, chained below
+      float* sums = shared_sums + ((long long)(tile - plan.t0 - plan.rounds * W) * groups.count +
+                                   groups.of(segment)) * ROWS * VSLOTS;
+      part.each([&](int r, int v, float value) {
+        if (v < VSLOTS) sums[r * VSLOTS + v] = value;
       });
-      acc.zero();
     }
+    part.zero();
   }
   if (!ok) {
     // let the copies already issued land before the ring is reused or left
@@ -393,25 +488,198 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
     for (int j = consumed; j < issued; ++j) tc::mbar_wait(&bars[j % S], (j / S) & 1, &never, nullptr);
   }
   if (plan.left > 0) {
-    // the leftover tiles: shares in shared memory (the drained rings), then
-    // summed in share order
-    __syncthreads();
-    float* partial = reinterpret_cast<float*>(smem);  // [W][ROWS][VSLOTS]
-    if (plan.shares(warp))
-      acc.each([&](int r, int v, float value) {
-        if (v < VSLOTS) partial[(warp * ROWS + r) * VSLOTS + v] = value;
-      });
+    // the leftover tiles: their group sums chained in group order
     __syncthreads();
     for (int e = threadIdx.x; e < plan.left * ROWS * VSLOTS; e += blockDim.x) {
       const int l = e / (ROWS * VSLOTS), r = (e / VSLOTS) % ROWS, v = e % VSLOTS;
       const int row = (plan.t0 + plan.rounds * W + l) * ROWS + r;
       if (row < rows && v < vectors) {
-        float total = 0.0f;
-        for (int p = 0; p < plan.parts; ++p)
-          total += partial[(((l * plan.parts) + p) * ROWS + r) * VSLOTS + v];
-        y[(long long)v * rows + row] = total;
+        float sum = 0.0f;
+        for (int g = 0; g < groups.count; ++g)
+          sum += __ldcg(shared_sums + ((long long)l * groups.count + g) * ROWS * VSLOTS +
+                        r * VSLOTS + v);
+        y[(long long)v * rows + row] = sum;
       }
     }
+  }
+}
+
+// ---- the balanced schedule: small launches, one or several matrices ----------------------
+// A launch's units are its (tile, group) pairs, tile-major across the
+// matrices of the launch, and warp w of the grid's G takes units [U w / G,
+// U (w + 1) / G) -- a contiguous run of segments -- so every warp of every SM
+// gets the same share, whatever the row counts. A warp that holds a whole
+// tile chains its groups in registers; a tile split between warps leaves its
+// group sums in global memory and the warp whose arrival completes the tile
+// (a count per tile) chains them. The bits are the tile schedule's.
+constexpr int MAX_MATRICES = 4;
+constexpr int SPLIT_UNITS = 8192;  // the most units a balanced launch takes
+
+struct SplitLaunch {
+  CUtensorMap maps[MAX_MATRICES];
+  float* y[MAX_MATRICES];
+  int rows[MAX_MATRICES];
+  int tile_end[MAX_MATRICES];  // matrix m holds the launch's tiles [tile_end[m - 1], tile_end[m])
+  int count, cols, vectors;
+  const uint8_t* records;
+  int* error;
+};
+
+// Groups arrived per tile of a balanced launch, zero between launches (the
+// completing warp clears its tile's).
+__device__ int split_arrivals[SPLIT_UNITS];
+
+template <typename T, int MODE>
+__global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
+    matvec_split_kernel(const __grid_constant__ SplitLaunch L) {
+  using Shape = RingShape<T>;
+  constexpr int W = Shape::WARPS, S = Shape::S, STAGE = Ring<T>::STAGE;
+  constexpr int VSLOTS = MODE == MODE_MMA ? 8 : MODE;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const int warp = threadIdx.x / WARP, lane = threadIdx.x % WARP;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Shape::BARS) + warp * S;
+  volatile int* abort = reinterpret_cast<int*>(smem + Shape::BARS + W * S * 8);
+  uint8_t* ring = smem + warp * S * STAGE;
+
+  const int blocks = L.cols / 32;
+  const int segments = (blocks + SEG_BLOCKS - 1) / SEG_BLOCKS;
+  const Groups groups(segments);
+  const long long U = (long long)L.tile_end[L.count - 1] * groups.count;
+  const long long G = (long long)gridDim.x * W, gw = (long long)blockIdx.x * W + warp;
+  // unit u starts at segment job (u / groups) segments + begin(u mod groups)
+  auto start = [&](long long u) {
+    return int(u / groups.count) * segments + groups.begin(int(u % groups.count));
+  };
+  const int j0 = start(U * gw / G), jobs = start(U * (gw + 1) / G) - j0;
+
+  if (threadIdx.x == 0) *abort = 0;
+  if (lane < S) tc::mbar_init(&bars[lane], 1);
+  tc::fence_barrier_init();
+  __syncthreads();
+
+  // the matrix of a launch tile, and the tile within it
+  auto locate = [&](int tile, int& m, int& local) {
+    m = 0;
+    while (m + 1 < L.count && tile >= L.tile_end[m]) ++m;
+    local = tile - (m > 0 ? L.tile_end[m - 1] : 0);
+  };
+  // job j: its weights by one 2-D tensor copy, and its x records' lines
+  // (the vectors' slots) into L1 ahead of use
+  auto issue = [&](int j) {
+    const int job = j0 + j, tile = job / segments, segment = job % segments;
+    int m, local;
+    locate(tile, m, local);
+    if (lane == 0) {
+      tc::mbar_expect_tx(&bars[j % S], uint32_t(STAGE));
+      tc::tma_load_2d(ring + (j % S) * STAGE, &L.maps[m], &bars[j % S],
+                      segment * (Ring<T>::SEG / 4), local * ROWS);
+    }
+    constexpr int LINES = MODE == MODE_DP4A_1 ? 1 : MODE == MODE_DP4A_2 ? 2 : 7;
+    for (int i = lane; i < SEG_BLOCKS * LINES; i += WARP) {
+      const int b = segment * SEG_BLOCKS + i / LINES;
+      if (b < blocks)
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(L.records + (long long)b * MMA_RECORD_BYTES +
+                                                      128 * (i % LINES)));
+    }
+    __syncwarp();
+  };
+
+  int issued = 0, landed = 0;
+  bool ok = true;
+  while (issued < jobs && issued < S) issue(issued++);
+  pdl_trigger();
+  pdl_wait();  // the weights' first copies are in flight; x is now ready
+  Acc<MODE> part, total;
+  part.zero();
+  total.zero();
+  float* chain = reinterpret_cast<float*>(smem + Shape::X_OFFSET) + warp * 16 * WARP;
+  bool whole = false;  // this warp holds the current tile whole
+  int first_group = 0;
+  // every job is walked, even after a failed wait (as zeros), so that the
+  // arrival counts stay whole for the next launch; the error word voids the
+  // results
+  for (int j = 0; j < jobs; ++j) {
+    const int job = j0 + j, tile = job / segments, segment = job % segments;
+    if (j == 0 || segment == 0) {
+      // a tile starts: whole if all its segments are in this warp's share
+      first_group = groups.of(segment);
+      whole = segment == 0 && j + segments <= jobs;
+    }
+    if (ok && j < issued) {
+      ok = tc::mbar_wait_warp(&bars[j % S], (j / S) & 1, abort, L.error);
+      if (ok) landed = j + 1;
+    }
+    if (ok && j < issued) {
+      const int first = segment * SEG_BLOCKS;
+      const int count = blocks - first < SEG_BLOCKS ? blocks - first : SEG_BLOCKS;
+      if constexpr (MODE == MODE_MMA)
+        segment_mma<T>(ring + (j % S) * STAGE, first, count, L.records, L.vectors, part.a);
+      else
+        segment_dp4a<T, MODE, false>(ring + (j % S) * STAGE, first, count, L.records, part.a);
+    }
+    __syncwarp();
+    if (ok && issued < jobs) issue(issued++);  // refill the freed stage
+    if (!groups.last(segment)) continue;  // a warp's share ends on a group's end
+    const int group = groups.of(segment);
+    int m, local;
+    locate(tile, m, local);
+    if (whole) {
+      const bool first_group = group == 0;
+      if constexpr (MODE == MODE_MMA) {
+        if (segment != segments - 1) {
+          part.chain_into(chain, first_group);
+        } else {
+          part.finish(chain, first_group);
+          part.each([&](int r, int v, float value) {
+            const int row = local * ROWS + r;
+            if (row < L.rows[m] && v < L.vectors) L.y[m][(long long)v * L.rows[m] + row] = value;
+          });
+        }
+      } else {
+        total.add(part);
+        if (segment == segments - 1) {
+          total.each([&](int r, int v, float value) {
+            const int row = local * ROWS + r;
+            if (row < L.rows[m] && v < L.vectors) L.y[m][(long long)v * L.rows[m] + row] = value;
+          });
+          total.zero();
+        }
+      }
+      part.zero();
+      continue;
+    }
+    float* tile_sums = group_partials + (long long)tile * groups.count * ROWS * VSLOTS;
+    part.each([&](int r, int v, float value) {
+      if (v < VSLOTS) tile_sums[(group * ROWS + r) * VSLOTS + v] = value;
+    });
+    part.zero();
+    if (segment != segments - 1 && j != jobs - 1) continue;
+    // this warp's groups of the tile are in memory: count them in; the warp
+    // that completes the tile chains its groups
+    __threadfence();
+    __syncwarp();
+    int done = 0;
+    if (lane == 0) {
+      const int mine = group - first_group + 1;
+      done = atomicAdd(&split_arrivals[tile], mine) + mine == groups.count;
+    }
+    if (!__shfl_sync(0xffffffffu, done, 0)) continue;
+    __threadfence();
+    for (int e = lane; e < ROWS * VSLOTS; e += WARP) {
+      const int r = e / VSLOTS, v = e % VSLOTS, row = local * ROWS + r;
+      if (row >= L.rows[m] || v >= L.vectors) continue;
+      float sum = 0.0f;
+      for (int g = 0; g < groups.count; ++g) sum += __ldcg(tile_sums + g * ROWS * VSLOTS + e);
+      L.y[m][(long long)v * L.rows[m] + row] = sum;
+    }
+    if (lane == 0) split_arrivals[tile] = 0;
+  }
+  if (!ok) {
+    // let the copies already issued land before the ring is left
+    volatile int never = 0;
+    for (int j = landed; j < issued; ++j) tc::mbar_wait(&bars[j % S], (j / S) & 1, &never, nullptr);
   }
 }
 
@@ -427,6 +695,10 @@ int launch_mode(const CUtensorMap& wmap, const uint8_t* records, float* y, int r
   }
   const int tiles = (rows + ROWS - 1) / ROWS;
   const unsigned grid = unsigned(tiles < sm_count() ? tiles : sm_count());
+  // each CTA's leftover tiles keep their group sums in group_partials
+  if ((long long)grid * Shape::WARPS * 8 * ROWS * 8 > PARTIAL_FLOATS)
+    return invalid("%u CTAs of leftover sums (at most %lld)", grid,
+                   PARTIAL_FLOATS / (Shape::WARPS * 8 * ROWS * 8));
   DRIFT_CUDA(launch_pdl(matvec_ring_kernel<T, MODE, XSMEM>, grid, Shape::WARPS * 32, smem, stream,
                         wmap, records, y, rows, cols, vectors, device_error_word()));
   return 0;
@@ -447,8 +719,61 @@ int launch_dp4a(const CUtensorMap& wmap, const uint8_t* records, float* y, int r
                                      stream);
 }
 
-// One configuration per matrix type, whatever the number of vectors, so a
-// row's blocks are summed in the same order whatever the batch.
+template <typename T, int MODE>
+int launch_split_mode(const SplitLaunch& launch, long long units, cudaStream_t stream) {
+  using Shape = RingShape<T>;
+  static bool configured = false;
+  if (!configured) {
+    DRIFT_CUDA(cudaFuncSetAttribute(matvec_split_kernel<T, MODE>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_SMEM));
+    configured = true;
+  }
+  long long grid = (units + Shape::WARPS - 1) / Shape::WARPS;  // at least a unit a warp
+  if (grid > sm_count()) grid = sm_count();
+  DRIFT_CUDA(launch_pdl(matvec_split_kernel<T, MODE>, unsigned(grid), Shape::WARPS * 32,
+                        Shape::BYTES + (MODE == MODE_MMA ? Shape::CHAIN_BYTES : 0), stream, launch));
+  return 0;
+}
+
+// The units of a product in the balanced schedule: tiles x groups.
+long long split_units(int64_t rows, int64_t cols) {
+  const int64_t segments = (cols / 32 + SEG_BLOCKS - 1) / SEG_BLOCKS;
+  return ((rows + ROWS - 1) / ROWS) * (segments < 8 ? segments : 8);
+}
+
+// One balanced launch over `count` matrices of one type sharing x (at most
+// 8 vectors, SPLIT_UNITS units together).
+template <typename T>
+int split_dispatch(int count, const uint8_t* const* weights, float* const* ys, const int64_t* rows,
+                   int cols, const uint8_t* records, int vectors, cudaStream_t stream) {
+  SplitLaunch launch = {};
+  int n = 0, tiles = 0;
+  for (int i = 0; i < count; ++i) {
+    if (rows[i] == 0) continue;
+    DRIFT_TRY(encode_word_rows(&launch.maps[n], weights[i], int64_t(cols / 32) * T::BYTES / 4,
+                               rows[i], Ring<T>::PITCH / 4, ROWS));
+    tiles += int((rows[i] + ROWS - 1) / ROWS);
+    launch.tile_end[n] = tiles;
+    launch.y[n] = ys[i];
+    launch.rows[n] = int(rows[i]);
+    ++n;
+  }
+  if (n == 0) return 0;
+  launch.count = n;
+  launch.cols = cols;
+  launch.vectors = vectors;
+  launch.records = records;
+  launch.error = device_error_word();
+  const long long segments = (cols / 32 + SEG_BLOCKS - 1) / SEG_BLOCKS;
+  const long long units = (long long)tiles * (segments < 8 ? segments : 8);
+  if (units > SPLIT_UNITS) return invalid("a balanced launch of %lld units", units);
+  if (vectors == 1) return launch_split_mode<T, MODE_DP4A_1>(launch, units, stream);
+  if (vectors == 2) return launch_split_mode<T, MODE_DP4A_2>(launch, units, stream);
+  return launch_split_mode<T, MODE_MMA>(launch, units, stream);
+}
+
+// One configuration per matrix type, whatever the number of vectors (and the
+// group chain makes a row's bits the same in any schedule).
 template <typename T>
 int ring_dispatch(const uint8_t* weight, const uint8_t* records, float* y, int rows, int cols,
                   int vectors, cudaStream_t stream) {
@@ -457,11 +782,14 @@ int ring_dispatch(const uint8_t* weight, const uint8_t* records, float* y, int r
                              Ring<T>::PITCH / 4, ROWS));
   if (vectors == 1) return launch_dp4a<T, MODE_DP4A_1>(wmap, records, y, rows, cols, vectors, stream);
   if (vectors == 2) return launch_dp4a<T, MODE_DP4A_2>(wmap, records, y, rows, cols, vectors, stream);
-  return launch_mode<T, MODE_MMA, false>(wmap, records, y, rows, cols, vectors, RingShape<T>::BYTES,
-                                         stream);
+  return launch_mode<T, MODE_MMA, false>(wmap, records, y, rows, cols, vectors,
+                                         RingShape<T>::BYTES + RingShape<T>::CHAIN_BYTES, stream);
 }
 
 #define DRIFT_RING_REGISTER(T, name)                                                        \
+  DRIFT_REGISTER(matvec_split_##name##_dp4a1, (matvec_split_kernel<T, MODE_DP4A_1>))          \
+  DRIFT_REGISTER(matvec_split_##name##_dp4a2, (matvec_split_kernel<T, MODE_DP4A_2>))          \
+  DRIFT_REGISTER(matvec_split_##name##_mma, (matvec_split_kernel<T, MODE_MMA>))               \
   DRIFT_REGISTER(matvec_ring_##name##_dp4a1, (matvec_ring_kernel<T, MODE_DP4A_1, false>))    \
   DRIFT_REGISTER(matvec_ring_##name##_dp4a1_xs, (matvec_ring_kernel<T, MODE_DP4A_1, true>))  \
   DRIFT_REGISTER(matvec_ring_##name##_dp4a2, (matvec_ring_kernel<T, MODE_DP4A_2, false>))    \
@@ -481,6 +809,49 @@ bool ring_supports(int weight_dtype, const void* weight, int64_t k) {
     return false;
   return row > 0 && row % 16 == 0 && (reinterpret_cast<uintptr_t>(weight) & 15) == 0 &&
          tensor_maps_available();
+}
+
+// Whether one balanced launch takes these products together (rows of one
+// type, the same columns): each alone would take the balanced schedule too,
+// so the results are the bits of separate products.
+bool ring_many_fits(int weight_dtype, int count, const void* const* weights, const int64_t* rows,
+                    int64_t cols) {
+  if (count < 2 || count > MAX_MATRICES) return false;
+  long long units = 0;
+  for (int i = 0; i < count; ++i) {
+    if (!ring_supports(weight_dtype, weights[i], cols)) return false;
+    units += split_units(rows[i], cols);
+  }
+  return units <= SPLIT_UNITS;
+}
+
+// Products sharing x's records in balanced launches, 8 vectors at a time.
+int matvec_ring_many(int weight_dtype, int count, const void* const* weights,
+                     const uint8_t* records, float* const* ys, const int64_t* rows, int64_t cols,
+                     int64_t vectors, cudaStream_t stream) {
+  if (count > MAX_MATRICES) return invalid("%d products in one launch", count);
+  const int64_t blocks = cols / 32;
+  for (int64_t first = 0; first < vectors; first += 8) {
+    const int n = int(vectors - first < 8 ? vectors - first : 8);
+    const uint8_t* w[MAX_MATRICES];
+    float* y[MAX_MATRICES];
+    for (int i = 0; i < count; ++i) {
+      w[i] = static_cast<const uint8_t*>(weights[i]);
+      y[i] = ys[i] + first * rows[i];
+    }
+    const uint8_t* r = records + (first / 8) * blocks * MMA_RECORD_BYTES;
+    switch (weight_dtype) {
+      case DRIFT_Q8_0:
+        DRIFT_TRY(split_dispatch<Q8_0T>(count, w, y, rows, int(cols), r, n, stream));
+        break;
+      case DRIFT_Q4_0:
+        DRIFT_TRY(split_dispatch<Q4_0T>(count, w, y, rows, int(cols), r, n, stream));
+        break;
+      default:
+        DRIFT_TRY(split_dispatch<Q4_1T>(count, w, y, rows, int(cols), r, n, stream));
+    }
+  }
+  return 0;
 }
 
 int matvec_ring(int weight_dtype, const void* weight, const uint8_t* records, float* y,
