@@ -68,6 +68,12 @@ SIGNATURES = {
     "drift_add_rms_norm": (_i32, [_p, _p, _p, _f32, _f32, _p, _i64, _i64, _p]),
     "drift_add": (_i32, [_p, _p, _p, _i64, _p]),
     "drift_gated": (_i32, [_i32, _p, _p, _p, _i64, _p]),
+    "drift_prepared_x_bytes": (_sz, [_i64, _i64]),
+    "drift_add_rms_norm_prepared": (_i32, [_p, _p, _p, _f32, _f32, _p, _i64, _i64, _p, _p]),
+    "drift_gated_prepared": (_i32, [_i32, _p, _p, _p, _i64, _i64, _p, _p]),
+    "drift_linears_prepared": (_i32, [_i32, _p, _p, _i32, _p, _p, _p, _p, _i64, _i64, _p]),
+    "drift_attention_decode_prepared": (_i32, [_p, _i32, _i32, _p, _p, _i32, _i32, _i32, _i32, _p,
+                                               _i32, _p, _i32, _f32, _i32, _f32, _p, _p, _p, _p]),
     "drift_rope": (_i32, [_p, _p, _p, _i32, _i32, _i32, _f32, _i32, _i32, _p]),
     "drift_route": (_i32, [_p, _p, _p, _i32, _i32, _i32, _p]),
     "drift_experts_linear": (_i32, [_i32, _p, _i64, _i32, _p, _i64, _i64, _i64, _p, _i64, _p,

@@ -21,6 +21,7 @@
 #include "common.cuh"
 #include "registry.cuh"
 #include "rowwise.cuh"
+#include "x22.cuh"
 
 namespace drift {
 
@@ -470,10 +471,14 @@ __global__ void __launch_bounds__(SPLIT_THREADS) attention_split_kernel(const At
 
 // Joins a query head's splits: out = sum_s o_s e^(m_s - M) / (sum_s l_s
 // e^(m_s - M) + e^(sink - M)), M the largest of the m_s and the sink.
+// With `records` (D a multiple of 32), also the x records of the output rows
+// for the product that follows (the o projection): warp w's 32 dimensions
+// are one block of the row.
 template <int D>
 __global__ void __launch_bounds__(ATT_THREADS) attention_join_kernel(const AttentionArgs a,
                                                                      const float* sinks,
-                                                                     float* out) {
+                                                                     float* out,
+                                                                     uint8_t* records) {
   pdl_trigger();  // the next kernel may launch and wait for this one
   pdl_wait();     // what the kernels before this one wrote is visible
   extern __shared__ float factor[];  // [splits]: e^(m_s - M), 0 for an empty split
@@ -512,7 +517,11 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_join_kernel(const Atten
       for (int j = 0; j < 8; ++j)
         if (s0 + j < a.splits && factor[s0 + j] > 0.0f) sum += o[j] * factor[s0 + j];
     }
-    out[((long long)t * a.q_heads + head) * D + d] = total > 0.0f ? sum / total : 0.0f;
+    const float value = total > 0.0f ? sum / total : 0.0f;
+    out[((long long)t * a.q_heads + head) * D + d] = value;
+    if constexpr (D % 32 == 0) {
+      if (records) x22_record_block(value, records, t, (head * D + d) / 32, a.q_heads * D / 32);
+    }
   }
 }
 
@@ -527,7 +536,8 @@ DRIFT_REGISTER(cache_write_f16, cache_write_kernel)
 DRIFT_REGISTER(attention_inputs_f32, attention_inputs_kernel)
 
 template <int D>
-int launch_attention(const AttentionArgs& a, const float* sinks, float* out, cudaStream_t stream) {
+int launch_attention(const AttentionArgs& a, const float* sinks, float* out, cudaStream_t stream,
+                     uint8_t* records = nullptr) {
   static bool configured = false;
   if (!configured) {
     DRIFT_CUDA(cudaFuncSetAttribute(attention_split_kernel<D>,
@@ -542,7 +552,7 @@ int launch_attention(const AttentionArgs& a, const float* sinks, float* out, cud
                         SPLIT_THREADS, SplitTile<D>::BYTES, stream, a));
   DRIFT_LAUNCHED("attention_split");
   DRIFT_CUDA(launch_pdl(attention_join_kernel<D>, dim3(a.q_heads, a.tokens), ATT_THREADS,
-                        a.splits * sizeof(float), stream, a, sinks, out));
+                        a.splits * sizeof(float), stream, a, sinks, out, records));
   DRIFT_LAUNCHED("attention_join");
   return 0;
 }
@@ -688,11 +698,12 @@ size_t drift_attention_workspace_bytes(int rows, int q_heads, int head_dim, int 
   return size_t(rows) * q_heads * splits * (head_dim + 2) * sizeof(float);
 }
 
-int drift_attention_decode(const float* q, int batch, int q_heads, const void* keys,
-                           const void* values, int pages, int page_size, int kv_heads,
-                           int head_dim, const int32_t* page_tables, int table_stride,
-                           const int32_t* positions, int max_key_count, float scale, int window,
-                           float softcap, const float* sinks, float* out, drift_stream_t stream) {
+static int attention_decode(const float* q, int batch, int q_heads, const void* keys,
+                            const void* values, int pages, int page_size, int kv_heads,
+                            int head_dim, const int32_t* page_tables, int table_stride,
+                            const int32_t* positions, int max_key_count, float scale, int window,
+                            float softcap, const float* sinks, float* out, uint8_t* records,
+                            drift_stream_t stream) {
   if (batch < 0 || q_heads <= 0) return invalid("attention: %d sequences of %d heads", batch, q_heads);
   DRIFT_TRY(check_cache(pages, page_size, kv_heads, head_dim, page_tables, table_stride,
                         max_key_count, "attention"));
@@ -731,11 +742,34 @@ int drift_attention_decode(const float* q, int batch, int q_heads, const void* k
   a.part_ml = a.part_o + parts * head_dim;
   const cudaStream_t s = cudaStream_t(stream);
   switch (head_dim) {
-    case 64: return launch_attention<64>(a, sinks, out, s);
-    case 80: return launch_attention<80>(a, sinks, out, s);
-    case 128: return launch_attention<128>(a, sinks, out, s);
-    default: return launch_attention<256>(a, sinks, out, s);
+    case 64: return launch_attention<64>(a, sinks, out, s, records);
+    case 80: return launch_attention<80>(a, sinks, out, s, records);
+    case 128: return launch_attention<128>(a, sinks, out, s, records);
+    default: return launch_attention<256>(a, sinks, out, s, records);
   }
+}
+
+int drift_attention_decode(const float* q, int batch, int q_heads, const void* keys,
+                           const void* values, int pages, int page_size, int kv_heads,
+                           int head_dim, const int32_t* page_tables, int table_stride,
+                           const int32_t* positions, int max_key_count, float scale, int window,
+                           float softcap, const float* sinks, float* out, drift_stream_t stream) {
+  return attention_decode(q, batch, q_heads, keys, values, pages, page_size, kv_heads, head_dim,
+                          page_tables, table_stride, positions, max_key_count, scale, window,
+                          softcap, sinks, out, nullptr, stream);
+}
+
+int drift_attention_decode_prepared(const float* q, int batch, int q_heads, const void* keys,
+                                    const void* values, int pages, int page_size, int kv_heads,
+                                    int head_dim, const int32_t* page_tables, int table_stride,
+                                    const int32_t* positions, int max_key_count, float scale,
+                                    int window, float softcap, const float* sinks, float* out,
+                                    void* prepared, drift_stream_t stream) {
+  if (!prepared) return invalid("attention: no prepared x");
+  if (head_dim % 32 != 0) return invalid("attention: prepared x needs heads of whole 32-value blocks");
+  return attention_decode(q, batch, q_heads, keys, values, pages, page_size, kv_heads, head_dim,
+                          page_tables, table_stride, positions, max_key_count, scale, window,
+                          softcap, sinks, out, static_cast<uint8_t*>(prepared), stream);
 }
 
 }  // extern "C"

@@ -12,10 +12,15 @@
 
 #include "common.cuh"
 #include "rowwise.cuh"
+#include "x22.cuh"
 #include "quant.cuh"
 #include "registry.cuh"
 
 namespace drift {
+
+size_t mma_workspace_bytes(int64_t m, int64_t k);
+int prepare_x_mma(int x_dtype, const void* x, int64_t m, int64_t k, uint8_t* records,
+                  cudaStream_t stream);
 
 // ---- the device error word -----------------------------------------------------------
 // Set (first flag wins) by kernels that meet an input the reference refuses,
@@ -95,17 +100,18 @@ DRIFT_REGISTER(gather_q4_1, gather_kernel<Q4_1T>)
 DRIFT_REGISTER(gather_rows_f32, gather_rows_f32_kernel)
 
 // ---- RMS norm ----------------------------------------------------------------------------
-// One block of 256 threads per row. With `y`, x += y first (written back: the
-// residual stream). The sum of squares is float (each thread's values in
+// One block of 256 threads per row (1024 for rows of more than 1024 values).
+// With `y`, x += y first (written back: the residual stream). The sum of squares is float (each thread's values in
 // order, then a fixed tree); 1 / sqrt(mean + eps) is rounded as IEEE division
 // and square root round it, not rsqrtf's approximation. Rows of up to 256 PER
 // values are held in registers, every load issued before the first use (a
 // row is one round trip to memory, not PER of them).
-template <int PER>
-__global__ void __launch_bounds__(256) rms_norm_kernel(float* __restrict__ x, const float* __restrict__ y,
+template <int PER, int THREADS>
+__global__ void __launch_bounds__(THREADS) rms_norm_kernel(float* __restrict__ x, const float* __restrict__ y,
                                                        const float* __restrict__ weight,
                                                        float* __restrict__ out, int cols,
-                                                       float epsilon, float weight_offset) {
+                                                       float epsilon, float weight_offset,
+                                                       uint8_t* __restrict__ records) {
   pdl_trigger();  // the next kernel may launch and wait for this one
   pdl_wait();     // what the kernels before this one wrote is visible
   __shared__ float partial[32];
@@ -115,7 +121,7 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(float* __restrict__ x, co
   float value[PER], w[PER];
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
-    const int c = threadIdx.x + i * 256;
+    const int c = threadIdx.x + i * THREADS;
     value[i] = c < cols ? row[c] : 0.0f;
     w[i] = c < cols ? weight[c] : 0.0f;
   }
@@ -123,12 +129,12 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(float* __restrict__ x, co
     float extra[PER];
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
-      const int c = threadIdx.x + i * 256;
+      const int c = threadIdx.x + i * THREADS;
       extra[i] = c < cols ? add[c] : 0.0f;
     }
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
-      const int c = threadIdx.x + i * 256;
+      const int c = threadIdx.x + i * THREADS;
       value[i] = value[i] + extra[i];
       if (c < cols) row[c] = value[i];
     }
@@ -140,8 +146,12 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(float* __restrict__ x, co
   const float scale = 1.0f / sqrtf(total / float(cols) + epsilon);
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
-    const int c = threadIdx.x + i * 256;
-    if (c < cols) target[c] = value[i] * scale * (w[i] + weight_offset);
+    const int c = threadIdx.x + i * THREADS;
+    const float normed = value[i] * scale * (w[i] + weight_offset);
+    if (c < cols) target[c] = normed;
+    // the next product's x records: warp w holds block 8 i + w of the row
+    // (cols a multiple of 32, so the test is the same for the whole warp)
+    if (records && c < cols) x22_record_block(normed, records, blockIdx.x, c / 32, cols / 32);
   }
 }
 
@@ -173,32 +183,29 @@ __global__ void __launch_bounds__(256) rms_norm_long_kernel(float* __restrict__ 
 }
 
 int launch_rms_norm(float* x, const float* y, const float* weight, float* out, int64_t rows,
-                    int64_t cols, float epsilon, float weight_offset, cudaStream_t stream) {
+                    int64_t cols, float epsilon, float weight_offset, cudaStream_t stream,
+                    uint8_t* records = nullptr) {
   const unsigned grid = unsigned(rows);
   const int c = int(cols);
-  if (cols <= 256)
-    DRIFT_CUDA(launch_pdl(rms_norm_kernel<1>, grid, 256, 0, stream, x, y, weight, out, c, epsilon,
-                          weight_offset));
-  else if (cols <= 512)
-    DRIFT_CUDA(launch_pdl(rms_norm_kernel<2>, grid, 256, 0, stream, x, y, weight, out, c, epsilon,
-                          weight_offset));
-  else if (cols <= 1024)
-    DRIFT_CUDA(launch_pdl(rms_norm_kernel<4>, grid, 256, 0, stream, x, y, weight, out, c, epsilon,
-                          weight_offset));
-  else if (cols <= 2048)
-    DRIFT_CUDA(launch_pdl(rms_norm_kernel<8>, grid, 256, 0, stream, x, y, weight, out, c, epsilon,
-                          weight_offset));
-  else if (cols <= 4096)
-    DRIFT_CUDA(launch_pdl(rms_norm_kernel<16>, grid, 256, 0, stream, x, y, weight, out, c, epsilon,
-                          weight_offset));
+#define DRIFT_NORM(PER, THREADS)                                                             \
+  DRIFT_CUDA(launch_pdl(rms_norm_kernel<PER, THREADS>, grid, THREADS, 0, stream, x, y, weight, \
+                        out, c, epsilon, weight_offset, records))
+  if (cols <= 256) DRIFT_NORM(1, 256);
+  else if (cols <= 512) DRIFT_NORM(2, 256);
+  else if (cols <= 1024) DRIFT_NORM(4, 256);
+  else if (cols <= 2048) DRIFT_NORM(2, 1024);
+  else if (cols <= 4096) DRIFT_NORM(4, 1024);
+  else if (cols <= 8192) DRIFT_NORM(8, 1024);
+  else if (cols <= 16384) DRIFT_NORM(16, 1024);
   else
     DRIFT_CUDA(launch_pdl(rms_norm_long_kernel, grid, 256, 0, stream, x, y, weight, out, c, epsilon,
                           weight_offset));
+#undef DRIFT_NORM
   DRIFT_LAUNCHED("rms_norm_f32");
   return 0;
 }
 
-DRIFT_REGISTER(rms_norm_f32, rms_norm_kernel<16>)
+DRIFT_REGISTER(rms_norm_f32, (rms_norm_kernel<4, 1024>))
 DRIFT_REGISTER(rms_norm_long_f32, rms_norm_long_kernel)
 
 // ---- elementwise ---------------------------------------------------------------------------
@@ -226,12 +233,19 @@ __device__ __forceinline__ float activate(float v, int kind) {
   }
 }
 
-__global__ void gated_kernel(const float* gate, const float* up, float* out, long long n, int kind) {
+// With `records`, also the next product's x records of rows of `cols` values
+// (cols and n multiples of 32: a warp's 32 consecutive values are one block,
+// and the loop's test is the same for the whole warp).
+__global__ void gated_kernel(const float* gate, const float* up, float* out, long long n, int kind,
+                             int cols, uint8_t* records) {
   pdl_trigger();  // the next kernel may launch and wait for this one
   pdl_wait();     // what the kernels before this one wrote is visible
   DRIFT_FOR_EACH(i, n) {
     const float u = kind == DRIFT_SITU ? 25.0f * tanhf(up[i] * 0.04f) : up[i];
-    out[i] = activate(gate[i], kind) * u;
+    const float value = activate(gate[i], kind) * u;
+    out[i] = value;
+    if (records)  // n < 2^31 here
+      x22_record_block(value, records, int(i) / cols, int(i) % cols / 32, cols / 32);
   }
 }
 
@@ -397,6 +411,44 @@ int drift_add_rms_norm(float* x, const float* y, const float* weight, float epsi
                          cudaStream_t(stream));
 }
 
+size_t drift_prepared_x_bytes(int64_t m, int64_t k) {
+  return m > 0 && k > 0 && k % 32 == 0 ? mma_workspace_bytes(m, k) : 0;
+}
+
+int drift_add_rms_norm_prepared(float* x, const float* y, const float* weight, float epsilon,
+                                float weight_offset, float* out, int64_t rows, int64_t cols,
+                                void* prepared, drift_stream_t stream) {
+  DRIFT_TRY(check_rows(y ? "addRmsNorm" : "rmsNorm", x, out, rows, cols));
+  if (rows == 0 || cols == 0) return 0;
+  if (!weight) return invalid("rmsNorm: no weight");
+  if (!prepared) return invalid("rmsNorm: no prepared x");
+  if (cols % 32 != 0) return invalid("rmsNorm: prepared x needs rows of whole 32-value blocks");
+  uint8_t* records = static_cast<uint8_t*>(prepared);
+  const cudaStream_t s = cudaStream_t(stream);
+  if (cols > 16384) {
+    // the long rows' kernel leaves the records to the preparation kernel
+    DRIFT_TRY(launch_rms_norm(x, y, weight, out, rows, cols, epsilon, weight_offset, s));
+    return prepare_x_mma(DRIFT_F32, out, rows, cols, records, s);
+  }
+  return launch_rms_norm(x, y, weight, out, rows, cols, epsilon, weight_offset, s, records);
+}
+
+int drift_gated_prepared(int kind, const float* gate, const float* up, float* out, int64_t rows,
+                         int64_t cols, void* prepared, drift_stream_t stream) {
+  if (kind < 0 || kind > 4) return invalid("gated: activation code %d", kind);
+  if (rows < 0 || cols < 0) return invalid("gated over [%lld, %lld]", (long long)rows,
+                                           (long long)cols);
+  if (rows == 0 || cols == 0) return 0;
+  if (!gate || !up || !out || !prepared) return invalid("gated: a null tensor");
+  if (cols % 32 != 0) return invalid("gated: prepared x needs rows of whole 32-value blocks");
+  if (rows * cols > 0x7fffffffll) return invalid("gated: %lld values to prepare", rows * cols);
+  const long long n = rows * cols;
+  DRIFT_CUDA(launch_pdl(gated_kernel, elementwise_grid(n), 256, 0, cudaStream_t(stream), gate, up,
+                        out, n, kind, int(cols), static_cast<uint8_t*>(prepared)));
+  DRIFT_LAUNCHED("gated_f32");
+  return 0;
+}
+
 int drift_add(const float* a, const float* b, float* out, int64_t n, drift_stream_t stream) {
   if (n < 0) return invalid("add over %lld values", (long long)n);
   if (n == 0) return 0;
@@ -414,7 +466,7 @@ int drift_gated(int kind, const float* gate, const float* up, float* out, int64_
   if (n == 0) return 0;
   if (!gate || !up || !out) return invalid("gated: a null tensor");
   DRIFT_CUDA(launch_pdl(gated_kernel, elementwise_grid(n), 256, 0, cudaStream_t(stream), gate, up,
-                        out, n, kind));
+                        out, n, kind, 32, static_cast<uint8_t*>(nullptr)));
   DRIFT_LAUNCHED("gated_f32");
   return 0;
 }

@@ -83,9 +83,11 @@ size_t drift_linear_workspace_bytes(int64_t m, int64_t k) {
 
 int drift_workspace_reserve(size_t bytes) { return workspace_reserve(bytes, nullptr); }
 
-int drift_linears(int x_dtype, const void* x, int count, const int* weight_dtypes,
-                  const void* const* weights, float* const* outs, const int64_t* ns, int64_t m,
-                  int64_t k, drift_stream_t stream) {
+// drift_linears, with x's records already written (`prepared`, or null to
+// write them here).
+static int linears(int x_dtype, const void* x, const void* prepared, int count,
+                   const int* weight_dtypes, const void* const* weights, float* const* outs,
+                   const int64_t* ns, int64_t m, int64_t k, cudaStream_t s) {
   if (count < 0 || (count > 0 && (!weight_dtypes || !weights || !outs || !ns)))
     return invalid("linears: %d products without their weights", count);
   for (int i = 0; i < count; ++i)
@@ -94,10 +96,9 @@ int drift_linears(int x_dtype, const void* x, int count, const int* weight_dtype
     // an empty sum: zero rows of out, or rows of zeros
     for (int i = 0; i < count; ++i)
       if (m > 0 && ns[i] > 0)
-        DRIFT_CUDA(cudaMemsetAsync(outs[i], 0, size_t(m * ns[i]) * 4, cudaStream_t(stream)));
+        DRIFT_CUDA(cudaMemsetAsync(outs[i], 0, size_t(m * ns[i]) * 4, s));
     return 0;
   }
-  const cudaStream_t s = cudaStream_t(stream);
   bool quantized = false, tensor_cores = false;
   for (int i = 0; i < count; ++i) {
     const bool tc = weight_dtypes[i] != DRIFT_F32 && m >= GEMM_MINIMUM_ROWS &&
@@ -105,13 +106,15 @@ int drift_linears(int x_dtype, const void* x, int count, const int* weight_dtype
     tensor_cores |= tc;
     quantized |= weight_dtypes[i] != DRIFT_F32 && !tc;
   }
-  const size_t records_bytes = quantized ? records_region(m, k) : 0;
+  const size_t records_bytes = quantized && !prepared ? records_region(m, k) : 0;
   void* w = nullptr;
-  if (quantized || tensor_cores)
+  if ((quantized && !prepared) || tensor_cores)
     DRIFT_TRY(workspace_reserve(records_bytes + (tensor_cores ? tc_workspace_bytes(m, k) : 0), &w));
-  uint8_t* records = static_cast<uint8_t*>(w);
+  const uint8_t* records =
+      prepared ? static_cast<const uint8_t*>(prepared) : static_cast<uint8_t*>(w);
   uint8_t* tc_region = static_cast<uint8_t*>(w) + records_bytes;
-  if (quantized) DRIFT_TRY(prepare_x_mma(x_dtype, x, m, k, records, s));  // one preparation for all
+  if (quantized && !prepared)  // one preparation for all
+    DRIFT_TRY(prepare_x_mma(x_dtype, x, m, k, static_cast<uint8_t*>(w), s));
   // streamed products of one type that fit one balanced launch take it
   // together (the same bits as one by one)
   bool together = quantized && !tensor_cores && count >= 2;
@@ -130,6 +133,23 @@ int drift_linears(int x_dtype, const void* x, int count, const int* weight_dtype
       DRIFT_TRY(matvec_prepared(weight_dtypes[i], weights[i], records, outs[i], ns[i], k, m, s));
   }
   return 0;
+}
+
+int drift_linears(int x_dtype, const void* x, int count, const int* weight_dtypes,
+                  const void* const* weights, float* const* outs, const int64_t* ns, int64_t m,
+                  int64_t k, drift_stream_t stream) {
+  return linears(x_dtype, x, nullptr, count, weight_dtypes, weights, outs, ns, m, k,
+                 cudaStream_t(stream));
+}
+
+int drift_linears_prepared(int x_dtype, const void* x, const void* prepared, int count,
+                           const int* weight_dtypes, const void* const* weights,
+                           float* const* outs, const int64_t* ns, int64_t m, int64_t k,
+                           drift_stream_t stream) {
+  if (!prepared) return invalid("linears: no prepared x");
+  if (x_dtype != DRIFT_F32) return invalid("linears: prepared x comes from F32 x");
+  return linears(x_dtype, x, prepared, count, weight_dtypes, weights, outs, ns, m, k,
+                 cudaStream_t(stream));
 }
 
 int drift_linear(int x_dtype, const void* x, int weight_dtype, const void* weight, float* out,

@@ -20,6 +20,7 @@
 
 #include "common.cuh"
 #include "mma_i8.cuh"
+#include "x22.cuh"
 #include "quant.cuh"
 #include "registry.cuh"
 
@@ -105,44 +106,13 @@ __global__ void __launch_bounds__(256) quantize_x22_mma_kernel(const void* x, ui
   const int lane = threadIdx.x % WARP;
   const int block = int(index % blocks);
   const int v = int(index / blocks);  // pass * 8 + slot
-  const int pass = v / 8, g = v % 8;
   float value = 0.0f;
   if (v < vectors) {
     const long long at = ((long long)v * blocks + block) * 32 + lane;
     value = BF16 ? __uint_as_float(uint32_t(reinterpret_cast<const uint16_t*>(x)[at]) << 16)
                  : reinterpret_cast<const float*>(x)[at];
   }
-  float amax = fabsf(value);
-  bool finite = isfinite(value);
-#pragma unroll
-  for (int o = 16; o > 0; o /= 2) {
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    finite = __all_sync(0xffffffffu, finite);
-  }
-  int X = 0;
-  float s = 0.0f;
-  if (!finite) {
-    s = __int_as_float(0x7fc00000);
-  } else if (amax > 0.0f) {
-    const int e = ilogbf(amax) + 1;
-    s = ldexpf(1.0f, e - X_BITS);
-    X = __float2int_rn(ldexpf(value, X_BITS - e));
-  }
-  uint8_t* record = records + ((long long)pass * blocks + block) * MMA_RECORD_BYTES;
-  // value j = lane sits in byte j % 4 of word j / 4 of each plane
-  const int w = lane / 4;
-  record[mma_plane_byte(g, 0, w) + lane % 4] = uint8_t(X & 0xff);
-  record[mma_plane_byte(g, 1, w) + lane % 4] = uint8_t((X >> 8) & 0xff);
-  record[mma_plane_byte(g, 2, w) + lane % 4] = uint8_t((X >> 16) & 0xff);
-  int sum = X;
-#pragma unroll
-  for (int o = 16; o > 0; o /= 2) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  if (lane == 0) {
-    uint8_t* scales = record + mma_scale_byte(g);
-    reinterpret_cast<float*>(scales)[0] = s;
-    reinterpret_cast<int*>(scales)[1] = sum;
-    reinterpret_cast<float*>(scales)[2] = float(sum);
-  }
+  x22_record_block(value, records, v, block, blocks);
 }
 
 // ---- the product -----------------------------------------------------------------

@@ -3,7 +3,8 @@ runner's DenseDecoder.run (runner/src/drift/runner/models/DenseDecoder.scala:
 778-939), for a batch of sequences, on one GPU or tensor-parallel across the
 GPUs of one box (drift_b200/tensor_parallel.py).
 
-Per token and layer: RMSNorm; q, k, v products (one x preparation); per-head
+Per token and layer: RMSNorm (writing the products' x records); q, k, v
+products in one launch; per-head
 q/k RMSNorm (Qwen3), RoPE of q and k and the new k, v into each sequence's
 paged F16 cache (one fused launch for the batch); attention over the caches
 (one launch for the batch); o product; residual add + RMSNorm; gate and up
@@ -165,6 +166,10 @@ class DenseDecoder:
         self.gate = torch.zeros(b, self.ffn, **f32)
         self.up = torch.zeros(b, self.ffn, **f32)
         self.logits = torch.zeros(b, self.vocab_rows, **f32)
+        # x's records for the products, written by the kernel that makes x
+        # (the norms, the attention join, SwiGLU): one buffer, each product
+        # reading it before the next producer writes it
+        self.prepared = ops.prepared_x(b, max(c.hidden, self.q_heads * hd, self.ffn))
         self.graph: Optional[torch.cuda.CUDAGraph] = None
         self._positions_host: list[int] = [0] * b
 
@@ -191,10 +196,12 @@ class DenseDecoder:
         device copy (so a captured step replays at new positions)."""
         ops, c, w = self.ops, self.config, self.weights
         b, hd = self.batch, c.head_dim
+        prepared = self.prepared
         ops.embedding(w.embedding, self.ids, self.x)
-        ops.rms_norm(self.x, w.layers[0].attention_norm, c.epsilon, 0.0, self.normed)
+        ops.add_rms_norm(self.x, None, RowNorm(w.layers[0].attention_norm, c.epsilon, 0.0,
+                                               self.normed), prepared)
         for index, (layer, cache) in enumerate(zip(w.layers, self.caches)):
-            ops.linears(self.normed, [layer.q, layer.k, layer.v], [self.q, self.k, self.v])
+            ops.linears(self.normed, [layer.q, layer.k, layer.v], [self.q, self.k, self.v], prepared)
             # per-head q/k norms, rope, cache write: one launch for the batch;
             # then every sequence's attention in one launch
             ops.attention_inputs_decode(
@@ -202,18 +209,20 @@ class DenseDecoder:
                 self.v.view(b, self.kv_heads, hd), layer.q_norm, layer.k_norm, c.epsilon,
                 self.positions, self.rope, self.q_turned, cache, self.page_tables)
             ops.attention_decode(self.q_turned, cache, self.page_tables, self.positions,
-                                 self.context, self.attention, self.attended)
-            ops.linear(self.attended.view(b, self.q_heads * hd), layer.o, self.projected)
+                                 self.context, self.attention, self.attended, prepared)
+            ops.linears(self.attended.view(b, self.q_heads * hd), [layer.o], [self.projected],
+                        prepared)
             self._all_reduce(self.projected)
             ops.add_rms_norm(self.x, self.projected,
-                             RowNorm(layer.mlp_norm, c.epsilon, 0.0, self.normed))
-            ops.linears(self.normed, [layer.gate, layer.up], [self.gate, self.up])
-            ops.gated(SILU, self.gate, self.up, self.gate)
-            ops.linear(self.gate, layer.down, self.projected)
+                             RowNorm(layer.mlp_norm, c.epsilon, 0.0, self.normed), prepared)
+            ops.linears(self.normed, [layer.gate, layer.up], [self.gate, self.up], prepared)
+            ops.gated(SILU, self.gate, self.up, self.gate, prepared)
+            ops.linears(self.gate, [layer.down], [self.projected], prepared)
             self._all_reduce(self.projected)
             following = w.layers[index + 1].attention_norm if index + 1 < len(w.layers) else w.final_norm
-            ops.add_rms_norm(self.x, self.projected, RowNorm(following, c.epsilon, 0.0, self.normed))
-        ops.linear(self.normed, w.lm_head, self.logits)
+            ops.add_rms_norm(self.x, self.projected, RowNorm(following, c.epsilon, 0.0, self.normed),
+                             prepared)
+        ops.linears(self.normed, [w.lm_head], [self.logits], prepared)
         return self.logits
 
     def reserve(self) -> None:

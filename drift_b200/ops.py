@@ -216,8 +216,18 @@ class CudaOps:
         """out = x · weightᵀ (ops/LinearOps.scala:147-150)."""
         self.linears(x, [weight], [out])
 
-    def linears(self, x: torch.Tensor, weights: Sequence, outs: Sequence[torch.Tensor]) -> None:
-        """Several products of the same x, x prepared once (LinearOps.scala:152-156)."""
+    def prepared_x(self, m: int, k: int) -> torch.Tensor:
+        """A buffer for the records of m rows of k values, which a producer
+        (add_rms_norm, gated, attention_decode with `prepared=`) writes for
+        the products that follow (linears with `prepared=`)."""
+        size = self.lib.drift_prepared_x_bytes(m, k)
+        _require(size > 0, f"no prepared x for [{m}, {k}]")
+        return torch.empty(size, dtype=torch.uint8, device="cuda")
+
+    def linears(self, x: torch.Tensor, weights: Sequence, outs: Sequence[torch.Tensor],
+                prepared: Optional[torch.Tensor] = None) -> None:
+        """Several products of the same x, x prepared once (LinearOps.scala:152-156);
+        `prepared`: x's records, already written by the kernel that made x."""
         shapes = [self._check_linear(x, w, o) for w, o in zip(weights, outs)]
         _require(len(weights) == len(outs), "linears: as many outs as weights")
         if not shapes:
@@ -231,8 +241,13 @@ class CudaOps:
         for i, (w, o, (_, n, _)) in enumerate(zip(weights, outs, shapes)):
             dtype, data = self._weight(w)
             dtypes[i], wptrs[i], optrs[i], ns[i] = dtype, data.data_ptr(), o.data_ptr(), n
-        status = self.lib.drift_linears(_x_dtype("linear", x), _ptr(x), count, dtypes, wptrs,
-                                        optrs, ns, m, k, self._stream())
+        if prepared is None:
+            status = self.lib.drift_linears(_x_dtype("linear", x), _ptr(x), count, dtypes, wptrs,
+                                            optrs, ns, m, k, self._stream())
+        else:
+            status = self.lib.drift_linears_prepared(_x_dtype("linear", x), _ptr(x),
+                                                     _ptr(prepared), count, dtypes, wptrs, optrs,
+                                                     ns, m, k, self._stream())
         check("drift_linears", status)
 
     def embedding(self, table: Stored, ids: torch.Tensor, out: torch.Tensor) -> None:
@@ -269,15 +284,23 @@ class CudaOps:
                                          rows, x.shape[-1], self._stream())
         check("drift_rms_norm", status)
 
-    def add_rms_norm(self, x, y, norm: RowNorm) -> None:
+    def add_rms_norm(self, x, y, norm: RowNorm, prepared: Optional[torch.Tensor] = None) -> None:
         """x += y, then norm's RMS norm of x into norm.out, one launch
-        (NormalisationOps.scala:217-224)."""
-        _f32("add", x, y)
-        _same_shape("add", x, y)
+        (NormalisationOps.scala:217-224); with `prepared`, norm.out's records
+        too (y None: the norm alone)."""
+        if y is not None:
+            _f32("add", x, y)
+            _same_shape("add", x, y)
         rows = self._check_row_wise("rmsNorm", x, norm.out, norm.weight)
-        status = self.lib.drift_add_rms_norm(_ptr(x), _ptr(y), _ptr(norm.weight), norm.epsilon,
-                                             norm.weight_offset, _ptr(norm.out), rows,
-                                             x.shape[-1], self._stream())
+        if prepared is None:
+            _require(y is not None, "addRmsNorm: no y")
+            status = self.lib.drift_add_rms_norm(_ptr(x), _ptr(y), _ptr(norm.weight), norm.epsilon,
+                                                 norm.weight_offset, _ptr(norm.out), rows,
+                                                 x.shape[-1], self._stream())
+        else:
+            status = self.lib.drift_add_rms_norm_prepared(
+                _ptr(x), _ptr(y), _ptr(norm.weight), norm.epsilon, norm.weight_offset,
+                _ptr(norm.out), rows, x.shape[-1], _ptr(prepared), self._stream())
         check("drift_add_rms_norm", status)
 
     def add(self, a, b, out) -> None:
@@ -287,12 +310,20 @@ class CudaOps:
         check("drift_add", self.lib.drift_add(_ptr(a), _ptr(b), _ptr(out), a.numel(),
                                               self._stream()))
 
-    def gated(self, kind: int, gate, up, out) -> None:
-        """out = kind(gate) × up: SwiGLU with SILU (NormalisationOps.scala:200-203)."""
+    def gated(self, kind: int, gate, up, out, prepared: Optional[torch.Tensor] = None) -> None:
+        """out = kind(gate) × up: SwiGLU with SILU (NormalisationOps.scala:200-203);
+        with `prepared`, out's records (rows of out's last dimension) too."""
         _f32("gated", gate, up, out)
         _same_shape("gated", gate, up, out)
-        check("drift_gated", self.lib.drift_gated(kind, _ptr(gate), _ptr(up), _ptr(out),
-                                                  gate.numel(), self._stream()))
+        if prepared is None:
+            status = self.lib.drift_gated(kind, _ptr(gate), _ptr(up), _ptr(out), gate.numel(),
+                                          self._stream())
+        else:
+            cols = out.shape[-1]
+            status = self.lib.drift_gated_prepared(kind, _ptr(gate), _ptr(up), _ptr(out),
+                                                   out.numel() // max(1, cols), cols,
+                                                   _ptr(prepared), self._stream())
+        check("drift_gated", status)
 
     # -- AttentionOps.rope (ops/AttentionOps.scala:42-45) ---------------------------------------------
     def rope(self, x, positions, rope: Rope, out) -> None:
@@ -377,9 +408,10 @@ class CudaOps:
         check("drift_attention_inputs_decode", status)
 
     def attention_decode(self, q, cache: KvCache, page_tables, positions, max_key_count: int,
-                         attention: Attention, out) -> None:
+                         attention: Attention, out, prepared: Optional[torch.Tensor] = None) -> None:
         """Attention of one query per sequence, all sequences in one launch:
-        row z of q [b, q_heads, D] at positions[z] over its keys 0..positions[z]."""
+        row z of q [b, q_heads, D] at positions[z] over its keys 0..positions[z];
+        with `prepared`, the records of out as [b, q_heads D] too."""
         _f32("attention", q, out)
         _same_shape("attention", q, out)
         b, q_heads, dim = q.shape
@@ -391,11 +423,15 @@ class CudaOps:
         _require(positions.dtype == torch.int32 and tuple(positions.shape) == (b,),
                  f"attention: positions {list(positions.shape)} for {b} sequences")
         _require(attention.causal, "a decode step's attention is causal")
-        status = self.lib.drift_attention_decode(
-            _ptr(q), b, q_heads, _ptr(cache.keys), _ptr(cache.values), cache.pages,
-            cache.page_size, cache.kv_heads, dim, _ptr(page_tables), int(page_tables.shape[1]),
-            _ptr(positions), max_key_count, attention.scale, int(attention.window or 0),
-            float(attention.softcap or 0.0), _ptr(attention.sinks), _ptr(out), self._stream())
+        args = (_ptr(q), b, q_heads, _ptr(cache.keys), _ptr(cache.values), cache.pages,
+                cache.page_size, cache.kv_heads, dim, _ptr(page_tables), int(page_tables.shape[1]),
+                _ptr(positions), max_key_count, attention.scale, int(attention.window or 0),
+                float(attention.softcap or 0.0), _ptr(attention.sinks), _ptr(out))
+        if prepared is None:
+            status = self.lib.drift_attention_decode(*args, self._stream())
+        else:
+            status = self.lib.drift_attention_decode_prepared(*args, _ptr(prepared),
+                                                              self._stream())
         check("drift_attention_decode", status)
 
     # -- ExpertsOps (ops/ExpertsOps.scala) -------------------------------------------------------------

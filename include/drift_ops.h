@@ -194,6 +194,38 @@ int drift_attention_decode(const float* q, int batch, int q_heads, const void* k
                            const int32_t* positions, int max_key_count, float scale, int window,
                            float softcap, const float* sinks, float* out, drift_stream_t stream);
 
+/* ---- prepared x (new) ------------------------------------------------------
+ * A product streams its weights against x's "records" (x per 32-value block as
+ * exact 24-bit integer planes and a scale). drift_linear writes them itself; a
+ * decode step can have the kernel that produces x write them instead, as the
+ * reference's own norm and gated kernels write the quantized x of the product
+ * that follows them (rms_norm_f32 / gated_f32 xq, xd, xs outputs,
+ * runner/kernels/norm.hip:34-35, elementwise.hip:58-59). The caller owns the
+ * buffer: drift_prepared_x_bytes(m, k) bytes for m rows of k values (k a
+ * multiple of 32). Results are bit for bit those of the unprepared calls. */
+size_t drift_prepared_x_bytes(int64_t m, int64_t k);
+/* drift_add_rms_norm (y null: drift_rms_norm), also writing out's records. */
+int drift_add_rms_norm_prepared(float* x, const float* y, const float* weight, float epsilon,
+                                float weight_offset, float* out, int64_t rows, int64_t cols,
+                                void* prepared, drift_stream_t stream);
+/* drift_gated over rows x cols values, also writing out's records. */
+int drift_gated_prepared(int kind, const float* gate, const float* up, float* out, int64_t rows,
+                         int64_t cols, void* prepared, drift_stream_t stream);
+/* drift_attention_decode (head_dim a multiple of 32), also writing the
+ * records of out viewed as [batch][q_heads * head_dim]. */
+int drift_attention_decode_prepared(const float* q, int batch, int q_heads, const void* keys,
+                                    const void* values, int pages, int page_size, int kv_heads,
+                                    int head_dim, const int32_t* page_tables, int table_stride,
+                                    const int32_t* positions, int max_key_count, float scale,
+                                    int window, float softcap, const float* sinks, float* out,
+                                    void* prepared, drift_stream_t stream);
+/* drift_linears over prepared records of F32 x (x itself is still read by
+ * the products of 32 rows or more, which take the tensor cores). */
+int drift_linears_prepared(int x_dtype, const void* x, const void* prepared, int count,
+                           const int* weight_dtypes, const void* const* weights,
+                           float* const* outs, const int64_t* ns, int64_t m, int64_t k,
+                           drift_stream_t stream);
+
 /* The library keeps one grow-only scratch buffer per device for the products'
  * prepared x (as the runner's HIP backend keeps grow-only scratch,
  * ops/HipBase.scala:341-351). Reserving it ahead keeps allocation out of a

@@ -1,0 +1,126 @@
+"""Prepared x: the producers of a product's x (add_rms_norm, gated, the decode
+attention) writing its records themselves, as the reference's rms_norm_f32 and
+gated_f32 write xq/xd/xs for the product that follows (runner/kernels/
+norm.hip:34-35, elementwise.hip:58-59). Products over prepared records are
+bit for bit the products that prepare x themselves."""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from drift_b200 import synthetic
+from drift_b200.ops import SILU, Attention, CudaOps, KvCache, RowNorm, Stored
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ops():
+    return CudaOps()
+
+
+def weights(rng, shapes, k, dtype=oracle.Q4_1):
+    return [Stored.upload(dtype, (n, k), synthetic.quantized(rng, dtype, n, k)) for n in shapes]
+
+
+@pytest.mark.parametrize("m", [1, 2, 5])
+@pytest.mark.parametrize("k", [1024, 4096, 6144])
+def test_norm_records_feed_linears(ops, m, k):
+    rng = np.random.default_rng(m * 7 + k)
+    ws = weights(rng, [384, 96, 96], k)
+    x = torch.from_numpy(rng.standard_normal((m, k)).astype(np.float32)).cuda()
+    y = torch.from_numpy(rng.standard_normal((m, k)).astype(np.float32)).cuda()
+    weight = torch.from_numpy((1 + 0.02 * rng.standard_normal(k)).astype(np.float32)).cuda()
+    prepared = ops.prepared_x(m, k)
+    x1, normed1 = x.clone(), torch.empty_like(x)
+    ops.add_rms_norm(x1, y, RowNorm(weight, 1e-6, 0.0, normed1), prepared)
+    fused = [torch.empty(m, w.shape[0], device="cuda") for w in ws]
+    ops.linears(normed1, ws, fused, prepared)
+    x2, normed2 = x.clone(), torch.empty_like(x)
+    ops.add_rms_norm(x2, y, RowNorm(weight, 1e-6, 0.0, normed2))
+    assert torch.equal(x1, x2) and torch.equal(normed1, normed2)
+    for w, f in zip(ws, fused):
+        alone = torch.empty_like(f)
+        ops.linear(normed2, w, alone)
+        assert torch.equal(f, alone)
+
+
+def test_norm_alone_records(ops):
+    """y None: the plain rmsNorm, with records."""
+    rng = np.random.default_rng(3)
+    m, k = 3, 2048
+    (w,) = weights(rng, [200], k)
+    x = torch.from_numpy(rng.standard_normal((m, k)).astype(np.float32)).cuda()
+    weight = torch.from_numpy((1 + 0.02 * rng.standard_normal(k)).astype(np.float32)).cuda()
+    prepared = ops.prepared_x(m, k)
+    normed = torch.empty_like(x)
+    ops.add_rms_norm(x, None, RowNorm(weight, 1e-6, 0.0, normed), prepared)
+    fused = torch.empty(m, 200, device="cuda")
+    ops.linears(normed, [w], [fused], prepared)
+    expected = torch.empty_like(normed)
+    ops.rms_norm(x, weight, 1e-6, 0.0, expected)
+    assert torch.equal(normed, expected)
+    alone = torch.empty_like(fused)
+    ops.linear(expected, w, alone)
+    assert torch.equal(fused, alone)
+
+
+@pytest.mark.parametrize("m", [1, 3, 16])
+def test_gated_records_feed_linear(ops, m):
+    rng = np.random.default_rng(m)
+    ffn, hidden = 1536, 512
+    (down,) = weights(rng, [hidden], ffn)
+    gate = torch.from_numpy(rng.standard_normal((m, ffn)).astype(np.float32)).cuda()
+    up = torch.from_numpy(rng.standard_normal((m, ffn)).astype(np.float32)).cuda()
+    prepared = ops.prepared_x(m, ffn)
+    hidden1 = torch.empty_like(gate)
+    ops.gated(SILU, gate, up, hidden1, prepared)
+    fused = torch.empty(m, hidden, device="cuda")
+    ops.linears(hidden1, [down], [fused], prepared)
+    hidden2 = torch.empty_like(gate)
+    ops.gated(SILU, gate, up, hidden2)
+    assert torch.equal(hidden1, hidden2)
+    alone = torch.empty_like(fused)
+    ops.linear(hidden2, down, alone)
+    assert torch.equal(fused, alone)
+
+
+@pytest.mark.parametrize("dim,q_heads,kv_heads", [(128, 8, 2), (64, 4, 4), (256, 4, 1)])
+def test_attention_records_feed_linear(ops, dim, q_heads, kv_heads):
+    rng = np.random.default_rng(dim)
+    batch, page_size, per_sequence = 3, 16, 8
+    pages = batch * per_sequence
+    cache = KvCache(torch.from_numpy(rng.standard_normal((pages, page_size, kv_heads, dim))
+                                     .astype(np.float16)).cuda(),
+                    torch.from_numpy(rng.standard_normal((pages, kv_heads, dim, page_size))
+                                     .astype(np.float16)).cuda(), page_size)
+    tables = torch.arange(pages, dtype=torch.int32, device="cuda").view(batch, per_sequence)
+    positions = torch.tensor([3, 40, 100], dtype=torch.int32, device="cuda")
+    q = torch.from_numpy(rng.standard_normal((batch, q_heads, dim)).astype(np.float32)).cuda()
+    attention = Attention(1.0 / math.sqrt(dim))
+    (o,) = weights(rng, [256], q_heads * dim)
+    prepared = ops.prepared_x(batch, q_heads * dim)
+    out1 = torch.empty_like(q)
+    ops.attention_decode(q, cache, tables, positions, per_sequence * page_size, attention, out1,
+                         prepared)
+    fused = torch.empty(batch, 256, device="cuda")
+    ops.linears(out1.view(batch, -1), [o], [fused], prepared)
+    out2 = torch.empty_like(q)
+    ops.attention_decode(q, cache, tables, positions, per_sequence * page_size, attention, out2)
+    assert torch.equal(out1, out2)
+    alone = torch.empty_like(fused)
+    ops.linear(out2.view(batch, -1), o, alone)
+    assert torch.equal(fused, alone)
+
+
+def test_prepared_refusals(ops):
+    x = torch.zeros(2, 100, device="cuda")
+    w = torch.ones(100, device="cuda")
+    buffer = torch.zeros(1 << 16, dtype=torch.uint8, device="cuda")
+    with pytest.raises(ValueError, match="32-value blocks"):
+        ops.add_rms_norm(x, None, RowNorm(w, 1e-6, 0.0, torch.empty_like(x)), buffer)
+    with pytest.raises(ValueError, match="32-value blocks"):
+        ops.gated(SILU, x, x, torch.empty_like(x), buffer)
