@@ -178,3 +178,55 @@ def test_fused_attention_inputs_are_the_separate_ops(ops):
     assert torch.equal(fused_q, q_turned)
     assert torch.equal(fused_cache.keys, cache.keys)
     assert torch.equal(fused_cache.values, cache.values)
+
+
+# The known answers of the reference's AttentionReferenceTests.scala:47-111 on
+# the GPU kernel (the oracle holds them in test_oracle_attention.py).
+
+def test_one_visible_key_gives_its_value(ops):
+    cache = KvCache.allocate(1, 16, 1, 16 * 4)
+    table = torch.zeros(1, dtype=torch.int32, device="cuda")
+    # heads of 64 (the kernels' narrowest): value d / 8 for d < 16, exact in F16
+    dim = 64
+    value = (torch.arange(dim, device="cuda") % 16 / 8).float().view(1, 1, dim)
+    ops.cache_write(torch.full((1, 1, dim), 0.5, device="cuda"), value, cache, table, 0)
+    q = torch.ones(1, 1, dim, device="cuda")
+    out = torch.empty_like(q)
+    ops.attention(q, cache, table, 0, 1, Attention(0.25 / 4), out)  # q.k x scale = 2
+    assert torch.equal(out, value)
+    ops.attention(q, cache, table, 0, 1,
+                  Attention(0.25 / 4, sinks=torch.tensor([2.0], device="cuda")), out)
+    assert torch.equal(out, value / 2)
+
+
+def plain_gpu(ops, shuffled=False, tokens=5, window=None, queries=None):
+    rng = np.random.default_rng(7)
+    key_count, q_heads, kv_heads, dim, page_size = 40, 4, 2, 64, 16
+    k = rng.standard_normal((key_count, kv_heads, dim)).astype(np.float32)
+    v = rng.standard_normal((key_count, kv_heads, dim)).astype(np.float32)
+    drawn = rng.standard_normal((5, q_heads, dim)).astype(np.float32)
+    q = drawn if queries is None else queries
+    table = torch.tensor([2, 0, 1] if shuffled else [0, 1, 2], dtype=torch.int32, device="cuda")
+    cache = KvCache.allocate(3, page_size, kv_heads, dim)
+    ops.cache_write(torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda(), cache, table, 0)
+    q = q[-tokens:]
+    out = torch.empty(tokens, q_heads, dim, device="cuda")
+    ops.attention(torch.from_numpy(q).cuda(), cache, table, key_count - tokens, key_count,
+                  Attention(1 / math.sqrt(dim), True, window), out)
+    return out, q
+
+
+def test_page_order_does_not_matter(ops):
+    assert torch.equal(plain_gpu(ops)[0], plain_gpu(ops, shuffled=True)[0])
+
+
+def test_prefill_then_decode_equals_one_longer_prefill(ops):
+    prefill, q = plain_gpu(ops)
+    decode, _ = plain_gpu(ops, tokens=1, queries=q)
+    assert torch.equal(prefill[-1:], decode)
+
+
+def test_a_whole_window_changes_nothing_and_a_narrow_one_does(ops):
+    full, _ = plain_gpu(ops)
+    assert torch.equal(plain_gpu(ops, window=40)[0], full)
+    assert not torch.equal(plain_gpu(ops, window=8)[0], full)

@@ -45,3 +45,66 @@ def test_attention_is_the_softmax_of_the_definition():
             w = np.exp(scores - scores.max())
             expected = (w @ vf[:seen, g]) / w.sum()
             np.testing.assert_allclose(got[t, h], expected.astype(np.float32), rtol=1e-6, atol=1e-7)
+
+
+# The known answers of the reference's AttentionReferenceTests.scala:47-111,
+# held by the oracle (the GPU kernel holds them in test_gpu_attention.py).
+
+def one_key_cache():
+    """A cache of one page whose position 0 holds k = 0.5, v = d / 8 (exact
+    in F16), 16 dimensions, one key head (AttentionReferenceTests.scala:47-58)."""
+    keys = np.zeros((1, 16, 1, 16), dtype=np.uint16)
+    values = np.zeros((1, 1, 16, 16), dtype=np.uint16)
+    value = (np.arange(16) / 8).astype(np.float32)
+    oracle.cache_write(np.full((1, 1, 16), 0.5, np.float32), value.reshape(1, 1, 16), keys,
+                       values, 16, np.zeros(1, np.int32), 0)
+    return keys, values, value
+
+
+def test_one_visible_key_gives_its_value():
+    keys, values, value = one_key_cache()
+    q = np.ones((1, 1, 16), np.float32)
+    out = oracle.attention(q, keys, values, 16, 1, np.zeros(1, np.int32), 0, 1, 0.25)
+    np.testing.assert_array_equal(out.reshape(16), value)
+    # a sink of the same logit as the key (q.k x scale = 2) takes half the weight
+    out = oracle.attention(q, keys, values, 16, 1, np.zeros(1, np.int32), 0, 1, 0.25,
+                           sinks=np.array([2.0], np.float32))
+    np.testing.assert_array_equal(out.reshape(16), value / 2)
+
+
+def plain_case(rng_seed=7, shuffled=False, tokens=5, window=0, queries=None):
+    """AttentionReferenceTests' `plain` case: 5 tokens over 40 keys, 4 query
+    heads over 2 key heads of 16, causal, pages of 16 (seeded here with
+    numpy: the shapes and the invariants are the reference's, not its draws)."""
+    rng = np.random.default_rng(rng_seed)
+    key_count, q_heads, kv_heads, dim, page_size = 40, 4, 2, 16, 16
+    pages = 3
+    k = rng.standard_normal((key_count, kv_heads, dim)).astype(np.float32)
+    v = rng.standard_normal((key_count, kv_heads, dim)).astype(np.float32)
+    drawn = rng.standard_normal((5, q_heads, dim)).astype(np.float32)
+    q = drawn if queries is None else queries
+    table = np.array([2, 0, 1] if shuffled else [0, 1, 2], np.int32)
+    keys = np.zeros((pages, page_size, kv_heads, dim), np.uint16)
+    values = np.zeros((pages, kv_heads, dim, page_size), np.uint16)
+    oracle.cache_write(k, v, keys, values, page_size, table, 0)
+    q = q[-tokens:]
+    return oracle.attention(q, keys, values, page_size, kv_heads, table, key_count - tokens,
+                            key_count, 1 / math.sqrt(dim), True, window), q
+
+
+def test_page_order_does_not_matter():
+    plain, _ = plain_case()
+    shuffled, _ = plain_case(shuffled=True)
+    np.testing.assert_array_equal(plain, shuffled)
+
+
+def test_prefill_then_decode_equals_one_longer_prefill():
+    prefill, q = plain_case()
+    decode, _ = plain_case(tokens=1, queries=q)
+    np.testing.assert_array_equal(prefill[-1:], decode)
+
+
+def test_a_whole_window_changes_nothing_and_a_narrow_one_does():
+    full, _ = plain_case()
+    np.testing.assert_array_equal(plain_case(window=40)[0], full)
+    assert not np.array_equal(plain_case(window=8)[0], full)
