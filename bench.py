@@ -1,8 +1,8 @@
-"""Benchmark of the quantized-matvec hot path on B200.
+"""Benchmark of the quantized-matvec hot path (benchmark config C2) on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
-Workload: Q4_1 weights (32-element blocks, f16
+Workload (benchmark config C2): Q4_1 weights (32-element blocks, f16
 scale d ~ U(0.002, 0.02) and min m = -8 d, 4-bit codes uniform), x bf16
 ~ N(0, 1), batches 1, 8 and 64 over the four shapes 4096x4096, 12288x4096,
 4096x12288 and 151936x4096 (the lm-head). One step is the whole sweep: for
@@ -12,7 +12,7 @@ weight in L2 from the previous visit (inputs larger than L2; no flush).
 
 The line's metric is weight-streaming throughput: algorithmic bytes
 (weights + x + y of every product) over the step time, in GB/s, also as a
-fraction of BASELINE's 8 TB/s. `value` is device time with inputs resident
+fraction of the nominal 8 TB/s. `value` is device time with inputs resident
 (the step replayed as a CUDA graph); `e2e` runs the same step through the
 public C ABI with host buffers, copying each x in and each y out inside the
 timed region. With N GPUs each rank runs its own sweep on its own weights
@@ -259,7 +259,7 @@ def run_gpu(args) -> dict | None:
     del weights, xs, ys, host_x, host_y
     torch.cuda.empty_cache()
 
-    # BASELINE C4: the dense decoder's decode step, tensor-parallel over the
+    # benchmark config C4: the dense decoder's decode step, tensor-parallel over the
     # job's GPUs (one NCCL group), tok/s at each batch
     decode = run_decode(args, ops, rank, world, stream) if args.decode else None
 
@@ -290,7 +290,7 @@ def run_gpu(args) -> dict | None:
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "q4_1 weights, bf16 x; int8 planes (dp4a, mma.sync s8) and f16 tcgen05 products, f32 out",
-        "data": "synthetic (seeded; BASELINE C2 value laws)",
+        "data": "synthetic (seeded; benchmark config C2 value laws)",
         "config": {
             "workload": "C2 Q4_1 matvec sweep: batches 1/8/64 x shapes 4096x4096, "
                         "12288x4096, 4096x12288, 151936x4096",
@@ -328,7 +328,7 @@ DECODE_CONTEXT = 4096
 
 
 def run_decode(args, ops, rank: int, world: int, stream) -> dict:
-    """Decode tok/s of BASELINE C4 (36 layers, hidden 4096, 32 q / 8 kv heads
+    """Decode tok/s of benchmark config C4 (36 layers, hidden 4096, 32 q / 8 kv heads
     of 128, FFN 12288, vocabulary 151936; random-init Q4_1 weights, Q8_0
     embedding; F16 KV caches prefilled with N(0, 1) to 4095 positions): one
     step at position 4095 (4096 keys) captured as a CUDA graph, replayed,
@@ -554,7 +554,7 @@ def run_reference(args) -> dict | None:
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "q4_1 weights, f32 x (bf16 widened), f64 sums",
-        "data": "synthetic (seeded; BASELINE C2 value laws)",
+        "data": "synthetic (seeded; benchmark config C2 value laws)",
         "config": {"workload": "C2 Q4_1 matvec sweep (row sample), CPU reference path"},
         "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads,
                          "kind": "port", "sample": sample},

@@ -15,7 +15,7 @@ the matching columns of o and down (row-split, one all-reduce each), and its
 share of the vocabulary rows of the lm-head; the embedding and the norms are
 replicated.
 
-This is the harness BASELINE's decode tok/s is measured on: weights are
+This is the harness the benchmark's decode tok/s is measured on: weights are
 random-init (the benchmark laws), the caches prefilled with N(0, 1) keys and
 values; a step is captured once as a CUDA graph and replayed.
 """
@@ -37,7 +37,7 @@ from .tensor_parallel import row_range
 
 @dataclass(frozen=True)
 class DenseConfig:
-    """A dense decoder's shape (BASELINE C4: Qwen3-8B-like)."""
+    """A dense decoder's shape (benchmark config C4: Qwen3-8B-like)."""
     layers: int = 36
     hidden: int = 4096
     q_heads: int = 32
@@ -175,7 +175,7 @@ class DenseDecoder:
 
     def prefill_random(self, positions: int, seed: int = 1) -> None:
         """Every sequence's cache holds `positions` positions of N(0, 1) keys
-        and values (BASELINE C4's prefilled cache), as F16."""
+        and values (benchmark config C4's prefilled cache), as F16."""
         g = torch.Generator(device="cuda")
         g.manual_seed(seed)
         used = (positions + self.config.page_size - 1) // self.config.page_size

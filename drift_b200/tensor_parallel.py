@@ -1,6 +1,6 @@
 """Tensor-parallel products across the GPUs of one box, one process per GPU.
 
-The split of the runner's dense layers that BASELINE's decode configs name
+The split of the runner's dense layers that the benchmark's decode configs name
 (column-split QKV / gate / up, row-split o / down with one all-reduce; the
 reference runs one device, runner/src/drift/runner/native/HipRuntime.scala:
 40-43, so this is the B200 build's own layout):

@@ -3,7 +3,7 @@ reference's CpuAttention.cacheWrite/attention, ops/CpuAttention.scala:
 181-288), over the reference's paged F16 cache layout.
 
 cacheWrite is bit-exact (F32 to F16, nearest even). attention is held to
-BASELINE's 1e-4 absolute + 1e-3 relative: the GPU sums in F32 where the CPU
+the benchmark's 1e-4 absolute + 1e-3 relative: the GPU sums in F32 where the CPU
 sums in Double.
 """
 

@@ -2,7 +2,7 @@
 on a small model against the same step composed from the oracle's ops (the
 reference's CpuOps), weights and caches downloaded from the GPU.
 
-Held to BASELINE's 1e-4 absolute + 1e-3 relative on the logits after two
+Held to the benchmark's 1e-4 absolute + 1e-3 relative on the logits after two
 layers: each op is within its own bar, and the step compounds them.
 """
 

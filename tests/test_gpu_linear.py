@@ -3,7 +3,7 @@ LinearTests, runner/gpuTest/src/drift/runner/LinearTests.scala, on this path).
 
 Up to 31 rows of x (the reference's matrix-vector path, float x) each case is
 held to two bars:
-- BASELINE's: |gpu - oracle| <= 1e-4 + 1e-3 |oracle|;
+- the benchmark's: |gpu - oracle| <= 1e-4 + 1e-3 |oracle|;
 - the rigorous bound of the x preparation: x enters as exact integers 21 bits
   below each 32-value block's largest |x| (drift_b200/csrc/quant.cuh), so an
   output can move by at most sum_k |w_k| * max|x_block| * 2^-21, plus float
@@ -136,7 +136,7 @@ def test_linear_rows_do_not_depend_on_batch(ops):
         assert torch.equal(one[0], batch[i])
 
 
-# The BASELINE C2 shapes at full size: sampled rows against the oracle.
+# The benchmark config C2 shapes at full size: sampled rows against the oracle.
 FULL = [(4096, 4096), (12288, 4096), (4096, 12288), (151936, 4096)]
 
 

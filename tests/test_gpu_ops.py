@@ -14,7 +14,7 @@ from tests.conftest import within
 
 pytestmark = pytest.mark.gpu
 
-# SmallOpsTests' awkward shapes (L22-29) and the BASELINE C3 ones.
+# SmallOpsTests' awkward shapes (L22-29) and the benchmark config C3 ones.
 SHAPES = [(1, 1), (3, 7), (2, 255), (5, 4097), (17, 2560), (1, 2048), (1, 4096), (64, 4096)]
 
 
@@ -42,7 +42,7 @@ def test_embedding_is_bit_exact(ops, dtype):
 
 
 def test_embedding_full_vocabulary_q8_0(ops):
-    """BASELINE C3: a Q8_0 table 151936 x 4096, random ids, b in {1, 8, 16, 64}."""
+    """benchmark config C3: a Q8_0 table 151936 x 4096, random ids, b in {1, 8, 16, 64}."""
     rng = np.random.default_rng(22)
     vocab, cols = 151936, 4096
     table = synthetic.quantized(rng, oracle.Q8_0, vocab, cols)
@@ -133,7 +133,7 @@ def test_add_and_gated_in_place(ops):
 # ---- rotary embedding --------------------------------------------------------------------------
 @pytest.mark.parametrize("layout", [NEOX, INTERLEAVED], ids=["neox", "interleaved"])
 def test_rope_matches_the_cpu_angle(ops, layout):
-    """BASELINE C3: theta 1e6, head_dim 128, positions up to 8191, q [b, 32,
+    """benchmark config C3: theta 1e6, head_dim 128, positions up to 8191, q [b, 32,
     128] and k [b, 8, 128]. The reference holds its own kernel to 1e-2
     (SmallOpsTests L450-500); this one computes the CPU's angle bit for bit
     and lands within about an ulp."""
@@ -164,7 +164,7 @@ def test_rope_partial_and_known_turns(ops):
 
 # ---- mixture of experts -------------------------------------------------------------------------
 def test_route_matches_oracle(ops):
-    """BASELINE C5: 512 experts, top-10, logits ~ N(0, 1)."""
+    """benchmark config C5: 512 experts, top-10, logits ~ N(0, 1)."""
     rng = np.random.default_rng(50)
     for tokens in (1, 16, 64):
         logits = synthetic.gaussian(rng, tokens, 512)

@@ -134,7 +134,7 @@ def test_two_gloo_ranks_reassemble_the_product(dtype):
     for rank, out, part, lo, hi, slowest in got:
         # the column split is the unsplit rows, bit for bit
         np.testing.assert_array_equal(part, hidden[:, lo:hi])
-        # the row split sums two float partials: BASELINE's bar
+        # the row split sums two float partials: the benchmark's bar
         ok, _, _, summary = within(out, expected, 1e-4, 1e-3)
         assert ok, summary
         assert slowest == float(world)

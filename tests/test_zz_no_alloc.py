@@ -6,7 +6,7 @@ Its scratch is a fixed array inside the library, so these tests call it
 through the C ABI directly and hold it to drift_linear, the entry point that
 allocates its scratch as it grows: same inputs, two calls in a row (the
 second must not see the first's leftovers), the tolerance the product tests
-use (BASELINE's 1e-4 absolute + 1e-3 relative). This file runs last, alone
+use (the benchmark's 1e-4 absolute + 1e-3 relative). This file runs last, alone
 or after the others.
 """
 
