@@ -345,10 +345,13 @@ def run_decode(args, ops, rank: int, world: int, stream) -> dict:
     peaks = measured_peaks()
     out = {"config": "C4 dense decode, TP over the job's GPUs", "tp": world,
            "context": DECODE_CONTEXT, "weights": "random-init Q4_1 (C2 law), Q8_0 embedding",
-           "kv_cache": "F16 paged (the reference's KvCache), prefilled N(0,1)"}
+           "kv_cache": "F16 paged (the reference's KvCache), prefilled N(0,1)",
+           "exchange": (("NVLink peer memory, fused with add + RMSNorm" if args.decode_exchange ==
+                         "peer" else "NCCL all-reduce") if world > 1 else None)}
     steps = max(5, min(args.steps, 30))
     for batch in args.decode_batches:
-        decoder = DenseDecoder(ops, config, weights, batch, DECODE_CONTEXT, group=group)
+        decoder = DenseDecoder(ops, config, weights, batch, DECODE_CONTEXT, group=group,
+                               exchange=args.decode_exchange)
         decoder.prefill_random(DECODE_CONTEXT - 1)
         decoder.capture([DECODE_CONTEXT - 1] * batch, stream)
         for _ in range(3):
@@ -615,6 +618,8 @@ def main() -> int:
     parser.add_argument("--no-decode", dest="decode", action="store_false",
                         help="skip the C4 decode tok/s measurement")
     parser.add_argument("--decode-batches", default="1,16")
+    parser.add_argument("--decode-exchange", choices=("peer", "nccl"), default="peer",
+                        help="tensor-parallel decode: the fused NVLink peer exchange, or NCCL")
     parser.add_argument("--decode-case", type=int, help="B: eager C4 decode steps (profiling)")
     parser.add_argument("--decode-layers", type=int, default=36)
     parser.add_argument("--case", help="B,N,K: run one product --repeat times (profiling)")

@@ -69,6 +69,12 @@ SIGNATURES = {
     "drift_add": (_i32, [_p, _p, _p, _i64, _p]),
     "drift_gated": (_i32, [_i32, _p, _p, _p, _i64, _p]),
     "drift_prepared_x_bytes": (_sz, [_i64, _i64]),
+    "drift_comm_handle_bytes": (_sz, []),
+    "drift_comm_create": (_i32, [_i32, _i32, _sz, _pp, _p]),
+    "drift_comm_open": (_i32, [_p, _p]),
+    "drift_comm_slot": (_i32, [_p, _i32, _pp]),
+    "drift_comm_destroy": (_i32, [_p]),
+    "drift_add_rms_norm_allreduce": (_i32, [_p, _i32, _p, _p, _f32, _f32, _p, _i64, _i64, _p, _p]),
     "drift_add_rms_norm_prepared": (_i32, [_p, _p, _p, _f32, _f32, _p, _i64, _i64, _p, _p]),
     "drift_gated_prepared": (_i32, [_i32, _p, _p, _p, _i64, _i64, _p, _p]),
     "drift_linears_prepared": (_i32, [_i32, _p, _p, _i32, _p, _p, _p, _p, _i64, _i64, _p]),

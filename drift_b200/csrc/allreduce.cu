@@ -1,0 +1,302 @@
+// The tensor-parallel decode step's exchange over NVLink peer memory, fused
+// into the kernel that consumes it. A row-split product (o, down: each rank
+// sums its own columns' share) writes its partial rows into one of two slots
+// of a buffer every rank of the group can read (CUDA IPC). The next kernel,
+// on every rank, is `add_rms_norm_allreduce`: it pushes its partial rows into
+// its receive slot on every rank (stores over NVLink), tells its peers they
+// are there, waits (bounded) until theirs have arrived, sums the ranks'
+// partials in rank order from its own memory -- every rank the same bits --
+// adds the sum to the residual, and normalises, writing the next product's x
+// records too. It
+// takes the place of the runner's all-reduce followed by addRmsNorm (an NCCL
+// collective and a norm launch) with one launch and one crossing of NVLink
+// per value.
+//
+// Synchronisation, per row of x (a CTA): the CTA counts its calls in a local
+// counter (every rank makes the same calls in the same order, so the counts
+// agree), stores the count into flag [row][rank] of every rank with a
+// system-scope release, then waits until its own flags [row][p] reach the
+// count for every p, with an acquire -- at most about a second, after which
+// it sets the device error word (code 3) and leaves the row as it was. The
+// two slots alternate between consecutive exchanges (o, then down), so a
+// receive slot is pushed into again only after every rank has signalled the
+// exchange in between, that is, after every rank has finished reading it.
+#include <cuda_runtime.h>
+
+#include <cstring>
+
+#include "common.cuh"
+#include "registry.cuh"
+#include "rowwise.cuh"
+#include "tc_common.cuh"
+#include "x22.cuh"
+
+namespace drift {
+
+int* device_error_word();
+
+namespace {
+
+constexpr int MAX_RANKS = 8;
+constexpr int MAX_ROWS = 64;
+
+// The buffer of a rank: two send slots of partial rows (the products write
+// them), two receive slots per rank (the ranks push their send slots there),
+// then the flags [MAX_ROWS][MAX_RANKS] that peers store into, then the local
+// call counts [MAX_ROWS].
+struct Comm {
+  int rank = 0, world = 1;
+  size_t slot_bytes = 0;
+  uint8_t* local = nullptr;
+  uint8_t* peers[MAX_RANKS] = {};
+  bool opened[MAX_RANKS] = {};
+  // send slot s; the copy of rank p's send slot s that p pushes here
+  size_t send_offset(int s) const { return s * slot_bytes; }
+  size_t receive_offset(int s, int p) const { return (2 + s * MAX_RANKS + p) * slot_bytes; }
+  size_t flags_offset() const { return (2 + 2 * MAX_RANKS) * slot_bytes; }
+  size_t counts_offset() const { return flags_offset() + MAX_ROWS * MAX_RANKS * 4; }
+  size_t total() const { return counts_offset() + MAX_ROWS * 4; }
+};
+
+struct ExchangeArgs {
+  const float* send;              // this rank's send slot
+  float* pushes[MAX_RANKS];       // this rank's receive slot on every rank
+  const float* received;          // this rank's receive slots (rank-major)
+  unsigned* flags[MAX_RANKS];     // the flags of every rank
+  unsigned* counts;               // this rank's call counts
+  long long slot_floats;          // floats from one rank's receive slot to the next
+  int rank, world;
+  int* error;
+};
+
+__device__ __forceinline__ void store_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned load_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// The row's exchange: signal, then wait for every rank. Thread 0 of the CTA;
+// returns whether every rank arrived.
+__device__ bool exchange_barrier(const ExchangeArgs& e, int row) {
+  const unsigned count = e.counts[row] + 1;
+  e.counts[row] = count;
+  // the CTA's pushes (ordered before this by the barrier) go out before the
+  // flags: each flag store is a system-scope release
+  for (int p = 0; p < e.world; ++p) store_release_sys(e.flags[p] + row * MAX_RANKS + e.rank, count);
+  const unsigned* mine = e.flags[e.rank] + row * MAX_RANKS;
+  const uint64_t start = tc::global_ns();
+  for (int p = 0; p < e.world; ++p) {
+    while (int(load_acquire_sys(mine + p) - count) < 0) {
+      if (tc::global_ns() - start > 1000000000ull) {
+        atomicCAS(e.error, 0, 3);
+        return false;
+      }
+      __nanosleep(200);
+    }
+  }
+  return true;
+}
+
+// x[row] += sum over ranks of the slots' row, in rank order; then out =
+// rmsNorm(x) and (records) out's x records: rms_norm_kernel's arithmetic.
+template <int PER, int THREADS>
+__global__ void __launch_bounds__(THREADS) add_rms_norm_allreduce_kernel(
+    const __grid_constant__ ExchangeArgs e, float* __restrict__ x, const float* __restrict__ weight,
+    float* __restrict__ out, int cols, float epsilon, float weight_offset,
+    uint8_t* __restrict__ records) {
+  pdl_trigger();  // the next kernel may launch and wait for this one
+  pdl_wait();     // this rank's partials (the product before) are written
+  __shared__ float partial[32];
+  __shared__ int arrived;
+  const int row_index = blockIdx.x;
+  // push this rank's partial row into its receive slot on every rank (plain
+  // stores over NVLink: no round trip to wait for)
+  {
+    const float* mine = e.send + (long long)row_index * cols;
+    float own[PER];
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int c = threadIdx.x + i * THREADS;
+      own[i] = c < cols ? mine[c] : 0.0f;
+    }
+    for (int p = 0; p < e.world; ++p) {
+      float* to = e.pushes[p] + (long long)row_index * cols;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const int c = threadIdx.x + i * THREADS;
+        if (c < cols) __stcg(to + c, own[i]);
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) arrived = exchange_barrier(e, row_index);
+  __syncthreads();
+  if (!arrived) return;
+  float* row = x + (long long)row_index * cols;
+  float value[PER], w[PER], sum[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int c = threadIdx.x + i * THREADS;
+    value[i] = c < cols ? row[c] : 0.0f;
+    w[i] = c < cols ? weight[c] : 0.0f;
+    sum[i] = 0.0f;
+  }
+  // every rank's values issued before the first is used, then summed in
+  // rank order
+  float part[MAX_RANKS][PER];
+#pragma unroll
+  for (int p = 0; p < MAX_RANKS; ++p) {
+    const float* peer = e.received + (p < e.world ? p : 0) * e.slot_floats + (long long)row_index * cols;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int c = threadIdx.x + i * THREADS;
+      part[p][i] = p < e.world && c < cols ? __ldcv(peer + c) : 0.0f;
+    }
+  }
+#pragma unroll
+  for (int p = 0; p < MAX_RANKS; ++p)
+    if (p < e.world) {
+#pragma unroll
+      for (int i = 0; i < PER; ++i) sum[i] += part[p][i];
+    }
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int c = threadIdx.x + i * THREADS;
+    value[i] = value[i] + sum[i];
+    if (c < cols) row[c] = value[i];
+  }
+  float squares = 0.0f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) squares = fmaf(value[i], value[i], squares);
+  const float total = block_sum(squares, partial);
+  const float scale = 1.0f / sqrtf(total / float(cols) + epsilon);
+  float* target = out + (long long)row_index * cols;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int c = threadIdx.x + i * THREADS;
+    const float normed = value[i] * scale * (w[i] + weight_offset);
+    if (c < cols) target[c] = normed;
+    if (records && c < cols) x22_record_block(normed, records, row_index, c / 32, cols / 32);
+  }
+}
+
+DRIFT_REGISTER(add_rms_norm_allreduce_f32, (add_rms_norm_allreduce_kernel<4, 1024>))
+
+}  // namespace
+}  // namespace drift
+
+using namespace drift;
+
+extern "C" {
+
+int drift_comm_create(int rank, int world, size_t slot_bytes, void** comm, void* handle) {
+  if (world < 1 || world > MAX_RANKS || rank < 0 || rank >= world)
+    return invalid("comm: rank %d of %d (at most %d ranks)", rank, world, MAX_RANKS);
+  if (!comm || !handle) return invalid("comm: no handle to fill");
+  Comm* c = new Comm;
+  c->rank = rank;
+  c->world = world;
+  c->slot_bytes = (slot_bytes + 255) & ~size_t(255);
+  void* memory = nullptr;
+  cudaError_t status = cudaMalloc(&memory, c->total());
+  if (status == cudaSuccess) status = cudaMemset(memory, 0, c->total());
+  cudaIpcMemHandle_t ipc;
+  if (status == cudaSuccess) status = cudaIpcGetMemHandle(&ipc, memory);
+  if (status != cudaSuccess) {
+    if (memory) cudaFree(memory);
+    delete c;
+    return cuda_status(status, "drift_comm_create");
+  }
+  c->local = static_cast<uint8_t*>(memory);
+  c->peers[rank] = c->local;
+  std::memcpy(handle, &ipc, sizeof(ipc));
+  *comm = c;
+  return 0;
+}
+
+size_t drift_comm_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+int drift_comm_open(void* comm, const void* handles) {
+  Comm* c = static_cast<Comm*>(comm);
+  if (!c || !handles) return invalid("comm: not created");
+  const uint8_t* h = static_cast<const uint8_t*>(handles);
+  for (int p = 0; p < c->world; ++p) {
+    if (p == c->rank || c->opened[p]) continue;
+    cudaIpcMemHandle_t ipc;
+    std::memcpy(&ipc, h + p * sizeof(ipc), sizeof(ipc));
+    void* peer = nullptr;
+    DRIFT_CUDA(cudaIpcOpenMemHandle(&peer, ipc, cudaIpcMemLazyEnablePeerAccess));
+    c->peers[p] = static_cast<uint8_t*>(peer);
+    c->opened[p] = true;
+  }
+  return 0;
+}
+
+int drift_comm_slot(void* comm, int slot, void** pointer) {
+  Comm* c = static_cast<Comm*>(comm);
+  if (!c || slot < 0 || slot > 1 || !pointer) return invalid("comm: slot %d", slot);
+  *pointer = c->local + c->send_offset(slot);
+  return 0;
+}
+
+int drift_comm_destroy(void* comm) {
+  Comm* c = static_cast<Comm*>(comm);
+  if (!c) return 0;
+  for (int p = 0; p < c->world; ++p)
+    if (c->opened[p]) cudaIpcCloseMemHandle(c->peers[p]);
+  if (c->local) cudaFree(c->local);
+  delete c;
+  return 0;
+}
+
+int drift_add_rms_norm_allreduce(void* comm, int slot, float* x, const float* weight,
+                                 float epsilon, float weight_offset, float* out, int64_t rows,
+                                 int64_t cols, void* prepared, drift_stream_t stream) {
+  Comm* c = static_cast<Comm*>(comm);
+  if (!c || slot < 0 || slot > 1) return invalid("addRmsNorm: no exchange slot %d", slot);
+  if (rows < 0 || cols <= 0 || rows > MAX_ROWS || cols > 4096)
+    return invalid("addRmsNorm over the exchange: [%lld, %lld] (at most %d rows of 4096)",
+                   (long long)rows, (long long)cols, MAX_ROWS);
+  if ((size_t)rows * cols * 4 > c->slot_bytes)
+    return invalid("addRmsNorm over the exchange: %lld bytes in a slot of %zu",
+                   (long long)(rows * cols * 4), c->slot_bytes);
+  if (!x || !weight || !out) return invalid("addRmsNorm: a null tensor");
+  if (prepared && cols % 32 != 0)
+    return invalid("rmsNorm: prepared x needs rows of whole 32-value blocks");
+  for (int p = 0; p < c->world; ++p)
+    if (!c->peers[p]) return invalid("addRmsNorm: rank %d's buffer is not open", p);
+  if (rows == 0) return 0;
+  ExchangeArgs e = {};
+  e.send = reinterpret_cast<const float*>(c->local + c->send_offset(slot));
+  e.received = reinterpret_cast<const float*>(c->local + c->receive_offset(slot, 0));
+  e.slot_floats = (long long)(c->slot_bytes / 4);
+  for (int p = 0; p < c->world; ++p) {
+    e.pushes[p] = reinterpret_cast<float*>(c->peers[p] + c->receive_offset(slot, c->rank));
+    e.flags[p] = reinterpret_cast<unsigned*>(c->peers[p] + c->flags_offset());
+  }
+  e.counts = reinterpret_cast<unsigned*>(c->local + c->counts_offset());
+  e.rank = c->rank;
+  e.world = c->world;
+  e.error = device_error_word();
+  uint8_t* records = static_cast<uint8_t*>(prepared);
+  const cudaStream_t s = cudaStream_t(stream);
+  const unsigned grid = unsigned(rows);
+  const int n = int(cols);
+  // the shapes of launch_rms_norm (layers.cu), so the norm's bits are its
+#define DRIFT_EXCHANGE(PER, THREADS)                                                           \
+  DRIFT_CUDA(launch_pdl(add_rms_norm_allreduce_kernel<PER, THREADS>, grid, THREADS, 0, s, e, x, \
+                        weight, out, n, epsilon, weight_offset, records))
+  if (cols <= 256) DRIFT_EXCHANGE(1, 256);
+  else if (cols <= 512) DRIFT_EXCHANGE(2, 256);
+  else if (cols <= 1024) DRIFT_EXCHANGE(4, 256);
+  else if (cols <= 2048) DRIFT_EXCHANGE(2, 1024);
+  else DRIFT_EXCHANGE(4, 1024);
+#undef DRIFT_EXCHANGE
+  DRIFT_LAUNCHED("add_rms_norm_allreduce");
+  return 0;
+}
+
+}  // extern "C"

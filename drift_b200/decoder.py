@@ -132,7 +132,7 @@ class DenseDecoder:
     or None for one GPU."""
 
     def __init__(self, ops: CudaOps, config: DenseConfig, weights: DenseWeights, batch: int,
-                 context: int, group=None):
+                 context: int, group=None, exchange: str = "peer"):
         c = self.config = config
         self.ops, self.weights, self.batch, self.context, self.group = ops, weights, batch, context, group
         world = weights.world
@@ -171,6 +171,12 @@ class DenseDecoder:
         # reading it before the next producer writes it
         self.prepared = ops.prepared_x(b, max(c.hidden, self.q_heads * hd, self.ffn))
         self.graph: Optional[torch.cuda.CUDAGraph] = None
+        # the row-split products' exchange: peer memory over NVLink, fused
+        # with the residual add and the norm ("peer"), or NCCL ("nccl")
+        self.exchange = None
+        if group is not None and exchange == "peer":
+            from .tensor_parallel import PeerExchange
+            self.exchange = PeerExchange(ops, group, b, c.hidden)
         self._positions_host: list[int] = [0] * b
 
     def prefill_random(self, positions: int, seed: int = 1) -> None:
@@ -210,18 +216,27 @@ class DenseDecoder:
                 self.positions, self.rope, self.q_turned, cache, self.page_tables)
             ops.attention_decode(self.q_turned, cache, self.page_tables, self.positions,
                                  self.context, self.attention, self.attended, prepared)
-            ops.linears(self.attended.view(b, self.q_heads * hd), [layer.o], [self.projected],
-                        prepared)
+            following = w.layers[index + 1].attention_norm if index + 1 < len(w.layers) else w.final_norm
+            mlp_norm = RowNorm(layer.mlp_norm, c.epsilon, 0.0, self.normed)
+            next_norm = RowNorm(following, c.epsilon, 0.0, self.normed)
+            attended = self.attended.view(b, self.q_heads * hd)
+            if self.exchange is not None:
+                # partials into the exchange's slots; every rank sums them
+                ops.linears(attended, [layer.o], [self.exchange.slots[0]], prepared)
+                self.exchange.add_rms_norm(0, self.x, mlp_norm, prepared)
+                ops.linears(self.normed, [layer.gate, layer.up], [self.gate, self.up], prepared)
+                ops.gated(SILU, self.gate, self.up, self.gate, prepared)
+                ops.linears(self.gate, [layer.down], [self.exchange.slots[1]], prepared)
+                self.exchange.add_rms_norm(1, self.x, next_norm, prepared)
+                continue
+            ops.linears(attended, [layer.o], [self.projected], prepared)
             self._all_reduce(self.projected)
-            ops.add_rms_norm(self.x, self.projected,
-                             RowNorm(layer.mlp_norm, c.epsilon, 0.0, self.normed), prepared)
+            ops.add_rms_norm(self.x, self.projected, mlp_norm, prepared)
             ops.linears(self.normed, [layer.gate, layer.up], [self.gate, self.up], prepared)
             ops.gated(SILU, self.gate, self.up, self.gate, prepared)
             ops.linears(self.gate, [layer.down], [self.projected], prepared)
             self._all_reduce(self.projected)
-            following = w.layers[index + 1].attention_norm if index + 1 < len(w.layers) else w.final_norm
-            ops.add_rms_norm(self.x, self.projected, RowNorm(following, c.epsilon, 0.0, self.normed),
-                             prepared)
+            ops.add_rms_norm(self.x, self.projected, next_norm, prepared)
         ops.linears(self.normed, [w.lm_head], [self.logits], prepared)
         return self.logits
 
@@ -256,5 +271,10 @@ class DenseDecoder:
         self.graph.replay()
 
     def release(self) -> None:
-        """Drops the graph (it must go before an NCCL group is destroyed)."""
+        """Drops the graph (it must go before an NCCL group is destroyed) and
+        the exchange's buffers."""
         self.graph = None
+        if self.exchange is not None:
+            torch.cuda.synchronize()
+            self.exchange.close()
+            self.exchange = None

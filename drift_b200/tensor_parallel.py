@@ -135,3 +135,66 @@ def max_over_ranks(value: float, device=None, group: Optional[Any] = None) -> fl
     t = torch.tensor([float(value)], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
     return float(t.item())
+
+
+class _DeviceArray:
+    """A CUDA array interface over memory this library allocated, so torch
+    can view it without a copy."""
+
+    def __init__(self, pointer: int, shape: tuple, typestr: str = "<f4"):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr,
+                                         "data": (pointer, False), "version": 3}
+
+
+class PeerExchange:
+    """The decode step's exchange over NVLink peer memory (the library's
+    drift_comm_*): two slots of `rows` x `cols` F32 partial rows per rank,
+    readable by every rank of `group`; `add_rms_norm` sums the ranks'
+    partials of a slot in rank order into x and normalises, in one launch.
+    Consecutive exchanges alternate slots (o, then down)."""
+
+    def __init__(self, ops, group, rows: int, cols: int):
+        import ctypes
+
+        import torch
+        import torch.distributed as dist
+
+        from ._lib import check
+
+        self.ops, self.lib = ops, ops.lib
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        comm = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(self.lib.drift_comm_handle_bytes())
+        check("drift_comm_create", self.lib.drift_comm_create(rank, world, rows * cols * 4,
+                                                              ctypes.byref(comm), handle))
+        self.comm = comm
+        handles: list = [None] * world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        joined = ctypes.create_string_buffer(b"".join(handles), len(handle.raw) * world)
+        check("drift_comm_open", self.lib.drift_comm_open(comm, joined))
+        self.slots = []
+        for slot in range(2):
+            pointer = ctypes.c_void_p()
+            check("drift_comm_slot", self.lib.drift_comm_slot(comm, slot, ctypes.byref(pointer)))
+            self.slots.append(torch.as_tensor(_DeviceArray(pointer.value, (rows, cols)),
+                                              device="cuda"))
+        dist.barrier(group=group)
+
+    def add_rms_norm(self, slot: int, x, norm, prepared=None) -> None:
+        """x += the sum over ranks of slot `slot` (rank order); norm.out =
+        rmsNorm(x) (and its records into `prepared`)."""
+        from ._lib import check
+
+        rows, cols = x.shape
+        status = self.lib.drift_add_rms_norm_allreduce(
+            self.comm, slot, x.data_ptr(), norm.weight.data_ptr(), norm.epsilon,
+            norm.weight_offset, norm.out.data_ptr(), rows, cols,
+            None if prepared is None else prepared.data_ptr(), self.ops._stream())
+        check("drift_add_rms_norm_allreduce", status)
+
+    def close(self) -> None:
+        if self.comm:
+            self.slots = []
+            self.lib.drift_comm_destroy(self.comm)
+            self.comm = None
+

@@ -226,6 +226,27 @@ int drift_linears_prepared(int x_dtype, const void* x, const void* prepared, int
                            float* const* outs, const int64_t* ns, int64_t m, int64_t k,
                            drift_stream_t stream);
 
+/* ---- the tensor-parallel exchange over NVLink (new) --------------------------
+ * The reference runs one device (native/HipRuntime.scala:40-43); a B200 box
+ * runs the decode step tensor-parallel, one process per GPU. Each rank creates
+ * a buffer of two slots of `slot_bytes` (CUDA IPC, peer-readable) and a handle
+ * of drift_comm_handle_bytes() bytes, gathers every rank's handle (rank
+ * order) and opens them. A row-split product writes its partial rows into a
+ * slot (drift_comm_slot); drift_add_rms_norm_allreduce then, on every rank,
+ * waits (bounded, about a second; then device error code 3) for every rank's
+ * partials of that slot, adds their sum in rank order to x and writes
+ * rmsNorm(x) (and, with `prepared`, its records): the runner's all-reduce and
+ * addRmsNorm in one launch. Consecutive exchanges must alternate slots; at
+ * most 64 rows of 4096 values. */
+size_t drift_comm_handle_bytes(void);
+int drift_comm_create(int rank, int world, size_t slot_bytes, void** comm, void* handle);
+int drift_comm_open(void* comm, const void* handles);
+int drift_comm_slot(void* comm, int slot, void** pointer);
+int drift_comm_destroy(void* comm);
+int drift_add_rms_norm_allreduce(void* comm, int slot, float* x, const float* weight,
+                                 float epsilon, float weight_offset, float* out, int64_t rows,
+                                 int64_t cols, void* prepared, drift_stream_t stream);
+
 /* The library keeps one grow-only scratch buffer per device for the products'
  * prepared x (as the runner's HIP backend keeps grow-only scratch,
  * ops/HipBase.scala:341-351). Reserving it ahead keeps allocation out of a
