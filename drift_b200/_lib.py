@@ -69,6 +69,10 @@ SIGNATURES = {
     "drift_add": (_i32, [_p, _p, _p, _i64, _p]),
     "drift_gated": (_i32, [_i32, _p, _p, _p, _i64, _p]),
     "drift_prepared_x_bytes": (_sz, [_i64, _i64]),
+    "drift_causal_conv": (_i32, [_p, _i32, _i32, _p, _i32, _i32, _p, _p, _p, _p]),
+    "drift_gated_delta_rule": (_i32, [_p, _i32, _i32, _i32, _i32, _i32, _p, _p, _p, _p, _p, _p, _p,
+                                      _p]),
+    "drift_gated_rms_norm": (_i32, [_p, _p, _p, _i32, _f32, _p, _i64, _i64, _i32, _p, _p]),
     "drift_comm_handle_bytes": (_sz, []),
     "drift_comm_create": (_i32, [_i32, _i32, _sz, _pp, _p]),
     "drift_comm_open": (_i32, [_p, _p]),

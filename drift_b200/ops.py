@@ -434,6 +434,61 @@ class CudaOps:
                                                               self._stream())
         check("drift_attention_decode", status)
 
+    # -- SequenceOps: Gated DeltaNet (ops/SequenceOps.scala) --------------------------------------
+    def causal_conv(self, x, weight, dilation: int, state, history, out) -> None:
+        """SiLU of the causal depthwise convolution of x [tokens, channels] with
+        weight [channels, taps]; state [span, channels] updated in place
+        (SequenceOps.causalConv; CpuSequence.scala:29-80)."""
+        _f32("causalConv", x, weight, state, out)
+        _same_shape("causalConv", x, out)
+        _require(x.dim() == 2, f"causalConv takes [tokens, channels], not {list(x.shape)}")
+        tokens, channels = x.shape
+        taps = weight.shape[-1]
+        _require(tuple(weight.shape) == (channels, taps) and taps <= 9,
+                 f"causalConv: weight {list(weight.shape)} for {channels} channels")
+        span = (taps - 1) * dilation
+        _require(dilation >= 1 and span <= 16 and tuple(state.shape) == (span, channels),
+                 f"causalConv: state {list(state.shape)}, expected [{span}, {channels}]")
+        status = self.lib.drift_causal_conv(_ptr(x), tokens, channels, _ptr(weight), taps, dilation,
+                                            _ptr(state), _ptr(history), _ptr(out), self._stream())
+        check("drift_causal_conv", status)
+
+    def gated_delta_rule(self, qkv, a, b, decay, dt_bias, state, rule, history, out) -> None:
+        """The gated delta rule of `rule` (key_heads, value_heads, dimension,
+        tiled_heads) over qkv [tokens, qkv_width]; state [value_heads, D, D]
+        updated in place; out [tokens, value_heads, D]
+        (SequenceOps.gatedDeltaRule; CpuSequence.scala:82-158)."""
+        key_heads, value_heads, d, tiled = rule
+        _f32("gatedDeltaRule", qkv, a, b, decay, dt_bias, state, out)
+        tokens = qkv.shape[0]
+        width = (2 * key_heads + value_heads) * d
+        _require(tuple(qkv.shape) == (tokens, width),
+                 f"gatedDeltaRule: qkv {list(qkv.shape)}, expected [{tokens}, {width}]")
+        _require(tuple(a.shape) == (tokens, value_heads) and tuple(b.shape) == tuple(a.shape),
+                 f"gatedDeltaRule: a {list(a.shape)}, b {list(b.shape)}")
+        _require(tuple(decay.shape) == (value_heads,) and tuple(dt_bias.shape) == (value_heads,),
+                 f"gatedDeltaRule: decay {list(decay.shape)}, dtBias {list(dt_bias.shape)}")
+        _require(tuple(state.shape) == (value_heads, d, d),
+                 f"gatedDeltaRule: state {list(state.shape)}")
+        _require(tuple(out.shape) == (tokens, value_heads, d),
+                 f"gatedDeltaRule: out {list(out.shape)}")
+        status = self.lib.drift_gated_delta_rule(
+            _ptr(qkv), tokens, key_heads, value_heads, d, int(tiled), _ptr(a), _ptr(b),
+            _ptr(decay), _ptr(dt_bias), _ptr(state), _ptr(history), _ptr(out), self._stream())
+        check("drift_gated_delta_rule", status)
+
+    def gated_rms_norm(self, x, weight, gate, kind: int, epsilon: float, out,
+                       prepared: Optional[torch.Tensor] = None, heads: int = 0) -> None:
+        """rmsNorm(x) × act(gate) per row (NormalisationOps.gatedRmsNorm); with
+        `prepared`, the records of out as [rows / heads, heads × cols]."""
+        rows = self._check_row_wise("gatedRmsNorm", x, out, weight)
+        _f32("gatedRmsNorm", gate)
+        _same_shape("gatedRmsNorm", x, gate)
+        status = self.lib.drift_gated_rms_norm(_ptr(x), _ptr(weight), _ptr(gate), kind, epsilon,
+                                               _ptr(out), rows, x.shape[-1], heads, _ptr(prepared),
+                                               self._stream())
+        check("drift_gated_rms_norm", status)
+
     # -- ExpertsOps (ops/ExpertsOps.scala) -------------------------------------------------------------
     def route(self, logits, ids, weights) -> None:
         """Top-k routing (ExpertsOps.scala:116-120; checks L252-269)."""

@@ -194,6 +194,32 @@ int drift_attention_decode(const float* q, int batch, int q_heads, const void* k
                            const int32_t* positions, int max_key_count, float scale, int window,
                            float softcap, const float* sinks, float* out, drift_stream_t stream);
 
+/* ---- Gated DeltaNet (the hybrid decoder's linear-attention layers) ---------
+ * SequenceOps.causalConv (ops/SequenceOps.scala; CPU ops/CpuSequence.scala:
+ * 29-80): x [tokens][channels], weight [channels][taps] (taps <= 9), state
+ * [(taps - 1) dilation][channels] (span <= 16, updated), out = SiLU(sum of the
+ * taps); history [tokens][span][channels] or NULL. */
+int drift_causal_conv(const float* x, int tokens, int channels, const float* weight, int taps,
+                      int dilation, float* state, float* history, float* out,
+                      drift_stream_t stream);
+/* SequenceOps.gatedDeltaRule (CpuSequence.scala:82-158): qkv [tokens][(2
+ * key_heads + value_heads) dim], a, b [tokens][value_heads], decay, dt_bias
+ * [value_heads], state [value_heads][dim][dim] (updated), out [tokens]
+ * [value_heads][dim]; history [tokens][value_heads][dim][dim] or NULL; value
+ * head h reads key head h % key_heads when `tiled`, h / (value_heads /
+ * key_heads) otherwise (ops/DeltaRule.scala:18-20). dim 32, 64 or 128. */
+int drift_gated_delta_rule(const float* qkv, int tokens, int key_heads, int value_heads, int dim,
+                           int tiled, const float* a, const float* b, const float* decay,
+                           const float* dt_bias, float* state, float* history, float* out,
+                           drift_stream_t stream);
+/* NormalisationOps.gatedRmsNorm (CpuNormalisation.scala:167-178): per row of
+ * cols (<= 512) values, rmsNorm(x) * weight * act(gate), act DRIFT_SILU or
+ * DRIFT_SIGMOID; out may be x. With `prepared` (rows = tokens x heads), the
+ * records of out viewed as [tokens][heads * cols] for the out projection. */
+int drift_gated_rms_norm(const float* x, const float* weight, const float* gate, int kind,
+                         float epsilon, float* out, int64_t rows, int64_t cols, int heads,
+                         void* prepared, drift_stream_t stream);
+
 /* ---- prepared x (new) ------------------------------------------------------
  * A product streams its weights against x's "records" (x per 32-value block as
  * exact 24-bit integer planes and a scale). drift_linear writes them itself; a

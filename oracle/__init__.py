@@ -75,6 +75,9 @@ def lib() -> ctypes.CDLL:
             "oracle_experts_gated_linear": (i32, [i32, p, i64, p, p, i64, i64, i64, p, i64, p]),
             "oracle_moe_combine": (None, [p, p, i64, i64, i64, p, p, p, p, p]),
             "oracle_moe_combine_norm": (None, [p, p, i64, i64, i64, p, p, p, p, p, f32, f32, p]),
+            "oracle_causal_conv": (None, [p, i32, i32, p, i32, i32, p, p, p]),
+            "oracle_gated_delta_rule": (None, [p, i32, i32, i32, i32, i32, p, p, p, p, p, p, p]),
+            "oracle_gated_rms_norm": (None, [p, p, p, i32, f32, p, i64, i64]),
         }
         for name, (restype, argtypes) in sigs.items():
             fn = getattr(_lib, name)
@@ -321,3 +324,52 @@ def attention(q, keys: np.ndarray, values: np.ndarray, page_size: int, kv_heads:
                            _p(table), query_start, key_count, scale, int(causal), window,
                            int(softcap is not None), float(softcap or 0.0), _p(sinks_arr), _p(out))
     return out
+
+
+# ---- Gated DeltaNet (ops/CpuSequence.scala:29-158) ---------------------------------------
+
+
+def causal_conv(x, weight, state, dilation: int = 1, keep_history: bool = False):
+    """CpuSequence.causalConv (SiLU included): x [tokens, channels], weight
+    [channels, taps], state [span, channels] (updated in place). Returns out
+    (and the history [tokens, span, channels] with keep_history)."""
+    x, weight = _f32(x), _f32(weight)
+    assert state.dtype == np.float32 and state.flags.c_contiguous
+    tokens, channels = x.shape
+    taps = weight.shape[1]
+    span = (taps - 1) * dilation
+    out = np.empty_like(x)
+    history = np.empty((tokens, span, channels), np.float32) if keep_history else None
+    lib().oracle_causal_conv(_p(x), tokens, channels, _p(weight), taps, dilation, _p(state),
+                             _p(history), _p(out))
+    return (out, history) if keep_history else out
+
+
+def gated_delta_rule(qkv, a, b, decay, dt_bias, state, key_heads: int, value_heads: int,
+                     tiled: bool = False, keep_history: bool = False):
+    """CpuSequence.gatedDeltaRule: qkv [tokens, (2 key_heads + value_heads) D],
+    a, b [tokens, value_heads], decay, dt_bias [value_heads], state
+    [value_heads, D, D] (updated in place). Returns out [tokens, value_heads,
+    D] (and the history [tokens, value_heads, D, D] with keep_history)."""
+    qkv = _f32(qkv)
+    tokens = qkv.shape[0]
+    d = state.shape[-1]
+    assert state.dtype == np.float32 and state.flags.c_contiguous
+    assert qkv.shape[1] == (2 * key_heads + value_heads) * d
+    out = np.empty((tokens, value_heads, d), np.float32)
+    history = np.empty((tokens, value_heads, d, d), np.float32) if keep_history else None
+    lib().oracle_gated_delta_rule(_p(qkv), tokens, key_heads, value_heads, d, int(tiled),
+                                  _p(_f32(a)), _p(_f32(b)), _p(_f32(decay)), _p(_f32(dt_bias)),
+                                  _p(state), _p(history), _p(out))
+    return (out, history) if keep_history else out
+
+
+def gated_rms_norm(x, weight, gate, kind: int, epsilon: float) -> np.ndarray:
+    """CpuNormalisation.gatedRmsNorm: rmsNorm(x) * act(gate) per row."""
+    x, gate = _f32(x), _f32(gate)
+    cols = x.shape[-1]
+    out = np.empty_like(x)
+    lib().oracle_gated_rms_norm(_p(x), _p(_f32(weight)), _p(gate), kind, epsilon, _p(out),
+                                x.size // cols, cols)
+    return out
+
