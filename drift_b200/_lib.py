@@ -73,6 +73,14 @@ SIGNATURES = {
     "drift_gated_delta_rule": (_i32, [_p, _i32, _i32, _i32, _i32, _i32, _p, _p, _p, _p, _p, _p, _p,
                                       _p]),
     "drift_gated_rms_norm": (_i32, [_p, _p, _p, _i32, _f32, _p, _i64, _i64, _i32, _p, _p]),
+    "drift_causal_conv_decode": (_i32, [_p, _i32, _i32, _p, _i32, _i32, _p, _p, _p]),
+    "drift_gated_delta_rule_decode": (_i32, [_p, _i32, _i32, _i32, _i32, _i32, _p, _p, _p, _p, _p,
+                                             _p, _p]),
+    "drift_attention_inputs_decode_split": (_i32, [_p, _p, _p, _i32, _i32, _i32, _i32, _p, _p, _f32,
+                                                   _f32, _p, _f32, _i32, _i32, _p, _p, _p, _i32,
+                                                   _i32, _p, _i32, _p]),
+    "drift_attention_decode_gated": (_i32, [_p, _i32, _i32, _p, _p, _i32, _i32, _i32, _i32, _p, _i32,
+                                            _p, _i32, _f32, _i32, _f32, _p, _p, _p, _i32, _p, _p]),
     "drift_comm_handle_bytes": (_sz, []),
     "drift_comm_create": (_i32, [_i32, _i32, _sz, _pp, _p]),
     "drift_comm_open": (_i32, [_p, _p]),

@@ -79,7 +79,7 @@ __global__ void cache_write_kernel(const float* __restrict__ k, const float* __r
 // nothing.
 __global__ void __launch_bounds__(256) attention_inputs_kernel(
     const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
-    int q_heads, int kv_heads, int dim, const float* __restrict__ q_norm,
+    int q_heads, int kv_heads, int dim, int q_stride, const float* __restrict__ q_norm,
     const float* __restrict__ k_norm, float epsilon, float weight_offset,
     const int* __restrict__ positions, float theta, int rotary, int layout, float* __restrict__ q_out,
     __half* keys, __half* values, int page_size, const int* __restrict__ tables, int table_stride,
@@ -91,7 +91,7 @@ __global__ void __launch_bounds__(256) attention_inputs_kernel(
   const int slot = blockIdx.x, z = blockIdx.y, d = threadIdx.x;
   const bool query = slot < q_heads;
   const int h = query ? slot : slot - q_heads;
-  const float* source = query ? q + ((long long)z * q_heads + h) * dim
+  const float* source = query ? q + ((long long)z * q_heads + h) * q_stride
                               : k + ((long long)z * kv_heads + h) * dim;
   const float* norm = query ? q_norm : k_norm;
   float value = d < dim ? source[d] : 0.0f;
@@ -478,7 +478,9 @@ template <int D>
 __global__ void __launch_bounds__(ATT_THREADS) attention_join_kernel(const AttentionArgs a,
                                                                      const float* sinks,
                                                                      float* out,
-                                                                     uint8_t* records) {
+                                                                     uint8_t* records,
+                                                                     const float* gate,
+                                                                     int gate_stride) {
   pdl_trigger();  // the next kernel may launch and wait for this one
   pdl_wait();     // what the kernels before this one wrote is visible
   extern __shared__ float factor[];  // [splits]: e^(m_s - M), 0 for an empty split
@@ -517,7 +519,13 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_join_kernel(const Atten
       for (int j = 0; j < 8; ++j)
         if (s0 + j < a.splits && factor[s0 + j] > 0.0f) sum += o[j] * factor[s0 + j];
     }
-    const float value = total > 0.0f ? sum / total : 0.0f;
+    float value = total > 0.0f ? sum / total : 0.0f;
+    if (gate) {
+      // the gated attention's output gate: value x sigmoid(gate) (the
+      // runner's gated(Sigmoid, gate, attended), models/HybridBlocks.scala)
+      const float g = gate[((long long)t * a.q_heads + head) * gate_stride + d];
+      value = (1.0f / (1.0f + expf(-g))) * value;
+    }
     out[((long long)t * a.q_heads + head) * D + d] = value;
     if constexpr (D % 32 == 0) {
       if (records) x22_record_block(value, records, t, (head * D + d) / 32, a.q_heads * D / 32);
@@ -537,7 +545,8 @@ DRIFT_REGISTER(attention_inputs_f32, attention_inputs_kernel)
 
 template <int D>
 int launch_attention(const AttentionArgs& a, const float* sinks, float* out, cudaStream_t stream,
-                     uint8_t* records = nullptr) {
+                     uint8_t* records = nullptr, const float* gate = nullptr,
+                     int gate_stride = 0) {
   static bool configured = false;
   if (!configured) {
     DRIFT_CUDA(cudaFuncSetAttribute(attention_split_kernel<D>,
@@ -552,7 +561,8 @@ int launch_attention(const AttentionArgs& a, const float* sinks, float* out, cud
                         SPLIT_THREADS, SplitTile<D>::BYTES, stream, a));
   DRIFT_LAUNCHED("attention_split");
   DRIFT_CUDA(launch_pdl(attention_join_kernel<D>, dim3(a.q_heads, a.tokens), ATT_THREADS,
-                        a.splits * sizeof(float), stream, a, sinks, out, records));
+                        a.splits * sizeof(float), stream, a, sinks, out, records, gate,
+                        gate_stride));
   DRIFT_LAUNCHED("attention_join");
   return 0;
 }
@@ -665,13 +675,13 @@ int drift_attention(const float* q, int tokens, int q_heads, const void* keys, c
   }
 }
 
-int drift_attention_inputs_decode(const float* q, const float* k, const float* v, int batch,
-                                  int q_heads, int kv_heads, int head_dim, const float* q_norm,
-                                  const float* k_norm, float epsilon, float weight_offset,
-                                  const int32_t* positions, float theta, int rotary, int layout,
-                                  float* q_out, void* keys, void* values, int pages,
-                                  int page_size, const int32_t* page_tables, int table_stride,
-                                  drift_stream_t stream) {
+static int attention_inputs_decode(const float* q, int q_stride, const float* k, const float* v,
+                                   int batch, int q_heads, int kv_heads, int head_dim,
+                                   const float* q_norm, const float* k_norm, float epsilon,
+                                   float weight_offset, const int32_t* positions, float theta,
+                                   int rotary, int layout, float* q_out, void* keys, void* values,
+                                   int pages, int page_size, const int32_t* page_tables,
+                                   int table_stride, drift_stream_t stream) {
   if (batch < 0 || q_heads <= 0) return invalid("attention inputs: %d sequences of %d heads", batch, q_heads);
   DRIFT_TRY(check_cache(pages, page_size, kv_heads, head_dim, page_tables, table_stride, 0,
                         "attention inputs"));
@@ -683,12 +693,40 @@ int drift_attention_inputs_decode(const float* q, const float* k, const float* v
   if ((reinterpret_cast<uintptr_t>(keys) | reinterpret_cast<uintptr_t>(values)) & 15)
     return invalid("attention inputs: the cache does not start on a 16-byte boundary");
   DRIFT_CUDA(launch_pdl(attention_inputs_kernel, dim3(q_heads + kv_heads, batch), 256, 0,
-                        cudaStream_t(stream), q, k, v, q_heads, kv_heads, head_dim, q_norm, k_norm,
+                        cudaStream_t(stream), q, k, v, q_heads, kv_heads, head_dim, q_stride,
+                        q_norm, k_norm,
                         epsilon, weight_offset, positions, theta, rotary, layout, q_out,
                         static_cast<__half*>(keys), static_cast<__half*>(values), page_size,
                         page_tables, table_stride, device_error_word()));
   DRIFT_LAUNCHED("attention_inputs");
   return 0;
+}
+
+int drift_attention_inputs_decode(const float* q, const float* k, const float* v, int batch,
+                                  int q_heads, int kv_heads, int head_dim, const float* q_norm,
+                                  const float* k_norm, float epsilon, float weight_offset,
+                                  const int32_t* positions, float theta, int rotary, int layout,
+                                  float* q_out, void* keys, void* values, int pages,
+                                  int page_size, const int32_t* page_tables, int table_stride,
+                                  drift_stream_t stream) {
+  return attention_inputs_decode(q, head_dim, k, v, batch, q_heads, kv_heads, head_dim, q_norm,
+                                 k_norm, epsilon, weight_offset, positions, theta, rotary, layout,
+                                 q_out, keys, values, pages, page_size, page_tables, table_stride,
+                                 stream);
+}
+
+int drift_attention_inputs_decode_split(const float* query_and_gate, const float* k,
+                                        const float* v, int batch, int q_heads, int kv_heads,
+                                        int head_dim, const float* q_norm, const float* k_norm,
+                                        float epsilon, float weight_offset,
+                                        const int32_t* positions, float theta, int rotary,
+                                        int layout, float* q_out, void* keys, void* values,
+                                        int pages, int page_size, const int32_t* page_tables,
+                                        int table_stride, drift_stream_t stream) {
+  return attention_inputs_decode(query_and_gate, 2 * head_dim, k, v, batch, q_heads, kv_heads,
+                                 head_dim, q_norm, k_norm, epsilon, weight_offset, positions,
+                                 theta, rotary, layout, q_out, keys, values, pages, page_size,
+                                 page_tables, table_stride, stream);
 }
 
 size_t drift_attention_workspace_bytes(int rows, int q_heads, int head_dim, int key_count) {
@@ -703,7 +741,7 @@ static int attention_decode(const float* q, int batch, int q_heads, const void* 
                             int head_dim, const int32_t* page_tables, int table_stride,
                             const int32_t* positions, int max_key_count, float scale, int window,
                             float softcap, const float* sinks, float* out, uint8_t* records,
-                            drift_stream_t stream) {
+                            const float* gate, int gate_stride, drift_stream_t stream) {
   if (batch < 0 || q_heads <= 0) return invalid("attention: %d sequences of %d heads", batch, q_heads);
   DRIFT_TRY(check_cache(pages, page_size, kv_heads, head_dim, page_tables, table_stride,
                         max_key_count, "attention"));
@@ -742,10 +780,10 @@ static int attention_decode(const float* q, int batch, int q_heads, const void* 
   a.part_ml = a.part_o + parts * head_dim;
   const cudaStream_t s = cudaStream_t(stream);
   switch (head_dim) {
-    case 64: return launch_attention<64>(a, sinks, out, s, records);
-    case 80: return launch_attention<80>(a, sinks, out, s, records);
-    case 128: return launch_attention<128>(a, sinks, out, s, records);
-    default: return launch_attention<256>(a, sinks, out, s, records);
+    case 64: return launch_attention<64>(a, sinks, out, s, records, gate, gate_stride);
+    case 80: return launch_attention<80>(a, sinks, out, s, records, gate, gate_stride);
+    case 128: return launch_attention<128>(a, sinks, out, s, records, gate, gate_stride);
+    default: return launch_attention<256>(a, sinks, out, s, records, gate, gate_stride);
   }
 }
 
@@ -756,7 +794,7 @@ int drift_attention_decode(const float* q, int batch, int q_heads, const void* k
                            float softcap, const float* sinks, float* out, drift_stream_t stream) {
   return attention_decode(q, batch, q_heads, keys, values, pages, page_size, kv_heads, head_dim,
                           page_tables, table_stride, positions, max_key_count, scale, window,
-                          softcap, sinks, out, nullptr, stream);
+                          softcap, sinks, out, nullptr, nullptr, 0, stream);
 }
 
 int drift_attention_decode_prepared(const float* q, int batch, int q_heads, const void* keys,
@@ -769,7 +807,24 @@ int drift_attention_decode_prepared(const float* q, int batch, int q_heads, cons
   if (head_dim % 32 != 0) return invalid("attention: prepared x needs heads of whole 32-value blocks");
   return attention_decode(q, batch, q_heads, keys, values, pages, page_size, kv_heads, head_dim,
                           page_tables, table_stride, positions, max_key_count, scale, window,
-                          softcap, sinks, out, static_cast<uint8_t*>(prepared), stream);
+                          softcap, sinks, out, static_cast<uint8_t*>(prepared), nullptr, 0,
+                          stream);
+}
+
+int drift_attention_decode_gated(const float* q, int batch, int q_heads, const void* keys,
+                                 const void* values, int pages, int page_size, int kv_heads,
+                                 int head_dim, const int32_t* page_tables, int table_stride,
+                                 const int32_t* positions, int max_key_count, float scale,
+                                 int window, float softcap, const float* sinks, float* out,
+                                 const float* gate, int gate_stride, void* prepared,
+                                 drift_stream_t stream) {
+  if (!gate || gate_stride < head_dim) return invalid("attention: no output gate");
+  if (prepared && head_dim % 32 != 0)
+    return invalid("attention: prepared x needs heads of whole 32-value blocks");
+  return attention_decode(q, batch, q_heads, keys, values, pages, page_size, kv_heads, head_dim,
+                          page_tables, table_stride, positions, max_key_count, scale, window,
+                          softcap, sinks, out, static_cast<uint8_t*>(prepared), gate, gate_stride,
+                          stream);
 }
 
 }  // extern "C"

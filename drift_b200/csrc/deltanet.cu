@@ -44,6 +44,10 @@ __global__ void __launch_bounds__(256) causal_conv_kernel(const float* __restric
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= channels) return;
   const int span = (taps - 1) * dilation;
+  // sequence blockIdx.y of a decode batch: its own tokens, state and out
+  x += (long long)blockIdx.y * tokens * channels;
+  out += (long long)blockIdx.y * tokens * channels;
+  state += (long long)blockIdx.y * span * channels;
   float window[MAX_SPAN];  // the inputs before the current token, oldest first
 #pragma unroll
   for (int i = 0; i < MAX_SPAN; ++i) window[i] = i < span ? state[(long long)i * channels + c] : 0.0f;
@@ -108,6 +112,15 @@ __global__ void __launch_bounds__(RULE_THREADS) gated_delta_rule_kernel(
   __shared__ float scratch[RULE_WARPS];
   const int h = blockIdx.x / SLICES, slice = blockIdx.x % SLICES;
   const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  {
+    // sequence blockIdx.y of a decode batch: its own tokens and state
+    const long long z = blockIdx.y;
+    qkv += z * tokens * (long long)(2 * key_heads + value_heads) * D;
+    a += z * tokens * value_heads;
+    b += z * tokens * value_heads;
+    out += z * tokens * (long long)value_heads * D;
+    state += z * (long long)value_heads * D * D;
+  }
   const int j = slice * RULE_COLUMNS + lane, i0 = warp * ROWS;
   const int kh = tiled ? h % key_heads : h / (value_heads / key_heads);
   const long long width = (long long)(2 * key_heads + value_heads) * D;
@@ -253,6 +266,52 @@ int drift_gated_delta_rule(const float* qkv, int tokens, int key_heads, int valu
   else
     DRIFT_CUDA(launch_pdl(gated_delta_rule_kernel<128>, grid, RULE_THREADS, 0, s, qkv, tokens,
                           key_heads, value_heads, tiled, a, b, decay, dt_bias, state, history, out));
+  DRIFT_LAUNCHED("delta_rule");
+  return 0;
+}
+
+int drift_causal_conv_decode(const float* x, int sequences, int channels, const float* weight,
+                             int taps, int dilation, float* states, float* out,
+                             drift_stream_t stream) {
+  if (sequences < 0 || channels < 0 || sequences > 65535)
+    return invalid("causalConv over %d sequences of %d channels", sequences, channels);
+  if (taps < 1 || taps > 9 || dilation < 1 || (taps - 1) * dilation > MAX_SPAN)
+    return invalid("causalConv: %d taps %d apart (at most 9 taps, a span of %d)", taps, dilation,
+                   MAX_SPAN);
+  if (sequences == 0 || channels == 0) return 0;
+  if (!x || !weight || !out || ((taps > 1) && !states)) return invalid("causalConv: a null tensor");
+  DRIFT_CUDA(launch_pdl(causal_conv_kernel, dim3(unsigned((channels + 255) / 256), unsigned(sequences)),
+                        256, 0, cudaStream_t(stream), x, 1, channels, weight, taps, dilation,
+                        states, static_cast<float*>(nullptr), out));
+  DRIFT_LAUNCHED("causal_conv_silu");
+  return 0;
+}
+
+int drift_gated_delta_rule_decode(const float* qkv, int sequences, int key_heads, int value_heads,
+                                  int dim, int tiled, const float* a, const float* b,
+                                  const float* decay, const float* dt_bias, float* states,
+                                  float* out, drift_stream_t stream) {
+  if (sequences < 0 || sequences > 65535 || key_heads <= 0 || value_heads <= 0 ||
+      value_heads % key_heads != 0)
+    return invalid("%d value heads over %d key heads (%d sequences)", value_heads, key_heads,
+                   sequences);
+  if (dim != 32 && dim != 64 && dim != 128)
+    return invalid("gatedDeltaRule: heads of %d (kernels take 32, 64, 128)", dim);
+  if (sequences == 0) return 0;
+  if (!qkv || !a || !b || !decay || !dt_bias || !states || !out)
+    return invalid("gatedDeltaRule: a null tensor");
+  const dim3 grid(unsigned(value_heads * (dim / RULE_COLUMNS)), unsigned(sequences));
+  const cudaStream_t s = cudaStream_t(stream);
+  float* none = nullptr;
+  if (dim == 32)
+    DRIFT_CUDA(launch_pdl(gated_delta_rule_kernel<32>, grid, RULE_THREADS, 0, s, qkv, 1,
+                          key_heads, value_heads, tiled, a, b, decay, dt_bias, states, none, out));
+  else if (dim == 64)
+    DRIFT_CUDA(launch_pdl(gated_delta_rule_kernel<64>, grid, RULE_THREADS, 0, s, qkv, 1,
+                          key_heads, value_heads, tiled, a, b, decay, dt_bias, states, none, out));
+  else
+    DRIFT_CUDA(launch_pdl(gated_delta_rule_kernel<128>, grid, RULE_THREADS, 0, s, qkv, 1,
+                          key_heads, value_heads, tiled, a, b, decay, dt_bias, states, none, out));
   DRIFT_LAUNCHED("delta_rule");
   return 0;
 }

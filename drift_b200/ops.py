@@ -382,15 +382,19 @@ class CudaOps:
         check("drift_attention", status)
 
     def attention_inputs_decode(self, q, k, v, q_norm, k_norm, epsilon: float, positions,
-                                rope: Rope, q_out, cache: KvCache, page_tables) -> None:
+                                rope: Rope, q_out, cache: KvCache, page_tables,
+                                weight_offset: float = 0.0) -> None:
         """A decode step's per-head q/k RMS norms, their rope and the cache
         write of k and v, for one token per sequence, in one launch.
-        q [b, q_heads, D], k, v [b, kv_heads, D]; positions I32 [b];
-        page_tables I32 [b, pages per sequence]."""
+        q [b, q_heads, D] -- or queryAndGate [b, q_heads, 2 D], whose first
+        half per head is the query -- k, v [b, kv_heads, D]; positions I32
+        [b]; page_tables I32 [b, pages per sequence]."""
         _f32("attentionInputs", q, k, v, q_out)
-        _same_shape("attentionInputs", q, q_out)
         _same_shape("attentionInputs", k, v)
-        b, q_heads, dim = q.shape
+        split = q.shape[-1] == 2 * q_out.shape[-1]
+        _require(split or tuple(q.shape) == tuple(q_out.shape),
+                 f"attentionInputs: q {list(q.shape)} for out {list(q_out.shape)}")
+        b, q_heads, dim = q_out.shape
         _require(k.dim() == 3 and k.shape[0] == b and tuple(k.shape[1:]) ==
                  (cache.kv_heads, cache.head_dim) and dim == cache.head_dim,
                  f"attentionInputs: {list(q.shape)}, {list(k.shape)} for a cache of "
@@ -400,15 +404,19 @@ class CudaOps:
         _require(page_tables.dtype == torch.int32 and page_tables.dim() == 2 and
                  page_tables.shape[0] == b and page_tables.is_contiguous(),
                  f"attentionInputs: page tables {list(page_tables.shape)} for {b} sequences")
-        status = self.lib.drift_attention_inputs_decode(
+        call = (self.lib.drift_attention_inputs_decode_split if split
+                else self.lib.drift_attention_inputs_decode)
+        status = call(
             _ptr(q), _ptr(k), _ptr(v), b, q_heads, cache.kv_heads, dim, _ptr(q_norm),
-            _ptr(k_norm), epsilon, 0.0, _ptr(positions), rope.theta, rope.rotary_dimensions,
-            rope.layout, _ptr(q_out), _ptr(cache.keys), _ptr(cache.values), cache.pages,
-            cache.page_size, _ptr(page_tables), int(page_tables.shape[1]), self._stream())
+            _ptr(k_norm), epsilon, weight_offset, _ptr(positions), rope.theta,
+            rope.rotary_dimensions, rope.layout, _ptr(q_out), _ptr(cache.keys),
+            _ptr(cache.values), cache.pages, cache.page_size, _ptr(page_tables),
+            int(page_tables.shape[1]), self._stream())
         check("drift_attention_inputs_decode", status)
 
     def attention_decode(self, q, cache: KvCache, page_tables, positions, max_key_count: int,
-                         attention: Attention, out, prepared: Optional[torch.Tensor] = None) -> None:
+                         attention: Attention, out, prepared: Optional[torch.Tensor] = None,
+                         gate: Optional[torch.Tensor] = None) -> None:
         """Attention of one query per sequence, all sequences in one launch:
         row z of q [b, q_heads, D] at positions[z] over its keys 0..positions[z];
         with `prepared`, the records of out as [b, q_heads D] too."""
@@ -427,7 +435,17 @@ class CudaOps:
                 cache.page_size, cache.kv_heads, dim, _ptr(page_tables), int(page_tables.shape[1]),
                 _ptr(positions), max_key_count, attention.scale, int(attention.window or 0),
                 float(attention.softcap or 0.0), _ptr(attention.sinks), _ptr(out))
-        if prepared is None:
+        if gate is not None:
+            # gate: [b, q_heads, stride] whose first D of each head gate the
+            # output (the second half of queryAndGate, viewed from there)
+            _require(gate.dtype == torch.float32 and gate.is_cuda and tuple(gate.shape) == (b, q_heads, dim),
+                     f"attention: gate {list(gate.shape)} {gate.dtype} for {list(q.shape)}")
+            stride = gate.stride(1)
+            _require(gate.stride(0) == q_heads * stride and gate.stride(2) == 1,
+                     "attention: the gate is rows of heads")
+            status = self.lib.drift_attention_decode_gated(*args, _ptr(gate), stride, _ptr(prepared),
+                                                           self._stream())
+        elif prepared is None:
             status = self.lib.drift_attention_decode(*args, self._stream())
         else:
             status = self.lib.drift_attention_decode_prepared(*args, _ptr(prepared),
@@ -476,6 +494,33 @@ class CudaOps:
             _ptr(qkv), tokens, key_heads, value_heads, d, int(tiled), _ptr(a), _ptr(b),
             _ptr(decay), _ptr(dt_bias), _ptr(state), _ptr(history), _ptr(out), self._stream())
         check("drift_gated_delta_rule", status)
+
+    def causal_conv_decode(self, x, weight, dilation: int, states, out) -> None:
+        """One token per sequence: x [S, channels], states [S, span, channels]."""
+        _f32("causalConv", x, weight, states, out)
+        _same_shape("causalConv", x, out)
+        sequences, channels = x.shape
+        taps = weight.shape[-1]
+        span = (taps - 1) * dilation
+        _require(tuple(states.shape) == (sequences, span, channels),
+                 f"causalConv: states {list(states.shape)}")
+        status = self.lib.drift_causal_conv_decode(_ptr(x), sequences, channels, _ptr(weight), taps,
+                                                   dilation, _ptr(states), _ptr(out), self._stream())
+        check("drift_causal_conv_decode", status)
+
+    def gated_delta_rule_decode(self, qkv, a, b, decay, dt_bias, states, rule, out) -> None:
+        """One token per sequence: qkv [S, width], a, b [S, value_heads],
+        states [S, value_heads, D, D], out [S, value_heads, D]."""
+        key_heads, value_heads, d, tiled = rule
+        _f32("gatedDeltaRule", qkv, a, b, decay, dt_bias, states, out)
+        sequences = qkv.shape[0]
+        _require(tuple(states.shape) == (sequences, value_heads, d, d),
+                 f"gatedDeltaRule: states {list(states.shape)}")
+        _require(tuple(out.shape) == (sequences, value_heads, d), f"gatedDeltaRule: out {list(out.shape)}")
+        status = self.lib.drift_gated_delta_rule_decode(
+            _ptr(qkv), sequences, key_heads, value_heads, d, int(tiled), _ptr(a), _ptr(b),
+            _ptr(decay), _ptr(dt_bias), _ptr(states), _ptr(out), self._stream())
+        check("drift_gated_delta_rule_decode", status)
 
     def gated_rms_norm(self, x, weight, gate, kind: int, epsilon: float, out,
                        prepared: Optional[torch.Tensor] = None, heads: int = 0) -> None:

@@ -212,6 +212,16 @@ int drift_gated_delta_rule(const float* qkv, int tokens, int key_heads, int valu
                            int tiled, const float* a, const float* b, const float* decay,
                            const float* dt_bias, float* state, float* history, float* out,
                            drift_stream_t stream);
+/* The decode step of a batch of sequences (new): one token per sequence, each
+ * with its own state -- x / qkv rows are the sequences, states [sequences]
+ * [span][channels] and [sequences][value_heads][dim][dim]. */
+int drift_causal_conv_decode(const float* x, int sequences, int channels, const float* weight,
+                             int taps, int dilation, float* states, float* out,
+                             drift_stream_t stream);
+int drift_gated_delta_rule_decode(const float* qkv, int sequences, int key_heads, int value_heads,
+                                  int dim, int tiled, const float* a, const float* b,
+                                  const float* decay, const float* dt_bias, float* states,
+                                  float* out, drift_stream_t stream);
 /* NormalisationOps.gatedRmsNorm (CpuNormalisation.scala:167-178): per row of
  * cols (<= 512) values, rmsNorm(x) * weight * act(gate), act DRIFT_SILU or
  * DRIFT_SIGMOID; out may be x. With `prepared` (rows = tokens x heads), the
@@ -272,6 +282,30 @@ int drift_comm_destroy(void* comm);
 int drift_add_rms_norm_allreduce(void* comm, int slot, float* x, const float* weight,
                                  float epsilon, float weight_offset, float* out, int64_t rows,
                                  int64_t cols, void* prepared, drift_stream_t stream);
+
+/* The gated attention of the hybrid decoder (models/HybridBlocks.scala:
+ * fullAttention): drift_attention_inputs_decode over queryAndGate [batch]
+ * [q_heads][2 head_dim], whose first half per head is the query
+ * (AttentionOps.attentionInputs' splitHalves, ops/AttentionOps.scala:73-107);
+ * and drift_attention_decode whose output is multiplied by sigmoid(gate)
+ * (gate + (z q_heads + h) gate_stride + d: the second half of queryAndGate
+ * with gate_stride 2 head_dim), as gated(Sigmoid, gate, attended) does, in
+ * the join; `prepared` may be NULL. */
+int drift_attention_inputs_decode_split(const float* query_and_gate, const float* k,
+                                        const float* v, int batch, int q_heads, int kv_heads,
+                                        int head_dim, const float* q_norm, const float* k_norm,
+                                        float epsilon, float weight_offset,
+                                        const int32_t* positions, float theta, int rotary,
+                                        int layout, float* q_out, void* keys, void* values,
+                                        int pages, int page_size, const int32_t* page_tables,
+                                        int table_stride, drift_stream_t stream);
+int drift_attention_decode_gated(const float* q, int batch, int q_heads, const void* keys,
+                                 const void* values, int pages, int page_size, int kv_heads,
+                                 int head_dim, const int32_t* page_tables, int table_stride,
+                                 const int32_t* positions, int max_key_count, float scale,
+                                 int window, float softcap, const float* sinks, float* out,
+                                 const float* gate, int gate_stride, void* prepared,
+                                 drift_stream_t stream);
 
 /* The library keeps one grow-only scratch buffer per device for the products'
  * prepared x (as the runner's HIP backend keeps grow-only scratch,
