@@ -262,6 +262,8 @@ def run_gpu(args) -> dict | None:
     # benchmark config C4: the dense decoder's decode step, tensor-parallel over the
     # job's GPUs (one NCCL group), tok/s at each batch
     decode = run_decode(args, ops, rank, world, stream) if args.decode else None
+    # benchmark config C5: the hybrid MoE decoder, a replica per GPU
+    hybrid = run_hybrid(args, ops, rank, world, stream) if args.decode else None
 
     times = torch.tensor([elapsed_ms, e2e_ms], device="cuda")
     if world > 1:
@@ -318,6 +320,7 @@ def run_gpu(args) -> dict | None:
         "clocks": clock_info,
         "sweep": sweep,
         "decode": decode,
+        "decode_hybrid": hybrid,
     }
     if args.cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(seconds=args.cpu_seconds)
@@ -380,6 +383,60 @@ def run_decode(args, ops, rank: int, world: int, stream) -> dict:
         decoder.release()
         del decoder
         torch.cuda.empty_cache()
+    return out
+
+
+def run_hybrid(args, ops, rank: int, world: int, stream) -> dict:
+    """Decode tok/s of benchmark config C5 (48 layers, hidden 2048: 36 Gated
+    DeltaNet layers of 16 heads of 128 and 12 gated full-attention layers of
+    16 / 2 heads of 256, each with 512 experts, top-10, FFN 512, and a shared
+    expert; random-init Q4_1 weights, F32 routers; DeltaNet states N(0, 0.02),
+    F16 caches prefilled with N(0, 1) to 4095 positions): a step captured as a
+    CUDA graph, replayed, timed with CUDA events, the slowest rank's time.
+    Expert parallelism is not built: with N GPUs each runs its own replica
+    (independent sequences), and tok/s is the job's total."""
+    import torch
+
+    from drift_b200.hybrid import HybridConfig, HybridDecoder, HybridWeights
+    from drift_b200.tensor_parallel import max_over_ranks
+
+    config = HybridConfig()
+    weights = HybridWeights.random(config, seed=rank)
+    peaks = measured_peaks()
+    per_token = weights.bytes_per_token(config)
+    out = {"config": "C5 hybrid MoE decode (Gated DeltaNet + gated attention + 512 experts)",
+           "parallelism": f"replicas x{world}" if world > 1 else "one GPU",
+           "context": DECODE_CONTEXT, "weights": "random-init Q4_1 (C2 law), F32 routers",
+           "weight_bytes_per_sequence_step": per_token}
+    steps = max(5, min(args.steps, 30))
+    for batch in args.decode_batches:
+        decoder = HybridDecoder(ops, config, weights, batch, DECODE_CONTEXT)
+        decoder.prefill_random(DECODE_CONTEXT - 1)
+        decoder.positions.fill_(DECODE_CONTEXT - 1)
+        decoder.capture(stream)
+        for _ in range(3):
+            decoder.replay()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(steps):
+                decoder.replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+        ms = max_over_ranks(start.elapsed_time(end) / steps, device="cuda")
+        out[f"b{batch}"] = {
+            "tok_s": round(world * batch / (ms / 1e3), 1),
+            "ms_per_step": round(ms, 4),
+            "steps": steps,
+            "fraction_of_measured_hbm_b1_bytes": round(per_token / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4)
+            if batch == 1 else None,
+        }
+        decoder.release()
+        del decoder
+        torch.cuda.empty_cache()
+    del weights
+    torch.cuda.empty_cache()
     return out
 
 
@@ -587,6 +644,27 @@ def run_case(spec: str, repeat: int, dtype: int = Q4_1) -> None:
     print(f"case {b}x{n}x{k} dtype {dtype}: {repeat} products, y[0,:4] = {y[0, :4].tolist()}")
 
 
+def run_hybrid_case(batch: int, layers: int, steps: int) -> None:
+    """`--hybrid-case B`: eager decode steps of C5 (with `--decode-layers`
+    layers), nothing timed -- the workload of a launch-list capture."""
+    import torch
+
+    from drift_b200.hybrid import HybridConfig, HybridDecoder, HybridWeights
+    from drift_b200.ops import CudaOps
+
+    torch.cuda.set_device(0)
+    config = HybridConfig(layers=min(layers, HybridConfig.layers))
+    decoder = HybridDecoder(CudaOps(), config, HybridWeights.random(config), batch,
+                            DECODE_CONTEXT)
+    decoder.prefill_random(DECODE_CONTEXT - 1)
+    decoder.positions.fill_(DECODE_CONTEXT - 1)
+    decoder.reserve()
+    for _ in range(steps):
+        decoder.step()
+    torch.cuda.synchronize()
+    print(f"hybrid case b{batch} x {config.layers} layers: {steps} steps")
+
+
 def run_decode_case(batch: int, layers: int, steps: int) -> None:
     """`--decode-case B`: eager decode steps of C4 (with `--decode-layers`
     layers), nothing timed -- the workload of a launch-list capture."""
@@ -621,6 +699,7 @@ def main() -> int:
     parser.add_argument("--decode-exchange", choices=("peer", "nccl"), default="peer",
                         help="tensor-parallel decode: the fused NVLink peer exchange, or NCCL")
     parser.add_argument("--decode-case", type=int, help="B: eager C4 decode steps (profiling)")
+    parser.add_argument("--hybrid-case", type=int, help="B: eager C5 decode steps (profiling)")
     parser.add_argument("--decode-layers", type=int, default=36)
     parser.add_argument("--case", help="B,N,K: run one product --repeat times (profiling)")
     parser.add_argument("--case-dtype", type=int, default=Q4_1)
@@ -630,6 +709,9 @@ def main() -> int:
     args.decode_batches = [int(b) for b in str(args.decode_batches).split(",") if b]
     if args.decode_case:
         run_decode_case(args.decode_case, args.decode_layers, args.repeat)
+        return 0
+    if args.hybrid_case:
+        run_hybrid_case(args.hybrid_case, args.decode_layers, args.repeat)
         return 0
     if args.case:
         run_case(args.case, args.repeat, args.case_dtype)
