@@ -12,6 +12,7 @@
 #include "common.cuh"
 #include "quant.cuh"
 #include "registry.cuh"
+#include "rowwise.cuh"
 
 namespace drift {
 
@@ -69,17 +70,30 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
     chosen_id[j] = best_expert;
     if ((best_expert & 31) == lane && best_expert < experts) taken |= 1u << (best_expert >> 5);
   }
-  if (lane == 0) {
-    double sum = 0.0;
-    double e[16];
-    for (int j = 0; j < k; ++j) {
-      e[j] = exp(double(chosen[j]) - double(chosen[0]));
-      sum += e[j];
-    }
-    for (int j = 0; j < k; ++j) {
-      ids[(long long)t * k + j] = chosen_id[j];
-      weights[(long long)t * k + j] = float(e[j] / sum);
-    }
+  // the softmax over the chosen: lane j's exponential (every lane holds the
+  // same chosen values), summed in slot order
+  double mine = 0.0;
+#pragma unroll
+  for (int j = 0; j < 16; ++j)
+    if (j == lane && j < k) mine = exp(double(chosen[j]) - double(chosen[0]));
+  double e[16];
+  double sum = 0.0;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    e[j] = __shfl_sync(0xffffffffu, mine, j);
+    if (j < k) sum += e[j];
+  }
+  if (lane < k) {
+    double ej = 0.0;
+    int id = 0;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (j == lane) {
+        ej = e[j];
+        id = chosen_id[j];
+      }
+    ids[(long long)t * k + lane] = id;
+    weights[(long long)t * k + lane] = float(ej / sum);
   }
 }
 
@@ -90,38 +104,6 @@ DRIFT_REGISTER(route_topk, route_kernel)
 // weight with x row s / divisor, prepared as for the plain product. The
 // warps of a CTA split rows and blocks as matvec_x22_kernel does. GATED: a
 // gate and an up weight of the same shape, out = silu(gate . x) * (up . x).
-template <typename T, int KS>
-__device__ __forceinline__ float expert_row_sum(const uint8_t* __restrict__ weight,
-                                                const uint32_t* __restrict__ record, int cols,
-                                                long long row, int kw) {
-  const int lane = threadIdx.x % WARP;
-  const int blocks = cols / 32;
-  const uint8_t* base = weight + row * (long long)blocks * T::BYTES;
-  float sum = 0.0f;
-  for (int c = kw * WARP + lane; c < blocks; c += WARP * KS) {
-    uint32_t w[T::WORDS];
-    load_block<T>(base, c, w);
-    const uint4* rec = reinterpret_cast<const uint4*>(record + (long long)c * X_RECORD_WORDS);
-    uint32_t planes[24];
-#pragma unroll
-    for (int i = 0; i < 6; ++i) {
-      const uint4 q = __ldg(rec + i);
-      planes[4 * i] = q.x;
-      planes[4 * i + 1] = q.y;
-      planes[4 * i + 2] = q.z;
-      planes[4 * i + 3] = q.w;
-    }
-    const uint4 tail = __ldg(rec + 6);
-    const Codes codes = T::decode(w, c);
-    int a0, a1, a2;
-    plane_sums<T>(codes, planes, a0, a1, a2);
-    sum += block_dot<T>(codes, a0, a1, a2, __uint_as_float(tail.x), int(tail.y));
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o /= 2) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  return sum;
-}
-
 // Each warp: rows of its group, k-split kw; 8 warps = (8 / KS) row groups.
 template <typename T, int KS, bool GATED>
 __global__ void __launch_bounds__(256) experts_x22_kernel(
@@ -148,14 +130,53 @@ __global__ void __launch_bounds__(256) experts_x22_kernel(
     }
     return;
   }
+  // the warp's rows side by side: each block of x is read once for all of
+  // them, and every row's weights of the block are in flight together; a
+  // row's sum is its lane's blocks in order, then the warp's lanes
   float g[ROWS], u[ROWS];
 #pragma unroll
+  for (int r = 0; r < ROWS; ++r) g[r] = u[r] = 0.0f;
+  const long long row_bytes = (long long)blocks * T::BYTES;
+  const uint8_t* gate_base = gate + expert * expert_bytes;
+  const uint8_t* up_base = up + expert * expert_bytes;
+  for (int c = kw * WARP + lane; c < blocks; c += WARP * KS) {
+    uint32_t wg[ROWS][T::WORDS], wu[ROWS][T::WORDS];
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) {
+      const long long row = row0 + r < rows ? row0 + r : row0;
+      load_block<T>(gate_base + row * row_bytes, c, wg[r]);
+      if (GATED) load_block<T>(up_base + row * row_bytes, c, wu[r]);
+    }
+    const uint4* rec = reinterpret_cast<const uint4*>(record + (long long)c * X_RECORD_WORDS);
+    uint32_t planes[24];
+#pragma unroll
+    for (int i = 0; i < 6; ++i) {
+      const uint4 q = __ldg(rec + i);
+      planes[4 * i] = q.x;
+      planes[4 * i + 1] = q.y;
+      planes[4 * i + 2] = q.z;
+      planes[4 * i + 3] = q.w;
+    }
+    const uint4 tail = __ldg(rec + 6);
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) {
+      int a0, a1, a2;
+      const Codes cg = T::decode(wg[r], c);
+      plane_sums<T>(cg, planes, a0, a1, a2);
+      g[r] += block_dot<T>(cg, a0, a1, a2, __uint_as_float(tail.x), int(tail.y));
+      if (GATED) {
+        const Codes cu = T::decode(wu[r], c);
+        plane_sums<T>(cu, planes, a0, a1, a2);
+        u[r] += block_dot<T>(cu, a0, a1, a2, __uint_as_float(tail.x), int(tail.y));
+      }
+    }
+  }
+#pragma unroll
   for (int r = 0; r < ROWS; ++r) {
-    g[r] = u[r] = 0.0f;
-    const int row = row0 + r;
-    if (row < rows) {
-      g[r] = expert_row_sum<T, KS>(gate + expert * expert_bytes, record, cols, row, kw);
-      if (GATED) u[r] = expert_row_sum<T, KS>(up + expert * expert_bytes, record, cols, row, kw);
+#pragma unroll
+    for (int o = 16; o > 0; o /= 2) {
+      g[r] += __shfl_xor_sync(0xffffffffu, g[r], o);
+      if (GATED) u[r] += __shfl_xor_sync(0xffffffffu, u[r], o);
     }
   }
   if (lane == 0) {
@@ -274,10 +295,12 @@ __device__ __forceinline__ float shared_gate(const float* x, const float* router
   return 1.0f / (1.0f + expf(-total));
 }
 
-// One block of 256 threads per token. NORM: the combined row is also the
+// One block of 1024 threads per token, PER values of the row a thread, every
+// load issued before the first use. NORM: the combined row is also the
 // residual stream (written back) and its RMS norm goes to `normed`.
-template <bool NORM>
-__global__ void __launch_bounds__(256) combine_kernel(
+constexpr int COMBINE_THREADS = 1024, MAX_COMBINE_K = 16;
+template <bool NORM, int PER>
+__global__ void __launch_bounds__(COMBINE_THREADS) combine_kernel(
     const float* __restrict__ expert_out, const float* __restrict__ weights,
     const float* __restrict__ shared_out, const float* __restrict__ shared_input,
     const float* __restrict__ shared_router, const float* residual, float* out, int k, int hidden,
@@ -287,40 +310,88 @@ __global__ void __launch_bounds__(256) combine_kernel(
   pdl_wait();     // what the kernels before this one wrote is visible
   __shared__ float partial[32];
   const long long t = blockIdx.x;
-  const float gate =
-      shared_out ? shared_gate(shared_input + t * hidden, shared_router, hidden, partial) : 0.0f;
-  float squares = 0.0f;
-  for (int c = threadIdx.x; c < hidden; c += blockDim.x) {
-    float sum = residual ? residual[t * hidden + c] : 0.0f;
-    float routed = 0.0f;
-    for (int j = 0; j < k; ++j)
-      routed = fmaf(weights[t * k + j], expert_out[(t * k + j) * hidden + c], routed);
-    sum += routed;
-    if (shared_out) sum = fmaf(gate, shared_out[t * hidden + c], sum);
-    out[t * hidden + c] = sum;
-    squares = fmaf(sum, sum, squares);
+  float routed[PER], res[PER], shared[PER], dot = 0.0f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int c = threadIdx.x + i * COMBINE_THREADS;
+    const bool in = c < hidden;
+    res[i] = residual && in ? residual[t * hidden + c] : 0.0f;
+    shared[i] = shared_out && in ? shared_out[t * hidden + c] : 0.0f;
+    if (shared_out && in) dot = fmaf(shared_input[t * hidden + c], shared_router[c], dot);
+    routed[i] = 0.0f;
+  }
+  // the routed experts' outputs, weighted, in slot order: GROUP slots'
+  // loads in flight at a time (32 values a thread)
+  constexpr int GROUP = 32 / PER < MAX_COMBINE_K ? 32 / PER : MAX_COMBINE_K;
+  for (int j0 = 0; j0 < k; j0 += GROUP) {
+    float part[GROUP][PER];
+#pragma unroll
+    for (int j = 0; j < GROUP; ++j)
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const int c = threadIdx.x + i * COMBINE_THREADS;
+        part[j][i] = j0 + j < k && c < hidden ? expert_out[(t * k + j0 + j) * hidden + c] : 0.0f;
+      }
+#pragma unroll
+    for (int j = 0; j < GROUP; ++j) {
+      if (j0 + j >= k) break;
+      const float wj = weights[t * k + j0 + j];
+#pragma unroll
+      for (int i = 0; i < PER; ++i) routed[i] = fmaf(wj, part[j][i], routed[i]);
+    }
+  }
+  // the shared expert's gate: sigmoid(x . router)
+  float gate = 0.0f;
+  if (shared_out) gate = 1.0f / (1.0f + expf(-block_sum(dot, partial)));
+  float squares = 0.0f, sum[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int c = threadIdx.x + i * COMBINE_THREADS;
+    sum[i] = res[i] + routed[i];
+    if (shared_out) sum[i] = fmaf(gate, shared[i], sum[i]);
+    if (c < hidden) out[t * hidden + c] = sum[i];
+    squares = fmaf(sum[i], sum[i], squares);
   }
   if (!NORM) return;
-#pragma unroll
-  for (int o = 16; o > 0; o /= 2) squares += __shfl_xor_sync(0xffffffffu, squares, o);
-  if (threadIdx.x % WARP == 0) partial[threadIdx.x / WARP] = squares;
-  __syncthreads();
-  float total = 0.0f;
-  for (int w = 0; w < int(blockDim.x / WARP); ++w) total += partial[w];
+  const float total = block_sum(squares, partial);
   const float scale = 1.0f / sqrtf(total / float(hidden) + epsilon);
-  for (int c = threadIdx.x; c < hidden; c += blockDim.x)
-    normed[t * hidden + c] = out[t * hidden + c] * scale * (norm_weight[c] + weight_offset);
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int c = threadIdx.x + i * COMBINE_THREADS;
+    if (c < hidden) normed[t * hidden + c] = sum[i] * scale * (norm_weight[c] + weight_offset);
+  }
 }
 
-DRIFT_REGISTER(moe_combine, combine_kernel<false>)
-DRIFT_REGISTER(moe_combine_norm, combine_kernel<true>)
+DRIFT_REGISTER(moe_combine, (combine_kernel<false, 2>))
+DRIFT_REGISTER(moe_combine_norm, (combine_kernel<true, 2>))
+
+template <bool NORM>
+static int launch_combine(const float* expert_out, const float* weights, int64_t tokens, int64_t k,
+                          int64_t hidden, const float* shared_out, const float* shared_input,
+                          const float* shared_router, const float* residual, float* out,
+                          const float* norm_weight, float* normed, float epsilon,
+                          float weight_offset, cudaStream_t stream) {
+  const unsigned grid = unsigned(tokens);
+#define DRIFT_COMBINE(PER)                                                                        \
+  DRIFT_CUDA(launch_pdl(combine_kernel<NORM, PER>, grid, COMBINE_THREADS, 0, stream, expert_out,  \
+                        weights, shared_out, shared_input, shared_router, residual, out, int(k), \
+                        int(hidden), norm_weight, normed, epsilon, weight_offset))
+  if (hidden <= 1024) DRIFT_COMBINE(1);
+  else if (hidden <= 2048) DRIFT_COMBINE(2);
+  else if (hidden <= 4096) DRIFT_COMBINE(4);
+  else DRIFT_COMBINE(8);
+#undef DRIFT_COMBINE
+  DRIFT_LAUNCHED(NORM ? "moe_combine_norm" : "moe_combine");
+  return 0;
+}
 
 static int check_combine(const float* expert_out, const float* weights, int64_t tokens, int64_t k,
                          int64_t hidden, const float* shared_out, const float* shared_input,
                          const float* shared_router, const void* out) {
-  if (tokens < 0 || k < 0 || hidden < 0 || tokens > 0x7fffffffll || hidden > 0x7fffffffll)
-    return invalid("moeCombine over [%lld, %lld] with k %lld", (long long)tokens,
-                   (long long)hidden, (long long)k);
+  if (tokens < 0 || k < 0 || hidden < 0 || tokens > 0x7fffffffll || hidden > 8192 ||
+      k > MAX_COMBINE_K)
+    return invalid("moeCombine over [%lld, %lld] with k %lld (at most 8192 wide, k 16)",
+                   (long long)tokens, (long long)hidden, (long long)k);
   if (tokens > 0 && hidden > 0 && (!out || (k > 0 && (!expert_out || !weights))))
     return invalid("moeCombine: a null tensor");
   if (shared_out && (!shared_input || !shared_router))
@@ -368,11 +439,9 @@ int drift_moe_combine(const float* expert_out, const float* weights, int64_t tok
   DRIFT_TRY(check_combine(expert_out, weights, tokens, k, hidden, shared_out, shared_input,
                           shared_router, out));
   if (tokens == 0 || hidden == 0) return 0;
-  DRIFT_CUDA(launch_pdl(combine_kernel<false>, unsigned(tokens), 256, 0, cudaStream_t(stream),
-                        expert_out, weights, shared_out, shared_input, shared_router, residual, out,
-                        int(k), int(hidden), nullptr, nullptr, 0.0f, 0.0f));
-  DRIFT_LAUNCHED("moe_combine");
-  return 0;
+  return launch_combine<false>(expert_out, weights, tokens, k, hidden, shared_out, shared_input,
+                               shared_router, residual, out, nullptr, nullptr, 0.0f, 0.0f,
+                               cudaStream_t(stream));
 }
 
 int drift_moe_combine_norm(const float* expert_out, const float* weights, int64_t tokens,
@@ -384,12 +453,9 @@ int drift_moe_combine_norm(const float* expert_out, const float* weights, int64_
                           shared_router, residual));
   if (tokens == 0 || hidden == 0) return 0;
   if (!norm_weight || !normed) return invalid("moeCombineNorm: no norm weight or output");
-  DRIFT_CUDA(launch_pdl(combine_kernel<true>, unsigned(tokens), 256, 0, cudaStream_t(stream),
-                        expert_out, weights, shared_out, shared_input, shared_router, residual,
-                        residual, int(k), int(hidden), norm_weight, normed, epsilon,
-                        weight_offset));
-  DRIFT_LAUNCHED("moe_combine_norm");
-  return 0;
+  return launch_combine<true>(expert_out, weights, tokens, k, hidden, shared_out, shared_input,
+                              shared_router, residual, residual, norm_weight, normed, epsilon,
+                              weight_offset, cudaStream_t(stream));
 }
 
 }  // extern "C"

@@ -277,29 +277,52 @@ DRIFT_REGISTER(rope_f32, rope_kernel)
 // ---- products with F32 weights (routers) -----------------------------------------------------
 // One warp per (row, vector): float4 loads when k is a multiple of 4, float
 // sums in a fixed order, then shuffles.
+// F32 weights (routers, DeltaNet's a and b): a CTA of 256 threads per (row,
+// vector), the row in 16-byte loads, every load of a thread issued before
+// its first use (a 4096-value row is one round trip), summed per thread in
+// column order, then the block's fixed tree.
 template <bool BF16>
 __global__ void __launch_bounds__(256) matvec_f32_kernel(const void* __restrict__ x,
                                                          const float* __restrict__ weight,
                                                          float* __restrict__ y, int m, int n, int k) {
   pdl_trigger();  // the next kernel may launch and wait for this one
   pdl_wait();     // what the kernels before this one wrote is visible
-  const long long index = (long long)blockIdx.x * (blockDim.x / WARP) + threadIdx.x / WARP;
-  if (index >= (long long)m * n) return;
-  const int lane = threadIdx.x % WARP;
-  const int row = int(index % n), vector = int(index / n);
+  __shared__ float partial[32];
+  const int row = blockIdx.x % n, vector = blockIdx.x / n;
   const float* w = weight + (long long)row * k;
   float sum = 0.0f;
-  for (int c = lane; c < k; c += WARP) {
-    float xv;
-    if (BF16)
-      xv = __uint_as_float(uint32_t(reinterpret_cast<const uint16_t*>(x)[(long long)vector * k + c]) << 16);
-    else
-      xv = reinterpret_cast<const float*>(x)[(long long)vector * k + c];
-    sum = fmaf(w[c], xv, sum);
-  }
+  if (!BF16 && k % 4 == 0 && (reinterpret_cast<uintptr_t>(weight) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+    const float4* x4 = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) +
+                                                       (long long)vector * k);
+    const int quads = k / 4;
+    for (int base = 0; base < quads; base += 4 * 256) {
+      float4 wv[4], xv[4];
 #pragma unroll
-  for (int o = 16; o > 0; o /= 2) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  if (lane == 0) y[(long long)vector * n + row] = sum;
+      for (int u = 0; u < 4; ++u) {
+        const int q = base + u * 256 + threadIdx.x;
+        wv[u] = q < quads ? __ldg(w4 + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+        xv[u] = q < quads ? x4[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        sum = fmaf(wv[u].x, xv[u].x, sum);
+        sum = fmaf(wv[u].y, xv[u].y, sum);
+        sum = fmaf(wv[u].z, xv[u].z, sum);
+        sum = fmaf(wv[u].w, xv[u].w, sum);
+      }
+    }
+  } else {
+    for (int c = threadIdx.x; c < k; c += 256) {
+      const float xv =
+          BF16 ? __uint_as_float(uint32_t(reinterpret_cast<const uint16_t*>(x)[(long long)vector * k + c]) << 16)
+               : reinterpret_cast<const float*>(x)[(long long)vector * k + c];
+      sum = fmaf(w[c], xv, sum);
+    }
+  }
+  const float total = block_sum(sum, partial);
+  if (threadIdx.x == 0) y[(long long)vector * n + row] = total;
 }
 
 DRIFT_REGISTER(matvec_f32_f32x, matvec_f32_kernel<false>)
@@ -307,8 +330,10 @@ DRIFT_REGISTER(matvec_f32_bf16x, matvec_f32_kernel<true>)
 
 int matvec_f32_weights(int x_dtype, const void* x, const float* weight, float* y, int64_t m,
                        int64_t n, int64_t k, cudaStream_t stream) {
-  const long long warps = m * n;
-  const unsigned grid = unsigned((warps + 7) / 8);
+  const long long ctas = m * n;
+  if (ctas > 0x7fffffffll) return invalid("F32 product of %lld rows x %lld vectors", (long long)n,
+                                          (long long)m);
+  const unsigned grid = unsigned(ctas);
   if (x_dtype == DRIFT_BF16)
     DRIFT_CUDA(launch_pdl(matvec_f32_kernel<true>, grid, 256, 0, stream, x, weight, y, int(m),
                           int(n), int(k)));
