@@ -393,30 +393,36 @@ def run_hybrid(args, ops, rank: int, world: int, stream) -> dict:
     expert; random-init Q4_1 weights, F32 routers; DeltaNet states N(0, 0.02),
     F16 caches prefilled with N(0, 1) to 4095 positions): a step captured as a
     CUDA graph, replayed, timed with CUDA events, the slowest rank's time.
-    Expert parallelism is not built: with N GPUs each runs its own replica
-    (independent sequences), and tok/s is the job's total."""
+    With N GPUs the model is split over them (expert parallelism for the
+    experts, DeltaNet and query heads and the lm-head by rank, the two
+    exchanges of a layer over the NVLink peer exchange)."""
     import torch
+    import torch.distributed as dist
 
     from drift_b200.hybrid import HybridConfig, HybridDecoder, HybridWeights
     from drift_b200.tensor_parallel import max_over_ranks
 
     config = HybridConfig()
-    weights = HybridWeights.random(config, seed=rank)
+    weights = HybridWeights.random(config, rank=rank, world=world)
+    group = dist.group.WORLD if world > 1 else None
     peaks = measured_peaks()
     per_token = weights.bytes_per_token(config)
     out = {"config": "C5 hybrid MoE decode (Gated DeltaNet + gated attention + 512 experts)",
-           "parallelism": f"replicas x{world}" if world > 1 else "one GPU",
+           "parallelism": (f"expert + head parallel x{world} (NVLink peer exchange)" if world > 1
+                           else "one GPU"),
            "context": DECODE_CONTEXT, "weights": "random-init Q4_1 (C2 law), F32 routers",
-           "weight_bytes_per_sequence_step": per_token}
+           "weight_bytes_per_sequence_step_per_gpu": per_token}
     steps = max(5, min(args.steps, 30))
     for batch in args.decode_batches:
-        decoder = HybridDecoder(ops, config, weights, batch, DECODE_CONTEXT)
+        decoder = HybridDecoder(ops, config, weights, batch, DECODE_CONTEXT, group=group)
         decoder.prefill_random(DECODE_CONTEXT - 1)
         decoder.positions.fill_(DECODE_CONTEXT - 1)
         decoder.capture(stream)
         for _ in range(3):
             decoder.replay()
         torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record(stream)
         with torch.cuda.stream(stream):
@@ -426,7 +432,7 @@ def run_hybrid(args, ops, rank: int, world: int, stream) -> dict:
         torch.cuda.synchronize()
         ms = max_over_ranks(start.elapsed_time(end) / steps, device="cuda")
         out[f"b{batch}"] = {
-            "tok_s": round(world * batch / (ms / 1e3), 1),
+            "tok_s": round(batch / (ms / 1e3), 1),
             "ms_per_step": round(ms, 4),
             "steps": steps,
             "fraction_of_measured_hbm_b1_bytes": round(per_token / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4)

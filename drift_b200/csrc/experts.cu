@@ -109,7 +109,8 @@ template <typename T, int KS, bool GATED>
 __global__ void __launch_bounds__(256) experts_x22_kernel(
     const uint8_t* __restrict__ gate, const uint8_t* __restrict__ up, long long expert_bytes,
     const int* __restrict__ ids, const uint32_t* __restrict__ records, int divisor,
-    float* __restrict__ y, int rows, int cols, long long experts, int* error) {
+    float* __restrict__ y, int rows, int cols, long long experts, long long first_expert,
+    int others_zero, int* error) {
   pdl_trigger();  // the next kernel may launch and wait for this one
   pdl_wait();     // what the kernels before this one wrote is visible
   constexpr int GROUPS = 8 / KS;
@@ -118,15 +119,18 @@ __global__ void __launch_bounds__(256) experts_x22_kernel(
   const int warp = threadIdx.x / WARP, lane = threadIdx.x % WARP;
   const int kw = warp % KS, group = warp / KS;
   const int slot = blockIdx.y;
-  const long long expert = ids[slot];
+  // the slot's expert in this weight (which holds experts [first_expert,
+  // first_expert + experts)); with others_zero, a slot of another rank's
+  // expert is zeros, not an error
+  const long long expert = ids[slot] - first_expert;
   const int row0 = (blockIdx.x * GROUPS + group) * ROWS;
   const int blocks = cols / 32;
   const uint32_t* record = records + (long long)(slot / divisor) * blocks * X_RECORD_WORDS;
   if (expert < 0 || expert >= experts) {
-    if (threadIdx.x == 0 && blockIdx.x == 0 && error) atomicCAS(error, 0, 1);
+    if (!others_zero && threadIdx.x == 0 && blockIdx.x == 0 && error) atomicCAS(error, 0, 1);
     for (int r = threadIdx.x; r < GROUPS * ROWS; r += blockDim.x) {
       const int row = blockIdx.x * GROUPS * ROWS + r;
-      if (row < rows) y[(long long)slot * rows + row] = __int_as_float(0x7fc00000);
+      if (row < rows) y[(long long)slot * rows + row] = others_zero ? 0.0f : __int_as_float(0x7fc00000);
     }
     return;
   }
@@ -217,7 +221,8 @@ DRIFT_EXPERTS_REGISTER(Q4_1T, q4_1)
 template <typename T, bool GATED>
 static int launch_experts(const uint8_t* gate, const uint8_t* up, long long expert_bytes,
                           const int* ids, const uint32_t* records, int divisor, float* y, int rows,
-                          int cols, int slots, long long experts, cudaStream_t stream) {
+                          int cols, int slots, long long experts, long long first_expert,
+                          int others_zero, cudaStream_t stream) {
   const int blocks = cols / 32;
   const int ks = blocks >= 128 ? 4 : (blocks >= 64 ? 2 : 1);
   const int rows_per_cta = 4 * (8 / ks);
@@ -225,13 +230,16 @@ static int launch_experts(const uint8_t* gate, const uint8_t* up, long long expe
   int* error = device_error_word();
   if (ks == 4)
     DRIFT_CUDA(launch_pdl(experts_x22_kernel<T, 4, GATED>, grid, 256, 0, stream, gate, up,
-                          expert_bytes, ids, records, divisor, y, rows, cols, experts, error));
+                          expert_bytes, ids, records, divisor, y, rows, cols, experts, first_expert,
+                          others_zero, error));
   else if (ks == 2)
     DRIFT_CUDA(launch_pdl(experts_x22_kernel<T, 2, GATED>, grid, 256, 0, stream, gate, up,
-                          expert_bytes, ids, records, divisor, y, rows, cols, experts, error));
+                          expert_bytes, ids, records, divisor, y, rows, cols, experts, first_expert,
+                          others_zero, error));
   else
     DRIFT_CUDA(launch_pdl(experts_x22_kernel<T, 1, GATED>, grid, 256, 0, stream, gate, up,
-                          expert_bytes, ids, records, divisor, y, rows, cols, experts, error));
+                          expert_bytes, ids, records, divisor, y, rows, cols, experts, first_expert,
+                          others_zero, error));
   DRIFT_LAUNCHED("experts_x22");
   return 0;
 }
@@ -239,7 +247,7 @@ static int launch_experts(const uint8_t* gate, const uint8_t* up, long long expe
 static int experts_common(bool gated, int x_dtype, const void* x, int64_t x_rows,
                           int weight_dtype, const void* gate, const void* up, int64_t experts,
                           int64_t n, int64_t k, const int32_t* ids, int64_t slots, float* out,
-                          cudaStream_t stream) {
+                          int64_t first_expert, int others_zero, cudaStream_t stream) {
   const char* name = gated ? "expertsGatedLinear" : "expertsLinear";
   if (x_dtype != DRIFT_F32 && x_dtype != DRIFT_BF16)
     return invalid("%s takes F32 (or BF16) x, not %s", name, dtype_name(x_dtype));
@@ -267,9 +275,11 @@ static int experts_common(bool gated, int x_dtype, const void* x, int64_t x_rows
   const uint8_t* u = static_cast<const uint8_t*>(up);
 #define DRIFT_EXPERTS_CASE(T)                                                                   \
   return gated ? launch_experts<T, true>(g, u, expert_bytes, ids, records, divisor, out, int(n), \
-                                         int(k), int(slots), experts, stream)                   \
+                                         int(k), int(slots), experts, first_expert, others_zero, \
+                                         stream)                                                \
                : launch_experts<T, false>(g, g, expert_bytes, ids, records, divisor, out, int(n), \
-                                          int(k), int(slots), experts, stream);
+                                          int(k), int(slots), experts, first_expert,             \
+                                          others_zero, stream);
   switch (weight_dtype) {
     case DRIFT_Q8_0: DRIFT_EXPERTS_CASE(Q8_0T)
     case DRIFT_Q4_0: DRIFT_EXPERTS_CASE(Q4_0T)
@@ -421,7 +431,16 @@ int drift_experts_linear(int x_dtype, const void* x, int64_t x_rows, int weight_
                          const void* weight, int64_t experts, int64_t n, int64_t k,
                          const int32_t* ids, int64_t slots, float* out, drift_stream_t stream) {
   return experts_common(false, x_dtype, x, x_rows, weight_dtype, weight, nullptr, experts, n, k,
-                        ids, slots, out, cudaStream_t(stream));
+                        ids, slots, out, 0, 0, cudaStream_t(stream));
+}
+
+int drift_experts_linear_local(int x_dtype, const void* x, int64_t x_rows, int weight_dtype,
+                               const void* weight, int64_t experts, int64_t first_expert,
+                               int64_t n, int64_t k, const int32_t* ids, int64_t slots,
+                               float* out, drift_stream_t stream) {
+  if (first_expert < 0) return invalid("expertsLinear: experts from %lld", (long long)first_expert);
+  return experts_common(false, x_dtype, x, x_rows, weight_dtype, weight, nullptr, experts, n, k,
+                        ids, slots, out, first_expert, 1, cudaStream_t(stream));
 }
 
 int drift_experts_gated_linear(int x_dtype, const void* x, int64_t x_rows, int weight_dtype,
@@ -429,7 +448,17 @@ int drift_experts_gated_linear(int x_dtype, const void* x, int64_t x_rows, int w
                                int64_t k, const int32_t* ids, int64_t slots, float* out,
                                drift_stream_t stream) {
   return experts_common(true, x_dtype, x, x_rows, weight_dtype, gate, up, experts, n, k, ids,
-                        slots, out, cudaStream_t(stream));
+                        slots, out, 0, 0, cudaStream_t(stream));
+}
+
+int drift_experts_gated_linear_local(int x_dtype, const void* x, int64_t x_rows, int weight_dtype,
+                                     const void* gate, const void* up, int64_t experts,
+                                     int64_t first_expert, int64_t n, int64_t k,
+                                     const int32_t* ids, int64_t slots, float* out,
+                                     drift_stream_t stream) {
+  if (first_expert < 0) return invalid("expertsGatedLinear: experts from %lld", (long long)first_expert);
+  return experts_common(true, x_dtype, x, x_rows, weight_dtype, gate, up, experts, n, k, ids,
+                        slots, out, first_expert, 1, cudaStream_t(stream));
 }
 
 int drift_moe_combine(const float* expert_out, const float* weights, int64_t tokens, int64_t k,

@@ -1,7 +1,7 @@
 """The hybrid MoE decoder's decode step on this library's ops: the op order of
 the runner's HybridBlocks (runner/src/drift/runner/models/HybridBlocks.scala:
 403-588) and Qwen35.decoderLayer (models/Qwen35.scala:356-410), for a batch
-of sequences on one GPU.
+of sequences, on one GPU or expert-parallel across the GPUs of a box.
 
 A layer is either Gated DeltaNet (three of every four) or gated full
 attention, then a mixture of experts:
@@ -19,6 +19,14 @@ attention, then a mixture of experts:
   shared expert's; the experts' down products and the shared one's; the
   combine (weights, the shared expert by sigmoid(x . shared router), the
   residual) and the next norm, one launch.
+
+With a process group (one process per GPU), the layers are split as the
+benchmark's expert-parallel configuration splits them (`Partition`): DeltaNet
+heads and query heads by rank (the key heads a rank's query heads read are
+its own), the out projections row-split, experts by id (routing replicated),
+the shared expert on rank 0, the lm-head by vocabulary rows; the two
+exchanges of a layer (the mixer's output, the mixture's) go through the
+NVLink peer exchange fused with the residual add and the norm.
 
 This is the harness of the benchmark's C5 decode tok/s: random-init weights
 (the benchmark's Q4_1 law; F32 routers, a and b, convolution, decay and norm
@@ -113,17 +121,68 @@ class HybridLayer:
     mixture: MixtureLayer
 
 
+@dataclass(frozen=True)
+class Partition:
+    """What rank `rank` of `world` holds (expert and tensor parallelism over
+    the GPUs of a box): its DeltaNet key and value heads, its query heads and
+    the key heads they read, its experts, its vocabulary rows."""
+    rank: int
+    world: int
+    delta_key_heads: tuple
+    delta_value_heads: tuple
+    q_heads: tuple
+    kv_heads: tuple
+    experts: tuple
+    vocab: tuple
+
+    @staticmethod
+    def of(c: "HybridConfig", rank: int = 0, world: int = 1) -> "Partition":
+        def even(total):
+            if total % world:
+                raise ValueError(f"{total} does not split {world} ways")
+            return (total * rank // world, total * (rank + 1) // world)
+
+        q = even(c.q_heads)
+        group = c.q_heads // c.kv_heads
+        kv = (q[0] // group, (q[1] - 1) // group + 1)  # the key heads of the rank's query heads
+        return Partition(rank, world, even(c.delta_key_heads), even(c.delta_value_heads), q, kv,
+                         even(c.experts), (c.vocab * rank // world, c.vocab * (rank + 1) // world))
+
+
+def _rows(w: Stored, ranges, width: int) -> Stored:
+    """The listed row ranges of w [N, K], concatenated."""
+    row = w.data.numel() // w.shape[0]
+    parts = [w.data[lo * row:hi * row] for lo, hi in ranges]
+    return Stored(w.dtype, (sum(hi - lo for lo, hi in ranges), width), torch.cat(parts).contiguous())
+
+
+def _columns(w: Stored, lo: int, hi: int) -> Stored:
+    """Columns [lo, hi) (whole 32-value blocks) of every row of w [N, K]."""
+    n, k = w.shape
+    row = w.data.numel() // n
+    per = row // (k // 32)
+    data = w.data.view(n, row)[:, lo // 32 * per:hi // 32 * per].contiguous().view(-1)
+    return Stored(w.dtype, (n, hi - lo), data)
+
+
 @dataclass
 class HybridWeights:
     embedding: Stored
     layers: list
     final_norm: torch.Tensor
     lm_head: Stored
+    part: Optional[Partition] = None
 
     @staticmethod
-    def random(c: HybridConfig, dtype: int = Q4_1, seed: int = 0) -> "HybridWeights":
+    def random(c: HybridConfig, dtype: int = Q4_1, seed: int = 0, rank: int = 0,
+               world: int = 1) -> "HybridWeights":
+        """Random-init weights by the benchmark laws, drawn on the device: this
+        rank's shards only (different ranks draw different numbers -- a timing
+        harness, not a model)."""
+        part = Partition.of(c, rank, world)
         g = torch.Generator(device="cuda")
-        g.manual_seed(seed)
+        g.manual_seed(seed * 1000 + rank)
+        span = lambda r: r[1] - r[0]
 
         def stored(n, k, experts: int = 0):
             rows = n * max(1, experts)
@@ -136,29 +195,28 @@ class HybridWeights:
         def norm(width):
             return 1.0 + 0.02 * torch.randn(width, generator=g, device="cuda")
 
-        channels = (2 * c.delta_key_heads + c.delta_value_heads) * c.delta_dim
-        value_width = c.delta_value_heads * c.delta_dim
+        dk, dv = span(part.delta_key_heads), span(part.delta_value_heads)
+        channels = (2 * dk + dv) * c.delta_dim
+        value_width = dv * c.delta_dim
+        qh, kvh, experts = span(part.q_heads), span(part.kv_heads), span(part.experts)
         layers = []
         for i in range(c.layers):
             if c.is_full(i):
-                mixer = FullLayer(stored(c.q_heads * 2 * c.head_dim, c.hidden),
-                                  stored(c.kv_heads * c.head_dim, c.hidden),
-                                  stored(c.kv_heads * c.head_dim, c.hidden),
+                mixer = FullLayer(stored(qh * 2 * c.head_dim, c.hidden),
+                                  stored(kvh * c.head_dim, c.hidden),
+                                  stored(kvh * c.head_dim, c.hidden),
                                   norm(c.head_dim), norm(c.head_dim),
-                                  stored(c.hidden, c.q_heads * c.head_dim))
+                                  stored(c.hidden, qh * c.head_dim))
             else:
                 mixer = DeltaLayer(stored(channels, c.hidden), stored(value_width, c.hidden),
-                                   f32(c.delta_value_heads, c.hidden, scale=0.02),
-                                   f32(c.delta_value_heads, c.hidden, scale=0.02),
+                                   f32(dv, c.hidden, scale=0.02), f32(dv, c.hidden, scale=0.02),
                                    f32(channels, c.conv_taps, scale=0.5),
-                                   -torch.exp(torch.rand(c.delta_value_heads, generator=g,
-                                                         device="cuda") * 2.5 - 1.0),
-                                   f32(c.delta_value_heads), norm(c.delta_dim),
-                                   stored(c.hidden, value_width))
+                                   -torch.exp(torch.rand(dv, generator=g, device="cuda") * 2.5 - 1.0),
+                                   f32(dv), norm(c.delta_dim), stored(c.hidden, value_width))
             mixture = MixtureLayer(f32(c.experts, c.hidden, scale=0.02),
-                                   stored(c.expert_ffn, c.hidden, c.experts),
-                                   stored(c.expert_ffn, c.hidden, c.experts),
-                                   stored(c.hidden, c.expert_ffn, c.experts),
+                                   stored(c.expert_ffn, c.hidden, experts),
+                                   stored(c.expert_ffn, c.hidden, experts),
+                                   stored(c.hidden, c.expert_ffn, experts),
                                    stored(c.shared_ffn, c.hidden, 1),
                                    stored(c.shared_ffn, c.hidden, 1),
                                    stored(c.hidden, c.shared_ffn),
@@ -166,7 +224,47 @@ class HybridWeights:
             layers.append(HybridLayer(norm(c.hidden), mixer, norm(c.hidden), mixture))
         return HybridWeights(Stored(Q8_0, (c.vocab, c.hidden),
                                     synthetic.quantized_device(Q8_0, c.vocab, c.hidden, g)),
-                             layers, norm(c.hidden), stored(c.vocab, c.hidden))
+                             layers, norm(c.hidden), stored(span(part.vocab), c.hidden), part)
+
+    def shard(self, c: HybridConfig, rank: int, world: int) -> "HybridWeights":
+        """Rank `rank`'s shards of these (whole-model) weights."""
+        part = Partition.of(c, rank, world)
+        d, hd = c.delta_dim, c.head_dim
+        kh, vh = part.delta_key_heads, part.delta_value_heads
+        layers = []
+        for layer in self.layers:
+            m = layer.mixer
+            if isinstance(m, FullLayer):
+                q0, q1 = part.q_heads
+                k0, k1 = part.kv_heads
+                mixer = FullLayer(_rows(m.q, [(q0 * 2 * hd, q1 * 2 * hd)], c.hidden),
+                                  _rows(m.k, [(k0 * hd, k1 * hd)], c.hidden),
+                                  _rows(m.v, [(k0 * hd, k1 * hd)], c.hidden),
+                                  m.q_norm, m.k_norm, _columns(m.o, q0 * hd, q1 * hd))
+            else:
+                keys = c.delta_key_heads * d
+                ranges = [(kh[0] * d, kh[1] * d), (keys + kh[0] * d, keys + kh[1] * d),
+                          (2 * keys + vh[0] * d, 2 * keys + vh[1] * d)]
+                conv = torch.cat([m.conv[lo:hi] for lo, hi in ranges]).contiguous()
+                mixer = DeltaLayer(_rows(m.qkv, ranges, c.hidden),
+                                   _rows(m.z, [(vh[0] * d, vh[1] * d)], c.hidden),
+                                   m.a[vh[0]:vh[1]].contiguous(), m.b[vh[0]:vh[1]].contiguous(),
+                                   conv, m.decay[vh[0]:vh[1]].contiguous(),
+                                   m.dt_bias[vh[0]:vh[1]].contiguous(), m.norm,
+                                   _columns(m.out, vh[0] * d, vh[1] * d))
+            x = layer.mixture
+            e0, e1 = part.experts
+
+            def experts(w: Stored) -> Stored:
+                per = w.data.numel() // w.shape[0]
+                return Stored(w.dtype, (e1 - e0,) + tuple(w.shape[1:]), w.data[e0 * per:e1 * per])
+
+            mixture = MixtureLayer(x.router, experts(x.gate), experts(x.up), experts(x.down),
+                                   x.shared_gate, x.shared_up, x.shared_down, x.shared_router)
+            layers.append(HybridLayer(layer.input_norm, mixer, layer.post_norm, mixture))
+        v0, v1 = part.vocab
+        return HybridWeights(self.embedding, layers, self.final_norm,
+                             _rows(self.lm_head, [(v0, v1)], c.hidden), part)
 
     def bytes_per_token(self, c: HybridConfig) -> int:
         """Weight bytes one sequence's decode step reads: every layer's
@@ -192,24 +290,35 @@ class HybridDecoder:
     """Decode steps for `batch` sequences of up to `context` positions."""
 
     def __init__(self, ops: CudaOps, config: HybridConfig, weights: HybridWeights, batch: int,
-                 context: int):
+                 context: int, group=None):
         c = self.config = config
         self.ops, self.weights, self.batch, self.context = ops, weights, batch, context
         b = batch
+        part = weights.part or Partition.of(c)
+        self.part = part
+        span = lambda r: r[1] - r[0]
+        # this rank's heads (all of them on one GPU)
+        self.delta_key_heads, self.delta_value_heads = (span(part.delta_key_heads),
+                                                        span(part.delta_value_heads))
+        self.q_heads, self.kv_heads = span(part.q_heads), span(part.kv_heads)
+        self.exchange = None
+        if group is not None and part.world > 1:
+            from .tensor_parallel import PeerExchange
+            self.exchange = PeerExchange(ops, group, b, c.hidden)
         f32 = dict(dtype=torch.float32, device="cuda")
         pages_per_sequence = (context + c.page_size - 1) // c.page_size
         self.page_tables = torch.arange(pages_per_sequence * b, dtype=torch.int32,
                                         device="cuda").view(b, pages_per_sequence)
-        self.channels = (2 * c.delta_key_heads + c.delta_value_heads) * c.delta_dim
-        self.value_width = c.delta_value_heads * c.delta_dim
+        self.channels = (2 * self.delta_key_heads + self.delta_value_heads) * c.delta_dim
+        self.value_width = self.delta_value_heads * c.delta_dim
         self.caches, self.conv_states, self.delta_states = {}, {}, {}
         for i, layer in enumerate(weights.layers):
             if isinstance(layer.mixer, FullLayer):
-                self.caches[i] = KvCache.allocate(pages_per_sequence * b, c.page_size, c.kv_heads,
-                                                  c.head_dim)
+                self.caches[i] = KvCache.allocate(pages_per_sequence * b, c.page_size,
+                                                  self.kv_heads, c.head_dim)
             else:
                 self.conv_states[i] = torch.zeros(b, c.conv_taps - 1, self.channels, **f32)
-                self.delta_states[i] = torch.zeros(b, c.delta_value_heads, c.delta_dim,
+                self.delta_states[i] = torch.zeros(b, self.delta_value_heads, c.delta_dim,
                                                    c.delta_dim, **f32)
         self.rope = Rope(c.theta, c.rotary)
         self.attention = Attention(1.0 / math.sqrt(c.head_dim))
@@ -222,15 +331,15 @@ class HybridDecoder:
         self.qkv = torch.zeros(b, self.channels, **f32)
         self.convolved = torch.zeros(b, self.channels, **f32)
         self.z = torch.zeros(b, self.value_width, **f32)
-        self.a = torch.zeros(b, c.delta_value_heads, **f32)
-        self.b = torch.zeros(b, c.delta_value_heads, **f32)
-        self.core = torch.zeros(b, c.delta_value_heads, c.delta_dim, **f32)
+        self.a = torch.zeros(b, self.delta_value_heads, **f32)
+        self.b = torch.zeros(b, self.delta_value_heads, **f32)
+        self.core = torch.zeros(b, self.delta_value_heads, c.delta_dim, **f32)
         # full attention
-        self.query_gate = torch.zeros(b, c.q_heads, 2 * c.head_dim, **f32)
-        self.k = torch.zeros(b, c.kv_heads, c.head_dim, **f32)
-        self.v = torch.zeros(b, c.kv_heads, c.head_dim, **f32)
-        self.q_turned = torch.zeros(b, c.q_heads, c.head_dim, **f32)
-        self.attended = torch.zeros(b, c.q_heads, c.head_dim, **f32)
+        self.query_gate = torch.zeros(b, self.q_heads, 2 * c.head_dim, **f32)
+        self.k = torch.zeros(b, self.kv_heads, c.head_dim, **f32)
+        self.v = torch.zeros(b, self.kv_heads, c.head_dim, **f32)
+        self.q_turned = torch.zeros(b, self.q_heads, c.head_dim, **f32)
+        self.attended = torch.zeros(b, self.q_heads, c.head_dim, **f32)
         # mixture
         self.logits_router = torch.zeros(b, c.experts, **f32)
         self.route_ids = torch.zeros(b, c.used, dtype=torch.int32, device="cuda")
@@ -240,8 +349,8 @@ class HybridDecoder:
         self.shared_ids = torch.zeros(b, dtype=torch.int32, device="cuda")
         self.shared_gated = torch.zeros(b, c.shared_ffn, **f32)
         self.shared_out = torch.zeros(b, c.hidden, **f32)
-        self.logits = torch.zeros(b, c.vocab, **f32)
-        widest = max(c.hidden, self.value_width, c.q_heads * c.head_dim, c.shared_ffn)
+        self.logits = torch.zeros(b, span(part.vocab), **f32)
+        widest = max(c.hidden, self.value_width, self.q_heads * c.head_dim, c.shared_ffn)
         self.prepared = ops.prepared_x(b, widest)
         self.graph: Optional[torch.cuda.CUDAGraph] = None
 
@@ -272,12 +381,13 @@ class HybridDecoder:
         ops.causal_conv_decode(self.qkv, layer.conv, 1, self.conv_states[index], self.convolved)
         ops.gated_delta_rule_decode(self.convolved, self.a, self.b, layer.decay, layer.dt_bias,
                                     self.delta_states[index],
-                                    (c.delta_key_heads, c.delta_value_heads, c.delta_dim, False),
+                                    (self.delta_key_heads, self.delta_value_heads, c.delta_dim,
+                                     False),
                                     self.core)
-        core = self.core.view(b * c.delta_value_heads, c.delta_dim)
-        ops.gated_rms_norm(core, layer.norm, self.z.view(b * c.delta_value_heads, c.delta_dim),
-                           SILU, c.epsilon, core, P, c.delta_value_heads)
-        ops.linears(self.core.view(b, self.value_width), [layer.out], [self.block_out], P)
+        core = self.core.view(b * self.delta_value_heads, c.delta_dim)
+        ops.gated_rms_norm(core, layer.norm, self.z.view(b * self.delta_value_heads, c.delta_dim),
+                           SILU, c.epsilon, core, P, self.delta_value_heads)
+        ops.linears(self.core.view(b, self.value_width), [layer.out], [self._block_out(0)], P)
 
     def _full(self, layer: FullLayer, index: int) -> None:
         ops, c, b, P = self.ops, self.config, self.batch, self.prepared
@@ -289,22 +399,46 @@ class HybridDecoder:
         ops.attention_decode(self.q_turned, self.caches[index], self.page_tables, self.positions,
                              self.context, self.attention, self.attended, P,
                              gate=self.query_gate[:, :, c.head_dim:])
-        ops.linears(self.attended.view(b, -1), [layer.o], [self.block_out], P)
+        ops.linears(self.attended.view(b, -1), [layer.o], [self._block_out(0)], P)
+
+    def _block_out(self, slot: int) -> torch.Tensor:
+        """Where a row-split output goes: the exchange's slot, or block_out."""
+        return self.exchange.slots[slot] if self.exchange is not None else self.block_out
 
     def _mixture(self, mixture: MixtureLayer, following: torch.Tensor) -> None:
         ops, c, P = self.ops, self.config, self.prepared
+        # routing is the same on every rank (the same x, the same router)
         ops.route_linear(self.normed, mixture.router, self.logits_router, self.route_ids,
                          self.route_weights)
+        next_norm = RowNorm(following, c.epsilon, 0.0, self.normed)
+        if self.exchange is None:
+            ops.experts_gated_linear(self.normed, mixture.gate, mixture.up,
+                                     self.route_ids.view(-1), self.expert_gated)
+            ops.experts_gated_linear(self.normed, mixture.shared_gate, mixture.shared_up,
+                                     self.shared_ids, self.shared_gated)
+            ops.experts_linear(self.expert_gated, mixture.down, self.route_ids.view(-1),
+                               self.expert_out)
+            ops.linears(self.shared_gated, [mixture.shared_down], [self.shared_out])
+            ops.moe_combine_norm(self.expert_out, self.route_weights,
+                                 SharedExpert(self.shared_out, self.normed, mixture.shared_router),
+                                 self.x, next_norm)
+            return
+        # expert parallelism: this rank's experts (other ranks' slots are
+        # zeros), the shared expert on rank 0, the partial combine into the
+        # exchange, summed over the ranks with the residual and normalised
+        first = self.part.experts[0]
         ops.experts_gated_linear(self.normed, mixture.gate, mixture.up, self.route_ids.view(-1),
-                                 self.expert_gated)
-        ops.experts_gated_linear(self.normed, mixture.shared_gate, mixture.shared_up,
-                                 self.shared_ids, self.shared_gated)
+                                 self.expert_gated, first_expert=first)
         ops.experts_linear(self.expert_gated, mixture.down, self.route_ids.view(-1),
-                           self.expert_out)
-        ops.linears(self.shared_gated, [mixture.shared_down], [self.shared_out])
-        ops.moe_combine_norm(self.expert_out, self.route_weights,
-                             SharedExpert(self.shared_out, self.normed, mixture.shared_router),
-                             self.x, RowNorm(following, c.epsilon, 0.0, self.normed))
+                           self.expert_out, first_expert=first)
+        shared = None
+        if self.part.rank == 0:
+            ops.experts_gated_linear(self.normed, mixture.shared_gate, mixture.shared_up,
+                                     self.shared_ids, self.shared_gated)
+            ops.linears(self.shared_gated, [mixture.shared_down], [self.shared_out])
+            shared = SharedExpert(self.shared_out, self.normed, mixture.shared_router)
+        ops.moe_combine(self.expert_out, self.route_weights, shared, None, self.exchange.slots[1])
+        self.exchange.add_rms_norm(1, self.x, next_norm)
 
     def step(self) -> torch.Tensor:
         """One decode step: self.ids at self.positions -> self.logits."""
@@ -316,8 +450,11 @@ class HybridDecoder:
                 self._full(layer.mixer, index)
             else:
                 self._delta(layer.mixer, index)
-            ops.add_rms_norm(self.x, self.block_out,
-                             RowNorm(layer.post_norm, c.epsilon, 0.0, self.normed))
+            post = RowNorm(layer.post_norm, c.epsilon, 0.0, self.normed)
+            if self.exchange is not None:
+                self.exchange.add_rms_norm(0, self.x, post)
+            else:
+                ops.add_rms_norm(self.x, self.block_out, post)
             following = (w.layers[index + 1].input_norm if index + 1 < len(w.layers)
                          else w.final_norm)
             self._mixture(layer.mixture, following)
@@ -327,9 +464,10 @@ class HybridDecoder:
     def reserve(self) -> None:
         c, lib = self.config, self.ops.lib
         from ._lib import check
-        widest = max(c.hidden, self.value_width, c.q_heads * c.head_dim, c.shared_ffn, c.expert_ffn)
+        widest = max(c.hidden, self.value_width, self.q_heads * c.head_dim, c.shared_ffn,
+                     c.expert_ffn)
         self.ops.reserve_workspace(self.batch * c.used, widest)
-        need = max(lib.drift_attention_workspace_bytes(self.batch, c.q_heads, c.head_dim,
+        need = max(lib.drift_attention_workspace_bytes(self.batch, self.q_heads, c.head_dim,
                                                        self.context),
                    lib.drift_linear_workspace_bytes(self.batch * c.used, widest))
         check("drift_workspace_reserve", lib.drift_workspace_reserve(need))
@@ -359,4 +497,9 @@ class HybridDecoder:
         self.graph.replay()
 
     def release(self) -> None:
+        """Drops the graph and the exchange's buffers."""
         self.graph = None
+        if self.exchange is not None:
+            torch.cuda.synchronize()
+            self.exchange.close()
+            self.exchange = None

@@ -570,24 +570,39 @@ class CudaOps:
                  f"expertsLinear: out {list(out.shape)}, expected [{slots}, {n}]")
         return slots, n, k, rows
 
-    def experts_linear(self, x, weight: Stored, ids, out) -> None:
+    def experts_linear(self, x, weight: Stored, ids, out, first_expert: Optional[int] = None) -> None:
         """Slot s: expert ids[s] of weight [experts, N, K] times x row
-        s / (slots / rows of x) (ExpertsOps.scala:122-126)."""
+        s / (slots / rows of x) (ExpertsOps.scala:122-126). `first_expert`:
+        the weight holds the model's experts from there on (expert
+        parallelism); other ranks' slots get zeros."""
         slots, n, k, rows = self._check_experts(x, weight, ids, out)
-        status = self.lib.drift_experts_linear(
-            _x_dtype("expertsLinear", x), _ptr(x), rows, weight.dtype, _ptr(weight.data),
-            weight.shape[0], n, k, _ptr(ids), slots, _ptr(out), self._stream())
+        if first_expert is None:
+            status = self.lib.drift_experts_linear(
+                _x_dtype("expertsLinear", x), _ptr(x), rows, weight.dtype, _ptr(weight.data),
+                weight.shape[0], n, k, _ptr(ids), slots, _ptr(out), self._stream())
+        else:
+            status = self.lib.drift_experts_linear_local(
+                _x_dtype("expertsLinear", x), _ptr(x), rows, weight.dtype, _ptr(weight.data),
+                weight.shape[0], first_expert, n, k, _ptr(ids), slots, _ptr(out), self._stream())
         check("drift_experts_linear", status)
 
-    def experts_gated_linear(self, x, gate: Stored, up: Stored, ids, out) -> None:
-        """silu(gate · x) × (up · x) per slot, one launch (ExpertsOps.scala:188-198)."""
+    def experts_gated_linear(self, x, gate: Stored, up: Stored, ids, out,
+                             first_expert: Optional[int] = None) -> None:
+        """silu(gate · x) × (up · x) per slot, one launch (ExpertsOps.scala:188-198);
+        `first_expert` as for experts_linear."""
         _require(tuple(gate.shape) == tuple(up.shape) and gate.dtype == up.dtype,
                  f"expertsGatedLinear needs equal shapes, got {list(gate.shape)}, "
                  f"{list(up.shape)}")
         slots, n, k, rows = self._check_experts(x, gate, ids, out)
-        status = self.lib.drift_experts_gated_linear(
-            _x_dtype("expertsGatedLinear", x), _ptr(x), rows, gate.dtype, _ptr(gate.data),
-            _ptr(up.data), gate.shape[0], n, k, _ptr(ids), slots, _ptr(out), self._stream())
+        if first_expert is None:
+            status = self.lib.drift_experts_gated_linear(
+                _x_dtype("expertsGatedLinear", x), _ptr(x), rows, gate.dtype, _ptr(gate.data),
+                _ptr(up.data), gate.shape[0], n, k, _ptr(ids), slots, _ptr(out), self._stream())
+        else:
+            status = self.lib.drift_experts_gated_linear_local(
+                _x_dtype("expertsGatedLinear", x), _ptr(x), rows, gate.dtype, _ptr(gate.data),
+                _ptr(up.data), gate.shape[0], first_expert, n, k, _ptr(ids), slots, _ptr(out),
+                self._stream())
         check("drift_experts_gated_linear", status)
 
     @staticmethod

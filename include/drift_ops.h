@@ -230,6 +230,20 @@ int drift_gated_rms_norm(const float* x, const float* weight, const float* gate,
                          float epsilon, float* out, int64_t rows, int64_t cols, int heads,
                          void* prepared, drift_stream_t stream);
 
+/* Expert parallelism (new): a rank's weight holds experts [first_expert,
+ * first_expert + experts) of the model's; `ids` are the model's; a slot whose
+ * expert is another rank's gets a row of zeros (drift_experts_linear and
+ * drift_experts_gated_linear flag such a slot as an error instead). */
+int drift_experts_linear_local(int x_dtype, const void* x, int64_t x_rows, int weight_dtype,
+                               const void* weight, int64_t experts, int64_t first_expert,
+                               int64_t n, int64_t k, const int32_t* ids, int64_t slots,
+                               float* out, drift_stream_t stream);
+int drift_experts_gated_linear_local(int x_dtype, const void* x, int64_t x_rows, int weight_dtype,
+                                     const void* gate, const void* up, int64_t experts,
+                                     int64_t first_expert, int64_t n, int64_t k,
+                                     const int32_t* ids, int64_t slots, float* out,
+                                     drift_stream_t stream);
+
 /* ---- prepared x (new) ------------------------------------------------------
  * A product streams its weights against x's "records" (x per 32-value block as
  * exact 24-bit integer planes and a scale). drift_linear writes them itself; a

@@ -3,7 +3,9 @@ drift_add_rms_norm_allreduce) on two GPUs, one process each: the fused
 exchange + residual add + RMSNorm equals the sum in rank order followed by
 addRmsNorm, bit for bit; and a two-rank decode step over the peer exchange
 equals the same step over NCCL's all-reduce (for two ranks both sums are
-p0 + p1). Skipped with fewer than two GPUs."""
+p0 + p1); and the expert-parallel hybrid MoE step (DeltaNet and query heads,
+experts and vocabulary split over two ranks) equals the whole model's step on
+one GPU within the benchmark's bar. Skipped with fewer than two GPUs."""
 
 import os
 import socket
@@ -108,3 +110,57 @@ def test_exchange_sums_in_rank_order_then_norms():
 @needs_two
 def test_decode_step_over_peer_memory_equals_nccl():
     torch.multiprocessing.spawn(_decode_ranks, args=(2, free_port()), nprocs=2, join=True)
+
+
+def _hybrid_ranks(rank: int, world: int, port: int):
+    dist = _init(rank, world, port)
+    from drift_b200.hybrid import HybridConfig, HybridDecoder, HybridWeights
+    from drift_b200.ops import CudaOps
+    try:
+        ops = CudaOps()
+        c = HybridConfig(layers=4, hidden=256, delta_key_heads=2, delta_value_heads=4,
+                         delta_dim=32, q_heads=4, kv_heads=2, head_dim=64, rotary=16, theta=1e6,
+                         experts=16, used=4, expert_ffn=64, shared_ffn=64, vocab=500)
+        full = HybridWeights.random(c, seed=5)          # the same on every rank
+        whole = HybridDecoder(ops, c, full, batch=2, context=64)
+        whole.prefill_random(25)
+        part = full.shard(c, rank, world)
+        split = HybridDecoder(ops, c, part, batch=2, context=64, group=dist.group.WORLD)
+        p = part.part
+        # the same caches and states, sliced to this rank's heads and channels
+        d = c.delta_dim
+        keys = c.delta_key_heads * d
+        ranges = [(p.delta_key_heads[0] * d, p.delta_key_heads[1] * d),
+                  (keys + p.delta_key_heads[0] * d, keys + p.delta_key_heads[1] * d),
+                  (2 * keys + p.delta_value_heads[0] * d, 2 * keys + p.delta_value_heads[1] * d)]
+        for i, cache in split.caches.items():
+            k0, k1 = p.kv_heads
+            cache.keys.copy_(whole.caches[i].keys[:, :, k0:k1])
+            cache.values.copy_(whole.caches[i].values[:, k0:k1])
+        for i, state in split.delta_states.items():
+            state.copy_(whole.delta_states[i][:, p.delta_value_heads[0]:p.delta_value_heads[1]])
+        for i, state in split.conv_states.items():
+            state.copy_(torch.cat([whole.conv_states[i][:, :, lo:hi] for lo, hi in ranges], dim=2))
+        for decoder in (whole, split):
+            decoder.ids.copy_(torch.tensor([7, 11], dtype=torch.int32))
+            decoder.positions.copy_(torch.tensor([25, 19], dtype=torch.int32))
+        expected = whole.step()[:, p.vocab[0]:p.vocab[1]].clone()
+        got = split.step().clone()
+        torch.cuda.synchronize()
+        bound = 1e-4 + 1e-3 * expected.abs()
+        assert ((got - expected).abs() <= bound).all(), float((got - expected).abs().max())
+        # the recurrent state moved as the whole model's did
+        for i, state in split.delta_states.items():
+            want = whole.delta_states[i][:, p.delta_value_heads[0]:p.delta_value_heads[1]]
+            assert ((state - want).abs() <= 1e-4 + 1e-3 * want.abs()).all()
+        split.capture()
+        split.release()
+        assert ops.take_device_error() == 0
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@needs_two
+def test_expert_parallel_hybrid_step_equals_the_whole_model():
+    torch.multiprocessing.spawn(_hybrid_ranks, args=(2, free_port()), nprocs=2, join=True)
