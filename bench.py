@@ -43,7 +43,7 @@ sys.path.insert(0, ROOT)
 
 SHAPES = [(4096, 4096), (12288, 4096), (4096, 12288), (151936, 4096)]
 BATCHES = [1, 8, 64]
-Q4_1 = 3
+Q4_1, Q8_0 = 3, 8  # GGML type ids
 METRIC = "quant matvec HBM GB/s (% of 8 TB/s); decode tok/s at 1/2/4/8 B200"
 NOMINAL_HBM_GBS = 8000.0
 
@@ -258,6 +258,9 @@ def run_gpu(args) -> dict | None:
     sweep = sweep_table(ops, weights, xs, ys, stream) if rank == 0 else None
     del weights, xs, ys, host_x, host_y
     torch.cuda.empty_cache()
+    # benchmark configs C1 (the Q8_0 product) and C3 (the layer ops), rank 0
+    configs = (measure_c1_c3(ops, stream, args.cpu_baseline)
+               if rank == 0 and args.decode else None)
 
     # benchmark config C4: the dense decoder's decode step, tensor-parallel over the
     # job's GPUs (one NCCL group), tok/s at each batch
@@ -321,6 +324,7 @@ def run_gpu(args) -> dict | None:
         "sweep": sweep,
         "decode": decode,
         "decode_hybrid": hybrid,
+        "c1_c3": configs,
     }
     if args.cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(seconds=args.cpu_seconds)
@@ -442,6 +446,92 @@ def run_hybrid(args, ops, rank: int, world: int, stream) -> dict:
         del decoder
         torch.cuda.empty_cache()
     del weights
+    torch.cuda.empty_cache()
+    return out
+
+
+def measure_c1_c3(ops, stream, cpu: bool) -> dict:
+    """C1: the Q8_0 4096 x 4096 product at batch 1 (F32 x; GPU, and the CPU
+    oracle on one host thread). C3: the layer ops at batches 1, 8, 16 and 64
+    -- RMSNorm of [b, 4096] (with the residual add), SwiGLU of [b, 12288],
+    RoPE of q [b, 32, 128] and k [b, 8, 128] (theta 1e6, positions in 0..8191),
+    the Q8_0 embedding gather from a 151936 x 4096 table -- each timed as a
+    replayed graph of 20 calls, GB/s = the benchmark's algorithmic bytes
+    (F32 here: the library's activations are F32) over the time."""
+    import time
+
+    import numpy as np
+    import torch
+
+    from drift_b200 import synthetic
+    from drift_b200.ops import SILU, Rope, RowNorm, Stored
+
+    out = {}
+    g = torch.Generator(device="cuda")
+    g.manual_seed(11)
+    # C1
+    n = k = 4096
+    w = Stored(Q8_0, (n, k), synthetic.quantized_device(Q8_0, n, k, g))
+    copies = rotation(w, 4 * L2_BYTES)
+    x = torch.randn(1, k, generator=g, device="cuda")
+    y = torch.empty(1, n, device="cuda")
+
+    def c1():
+        for c in copies:
+            ops.linear(x, c, y)
+    ms = timed_graph(c1, stream, 10) / len(copies)
+    c1_bytes = n * (k // 32) * 34 + 4 * k + 4 * n
+    out["c1"] = {"shape": "4096x4096 Q8_0, b=1", "us": round(ms * 1e3, 2),
+                 "gbs": round(c1_bytes / (ms / 1e3) / 1e9, 1)}
+    if cpu:
+        import oracle
+        rng = np.random.default_rng(0)
+        wh = synthetic.quantized(rng, Q8_0, n, k)
+        xh = rng.standard_normal((1, k)).astype(np.float32)
+        start, runs = time.perf_counter(), 0
+        while time.perf_counter() - start < 5.0:
+            oracle.linear(Q8_0, xh, wh, n, k)
+            runs += 1
+        elapsed = time.perf_counter() - start
+        out["c1"]["cpu_oracle_gbs_1_thread"] = round(c1_bytes * runs / elapsed / 1e9, 3)
+    del copies, w
+    # C3
+    table = Stored(Q8_0, (151936, 4096), synthetic.quantized_device(Q8_0, 151936, 4096, g))
+    hidden, ffn = 4096, 12288
+    weight = 1 + 0.02 * torch.randn(hidden, generator=g, device="cuda")
+    rope = Rope(1e6, 128)
+    rows = []
+    for b in (1, 8, 16, 64):
+        xs = torch.randn(b, hidden, generator=g, device="cuda")
+        ys = torch.randn(b, hidden, generator=g, device="cuda")
+        normed = torch.empty_like(xs)
+        gate = torch.randn(b, ffn, generator=g, device="cuda")
+        up = torch.randn(b, ffn, generator=g, device="cuda")
+        hid = torch.empty_like(gate)
+        q = torch.randn(b, 32, 128, generator=g, device="cuda")
+        kk = torch.randn(b, 8, 128, generator=g, device="cuda")
+        qo, ko = torch.empty_like(q), torch.empty_like(kk)
+        positions = torch.randint(0, 8192, (b,), generator=g, device="cuda", dtype=torch.int32)
+        ids = torch.randint(0, 151936, (b,), generator=g, device="cuda", dtype=torch.int32)
+        gathered = torch.empty(b, hidden, device="cuda")
+        cases = {
+            "add_rms_norm": (lambda: ops.add_rms_norm(xs, ys, RowNorm(weight, 1e-6, 0.0, normed)),
+                             3 * b * hidden * 4 + hidden * 4),
+            "swiglu": (lambda: ops.gated(SILU, gate, up, hid), 3 * b * ffn * 4),
+            "rope_q_k": (lambda: (ops.rope(q, positions, rope, qo), ops.rope(kk, positions, rope, ko)),
+                         2 * b * 40 * 128 * 4),
+            "embedding_q8_0": (lambda: ops.embedding(table, ids, gathered),
+                               b * 4352 + b * hidden * 4),
+        }
+        for name, (fn, nbytes) in cases.items():
+            def repeat(fn=fn):
+                for _ in range(20):
+                    fn()
+            ms = timed_graph(repeat, stream, 10) / 20
+            rows.append({"op": name, "batch": b, "us": round(ms * 1e3, 2),
+                         "gbs": round(nbytes / (ms / 1e3) / 1e9, 1)})
+    out["c3"] = rows
+    del table
     torch.cuda.empty_cache()
     return out
 
