@@ -12,8 +12,9 @@
 // copies, forms scores and weighted values with mma.sync on F16 operands
 // (q and the weights as two F16 terms each, so the sums are F32-grade), and
 // leaves, per query head, the largest score, the sum of exp(score - largest)
-// and the unnormalised weighted sum. A second kernel joins the splits (and
-// the sink, if any) per query head. Scores and sums in F32 (the CPU
+// and the unnormalised weighted sum. The last split of each (row, key head)
+// to finish joins the splits (and the sink, if any) for its query heads --
+// or, past 256 splits, a second kernel does. Scores and sums in F32 (the CPU
 // reference accumulates in Double; the 1e-4 + 1e-3 |e| tolerance applies).
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -132,7 +133,20 @@ struct AttentionArgs {
   float scale;
   int causal, window, has_softcap;
   float softcap;
+  // the join, when the last split of each (row, key head) does it
+  int fused_join;
+  const float* sinks;
+  float* out;
+  uint8_t* records;
+  const float* gate;
+  int gate_stride;
 };
+
+// Splits arrived per (row, key head) of a launch whose last split joins;
+// zero between launches (the joining CTA clears its entry).
+constexpr int MAX_JOINS = 1 << 16;
+constexpr int MAX_FUSED_SPLITS = 256;
+__device__ unsigned join_arrivals[MAX_JOINS];
 
 // Row z's page table, key count and query position.
 struct Query {
@@ -161,6 +175,66 @@ __device__ __forceinline__ void visible(const AttentionArgs& a, const Query& que
   if (a.causal && query.position + 1 < hi) hi = query.position + 1;
   lo = 0;
   if (a.window > 0 && query.position - a.window + 1 > lo) lo = query.position - a.window + 1;
+}
+
+// Joins a query head's splits: out = sum_s o_s e^(m_s - M) / (sum_s l_s
+// e^(m_s - M) + e^(sink - M)), M the largest of the m_s and the sink.
+// With `records` (D a multiple of 32), also the x records of the output rows
+// for the product that follows (the o projection): warp w's 32 dimensions
+// are one block of the row. With `gate`, the gated attention's output gate:
+// value x sigmoid(gate) (the runner's gated(Sigmoid, gate, attended),
+// models/HybridBlocks.scala). Called by every thread of the CTA; the
+// partials are read at L2 (other CTAs of the same launch may have written
+// them).
+template <int D, int THREADS>
+__device__ void join_head(const AttentionArgs& a, const float* sinks, float* out,
+                          uint8_t* records, const float* gate, int gate_stride, int head, int t,
+                          float* factor, float* shared_total) {
+  const long long base = ((long long)t * a.q_heads + head) * a.splits;
+  if (threadIdx.x < 32) {
+    float largest = -INFINITY;
+    for (int s = threadIdx.x; s < a.splits; s += 32)
+      if (__ldcg(a.part_ml + (base + s) * 2 + 1) > 0.0f)
+        largest = fmaxf(largest, __ldcg(a.part_ml + (base + s) * 2));
+#pragma unroll
+    for (int o = 16; o > 0; o /= 2) largest = fmaxf(largest, __shfl_xor_sync(0xffffffffu, largest, o));
+    if (sinks) largest = fmaxf(largest, sinks[head]);
+    float total = 0.0f;
+    for (int s = threadIdx.x; s < a.splits; s += 32) {
+      const float l = __ldcg(a.part_ml + (base + s) * 2 + 1);
+      const float f = l > 0.0f ? expf(__ldcg(a.part_ml + (base + s) * 2) - largest) : 0.0f;
+      factor[s] = f;
+      total += l * f;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o /= 2) total += __shfl_xor_sync(0xffffffffu, total, o);
+    if (threadIdx.x == 0) *shared_total = total + (sinks ? expf(sinks[head] - largest) : 0.0f);
+  }
+  __syncthreads();
+  const float total = *shared_total;
+  for (int d = threadIdx.x; d < D; d += THREADS) {
+    // eight splits' loads in flight at a time, summed in split order
+    float sum = 0.0f;
+    for (int s0 = 0; s0 < a.splits; s0 += 8) {
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        o[j] = s0 + j < a.splits ? __ldcg(a.part_o + (base + s0 + j) * D + d) : 0.0f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (s0 + j < a.splits && factor[s0 + j] > 0.0f) sum += o[j] * factor[s0 + j];
+    }
+    float value = total > 0.0f ? sum / total : 0.0f;
+    if (gate) {
+      const float g = gate[((long long)t * a.q_heads + head) * gate_stride + d];
+      value = (1.0f / (1.0f + expf(-g))) * value;
+    }
+    out[((long long)t * a.q_heads + head) * D + d] = value;
+    if constexpr (D % 32 == 0) {
+      if (records) x22_record_block(value, records, t, (head * D + d) / 32, a.q_heads * D / 32);
+    }
+  }
+  __syncthreads();  // factor and the total are reused for the next head
 }
 
 // A split's tile: KEYS keys of one key head against the (up to 16) query
@@ -467,13 +541,26 @@ __global__ void __launch_bounds__(SPLIT_THREADS) attention_split_kernel(const At
     a.part_ml[(at0 + (long long)tid * a.splits) * 2] = largest;
     a.part_ml[(at0 + (long long)tid * a.splits) * 2 + 1] = total;
   }
+  if (!a.fused_join) return;
+  // the last split of this (row, key head) to finish joins its query heads
+  __shared__ int joins;
+  __shared__ float factor[MAX_FUSED_SPLITS];
+  __shared__ float shared_total;
+  __syncthreads();
+  unsigned* arrivals = join_arrivals + (long long)z * a.kv_heads + head;
+  if (tid == 0) {
+    __threadfence();
+    joins = atomicAdd(arrivals, 1u) == unsigned(a.splits - 1);
+    if (joins) __threadfence();
+  }
+  __syncthreads();
+  if (!joins) return;
+  for (int q = 0; q < group; ++q)
+    join_head<D, SPLIT_THREADS>(a, a.sinks, a.out, a.records, a.gate, a.gate_stride,
+                                head * group + q, z, factor, &shared_total);
+  if (tid == 0) *arrivals = 0;
 }
 
-// Joins a query head's splits: out = sum_s o_s e^(m_s - M) / (sum_s l_s
-// e^(m_s - M) + e^(sink - M)), M the largest of the m_s and the sink.
-// With `records` (D a multiple of 32), also the x records of the output rows
-// for the product that follows (the o projection): warp w's 32 dimensions
-// are one block of the row.
 template <int D>
 __global__ void __launch_bounds__(ATT_THREADS) attention_join_kernel(const AttentionArgs a,
                                                                      const float* sinks,
@@ -485,52 +572,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_join_kernel(const Atten
   pdl_wait();     // what the kernels before this one wrote is visible
   extern __shared__ float factor[];  // [splits]: e^(m_s - M), 0 for an empty split
   __shared__ float shared_total;
-  const int head = blockIdx.x, t = blockIdx.y;
-  const long long base = ((long long)t * a.q_heads + head) * a.splits;
-  if (threadIdx.x < 32) {
-    float largest = -INFINITY;
-    for (int s = threadIdx.x; s < a.splits; s += 32)
-      if (a.part_ml[(base + s) * 2 + 1] > 0.0f) largest = fmaxf(largest, a.part_ml[(base + s) * 2]);
-#pragma unroll
-    for (int o = 16; o > 0; o /= 2) largest = fmaxf(largest, __shfl_xor_sync(0xffffffffu, largest, o));
-    if (sinks) largest = fmaxf(largest, sinks[head]);
-    float total = 0.0f;
-    for (int s = threadIdx.x; s < a.splits; s += 32) {
-      const float l = a.part_ml[(base + s) * 2 + 1];
-      const float f = l > 0.0f ? expf(a.part_ml[(base + s) * 2] - largest) : 0.0f;
-      factor[s] = f;
-      total += l * f;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o /= 2) total += __shfl_xor_sync(0xffffffffu, total, o);
-    if (threadIdx.x == 0) shared_total = total + (sinks ? expf(sinks[head] - largest) : 0.0f);
-  }
-  __syncthreads();
-  const float total = shared_total;
-  for (int d = threadIdx.x; d < D; d += ATT_THREADS) {
-    // eight splits' loads in flight at a time, summed in split order
-    float sum = 0.0f;
-    for (int s0 = 0; s0 < a.splits; s0 += 8) {
-      float o[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        o[j] = s0 + j < a.splits ? a.part_o[(base + s0 + j) * D + d] : 0.0f;
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (s0 + j < a.splits && factor[s0 + j] > 0.0f) sum += o[j] * factor[s0 + j];
-    }
-    float value = total > 0.0f ? sum / total : 0.0f;
-    if (gate) {
-      // the gated attention's output gate: value x sigmoid(gate) (the
-      // runner's gated(Sigmoid, gate, attended), models/HybridBlocks.scala)
-      const float g = gate[((long long)t * a.q_heads + head) * gate_stride + d];
-      value = (1.0f / (1.0f + expf(-g))) * value;
-    }
-    out[((long long)t * a.q_heads + head) * D + d] = value;
-    if constexpr (D % 32 == 0) {
-      if (records) x22_record_block(value, records, t, (head * D + d) / 32, a.q_heads * D / 32);
-    }
-  }
+  join_head<D, ATT_THREADS>(a, sinks, out, records, gate, gate_stride, blockIdx.x, blockIdx.y,
+                            factor, &shared_total);
 }
 
 #define DRIFT_ATTENTION_REGISTER(D)                                                   \
@@ -557,11 +600,22 @@ int launch_attention(const AttentionArgs& a, const float* sinks, float* out, cud
                                     cudaFuncAttributePreferredSharedMemoryCarveout, 100));
     configured = true;
   }
+  // the join in the last split of each (row, key head) when its factors fit
+  // in shared memory and the arrival counts in their array; else its own
+  // launch
+  AttentionArgs args = a;
+  args.fused_join = a.splits <= MAX_FUSED_SPLITS && (long long)a.tokens * a.kv_heads <= MAX_JOINS;
+  args.sinks = sinks;
+  args.out = out;
+  args.records = records;
+  args.gate = gate;
+  args.gate_stride = gate_stride;
   DRIFT_CUDA(launch_pdl(attention_split_kernel<D>, dim3(a.splits, a.kv_heads, a.tokens),
-                        SPLIT_THREADS, SplitTile<D>::BYTES, stream, a));
+                        SPLIT_THREADS, SplitTile<D>::BYTES, stream, args));
   DRIFT_LAUNCHED("attention_split");
+  if (args.fused_join) return 0;
   DRIFT_CUDA(launch_pdl(attention_join_kernel<D>, dim3(a.q_heads, a.tokens), ATT_THREADS,
-                        a.splits * sizeof(float), stream, a, sinks, out, records, gate,
+                        a.splits * sizeof(float), stream, args, sinks, out, records, gate,
                         gate_stride));
   DRIFT_LAUNCHED("attention_join");
   return 0;
