@@ -309,6 +309,89 @@ __device__ __forceinline__ void split_pair(float x0, float x1, uint32_t& hi, uin
 // the 8 warps takes an eighth of the dimensions of p.v over all of the
 // split's keys. Positions outside the visible range are never read from the
 // cache: their scores are -inf and their value columns zeros.
+// The join of one (row, key head)'s query heads by the split CTA that
+// finished last, its threads side by side: warp w takes the factors of heads
+// w, w + 8; then each thread sums (head, two dimensions) pairs over the
+// splits with sixteen splits' loads in flight; then, with `records`, the x
+// records from the values in shared memory. Per output it is join_head's
+// arithmetic in join_head's order, so the two give the same bits. `smem`:
+// the split's tile, whose keys and values are no longer read.
+template <int D>
+__device__ void join_group(const AttentionArgs& a, int z, int kv_head, int group, uint8_t* smem) {
+  float* factor = reinterpret_cast<float*>(smem);        // [group][splits]
+  float* total = factor + MAX_GROUP * MAX_FUSED_SPLITS;  // [group]
+  float* value = total + MAX_GROUP;                      // [group][D]
+  const int S = a.splits;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const float2* ml = reinterpret_cast<const float2*>(a.part_ml);
+  for (int q = warp; q < group; q += SPLIT_THREADS / 32) {
+    const int head = kv_head * group + q;
+    const long long base = ((long long)z * a.q_heads + head) * S;
+    float largest = -INFINITY;
+    for (int s = lane; s < S; s += 32) {
+      const float2 v = __ldcg(ml + base + s);
+      if (v.y > 0.0f) largest = fmaxf(largest, v.x);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o /= 2) largest = fmaxf(largest, __shfl_xor_sync(0xffffffffu, largest, o));
+    if (a.sinks) largest = fmaxf(largest, a.sinks[head]);
+    float sum = 0.0f;
+    for (int s = lane; s < S; s += 32) {
+      const float2 v = __ldcg(ml + base + s);
+      const float f = v.y > 0.0f ? expf(v.x - largest) : 0.0f;
+      factor[q * S + s] = f;
+      sum += v.y * f;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o /= 2) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) total[q] = sum + (a.sinks ? expf(a.sinks[head] - largest) : 0.0f);
+  }
+  __syncthreads();
+  constexpr int HALF = D / 2;
+  for (int p = threadIdx.x; p < group * HALF; p += SPLIT_THREADS) {
+    const int q = p / HALF, d = 2 * (p % HALF);
+    const int head = kv_head * group + q;
+    const long long base = ((long long)z * a.q_heads + head) * S;
+    const float* f = factor + q * S;
+    float sum0 = 0.0f, sum1 = 0.0f;
+    for (int s0 = 0; s0 < S; s0 += 16) {
+      float2 o[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        o[j] = s0 + j < S ? __ldcg(reinterpret_cast<const float2*>(a.part_o + (base + s0 + j) * D + d))
+                          : make_float2(0.0f, 0.0f);
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (s0 + j < S && f[s0 + j] > 0.0f) {
+          sum0 += o[j].x * f[s0 + j];
+          sum1 += o[j].y * f[s0 + j];
+        }
+    }
+    const float t = total[q];
+    float v0 = t > 0.0f ? sum0 / t : 0.0f, v1 = t > 0.0f ? sum1 / t : 0.0f;
+    const long long at = ((long long)z * a.q_heads + head) * D + d;
+    if (a.gate) {
+      const float* g = a.gate + ((long long)z * a.q_heads + head) * a.gate_stride + d;
+      v0 = (1.0f / (1.0f + expf(-g[0]))) * v0;
+      v1 = (1.0f / (1.0f + expf(-g[1]))) * v1;
+    }
+    a.out[at] = v0;
+    a.out[at + 1] = v1;
+    value[q * D + d] = v0;
+    value[q * D + d + 1] = v1;
+  }
+  if constexpr (D % 32 == 0) {
+    if (a.records) {
+      __syncthreads();
+      // whole warps: group x D and the stride are multiples of 32
+      for (int i = threadIdx.x; i < group * D; i += SPLIT_THREADS) {
+        const int head = kv_head * group + i / D, d = i % D;
+        x22_record_block(value[i], a.records, z, (head * D + d) / 32, a.q_heads * D / 32);
+      }
+    }
+  }
+}
+
 template <int D>
 __global__ void __launch_bounds__(SPLIT_THREADS) attention_split_kernel(const AttentionArgs a) {
   pdl_trigger();  // the next kernel may launch and wait for this one
@@ -543,10 +626,10 @@ __global__ void __launch_bounds__(SPLIT_THREADS) attention_split_kernel(const At
   }
   if (!a.fused_join) return;
   // the last split of this (row, key head) to finish joins its query heads
+  static_assert(T::BYTES >= 4 * (MAX_GROUP * MAX_FUSED_SPLITS + MAX_GROUP + MAX_GROUP * D),
+                "the join's factors and values fit in the tile");
   __shared__ int joins;
-  __shared__ float factor[MAX_FUSED_SPLITS];
-  __shared__ float shared_total;
-  __syncthreads();
+  __syncthreads();  // (every warp is done with the tile)
   unsigned* arrivals = join_arrivals + (long long)z * a.kv_heads + head;
   if (tid == 0) {
     __threadfence();
@@ -555,9 +638,7 @@ __global__ void __launch_bounds__(SPLIT_THREADS) attention_split_kernel(const At
   }
   __syncthreads();
   if (!joins) return;
-  for (int q = 0; q < group; ++q)
-    join_head<D, SPLIT_THREADS>(a, a.sinks, a.out, a.records, a.gate, a.gate_stride,
-                                head * group + q, z, factor, &shared_total);
+  join_group<D>(a, z, head, group, tile);
   if (tid == 0) *arrivals = 0;
 }
 
