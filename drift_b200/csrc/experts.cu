@@ -10,6 +10,7 @@
 #include <cuda_runtime.h>
 
 #include "common.cuh"
+#include "mma_i8.cuh"
 #include "quant.cuh"
 #include "registry.cuh"
 #include "rowwise.cuh"
@@ -18,9 +19,9 @@ namespace drift {
 
 int* device_error_word();
 int workspace_reserve(size_t bytes, void** pointer);
-size_t linear_workspace_bytes(int64_t m, int64_t k);
-int prepare_x(int x_dtype, const void* x, int64_t m, int64_t k, uint32_t* records,
-              cudaStream_t stream);
+size_t mma_workspace_bytes(int64_t m, int64_t k);
+int prepare_x_mma(int x_dtype, const void* x, int64_t m, int64_t k, uint8_t* records,
+                  cudaStream_t stream);
 
 // ---- routing ----------------------------------------------------------------------------
 // One warp per token: the k largest of `experts` <= 512 logits, the lower
@@ -101,14 +102,16 @@ DRIFT_REGISTER(route_topk, route_kernel)
 
 // ---- experts' products ---------------------------------------------------------------------
 // Slot s (blockIdx.y) multiplies expert ids[s] of a [experts][rows][cols]
-// weight with x row s / divisor, prepared as for the plain product. The
+// weight with x row s / divisor, prepared as for the plain product (the
+// tensor-core layout: row v's part of block c is the 112-byte slot v % 8 of
+// record (v / 8, c), its plane words in the order 0, 4, 1, 5, 2, 6, 3, 7). The
 // warps of a CTA split rows and blocks as matvec_x22_kernel does. GATED: a
 // gate and an up weight of the same shape, out = silu(gate . x) * (up . x).
 // Each warp: rows of its group, k-split kw; 8 warps = (8 / KS) row groups.
 template <typename T, int KS, bool GATED>
 __global__ void __launch_bounds__(256) experts_x22_kernel(
     const uint8_t* __restrict__ gate, const uint8_t* __restrict__ up, long long expert_bytes,
-    const int* __restrict__ ids, const uint32_t* __restrict__ records, int divisor,
+    const int* __restrict__ ids, const uint8_t* __restrict__ records, int divisor,
     float* __restrict__ y, int rows, int cols, long long experts, long long first_expert,
     int others_zero, int* error) {
   pdl_trigger();  // the next kernel may launch and wait for this one
@@ -125,7 +128,9 @@ __global__ void __launch_bounds__(256) experts_x22_kernel(
   const long long expert = ids[slot] - first_expert;
   const int row0 = (blockIdx.x * GROUPS + group) * ROWS;
   const int blocks = cols / 32;
-  const uint32_t* record = records + (long long)(slot / divisor) * blocks * X_RECORD_WORDS;
+  const int v = slot / divisor;
+  const uint8_t* record =
+      records + (long long)(v / 8) * blocks * MMA_RECORD_BYTES + MMA_SLOT_BYTES * (v % 8);
   if (expert < 0 || expert >= experts) {
     if (!others_zero && threadIdx.x == 0 && blockIdx.x == 0 && error) atomicCAS(error, 0, 1);
     for (int r = threadIdx.x; r < GROUPS * ROWS; r += blockDim.x) {
@@ -151,17 +156,22 @@ __global__ void __launch_bounds__(256) experts_x22_kernel(
       load_block<T>(gate_base + row * row_bytes, c, wg[r]);
       if (GATED) load_block<T>(up_base + row * row_bytes, c, wu[r]);
     }
-    const uint4* rec = reinterpret_cast<const uint4*>(record + (long long)c * X_RECORD_WORDS);
+    const uint4* rec = reinterpret_cast<const uint4*>(record + (long long)c * MMA_RECORD_BYTES);
+    // stored words 0..7 of a plane hold words 0, 4, 1, 5, 2, 6, 3, 7
     uint32_t planes[24];
 #pragma unroll
-    for (int i = 0; i < 6; ++i) {
-      const uint4 q = __ldg(rec + i);
-      planes[4 * i] = q.x;
-      planes[4 * i + 1] = q.y;
-      planes[4 * i + 2] = q.z;
-      planes[4 * i + 3] = q.w;
+    for (int p = 0; p < 3; ++p) {
+      const uint4 q0 = __ldg(rec + 2 * p), q1 = __ldg(rec + 2 * p + 1);
+      planes[8 * p + 0] = q0.x;
+      planes[8 * p + 4] = q0.y;
+      planes[8 * p + 1] = q0.z;
+      planes[8 * p + 5] = q0.w;
+      planes[8 * p + 2] = q1.x;
+      planes[8 * p + 6] = q1.y;
+      planes[8 * p + 3] = q1.z;
+      planes[8 * p + 7] = q1.w;
     }
-    const uint4 tail = __ldg(rec + 6);
+    const uint4 tail = __ldg(rec + 6);  // s, sum X at bytes 96, 100
 #pragma unroll
     for (int r = 0; r < ROWS; ++r) {
       int a0, a1, a2;
@@ -220,7 +230,7 @@ DRIFT_EXPERTS_REGISTER(Q4_1T, q4_1)
 
 template <typename T, bool GATED>
 static int launch_experts(const uint8_t* gate, const uint8_t* up, long long expert_bytes,
-                          const int* ids, const uint32_t* records, int divisor, float* y, int rows,
+                          const int* ids, const uint8_t* records, int divisor, float* y, int rows,
                           int cols, int slots, long long experts, long long first_expert,
                           int others_zero, cudaStream_t stream) {
   const int blocks = cols / 32;
@@ -247,7 +257,8 @@ static int launch_experts(const uint8_t* gate, const uint8_t* up, long long expe
 static int experts_common(bool gated, int x_dtype, const void* x, int64_t x_rows,
                           int weight_dtype, const void* gate, const void* up, int64_t experts,
                           int64_t n, int64_t k, const int32_t* ids, int64_t slots, float* out,
-                          int64_t first_expert, int others_zero, cudaStream_t stream) {
+                          int64_t first_expert, int others_zero, const void* prepared,
+                          cudaStream_t stream) {
   const char* name = gated ? "expertsGatedLinear" : "expertsLinear";
   if (x_dtype != DRIFT_F32 && x_dtype != DRIFT_BF16)
     return invalid("%s takes F32 (or BF16) x, not %s", name, dtype_name(x_dtype));
@@ -265,10 +276,13 @@ static int experts_common(bool gated, int x_dtype, const void* x, int64_t x_rows
   if (slots == 0) return 0;
   if (!x || !gate || (gated && !up) || !ids || !out) return invalid("%s: a null tensor", name);
   if (slots > 65535) return invalid("%s: %lld slots in one launch", name, (long long)slots);
-  void* w = nullptr;
-  DRIFT_TRY(workspace_reserve(linear_workspace_bytes(x_rows, k), &w));
-  uint32_t* records = static_cast<uint32_t*>(w);
-  DRIFT_TRY(prepare_x(x_dtype, x, x_rows, k, records, stream));
+  const uint8_t* records = static_cast<const uint8_t*>(prepared);
+  if (!records) {
+    void* w = nullptr;
+    DRIFT_TRY(workspace_reserve(mma_workspace_bytes(x_rows, k), &w));
+    DRIFT_TRY(prepare_x_mma(x_dtype, x, x_rows, k, static_cast<uint8_t*>(w), stream));
+    records = static_cast<const uint8_t*>(w);
+  }
   const long long expert_bytes = n * row;
   const int divisor = int(slots / x_rows);
   const uint8_t* g = static_cast<const uint8_t*>(gate);
@@ -431,16 +445,16 @@ int drift_experts_linear(int x_dtype, const void* x, int64_t x_rows, int weight_
                          const void* weight, int64_t experts, int64_t n, int64_t k,
                          const int32_t* ids, int64_t slots, float* out, drift_stream_t stream) {
   return experts_common(false, x_dtype, x, x_rows, weight_dtype, weight, nullptr, experts, n, k,
-                        ids, slots, out, 0, 0, cudaStream_t(stream));
+                        ids, slots, out, 0, 0, nullptr, cudaStream_t(stream));
 }
 
 int drift_experts_linear_local(int x_dtype, const void* x, int64_t x_rows, int weight_dtype,
                                const void* weight, int64_t experts, int64_t first_expert,
                                int64_t n, int64_t k, const int32_t* ids, int64_t slots,
-                               float* out, drift_stream_t stream) {
+                               float* out, const void* prepared, drift_stream_t stream) {
   if (first_expert < 0) return invalid("expertsLinear: experts from %lld", (long long)first_expert);
   return experts_common(false, x_dtype, x, x_rows, weight_dtype, weight, nullptr, experts, n, k,
-                        ids, slots, out, first_expert, 1, cudaStream_t(stream));
+                        ids, slots, out, first_expert, 1, prepared, cudaStream_t(stream));
 }
 
 int drift_experts_gated_linear(int x_dtype, const void* x, int64_t x_rows, int weight_dtype,
@@ -448,17 +462,17 @@ int drift_experts_gated_linear(int x_dtype, const void* x, int64_t x_rows, int w
                                int64_t k, const int32_t* ids, int64_t slots, float* out,
                                drift_stream_t stream) {
   return experts_common(true, x_dtype, x, x_rows, weight_dtype, gate, up, experts, n, k, ids,
-                        slots, out, 0, 0, cudaStream_t(stream));
+                        slots, out, 0, 0, nullptr, cudaStream_t(stream));
 }
 
 int drift_experts_gated_linear_local(int x_dtype, const void* x, int64_t x_rows, int weight_dtype,
                                      const void* gate, const void* up, int64_t experts,
                                      int64_t first_expert, int64_t n, int64_t k,
                                      const int32_t* ids, int64_t slots, float* out,
-                                     drift_stream_t stream) {
+                                     const void* prepared, drift_stream_t stream) {
   if (first_expert < 0) return invalid("expertsGatedLinear: experts from %lld", (long long)first_expert);
   return experts_common(true, x_dtype, x, x_rows, weight_dtype, gate, up, experts, n, k, ids,
-                        slots, out, first_expert, 1, cudaStream_t(stream));
+                        slots, out, first_expert, 1, prepared, cudaStream_t(stream));
 }
 
 int drift_moe_combine(const float* expert_out, const float* weights, int64_t tokens, int64_t k,

@@ -11,9 +11,6 @@
 namespace drift {
 
 int workspace_reserve(size_t bytes, void** pointer);
-size_t linear_workspace_bytes(int64_t m, int64_t k);
-int prepare_x(int x_dtype, const void* x, int64_t m, int64_t k, uint32_t* records,
-              cudaStream_t stream);
 int matvec_prepared(int weight_dtype, const void* weight, const uint8_t* records, float* y,
                     int64_t rows, int64_t cols, int64_t vectors, cudaStream_t stream);
 size_t mma_workspace_bytes(int64_t m, int64_t k);
@@ -76,9 +73,8 @@ static size_t records_region(int64_t m, int64_t k) {
 }
 
 size_t drift_linear_workspace_bytes(int64_t m, int64_t k) {
-  const size_t a = linear_workspace_bytes(m, k);  // the experts' x records
-  const size_t b = records_region(m, k) + (m >= GEMM_MINIMUM_ROWS ? tc_workspace_bytes(m, k) : 0);
-  return a > b ? a : b;
+  // (the experts' products use the records region alone)
+  return records_region(m, k) + (m >= GEMM_MINIMUM_ROWS ? tc_workspace_bytes(m, k) : 0);
 }
 
 int drift_workspace_reserve(size_t bytes) { return workspace_reserve(bytes, nullptr); }

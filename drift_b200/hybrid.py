@@ -407,15 +407,17 @@ class HybridDecoder:
 
     def _mixture(self, mixture: MixtureLayer, following: torch.Tensor) -> None:
         ops, c, P = self.ops, self.config, self.prepared
-        # routing is the same on every rank (the same x, the same router)
+        # routing is the same on every rank (the same x, the same router);
+        # the post norm wrote normed's records into P for the router and the
+        # gate and up products (the weights hold every expert from 0 on)
         ops.route_linear(self.normed, mixture.router, self.logits_router, self.route_ids,
-                         self.route_weights)
+                         self.route_weights, P)
         next_norm = RowNorm(following, c.epsilon, 0.0, self.normed)
         if self.exchange is None:
             ops.experts_gated_linear(self.normed, mixture.gate, mixture.up,
-                                     self.route_ids.view(-1), self.expert_gated)
+                                     self.route_ids.view(-1), self.expert_gated, 0, P)
             ops.experts_gated_linear(self.normed, mixture.shared_gate, mixture.shared_up,
-                                     self.shared_ids, self.shared_gated)
+                                     self.shared_ids, self.shared_gated, 0, P)
             ops.experts_linear(self.expert_gated, mixture.down, self.route_ids.view(-1),
                                self.expert_out)
             ops.linears(self.shared_gated, [mixture.shared_down], [self.shared_out])
@@ -428,13 +430,13 @@ class HybridDecoder:
         # exchange, summed over the ranks with the residual and normalised
         first = self.part.experts[0]
         ops.experts_gated_linear(self.normed, mixture.gate, mixture.up, self.route_ids.view(-1),
-                                 self.expert_gated, first_expert=first)
+                                 self.expert_gated, first_expert=first, prepared=P)
         ops.experts_linear(self.expert_gated, mixture.down, self.route_ids.view(-1),
                            self.expert_out, first_expert=first)
         shared = None
         if self.part.rank == 0:
             ops.experts_gated_linear(self.normed, mixture.shared_gate, mixture.shared_up,
-                                     self.shared_ids, self.shared_gated)
+                                     self.shared_ids, self.shared_gated, 0, P)
             ops.linears(self.shared_gated, [mixture.shared_down], [self.shared_out])
             shared = SharedExpert(self.shared_out, self.normed, mixture.shared_router)
         ops.moe_combine(self.expert_out, self.route_weights, shared, None, self.exchange.slots[1])
@@ -452,9 +454,9 @@ class HybridDecoder:
                 self._delta(layer.mixer, index)
             post = RowNorm(layer.post_norm, c.epsilon, 0.0, self.normed)
             if self.exchange is not None:
-                self.exchange.add_rms_norm(0, self.x, post)
+                self.exchange.add_rms_norm(0, self.x, post, P)
             else:
-                ops.add_rms_norm(self.x, self.block_out, post)
+                ops.add_rms_norm(self.x, self.block_out, post, P)
             following = (w.layers[index + 1].input_norm if index + 1 < len(w.layers)
                          else w.final_norm)
             self._mixture(layer.mixture, following)

@@ -549,9 +549,11 @@ class CudaOps:
                                       self._stream())
         check("drift_route", status)
 
-    def route_linear(self, x, router, logits, ids, weights) -> None:
-        """A router's logits = x · routerᵀ, then route (ExpertsOps.scala:176-186)."""
-        self.linear(x, router, logits)
+    def route_linear(self, x, router, logits, ids, weights,
+                     prepared: Optional[torch.Tensor] = None) -> None:
+        """A router's logits = x · routerᵀ, then route (ExpertsOps.scala:176-186);
+        `prepared` as for linears."""
+        self.linears(x, [router], [logits], prepared)
         self.route(logits, ids, weights)
 
     @staticmethod
@@ -570,12 +572,17 @@ class CudaOps:
                  f"expertsLinear: out {list(out.shape)}, expected [{slots}, {n}]")
         return slots, n, k, rows
 
-    def experts_linear(self, x, weight: Stored, ids, out, first_expert: Optional[int] = None) -> None:
+    def experts_linear(self, x, weight: Stored, ids, out, first_expert: Optional[int] = None,
+                       prepared: Optional[torch.Tensor] = None) -> None:
         """Slot s: expert ids[s] of weight [experts, N, K] times x row
         s / (slots / rows of x) (ExpertsOps.scala:122-126). `first_expert`:
         the weight holds the model's experts from there on (expert
-        parallelism); other ranks' slots get zeros."""
+        parallelism); other ranks' slots get zeros. `prepared` (with
+        `first_expert`): x's records, already written by the kernel that
+        made x."""
         slots, n, k, rows = self._check_experts(x, weight, ids, out)
+        _require(prepared is None or first_expert is not None,
+                 "expertsLinear: a prepared x goes with first_expert")
         if first_expert is None:
             status = self.lib.drift_experts_linear(
                 _x_dtype("expertsLinear", x), _ptr(x), rows, weight.dtype, _ptr(weight.data),
@@ -583,17 +590,21 @@ class CudaOps:
         else:
             status = self.lib.drift_experts_linear_local(
                 _x_dtype("expertsLinear", x), _ptr(x), rows, weight.dtype, _ptr(weight.data),
-                weight.shape[0], first_expert, n, k, _ptr(ids), slots, _ptr(out), self._stream())
+                weight.shape[0], first_expert, n, k, _ptr(ids), slots, _ptr(out),
+                _ptr(prepared), self._stream())
         check("drift_experts_linear", status)
 
     def experts_gated_linear(self, x, gate: Stored, up: Stored, ids, out,
-                             first_expert: Optional[int] = None) -> None:
+                             first_expert: Optional[int] = None,
+                             prepared: Optional[torch.Tensor] = None) -> None:
         """silu(gate · x) × (up · x) per slot, one launch (ExpertsOps.scala:188-198);
-        `first_expert` as for experts_linear."""
+        `first_expert` and `prepared` as for experts_linear."""
         _require(tuple(gate.shape) == tuple(up.shape) and gate.dtype == up.dtype,
                  f"expertsGatedLinear needs equal shapes, got {list(gate.shape)}, "
                  f"{list(up.shape)}")
         slots, n, k, rows = self._check_experts(x, gate, ids, out)
+        _require(prepared is None or first_expert is not None,
+                 "expertsGatedLinear: a prepared x goes with first_expert")
         if first_expert is None:
             status = self.lib.drift_experts_gated_linear(
                 _x_dtype("expertsGatedLinear", x), _ptr(x), rows, gate.dtype, _ptr(gate.data),
@@ -602,7 +613,7 @@ class CudaOps:
             status = self.lib.drift_experts_gated_linear_local(
                 _x_dtype("expertsGatedLinear", x), _ptr(x), rows, gate.dtype, _ptr(gate.data),
                 _ptr(up.data), gate.shape[0], first_expert, n, k, _ptr(ids), slots, _ptr(out),
-                self._stream())
+                _ptr(prepared), self._stream())
         check("drift_experts_gated_linear", status)
 
     @staticmethod

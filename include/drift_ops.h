@@ -237,12 +237,12 @@ int drift_gated_rms_norm(const float* x, const float* weight, const float* gate,
 int drift_experts_linear_local(int x_dtype, const void* x, int64_t x_rows, int weight_dtype,
                                const void* weight, int64_t experts, int64_t first_expert,
                                int64_t n, int64_t k, const int32_t* ids, int64_t slots,
-                               float* out, drift_stream_t stream);
+                               float* out, const void* prepared, drift_stream_t stream);
 int drift_experts_gated_linear_local(int x_dtype, const void* x, int64_t x_rows, int weight_dtype,
                                      const void* gate, const void* up, int64_t experts,
                                      int64_t first_expert, int64_t n, int64_t k,
                                      const int32_t* ids, int64_t slots, float* out,
-                                     drift_stream_t stream);
+                                     const void* prepared, drift_stream_t stream);
 
 /* ---- prepared x (new) ------------------------------------------------------
  * A product streams its weights against x's "records" (x per 32-value block as

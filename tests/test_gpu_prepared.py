@@ -116,6 +116,47 @@ def test_attention_records_feed_linear(ops, dim, q_heads, kv_heads):
     assert torch.equal(fused, alone)
 
 
+@pytest.mark.parametrize("dtype", [oracle.Q8_0, oracle.Q4_0, oracle.Q4_1],
+                         ids=lambda t: oracle.NAMES[t])
+@pytest.mark.parametrize("tokens", [1, 3, 9])
+def test_norm_records_feed_experts(ops, dtype, tokens):
+    """The post norm's records feeding the router, the experts' gate and up
+    products and a plain expert product (9 tokens: rows past the first
+    8-row record): bit for bit the products that prepare x themselves."""
+    rng = np.random.default_rng(90 + 7 * dtype + tokens)
+    experts, ffn, hidden, used = 16, 256, 2048, 4
+    gate = Stored.upload(dtype, (experts, ffn, hidden),
+                         synthetic.quantized(rng, dtype, experts * ffn, hidden))
+    up = Stored.upload(dtype, (experts, ffn, hidden),
+                       synthetic.quantized(rng, dtype, experts * ffn, hidden))
+    (router,) = weights(rng, [experts], hidden, dtype)
+    x = torch.from_numpy(rng.standard_normal((tokens, hidden)).astype(np.float32)).cuda()
+    weight = torch.from_numpy((1 + 0.02 * rng.standard_normal(hidden)).astype(np.float32)).cuda()
+    prepared = ops.prepared_x(tokens, hidden)
+    normed = torch.empty_like(x)
+    ops.add_rms_norm(x, None, RowNorm(weight, 1e-6, 0.0, normed), prepared)
+    ids = torch.from_numpy(np.stack([rng.permutation(experts)[:used] for _ in range(tokens)])
+                           .astype(np.int32).reshape(-1)).cuda()
+    logits = [torch.empty(tokens, experts, device="cuda") for _ in range(2)]
+    route_ids = [torch.empty(tokens, used, dtype=torch.int32, device="cuda") for _ in range(2)]
+    route_weights = [torch.empty(tokens, used, device="cuda") for _ in range(2)]
+    ops.route_linear(normed, router, logits[0], route_ids[0], route_weights[0], prepared)
+    ops.route_linear(normed, router, logits[1], route_ids[1], route_weights[1])
+    assert torch.equal(logits[0], logits[1]) and torch.equal(route_ids[0], route_ids[1])
+    gated = [torch.empty(tokens * used, ffn, device="cuda") for _ in range(2)]
+    ops.experts_gated_linear(normed, gate, up, ids, gated[0], first_expert=0, prepared=prepared)
+    ops.experts_gated_linear(normed, gate, up, ids, gated[1])
+    assert torch.equal(gated[0], gated[1])
+    plain = [torch.empty(tokens * used, ffn, device="cuda") for _ in range(2)]
+    ops.experts_linear(normed, gate, ids, plain[0], first_expert=0, prepared=prepared)
+    ops.experts_linear(normed, gate, ids, plain[1])
+    assert torch.equal(plain[0], plain[1])
+    # and the product itself against the oracle
+    expected = oracle.experts_linear(dtype, normed.cpu().numpy(), gate.data.cpu().numpy(), experts,
+                                     ffn, hidden, ids.cpu().numpy().reshape(tokens, used))
+    assert np.allclose(plain[0].cpu().numpy(), expected, rtol=1e-3, atol=1e-4)
+
+
 def test_prepared_refusals(ops):
     x = torch.zeros(2, 100, device="cuda")
     w = torch.ones(100, device="cuda")
