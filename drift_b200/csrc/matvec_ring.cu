@@ -286,17 +286,26 @@ struct Acc {
   }
 };
 
-// A row's sum is a chain over fixed groups of its segments: min(8, segments)
-// groups, group g holding segments [segments g / G, segments (g + 1) / G);
+// A row's sum is a chain over fixed groups of its segments -- G of them:
+// min(16, segments) for rows of 32 segments (8192 columns) or more, else
+// min(8, segments) -- group g holding segments [segments g / G,
+// segments (g + 1) / G);
 // a group is summed block by block from zero and the row is
 // ((group_0 + group_1) + group_2) + ... Whichever warps take which groups,
 // the bits are the same -- so the schedule (tiles per warp, splits between
 // warps and CTAs, other matrices sharing a launch, the number of vectors)
 // never shows in the result.
+// (Long rows need 16 units a tile to spread a few tiles over the SMs; on
+// 4096-column rows the extra partial sums cost more than they give back.)
+constexpr int MAX_GROUPS = 16, LONG_SEGMENTS = 32;
+__host__ __device__ constexpr int group_count(long long segments) {
+  const long long most = segments >= LONG_SEGMENTS ? MAX_GROUPS : 8;
+  return int(segments < most ? segments : most);
+}
 struct Groups {
   int segments, count, first_end;
   unsigned long long ends;  // bit s: segment s ends a group (segments below 64)
-  __device__ explicit Groups(int s) : segments(s), count(s < 8 ? s : 8), ends(0) {
+  __device__ explicit Groups(int s) : segments(s), count(group_count(s)), ends(0) {
     for (int g = 1; g <= count; ++g)
       if (begin(g) - 1 < 64) ends |= 1ull << (begin(g) - 1);
     first_end = begin(1);
@@ -312,8 +321,61 @@ struct Groups {
 // Group sums of tiles split between warps: [slot][group][ROWS][slots], the
 // slot a tile's index in a balanced launch, or a CTA's leftover tile in the
 // tile schedule.
-constexpr long long PARTIAL_FLOATS = 5ll << 20;
-__device__ float group_partials[PARTIAL_FLOATS];
+// (the tile schedule's most: 148 CTAs x 8 warps x 16 groups x 64 rows x 8
+// slots, 9.7 M; a balanced launch's: 8192 units x 64 rows x 8 slots, 4.2 M)
+constexpr long long PARTIAL_FLOATS = 10ll << 20;
+__device__ __align__(16) float group_partials[PARTIAL_FLOATS];
+
+// The chain of a tile's group sums (each ROWS x VSLOTS floats, `stride`
+// floats apart from the next group's), N outputs a lane at a time (4 for
+// the MMA mode, 2 for the dp4a modes) with eight groups' loads in flight;
+// out(e, sum) takes output e of the tile. The order is ((0 + g0) + g1) + ...
+// whatever the schedule.
+template <int N>
+struct Lanes;
+template <>
+struct Lanes<4> {
+  using type = float4;
+  __device__ static float get(const float4& v, int i) {
+    return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+  }
+  __device__ static void add(float4& s, const float4& v) {
+    s.x += v.x;
+    s.y += v.y;
+    s.z += v.z;
+    s.w += v.w;
+  }
+};
+template <>
+struct Lanes<2> {
+  using type = float2;
+  __device__ static float get(const float2& v, int i) { return i == 0 ? v.x : v.y; }
+  __device__ static void add(float2& s, const float2& v) {
+    s.x += v.x;
+    s.y += v.y;
+  }
+};
+
+template <int VSLOTS, typename OUT>
+__device__ __forceinline__ void chain_groups(const float* sums, long long stride, int count,
+                                             int first, int step, OUT out) {
+  constexpr int N = VSLOTS == 8 ? 4 : 2, E = ROWS * VSLOTS, BATCH = VSLOTS == 2 ? 4 : 8;
+  using V = typename Lanes<N>::type;
+  for (int en = first; en < E / N; en += step) {
+    V sum = {};
+    for (int g0 = 0; g0 < count; g0 += BATCH) {
+      V p[BATCH];
+#pragma unroll
+      for (int g = 0; g < BATCH; ++g)
+        if (g0 + g < count) p[g] = __ldcg(reinterpret_cast<const V*>(sums + (g0 + g) * stride) + en);
+#pragma unroll
+      for (int g = 0; g < BATCH; ++g)
+        if (g0 + g < count) Lanes<N>::add(sum, p[g]);
+    }
+#pragma unroll
+    for (int i = 0; i < N; ++i) out(N * en + i, Lanes<N>::get(sum, i));
+  }
+}
 
 // The CTA's schedule. CTA c owns tiles [t0, t0 + count), an even share of the
 // matrix's. Its W warps take them in rounds -- warp w sums tile t0 + f W + w
@@ -488,18 +550,16 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
     for (int j = consumed; j < issued; ++j) tc::mbar_wait(&bars[j % S], (j / S) & 1, &never, nullptr);
   }
   if (plan.left > 0) {
-    // the leftover tiles: their group sums chained in group order
+    // the leftover tiles: their group sums chained in group order, warp w
+    // taking tiles w, w + W, ...
     __syncthreads();
-    for (int e = threadIdx.x; e < plan.left * ROWS * VSLOTS; e += blockDim.x) {
-      const int l = e / (ROWS * VSLOTS), r = (e / VSLOTS) % ROWS, v = e % VSLOTS;
-      const int row = (plan.t0 + plan.rounds * W + l) * ROWS + r;
-      if (row < rows && v < vectors) {
-        float sum = 0.0f;
-        for (int g = 0; g < groups.count; ++g)
-          sum += __ldcg(shared_sums + ((long long)l * groups.count + g) * ROWS * VSLOTS +
-                        r * VSLOTS + v);
-        y[(long long)v * rows + row] = sum;
-      }
+    for (int l = warp; l < plan.left; l += W) {
+      const int tile = plan.t0 + plan.rounds * W + l;
+      chain_groups<VSLOTS>(shared_sums + (long long)l * groups.count * ROWS * VSLOTS,
+                           ROWS * VSLOTS, groups.count, lane, WARP, [&](int e, float sum) {
+                             const int r = e / VSLOTS, v = e % VSLOTS, row = tile * ROWS + r;
+                             if (row < rows && v < vectors) y[(long long)v * rows + row] = sum;
+                           });
     }
   }
 }
@@ -667,13 +727,10 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
     }
     if (!__shfl_sync(0xffffffffu, done, 0)) continue;
     __threadfence();
-    for (int e = lane; e < ROWS * VSLOTS; e += WARP) {
+    chain_groups<VSLOTS>(tile_sums, ROWS * VSLOTS, groups.count, lane, WARP, [&](int e, float sum) {
       const int r = e / VSLOTS, v = e % VSLOTS, row = local * ROWS + r;
-      if (row >= L.rows[m] || v >= L.vectors) continue;
-      float sum = 0.0f;
-      for (int g = 0; g < groups.count; ++g) sum += __ldcg(tile_sums + g * ROWS * VSLOTS + e);
-      L.y[m][(long long)v * L.rows[m] + row] = sum;
-    }
+      if (row < L.rows[m] && v < L.vectors) L.y[m][(long long)v * L.rows[m] + row] = sum;
+    });
     if (lane == 0) split_arrivals[tile] = 0;
   }
   if (!ok) {
@@ -696,9 +753,9 @@ int launch_mode(const CUtensorMap& wmap, const uint8_t* records, float* y, int r
   const int tiles = (rows + ROWS - 1) / ROWS;
   const unsigned grid = unsigned(tiles < sm_count() ? tiles : sm_count());
   // each CTA's leftover tiles keep their group sums in group_partials
-  if ((long long)grid * Shape::WARPS * 8 * ROWS * 8 > PARTIAL_FLOATS)
+  if ((long long)grid * Shape::WARPS * MAX_GROUPS * ROWS * 8 > PARTIAL_FLOATS)
     return invalid("%u CTAs of leftover sums (at most %lld)", grid,
-                   PARTIAL_FLOATS / (Shape::WARPS * 8 * ROWS * 8));
+                   PARTIAL_FLOATS / (Shape::WARPS * MAX_GROUPS * ROWS * 8));
   DRIFT_CUDA(launch_pdl(matvec_ring_kernel<T, MODE, XSMEM>, grid, Shape::WARPS * 32, smem, stream,
                         wmap, records, y, rows, cols, vectors, device_error_word()));
   return 0;
@@ -738,7 +795,7 @@ int launch_split_mode(const SplitLaunch& launch, long long units, cudaStream_t s
 // The units of a product in the balanced schedule: tiles x groups.
 long long split_units(int64_t rows, int64_t cols) {
   const int64_t segments = (cols / 32 + SEG_BLOCKS - 1) / SEG_BLOCKS;
-  return ((rows + ROWS - 1) / ROWS) * (segments < 8 ? segments : 8);
+  return ((rows + ROWS - 1) / ROWS) * group_count(segments);
 }
 
 // One balanced launch over `count` matrices of one type sharing x (at most
@@ -765,7 +822,7 @@ int split_dispatch(int count, const uint8_t* const* weights, float* const* ys, c
   launch.records = records;
   launch.error = device_error_word();
   const long long segments = (cols / 32 + SEG_BLOCKS - 1) / SEG_BLOCKS;
-  const long long units = (long long)tiles * (segments < 8 ? segments : 8);
+  const long long units = (long long)tiles * group_count(segments);
   if (units > SPLIT_UNITS) return invalid("a balanced launch of %lld units", units);
   if (vectors == 1) return launch_split_mode<T, MODE_DP4A_1>(launch, units, stream);
   if (vectors == 2) return launch_split_mode<T, MODE_DP4A_2>(launch, units, stream);
@@ -773,10 +830,19 @@ int split_dispatch(int count, const uint8_t* const* weights, float* const* ys, c
 }
 
 // One configuration per matrix type, whatever the number of vectors (and the
-// group chain makes a row's bits the same in any schedule).
+// group chain makes a row's bits the same in any schedule). A matrix of
+// fewer tiles than SMs takes the balanced schedule, whose (tile, group)
+// units reach every SM, for 1-2 vectors and for long rows; the MMA mode's
+// products of shorter rows keep the tile schedule, which leaves SMs free for
+// the next launch's early weight copies.
 template <typename T>
 int ring_dispatch(const uint8_t* weight, const uint8_t* records, float* y, int rows, int cols,
                   int vectors, cudaStream_t stream) {
+  const int64_t rows64 = rows;
+  const bool few_tiles = (rows + ROWS - 1) / ROWS < sm_count();
+  const bool long_rows = (cols / 32 + SEG_BLOCKS - 1) / SEG_BLOCKS >= LONG_SEGMENTS;
+  if (few_tiles && (vectors <= 2 || long_rows) && split_units(rows64, cols) <= SPLIT_UNITS)
+    return split_dispatch<T>(1, &weight, &y, &rows64, cols, records, vectors, stream);
   CUtensorMap wmap;
   DRIFT_TRY(encode_word_rows(&wmap, weight, int64_t(cols / 32) * T::BYTES / 4, rows,
                              Ring<T>::PITCH / 4, ROWS));
