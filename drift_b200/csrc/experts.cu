@@ -14,6 +14,7 @@
 #include "quant.cuh"
 #include "registry.cuh"
 #include "rowwise.cuh"
+#include "x22.cuh"
 
 namespace drift {
 
@@ -329,7 +330,7 @@ __global__ void __launch_bounds__(COMBINE_THREADS) combine_kernel(
     const float* __restrict__ shared_out, const float* __restrict__ shared_input,
     const float* __restrict__ shared_router, const float* residual, float* out, int k, int hidden,
     const float* __restrict__ norm_weight, float* __restrict__ normed, float epsilon,
-    float weight_offset) {
+    float weight_offset, uint8_t* records) {
   pdl_trigger();  // the next kernel may launch and wait for this one
   pdl_wait();     // what the kernels before this one wrote is visible
   __shared__ float partial[32];
@@ -382,7 +383,11 @@ __global__ void __launch_bounds__(COMBINE_THREADS) combine_kernel(
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
     const int c = threadIdx.x + i * COMBINE_THREADS;
-    if (c < hidden) normed[t * hidden + c] = sum[i] * scale * (norm_weight[c] + weight_offset);
+    if (c >= hidden) continue;  // (whole warps when hidden is a multiple of 32)
+    const float value = sum[i] * scale * (norm_weight[c] + weight_offset);
+    normed[t * hidden + c] = value;
+    // warp w holds columns 1024 i + 32 w .. + 31: block 32 i + w of the row
+    if (records) x22_record_block(value, records, int(t), c / 32, hidden / 32);
   }
 }
 
@@ -394,12 +399,12 @@ static int launch_combine(const float* expert_out, const float* weights, int64_t
                           int64_t hidden, const float* shared_out, const float* shared_input,
                           const float* shared_router, const float* residual, float* out,
                           const float* norm_weight, float* normed, float epsilon,
-                          float weight_offset, cudaStream_t stream) {
+                          float weight_offset, cudaStream_t stream, uint8_t* records = nullptr) {
   const unsigned grid = unsigned(tokens);
 #define DRIFT_COMBINE(PER)                                                                        \
   DRIFT_CUDA(launch_pdl(combine_kernel<NORM, PER>, grid, COMBINE_THREADS, 0, stream, expert_out,  \
                         weights, shared_out, shared_input, shared_router, residual, out, int(k), \
-                        int(hidden), norm_weight, normed, epsilon, weight_offset))
+                        int(hidden), norm_weight, normed, epsilon, weight_offset, records))
   if (hidden <= 1024) DRIFT_COMBINE(1);
   else if (hidden <= 2048) DRIFT_COMBINE(2);
   else if (hidden <= 4096) DRIFT_COMBINE(4);
@@ -499,6 +504,26 @@ int drift_moe_combine_norm(const float* expert_out, const float* weights, int64_
   return launch_combine<true>(expert_out, weights, tokens, k, hidden, shared_out, shared_input,
                               shared_router, residual, residual, norm_weight, normed, epsilon,
                               weight_offset, cudaStream_t(stream));
+}
+
+int drift_moe_combine_norm_prepared(const float* expert_out, const float* weights, int64_t tokens,
+                                    int64_t k, int64_t hidden, const float* shared_out,
+                                    const float* shared_input, const float* shared_router,
+                                    float* residual, const float* norm_weight, float epsilon,
+                                    float weight_offset, float* normed, void* prepared,
+                                    drift_stream_t stream) {
+  if (!prepared)
+    return drift_moe_combine_norm(expert_out, weights, tokens, k, hidden, shared_out, shared_input,
+                                  shared_router, residual, norm_weight, epsilon, weight_offset,
+                                  normed, stream);
+  DRIFT_TRY(check_combine(expert_out, weights, tokens, k, hidden, shared_out, shared_input,
+                          shared_router, residual));
+  if (hidden % 32 != 0) return invalid("moeCombineNorm: records of %lld columns", (long long)hidden);
+  if (tokens == 0 || hidden == 0) return 0;
+  if (!norm_weight || !normed) return invalid("moeCombineNorm: no norm weight or output");
+  return launch_combine<true>(expert_out, weights, tokens, k, hidden, shared_out, shared_input,
+                              shared_router, residual, residual, norm_weight, normed, epsilon,
+                              weight_offset, cudaStream_t(stream), static_cast<uint8_t*>(prepared));
 }
 
 }  // extern "C"

@@ -374,10 +374,10 @@ class HybridDecoder:
 
     def _delta(self, layer: DeltaLayer, index: int) -> None:
         ops, c, b, P = self.ops, self.config, self.batch, self.prepared
-        # (the layer's input comes from the mixture's combine + norm, which
-        # writes no records: the products prepare x themselves)
+        # (the layer's input and its records come from the previous mixture's
+        # combine + norm, or the first norm)
         ops.linears(self.normed, [layer.qkv, layer.z, layer.a, layer.b],
-                    [self.qkv, self.z, self.a, self.b])
+                    [self.qkv, self.z, self.a, self.b], P)
         ops.causal_conv_decode(self.qkv, layer.conv, 1, self.conv_states[index], self.convolved)
         ops.gated_delta_rule_decode(self.convolved, self.a, self.b, layer.decay, layer.dt_bias,
                                     self.delta_states[index],
@@ -392,7 +392,7 @@ class HybridDecoder:
     def _full(self, layer: FullLayer, index: int) -> None:
         ops, c, b, P = self.ops, self.config, self.batch, self.prepared
         ops.linears(self.normed, [layer.q, layer.k, layer.v],
-                    [self.query_gate.view(b, -1), self.k.view(b, -1), self.v.view(b, -1)])
+                    [self.query_gate.view(b, -1), self.k.view(b, -1), self.v.view(b, -1)], P)
         ops.attention_inputs_decode(self.query_gate, self.k, self.v, layer.q_norm, layer.k_norm,
                                     c.epsilon, self.positions, self.rope, self.q_turned,
                                     self.caches[index], self.page_tables)
@@ -423,7 +423,7 @@ class HybridDecoder:
             ops.linears(self.shared_gated, [mixture.shared_down], [self.shared_out])
             ops.moe_combine_norm(self.expert_out, self.route_weights,
                                  SharedExpert(self.shared_out, self.normed, mixture.shared_router),
-                                 self.x, next_norm)
+                                 self.x, next_norm, P)
             return
         # expert parallelism: this rank's experts (other ranks' slots are
         # zeros), the shared expert on rank 0, the partial combine into the
@@ -440,13 +440,14 @@ class HybridDecoder:
             ops.linears(self.shared_gated, [mixture.shared_down], [self.shared_out])
             shared = SharedExpert(self.shared_out, self.normed, mixture.shared_router)
         ops.moe_combine(self.expert_out, self.route_weights, shared, None, self.exchange.slots[1])
-        self.exchange.add_rms_norm(1, self.x, next_norm)
+        self.exchange.add_rms_norm(1, self.x, next_norm, P)
 
     def step(self) -> torch.Tensor:
         """One decode step: self.ids at self.positions -> self.logits."""
         ops, c, w, P = self.ops, self.config, self.weights, self.prepared
         ops.embedding(w.embedding, self.ids, self.x)
-        ops.rms_norm(self.x, w.layers[0].input_norm, c.epsilon, 0.0, self.normed)
+        ops.add_rms_norm(self.x, None, RowNorm(w.layers[0].input_norm, c.epsilon, 0.0, self.normed),
+                         P)
         for index, layer in enumerate(w.layers):
             if isinstance(layer.mixer, FullLayer):
                 self._full(layer.mixer, index)
@@ -460,7 +461,7 @@ class HybridDecoder:
             following = (w.layers[index + 1].input_norm if index + 1 < len(w.layers)
                          else w.final_norm)
             self._mixture(layer.mixture, following)
-        ops.linears(self.normed, [w.lm_head], [self.logits])
+        ops.linears(self.normed, [w.lm_head], [self.logits], P)
         return self.logits
 
     def reserve(self) -> None:

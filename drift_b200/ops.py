@@ -648,14 +648,15 @@ class CudaOps:
         check("drift_moe_combine", status)
 
     def moe_combine_norm(self, expert_out, weights, shared: Optional[SharedExpert], residual,
-                         norm: RowNorm) -> None:
+                         norm: RowNorm, prepared: Optional[torch.Tensor] = None) -> None:
         """moe_combine into the residual, then norm's RMS norm of it into
-        norm.out, one launch (ExpertsOps.scala:140-152)."""
+        norm.out, one launch (ExpertsOps.scala:140-152); with `prepared`,
+        norm.out's records too."""
         tokens, k, hidden = self._check_combine(expert_out, weights, shared, residual, residual)
         self._check_row_wise("rmsNorm", residual, norm.out, norm.weight)
-        status = self.lib.drift_moe_combine_norm(
+        status = self.lib.drift_moe_combine_norm_prepared(
             _ptr(expert_out), _ptr(weights), tokens, k, hidden,
             _ptr(shared.output) if shared else None, _ptr(shared.input) if shared else None,
             _ptr(shared.router) if shared else None, _ptr(residual), _ptr(norm.weight),
-            norm.epsilon, norm.weight_offset, _ptr(norm.out), self._stream())
+            norm.epsilon, norm.weight_offset, _ptr(norm.out), _ptr(prepared), self._stream())
         check("drift_moe_combine_norm", status)

@@ -258,6 +258,15 @@ size_t drift_prepared_x_bytes(int64_t m, int64_t k);
 int drift_add_rms_norm_prepared(float* x, const float* y, const float* weight, float epsilon,
                                 float weight_offset, float* out, int64_t rows, int64_t cols,
                                 void* prepared, drift_stream_t stream);
+/* drift_moe_combine_norm (hidden a multiple of 32), also writing normed's
+ * records: the next layer's input, as the reference's moe_combine_norm feeds
+ * the next layer's products (norm.hip:43-59). */
+int drift_moe_combine_norm_prepared(const float* expert_out, const float* weights, int64_t tokens,
+                                    int64_t k, int64_t hidden, const float* shared_out,
+                                    const float* shared_input, const float* shared_router,
+                                    float* residual, const float* norm_weight, float epsilon,
+                                    float weight_offset, float* normed, void* prepared,
+                                    drift_stream_t stream);
 /* drift_gated over rows x cols values, also writing out's records. */
 int drift_gated_prepared(int kind, const float* gate, const float* up, float* out, int64_t rows,
                          int64_t cols, void* prepared, drift_stream_t stream);

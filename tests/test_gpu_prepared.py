@@ -12,7 +12,7 @@ import torch
 
 import oracle
 from drift_b200 import synthetic
-from drift_b200.ops import SILU, Attention, CudaOps, KvCache, RowNorm, Stored
+from drift_b200.ops import SILU, Attention, CudaOps, KvCache, RowNorm, SharedExpert, Stored
 
 pytestmark = pytest.mark.gpu
 
@@ -155,6 +155,35 @@ def test_norm_records_feed_experts(ops, dtype, tokens):
     expected = oracle.experts_linear(dtype, normed.cpu().numpy(), gate.data.cpu().numpy(), experts,
                                      ffn, hidden, ids.cpu().numpy().reshape(tokens, used))
     assert np.allclose(plain[0].cpu().numpy(), expected, rtol=1e-3, atol=1e-4)
+
+
+@pytest.mark.parametrize("tokens", [1, 3, 9])
+def test_combine_norm_records_feed_linears(ops, tokens):
+    """moe_combine_norm writing the next layer's records (shared expert on):
+    the residual, the norm and the products over them bit for bit those of
+    the unprepared calls."""
+    rng = np.random.default_rng(120 + tokens)
+    k, hidden = 10, 2048
+    (w,) = weights(rng, [512], hidden)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).cuda()
+    expert_out = dev(rng.standard_normal((tokens * k, hidden)))
+    route = dev(rng.random((tokens, k)))
+    shared = SharedExpert(dev(rng.standard_normal((tokens, hidden))),
+                          dev(rng.standard_normal((tokens, hidden))),
+                          dev(0.02 * rng.standard_normal(hidden)))
+    residual = dev(rng.standard_normal((tokens, hidden)))
+    norm_weight = dev(1 + 0.02 * rng.standard_normal(hidden))
+    prepared = ops.prepared_x(tokens, hidden)
+    r1, n1 = residual.clone(), torch.empty_like(residual)
+    ops.moe_combine_norm(expert_out, route, shared, r1, RowNorm(norm_weight, 1e-6, 0.0, n1),
+                         prepared)
+    r2, n2 = residual.clone(), torch.empty_like(residual)
+    ops.moe_combine_norm(expert_out, route, shared, r2, RowNorm(norm_weight, 1e-6, 0.0, n2))
+    assert torch.equal(r1, r2) and torch.equal(n1, n2)
+    fused, alone = torch.empty(tokens, 512, device="cuda"), torch.empty(tokens, 512, device="cuda")
+    ops.linears(n1, [w], [fused], prepared)
+    ops.linear(n2, w, alone)
+    assert torch.equal(fused, alone)
 
 
 def test_prepared_refusals(ops):
