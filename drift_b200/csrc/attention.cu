@@ -251,9 +251,11 @@ __device__ void join_head(const AttentionArgs& a, const float* sinks, float* out
 // 16-byte chunk from each of eight consecutive rows, so chunk c of row r sits
 // at chunk c ^ (r mod 8) of its row: the eight reads land on distinct banks.
 // (80-wide key rows, ten chunks, are padded by a chunk instead.)
+__host__ __device__ constexpr int split_keys(int head_dim) { return head_dim > 128 ? 64 : 128; }
+
 template <int D>
 struct SplitTile {
-  static constexpr int KEYS = D > 128 ? 64 : 128;  // keys of a split
+  static constexpr int KEYS = split_keys(D);  // keys of a split
   static constexpr int WARPS = SPLIT_THREADS / 32;
   static constexpr int QW = KEYS / 16;             // warps that score: 16 keys each
   static constexpr int NT = 2;                     // 8-key tiles of a warp's scores
@@ -703,7 +705,7 @@ int launch_attention(const AttentionArgs& a, const float* sinks, float* out, cud
 }
 
 // Keys a split of attention takes, by head width.
-int keys_per_split(int head_dim) { return head_dim > 128 ? 64 : 128; }
+int keys_per_split(int head_dim) { return split_keys(head_dim); }
 
 // The most splits the join takes (their factors in 48 KB of shared memory).
 constexpr int MAX_SPLITS = 48 * 1024 / 4 - 16;

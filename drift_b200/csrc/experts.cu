@@ -105,10 +105,12 @@ DRIFT_REGISTER(route_topk, route_kernel)
 // Slot s (blockIdx.y) multiplies expert ids[s] of a [experts][rows][cols]
 // weight with x row s / divisor, prepared as for the plain product (the
 // tensor-core layout: row v's part of block c is the 112-byte slot v % 8 of
-// record (v / 8, c), its plane words in the order 0, 4, 1, 5, 2, 6, 3, 7). The
-// warps of a CTA split rows and blocks as matvec_x22_kernel does. GATED: a
-// gate and an up weight of the same shape, out = silu(gate . x) * (up . x).
-// Each warp: rows of its group, k-split kw; 8 warps = (8 / KS) row groups.
+// record (v / 8, c), its plane words in the order 0, 4, 1, 5, 2, 6, 3, 7).
+// GATED: a gate and an up weight of the same shape, out = silu(gate . x) *
+// (up . x). The 8 warps of a CTA are 8 / KS row groups of KS k-splits: warp
+// (group, kw) takes 4 rows of its group and, lane l, blocks 32 kw + l,
+// 32 (kw + KS) + l, ...; the k-splits' sums meet in shared memory in a fixed
+// order.
 template <typename T, int KS, bool GATED>
 __global__ void __launch_bounds__(256) experts_x22_kernel(
     const uint8_t* __restrict__ gate, const uint8_t* __restrict__ up, long long expert_bytes,

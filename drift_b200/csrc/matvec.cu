@@ -1,21 +1,16 @@
 // Decode-shaped products over quantized weights: y[v, row] = sum_k W[row, k] *
-// x[v, k] for up to 8 vectors v (the runner's matvec_float_x_<t>,
+// x[v, k] for up to 8 vectors v at a pass (the runner's matvec_float_x_<t>,
 // kernels/matvec.hip:418-543, 915-924, and its dispatch
 // ops/HipLinear.scala:104-276).
 //
 // B200 design (not the reference's): x is first prepared per 32-value block
-// into exact integer byte planes (quantize_x22, quant.cuh), so a weight block
-// meets x in dp4a -- 24 dp4a and a short float epilogue per 32 weights and
-// vector, about 2.5 instructions per weight byte for Q4_1 at one vector -- and
-// the streaming of weights, not the arithmetic, bounds the kernel at HBM rate.
-//
-// Work split: a warp takes a group of 8 rows and KS warps of a 256-thread CTA
-// split those rows' blocks between them (lane l of k-split w takes blocks
-// 32 w + l, 32 (w + KS) + l, ...), so small matrices still fill every SM.
-// Each lane loads the aligned words of its block in 8 rows before decoding any
-// (40-72 loads in flight per lane), meets them with the x records of up to V
-// vectors (kept in registers across the 8 rows), and sums in float. The
-// warp's sums reduce by shuffles, the k-splits' through shared memory.
+// into exact integer byte planes (quantize_x22_mma, quant.cuh / mma_i8.cuh),
+// so a weight block meets x in integer dot products -- dp4a for one or two
+// vectors, mma.sync m16n8k32 for more -- and a short float epilogue per 32
+// weights and vector. Weights whose rows are whole 16-byte units stream
+// through shared memory (matvec_ring.cu); this file holds the preparation,
+// the same MMA arithmetic reading weights straight from global memory for
+// the other rows, and the dispatch between them.
 #include <cuda_runtime.h>
 
 #include "common.cuh"
@@ -27,74 +22,9 @@
 namespace drift {
 
 // ---- x preparation ---------------------------------------------------------------
-// One warp per 32-value block of x (m rows of k, blocks = m * k / 32), lane j
-// holding value j; the record layout is quant.cuh's.
-template <bool BF16>
-__device__ __forceinline__ void quantize_x22_block(const void* x, uint32_t* records, long long block) {
-  const int lane = threadIdx.x % WARP;
-  float v;
-  if (BF16) {
-    const uint16_t bits = reinterpret_cast<const uint16_t*>(x)[block * 32 + lane];
-    v = __uint_as_float(uint32_t(bits) << 16);
-  } else {
-    v = reinterpret_cast<const float*>(x)[block * 32 + lane];
-  }
-  float amax = fabsf(v);
-  bool finite = isfinite(v);
-#pragma unroll
-  for (int o = 16; o > 0; o /= 2) {
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    finite = __all_sync(0xffffffffu, finite);
-  }
-  int X = 0;
-  float s = 0.0f;
-  if (!finite) {
-    s = __int_as_float(0x7fc00000);  // a NaN scale: the block's products come out NaN
-  } else if (amax > 0.0f) {
-    const int e = ilogbf(amax) + 1;  // 2^(e-1) <= amax < 2^e
-    s = ldexpf(1.0f, e - X_BITS);
-    X = __float2int_rn(ldexpf(v, X_BITS - e));  // exact scaling, then round to nearest even
-  }
-  uint32_t* record = records + block * X_RECORD_WORDS;
-  uint8_t* bytes = reinterpret_cast<uint8_t*>(record);
-  bytes[lane] = uint8_t(X & 0xff);
-  bytes[32 + lane] = uint8_t((X >> 8) & 0xff);
-  bytes[64 + lane] = uint8_t((X >> 16) & 0xff);
-  int sum = X;
-#pragma unroll
-  for (int o = 16; o > 0; o /= 2) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  if (lane == 0) {
-    record[24] = __float_as_uint(s);
-    record[25] = uint32_t(sum);
-  }
-}
-
-template <bool BF16>
-__global__ void __launch_bounds__(256) quantize_x22_kernel(const void* x, uint32_t* records,
-                                                          long long blocks) {
-  pdl_trigger();  // the next kernel may launch and wait for this one
-  pdl_wait();     // what the kernels before this one wrote is visible
-  const long long block = (long long)blockIdx.x * (blockDim.x / WARP) + threadIdx.x / WARP;
-  if (block >= blocks) return;
-  quantize_x22_block<BF16>(x, records, block);
-}
-
-extern "C" __global__ void __launch_bounds__(256)
-    quantize_x22_f32(const float* x, uint32_t* records, long long blocks) {
-  const long long block = (long long)blockIdx.x * (blockDim.x / WARP) + threadIdx.x / WARP;
-  if (block >= blocks) return;
-  quantize_x22_block<false>(x, records, block);
-}
-
-extern "C" __global__ void __launch_bounds__(256)
-    quantize_x22_bf16(const uint16_t* x, uint32_t* records, long long blocks) {
-  const long long block = (long long)blockIdx.x * (blockDim.x / WARP) + threadIdx.x / WARP;
-  if (block >= blocks) return;
-  quantize_x22_block<true>(x, records, block);
-}
-
-// The same preparation into the MMA layout (mma_i8.cuh): block `block` of
-// vector v (pass v / 8, slot g = v % 8).
+// One warp per 32-value block of each vector (lane j holding value j), into
+// the MMA record layout (mma_i8.cuh): block `block` of vector v (pass v / 8,
+// slot g = v % 8); vectors past m in the last pass get zero slots.
 template <bool BF16>
 __global__ void __launch_bounds__(256) quantize_x22_mma_kernel(const void* x, uint8_t* records,
                                                               int vectors, int blocks) {
@@ -116,124 +46,6 @@ __global__ void __launch_bounds__(256) quantize_x22_mma_kernel(const void* x, ui
 }
 
 // ---- the product -----------------------------------------------------------------
-constexpr int ROWS_PER_GROUP = 8;
-constexpr int MAX_V = 2;
-
-// y[v * rows + row] for rows [row0, row0 + 8) of one warp's share of blocks;
-// `sums` collects them per (row, vector).
-template <typename T, int V, int KS>
-__device__ __forceinline__ void matvec_x22_group(const uint8_t* __restrict__ weight,
-                                                 const uint32_t* __restrict__ records, int rows,
-                                                 int cols, int vectors, int row0, int kw,
-                                                 float (&sums)[ROWS_PER_GROUP][V]) {
-  const int lane = threadIdx.x % WARP;
-  const int blocks = cols / 32;
-  const long long row_bytes = (long long)blocks * T::BYTES;
-#pragma unroll
-  for (int r = 0; r < ROWS_PER_GROUP; ++r)
-#pragma unroll
-    for (int v = 0; v < V; ++v) sums[r][v] = 0.0f;
-
-  for (int c = kw * WARP + lane; c < blocks; c += WARP * KS) {
-    uint32_t w[ROWS_PER_GROUP][T::WORDS];
-#pragma unroll
-    for (int r = 0; r < ROWS_PER_GROUP; ++r) {
-      if (row0 + r < rows) {
-        load_block<T>(weight + (long long)(row0 + r) * row_bytes, c, w[r]);
-      } else {
-#pragma unroll
-        for (int i = 0; i < T::WORDS; ++i) w[r][i] = 0;
-      }
-    }
-    uint32_t planes[V][24];
-    float s[V];
-    int sum_x[V];
-#pragma unroll
-    for (int v = 0; v < V; ++v) {
-      if (v < vectors) {
-        const uint4* rec =
-            reinterpret_cast<const uint4*>(records + ((long long)v * blocks + c) * X_RECORD_WORDS);
-#pragma unroll
-        for (int i = 0; i < 6; ++i) {
-          const uint4 q = __ldg(rec + i);
-          planes[v][4 * i] = q.x;
-          planes[v][4 * i + 1] = q.y;
-          planes[v][4 * i + 2] = q.z;
-          planes[v][4 * i + 3] = q.w;
-        }
-        const uint4 tail = __ldg(rec + 6);
-        s[v] = __uint_as_float(tail.x);
-        sum_x[v] = int(tail.y);
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < ROWS_PER_GROUP; ++r) {
-      const Codes codes = T::decode(w[r], c);
-#pragma unroll
-      for (int v = 0; v < V; ++v) {
-        if (v < vectors) {
-          int a0, a1, a2;
-          plane_sums<T>(codes, planes[v], a0, a1, a2);
-          sums[r][v] += block_dot<T>(codes, a0, a1, a2, s[v], sum_x[v]);
-        }
-      }
-    }
-  }
-}
-
-// Grid: ceil(rows / (8 * 8 / KS)) CTAs of 256 threads; the x records of
-// `vectors` <= V vectors at `records`.
-template <typename T, int V, int KS>
-__global__ void __launch_bounds__(256) matvec_x22_kernel(const uint8_t* __restrict__ weight,
-                                                         const uint32_t* __restrict__ records,
-                                                         float* __restrict__ y, int rows, int cols,
-                                                         int vectors) {
-  pdl_trigger();  // the next kernel may launch and wait for this one
-  pdl_wait();     // what the kernels before this one wrote is visible
-  constexpr int GROUPS = 8 / KS;  // row groups per CTA
-  __shared__ float partial[8][ROWS_PER_GROUP][V];
-  const int warp = threadIdx.x / WARP, lane = threadIdx.x % WARP;
-  const int kw = warp % KS, group = warp / KS;
-  const int row0 = (blockIdx.x * GROUPS + group) * ROWS_PER_GROUP;
-  float sums[ROWS_PER_GROUP][V];
-  if (row0 < rows) {
-    matvec_x22_group<T, V, KS>(weight, records, rows, cols, vectors, row0, kw, sums);
-  } else {
-#pragma unroll
-    for (int r = 0; r < ROWS_PER_GROUP; ++r)
-#pragma unroll
-      for (int v = 0; v < V; ++v) sums[r][v] = 0.0f;
-  }
-#pragma unroll
-  for (int r = 0; r < ROWS_PER_GROUP; ++r)
-#pragma unroll
-    for (int v = 0; v < V; ++v) {
-      float total = sums[r][v];
-#pragma unroll
-      for (int o = 16; o > 0; o /= 2) total += __shfl_xor_sync(0xffffffffu, total, o);
-      sums[r][v] = total;
-    }
-  if (lane == 0) {
-#pragma unroll
-    for (int r = 0; r < ROWS_PER_GROUP; ++r)
-#pragma unroll
-      for (int v = 0; v < V; ++v) partial[warp][r][v] = sums[r][v];
-  }
-  __syncthreads();
-  // thread (group, r, v): the k-splits' sums in a fixed order
-  const int t = threadIdx.x;
-  if (t < GROUPS * ROWS_PER_GROUP * V) {
-    const int g = t / (ROWS_PER_GROUP * V), r = (t / V) % ROWS_PER_GROUP, v = t % V;
-    const int row = (blockIdx.x * GROUPS + g) * ROWS_PER_GROUP + r;
-    if (row < rows && v < vectors) {
-      float total = 0.0f;
-#pragma unroll
-      for (int k = 0; k < KS; ++k) total += partial[g * KS + k][r][v];
-      y[(long long)v * rows + row] = total;
-    }
-  }
-}
-
 // Grid: ceil(rows / (16 MT (8 / KS))) CTAs of 256 threads. Warp (group, kw)
 // takes rows [16 MT group, +16 MT) of the CTA's and the kw-th contiguous
 // share of the blocks; up to 8 vectors, x records in the MMA layout.
@@ -321,15 +133,10 @@ __global__ void __launch_bounds__(256) matvec_mma_kernel(const uint8_t* __restri
 
 // ---- by-name kernels ------------------------------------------------------------------
 // Every instantiation, for hosts that launch by name (drift_module_get_function
-// with a NULL module): matvec_x22_<type>_v<V>_ks<KS>, 256 threads, grid
-// ceil(rows / (64 / KS)), arguments (weight, records, y, rows, cols, vectors).
-#define DRIFT_MATVEC_REGISTER(T, name)                                        \
-  DRIFT_REGISTER(matvec_x22_##name##_v1_ks1, (matvec_x22_kernel<T, 1, 1>))    \
-  DRIFT_REGISTER(matvec_x22_##name##_v1_ks2, (matvec_x22_kernel<T, 1, 2>))    \
-  DRIFT_REGISTER(matvec_x22_##name##_v1_ks4, (matvec_x22_kernel<T, 1, 4>))    \
-  DRIFT_REGISTER(matvec_x22_##name##_v2_ks1, (matvec_x22_kernel<T, 2, 1>))    \
-  DRIFT_REGISTER(matvec_x22_##name##_v2_ks2, (matvec_x22_kernel<T, 2, 2>))    \
-  DRIFT_REGISTER(matvec_x22_##name##_v2_ks4, (matvec_x22_kernel<T, 2, 4>))
+// with a NULL module): matvec_mma_<type>_mt<MT>_ks<KS>, 256 threads, grid
+// ceil(rows / (16 MT (8 / KS))), arguments (weight, records, y, rows, cols,
+// vectors); quantize_x22_mma_<x type>, a warp per (vector, block), arguments
+// (x, records, vectors, blocks).
 #define DRIFT_MMA_REGISTER(T, name)                                               \
   DRIFT_REGISTER(matvec_mma_##name##_mt2_ks1, (matvec_mma_kernel<T, 2, 1>))       \
   DRIFT_REGISTER(matvec_mma_##name##_mt2_ks2, (matvec_mma_kernel<T, 2, 2>))       \
@@ -338,11 +145,8 @@ __global__ void __launch_bounds__(256) matvec_mma_kernel(const uint8_t* __restri
 DRIFT_MMA_REGISTER(Q8_0T, q8_0)
 DRIFT_MMA_REGISTER(Q4_0T, q4_0)
 DRIFT_MMA_REGISTER(Q4_1T, q4_1)
-DRIFT_MATVEC_REGISTER(Q8_0T, q8_0)
-DRIFT_MATVEC_REGISTER(Q4_0T, q4_0)
-DRIFT_MATVEC_REGISTER(Q4_1T, q4_1)
-DRIFT_REGISTER(quantize_x22_f32, quantize_x22_f32)
-DRIFT_REGISTER(quantize_x22_bf16, quantize_x22_bf16)
+DRIFT_REGISTER(quantize_x22_mma_f32, quantize_x22_mma_kernel<false>)
+DRIFT_REGISTER(quantize_x22_mma_bf16, quantize_x22_mma_kernel<true>)
 
 // ---- dispatch ----------------------------------------------------------------------------
 struct Workspace {
@@ -369,10 +173,6 @@ int workspace_reserve(size_t bytes, void** pointer) {
   return 0;
 }
 
-size_t linear_workspace_bytes(int64_t m, int64_t k) {
-  return size_t(m) * size_t(k / 32) * X_RECORD_BYTES;
-}
-
 size_t mma_workspace_bytes(int64_t m, int64_t k) {
   return size_t((m + 7) / 8) * size_t(k / 32) * MMA_RECORD_BYTES;
 }
@@ -389,41 +189,6 @@ int prepare_x_mma(int x_dtype, const void* x, int64_t m, int64_t k, uint8_t* rec
   else
     DRIFT_CUDA(launch_pdl(quantize_x22_mma_kernel<false>, grid, 256, 0, stream, x, records, int(m),
                           int(blocks)));
-  return 0;
-}
-
-int prepare_x(int x_dtype, const void* x, int64_t m, int64_t k, uint32_t* records,
-              cudaStream_t stream) {
-  const long long blocks = m * (k / 32);
-  if (blocks == 0) return 0;
-  const unsigned grid = unsigned((blocks + 7) / 8);
-  if (x_dtype == DRIFT_BF16)
-    DRIFT_CUDA(launch_pdl(quantize_x22_kernel<true>, grid, 256, 0, stream, x, records, blocks));
-  else
-    DRIFT_CUDA(launch_pdl(quantize_x22_kernel<false>, grid, 256, 0, stream, x, records, blocks));
-  DRIFT_LAUNCHED("quantize_x22");
-  return 0;
-}
-
-template <typename T, int V>
-static int launch_matvec_v(const uint8_t* weight, const uint32_t* records, float* y, int rows,
-                           int cols, int vectors, cudaStream_t stream) {
-  const int blocks = cols / 32;
-  // k-splits: one block per lane at most in the first pass when the row is
-  // short; up to 4 warps share a row group's blocks
-  const int ks = blocks >= 128 ? 4 : (blocks >= 64 ? 2 : 1);
-  const int rows_per_cta = ROWS_PER_GROUP * 8 / ks;
-  const unsigned grid = unsigned((rows + rows_per_cta - 1) / rows_per_cta);
-  if (ks == 4)
-    DRIFT_CUDA(launch_pdl(matvec_x22_kernel<T, V, 4>, grid, 256, 0, stream, weight, records, y, rows,
-                          cols, vectors));
-  else if (ks == 2)
-    DRIFT_CUDA(launch_pdl(matvec_x22_kernel<T, V, 2>, grid, 256, 0, stream, weight, records, y, rows,
-                          cols, vectors));
-  else
-    DRIFT_CUDA(launch_pdl(matvec_x22_kernel<T, V, 1>, grid, 256, 0, stream, weight, records, y, rows,
-                          cols, vectors));
-  DRIFT_LAUNCHED("matvec_x22");
   return 0;
 }
 

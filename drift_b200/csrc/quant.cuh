@@ -31,17 +31,9 @@ namespace drift {
 // (kernels/quantize.h:6-25, max|x|/127). X is split into three byte planes
 // X = P0 + 256 P1 + 65536 P2 (P0, P1 unsigned, P2 signed) that dp4a meets
 // four at a time with the weights' integer codes; the code-times-plane sums
-// are exact, so the only rounding is of x to s and the float epilogue.
-//
-// One record per (vector, block): 32 words.
-//   words 0..7   plane 0 bytes of values 0..31
-//   words 8..15  plane 1
-//   words 16..23 plane 2
-//   word 24      s, as float bits (NaN when the block holds a NaN or infinity)
-//   word 25      sum_j X_j (int)
-//   words 26..31 unused
-constexpr int X_RECORD_WORDS = 32;
-constexpr int X_RECORD_BYTES = X_RECORD_WORDS * 4;
+// are exact, so the only rounding is of x to s and the float epilogue. The
+// records' layout (eight vectors to a 896-byte record per block, one slot
+// each) is mma_i8.cuh's; s is NaN when the block holds a NaN or infinity.
 constexpr int X_BITS = 21;
 
 // ---- dp4a in the four signednesses ----------------------------------------------

@@ -43,7 +43,7 @@ def test_every_declared_function_is_exported(lib, name):
 
 def test_kernels_are_listed_by_name(lib):
     names = [lib.drift_kernel_name(i).decode() for i in range(lib.drift_kernel_count())]
-    for expected in ["matvec_x22_q4_1_v1_ks4", "matvec_x22_q8_0_v2_ks1", "quantize_x22_bf16",
+    for expected in ["matvec_ring_q4_1_dp4a1", "matvec_split_q8_0_mma", "quantize_x22_mma_bf16",
                      "gather_q8_0", "rms_norm_f32", "gated_f32", "rope_f32", "route_topk",
                      "experts_gated_x22_q4_1_ks2", "moe_combine_norm"]:
         assert expected in names
