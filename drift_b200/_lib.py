@@ -97,7 +97,7 @@ SIGNATURES = {
     "drift_experts_linear_local": (_i32, [_i32, _p, _i64, _i32, _p, _i64, _i64, _i64, _i64, _p,
                                           _i64, _p, _p, _p]),
     "drift_experts_gated_linear_local": (_i32, [_i32, _p, _i64, _i32, _p, _p, _i64, _i64, _i64,
-                                                _i64, _p, _i64, _p, _p, _p]),
+                                                _i64, _p, _i64, _p, _p, _i32, _p]),
     "drift_experts_linear": (_i32, [_i32, _p, _i64, _i32, _p, _i64, _i64, _i64, _p, _i64, _p,
                                     _p]),
     "drift_experts_gated_linear": (_i32, [_i32, _p, _i64, _i32, _p, _p, _i64, _i64, _i64, _p,

@@ -14,7 +14,7 @@
 // leaves, per query head, the largest score, the sum of exp(score - largest)
 // and the unnormalised weighted sum. The last split of each (row, key head)
 // to finish joins the splits (and the sink, if any) for its query heads --
-// or, past 256 splits, a second kernel does. Scores and sums in F32 (the CPU
+// or, when that is more than 32768 partial floats, a second kernel does. Scores and sums in F32 (the CPU
 // reference accumulates in Double; the 1e-4 + 1e-3 |e| tolerance applies).
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -146,6 +146,10 @@ struct AttentionArgs {
 // zero between launches (the joining CTA clears its entry).
 constexpr int MAX_JOINS = 1 << 16;
 constexpr int MAX_FUSED_SPLITS = 256;
+// The most partial floats (query heads x D x splits) the joining CTA reads:
+// past it one CTA per query head (the separate join) is faster -- C4's 4 x
+// 128 x 32 joins faster in the last split, C5's 8 x 256 x 64 slower.
+constexpr int MAX_FUSED_JOIN_FLOATS = 32768;
 __device__ unsigned join_arrivals[MAX_JOINS];
 
 // Row z's page table, key count and query position.
@@ -687,7 +691,8 @@ int launch_attention(const AttentionArgs& a, const float* sinks, float* out, cud
   // in shared memory and the arrival counts in their array; else its own
   // launch
   AttentionArgs args = a;
-  args.fused_join = a.splits <= MAX_FUSED_SPLITS && (long long)a.tokens * a.kv_heads <= MAX_JOINS;
+  args.fused_join = a.splits <= MAX_FUSED_SPLITS && (long long)a.tokens * a.kv_heads <= MAX_JOINS &&
+                    (long long)(a.q_heads / a.kv_heads) * D * a.splits <= MAX_FUSED_JOIN_FLOATS;
   args.sinks = sinks;
   args.out = out;
   args.records = records;

@@ -103,7 +103,9 @@ DRIFT_REGISTER(route_topk, route_kernel)
 
 // ---- experts' products ---------------------------------------------------------------------
 // Slot s (blockIdx.y) multiplies expert ids[s] of a [experts][rows][cols]
-// weight with x row s / divisor, prepared as for the plain product (the
+// weight with x row s / divisor -- or, past `routed_slots` (a shared expert's
+// slots, one per x row), x row s - routed_slots -- prepared as for the plain
+// product (the
 // tensor-core layout: row v's part of block c is the 112-byte slot v % 8 of
 // record (v / 8, c), its plane words in the order 0, 4, 1, 5, 2, 6, 3, 7).
 // GATED: a gate and an up weight of the same shape, out = silu(gate . x) *
@@ -115,8 +117,8 @@ template <typename T, int KS, bool GATED>
 __global__ void __launch_bounds__(256) experts_x22_kernel(
     const uint8_t* __restrict__ gate, const uint8_t* __restrict__ up, long long expert_bytes,
     const int* __restrict__ ids, const uint8_t* __restrict__ records, int divisor,
-    float* __restrict__ y, int rows, int cols, long long experts, long long first_expert,
-    int others_zero, int* error) {
+    int routed_slots, float* __restrict__ y, int rows, int cols, long long experts,
+    long long first_expert, int others_zero, int* error) {
   pdl_trigger();  // the next kernel may launch and wait for this one
   pdl_wait();     // what the kernels before this one wrote is visible
   constexpr int GROUPS = 8 / KS;
@@ -131,7 +133,7 @@ __global__ void __launch_bounds__(256) experts_x22_kernel(
   const long long expert = ids[slot] - first_expert;
   const int row0 = (blockIdx.x * GROUPS + group) * ROWS;
   const int blocks = cols / 32;
-  const int v = slot / divisor;
+  const int v = slot < routed_slots ? slot / divisor : slot - routed_slots;
   const uint8_t* record =
       records + (long long)(v / 8) * blocks * MMA_RECORD_BYTES + MMA_SLOT_BYTES * (v % 8);
   if (expert < 0 || expert >= experts) {
@@ -233,7 +235,8 @@ DRIFT_EXPERTS_REGISTER(Q4_1T, q4_1)
 
 template <typename T, bool GATED>
 static int launch_experts(const uint8_t* gate, const uint8_t* up, long long expert_bytes,
-                          const int* ids, const uint8_t* records, int divisor, float* y, int rows,
+                          const int* ids, const uint8_t* records, int divisor, int routed_slots,
+                          float* y, int rows,
                           int cols, int slots, long long experts, long long first_expert,
                           int others_zero, cudaStream_t stream) {
   const int blocks = cols / 32;
@@ -243,16 +246,16 @@ static int launch_experts(const uint8_t* gate, const uint8_t* up, long long expe
   int* error = device_error_word();
   if (ks == 4)
     DRIFT_CUDA(launch_pdl(experts_x22_kernel<T, 4, GATED>, grid, 256, 0, stream, gate, up,
-                          expert_bytes, ids, records, divisor, y, rows, cols, experts, first_expert,
-                          others_zero, error));
+                          expert_bytes, ids, records, divisor, routed_slots, y, rows, cols, experts,
+                          first_expert, others_zero, error));
   else if (ks == 2)
     DRIFT_CUDA(launch_pdl(experts_x22_kernel<T, 2, GATED>, grid, 256, 0, stream, gate, up,
-                          expert_bytes, ids, records, divisor, y, rows, cols, experts, first_expert,
-                          others_zero, error));
+                          expert_bytes, ids, records, divisor, routed_slots, y, rows, cols, experts,
+                          first_expert, others_zero, error));
   else
     DRIFT_CUDA(launch_pdl(experts_x22_kernel<T, 1, GATED>, grid, 256, 0, stream, gate, up,
-                          expert_bytes, ids, records, divisor, y, rows, cols, experts, first_expert,
-                          others_zero, error));
+                          expert_bytes, ids, records, divisor, routed_slots, y, rows, cols, experts,
+                          first_expert, others_zero, error));
   DRIFT_LAUNCHED("experts_x22");
   return 0;
 }
@@ -261,13 +264,13 @@ static int experts_common(bool gated, int x_dtype, const void* x, int64_t x_rows
                           int weight_dtype, const void* gate, const void* up, int64_t experts,
                           int64_t n, int64_t k, const int32_t* ids, int64_t slots, float* out,
                           int64_t first_expert, int others_zero, const void* prepared,
-                          cudaStream_t stream) {
+                          cudaStream_t stream, int shared_tail = 0) {
   const char* name = gated ? "expertsGatedLinear" : "expertsLinear";
   if (x_dtype != DRIFT_F32 && x_dtype != DRIFT_BF16)
     return invalid("%s takes F32 (or BF16) x, not %s", name, dtype_name(x_dtype));
   if (weight_dtype != DRIFT_Q8_0 && weight_dtype != DRIFT_Q4_0 && weight_dtype != DRIFT_Q4_1)
     return invalid("no kernels for %s experts yet", dtype_name(weight_dtype));
-  if (x_rows <= 0 || slots < 0 || slots % x_rows != 0)
+  if (x_rows <= 0 || slots < 0 || slots % x_rows != 0 || (shared_tail && slots < 2 * x_rows))
     return invalid("%s: x [%lld, %lld] for %lld slots of %lld", name, (long long)x_rows,
                    (long long)k, (long long)slots, (long long)k);
   const int64_t row = byte_size(weight_dtype, k);
@@ -287,14 +290,19 @@ static int experts_common(bool gated, int x_dtype, const void* x, int64_t x_rows
     records = static_cast<const uint8_t*>(w);
   }
   const long long expert_bytes = n * row;
-  const int divisor = int(slots / x_rows);
+  // with a shared tail, the last x_rows slots are one per x row
+  const int64_t routed = shared_tail ? slots - x_rows : slots;
+  const int divisor = int(routed / x_rows);
+  const int routed_slots = int(routed);
   const uint8_t* g = static_cast<const uint8_t*>(gate);
   const uint8_t* u = static_cast<const uint8_t*>(up);
 #define DRIFT_EXPERTS_CASE(T)                                                                   \
-  return gated ? launch_experts<T, true>(g, u, expert_bytes, ids, records, divisor, out, int(n), \
+  return gated ? launch_experts<T, true>(g, u, expert_bytes, ids, records, divisor,         \
+                                         routed_slots, out, int(n),                            \
                                          int(k), int(slots), experts, first_expert, others_zero, \
                                          stream)                                                \
-               : launch_experts<T, false>(g, g, expert_bytes, ids, records, divisor, out, int(n), \
+               : launch_experts<T, false>(g, g, expert_bytes, ids, records, divisor,       \
+                                          routed_slots, out, int(n),                           \
                                           int(k), int(slots), experts, first_expert,             \
                                           others_zero, stream);
   switch (weight_dtype) {
@@ -476,10 +484,12 @@ int drift_experts_gated_linear_local(int x_dtype, const void* x, int64_t x_rows,
                                      const void* gate, const void* up, int64_t experts,
                                      int64_t first_expert, int64_t n, int64_t k,
                                      const int32_t* ids, int64_t slots, float* out,
-                                     const void* prepared, drift_stream_t stream) {
+                                     const void* prepared, int shared_tail,
+                                     drift_stream_t stream) {
   if (first_expert < 0) return invalid("expertsGatedLinear: experts from %lld", (long long)first_expert);
   return experts_common(true, x_dtype, x, x_rows, weight_dtype, gate, up, experts, n, k, ids,
-                        slots, out, first_expert, 1, prepared, cudaStream_t(stream));
+                        slots, out, first_expert, 1, prepared, cudaStream_t(stream),
+                        shared_tail != 0);
 }
 
 int drift_moe_combine(const float* expert_out, const float* weights, int64_t tokens, int64_t k,

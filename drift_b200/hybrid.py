@@ -111,6 +111,15 @@ class MixtureLayer:
     shared_up: Stored
     shared_down: Stored          # [hidden, shared ffn]
     shared_router: torch.Tensor  # F32 [hidden]
+    # (gate, up, down) of experts + 1 experts, the last the shared expert,
+    # when the fields above are views of them (one launch serves both)
+    fused: Optional[tuple] = None
+
+
+def _expert_range(w: Stored, e0: int, e1: int) -> Stored:
+    """Experts [e0, e1) of an [experts, n, k] weight, as a view."""
+    per = w.data.numel() // w.shape[0]
+    return Stored(w.dtype, (e1 - e0,) + tuple(w.shape[1:]), w.data[e0 * per:e1 * per])
 
 
 @dataclass
@@ -213,14 +222,29 @@ class HybridWeights:
                                    f32(channels, c.conv_taps, scale=0.5),
                                    -torch.exp(torch.rand(dv, generator=g, device="cuda") * 2.5 - 1.0),
                                    f32(dv), norm(c.delta_dim), stored(c.hidden, value_width))
-            mixture = MixtureLayer(f32(c.experts, c.hidden, scale=0.02),
-                                   stored(c.expert_ffn, c.hidden, experts),
-                                   stored(c.expert_ffn, c.hidden, experts),
-                                   stored(c.hidden, c.expert_ffn, experts),
-                                   stored(c.shared_ffn, c.hidden, 1),
-                                   stored(c.shared_ffn, c.hidden, 1),
-                                   stored(c.hidden, c.shared_ffn),
-                                   f32(c.hidden, scale=0.02))
+            if world == 1 and c.shared_ffn == c.expert_ffn:
+                # the shared expert as expert `experts` of the routed weights
+                router = f32(c.experts, c.hidden, scale=0.02)
+                gate, up, down = (stored(c.expert_ffn, c.hidden, experts + 1),
+                                  stored(c.expert_ffn, c.hidden, experts + 1),
+                                  stored(c.hidden, c.expert_ffn, experts + 1))
+                last = _expert_range(down, experts, experts + 1)
+                mixture = MixtureLayer(router, _expert_range(gate, 0, experts),
+                                       _expert_range(up, 0, experts),
+                                       _expert_range(down, 0, experts),
+                                       _expert_range(gate, experts, experts + 1),
+                                       _expert_range(up, experts, experts + 1),
+                                       Stored(dtype, (c.hidden, c.shared_ffn), last.data),
+                                       f32(c.hidden, scale=0.02), (gate, up, down))
+            else:
+                mixture = MixtureLayer(f32(c.experts, c.hidden, scale=0.02),
+                                       stored(c.expert_ffn, c.hidden, experts),
+                                       stored(c.expert_ffn, c.hidden, experts),
+                                       stored(c.hidden, c.expert_ffn, experts),
+                                       stored(c.shared_ffn, c.hidden, 1),
+                                       stored(c.shared_ffn, c.hidden, 1),
+                                       stored(c.hidden, c.shared_ffn),
+                                       f32(c.hidden, scale=0.02))
             layers.append(HybridLayer(norm(c.hidden), mixer, norm(c.hidden), mixture))
         return HybridWeights(Stored(Q8_0, (c.vocab, c.hidden),
                                     synthetic.quantized_device(Q8_0, c.vocab, c.hidden, g)),
@@ -254,12 +278,8 @@ class HybridWeights:
                                    _columns(m.out, vh[0] * d, vh[1] * d))
             x = layer.mixture
             e0, e1 = part.experts
-
-            def experts(w: Stored) -> Stored:
-                per = w.data.numel() // w.shape[0]
-                return Stored(w.dtype, (e1 - e0,) + tuple(w.shape[1:]), w.data[e0 * per:e1 * per])
-
-            mixture = MixtureLayer(x.router, experts(x.gate), experts(x.up), experts(x.down),
+            mixture = MixtureLayer(x.router, _expert_range(x.gate, e0, e1),
+                                   _expert_range(x.up, e0, e1), _expert_range(x.down, e0, e1),
                                    x.shared_gate, x.shared_up, x.shared_down, x.shared_router)
             layers.append(HybridLayer(layer.input_norm, mixer, layer.post_norm, mixture))
         v0, v1 = part.vocab
@@ -342,13 +362,21 @@ class HybridDecoder:
         self.attended = torch.zeros(b, self.q_heads, c.head_dim, **f32)
         # mixture
         self.logits_router = torch.zeros(b, c.experts, **f32)
-        self.route_ids = torch.zeros(b, c.used, dtype=torch.int32, device="cuda")
+        # the routed slots, then one shared slot per sequence: the ids (the
+        # shared ones the shared expert's index in fused weights), the SwiGLU
+        # outputs and the down outputs as one buffer each, viewed per part
+        routed = b * c.used
+        self.all_ids = torch.full((routed + b,), c.experts, dtype=torch.int32, device="cuda")
+        self.route_ids = self.all_ids[:routed].view(b, c.used)
         self.route_weights = torch.zeros(b, c.used, **f32)
-        self.expert_gated = torch.zeros(b * c.used, c.expert_ffn, **f32)
-        self.expert_out = torch.zeros(b * c.used, c.hidden, **f32)
+        self.all_gated = torch.zeros(routed + b, c.expert_ffn, **f32)
+        self.expert_gated = self.all_gated[:routed]
+        self.all_out = torch.zeros(routed + b, c.hidden, **f32)
+        self.expert_out = self.all_out[:routed]
         self.shared_ids = torch.zeros(b, dtype=torch.int32, device="cuda")
-        self.shared_gated = torch.zeros(b, c.shared_ffn, **f32)
-        self.shared_out = torch.zeros(b, c.hidden, **f32)
+        self.shared_gated = (self.all_gated[routed:] if c.shared_ffn == c.expert_ffn
+                             else torch.zeros(b, c.shared_ffn, **f32))
+        self.shared_out = self.all_out[routed:]
         self.logits = torch.zeros(b, span(part.vocab), **f32)
         widest = max(c.hidden, self.value_width, self.q_heads * c.head_dim, c.shared_ffn)
         self.prepared = ops.prepared_x(b, widest)
@@ -413,6 +441,17 @@ class HybridDecoder:
         ops.route_linear(self.normed, mixture.router, self.logits_router, self.route_ids,
                          self.route_weights, P)
         next_norm = RowNorm(following, c.epsilon, 0.0, self.normed)
+        if self.exchange is None and mixture.fused is not None:
+            # routed and shared experts in one launch each: gate/up (the
+            # shared slots last, one per sequence), then down
+            gate, up, down = mixture.fused
+            ops.experts_gated_linear(self.normed, gate, up, self.all_ids, self.all_gated, 0, P,
+                                     shared_tail=True)
+            ops.experts_linear(self.all_gated, down, self.all_ids, self.all_out)
+            ops.moe_combine_norm(self.expert_out, self.route_weights,
+                                 SharedExpert(self.shared_out, self.normed, mixture.shared_router),
+                                 self.x, next_norm, P)
+            return
         if self.exchange is None:
             ops.experts_gated_linear(self.normed, mixture.gate, mixture.up,
                                      self.route_ids.view(-1), self.expert_gated, 0, P)

@@ -596,15 +596,18 @@ class CudaOps:
 
     def experts_gated_linear(self, x, gate: Stored, up: Stored, ids, out,
                              first_expert: Optional[int] = None,
-                             prepared: Optional[torch.Tensor] = None) -> None:
+                             prepared: Optional[torch.Tensor] = None,
+                             shared_tail: bool = False) -> None:
         """silu(gate · x) × (up · x) per slot, one launch (ExpertsOps.scala:188-198);
-        `first_expert` and `prepared` as for experts_linear."""
+        `first_expert` and `prepared` as for experts_linear. `shared_tail`
+        (with `first_expert`): the last rows-of-x slots are a shared expert's,
+        one per row of x, the slots before them routed."""
         _require(tuple(gate.shape) == tuple(up.shape) and gate.dtype == up.dtype,
                  f"expertsGatedLinear needs equal shapes, got {list(gate.shape)}, "
                  f"{list(up.shape)}")
         slots, n, k, rows = self._check_experts(x, gate, ids, out)
-        _require(prepared is None or first_expert is not None,
-                 "expertsGatedLinear: a prepared x goes with first_expert")
+        _require((prepared is None and not shared_tail) or first_expert is not None,
+                 "expertsGatedLinear: a prepared x or a shared tail goes with first_expert")
         if first_expert is None:
             status = self.lib.drift_experts_gated_linear(
                 _x_dtype("expertsGatedLinear", x), _ptr(x), rows, gate.dtype, _ptr(gate.data),
@@ -613,7 +616,7 @@ class CudaOps:
             status = self.lib.drift_experts_gated_linear_local(
                 _x_dtype("expertsGatedLinear", x), _ptr(x), rows, gate.dtype, _ptr(gate.data),
                 _ptr(up.data), gate.shape[0], first_expert, n, k, _ptr(ids), slots, _ptr(out),
-                _ptr(prepared), self._stream())
+                _ptr(prepared), int(shared_tail), self._stream())
         check("drift_experts_gated_linear", status)
 
     @staticmethod

@@ -238,11 +238,16 @@ int drift_experts_linear_local(int x_dtype, const void* x, int64_t x_rows, int w
                                const void* weight, int64_t experts, int64_t first_expert,
                                int64_t n, int64_t k, const int32_t* ids, int64_t slots,
                                float* out, const void* prepared, drift_stream_t stream);
+/* With shared_tail, the last x_rows slots are a shared expert's, one per x
+ * row in order (its weights one more expert of gate and up), the slots
+ * before them routed (slots - x_rows) / x_rows to a row: the routed and the
+ * shared experts' products in one launch. */
 int drift_experts_gated_linear_local(int x_dtype, const void* x, int64_t x_rows, int weight_dtype,
                                      const void* gate, const void* up, int64_t experts,
                                      int64_t first_expert, int64_t n, int64_t k,
                                      const int32_t* ids, int64_t slots, float* out,
-                                     const void* prepared, drift_stream_t stream);
+                                     const void* prepared, int shared_tail,
+                                     drift_stream_t stream);
 
 /* ---- prepared x (new) ------------------------------------------------------
  * A product streams its weights against x's "records" (x per 32-value block as

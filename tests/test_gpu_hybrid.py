@@ -6,6 +6,7 @@ weights, caches and states downloaded from the GPU. Held to the benchmark's
 1e-4 absolute + 1e-3 relative on the logits after four layers (three DeltaNet,
 one gated full attention, each with a mixture of experts)."""
 
+import dataclasses
 import math
 
 import numpy as np
@@ -22,6 +23,9 @@ pytestmark = pytest.mark.gpu
 SMALL = HybridConfig(layers=4, hidden=256, delta_key_heads=2, delta_value_heads=4, delta_dim=32,
                      q_heads=4, kv_heads=2, head_dim=64, rotary=16, theta=1e6, experts=16,
                      used=4, expert_ffn=64, shared_ffn=64, vocab=500)
+# a shared expert of another width: its own launches (SMALL's rides in the
+# routed experts' launches, as one more expert of their weights)
+APART = dataclasses.replace(SMALL, shared_ffn=128)
 
 
 def host(t):
@@ -98,9 +102,9 @@ def reference_step(c, w, d, ids, positions):
     return oracle.linear(w.lm_head.dtype, normed, host(w.lm_head.data), c.vocab, c.hidden)
 
 
+@pytest.mark.parametrize("c", [SMALL, APART], ids=["shared-in-experts", "shared-apart"])
 @pytest.mark.parametrize("batch", [1, 3])
-def test_hybrid_step_matches_the_oracle(batch):
-    c = SMALL
+def test_hybrid_step_matches_the_oracle(c, batch):
     ops = CudaOps()
     weights = HybridWeights.random(c, seed=7)
     decoder = HybridDecoder(ops, c, weights, batch=batch, context=64)

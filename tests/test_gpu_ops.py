@@ -235,6 +235,31 @@ def test_experts_linear_and_gated(ops, dtype):
         assert ok, summary
 
 
+def test_shared_expert_rides_in_the_routed_launch(ops):
+    """A shared tail: the routed slots, then one slot per row of x for the
+    shared expert (one more expert of the weights), in one launch -- bit for
+    bit the routed launch and the shared expert's launch apart."""
+    rng = np.random.default_rng(62)
+    experts, ffn, hidden, used, tokens = 8, 128, 1024, 3, 5
+    dtype = oracle.Q4_1
+    sg = Stored.upload(dtype, (experts + 1, ffn, hidden),
+                       synthetic.quantized(rng, dtype, (experts + 1) * ffn, hidden))
+    su = Stored.upload(dtype, (experts + 1, ffn, hidden),
+                       synthetic.quantized(rng, dtype, (experts + 1) * ffn, hidden))
+    x = dev((0.05 * synthetic.gaussian(rng, tokens, hidden)).astype(np.float32))
+    routed_ids = rng.integers(0, experts, tokens * used).astype(np.int32)
+    ids = np.concatenate([routed_ids, np.full(tokens, experts, np.int32)])
+    together = torch.empty(tokens * (used + 1), ffn, device="cuda")
+    ops.experts_gated_linear(x, sg, su, dev(ids), together, first_expert=0, shared_tail=True)
+    routed = torch.empty(tokens * used, ffn, device="cuda")
+    ops.experts_gated_linear(x, sg, su, dev(routed_ids), routed)
+    shared = torch.empty(tokens, ffn, device="cuda")
+    ops.experts_gated_linear(x, sg, su, dev(np.full(tokens, experts, np.int32)), shared)
+    assert torch.equal(together[:tokens * used], routed)
+    assert torch.equal(together[tokens * used:], shared)
+    assert ops.take_device_error() == 0
+
+
 def test_experts_bad_id_is_flagged(ops):
     rng = np.random.default_rng(61)
     w = Stored.upload(oracle.Q4_1, (2, 64, 64), synthetic.quantized(rng, oracle.Q4_1, 128, 64))
