@@ -472,6 +472,7 @@ __global__ void __launch_bounds__(SPLIT_THREADS) attention_split_kernel(const At
     const unsigned at = key_at[k];
     if (at != NONE) cp_async16(ks + T::key_chunk(k, c), a.keys + 8 * ((long long)at + c));
   }
+  asm volatile("cp.async.commit_group;" ::: "memory");  // the keys: group 1
   // values, a 16-byte run of 8 positions of one dimension at a time (a run
   // never crosses a page: pages are multiples of 16 positions)
   const long long column = ps / 8;  // 16-byte units from one dimension to the next
@@ -499,7 +500,8 @@ __global__ void __launch_bounds__(SPLIT_THREADS) attention_split_kernel(const At
       *reinterpret_cast<uint4*>(to) = *reinterpret_cast<const uint4*>(run);
     }
   }
-  asm volatile("cp.async.commit_group;\n\tcp.async.wait_all;" ::: "memory");
+  // the values (group 2) keep coming while the keys are scored
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 1;" ::: "memory");
   __syncthreads();
 
   // scores of this warp's keys: s[j] holds rows (g, g + 8), keys
@@ -584,6 +586,7 @@ __global__ void __launch_bounds__(SPLIT_THREADS) attention_split_kernel(const At
     frags[(warp * 2) * 32 + lane] = h;
     frags[(warp * 2 + 1) * 32 + lane] = w;
   }
+  asm volatile("cp.async.wait_all;" ::: "memory");  // the values are in
   __syncthreads();
 
   // p.v for this warp's dimension tiles [ND w / 8, ND (w + 1) / 8)
