@@ -275,21 +275,17 @@ __global__ void rope_kernel(const float* __restrict__ x, const int* __restrict__
 DRIFT_REGISTER(rope_f32, rope_kernel)
 
 // ---- products with F32 weights (routers) -----------------------------------------------------
-// One warp per (row, vector): float4 loads when k is a multiple of 4, float
-// sums in a fixed order, then shuffles.
 // F32 weights (routers, DeltaNet's a and b): a CTA of 256 threads per (row,
 // vector), the row in 16-byte loads, every load of a thread issued before
 // its first use (a 4096-value row is one round trip), summed per thread in
-// column order, then the block's fixed tree.
+// column order, then the block's fixed tree. `weight` is the matrix's first
+// row (whose alignment picks the path, so a row sums the same way in either
+// kernel below), w the row's.
 template <bool BF16>
-__global__ void __launch_bounds__(256) matvec_f32_kernel(const void* __restrict__ x,
-                                                         const float* __restrict__ weight,
-                                                         float* __restrict__ y, int m, int n, int k) {
-  pdl_trigger();  // the next kernel may launch and wait for this one
-  pdl_wait();     // what the kernels before this one wrote is visible
-  __shared__ float partial[32];
-  const int row = blockIdx.x % n, vector = blockIdx.x / n;
-  const float* w = weight + (long long)row * k;
+__device__ __forceinline__ float f32_row_dot(const void* __restrict__ x,
+                                             const float* __restrict__ weight,
+                                             const float* __restrict__ w, int vector, int k,
+                                             float* partial) {
   float sum = 0.0f;
   if (!BF16 && k % 4 == 0 && (reinterpret_cast<uintptr_t>(weight) & 15) == 0 &&
       (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
@@ -321,12 +317,53 @@ __global__ void __launch_bounds__(256) matvec_f32_kernel(const void* __restrict_
       sum = fmaf(w[c], xv, sum);
     }
   }
-  const float total = block_sum(sum, partial);
+  return block_sum(sum, partial);
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(256) matvec_f32_kernel(const void* __restrict__ x,
+                                                         const float* __restrict__ weight,
+                                                         float* __restrict__ y, int m, int n, int k) {
+  pdl_trigger();  // the next kernel may launch and wait for this one
+  pdl_wait();     // what the kernels before this one wrote is visible
+  __shared__ float partial[32];
+  const int row = blockIdx.x % n, vector = blockIdx.x / n;
+  const float total = f32_row_dot<BF16>(x, weight, weight + (long long)row * k, vector, k, partial);
   if (threadIdx.x == 0) y[(long long)vector * n + row] = total;
+}
+
+// Up to four F32 products of the same x in one launch: CTA (vector, r) takes
+// row r of the matrices' rows laid end to end.
+constexpr int MAX_F32_MATRICES = 4;
+struct F32Launch {
+  const float* weight[MAX_F32_MATRICES];
+  float* y[MAX_F32_MATRICES];
+  int n[MAX_F32_MATRICES];
+  int end[MAX_F32_MATRICES];  // matrix i holds rows [end[i - 1], end[i])
+  int count;
+};
+
+template <bool BF16>
+__global__ void __launch_bounds__(256) matvec_f32_many_kernel(const void* __restrict__ x,
+                                                              const __grid_constant__ F32Launch L,
+                                                              int k) {
+  pdl_trigger();  // the next kernel may launch and wait for this one
+  pdl_wait();     // what the kernels before this one wrote is visible
+  __shared__ float partial[32];
+  const int rows = L.end[L.count - 1];
+  const int r = blockIdx.x % rows, vector = blockIdx.x / rows;
+  int i = 0;
+  while (i + 1 < L.count && r >= L.end[i]) ++i;
+  const int row = r - (i > 0 ? L.end[i - 1] : 0);
+  const float total =
+      f32_row_dot<BF16>(x, L.weight[i], L.weight[i] + (long long)row * k, vector, k, partial);
+  if (threadIdx.x == 0) L.y[i][(long long)vector * L.n[i] + row] = total;
 }
 
 DRIFT_REGISTER(matvec_f32_f32x, matvec_f32_kernel<false>)
 DRIFT_REGISTER(matvec_f32_bf16x, matvec_f32_kernel<true>)
+DRIFT_REGISTER(matvec_f32_many_f32x, matvec_f32_many_kernel<false>)
+DRIFT_REGISTER(matvec_f32_many_bf16x, matvec_f32_many_kernel<true>)
 
 int matvec_f32_weights(int x_dtype, const void* x, const float* weight, float* y, int64_t m,
                        int64_t n, int64_t k, cudaStream_t stream) {
@@ -341,6 +378,36 @@ int matvec_f32_weights(int x_dtype, const void* x, const float* weight, float* y
     DRIFT_CUDA(launch_pdl(matvec_f32_kernel<false>, grid, 256, 0, stream, x, weight, y, int(m),
                           int(n), int(k)));
   DRIFT_LAUNCHED("matvec_f32");
+  return 0;
+}
+
+// F32 products of the same x (count <= 4, no empty matrix), one launch: each
+// row the bits of matvec_f32_weights.
+int matvec_f32_many(int x_dtype, const void* x, int count, const float* const* weights,
+                    float* const* ys, const int64_t* ns, int64_t m, int64_t k,
+                    cudaStream_t stream) {
+  if (count < 1 || count > MAX_F32_MATRICES) return invalid("%d F32 products in one launch", count);
+  F32Launch launch = {};
+  long long rows = 0;
+  for (int i = 0; i < count; ++i) {
+    if (ns[i] <= 0) return invalid("an empty F32 product in a shared launch");
+    rows += ns[i];
+    launch.weight[i] = weights[i];
+    launch.y[i] = ys[i];
+    launch.n[i] = int(ns[i]);
+    launch.end[i] = int(rows);
+  }
+  launch.count = count;
+  const long long ctas = m * rows;
+  if (rows > 0x7fffffffll || ctas > 0x7fffffffll)
+    return invalid("F32 products of %lld rows x %lld vectors", rows, (long long)m);
+  if (x_dtype == DRIFT_BF16)
+    DRIFT_CUDA(launch_pdl(matvec_f32_many_kernel<true>, unsigned(ctas), 256, 0, stream, x, launch,
+                          int(k)));
+  else
+    DRIFT_CUDA(launch_pdl(matvec_f32_many_kernel<false>, unsigned(ctas), 256, 0, stream, x,
+                          launch, int(k)));
+  DRIFT_LAUNCHED("matvec_f32_many");
   return 0;
 }
 

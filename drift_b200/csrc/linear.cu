@@ -4,6 +4,8 @@
 // re-decided for B200.
 #include <cuda_runtime.h>
 
+#include <vector>
+
 #include "common.cuh"
 #include "quant.cuh"
 #include "registry.cuh"
@@ -16,6 +18,9 @@ int matvec_prepared(int weight_dtype, const void* weight, const uint8_t* records
 size_t mma_workspace_bytes(int64_t m, int64_t k);
 int prepare_x_mma(int x_dtype, const void* x, int64_t m, int64_t k, uint8_t* records,
                   cudaStream_t stream);
+int matvec_f32_many(int x_dtype, const void* x, int count, const float* const* weights,
+                    float* const* ys, const int64_t* ns, int64_t m, int64_t k,
+                    cudaStream_t stream);
 int matvec_f32_weights(int x_dtype, const void* x, const float* weight, float* y, int64_t m,
                        int64_t n, int64_t k, cudaStream_t stream);
 bool tc_supports(int weight_dtype, const void* weight, int64_t k);
@@ -111,14 +116,58 @@ static int linears(int x_dtype, const void* x, const void* prepared, int count,
   uint8_t* tc_region = static_cast<uint8_t*>(w) + records_bytes;
   if (quantized && !prepared)  // one preparation for all
     DRIFT_TRY(prepare_x_mma(x_dtype, x, m, k, static_cast<uint8_t*>(w), s));
-  // streamed products of one type that fit one balanced launch take it
-  // together (the same bits as one by one)
-  bool together = quantized && !tensor_cores && count >= 2;
-  for (int i = 1; together && i < count; ++i) together = weight_dtypes[i] == weight_dtypes[0];
-  if (together && ring_many_fits(weight_dtypes[0], count, weights, ns, k))
-    return matvec_ring_many(weight_dtypes[0], count, weights, records, outs, ns, k, m, s);
+  // Shared launches, each product's bits those of its own launch: streamed
+  // products of one type that fit one balanced launch (up to 4) take it
+  // together, and the F32 products one launch (up to 4).
+  constexpr int SHARED = 4;
+  auto streamed = [&](int i) {
+    return weight_dtypes[i] != DRIFT_F32 &&
+           !(m >= GEMM_MINIMUM_ROWS && tc_supports(weight_dtypes[i], weights[i], k));
+  };
+  std::vector<char> done(size_t(count), 0);
   for (int i = 0; i < count; ++i) {
-    if (ns[i] == 0) continue;
+    if (done[i] || ns[i] == 0 || !streamed(i)) continue;
+    int which[SHARED], c = 0;
+    const void* w[SHARED];
+    float* o[SHARED];
+    int64_t n[SHARED];
+    for (int j = i; j < count && c < SHARED; ++j)
+      if (!done[j] && ns[j] > 0 && streamed(j) && weight_dtypes[j] == weight_dtypes[i]) {
+        which[c] = j;
+        w[c] = weights[j];
+        o[c] = outs[j];
+        n[c] = ns[j];
+        ++c;
+      }
+    if (c < 2 || !ring_many_fits(weight_dtypes[i], c, w, n, k)) continue;
+    DRIFT_TRY(matvec_ring_many(weight_dtypes[i], c, w, records, o, n, k, m, s));
+    for (int j = 0; j < c; ++j) done[which[j]] = 1;
+  }
+  {
+    int which[SHARED], c = 0;
+    const float* w[SHARED];
+    float* o[SHARED];
+    int64_t n[SHARED];
+    auto flush = [&]() -> int {
+      if (c >= 2) {
+        DRIFT_TRY(matvec_f32_many(x_dtype, x, c, w, o, n, m, k, s));
+        for (int j = 0; j < c; ++j) done[which[j]] = 1;
+      }
+      c = 0;
+      return 0;
+    };
+    for (int i = 0; i < count; ++i) {
+      if (done[i] || ns[i] == 0 || weight_dtypes[i] != DRIFT_F32) continue;
+      which[c] = i;
+      w[c] = static_cast<const float*>(weights[i]);
+      o[c] = outs[i];
+      n[c] = ns[i];
+      if (++c == SHARED) DRIFT_TRY(flush());
+    }
+    DRIFT_TRY(flush());
+  }
+  for (int i = 0; i < count; ++i) {
+    if (done[i] || ns[i] == 0) continue;
     if (weight_dtypes[i] == DRIFT_F32)
       DRIFT_TRY(matvec_f32_weights(x_dtype, x, static_cast<const float*>(weights[i]), outs[i], m,
                                    ns[i], k, s));

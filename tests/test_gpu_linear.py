@@ -122,6 +122,27 @@ def test_linears_share_one_preparation(ops, dtype):
         assert torch.equal(alone, t)
 
 
+@pytest.mark.parametrize("m", [1, 2, 5])
+def test_mixed_linears_share_launches(ops, m):
+    """A list of two Q4_1, two F32 and one Q8_0 products of one x (a DeltaNet
+    layer's qkv, z, a, b, plus another type): the Q4_1 pair shares a launch,
+    the F32 pair another, and every output is bit for bit its product alone."""
+    rng = np.random.default_rng(13 + m)
+    k = 2048
+    ws = [Stored.upload(oracle.Q4_1, (384, k), synthetic.quantized(rng, oracle.Q4_1, 384, k)),
+          Stored.upload(oracle.Q4_1, (128, k), synthetic.quantized(rng, oracle.Q4_1, 128, k)),
+          torch.from_numpy((0.02 * rng.standard_normal((16, k))).astype(np.float32)).cuda(),
+          torch.from_numpy((0.02 * rng.standard_normal((16, k))).astype(np.float32)).cuda(),
+          Stored.upload(oracle.Q8_0, (96, k), synthetic.quantized(rng, oracle.Q8_0, 96, k))]
+    x = torch.from_numpy(synthetic.gaussian(rng, m, k)).cuda()
+    together = [torch.empty(m, w.shape[0], device="cuda") for w in ws]
+    ops.linears(x, ws, together)
+    for w, t in zip(ws, together):
+        alone = torch.empty_like(t)
+        ops.linear(x, w, alone)
+        assert torch.equal(alone, t)
+
+
 def test_linear_rows_do_not_depend_on_batch(ops):
     """A row's sum is the same whether it comes alone or with 7 others."""
     rng = np.random.default_rng(12)
