@@ -219,37 +219,77 @@ def run_gpu(args) -> dict | None:
     barrier()
     torch.cuda.synchronize()
 
-    # e2e: the public C ABI with host buffers, copies inside the timed region
-    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    # e2e: the public C ABI with host buffers, copies inside the timed region.
+    # As a host of the library pipelines a step: x in on one stream, the
+    # product on a second, y out on a third, ordered per buffer by events (a
+    # copy in waits for the last product that read its x buffer, a product
+    # for its x and for the last copy out of its y buffer), so the copy
+    # engines run while the products do. Every byte of every step is copied.
+    def created(call, name):
+        handle = ctypes.c_void_p()
+        check(name, call(ctypes.byref(handle)))
+        return handle
+
+    def wait(stream, event):
+        check("drift_stream_wait_event", lib.drift_stream_wait_event(stream, event))
+
+    def record(event, stream):
+        check("drift_event_record", lib.drift_event_record(event, stream))
+
+    s_in, s_run, s_out = (created(lib.drift_stream_create, "drift_stream_create")
+                          for _ in range(3))
+    keys = [(b, n, k) for b in BATCHES for n, k in SHAPES]
+    copied_in, computed, copied_out = (
+        {key: created(lib.drift_event_create, "drift_event_create") for key in keys}
+        for _ in range(3))
 
     def e2e_step():
-        for b in BATCHES:
-            for n, k in SHAPES:
-                hx, dx = host_x[(b, n, k)], xs[(b, n, k)]
-                check("drift_memcpy_async", lib.drift_memcpy_async(
-                    ctypes.c_void_p(dx.data_ptr()), ctypes.c_void_p(hx.data_ptr()),
-                    hx.numel() * 2, 1, s))
-                w = weights[(n, k)]
-                check("drift_linear", lib.drift_linear(
-                    30, ctypes.c_void_p(dx.data_ptr()), Q4_1, ctypes.c_void_p(w.data.data_ptr()),
-                    ctypes.c_void_p(ys[(b, n, k)].data_ptr()), b, n, k, s))
-                hy = host_y[(b, n, k)]
-                check("drift_memcpy_async", lib.drift_memcpy_async(
-                    ctypes.c_void_p(hy.data_ptr()), ctypes.c_void_p(ys[(b, n, k)].data_ptr()),
-                    hy.numel() * 4, 2, s))
+        for key in keys:
+            b, n, k = key
+            hx, dx, y, hy = host_x[key], xs[key], ys[key], host_y[key]
+            wait(s_in, computed[key])
+            check("drift_memcpy_async", lib.drift_memcpy_async(
+                ctypes.c_void_p(dx.data_ptr()), ctypes.c_void_p(hx.data_ptr()),
+                hx.numel() * 2, 1, s_in))
+            record(copied_in[key], s_in)
+            wait(s_run, copied_in[key])
+            wait(s_run, copied_out[key])
+            w = weights[(n, k)]
+            check("drift_linear", lib.drift_linear(
+                30, ctypes.c_void_p(dx.data_ptr()), Q4_1, ctypes.c_void_p(w.data.data_ptr()),
+                ctypes.c_void_p(y.data_ptr()), b, n, k, s_run))
+            record(computed[key], s_run)
+            wait(s_out, computed[key])
+            check("drift_memcpy_async", lib.drift_memcpy_async(
+                ctypes.c_void_p(hy.data_ptr()), ctypes.c_void_p(y.data_ptr()),
+                hy.numel() * 4, 2, s_out))
+            record(copied_out[key], s_out)
 
     for _ in range(max(1, args.warmup)):
         e2e_step()
-    torch.cuda.synchronize()
+    check("drift_device_synchronize", lib.drift_device_synchronize())
     barrier()
     torch.cuda.synchronize()
-    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e_start.record()
+    e_start, e_end, drained = (created(lib.drift_event_create, "drift_event_create")
+                               for _ in range(3))
+    record(e_start, s_run)
+    wait(s_in, e_start)
+    wait(s_out, e_start)
     for _ in range(args.steps):
         e2e_step()
-    e_end.record()
-    torch.cuda.synchronize()
-    e2e_ms = e_start.elapsed_time(e_end)
+    record(drained, s_out)  # the last copy out (the products waited for every copy in)
+    wait(s_run, drained)
+    record(e_end, s_run)
+    check("drift_device_synchronize", lib.drift_device_synchronize())
+    e2e_elapsed = ctypes.c_float()
+    check("drift_event_elapsed_time",
+          lib.drift_event_elapsed_time(ctypes.byref(e2e_elapsed), e_start, e_end))
+    e2e_ms = float(e2e_elapsed.value)
+    for handle in [e_start, e_end, drained, *copied_in.values(), *computed.values(),
+                   *copied_out.values()]:
+        check("drift_event_destroy", lib.drift_event_destroy(handle))
+    for handle in (s_in, s_run, s_out):
+        check("drift_stream_destroy", lib.drift_stream_destroy(handle))
     h2d = sum(b * k * 2 for b in BATCHES for n, k in SHAPES)
     d2h = sum(b * n * 4 for b in BATCHES for n, k in SHAPES)
 

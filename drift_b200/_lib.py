@@ -50,6 +50,7 @@ SIGNATURES = {
     "drift_event_create": (_i32, [_pp]),
     "drift_event_destroy": (_i32, [_p]),
     "drift_event_record": (_i32, [_p, _p]),
+    "drift_stream_wait_event": (_i32, [_p, _p]),
     "drift_event_synchronize": (_i32, [_p]),
     "drift_event_elapsed_time": (_i32, [ctypes.POINTER(ctypes.c_float), _p, _p]),
     "drift_module_load_data": (_i32, [_pp, _p]),

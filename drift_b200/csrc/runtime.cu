@@ -249,6 +249,11 @@ int drift_event_record(drift_event_t event, drift_stream_t stream) {
   return cuda_status(cudaEventRecord(cudaEvent_t(event), cudaStream_t(stream)), "cudaEventRecord");
 }
 
+int drift_stream_wait_event(drift_stream_t stream, drift_event_t event) {
+  return cuda_status(cudaStreamWaitEvent(cudaStream_t(stream), cudaEvent_t(event), 0),
+                     "cudaStreamWaitEvent");
+}
+
 int drift_event_synchronize(drift_event_t event) {
   return cuda_status(cudaEventSynchronize(cudaEvent_t(event)), "cudaEventSynchronize");
 }

@@ -85,6 +85,11 @@ int drift_event_destroy(drift_event_t event);
 int drift_event_record(drift_event_t event, drift_stream_t stream);
 int drift_event_synchronize(drift_event_t event);
 int drift_event_elapsed_time(float* milliseconds, drift_event_t start, drift_event_t end);
+/* New (the reference's binding has no counterpart; hipStreamWaitEvent is the
+ * HIP call): work queued on `stream` after this waits for the event's last
+ * record -- how a host overlaps copies on one stream with products on
+ * another. */
+int drift_stream_wait_event(drift_stream_t stream, drift_event_t event);
 
 /* hipModuleLoadData / Unload / GetFunction (HipRuntime.scala:103-106): a cubin
  * or fatbin image built for sm_100a. drift_module_get_function with module NULL
