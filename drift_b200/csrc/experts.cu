@@ -109,16 +109,19 @@ DRIFT_REGISTER(route_topk, route_kernel)
 // tensor-core layout: row v's part of block c is the 112-byte slot v % 8 of
 // record (v / 8, c), its plane words in the order 0, 4, 1, 5, 2, 6, 3, 7).
 // GATED: a gate and an up weight of the same shape, out = silu(gate . x) *
-// (up . x). The 8 warps of a CTA are 8 / KS row groups of KS k-splits: warp
+// (up . x). XQ (plain products, one x row a slot): each CTA prepares its
+// slot's F32 x row itself, into shared memory (x22_record_slot: the bytes
+// of the preparation launch it replaces), rather than read records. The 8
+// warps of a CTA are 8 / KS row groups of KS k-splits: warp
 // (group, kw) takes 4 rows of its group and, lane l, blocks 32 kw + l,
 // 32 (kw + KS) + l, ...; the k-splits' sums meet in shared memory in a fixed
 // order.
-template <typename T, int KS, bool GATED>
+template <typename T, int KS, bool GATED, bool XQ = false>
 __global__ void __launch_bounds__(256) experts_x22_kernel(
     const uint8_t* __restrict__ gate, const uint8_t* __restrict__ up, long long expert_bytes,
     const int* __restrict__ ids, const uint8_t* __restrict__ records, int divisor,
     int routed_slots, float* __restrict__ y, int rows, int cols, long long experts,
-    long long first_expert, int others_zero, int* error) {
+    long long first_expert, int others_zero, int* error, const float* __restrict__ x) {
   pdl_trigger();  // the next kernel may launch and wait for this one
   pdl_wait();     // what the kernels before this one wrote is visible
   constexpr int GROUPS = 8 / KS;
@@ -134,8 +137,11 @@ __global__ void __launch_bounds__(256) experts_x22_kernel(
   const int row0 = (blockIdx.x * GROUPS + group) * ROWS;
   const int blocks = cols / 32;
   const int v = slot < routed_slots ? slot / divisor : slot - routed_slots;
+  extern __shared__ __align__(16) uint8_t x_slots[];  // XQ: [blocks][112 bytes]
   const uint8_t* record =
-      records + (long long)(v / 8) * blocks * MMA_RECORD_BYTES + MMA_SLOT_BYTES * (v % 8);
+      XQ ? x_slots
+         : records + (long long)(v / 8) * blocks * MMA_RECORD_BYTES + MMA_SLOT_BYTES * (v % 8);
+  constexpr int STRIDE = XQ ? MMA_SLOT_BYTES : MMA_RECORD_BYTES;  // from one block to the next
   if (expert < 0 || expert >= experts) {
     if (!others_zero && threadIdx.x == 0 && blockIdx.x == 0 && error) atomicCAS(error, 0, 1);
     for (int r = threadIdx.x; r < GROUPS * ROWS; r += blockDim.x) {
@@ -144,6 +150,15 @@ __global__ void __launch_bounds__(256) experts_x22_kernel(
     }
     return;
   }
+  if constexpr (XQ) {
+    for (int c = warp; c < blocks; c += 8)
+      x22_record_slot(x[(long long)v * cols + 32 * c + lane], x_slots + c * MMA_SLOT_BYTES);
+    __syncthreads();
+  }
+  auto load = [](const uint4* a) {
+    if constexpr (XQ) return *a;
+    else return __ldg(a);
+  };
   // the warp's rows side by side: each block of x is read once for all of
   // them, and every row's weights of the block are in flight together; a
   // row's sum is its lane's blocks in order, then the warp's lanes
@@ -161,12 +176,12 @@ __global__ void __launch_bounds__(256) experts_x22_kernel(
       load_block<T>(gate_base + row * row_bytes, c, wg[r]);
       if (GATED) load_block<T>(up_base + row * row_bytes, c, wu[r]);
     }
-    const uint4* rec = reinterpret_cast<const uint4*>(record + (long long)c * MMA_RECORD_BYTES);
+    const uint4* rec = reinterpret_cast<const uint4*>(record + (long long)c * STRIDE);
     // stored words 0..7 of a plane hold words 0, 4, 1, 5, 2, 6, 3, 7
     uint32_t planes[24];
 #pragma unroll
     for (int p = 0; p < 3; ++p) {
-      const uint4 q0 = __ldg(rec + 2 * p), q1 = __ldg(rec + 2 * p + 1);
+      const uint4 q0 = load(rec + 2 * p), q1 = load(rec + 2 * p + 1);
       planes[8 * p + 0] = q0.x;
       planes[8 * p + 4] = q0.y;
       planes[8 * p + 1] = q0.z;
@@ -176,7 +191,7 @@ __global__ void __launch_bounds__(256) experts_x22_kernel(
       planes[8 * p + 3] = q1.z;
       planes[8 * p + 7] = q1.w;
     }
-    const uint4 tail = __ldg(rec + 6);  // s, sum X at bytes 96, 100
+    const uint4 tail = load(rec + 6);  // s, sum X at bytes 96, 100
 #pragma unroll
     for (int r = 0; r < ROWS; ++r) {
       int a0, a1, a2;
@@ -238,24 +253,40 @@ static int launch_experts(const uint8_t* gate, const uint8_t* up, long long expe
                           const int* ids, const uint8_t* records, int divisor, int routed_slots,
                           float* y, int rows,
                           int cols, int slots, long long experts, long long first_expert,
-                          int others_zero, cudaStream_t stream) {
+                          int others_zero, cudaStream_t stream, const float* xq = nullptr) {
   const int blocks = cols / 32;
   const int ks = blocks >= 128 ? 4 : (blocks >= 64 ? 2 : 1);
   const int rows_per_cta = 4 * (8 / ks);
   const dim3 grid(unsigned((rows + rows_per_cta - 1) / rows_per_cta), unsigned(slots));
   int* error = device_error_word();
+  if constexpr (!GATED) {
+    if (xq) {
+      // x prepared in the kernel: one x row a slot, blocks x 112 bytes of it
+      const int smem = blocks * MMA_SLOT_BYTES;
+#define DRIFT_EXPERTS_XQ(KS)                                                                     \
+  DRIFT_CUDA(launch_pdl(experts_x22_kernel<T, KS, false, true>, grid, 256, smem, stream, gate, up, \
+                        expert_bytes, ids, records, divisor, routed_slots, y, rows, cols, experts,  \
+                        first_expert, others_zero, error, xq))
+      if (ks == 4) DRIFT_EXPERTS_XQ(4);
+      else if (ks == 2) DRIFT_EXPERTS_XQ(2);
+      else DRIFT_EXPERTS_XQ(1);
+#undef DRIFT_EXPERTS_XQ
+      DRIFT_LAUNCHED("experts_x22");
+      return 0;
+    }
+  }
   if (ks == 4)
     DRIFT_CUDA(launch_pdl(experts_x22_kernel<T, 4, GATED>, grid, 256, 0, stream, gate, up,
                           expert_bytes, ids, records, divisor, routed_slots, y, rows, cols, experts,
-                          first_expert, others_zero, error));
+                          first_expert, others_zero, error, nullptr));
   else if (ks == 2)
     DRIFT_CUDA(launch_pdl(experts_x22_kernel<T, 2, GATED>, grid, 256, 0, stream, gate, up,
                           expert_bytes, ids, records, divisor, routed_slots, y, rows, cols, experts,
-                          first_expert, others_zero, error));
+                          first_expert, others_zero, error, nullptr));
   else
     DRIFT_CUDA(launch_pdl(experts_x22_kernel<T, 1, GATED>, grid, 256, 0, stream, gate, up,
                           expert_bytes, ids, records, divisor, routed_slots, y, rows, cols, experts,
-                          first_expert, others_zero, error));
+                          first_expert, others_zero, error, nullptr));
   DRIFT_LAUNCHED("experts_x22");
   return 0;
 }
@@ -283,7 +314,14 @@ static int experts_common(bool gated, int x_dtype, const void* x, int64_t x_rows
   if (!x || !gate || (gated && !up) || !ids || !out) return invalid("%s: a null tensor", name);
   if (slots > 65535) return invalid("%s: %lld slots in one launch", name, (long long)slots);
   const uint8_t* records = static_cast<const uint8_t*>(prepared);
-  if (!records) {
+  // one F32 x row a slot (a down product): each CTA prepares its row itself,
+  // the launch that would prepare x is left out (up to 128 blocks: 14 KB of
+  // shared memory)
+  const float* xq = !records && !gated && !shared_tail && x_dtype == DRIFT_F32 &&
+                            x_rows == slots && k / 32 <= 128
+                        ? static_cast<const float*>(x)
+                        : nullptr;
+  if (!records && !xq) {
     void* w = nullptr;
     DRIFT_TRY(workspace_reserve(mma_workspace_bytes(x_rows, k), &w));
     DRIFT_TRY(prepare_x_mma(x_dtype, x, x_rows, k, static_cast<uint8_t*>(w), stream));
@@ -304,7 +342,7 @@ static int experts_common(bool gated, int x_dtype, const void* x, int64_t x_rows
                : launch_experts<T, false>(g, g, expert_bytes, ids, records, divisor,       \
                                           routed_slots, out, int(n),                           \
                                           int(k), int(slots), experts, first_expert,             \
-                                          others_zero, stream);
+                                          others_zero, stream, xq);
   switch (weight_dtype) {
     case DRIFT_Q8_0: DRIFT_EXPERTS_CASE(Q8_0T)
     case DRIFT_Q4_0: DRIFT_EXPERTS_CASE(Q4_0T)

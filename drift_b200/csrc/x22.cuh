@@ -12,11 +12,10 @@
 
 namespace drift {
 
-// A warp's 32 values of block `block` of vector v (lane j holding value j),
-// into the records of `blocks`-block vectors: the same bytes the preparation
+// A warp's 32 values of one block (lane j holding value j) into one vector's
+// 112-byte slot of a record (mma_i8.cuh): the same bytes the preparation
 // kernel (matvec.cu) writes for the same values. All 32 lanes take part.
-__device__ __forceinline__ void x22_record_block(float value, uint8_t* records, int v, int block,
-                                                 int blocks) {
+__device__ __forceinline__ void x22_record_slot(float value, uint8_t* slot) {
   const int lane = threadIdx.x % 32;
   // the largest magnitude by its bits (one warp reduction): an Inf or NaN
   // anywhere shows as bits of 0x7f800000 or more
@@ -39,20 +38,27 @@ __device__ __forceinline__ void x22_record_block(float value, uint8_t* records, 
     s = ldexpf(1.0f, e - X_BITS);
     X = __float2int_rn(ldexpf(value, X_BITS - e));
   }
-  const int pass = v / 8, g = v % 8;
-  uint8_t* record = records + ((long long)pass * blocks + block) * MMA_RECORD_BYTES;
   // value j = lane sits in byte j % 4 of word j / 4 of each plane
   const int w = lane / 4;
-  record[mma_plane_byte(g, 0, w) + lane % 4] = uint8_t(X & 0xff);
-  record[mma_plane_byte(g, 1, w) + lane % 4] = uint8_t((X >> 8) & 0xff);
-  record[mma_plane_byte(g, 2, w) + lane % 4] = uint8_t((X >> 16) & 0xff);
+  slot[mma_plane_byte(0, 0, w) + lane % 4] = uint8_t(X & 0xff);
+  slot[mma_plane_byte(0, 1, w) + lane % 4] = uint8_t((X >> 8) & 0xff);
+  slot[mma_plane_byte(0, 2, w) + lane % 4] = uint8_t((X >> 16) & 0xff);
   const int sum = __reduce_add_sync(0xffffffffu, X);
   if (lane == 0) {
-    uint8_t* scales = record + mma_scale_byte(g);
+    uint8_t* scales = slot + mma_scale_byte(0);
     reinterpret_cast<float*>(scales)[0] = s;
     reinterpret_cast<int*>(scales)[1] = sum;
     reinterpret_cast<float*>(scales)[2] = float(sum);
   }
+}
+
+// The same for block `block` of vector v of `blocks`-block vectors, in the
+// records' own layout (pass v / 8, slot v % 8).
+__device__ __forceinline__ void x22_record_block(float value, uint8_t* records, int v, int block,
+                                                 int blocks) {
+  const int pass = v / 8, g = v % 8;
+  x22_record_slot(value, records + ((long long)pass * blocks + block) * MMA_RECORD_BYTES +
+                             MMA_SLOT_BYTES * g);
 }
 
 }  // namespace drift

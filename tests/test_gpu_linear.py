@@ -143,6 +143,69 @@ def test_mixed_linears_share_launches(ops, m):
         assert torch.equal(alone, t)
 
 
+def test_pipelined_host_copies(ops):
+    """A host's pipeline through the C ABI: x copied in on one stream, the
+    product on a second, y copied out on a third, ordered per buffer by
+    events (drift_stream_wait_event), two steps in a row with new x each step
+    and the same buffers: every host y is bit for bit the product of its step's
+    x."""
+    import ctypes
+    lib = ops.lib
+    rng = np.random.default_rng(14)
+    k = 4096
+    cases = [(1, 512), (8, 1024), (3, 256)]
+    weights = {n: Stored.upload(oracle.Q4_1, (n, k), synthetic.quantized(rng, oracle.Q4_1, n, k))
+               for _, n in cases}
+    host_x = {c: torch.empty(c[0], k, dtype=torch.float32).pin_memory() for c in cases}
+    host_y = {c: torch.empty(c[0], c[1], dtype=torch.float32).pin_memory() for c in cases}
+    dev_x = {c: torch.empty(c[0], k, device="cuda") for c in cases}
+    dev_y = {c: torch.empty(c[0], c[1], device="cuda") for c in cases}
+
+    def created(call):
+        handle = ctypes.c_void_p()
+        assert call(ctypes.byref(handle)) == 0
+        return handle
+
+    streams = [created(lib.drift_stream_create) for _ in range(3)]
+    s_in, s_run, s_out = streams
+    events = {c: [created(lib.drift_event_create) for _ in range(3)] for c in cases}
+    torch.cuda.synchronize()
+    for step in range(2):
+        xs = {c: synthetic.gaussian(rng, c[0], k) for c in cases}
+        for c in cases:
+            host_x[c].copy_(torch.from_numpy(xs[c]))
+        for c in cases:
+            m, n = c
+            copied_in, computed, copied_out = events[c]
+            assert lib.drift_stream_wait_event(s_in, computed) == 0
+            assert lib.drift_memcpy_async(ctypes.c_void_p(dev_x[c].data_ptr()),
+                                          ctypes.c_void_p(host_x[c].data_ptr()), m * k * 4, 1,
+                                          s_in) == 0
+            assert lib.drift_event_record(copied_in, s_in) == 0
+            assert lib.drift_stream_wait_event(s_run, copied_in) == 0
+            assert lib.drift_stream_wait_event(s_run, copied_out) == 0
+            assert lib.drift_linear(0, ctypes.c_void_p(dev_x[c].data_ptr()), oracle.Q4_1,
+                                    ctypes.c_void_p(weights[n].data.data_ptr()),
+                                    ctypes.c_void_p(dev_y[c].data_ptr()), m, n, k, s_run) == 0
+            assert lib.drift_event_record(computed, s_run) == 0
+            assert lib.drift_stream_wait_event(s_out, computed) == 0
+            assert lib.drift_memcpy_async(ctypes.c_void_p(host_y[c].data_ptr()),
+                                          ctypes.c_void_p(dev_y[c].data_ptr()), m * n * 4, 2,
+                                          s_out) == 0
+            assert lib.drift_event_record(copied_out, s_out) == 0
+        assert lib.drift_device_synchronize() == 0
+        for c in cases:
+            expected = torch.empty(c[0], c[1], device="cuda")
+            ops.linear(torch.from_numpy(xs[c]).cuda(), weights[c[1]], expected)
+            torch.cuda.synchronize()
+            assert torch.equal(host_y[c], expected.cpu()), (step, c)
+    for c in cases:
+        for e in events[c]:
+            assert lib.drift_event_destroy(e) == 0
+    for handle in streams:
+        assert lib.drift_stream_destroy(handle) == 0
+
+
 def test_linear_rows_do_not_depend_on_batch(ops):
     """A row's sum is the same whether it comes alone or with 7 others."""
     rng = np.random.default_rng(12)

@@ -260,6 +260,31 @@ def test_shared_expert_rides_in_the_routed_launch(ops):
     assert ops.take_device_error() == 0
 
 
+@pytest.mark.parametrize("dtype", [oracle.Q8_0, oracle.Q4_0, oracle.Q4_1],
+                         ids=lambda t: oracle.NAMES[t])
+def test_down_product_prepares_x_in_the_kernel(ops, dtype):
+    """expertsLinear with one F32 x row a slot (a down product) prepares x in
+    the experts kernel; the same rows shared two slots each go through the
+    preparation launch: bit for bit the same outputs, on two calls in a row."""
+    rng = np.random.default_rng(63 + dtype)
+    experts, hidden, ffn, slots = 12, 256, 512, 10
+    down = Stored.upload(dtype, (experts, hidden, ffn),
+                         synthetic.quantized(rng, dtype, experts * hidden, ffn))
+    for call in range(2):
+        rows = synthetic.gaussian(rng, slots // 2, ffn)
+        ids = dev(rng.integers(0, experts, slots).astype(np.int32))
+        alone = torch.empty(slots, hidden, device="cuda")
+        ops.experts_linear(dev(np.repeat(rows, 2, axis=0)), down, ids, alone)
+        shared = torch.empty(slots, hidden, device="cuda")
+        ops.experts_linear(dev(rows), down, ids, shared)
+        assert torch.equal(alone, shared), call
+        expected = oracle.experts_linear(dtype, np.repeat(rows, 2, axis=0), down.data.cpu().numpy(),
+                                         experts, hidden, ffn, ids.cpu().numpy())
+        ok, _, _, summary = within(alone.cpu().numpy(), expected, 1e-4, 1e-3)
+        assert ok, summary
+    assert ops.take_device_error() == 0
+
+
 def test_experts_bad_id_is_flagged(ops):
     rng = np.random.default_rng(61)
     w = Stored.upload(oracle.Q4_1, (2, 64, 64), synthetic.quantized(rng, oracle.Q4_1, 128, 64))
