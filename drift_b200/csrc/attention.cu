@@ -31,7 +31,6 @@ int* device_error_word();
 
 namespace {
 
-constexpr int ATT_THREADS = 128;    // the join's threads
 constexpr int SPLIT_THREADS = 256;  // the splits' threads: 8 warps
 constexpr int MAX_GROUP = 16;   // query heads per key head, at most
 
@@ -322,6 +321,10 @@ __device__ __forceinline__ void split_pair(float x0, float x1, uint32_t& hi, uin
 // records from the values in shared memory. Per output it is join_head's
 // arithmetic in join_head's order, so the two give the same bits. `smem`:
 // the split's tile, whose keys and values are no longer read.
+constexpr int JOIN_GROUP_SPLITS = MAX_GROUP * MAX_FUSED_SPLITS;  // one head's splits, at most
+template <int D>
+constexpr int join_group_bytes() { return 4 * (MAX_GROUP * MAX_FUSED_SPLITS + MAX_GROUP + MAX_GROUP * D); }
+
 template <int D>
 __device__ void join_group(const AttentionArgs& a, int z, int kv_head, int group, uint8_t* smem) {
   float* factor = reinterpret_cast<float*>(smem);        // [group][splits]
@@ -652,18 +655,24 @@ __global__ void __launch_bounds__(SPLIT_THREADS) attention_split_kernel(const At
 }
 
 template <int D>
-__global__ void __launch_bounds__(ATT_THREADS) attention_join_kernel(const AttentionArgs a,
-                                                                     const float* sinks,
-                                                                     float* out,
-                                                                     uint8_t* records,
-                                                                     const float* gate,
-                                                                     int gate_stride) {
+__global__ void __launch_bounds__(SPLIT_THREADS) attention_join_kernel(const AttentionArgs a,
+                                                                       const float* sinks,
+                                                                       float* out,
+                                                                       uint8_t* records,
+                                                                       const float* gate,
+                                                                       int gate_stride) {
   pdl_trigger();  // the next kernel may launch and wait for this one
   pdl_wait();     // what the kernels before this one wrote is visible
-  extern __shared__ float factor[];  // [splits]: e^(m_s - M), 0 for an empty split
+  extern __shared__ __align__(16) float factor[];
   __shared__ float shared_total;
-  join_head<D, ATT_THREADS>(a, sinks, out, records, gate, gate_stride, blockIdx.x, blockIdx.y,
-                            factor, &shared_total);
+  // query head blockIdx.x of row blockIdx.y: as a group of one, with every
+  // pair of dimensions' sixteen splits in flight; past 4096 splits (the
+  // group routine's factor area) one split's loads after another
+  if (a.splits <= JOIN_GROUP_SPLITS)
+    join_group<D>(a, blockIdx.y, blockIdx.x, 1, reinterpret_cast<uint8_t*>(factor));
+  else
+    join_head<D, SPLIT_THREADS>(a, sinks, out, records, gate, gate_stride, blockIdx.x,
+                                blockIdx.y, factor, &shared_total);
 }
 
 #define DRIFT_ATTENTION_REGISTER(D)                                                   \
@@ -705,9 +714,10 @@ int launch_attention(const AttentionArgs& a, const float* sinks, float* out, cud
                         SPLIT_THREADS, SplitTile<D>::BYTES, stream, args));
   DRIFT_LAUNCHED("attention_split");
   if (args.fused_join) return 0;
-  DRIFT_CUDA(launch_pdl(attention_join_kernel<D>, dim3(a.q_heads, a.tokens), ATT_THREADS,
-                        a.splits * sizeof(float), stream, args, sinks, out, records, gate,
-                        gate_stride));
+  const size_t join_bytes =
+      a.splits <= JOIN_GROUP_SPLITS ? join_group_bytes<D>() : a.splits * sizeof(float);
+  DRIFT_CUDA(launch_pdl(attention_join_kernel<D>, dim3(a.q_heads, a.tokens), SPLIT_THREADS,
+                        join_bytes, stream, args, sinks, out, records, gate, gate_stride));
   DRIFT_LAUNCHED("attention_join");
   return 0;
 }

@@ -59,15 +59,20 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
         best_expert = e;
       }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o /= 2) {
-      const float other = __shfl_xor_sync(0xffffffffu, best, o);
-      const int other_expert = __shfl_xor_sync(0xffffffffu, best_expert, o);
-      if (other > best || (other == best && other_expert < best_expert)) {
-        best = other;
-        best_expert = other_expert;
-      }
+    // the warp's largest (value, then lowest expert) in two reductions: the
+    // largest value by an order-keeping key (-0 folded into +0, which
+    // compare equal; 0 for a lane with no candidate), then the lowest expert
+    // among the lanes holding it; its value from its own lane
+    unsigned key = 0;
+    if (best_expert != (1 << 30)) {
+      unsigned bits = __float_as_uint(best);
+      if ((bits << 1) == 0) bits = 0;
+      key = (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
     }
+    const unsigned top = __reduce_max_sync(0xffffffffu, key);
+    best_expert = int(__reduce_min_sync(0xffffffffu, key == top ? unsigned(best_expert)
+                                                                : unsigned(1 << 30)));
+    best = top == 0 ? -INFINITY : __shfl_sync(0xffffffffu, best, best_expert & 31);
     chosen[j] = best;
     chosen_id[j] = best_expert;
     if ((best_expert & 31) == lane && best_expert < experts) taken |= 1u << (best_expert >> 5);

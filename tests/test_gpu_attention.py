@@ -65,6 +65,7 @@ CASES = [
     (1, 32, 8, 128, 300, 16, True, 0, None, False),     # several splits
     (1, 32, 8, 128, 4096, 16, True, 0, None, False),    # C4's context
     (1, 16, 2, 256, 1000, 32, True, 0, None, False),    # C5's full attention (group 8)
+    (1, 16, 2, 256, 4096, 32, True, 0, None, False),    # C5's context: the separate join
     (1, 8, 8, 64, 129, 16, True, 0, None, False),
     (1, 10, 2, 80, 200, 16, True, 0, None, False),      # the 80-wide kernel
     (7, 32, 8, 128, 250, 16, True, 0, None, False),     # a prefill chunk, causal
@@ -139,6 +140,38 @@ def test_batched_decode_is_each_sequence_alone(ops, dim, q_heads, kv_heads):
     batched = torch.empty_like(q)
     ops.attention_decode(q, cache, table_dev, positions, per_sequence * page_size, attention,
                          batched)
+    for i, n in enumerate(lengths):
+        alone = torch.empty(1, q_heads, dim, device="cuda")
+        ops.attention(q[i:i + 1], cache, table_dev[i], n - 1, n, attention, alone)
+        assert torch.equal(batched[i:i + 1], alone), f"sequence {i}"
+
+
+def test_separate_join_is_the_fused_join(ops):
+    """C5's attention shape (16 query heads on 2 key heads of 256): decoded in a
+    launch sized for 4096 positions (64 splits: the join is a launch of its
+    own) and alone at their own lengths (the last split CTA joins): the same
+    bits."""
+    rng = np.random.default_rng(256)
+    dim, q_heads, kv_heads, page_size = 256, 16, 2, 32
+    lengths = [130, 300]
+    per_sequence = 4096 // page_size
+    batch = len(lengths)
+    pages = batch * per_sequence
+    tables = rng.permutation(pages).astype(np.int32).reshape(batch, per_sequence)
+    keys = np.zeros((pages, page_size, kv_heads, dim), dtype=np.uint16)
+    values = np.zeros((pages, kv_heads, dim, page_size), dtype=np.uint16)
+    for i, n in enumerate(lengths):
+        k = rng.standard_normal((n, kv_heads, dim)).astype(np.float32)
+        v = rng.standard_normal((n, kv_heads, dim)).astype(np.float32)
+        oracle.cache_write(k, v, keys, values, page_size, tables[i], 0)
+    cache = KvCache(torch.from_numpy(keys.view(np.float16)).cuda(),
+                    torch.from_numpy(values.view(np.float16)).cuda(), page_size)
+    q = torch.from_numpy(rng.standard_normal((batch, q_heads, dim)).astype(np.float32)).cuda()
+    table_dev = torch.from_numpy(tables).cuda()
+    positions = torch.tensor([n - 1 for n in lengths], dtype=torch.int32, device="cuda")
+    attention = Attention(1.0 / math.sqrt(dim))
+    batched = torch.empty_like(q)
+    ops.attention_decode(q, cache, table_dev, positions, 4096, attention, batched)
     for i, n in enumerate(lengths):
         alone = torch.empty(1, q_heads, dim, device="cuda")
         ops.attention(q[i:i + 1], cache, table_dev[i], n - 1, n, attention, alone)

@@ -184,6 +184,24 @@ def test_route_ties_take_the_lower_expert(ops):
     assert ids.cpu().numpy().tolist() == [[1, 2, 4, 0]]
 
 
+def test_route_ties_across_lanes(ops):
+    """Equal logits in one lane's experts and in different lanes' (5, 37 and
+    6; the four zeros, two of them -0.0), then -inf ones: value first, the
+    lower expert among equals, -0.0 equal to 0.0."""
+    logits = np.full((1, 64), -np.inf, np.float32)
+    for e in (5, 37, 6):
+        logits[0, e] = 3.0
+    logits[0, [0, 33]] = -0.0
+    logits[0, [32, 1]] = 0.0
+    ids = torch.empty(1, 8, dtype=torch.int32, device="cuda")
+    weights = torch.empty(1, 8, device="cuda")
+    ops.route(dev(logits), ids, weights)
+    assert ids.cpu().numpy().tolist() == [[5, 6, 37, 0, 1, 32, 33, 2]]
+    e_ids, e_weights = oracle.route(logits, 8)
+    assert np.array_equal(ids.cpu().numpy(), e_ids)
+    assert within(weights.cpu().numpy(), e_weights, 1e-7, 1e-6)[0]
+
+
 @pytest.mark.parametrize("dtype", [oracle.Q8_0, oracle.Q4_1], ids=lambda t: oracle.NAMES[t])
 def test_experts_linear_and_gated(ops, dtype):
     """C5 shapes with fewer experts: gate/up [E, 512, 2048], down [E, 2048, 512];
