@@ -16,6 +16,14 @@
  * blocks along K (tensor/Tensor.scala:75-87); `out` is written, never read,
  * and may alias an input for elementwise operations. Pointers are device
  * addresses of the current device.
+ *
+ * One stream of operations per device at a time: the products' x records
+ * (the grow-only workspace), their group sums and arrival counts, and the
+ * attention join's arrival counts live in per-device buffers that every call
+ * shares, so operations whose kernels overlap on the GPU (calls on different
+ * streams, or from different host threads, not ordered by events) race.
+ * Calls in one stream, or ordered between streams by events, do not; copies
+ * may run on other streams meanwhile (drift_stream_wait_event).
  */
 #ifndef DRIFT_OPS_H
 #define DRIFT_OPS_H
