@@ -785,7 +785,10 @@ int launch_split_mode(const SplitLaunch& launch, long long units, cudaStream_t s
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_SMEM));
     configured = true;
   }
-  long long grid = (units + Shape::WARPS - 1) / Shape::WARPS;  // at least a unit a warp
+  // 1-2 vectors: a CTA per unit up to the SM count, so a few-unit product
+  // streams through every SM (8 units to a CTA left SMs idle: the C4 step at
+  // batch 1 1.2 % slower); the MMA mode keeps 8 units to a CTA, faster there
+  long long grid = MODE == MODE_MMA ? (units + Shape::WARPS - 1) / Shape::WARPS : units;
   if (grid > sm_count()) grid = sm_count();
   DRIFT_CUDA(launch_pdl(matvec_split_kernel<T, MODE>, unsigned(grid), Shape::WARPS * 32,
                         Shape::BYTES + (MODE == MODE_MMA ? Shape::CHAIN_BYTES : 0), stream, launch));
