@@ -689,16 +689,9 @@ template <int D>
 int launch_attention(const AttentionArgs& a, const float* sinks, float* out, cudaStream_t stream,
                      uint8_t* records = nullptr, const float* gate = nullptr,
                      int gate_stride = 0) {
-  static bool configured = false;
-  if (!configured) {
-    DRIFT_CUDA(cudaFuncSetAttribute(attention_split_kernel<D>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    SplitTile<D>::BYTES));
-    // all of L1 as shared memory, so that two or more splits share an SM
-    DRIFT_CUDA(cudaFuncSetAttribute(attention_split_kernel<D>,
-                                    cudaFuncAttributePreferredSharedMemoryCarveout, 100));
-    configured = true;
-  }
+  // all of L1 as shared memory, so that two or more splits share an SM
+  static PerDevice configured;
+  DRIFT_TRY(ensure_shared_memory(configured, attention_split_kernel<D>, SplitTile<D>::BYTES, 100));
   // the join in the last split of each (row, key head) when its factors fit
   // in shared memory and the arrival counts in their array; else its own
   // launch

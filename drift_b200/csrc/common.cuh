@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <string>
@@ -38,6 +39,44 @@ const char* dtype_name(int dtype);
 int sm_count();
 
 constexpr int WARP = 32;
+
+// A kernel attribute set once per device: attributes such as the dynamic
+// shared memory limit belong to a device's context, so a process that runs
+// products on several GPUs sets them on each (devices 0-63; others are set on
+// every call).
+class PerDevice {
+ public:
+  bool done() const {
+    const int d = current();
+    return d >= 0 && d < 64 && ((bits_.load(std::memory_order_acquire) >> d) & 1u);
+  }
+  void mark() {
+    const int d = current();
+    if (d >= 0 && d < 64) bits_.fetch_or(uint64_t(1) << d, std::memory_order_release);
+  }
+
+ private:
+  static int current() {
+    int d = -1;
+    return cudaGetDevice(&d) == cudaSuccess ? d : -1;
+  }
+  std::atomic<uint64_t> bits_{0};
+};
+
+// Raises `kernel`'s dynamic shared memory limit to `bytes` on the current
+// device the first time it is asked there (and, with carveout >= 0, the
+// shared-memory share of L1); 0 or a drift status.
+template <typename Kernel>
+int ensure_shared_memory(PerDevice& once, Kernel* kernel, int bytes, int carveout = -1) {
+  if (once.done()) return 0;
+  cudaError_t status =
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (status == cudaSuccess && carveout >= 0)
+    status = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, carveout);
+  if (status != cudaSuccess) return cuda_status(status, "cudaFuncSetAttribute");
+  once.mark();
+  return 0;
+}
 
 }  // namespace drift
 

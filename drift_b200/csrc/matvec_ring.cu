@@ -744,12 +744,8 @@ template <typename T, int MODE, bool XSMEM>
 int launch_mode(const CUtensorMap& wmap, const uint8_t* records, float* y, int rows, int cols,
                 int vectors, int smem, cudaStream_t stream) {
   using Shape = RingShape<T>;
-  static bool configured = false;
-  if (!configured) {
-    DRIFT_CUDA(cudaFuncSetAttribute(matvec_ring_kernel<T, MODE, XSMEM>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_SMEM));
-    configured = true;
-  }
+  static PerDevice configured;
+  DRIFT_TRY(ensure_shared_memory(configured, matvec_ring_kernel<T, MODE, XSMEM>, MAX_SMEM));
   const int tiles = (rows + ROWS - 1) / ROWS;
   const unsigned grid = unsigned(tiles < sm_count() ? tiles : sm_count());
   // each CTA's leftover tiles keep their group sums in group_partials
@@ -779,12 +775,8 @@ int launch_dp4a(const CUtensorMap& wmap, const uint8_t* records, float* y, int r
 template <typename T, int MODE>
 int launch_split_mode(const SplitLaunch& launch, long long units, cudaStream_t stream) {
   using Shape = RingShape<T>;
-  static bool configured = false;
-  if (!configured) {
-    DRIFT_CUDA(cudaFuncSetAttribute(matvec_split_kernel<T, MODE>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_SMEM));
-    configured = true;
-  }
+  static PerDevice configured;
+  DRIFT_TRY(ensure_shared_memory(configured, matvec_split_kernel<T, MODE>, MAX_SMEM));
   // 1-2 vectors: a CTA per unit up to the SM count, so a few-unit product
   // streams through every SM (8 units to a CTA left SMs idle: the C4 step at
   // batch 1 1.2 % slower); the MMA mode keeps 8 units to a CTA, faster there

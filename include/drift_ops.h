@@ -373,8 +373,12 @@ int drift_linear_static(int x_dtype, const void* x, int weight_dtype, const void
                         float* out, int64_t m, int64_t n, int64_t k, drift_stream_t stream);
 
 /* Reads and clears the current device's error word: 0 if no kernel flagged
- * anything since the last call, else the first flag (1 = an id outside its
- * table, 2 = a bounded wait gave up). Synchronises the device. */
+ * anything since the last call, else the first flag:
+ *   1 = an id outside its table (the row is written as NaN);
+ *   2 = a bounded wait inside a kernel gave up (its outputs are incomplete);
+ *   3 = the tensor-parallel exchange's wait for a peer rank gave up (the
+ *       rows it was exchanging are left as they were: x and out unchanged).
+ * Synchronises the device. */
 int drift_device_error_take(int* code);
 
 #ifdef __cplusplus
