@@ -1,18 +1,20 @@
 """Quantized products on the GPU against the CPU oracle (the reference's
 LinearTests, runner/gpuTest/src/drift/runner/LinearTests.scala, on this path).
 
-Up to 31 rows of x (the reference's matrix-vector path, float x) each case is
-held to two bars:
-- the benchmark's: |gpu - oracle| <= 1e-4 + 1e-3 |oracle|;
-- the rigorous bound of the x preparation: x enters as exact integers 21 bits
+Every case is held to the benchmark's bar: |gpu - oracle| <= 1e-4 + 1e-3
+|oracle| (the oracle restates CpuLinear.linear: Double sums in column order).
+On top of it:
+- up to 31 rows of x (the reference's matrix-vector path, float x), the
+  rigorous bound of the x preparation: x enters as exact integers 21 bits
   below each 32-value block's largest |x| (drift_b200/csrc/quant.cuh), so an
   output can move by at most sum_k |w_k| * max|x_block| * 2^-21, plus float
   rounding of the sums, 1e-5 of the output scale (the reference's own
-  float-x tolerance, LinearTests.scala:154-157).
-From 32 rows on, a product is the reference's GEMM path (weights dequantized to
-F16, x rounded to F16, F32 accumulation: ops/HipLinear.scala:389-469), here on
-the tcgen05 tensor cores, and is held to the reference's own bound for it
-(LinearTests.scala:139-147): |gpu - oracle| <= (2 sum|w x| + |y|) 2^-11 1.01.
+  float-x tolerance, LinearTests.scala:154-157);
+- from 32 rows on (the reference's GEMM path, ops/HipLinear.scala:389-469,
+  here on the tcgen05 tensor cores with exact two-term F16 operands), also
+  the reference's own bound for its F16 GEMM (LinearTests.scala:139-147):
+  |gpu - oracle| <= (2 sum|w x| + |y|) 2^-11 1.01, which the benchmark's bar
+  is far inside.
 """
 
 import numpy as np
@@ -85,6 +87,8 @@ def test_linear_matches_oracle(ops, dtype, case, x_bf16):
     for law in ("tests", "bench"):
         actual, expected, limit = run_case(ops, dtype, m, n, k, seed=hash(case) % 1000,
                                            x_bf16=x_bf16, law=law)
+        ok, _, _, summary = within(actual, expected, 1e-4, 1e-3)
+        assert ok, f"{law} weights: {summary}"
         if m >= 32:
             rng = np.random.default_rng(hash(case) % 1000)
             w = (synthetic.random_blocks if law == "tests" else synthetic.quantized)(
@@ -97,8 +101,6 @@ def test_linear_matches_oracle(ops, dtype, case, x_bf16):
             assert (err <= bound).all(), \
                 f"{law} weights: worst at {(err / bound).max():.2f} of the GEMM bound"
             continue
-        ok, _, _, summary = within(actual, expected, 1e-4, 1e-3)
-        assert ok, f"{law} weights: {summary}"
         scale = np.abs(expected).max()
         err = np.abs(actual.astype(np.float64) - expected)
         assert (err <= limit + 1e-5 * scale).all(), \
@@ -220,34 +222,42 @@ def test_linear_rows_do_not_depend_on_batch(ops):
         assert torch.equal(one[0], batch[i])
 
 
-# The benchmark config C2 shapes at full size: sampled rows against the oracle.
+# The benchmark config C2 shapes at full size: sampled rows against the oracle,
+# at the benchmark's bar for every batch; from 32 rows (the tensor-core path)
+# for all three storage types, and the worst error is printed.
 FULL = [(4096, 4096), (12288, 4096), (4096, 12288), (151936, 4096)]
+FULL_CASES = ([(oracle.Q4_1, m) for m in (1, 8)]
+              + [(t, m) for t in TYPES for m in (32, 64)])
 
 
 @pytest.mark.parametrize("shape", FULL, ids=lambda s: f"{s[0]}x{s[1]}")
-@pytest.mark.parametrize("m", [1, 8, 64])
-def test_full_size_q4_1_sampled_rows(ops, shape, m):
+@pytest.mark.parametrize("case", FULL_CASES, ids=lambda c: f"{oracle.NAMES[c[0]]}-m{c[1]}")
+def test_full_size_sampled_rows(ops, shape, case):
+    dtype, m = case
     n, k = shape
-    rng = np.random.default_rng(n + k + m)
-    w = synthetic.quantized(rng, oracle.Q4_1, n, k)
+    rng = np.random.default_rng(n + k + m + dtype)
+    generator = torch.Generator(device="cuda")
+    generator.manual_seed(n + k + m + dtype)
+    stored = synthetic.quantized_device(dtype, n, k, generator=generator)
+    w = stored.cpu().numpy()
     bits = synthetic.bf16_bits(synthetic.gaussian(rng, m, k))
     x_eff = synthetic.bf16_values(bits)
-    weight = Stored.upload(oracle.Q4_1, (n, k), w)
+    weight = Stored(dtype, (n, k), stored)
     out = torch.empty((m, n), device="cuda")
     ops.linear(torch.from_numpy(bits.view(np.int16)).cuda().view(torch.bfloat16), weight, out)
     torch.cuda.synchronize()
     rows = np.unique(np.concatenate([[0, n - 1], rng.integers(0, n, 200)]))
-    expected = oracle.linear_rows(oracle.Q4_1, x_eff, w, n, k, rows)
+    expected = oracle.linear_rows(dtype, x_eff, w, n, k, rows)
     actual = out.cpu().numpy()[:, rows]
+    ok, _, worst, summary = within(actual, expected, 1e-4, 1e-3)
+    print(f"{oracle.NAMES[dtype]} [{m}, {k}] x [{n}, {k}]: max |gpu - oracle| {worst:.3g}")
+    assert ok, summary
     if m >= 32:
-        decoded = np.stack([oracle.decode(oracle.Q4_1, w[r * (k // 32) * 20:(r + 1) * (k // 32) * 20], k)
-                            for r in rows])
+        size = oracle.row_bytes(dtype, k)
+        decoded = np.stack([oracle.decode(dtype, w[r * size:(r + 1) * size], k) for r in rows])
         err = np.abs(actual.astype(np.float64) - expected)
         bound = gemm_bound(decoded, x_eff, expected)
         assert (err <= bound).all(), f"worst at {(err / bound).max():.2f} of the GEMM bound"
-    else:
-        ok, _, _, summary = within(actual, expected, 1e-4, 1e-3)
-        assert ok, summary
     assert torch.isfinite(out).all()
 
 
