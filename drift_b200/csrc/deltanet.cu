@@ -217,9 +217,9 @@ __global__ void __launch_bounds__(128) gated_rms_norm_kernel(
   }
 }
 
-DRIFT_REGISTER(causal_conv_silu, causal_conv_kernel)
+DRIFT_REGISTER(causal_conv_batched, causal_conv_kernel)
 DRIFT_REGISTER(delta_rule_d128, gated_delta_rule_kernel<128>)
-DRIFT_REGISTER(gated_rms_norm_f32, gated_rms_norm_kernel<1>)
+DRIFT_REGISTER(gated_rms_norm_records_f32, gated_rms_norm_kernel<1>)
 
 }  // namespace
 }  // namespace drift

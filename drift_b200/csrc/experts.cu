@@ -444,8 +444,8 @@ __global__ void __launch_bounds__(COMBINE_THREADS) combine_kernel(
   }
 }
 
-DRIFT_REGISTER(moe_combine, (combine_kernel<false, 2>))
-DRIFT_REGISTER(moe_combine_norm, (combine_kernel<true, 2>))
+DRIFT_REGISTER(moe_combine_rows, (combine_kernel<false, 2>))
+DRIFT_REGISTER(moe_combine_norm_records, (combine_kernel<true, 2>))
 
 template <bool NORM>
 static int launch_combine(const float* expert_out, const float* weights, int64_t tokens, int64_t k,

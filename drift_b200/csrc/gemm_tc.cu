@@ -582,7 +582,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
         const int tile = u / plan.splits;
         const int rt = tile % plan.row_tiles, pass = tile / plan.row_tiles;
-        for (int c = plan.chunk_begin(u); c < plan.chunk_end(u); ++c, ++gc) {
+        const int c1 = plan.chunk_end(u);
+        for (int c = plan.chunk_begin(u); c < c1; ++c, ++gc) {
           const int s = gc % S;
           if (gc >= S && !(ok = tc::mbar_wait(&empty[s], ((gc / S) - 1) & 1, abort, error))) break;
           if (weights) {
@@ -618,7 +619,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     int gc = 0;
     bool ok = true;
     for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
-      for (int c = plan.chunk_begin(u); ok && c < plan.chunk_end(u); ++c, ++gc) {
+      const int c1 = plan.chunk_end(u);  // (a 64-bit division: once a unit)
+      for (int c = plan.chunk_begin(u); ok && c < c1; ++c, ++gc) {
         if (gc >= 2 && !(ok = wait_warp(&acc_empty[accr.slot], accr.phase ^ 1u, abort, error)))
           break;
         if (!(ok = wait_warp(&x_full[xr.slot], xr.phase, abort, error))) break;
@@ -671,7 +673,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     int gc = 0;
     bool ok = true;
     for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
-      for (int c = plan.chunk_begin(u); ok && c < plan.chunk_end(u); ++c, ++gc) {
+      const int c1 = plan.chunk_end(u);
+      for (int c = plan.chunk_begin(u); ok && c < c1; ++c, ++gc) {
         if (!(ok = wait_warp(&w_full[wr.slot], wr.phase, abort, error))) break;
         if (2 * gc + half >= 3 &&
             !(ok = wait_warp(&a_empty[ar.slot], ar.phase ^ 1u, abort, error)))

@@ -94,10 +94,10 @@ __global__ void gather_rows_f32_kernel(const float* __restrict__ table, const in
   out[index] = table[id * cols + index % cols];
 }
 
-DRIFT_REGISTER(gather_q8_0, gather_kernel<Q8_0T>)
-DRIFT_REGISTER(gather_q4_0, gather_kernel<Q4_0T>)
-DRIFT_REGISTER(gather_q4_1, gather_kernel<Q4_1T>)
-DRIFT_REGISTER(gather_rows_f32, gather_rows_f32_kernel)
+DRIFT_REGISTER(gather_checked_q8_0, gather_kernel<Q8_0T>)
+DRIFT_REGISTER(gather_checked_q4_0, gather_kernel<Q4_0T>)
+DRIFT_REGISTER(gather_checked_q4_1, gather_kernel<Q4_1T>)
+DRIFT_REGISTER(gather_rows_checked_f32, gather_rows_f32_kernel)
 
 // ---- RMS norm ----------------------------------------------------------------------------
 // One block of 256 threads per row (1024 for rows of more than 1024 values).
@@ -205,7 +205,7 @@ int launch_rms_norm(float* x, const float* y, const float* weight, float* out, i
   return 0;
 }
 
-DRIFT_REGISTER(rms_norm_f32, (rms_norm_kernel<4, 1024>))
+DRIFT_REGISTER(rms_norm_records_f32, (rms_norm_kernel<4, 1024>))
 DRIFT_REGISTER(rms_norm_long_f32, rms_norm_long_kernel)
 
 // ---- elementwise ---------------------------------------------------------------------------
@@ -219,20 +219,6 @@ __global__ void add_kernel(const float* a, const float* b, float* out, long long
   DRIFT_FOR_EACH(i, n) out[i] = a[i] + b[i];
 }
 
-// Activation codes of ops/Activation.scala:5-19.
-__device__ __forceinline__ float activate(float v, int kind) {
-  switch (kind) {
-    case DRIFT_SILU: return v / (1.0f + expf(-v));
-    case DRIFT_GELU_TANH: {
-      const float inner = 0.7978845608028654f * (v + 0.044715f * v * v * v);
-      return 0.5f * v * (1.0f + tanhf(inner));
-    }
-    case DRIFT_GELU_ERF: return 0.5f * v * (1.0f + erff(v * 0.7071067811865476f));
-    case DRIFT_SIGMOID: return 1.0f / (1.0f + expf(-v));
-    default: return 4.0f * tanhf(v * 0.25f) / (1.0f + expf(-v));
-  }
-}
-
 // With `records`, also the next product's x records of rows of `cols` values
 // (cols and n multiples of 32: a warp's 32 consecutive values are one block,
 // and the loop's test is the same for the whole warp).
@@ -241,8 +227,7 @@ __global__ void gated_kernel(const float* gate, const float* up, float* out, lon
   pdl_trigger();  // the next kernel may launch and wait for this one
   pdl_wait();     // what the kernels before this one wrote is visible
   DRIFT_FOR_EACH(i, n) {
-    const float u = kind == DRIFT_SITU ? 25.0f * tanhf(up[i] * 0.04f) : up[i];
-    const float value = activate(gate[i], kind) * u;
+    const float value = activate(gate[i], kind) * gated_up(up[i], kind);
     out[i] = value;
     if (records)  // n < 2^31 here
       x22_record_block(value, records, int(i) / cols, int(i) % cols / 32, cols / 32);
@@ -250,7 +235,7 @@ __global__ void gated_kernel(const float* gate, const float* up, float* out, lon
 }
 
 DRIFT_REGISTER(add_f32, add_kernel)
-DRIFT_REGISTER(gated_f32, gated_kernel)
+DRIFT_REGISTER(gated_records_f32, gated_kernel)
 
 // ---- rotary embedding ---------------------------------------------------------------------
 // One thread per value of x [tokens, heads, head_dim]. The angle is the CPU
@@ -272,7 +257,7 @@ __global__ void rope_kernel(const float* __restrict__ x, const int* __restrict__
   out[index] = rope_turn(x + (index - d), d, positions[t], theta, rotary, layout);
 }
 
-DRIFT_REGISTER(rope_f32, rope_kernel)
+DRIFT_REGISTER(rope_single_f32, rope_kernel)
 
 // ---- products with F32 weights (routers) -----------------------------------------------------
 // F32 weights (routers, DeltaNet's a and b): a CTA of 256 threads per (row,

@@ -22,6 +22,27 @@ __device__ __forceinline__ float block_sum(float value, float* partial) {
   return total;
 }
 
+// ---- activations ----------------------------------------------------------------------------
+// Activation codes of ops/Activation.scala:5-19 (expf and tanhf called, as the
+// runner's own kernels call them, elementwise.hip:31-42).
+__device__ __forceinline__ float activate(float v, int kind) {
+  switch (kind) {
+    case DRIFT_SILU: return v / (1.0f + expf(-v));
+    case DRIFT_GELU_TANH: {
+      const float inner = 0.7978845608028654f * (v + 0.044715f * v * v * v);
+      return 0.5f * v * (1.0f + tanhf(inner));
+    }
+    case DRIFT_GELU_ERF: return 0.5f * v * (1.0f + erff(v * 0.7071067811865476f));
+    case DRIFT_SIGMOID: return 1.0f / (1.0f + expf(-v));
+    default: return 4.0f * tanhf(v * 0.25f) / (1.0f + expf(-v));
+  }
+}
+
+// The up half of a gated activation: SiTU-GLU bounds it, 25 tanh(up / 25).
+__device__ __forceinline__ float gated_up(float up, int kind) {
+  return kind == DRIFT_SITU ? 25.0f * tanhf(up * 0.04f) : up;
+}
+
 // ---- rotary embedding ---------------------------------------------------------------------
 // Value d of a head after the turn: the angle is the CPU reference's to the
 // bit -- the inverse frequency 1f / (float) pow(theta, 2 pair / rotary) (pow
@@ -46,6 +67,62 @@ __device__ __forceinline__ float rope_turn(const float* head, int d, int positio
   const float power = float(pow(double(theta), __ddiv_rn(2.0 * pair, double(rotary))));
   const float inverse = __fdiv_rn(1.0f, power);
   const float angle = __fmul_rn(float(position), inverse);
+  double s, c;
+  sincos(double(angle), &s, &c);
+  const double a = first ? double(head[d]) : double(head[partner]);
+  const double b = first ? double(head[partner]) : double(head[d]);
+  const double value = first ? __dsub_rn(__dmul_rn(a, c), __dmul_rn(b, s))
+                             : __dadd_rn(__dmul_rn(a, s), __dmul_rn(b, c));
+  return float(value);
+}
+
+// The same turn with mRoPE sections (ops/Rope.scala:12-35, CpuAttention.rope:
+// ops/CpuAttention.scala:92-146): pair i takes positions[section * tokens + t]
+// where `sections` is 0 (one position a token), 1 (contiguous: s0 temporal,
+// s1 height pairs, the rest width), 2 (interleaved: height when i % 3 == 1
+// and i < 3 s1, width when i % 3 == 2 and i < 3 s2, else temporal) or 3
+// (axes: s0..s3 pairs in turn, axis a's pair j of n turning by theta^(-j/n)).
+__device__ __forceinline__ float rope_turn_sections(const float* head, int d,
+                                                    const int* positions, int t, int tokens,
+                                                    float theta, int rotary, int layout,
+                                                    int sections, int s0, int s1, int s2,
+                                                    int s3) {
+  if (d >= rotary) return head[d];
+  const int half = rotary / 2;
+  int pair, partner;
+  bool first;
+  if (layout == DRIFT_ROPE_NEOX) {
+    pair = d % half;
+    first = d < half;
+    partner = first ? d + half : d - half;
+  } else {
+    pair = d / 2;
+    first = d % 2 == 0;
+    partner = first ? d + 1 : d - 1;
+  }
+  int section = 0;
+  double exponent = __ddiv_rn(2.0 * pair, double(rotary));
+  if (sections == 1) {
+    section = pair < s0 ? 0 : (pair < s0 + s1 ? 1 : 2);
+  } else if (sections == 2) {
+    section = (pair % 3 == 1 && pair < 3 * s1) ? 1 : ((pair % 3 == 2 && pair < 3 * s2) ? 2 : 0);
+  } else if (sections == 3) {
+    const int sizes[4] = {s0, s1, s2, s3};
+    int start = 0;
+    section = 3;
+    for (int a = 0; a < 4; ++a) {
+      if (pair < start + sizes[a]) {
+        section = a;
+        break;
+      }
+      start += sizes[a];
+    }
+    if (section == 3 && pair >= start + s3) start -= s3;  // past every axis: the last one's
+    exponent = __ddiv_rn(double(pair - start), double(sizes[section]));
+  }
+  const float power = float(pow(double(theta), exponent));
+  const float inverse = __fdiv_rn(1.0f, power);
+  const float angle = __fmul_rn(float(positions[(long long)section * tokens + t]), inverse);
   double s, c;
   sincos(double(angle), &s, &c);
   const double a = first ? double(head[d]) : double(head[partner]);

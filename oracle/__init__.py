@@ -70,6 +70,8 @@ def lib() -> ctypes.CDLL:
             "oracle_activation": (None, [i32, f32, p, p, i64]),
             "oracle_inverse_frequency": (f32, [f32, i32, i32]),
             "oracle_rope": (None, [p, p, p, i32, i32, i32, f32, i32, i32]),
+            "oracle_rope_sections": (None, [p, p, p, i32, i32, i32, f32, i32, i32, i32, i32, i32,
+                                            i32, i32]),
             "oracle_route": (None, [p, i32, i32, i32, p, p]),
             "oracle_experts_linear": (i32, [i32, p, i64, p, i64, i64, i64, p, i64, p]),
             "oracle_experts_gated_linear": (i32, [i32, p, i64, p, p, i64, i64, i64, p, i64, p]),
@@ -221,6 +223,20 @@ def rope(x, positions, theta: float, rotary: int, layout: int) -> np.ndarray:
     positions = np.ascontiguousarray(positions, dtype=np.int32)
     out = np.empty_like(x)
     lib().oracle_rope(_p(x), _p(positions), _p(out), tokens, heads, dim, theta, rotary, layout)
+    return out
+
+
+def rope_sections(x, positions, theta: float, rotary: int, layout: int, sections: int,
+                  sizes=(0, 0, 0, 0)) -> np.ndarray:
+    """CpuAttention.rope with mRoPE sections (codes of RopeSections); x
+    [tokens, heads, D], positions [positions per token, tokens]."""
+    x = _f32(x)
+    tokens, heads, dim = x.shape
+    positions = np.ascontiguousarray(positions, dtype=np.int32)
+    out = np.empty_like(x)
+    s0, s1, s2, s3 = (list(sizes) + [0, 0, 0, 0])[:4]
+    lib().oracle_rope_sections(_p(x), _p(positions), _p(out), tokens, heads, dim, theta, rotary,
+                               layout, sections, s0, s1, s2, s3)
     return out
 
 

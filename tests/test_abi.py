@@ -44,9 +44,18 @@ def test_every_declared_function_is_exported(lib, name):
 def test_kernels_are_listed_by_name(lib):
     names = [lib.drift_kernel_name(i).decode() for i in range(lib.drift_kernel_count())]
     for expected in ["matvec_ring_q4_1_dp4a1", "matvec_split_q8_0_mma", "quantize_x22_mma_bf16",
-                     "gather_q8_0", "rms_norm_f32", "gated_f32", "rope_f32", "route_topk",
-                     "experts_gated_x22_q4_1_ks2", "moe_combine_norm"]:
+                     "experts_gated_x22_q4_1_ks2", "linear_tc_q4_1",
+                     # the runner's own names (runner/kernels/*.hip), with its argument lists
+                     "gather_q8_0", "gather_q4_0", "gather_rows_f32", "rms_norm_f32", "gated_f32",
+                     "rope_f32", "route_topk", "moe_combine", "moe_combine_norm",
+                     "causal_conv_silu", "gated_rms_norm_f32", "add_f32", "matvec_rows_f32",
+                     "matvec_float_x_q8_0", "matvec_float_x_narrow_q4_0",
+                     "matvec_float_x_multi_q8_0", "matvec_float_x_multi_narrow_q4_0",
+                     "matvec_split_q4_0",
+                     # new names in the same pattern for Q4_1
+                     "gather_q4_1", "matvec_float_x_q4_1", "matvec_split_q4_1"]:
         assert expected in names
+    assert len(names) == len(set(names)), "a kernel name is registered twice"
     assert lib.drift_kernel_name(len(names)) is None
 
 
