@@ -293,14 +293,15 @@ def run_gpu(args) -> dict | None:
     h2d = sum(b * k * 2 for b in BATCHES for n, k in SHAPES)
     d2h = sum(b * n * 4 for b in BATCHES for n, k in SHAPES)
 
-    # the dominant kernel alone: the lm-head product at batch 1, replayed
-    dominant = dominant_kernel(ops, weights, xs, ys, stream)
+    # every product alone (rank 0), and the one with the largest share of the step
     sweep = sweep_table(ops, weights, xs, ys, stream) if rank == 0 else None
+    dominant = dominant_kernel(sweep) if sweep else None
     del weights, xs, ys, host_x, host_y
     torch.cuda.empty_cache()
     # benchmark configs C1 (the Q8_0 product) and C3 (the layer ops), rank 0
     configs = (measure_c1_c3(ops, stream, args.cpu_baseline)
                if rank == 0 and args.decode else None)
+    read_only = read_only_gbs(lib, stream) if rank == 0 else None
 
     # benchmark config C4: the dense decoder's decode step, tensor-parallel over the
     # job's GPUs (one NCCL group), tok/s at each batch
@@ -319,6 +320,7 @@ def run_gpu(args) -> dict | None:
     if rank != 0:
         return None
 
+    traffic, traffic_source = profiled_traffic(dominant["batch"], dominant["shape"])
     total_bytes = step_bytes() * args.steps * world
     value = total_bytes / (elapsed_ms / 1e3) / 1e9
     e2e_value = total_bytes / (e2e_ms / 1e3) / 1e9
@@ -344,20 +346,28 @@ def run_gpu(args) -> dict | None:
             "parallelism": f"replicas x{world} (weak scaling, no exchange)",
             "fraction_of_8TBs": round(value / world / NOMINAL_HBM_GBS, 4),
             "fraction_of_measured_hbm": round(value / world / peaks["hbm_gbs"], 4),
+            "fraction_of_read_only_hbm": round(value / world / read_only, 4),
+            # decode tok/s (C4 dense, tensor parallel over the job's GPUs; C5
+            # hybrid MoE, expert + head parallel), whole job
+            "decode_tok_s": decode_summary(decode, hybrid),
         },
         "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": launches_per_step * args.steps,
         "roofline": {
             "bound": "hbm",
-            "kernel": "matvec_ring_q4_1 (+ quantize_x22_mma), lm-head 151936x4096, batch 1",
+            "kernel": f"{dominant['kernel']}, {dominant['shape']}, batch {dominant['batch']}",
+            "step_share": round(dominant["share"], 4),
             "achieved": round(dominant["gbs"], 1),
             "peak": peaks["hbm_gbs"],
             "peak_source": peaks["source"] + " (MEASURED_PEAKS.json hbm_gbs, copy)",
             "unit": "GB/s",
             "frac": round(dominant["gbs"] / peaks["hbm_gbs"], 4),
-            "traffic": profiled_traffic(),
-            "traffic_source": "profiles/matvec_ring_q4_1_lmhead.md (ncu dram read + write, one launch)",
+            "read_only_peak": round(read_only, 1),
+            "frac_of_read_only": round(dominant["gbs"] / read_only, 4),
+            "traffic": traffic,
+            "traffic_source": (f"{traffic_source} (ncu dram read + write, one launch)"
+                               if traffic_source else None),
             "launch_us": round(dominant["us"], 3),
         },
         "clocks": clock_info,
@@ -372,6 +382,18 @@ def run_gpu(args) -> dict | None:
 
 
 DECODE_CONTEXT = 4096
+
+
+def decode_summary(decode: dict | None, hybrid: dict | None) -> dict | None:
+    """The decode lines' tok/s in one small dict: c4_b1, c4_b16, c5_b1, c5_b16."""
+    if not decode and not hybrid:
+        return None
+    out = {}
+    for tag, line in (("c4", decode), ("c5", hybrid)):
+        for key, row in (line or {}).items():
+            if key.startswith("b") and isinstance(row, dict) and "tok_s" in row:
+                out[f"{tag}_{key}"] = row["tok_s"]
+    return out
 
 
 def run_decode(args, ops, rank: int, world: int, stream) -> dict:
@@ -576,17 +598,20 @@ def measure_c1_c3(ops, stream, cpu: bool) -> dict:
     return out
 
 
-def profiled_traffic() -> int | None:
-    """DRAM bytes (read + write) of one lm-head batch-1 launch of the ring
-    kernel, as the committed ncu summary records them."""
-    path = os.path.join(ROOT, "profiles", "matvec_ring_q4_1_lmhead.md")
-    try:
-        for line in open(path):
-            if line.startswith("traffic_bytes_b1:"):
-                return int(line.split(":")[1])
-    except OSError:
-        pass
-    return None
+def profiled_traffic(batch: int, shape: str) -> tuple:
+    """DRAM bytes (read + write) of one launch of the product's kernel from a
+    committed ncu summary (a line `traffic_bytes b<batch> <shape>: <bytes>`
+    in profiles/*.md), and the summary's name; (None, None) if none has it."""
+    folder = os.path.join(ROOT, "profiles")
+    key = f"traffic_bytes b{batch} {shape}:"
+    for name in sorted(os.listdir(folder)) if os.path.isdir(folder) else []:
+        try:
+            for line in open(os.path.join(folder, name)):
+                if line.startswith(key):
+                    return int(line.split(":")[1]), f"profiles/{name}"
+        except (OSError, ValueError):
+            continue
+    return None, None
 
 
 def count_launches(graph) -> int:
@@ -641,18 +666,63 @@ def rotation(weight, minimum_bytes: int) -> list:
                        for _ in range(count - 1)]
 
 
-def dominant_kernel(ops, weights, xs, ys, stream) -> dict:
-    """The lm-head product at batch 1 alone, cycling through copies of its
-    weight that stream 4x L2 between reuses."""
-    n, k = 151936, 4096
-    copies = rotation(weights[(n, k)], 4 * L2_BYTES)
+def product_kernel(batch: int) -> str:
+    """The kernel that carries a product of `batch` rows of x (drift_linear's
+    dispatch): the tcgen05 product from 32 rows, the ring kernel's integer
+    MMA mode for 3-31 (passes of 8), its dp4a mode for 1-2."""
+    if batch >= 32:
+        return "linear_tc_q4_1 (+ tc_prepare_x)"
+    if batch >= 3:
+        return "matvec_ring_q4_1_mma (+ quantize_x22_mma)"
+    return "matvec_ring_q4_1_dp4a (+ quantize_x22_mma)"
 
-    def fn():
-        for w in copies:
-            ops.linear(xs[(1, n, k)], w, ys[(1, n, k)])
 
-    ms = timed_graph(fn, stream, 20) / len(copies)
-    return {"us": ms * 1e3, "gbs": algorithmic_bytes(n, k, 1) / (ms / 1e3) / 1e9}
+def dominant_kernel(sweep: list) -> dict:
+    """The product with the largest share of the step (the sweep times each
+    product alone, its weight copies cycling 4x L2 apart): its time, share and
+    achieved GB/s of algorithmic bytes."""
+    total = sum(r["us"] for r in sweep)
+    top = max(sweep, key=lambda r: r["us"])
+    n, k = (int(v) for v in top["shape"].split("x"))
+    return {"us": top["us"], "gbs": algorithmic_bytes(n, k, top["batch"]) / (top["us"] / 1e6) / 1e9,
+            "share": top["us"] / total, "batch": top["batch"], "shape": top["shape"],
+            "kernel": product_kernel(top["batch"])}
+
+
+def read_only_gbs(lib, stream) -> float:
+    """The read-only HBM ceiling: the library's read_sum_f32x4 (the reference's
+    bandwidth probe, kernels/bandwidth.hip:5-20, launched by name as
+    MemoryBandwidth does) over 4 GiB, ten passes, CUDA events."""
+    import torch
+
+    from drift_b200._lib import check
+
+    n4 = (4 << 30) // 16
+    data = torch.ones(n4 * 4, device="cuda")
+    blocks = 148 * 16
+    partials = torch.empty(blocks, device="cuda")
+    function = ctypes.c_void_p()
+    check("drift_module_get_function",
+          lib.drift_module_get_function(ctypes.byref(function), None, b"read_sum_f32x4"))
+    args = [ctypes.c_void_p(data.data_ptr()), ctypes.c_int64(n4), ctypes.c_void_p(partials.data_ptr())]
+    slots = (ctypes.c_void_p * 3)(*[ctypes.cast(ctypes.pointer(a), ctypes.c_void_p) for a in args])
+    handle = ctypes.c_void_p(stream.cuda_stream)
+
+    def run():
+        check("read_sum_f32x4", lib.drift_module_launch_kernel(function, blocks, 1, 1, 256, 1, 1, 0,
+                                                               handle, slots, None))
+    run()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(10):
+        run()
+    end.record(stream)
+    torch.cuda.synchronize()
+    assert abs(float(partials.double().sum()) - n4 * 4) < 1e-3 * n4 * 4, "read_sum_f32x4 sum"
+    del data
+    torch.cuda.empty_cache()
+    return n4 * 16 * 10 / (start.elapsed_time(end) / 1e3) / 1e9
 
 
 def sweep_table(ops, weights, xs, ys, stream) -> list:

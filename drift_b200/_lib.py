@@ -95,6 +95,11 @@ SIGNATURES = {
                                                _i32, _p, _i32, _f32, _i32, _f32, _p, _p, _p, _p]),
     "drift_rope": (_i32, [_p, _p, _p, _i32, _i32, _i32, _f32, _i32, _i32, _p]),
     "drift_route": (_i32, [_p, _p, _p, _i32, _i32, _i32, _p]),
+    "drift_argmax": (_i32, [_p, _i64, _i64, _i64, _p, _p, _p]),
+    "drift_argmax_merge": (_i32, [_p, _p, _i64, _i64, _p, _p, _p]),
+    "drift_candidates": (_i32, [_p, _i64, _i64, _i64, _i32, _p, _p, _p]),
+    "drift_candidates_workspace_bytes": (_sz, [_i64, _i64, _i32]),
+    "drift_candidates_merge": (_i32, [_p, _p, _i64, _i64, _i32, _p, _p, _p]),
     "drift_experts_linear_local": (_i32, [_i32, _p, _i64, _i32, _p, _i64, _i64, _i64, _i64, _p,
                                           _i64, _p, _p, _p]),
     "drift_experts_gated_linear_local": (_i32, [_i32, _p, _i64, _i32, _p, _p, _i64, _i64, _i64,

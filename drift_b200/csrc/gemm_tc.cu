@@ -429,12 +429,11 @@ struct TcLayout {
   static constexpr int X_OFFSET = W_STAGES * RAW_PADDED;
   static constexpr int M_OFFSET = X_OFFSET + X_STAGES * XC::BYTES;
   static constexpr int BARRIER_OFFSET = M_OFFSET + M_SLOTS * M_TILE_BYTES;
-  // w_full, w_empty [W], x_full, x_empty [X], a_full, a_empty [3], acc_full,
-  // acc_empty [2], m_empty [3], tmem slot, abort
+  // w_full, w_empty [W], ready, half1, a_empty, done [3], tmem slot, abort
   static constexpr int SMEM_BYTES = BARRIER_OFFSET + 512 + 1024;  // + alignment slack
   static_assert(W_STAGES >= 2, "raw weight ring");
   static_assert(XC::BYTES % 1024 == 0, "x chunks keep the swizzle atoms aligned");
-  static_assert((2 * W_STAGES + 2 * X_STAGES + 13) * 8 + 8 <= 512, "barrier area");
+  static_assert((2 * W_STAGES + 12) * 8 + 8 <= 512, "barrier area");
   static_assert(SMEM_BYTES <= 232448, "shared memory");
 };
 
@@ -524,16 +523,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BARRIER_OFFSET);
+  // Chunk c's hand-offs, so the MMA warp waits twice a chunk and commits
+  // three times:
+  //  - ready[c % 3]: the MMA may start chunk c -- its x landed (the x
+  //    producer's expected bytes), its first half's A is in TMEM (four dequant
+  //    warps) and its accumulator (c % 2) was read back (four epilogue warps,
+  //    after chunk c - 2);
+  //  - half1[c % 3]: its second half's A is in TMEM (four dequant warps);
+  //  - a_empty[q % 3]: half chunk q's A set may be refilled (MMA commit);
+  //  - done[c % 3]: chunk c's MMAs completed (MMA commit): its accumulator
+  //    may be read, its x slot and min tile reused.
   uint64_t* w_full = bars;
   uint64_t* w_empty = w_full + WS;
-  uint64_t* x_full = w_empty + WS;
-  uint64_t* x_empty = x_full + XS;
-  uint64_t* a_full = x_empty + XS;  // [3]: half-chunk number mod 3
-  uint64_t* a_empty = a_full + 3;
-  uint64_t* acc_full = a_empty + 3;
-  uint64_t* acc_empty = acc_full + 2;
-  uint64_t* m_empty = acc_empty + 2;  // [3]: chunk number mod 3 (Q4 types)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(m_empty + 3);
+  uint64_t* ready = w_empty + WS;
+  uint64_t* half1 = ready + 3;
+  uint64_t* a_empty = half1 + 3;
+  uint64_t* done = a_empty + 3;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 3);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -544,18 +550,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       tc::mbar_init(&w_full[s], 1);
       tc::mbar_init(&w_empty[s], DEQUANT_WARPS);
     }
-    for (int s = 0; s < XS; ++s) {
-      tc::mbar_init(&x_full[s], 1);
-      tc::mbar_init(&x_empty[s], 1);  // the MMA's commit
-    }
     for (int i = 0; i < 3; ++i) {
-      tc::mbar_init(&a_full[i], DEQUANT_WARPS / 2);  // a half's four lane quarters
-      tc::mbar_init(&a_empty[i], 1);                 // the MMA's commit
-      tc::mbar_init(&m_empty[i], 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      tc::mbar_init(&acc_full[b], 1);                // the MMA's commit
-      tc::mbar_init(&acc_empty[b], EPILOGUE_WARPS);  // every lane quarter read back
+      tc::mbar_init(&ready[i], DEQUANT_WARPS / 2 + EPILOGUE_WARPS + 1);
+      tc::mbar_init(&half1[i], DEQUANT_WARPS / 2);
+      tc::mbar_init(&a_empty[i], 1);
+      tc::mbar_init(&done[i], 1);
     }
     *abort = 0;
     tc::fence_barrier_init();
@@ -570,39 +569,54 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   // else reads x or writes out, scratch and counters.
   if (warp != W_WARP) pdl_wait();
 
-  if (warp == W_WARP || warp == X_WARP) {
-    // ---- producers: raw weights (2-D tensor copy of 128 rows), x (one bulk copy) ----
+  if (warp == W_WARP) {
+    // ---- weight producer: a 2-D tensor copy of 128 rows' chunk into the ring ----
     if (lane == 0) {
-      const bool weights = warp == W_WARP;
-      const int S = weights ? WS : XS;
-      uint64_t* full = weights ? w_full : x_full;
-      uint64_t* empty = weights ? w_empty : x_empty;
       int gc = 0;
       bool ok = true;
       for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
-        const int tile = u / plan.splits;
-        const int rt = tile % plan.row_tiles, pass = tile / plan.row_tiles;
+        const int rt = (u / plan.splits) % plan.row_tiles;
         const int c1 = plan.chunk_end(u);
         for (int c = plan.chunk_begin(u); c < c1; ++c, ++gc) {
-          const int s = gc % S;
-          if (gc >= S && !(ok = tc::mbar_wait(&empty[s], ((gc / S) - 1) & 1, abort, error))) break;
-          if (weights) {
-            tc::mbar_expect_tx(&full[s], L::RAW_BYTES);
-            tc::tma_load_2d(smem + s * L::RAW_PADDED, &wmap, &full[s], c * Unpack<T>::RAW_WORDS,
-                            rt * TILE_ROWS);
-          } else {
-            tc::mbar_expect_tx(&full[s], XC::BYTES);
-            tc::bulk_load(smem + L::X_OFFSET + s * XC::BYTES,
-                          xs + ((long long)pass * plan.chunks + c) * XC::BYTES, XC::BYTES,
-                          &full[s]);
-          }
+          const int s = gc % WS;
+          if (gc >= WS && !(ok = tc::mbar_wait(&w_empty[s], ((gc / WS) - 1) & 1, abort, error)))
+            break;
+          tc::mbar_expect_tx(&w_full[s], L::RAW_BYTES);
+          tc::tma_load_2d(smem + s * L::RAW_PADDED, &wmap, &w_full[s], c * Unpack<T>::RAW_WORDS,
+                          rt * TILE_ROWS);
         }
       }
       if (!ok) {
         // let the copies already issued land before the CTA leaves
-        for (int j = gc - S < 0 ? 0 : gc - S; j < gc; ++j) {
+        for (int j = gc - WS < 0 ? 0 : gc - WS; j < gc; ++j) {
           volatile int never = 0;
-          tc::mbar_wait(&full[j % S], (j / S) & 1, &never, nullptr);
+          tc::mbar_wait(&w_full[j % WS], (j / WS) & 1, &never, nullptr);
+        }
+      }
+    }
+  } else if (warp == X_WARP) {
+    // ---- x producer: one bulk copy per chunk, completing on the chunk's ready ----
+    if (lane == 0) {
+      int gc = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
+        const int pass = (u / plan.splits) / plan.row_tiles;
+        const int c1 = plan.chunk_end(u);
+        for (int c = plan.chunk_begin(u); c < c1; ++c, ++gc) {
+          // the slot's last chunk, gc - XS, is done
+          if (gc >= XS &&
+              !(ok = tc::mbar_wait(&done[(gc - XS) % 3], ((gc - XS) / 3) & 1, abort, error)))
+            break;
+          tc::mbar_expect_tx(&ready[gc % 3], XC::BYTES);
+          tc::bulk_load(smem + L::X_OFFSET + (gc % XS) * XC::BYTES,
+                        xs + ((long long)pass * plan.chunks + c) * XC::BYTES, XC::BYTES,
+                        &ready[gc % 3]);
+        }
+      }
+      if (!ok) {
+        for (int j = gc - XS < 0 ? 0 : gc - XS; j < gc; ++j) {
+          volatile int never = 0;
+          tc::mbar_wait(&ready[j % 3], (j / 3) & 1, &never, nullptr);
         }
       }
     }
@@ -613,23 +627,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // core's own F32 sums, which drop low bits as a chain of MMAs grows, span
     // one chunk only.
     const uint32_t idesc = tc::instr_desc_f16(TILE_ROWS, TILE_VECTORS);
-    Ring<XS> xr;
-    Ring<3> ar, mr;
-    Ring<2> accr;
+    Ring<3> cr;  // chunk gc: ready, half1 and done slot, and their phase
+    Ring<3> ar;  // half chunk 2 gc + h: A set
     int gc = 0;
     bool ok = true;
     for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
       const int c1 = plan.chunk_end(u);  // (a 64-bit division: once a unit)
       for (int c = plan.chunk_begin(u); ok && c < c1; ++c, ++gc) {
-        if (gc >= 2 && !(ok = wait_warp(&acc_empty[accr.slot], accr.phase ^ 1u, abort, error)))
-          break;
-        if (!(ok = wait_warp(&x_full[xr.slot], xr.phase, abort, error))) break;
-        const uint32_t acc = tmem + 64 * accr.slot;
-        const uint32_t x_address = tc::smem_u32(smem + L::X_OFFSET + xr.slot * XC::BYTES);
+        const uint32_t acc = tmem + 64 * (gc & 1);
+        const uint32_t x_address = tc::smem_u32(smem + L::X_OFFSET + (gc % XS) * XC::BYTES);
         const uint64_t x_desc = tc::smem_desc_sw128(x_address);
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          if (!(ok = wait_warp(&a_full[ar.slot], ar.phase, abort, error))) break;
+          uint64_t* gate = h == 0 ? &ready[cr.slot] : &half1[cr.slot];
+          if (!(ok = wait_warp(gate, cr.phase, abort, error))) break;
           tc::fence_after_sync();
           const uint32_t a = tmem + 128 + 128 * ar.slot;
           // one half: its 8 K-steps, each hi * x and lo * x (and hi * x_lo),
@@ -646,20 +657,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           if (SUMS && h == 1)
             mma_f16_ss_warp(acc,
                             smem_desc_interleave(
-                                tc::smem_u32(smem + L::M_OFFSET + mr.slot * M_TILE_BYTES)),
+                                tc::smem_u32(smem + L::M_OFFSET + cr.slot * M_TILE_BYTES)),
                             smem_desc_interleave(x_address + XC::S_OFFSET), idesc, 1u);
           tc::mma_commit_warp(&a_empty[ar.slot]);
           ar.advance();
         }
         if (!ok) break;
-        tc::mma_commit_warp(&x_empty[xr.slot]);
-        xr.advance();
-        if (SUMS) {
-          tc::mma_commit_warp(&m_empty[mr.slot]);
-          mr.advance();
-        }
-        tc::mma_commit_warp(&acc_full[accr.slot]);
-        accr.advance();
+        tc::mma_commit_warp(&done[cr.slot]);
+        cr.advance();
       }
     }
   } else if (warp < DEQUANT_WARPS) {
@@ -668,7 +673,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int row_in_tile = quarter * 32 + lane;
     const uint32_t lane_base = uint32_t(quarter * 32) << 16;
     Ring<WS> wr;
-    Ring<3> ar, mr;  // this warp's half chunks are every other one
+    Ring<3> ar;  // this warp's half chunks are every other one
+    Ring<3> cr;  // the chunk: its ready / half1 slot and min tile
     ar.advance(half);
     int gc = 0;
     bool ok = true;
@@ -679,7 +685,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (2 * gc + half >= 3 &&
             !(ok = wait_warp(&a_empty[ar.slot], ar.phase ^ 1u, abort, error)))
           break;
-        if (SUMS && gc >= 3 && !(ok = wait_warp(&m_empty[mr.slot], mr.phase ^ 1u, abort, error)))
+        // the min tile's last chunk, gc - 3, is done
+        if (SUMS && gc >= 3 && !(ok = wait_warp(&done[cr.slot], cr.phase ^ 1u, abort, error)))
           break;
         tc::fence_after_sync();
         const uint8_t* raw_row =
@@ -692,18 +699,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (SUMS) {
           // the four blocks' min terms at K 4h.. and 8 + 4h.. of the chunk's
           // min tile row
-          uint8_t* tile = smem + L::M_OFFSET + mr.slot * M_TILE_BYTES;
+          uint8_t* tile = smem + L::M_OFFSET + cr.slot * M_TILE_BYTES;
           const uint2 pair = make_uint2(mins[0], mins[1]);
           *reinterpret_cast<uint2*>(tile + interleave_offset(row_in_tile, 4 * half)) = pair;
           *reinterpret_cast<uint2*>(tile + interleave_offset(row_in_tile, 8 + 4 * half)) = pair;
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          mr.advance();
         }
         tc::tmem_store_wait();
         tc::fence_before_sync();
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&a_full[ar.slot]);
+        if (lane == 0) tc::mbar_arrive(half == 0 ? &ready[cr.slot] : &half1[cr.slot]);
         ar.advance(2);
+        cr.advance();
       }
     }
   } else if (warp < FIRST_EPILOGUE + EPILOGUE_WARPS) {
@@ -715,23 +722,30 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     float sum[TILE_VECTORS];
 #pragma unroll
     for (int i = 0; i < TILE_VECTORS; ++i) sum[i] = 0.0f;
-    Ring<2> accr;
+    // both accumulators start empty: chunks 0 and 1 may start
+    if (lane == 0) {
+      tc::mbar_arrive(&ready[0]);
+      tc::mbar_arrive(&ready[1]);
+    }
+    Ring<3> cr;
+    int gc = 0;
     bool ok = true;
     for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
       const int c0 = plan.chunk_begin(u), c1 = plan.chunk_end(u);
-      for (int c = c0; ok && c < c1; ++c) {
-        if (!(ok = wait_warp(&acc_full[accr.slot], accr.phase, abort, error))) break;
+      for (int c = c0; ok && c < c1; ++c, ++gc) {
+        if (!(ok = wait_warp(&done[cr.slot], cr.phase, abort, error))) break;
         tc::fence_after_sync();
-        const uint32_t at = tmem + lane_base + 64 * accr.slot;
+        const uint32_t at = tmem + lane_base + 64 * (gc & 1);
 #pragma unroll
         for (int part = 0; part < 2; ++part) {
           uint32_t v[32];
           tmem_load_32_nowait(at + 32 * part, v);
           asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
           if (part == 1) {
+            // the accumulator is free for chunk gc + 2
             tc::fence_before_sync();
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(&acc_empty[accr.slot]);
+            if (lane == 0) tc::mbar_arrive(&ready[(cr.slot + 2) % 3]);
           }
           if (c == c0) {
 #pragma unroll
@@ -742,7 +756,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
               sum[32 * part + i] = __fadd_rn(sum[32 * part + i], __uint_as_float(v[i]));
           }
         }
-        accr.advance();
+        cr.advance();
       }
       if (!ok) break;
       // the unit's output: this thread's row, all 64 vectors of the pass

@@ -432,9 +432,36 @@ __global__ void gated_rms_norm_by_name(const float* x, const float* __restrict__
   }
 }
 
+// ---- the read-only bandwidth probe (bandwidth.hip:5-20) ---------------------------------------
+// read_sum_f32x4(x, n4, partials): n4 float4 values read once, one partial
+// sum per block -- how fast HBM serves pure reads (the copy peak counts a
+// write for every read). Four loads of a thread in flight at a time.
+__global__ void __launch_bounds__(256)
+    read_sum_by_name(const float4* __restrict__ x, long long n4, float* __restrict__ partials) {
+  __shared__ float partial[32];
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  float sum = 0.0f;
+  for (; i + 3 * stride < n4; i += 4 * stride) {
+    float4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) v[u] = __ldcs(x + i + u * stride);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) sum += (v[u].x + v[u].y) + (v[u].z + v[u].w);
+  }
+  for (; i < n4; i += stride) {
+    const float4 v = __ldcs(x + i);
+    sum += (v.x + v.y) + (v.z + v.w);
+  }
+  const float total = block_sum(sum, partial);
+  if (threadIdx.x == 0) partials[blockIdx.x] = total;
+}
+
 }  // namespace
 
-#define DRIFT_BY_NAME_TYPE(name, T)                                                 \
+DRIFT_REGISTER(read_sum_f32x4, read_sum_by_name)
+
+#define DRIFT_BY_NAME_TYPE(name, T)                                               \
   DRIFT_REGISTER(gather_##name, gather_by_name<T>)                                  \
   DRIFT_REGISTER(matvec_float_x_##name, matvec_by_name<T>)                         \
   DRIFT_REGISTER(matvec_float_x_narrow_##name, matvec_by_name<T>)                  \

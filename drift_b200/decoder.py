@@ -166,6 +166,12 @@ class DenseDecoder:
         self.gate = torch.zeros(b, self.ffn, **f32)
         self.up = torch.zeros(b, self.ffn, **f32)
         self.logits = torch.zeros(b, self.vocab_rows, **f32)
+        # the greedy choice of each sequence's next token over the whole
+        # vocabulary (this rank's rows, gathered and merged across ranks)
+        self.next_ids = torch.zeros(b, dtype=torch.int32, device="cuda")
+        vocab_lo, _ = row_range(c.vocab, weights.rank, weights.world)
+        from .tensor_parallel import VocabSampler
+        self.sampler = VocabSampler(ops, b, vocab_lo, group, device="cuda")
         # x's records for the products, written by the kernel that makes x
         # (the norms, the attention join, SwiGLU): one buffer, each product
         # reading it before the next producer writes it
@@ -198,8 +204,10 @@ class DenseDecoder:
     def step(self, positions: Optional[list[int]] = None) -> torch.Tensor:
         """One decode step: self.ids at self.positions (device, one per
         sequence, set by the caller) -> self.logits [batch, this rank's
-        vocabulary rows]. `positions` is not needed: the kernels read the
-        device copy (so a captured step replays at new positions)."""
+        vocabulary rows] and self.next_ids [batch], each sequence's greedy
+        next token (the argmax over the whole vocabulary; a generation loop
+        copies it into self.ids). `positions` is not needed: the kernels read
+        the device copy (so a captured step replays at new positions)."""
         ops, c, w = self.ops, self.config, self.weights
         b, hd = self.batch, c.head_dim
         prepared = self.prepared
@@ -238,6 +246,7 @@ class DenseDecoder:
             self._all_reduce(self.projected)
             ops.add_rms_norm(self.x, self.projected, next_norm, prepared)
         ops.linears(self.normed, [w.lm_head], [self.logits], prepared)
+        self.sampler(self.logits, self.next_ids)
         return self.logits
 
     def reserve(self) -> None:

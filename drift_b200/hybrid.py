@@ -378,6 +378,11 @@ class HybridDecoder:
                              else torch.zeros(b, c.shared_ffn, **f32))
         self.shared_out = self.all_out[routed:]
         self.logits = torch.zeros(b, span(part.vocab), **f32)
+        # each sequence's greedy next token over the whole vocabulary
+        self.next_ids = torch.zeros(b, dtype=torch.int32, device="cuda")
+        from .tensor_parallel import VocabSampler
+        self.sampler = VocabSampler(ops, b, part.vocab[0], group if part.world > 1 else None,
+                                    device="cuda")
         widest = max(c.hidden, self.value_width, self.q_heads * c.head_dim, c.shared_ffn)
         self.prepared = ops.prepared_x(b, widest)
         self.graph: Optional[torch.cuda.CUDAGraph] = None
@@ -482,7 +487,9 @@ class HybridDecoder:
         self.exchange.add_rms_norm(1, self.x, next_norm, P)
 
     def step(self) -> torch.Tensor:
-        """One decode step: self.ids at self.positions -> self.logits."""
+        """One decode step: self.ids at self.positions -> self.logits (this
+        rank's vocabulary rows) and self.next_ids (each sequence's greedy next
+        token over the whole vocabulary)."""
         ops, c, w, P = self.ops, self.config, self.weights, self.prepared
         ops.embedding(w.embedding, self.ids, self.x)
         ops.add_rms_norm(self.x, None, RowNorm(w.layers[0].input_norm, c.epsilon, 0.0, self.normed),
@@ -501,6 +508,7 @@ class HybridDecoder:
                          else w.final_norm)
             self._mixture(layer.mixture, following)
         ops.linears(self.normed, [w.lm_head], [self.logits], P)
+        self.sampler(self.logits, self.next_ids)
         return self.logits
 
     def reserve(self) -> None:

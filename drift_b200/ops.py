@@ -534,6 +534,41 @@ class CudaOps:
                                                self._stream())
         check("drift_gated_rms_norm", status)
 
+    # -- SequenceOps sampling (ops/SequenceOps.scala:14-20) ------------------------------------------
+    def argmax(self, values, ids, out_values=None, id_offset: int = 0) -> None:
+        """Each row's argmax (CpuSequence.argmax's order) into ids [rows]
+        (int32), plus id_offset; its value into out_values when given."""
+        _f32("argmax", values)
+        width = values.shape[-1]
+        rows = values.numel() // max(width, 1)
+        _require(ids.dtype == torch.int32 and ids.numel() == rows, f"argmax: ids {list(ids.shape)}")
+        check("drift_argmax", self.lib.drift_argmax(_ptr(values), rows, width, id_offset, _ptr(ids),
+                                                    _ptr(out_values), self._stream()))
+
+    def argmax_merge(self, values, ids_in, ids, out_values=None) -> None:
+        """The argmax over gathered (value, id) pairs [rows, n]."""
+        rows, n = values.shape
+        check("drift_argmax_merge", self.lib.drift_argmax_merge(
+            _ptr(values), _ptr(ids_in), rows, n, _ptr(ids), _ptr(out_values), self._stream()))
+
+    def candidates(self, values, count: int, ids, out_values=None, id_offset: int = 0) -> None:
+        """Each row's `count` largest (Candidates.of's order) into ids / out_values
+        [rows, count], plus id_offset (SequenceOps.requireCandidates: 1 to 1024)."""
+        _f32("candidates", values)
+        _require(1 <= count <= 1024, f"{count} candidates, 1 to 1024")
+        width = values.shape[-1]
+        rows = values.numel() // max(width, 1)
+        check("drift_candidates", self.lib.drift_candidates(
+            _ptr(values), rows, width, id_offset, count, _ptr(ids), _ptr(out_values),
+            self._stream()))
+
+    def candidates_merge(self, values, ids_in, count: int, ids, out_values=None) -> None:
+        """The `count` largest of gathered (value, id) pairs [rows, n]."""
+        rows, n = values.shape
+        check("drift_candidates_merge", self.lib.drift_candidates_merge(
+            _ptr(values), _ptr(ids_in), rows, n, count, _ptr(ids), _ptr(out_values),
+            self._stream()))
+
     # -- ExpertsOps (ops/ExpertsOps.scala) -------------------------------------------------------------
     def route(self, logits, ids, weights) -> None:
         """Top-k routing (ExpertsOps.scala:116-120; checks L252-269)."""

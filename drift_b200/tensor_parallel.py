@@ -137,6 +137,49 @@ def max_over_ranks(value: float, device=None, group: Optional[Any] = None) -> fl
     return float(t.item())
 
 
+class VocabSampler:
+    """The greedy choice of the next token with the lm-head split by
+    vocabulary rows: each rank's argmax over its rows [offset, offset +
+    rows) as (value, id) pairs -- the id global, so the reference's rule for
+    a NaN at id 0 holds across shards -- one all-gather of the pairs (ids and
+    value bits in one int32 tensor), then every rank merges the same pairs
+    and picks the same ids (SequenceOps.argmax, CpuSequence.scala:12-22, over
+    the whole vocabulary). On one rank: the argmax itself.
+
+    `ops` supplies argmax(values, ids, out_values, id_offset) and
+    argmax_merge(values, ids_in, ids, out_values) (CudaOps on a GPU); the
+    gathers are torch.distributed's (NCCL, capturable in a CUDA graph)."""
+
+    def __init__(self, ops: Any, batch: int, offset: int, group: Optional[Any] = None,
+                 device=None):
+        import torch
+        import torch.distributed as dist
+
+        self.ops, self.batch, self.offset, self.group = ops, batch, offset, group
+        self.world = dist.get_world_size(group) if group is not None else 1
+        if self.world > 1:
+            # [2, batch]: row 0 the ids, row 1 the values' bits
+            self.local = torch.zeros(2, batch, dtype=torch.int32, device=device)
+            # the ranks' pairs one after the other: [world * 2, batch]
+            self.gathered = torch.zeros(self.world * 2, batch, dtype=torch.int32, device=device)
+
+    def __call__(self, logits, out_ids) -> None:
+        """out_ids [batch] (int32) <- each row's argmax over the whole vocabulary."""
+        import torch.distributed as dist
+
+        if self.world == 1:
+            self.ops.argmax(logits, out_ids, None, self.offset)
+            return
+        import torch
+
+        values = self.local[1].view(torch.float32)
+        self.ops.argmax(logits, self.local[0], values, self.offset)
+        dist.all_gather_into_tensor(self.gathered, self.local, group=self.group)
+        pairs = self.gathered.view(self.world, 2, self.batch).permute(1, 2, 0).contiguous()
+        # pairs: [2, batch, world]
+        self.ops.argmax_merge(pairs[1].view(torch.float32), pairs[0], out_ids, None)
+
+
 class _DeviceArray:
     """A CUDA array interface over memory this library allocated, so torch
     can view it without a copy."""

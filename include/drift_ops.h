@@ -113,6 +113,34 @@ int drift_rope(const float* x, const int32_t* positions, float* out, int tokens,
 int drift_route(const float* logits, int32_t* ids, float* weights, int tokens, int experts, int k,
                 drift_stream_t stream);
 
+/* SequenceOps.argmax (ops/SequenceOps.scala:14; CpuSequence.scala:12-22;
+ * HipSequence.scala:15-27, kernels/norm.hip:119-153), per row: ids[r] = the
+ * first index of row r's largest value, compared with `>` from index 0 (a NaN
+ * never wins except at index 0), plus id_offset (a vocabulary shard's first
+ * id: the rule about index 0 is about id 0); out_values[r] (may be NULL) the
+ * value. rows <= 4096. */
+int drift_argmax(const float* values, int64_t rows, int64_t width, int64_t id_offset, int32_t* ids,
+                 float* out_values, drift_stream_t stream);
+/* The merge of gathered argmaxes (new: tensor parallelism splits the
+ * vocabulary): rows of n (value, id) pairs -> the pair argmax would pick over
+ * the whole row, the same on every rank. */
+int drift_argmax_merge(const float* values, const int32_t* ids_in, int64_t rows, int64_t n,
+                       int32_t* ids, float* out_values, drift_stream_t stream);
+/* SequenceOps.candidates (SequenceOps.scala:20; Candidates.of,
+ * ops/Candidates.scala:30-35; HipSequence.scala:43-100, norm.hip:322-363):
+ * each row's `count` (1 to 1024) largest values, largest first, the lower
+ * index first among equals (-0 as 0, a positive NaN above +inf): ids (plus
+ * id_offset) and values, [rows][count] (only the first min(count, width) of a
+ * row are written). rows <= 4096. Uses the library's scratch
+ * (drift_candidates_workspace_bytes). */
+int drift_candidates(const float* values, int64_t rows, int64_t width, int64_t id_offset, int count,
+                     int32_t* ids, float* out_values, drift_stream_t stream);
+size_t drift_candidates_workspace_bytes(int64_t rows, int64_t width, int count);
+/* The merge of gathered candidates: rows of n (value, id) pairs with unique
+ * ids -> the row's `count` largest by the same order, ids compared as ids. */
+int drift_candidates_merge(const float* values, const int32_t* ids_in, int64_t rows, int64_t n,
+                           int count, int32_t* ids, float* out_values, drift_stream_t stream);
+
 /* Ops.expertsLinear (ExpertsOps.scala:122-126; HipExperts.scala:76-168): slot
  * s multiplies expert ids[s] of weight [experts, n, k] with x row
  * s / (slots / x_rows), into out [slots, n]. An id outside [0, experts)

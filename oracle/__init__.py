@@ -70,6 +70,8 @@ def lib() -> ctypes.CDLL:
             "oracle_activation": (None, [i32, f32, p, p, i64]),
             "oracle_inverse_frequency": (f32, [f32, i32, i32]),
             "oracle_rope": (None, [p, p, p, i32, i32, i32, f32, i32, i32]),
+            "oracle_argmax": (ctypes.c_int64, [p, ctypes.c_int64]),
+            "oracle_candidates": (i32, [p, ctypes.c_int64, ctypes.c_int64, i32, p, p]),
             "oracle_rope_sections": (None, [p, p, p, i32, i32, i32, f32, i32, i32, i32, i32, i32,
                                             i32, i32]),
             "oracle_route": (None, [p, i32, i32, i32, p, p]),
@@ -238,6 +240,27 @@ def rope_sections(x, positions, theta: float, rotary: int, layout: int, sections
     lib().oracle_rope_sections(_p(x), _p(positions), _p(out), tokens, heads, dim, theta, rotary,
                                layout, sections, s0, s1, s2, s3)
     return out
+
+
+def argmax(values) -> int:
+    """CpuSequence.argmax over all the values: the first index of the largest
+    by `>` from index 0 (a NaN never wins unless at index 0)."""
+    values = _f32(values).reshape(-1)
+    return int(lib().oracle_argmax(_p(values), values.size))
+
+
+def candidates(values, count: int):
+    """Candidates.of: each row's `count` largest (ids, values), largest first,
+    the lower index first among equals (-0 ranks as 0; NaN above +inf)."""
+    values = _f32(values)
+    width = values.shape[-1]
+    rows = values.size // width
+    kept = min(count, width)
+    ids = np.empty((rows, kept), np.int32)
+    out = np.empty((rows, kept), np.float32)
+    if lib().oracle_candidates(_p(values), rows, width, count, _p(ids), _p(out)) != 0:
+        raise ValueError("oracle candidates refused its arguments")
+    return ids, out
 
 
 def route(logits, k: int):

@@ -80,6 +80,8 @@ def test_decode_step_matches_the_oracle(batch):
     expected = reference_step(c, weights, caches, tables, ids, positions)
     ok, _, _, summary = within(logits, expected, 1e-4, 1e-3)
     assert ok, summary
+    # the step's greedy choice: the CPU argmax of its own logits, bit for bit
+    assert list(decoder.next_ids.cpu().numpy()) == [oracle.argmax(row) for row in logits]
     # the caches took the new keys and values: the same F16 values, give or
     # take the rounding of inputs that differ in their last F32 bits (the
     # write itself is bit-exact, test_gpu_attention.py)
@@ -103,4 +105,5 @@ def test_captured_step_replays_the_eager_step():
     decoder.replay()
     torch.cuda.synchronize()
     assert torch.equal(decoder.logits, eager)
+    assert list(decoder.next_ids.cpu().numpy()) == [oracle.argmax(r) for r in eager.cpu().numpy()]
     decoder.release()

@@ -5,7 +5,9 @@ addRmsNorm, bit for bit; and a two-rank decode step over the peer exchange
 equals the same step over NCCL's all-reduce (for two ranks both sums are
 p0 + p1); and the expert-parallel hybrid MoE step (DeltaNet and query heads,
 experts and vocabulary split over two ranks) equals the whole model's step on
-one GPU within the benchmark's bar. Skipped with fewer than two GPUs."""
+one GPU within the benchmark's bar; in both, every rank's greedy next token
+is the argmax of the whole vocabulary's gathered row. Skipped with fewer
+than two GPUs."""
 
 import os
 import socket
@@ -13,6 +15,8 @@ from datetime import timedelta
 
 import pytest
 import torch
+
+import oracle
 
 pytestmark = pytest.mark.gpu
 
@@ -89,6 +93,12 @@ def _decode_ranks(rank: int, world: int, port: int):
             decoder.ids.copy_(torch.tensor([1, 2, 3], dtype=torch.int32))
             decoder.positions.copy_(torch.tensor([20, 18, 7], dtype=torch.int32))
             logits[exchange] = decoder.step().clone()
+            # the greedy choice over both ranks' vocabulary rows: every rank
+            # picks the argmax of the whole gathered row
+            gathered = [torch.empty_like(logits[exchange]) for _ in range(world)]
+            dist.all_gather(gathered, logits[exchange])
+            whole = torch.cat(gathered, dim=1).cpu().numpy()
+            assert list(decoder.next_ids.cpu().numpy()) == [oracle.argmax(r) for r in whole]
             # and captured: the replay equals the eager step
             decoder.capture([20, 18, 7])
             decoder.replay()
@@ -147,6 +157,12 @@ def _hybrid_ranks(rank: int, world: int, port: int):
         expected = whole.step()[:, p.vocab[0]:p.vocab[1]].clone()
         got = split.step().clone()
         torch.cuda.synchronize()
+        # the greedy choice over the split vocabulary: the argmax of the
+        # gathered rows on every rank
+        gathered = [torch.empty_like(got) for _ in range(world)]
+        dist.all_gather(gathered, got)
+        rows = torch.cat(gathered, dim=1).cpu().numpy()
+        assert list(split.next_ids.cpu().numpy()) == [oracle.argmax(r) for r in rows]
         bound = 1e-4 + 1e-3 * expected.abs()
         assert ((got - expected).abs() <= bound).all(), float((got - expected).abs().max())
         # the recurrent state moved as the whole model's did

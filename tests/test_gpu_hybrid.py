@@ -126,6 +126,8 @@ def test_hybrid_step_matches_the_oracle(c, batch):
     expected = reference_step(c, weights, before, ids, positions)
     ok, _, _, summary = within(logits, expected, 1e-4, 1e-3)
     assert ok, summary
+    # the step's greedy choice: the CPU argmax of its own logits, bit for bit
+    assert list(decoder.next_ids.cpu().numpy()) == [oracle.argmax(row) for row in logits]
     # the recurrent states moved as the oracle's did
     for i, state in decoder.delta_states.items():
         ok, _, _, summary = within(state.cpu().numpy(), before["delta"][i], 1e-4, 1e-3)

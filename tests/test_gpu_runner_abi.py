@@ -318,3 +318,14 @@ def test_add_f32(lib):
     out = torch.empty(5000, device="cuda")
     launch(lib, "add_f32", (5000 + 255) // 256, 256, P(dev(a)), P(dev(b)), P(out), I64(5000))
     assert np.array_equal(out.cpu().numpy(), a + b)
+
+
+def test_read_sum_f32x4(lib):
+    """The bandwidth probe (bandwidth.hip:5-20): one partial sum per block of
+    a grid-stride read; the partials add up to the data's sum."""
+    rng = np.random.default_rng(100)
+    n4 = 1 << 20
+    data = rng.integers(-8, 8, 4 * n4).astype(np.float32)  # sums exact in F32
+    partials = torch.empty(96, device="cuda")
+    launch(lib, "read_sum_f32x4", 96, 256, P(dev(data)), I64(n4), P(partials))
+    assert float(partials.double().sum()) == float(data.astype(np.float64).sum())

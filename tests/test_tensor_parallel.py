@@ -138,3 +138,76 @@ def test_two_gloo_ranks_reassemble_the_product(dtype):
         ok, _, _, summary = within(out, expected, 1e-4, 1e-3)
         assert ok, summary
         assert slowest == float(world)
+
+
+# ---- the greedy choice over vocabulary shards (VocabSampler) ------------------------------------
+class KeyedArgmax:
+    """The device argmax's order on the host (numpy): the value's order bits
+    (a NaN lowest, except at id 0, which is highest) above the id, lower ids
+    first -- so a shard's local choice and the merge pick what
+    CpuSequence.argmax picks over the whole row."""
+
+    @staticmethod
+    def _keys(values, ids):
+        bits = values.astype(np.float32).copy()
+        bits[bits == 0] = 0.0
+        u = bits.view(np.uint32).astype(np.uint64)
+        order = np.where(u & 0x80000000, (~u) & 0xFFFFFFFF, u | 0x80000000)
+        nan = np.isnan(values)
+        order = np.where(nan, np.where(ids == 0, 0xFFFFFFFF, 0), order).astype(np.uint64)
+        return (order << np.uint64(32)) | ((~ids.astype(np.uint64)) & np.uint64(0xFFFFFFFF))
+
+    def argmax(self, values, ids, out_values, id_offset):
+        v = values.numpy()
+        rows, width = v.shape
+        index = np.arange(width, dtype=np.int64) + id_offset
+        best = self._keys(v, np.broadcast_to(index, v.shape)).argmax(axis=1)
+        ids.copy_(torch.from_numpy((best + id_offset).astype(np.int32)))
+        if out_values is not None:
+            out_values.copy_(torch.from_numpy(v[np.arange(rows), best]))
+
+    def argmax_merge(self, values, ids_in, ids, out_values):
+        v, g = values.numpy(), ids_in.numpy().astype(np.int64)
+        best = self._keys(v, g).argmax(axis=1)
+        ids.copy_(torch.from_numpy(g[np.arange(v.shape[0]), best].astype(np.int32)))
+
+
+def _sampler_rank(rank, world, port, results):
+    from drift_b200.tensor_parallel import VocabSampler, row_range
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=__import__("datetime").timedelta(seconds=60))
+    try:
+        rng = np.random.default_rng(3)  # every rank draws the same logits
+        rows, vocab = 4, 1003
+        logits = rng.standard_normal((rows, vocab)).astype(np.float32)
+        logits[0, 17] = logits[0, 900] = 9.0   # a tie across shards: the lower id
+        logits[1, 0] = np.nan                  # a NaN at id 0: id 0, whatever follows
+        logits[2, 5] = np.nan                  # a NaN elsewhere never wins
+        lo, hi = row_range(vocab, rank, world)
+        sampler = VocabSampler(KeyedArgmax(), rows, lo, dist.group.WORLD)
+        ids = torch.empty(rows, dtype=torch.int32)
+        sampler(torch.from_numpy(np.ascontiguousarray(logits[:, lo:hi])), ids)
+        results.put((rank, ids.numpy().copy(), logits))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_vocabulary_shards_choose_the_whole_rows_argmax(world):
+    """Each gloo rank holds a vocabulary shard; after the sampler's gather and
+    merge every rank holds CpuSequence.argmax of the whole rows."""
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_sampler_rank, args=(r, world, port, results))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    got = [results.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, ids, logits in got:
+        assert list(ids) == [oracle.argmax(row) for row in logits], rank
