@@ -83,7 +83,7 @@ SIGNATURES = {
     "drift_attention_decode_gated": (_i32, [_p, _i32, _i32, _p, _p, _i32, _i32, _i32, _i32, _p, _i32,
                                             _p, _i32, _f32, _i32, _f32, _p, _p, _p, _i32, _p, _p]),
     "drift_comm_handle_bytes": (_sz, []),
-    "drift_comm_create": (_i32, [_i32, _i32, _sz, _pp, _p]),
+    "drift_comm_create": (_i32, [_i32, _i32, _sz, _i64, _pp, _p]),
     "drift_comm_open": (_i32, [_p, _p]),
     "drift_comm_slot": (_i32, [_p, _i32, _pp]),
     "drift_comm_destroy": (_i32, [_p]),

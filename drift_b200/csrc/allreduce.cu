@@ -16,8 +16,9 @@
 // counter (every rank makes the same calls in the same order, so the counts
 // agree), stores the count into flag [row][rank] of every rank with a
 // system-scope release, then waits until its own flags [row][p] reach the
-// count for every p, with an acquire -- at most about a second, after which
-// it sets the device error word (code 3) and leaves the row as it was. The
+// count for every p, with an acquire -- at most the comm's wait limit (one
+// second unless drift_comm_create names another), after which it sets the
+// device error word (code 3) and leaves the row as it was. The
 // two slots alternate between consecutive exchanges (o, then down), so a
 // receive slot is pushed into again only after every rank has signalled the
 // exchange in between, that is, after every rank has finished reading it.
@@ -47,6 +48,7 @@ constexpr int MAX_ROWS = 64;
 struct Comm {
   int rank = 0, world = 1;
   size_t slot_bytes = 0;
+  unsigned long long wait_ns = 0;
   uint8_t* local = nullptr;
   uint8_t* peers[MAX_RANKS] = {};
   bool opened[MAX_RANKS] = {};
@@ -65,6 +67,7 @@ struct ExchangeArgs {
   unsigned* flags[MAX_RANKS];     // the flags of every rank
   unsigned* counts;               // this rank's call counts
   long long slot_floats;          // floats from one rank's receive slot to the next
+  unsigned long long wait_ns;     // how long a row waits for its peers
   int rank, world;
   int* error;
 };
@@ -90,7 +93,7 @@ __device__ bool exchange_barrier(const ExchangeArgs& e, int row) {
   const uint64_t start = tc::global_ns();
   for (int p = 0; p < e.world; ++p) {
     while (int(load_acquire_sys(mine + p) - count) < 0) {
-      if (tc::global_ns() - start > 1000000000ull) {
+      if (tc::global_ns() - start > e.wait_ns) {
         atomicCAS(e.error, 0, 3);
         return false;
       }
@@ -192,13 +195,18 @@ using namespace drift;
 
 extern "C" {
 
-int drift_comm_create(int rank, int world, size_t slot_bytes, void** comm, void* handle) {
+int drift_comm_create(int rank, int world, size_t slot_bytes, int64_t wait_limit_ns, void** comm,
+                      void* handle) {
   if (world < 1 || world > MAX_RANKS || rank < 0 || rank >= world)
     return invalid("comm: rank %d of %d (at most %d ranks)", rank, world, MAX_RANKS);
   if (!comm || !handle) return invalid("comm: no handle to fill");
+  if (wait_limit_ns < 0 || wait_limit_ns > 60000000000ll)
+    return invalid("comm: a wait limit of %lld ns (0 for one second, at most 60 s)",
+                   (long long)wait_limit_ns);
   Comm* c = new Comm;
   c->rank = rank;
   c->world = world;
+  c->wait_ns = wait_limit_ns ? (unsigned long long)wait_limit_ns : 1000000000ull;
   c->slot_bytes = (slot_bytes + 255) & ~size_t(255);
   void* memory = nullptr;
   cudaError_t status = cudaMalloc(&memory, c->total());
@@ -280,6 +288,7 @@ int drift_add_rms_norm_allreduce(void* comm, int slot, float* x, const float* we
   e.counts = reinterpret_cast<unsigned*>(c->local + c->counts_offset());
   e.rank = c->rank;
   e.world = c->world;
+  e.wait_ns = c->wait_ns;
   e.error = device_error_word();
   uint8_t* records = static_cast<uint8_t*>(prepared);
   const cudaStream_t s = cudaStream_t(stream);

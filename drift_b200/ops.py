@@ -177,7 +177,9 @@ class CudaOps:
         torch.cuda.current_stream().synchronize()
 
     def take_device_error(self) -> int:
-        """The device error word (1: an id outside its table), cleared."""
+        """The device error word, cleared: 0 none, 1 an id outside its table,
+        2 a bounded wait inside a kernel gave up, 3 the tensor-parallel
+        exchange's wait for a peer rank gave up."""
         code = ctypes.c_int(0)
         check("drift_device_error_take", self.lib.drift_device_error_take(ctypes.byref(code)))
         return code.value

@@ -194,9 +194,12 @@ class PeerExchange:
     drift_comm_*): two slots of `rows` x `cols` F32 partial rows per rank,
     readable by every rank of `group`; `add_rms_norm` sums the ranks'
     partials of a slot in rank order into x and normalises, in one launch.
-    Consecutive exchanges alternate slots (o, then down)."""
+    Consecutive exchanges alternate slots (o, then down). A row waits for
+    its peers at most `wait_limit_ns` (0: one second); a wait that runs out
+    sets device error 3 and leaves the row as it was, and the exchange must
+    then be closed on every rank."""
 
-    def __init__(self, ops, group, rows: int, cols: int):
+    def __init__(self, ops, group, rows: int, cols: int, wait_limit_ns: int = 0):
         import ctypes
 
         import torch
@@ -209,7 +212,8 @@ class PeerExchange:
         comm = ctypes.c_void_p()
         handle = ctypes.create_string_buffer(self.lib.drift_comm_handle_bytes())
         check("drift_comm_create", self.lib.drift_comm_create(rank, world, rows * cols * 4,
-                                                              ctypes.byref(comm), handle))
+                                                              wait_limit_ns, ctypes.byref(comm),
+                                                              handle))
         self.comm = comm
         handles: list = [None] * world
         dist.all_gather_object(handles, handle.raw, group=group)

@@ -333,13 +333,19 @@ int drift_linears_prepared(int x_dtype, const void* x, const void* prepared, int
  * of drift_comm_handle_bytes() bytes, gathers every rank's handle (rank
  * order) and opens them. A row-split product writes its partial rows into a
  * slot (drift_comm_slot); drift_add_rms_norm_allreduce then, on every rank,
- * waits (bounded, about a second; then device error code 3) for every rank's
- * partials of that slot, adds their sum in rank order to x and writes
- * rmsNorm(x) (and, with `prepared`, its records): the runner's all-reduce and
- * addRmsNorm in one launch. Consecutive exchanges must alternate slots; at
- * most 64 rows of 4096 values. */
+ * waits for every rank's partials of that slot, adds their sum in rank order
+ * to x and writes rmsNorm(x) (and, with `prepared`, its records): the
+ * runner's all-reduce and addRmsNorm in one launch. Consecutive exchanges
+ * must alternate slots; at most 64 rows of 4096 values.
+ * Each row's wait is bounded by `wait_limit_ns` (0: one second; at most 60
+ * s). When it runs out -- a rank that skipped or never reached the exchange
+ * -- the kernel sets device error code 3, leaves that row's x and out as
+ * they were and returns; the ranks' exchange counts then disagree, so every
+ * rank synchronizes and destroys the comm (after a host barrier: a peer may
+ * still be pushing into this rank's buffer until its own call returns). */
 size_t drift_comm_handle_bytes(void);
-int drift_comm_create(int rank, int world, size_t slot_bytes, void** comm, void* handle);
+int drift_comm_create(int rank, int world, size_t slot_bytes, int64_t wait_limit_ns, void** comm,
+                      void* handle);
 int drift_comm_open(void* comm, const void* handles);
 int drift_comm_slot(void* comm, int slot, void** pointer);
 int drift_comm_destroy(void* comm);
