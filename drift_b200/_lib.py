@@ -73,6 +73,8 @@ SIGNATURES = {
     "drift_causal_conv": (_i32, [_p, _i32, _i32, _p, _i32, _i32, _p, _p, _p, _p]),
     "drift_gated_delta_rule": (_i32, [_p, _i32, _i32, _i32, _i32, _i32, _p, _p, _p, _p, _p, _p, _p,
                                       _p]),
+    "drift_delta_decode_step": (_i32, [_p, _p, _i32, _i32, _i32, _i32, _i32, _p, _i32, _p, _p, _p,
+                                        _p, _p, _p, _p, _p, _f32, _p, _p, _p]),
     "drift_gated_rms_norm": (_i32, [_p, _p, _p, _i32, _f32, _p, _i64, _i64, _i32, _p, _p]),
     "drift_causal_conv_decode": (_i32, [_p, _i32, _i32, _p, _i32, _i32, _p, _p, _p]),
     "drift_gated_delta_rule_decode": (_i32, [_p, _i32, _i32, _i32, _i32, _i32, _p, _p, _p, _p, _p,
@@ -91,6 +93,8 @@ SIGNATURES = {
     "drift_add_rms_norm_prepared": (_i32, [_p, _p, _p, _f32, _f32, _p, _i64, _i64, _p, _p]),
     "drift_gated_prepared": (_i32, [_i32, _p, _p, _p, _i64, _i64, _p, _p]),
     "drift_linears_prepared": (_i32, [_i32, _p, _p, _i32, _p, _p, _p, _p, _i64, _i64, _p]),
+    "drift_linears_gated_prepared": (_i32, [_i32, _i32, _p, _p, _i32, _p, _p, _p, _p, _p, _i64,
+                                            _i64, _i64, _p, _p]),
     "drift_attention_decode_prepared": (_i32, [_p, _i32, _i32, _p, _p, _i32, _i32, _i32, _i32, _p,
                                                _i32, _p, _i32, _f32, _i32, _f32, _p, _p, _p, _p]),
     "drift_rope": (_i32, [_p, _p, _p, _i32, _i32, _i32, _f32, _i32, _i32, _p]),

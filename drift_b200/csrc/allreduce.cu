@@ -1,27 +1,27 @@
 // The tensor-parallel decode step's exchange over NVLink peer memory, fused
 // into the kernel that consumes it. A row-split product (o, down: each rank
-// sums its own columns' share) writes its partial rows into one of two slots
-// of a buffer every rank of the group can read (CUDA IPC). The next kernel,
-// on every rank, is `add_rms_norm_allreduce`: it pushes its partial rows into
-// its receive slot on every rank (stores over NVLink), tells its peers they
-// are there, waits (bounded) until theirs have arrived, sums the ranks'
-// partials in rank order from its own memory -- every rank the same bits --
-// adds the sum to the residual, and normalises, writing the next product's x
-// records too. It
-// takes the place of the runner's all-reduce followed by addRmsNorm (an NCCL
-// collective and a norm launch) with one launch and one crossing of NVLink
-// per value.
+// sums its own columns' share) writes its partial rows into one of two send
+// slots. The next kernel, on every rank, is `add_rms_norm_allreduce`: it
+// pushes its partial rows into its lane of the slot on every rank (stores
+// over NVLink), waits (bounded) until every rank's lane holds this call's
+// rows, sums the ranks' partials in rank order from its own memory -- every
+// rank the same bits -- adds the sum to the residual, and normalises,
+// writing the next product's x records too. It takes the place of the
+// runner's all-reduce followed by addRmsNorm (an NCCL collective and a norm
+// launch) with one launch and one crossing of NVLink per value.
 //
-// Synchronisation, per row of x (a CTA): the CTA counts its calls in a local
+// Synchronisation: each value travels with its row's call count in one
+// 64-bit word (value bits low, count high), stored and loaded whole, so a
+// word that shows this call's count holds this call's value -- no fence and
+// no separate flag round trip. A CTA (one row) counts its calls in a local
 // counter (every rank makes the same calls in the same order, so the counts
-// agree), stores the count into flag [row][rank] of every rank with a
-// system-scope release, then waits until its own flags [row][p] reach the
-// count for every p, with an acquire -- at most the comm's wait limit (one
-// second unless drift_comm_create names another), after which it sets the
-// device error word (code 3) and leaves the row as it was. The
-// two slots alternate between consecutive exchanges (o, then down), so a
-// receive slot is pushed into again only after every rank has signalled the
-// exchange in between, that is, after every rank has finished reading it.
+// agree) and polls its lanes' words until each shows the count -- at most
+// the comm's wait limit (one second unless drift_comm_create names
+// another), after which it sets the device error word (code 3) and leaves
+// the row as it was. The two slots alternate between consecutive exchanges
+// (o, then down), so a lane is pushed into again only after every rank has
+// passed the exchange in between, that is, after every rank has finished
+// reading it.
 #include <cuda_runtime.h>
 
 #include <cstring>
@@ -42,9 +42,8 @@ constexpr int MAX_RANKS = 8;
 constexpr int MAX_ROWS = 64;
 
 // The buffer of a rank: two send slots of partial rows (the products write
-// them), two receive slots per rank (the ranks push their send slots there),
-// then the flags [MAX_ROWS][MAX_RANKS] that peers store into, then the local
-// call counts [MAX_ROWS].
+// them, F32), then per slot a lane per rank of 64-bit words (value, count)
+// that the ranks push into, then the local call counts [MAX_ROWS].
 struct Comm {
   int rank = 0, world = 1;
   size_t slot_bytes = 0;
@@ -52,55 +51,31 @@ struct Comm {
   uint8_t* local = nullptr;
   uint8_t* peers[MAX_RANKS] = {};
   bool opened[MAX_RANKS] = {};
-  // send slot s; the copy of rank p's send slot s that p pushes here
+  // send slot s; rank p's lane of slot s (twice the slot: a word per value)
   size_t send_offset(int s) const { return s * slot_bytes; }
-  size_t receive_offset(int s, int p) const { return (2 + s * MAX_RANKS + p) * slot_bytes; }
-  size_t flags_offset() const { return (2 + 2 * MAX_RANKS) * slot_bytes; }
-  size_t counts_offset() const { return flags_offset() + MAX_ROWS * MAX_RANKS * 4; }
+  size_t lane_offset(int s, int p) const { return 2 * slot_bytes + (s * MAX_RANKS + p) * 2 * slot_bytes; }
+  size_t counts_offset() const { return 2 * slot_bytes + 2 * MAX_RANKS * 2 * slot_bytes; }
   size_t total() const { return counts_offset() + MAX_ROWS * 4; }
 };
 
 struct ExchangeArgs {
-  const float* send;              // this rank's send slot
-  float* pushes[MAX_RANKS];       // this rank's receive slot on every rank
-  const float* received;          // this rank's receive slots (rank-major)
-  unsigned* flags[MAX_RANKS];     // the flags of every rank
-  unsigned* counts;               // this rank's call counts
-  long long slot_floats;          // floats from one rank's receive slot to the next
-  unsigned long long wait_ns;     // how long a row waits for its peers
+  const float* send;                      // this rank's send slot
+  unsigned long long* pushes[MAX_RANKS];  // this rank's lane of the slot on every rank
+  const unsigned long long* lanes;        // this rank's lanes of the slot (rank-major)
+  unsigned* counts;                       // this rank's call counts
+  long long lane_words;                   // words from one rank's lane to the next
+  unsigned long long wait_ns;             // how long a row waits for its peers
   int rank, world;
   int* error;
 };
 
-__device__ __forceinline__ void store_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void store_relaxed_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ unsigned load_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long load_relaxed_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
-}
-
-// The row's exchange: signal, then wait for every rank. Thread 0 of the CTA;
-// returns whether every rank arrived.
-__device__ bool exchange_barrier(const ExchangeArgs& e, int row) {
-  const unsigned count = e.counts[row] + 1;
-  e.counts[row] = count;
-  // the CTA's pushes (ordered before this by the barrier) go out before the
-  // flags: each flag store is a system-scope release
-  for (int p = 0; p < e.world; ++p) store_release_sys(e.flags[p] + row * MAX_RANKS + e.rank, count);
-  const unsigned* mine = e.flags[e.rank] + row * MAX_RANKS;
-  const uint64_t start = tc::global_ns();
-  for (int p = 0; p < e.world; ++p) {
-    while (int(load_acquire_sys(mine + p) - count) < 0) {
-      if (tc::global_ns() - start > e.wait_ns) {
-        atomicCAS(e.error, 0, 3);
-        return false;
-      }
-      __nanosleep(200);
-    }
-  }
-  return true;
 }
 
 // x[row] += sum over ranks of the slots' row, in rank order; then out =
@@ -113,31 +88,77 @@ __global__ void __launch_bounds__(THREADS) add_rms_norm_allreduce_kernel(
   pdl_trigger();  // the next kernel may launch and wait for this one
   pdl_wait();     // this rank's partials (the product before) are written
   __shared__ float partial[32];
-  __shared__ int arrived;
+  __shared__ unsigned call;
+  __shared__ int failed;
   const int row_index = blockIdx.x;
-  // push this rank's partial row into its receive slot on every rank (plain
-  // stores over NVLink: no round trip to wait for)
+  if (threadIdx.x == 0) {
+    call = e.counts[row_index] + 1;
+    e.counts[row_index] = call;
+    failed = 0;
+  }
+  __syncthreads();
+  const unsigned long long count = (unsigned long long)call << 32;
+  static_assert(MAX_RANKS * PER <= 32, "a thread's words fit one bit mask");
+  // push this rank's partial row into its lane on every rank (plain stores
+  // over NVLink: no round trip to wait for)
   {
     const float* mine = e.send + (long long)row_index * cols;
-    float own[PER];
+    unsigned long long own[PER];
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
       const int c = threadIdx.x + i * THREADS;
-      own[i] = c < cols ? mine[c] : 0.0f;
+      own[i] = count | (c < cols ? __float_as_uint(mine[c]) : 0u);
     }
     for (int p = 0; p < e.world; ++p) {
-      float* to = e.pushes[p] + (long long)row_index * cols;
+      unsigned long long* to = e.pushes[p] + (long long)row_index * cols;
 #pragma unroll
       for (int i = 0; i < PER; ++i) {
         const int c = threadIdx.x + i * THREADS;
-        if (c < cols) __stcg(to + c, own[i]);
+        if (c < cols) store_relaxed_sys(to + c, own[i]);
       }
     }
   }
+  // every rank's words of this row, each polled until it shows this call
+  // (a pass's loads all in flight before the first is checked)
+  float part[MAX_RANKS][PER];
+  unsigned pending = 0;  // bit p PER + i: rank p's value i not yet in
+#pragma unroll
+  for (int p = 0; p < MAX_RANKS; ++p)
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      part[p][i] = 0.0f;
+      if (p < e.world && threadIdx.x + i * THREADS < cols) pending |= 1u << (p * PER + i);
+    }
+  const uint64_t start = tc::global_ns();
+  while (pending) {
+#pragma unroll
+    for (int p = 0; p < MAX_RANKS; ++p) {
+      if (p >= e.world) break;
+      const unsigned long long* lane = e.lanes + p * e.lane_words + (long long)row_index * cols;
+      unsigned long long w[PER];
+#pragma unroll
+      for (int i = 0; i < PER; ++i)
+        w[i] = (pending >> (p * PER + i)) & 1u ? load_relaxed_sys(lane + threadIdx.x + i * THREADS)
+                                               : 0ull;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const unsigned bit = 1u << (p * PER + i);
+        if ((pending & bit) && unsigned(w[i] >> 32) == call) {
+          part[p][i] = __uint_as_float(unsigned(w[i]));
+          pending &= ~bit;
+        }
+      }
+    }
+    if (!pending) break;
+    if (tc::global_ns() - start > e.wait_ns) {
+      atomicCAS(e.error, 0, 3);
+      failed = 1;
+      break;
+    }
+    __nanosleep(64);
+  }
   __syncthreads();
-  if (threadIdx.x == 0) arrived = exchange_barrier(e, row_index);
-  __syncthreads();
-  if (!arrived) return;
+  if (failed) return;
   float* row = x + (long long)row_index * cols;
   float value[PER], w[PER], sum[PER];
 #pragma unroll
@@ -147,18 +168,7 @@ __global__ void __launch_bounds__(THREADS) add_rms_norm_allreduce_kernel(
     w[i] = c < cols ? weight[c] : 0.0f;
     sum[i] = 0.0f;
   }
-  // every rank's values issued before the first is used, then summed in
-  // rank order
-  float part[MAX_RANKS][PER];
-#pragma unroll
-  for (int p = 0; p < MAX_RANKS; ++p) {
-    const float* peer = e.received + (p < e.world ? p : 0) * e.slot_floats + (long long)row_index * cols;
-#pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      const int c = threadIdx.x + i * THREADS;
-      part[p][i] = p < e.world && c < cols ? __ldcv(peer + c) : 0.0f;
-    }
-  }
+  // summed in rank order
 #pragma unroll
   for (int p = 0; p < MAX_RANKS; ++p)
     if (p < e.world) {
@@ -279,12 +289,10 @@ int drift_add_rms_norm_allreduce(void* comm, int slot, float* x, const float* we
   if (rows == 0) return 0;
   ExchangeArgs e = {};
   e.send = reinterpret_cast<const float*>(c->local + c->send_offset(slot));
-  e.received = reinterpret_cast<const float*>(c->local + c->receive_offset(slot, 0));
-  e.slot_floats = (long long)(c->slot_bytes / 4);
-  for (int p = 0; p < c->world; ++p) {
-    e.pushes[p] = reinterpret_cast<float*>(c->peers[p] + c->receive_offset(slot, c->rank));
-    e.flags[p] = reinterpret_cast<unsigned*>(c->peers[p] + c->flags_offset());
-  }
+  e.lanes = reinterpret_cast<const unsigned long long*>(c->local + c->lane_offset(slot, 0));
+  e.lane_words = (long long)(2 * c->slot_bytes / 8);
+  for (int p = 0; p < c->world; ++p)
+    e.pushes[p] = reinterpret_cast<unsigned long long*>(c->peers[p] + c->lane_offset(slot, c->rank));
   e.counts = reinterpret_cast<unsigned*>(c->local + c->counts_offset());
   e.rank = c->rank;
   e.world = c->world;

@@ -217,7 +217,152 @@ __global__ void __launch_bounds__(128) gated_rms_norm_kernel(
   }
 }
 
+// A DeltaNet layer's decode step after its input products, one CTA per
+// (value head h, sequence), when every value head has a key head of its own
+// (key_heads == value_heads: a CTA then owns its q, k and v channels and
+// their convolution state): the causal convolution of the head's 3 D
+// channels (causal_conv_kernel's arithmetic), the gated delta rule on its
+// D x D state (gated_delta_rule_kernel's: 4 D / 32 warps, warp w the
+// columns of slice w % 4 and the rows of group w / 4, the column sums met
+// in the same order), then the RMS norm of the head's output times SiLU(z)
+// with the out projection's records (gated_rms_norm_kernel's) -- three
+// launches' work in one, with the same bits.
+constexpr int STEP_D = 128, STEP_THREADS = 4 * STEP_D;  // 16 warps
+__global__ void __launch_bounds__(STEP_THREADS) delta_decode_step_kernel(
+    const float* __restrict__ qkv, const float* __restrict__ z, int heads,
+    const float* __restrict__ conv_weight, int taps, float* __restrict__ conv_states,
+    const float* __restrict__ a, const float* __restrict__ b, const float* __restrict__ decay,
+    const float* __restrict__ dt_bias, float* __restrict__ states,
+    const float* __restrict__ norm_weight, float epsilon, float* __restrict__ out,
+    uint8_t* __restrict__ records) {
+  pdl_trigger();  // the next kernel may launch and wait for this one
+  pdl_wait();     // what the kernels before this one wrote is visible
+  constexpr int D = STEP_D, ROWS = D / RULE_WARPS, SLICES = D / RULE_COLUMNS;
+  __shared__ float conv[3 * D];  // the head's convolved q, k, v
+  __shared__ float sums[RULE_WARPS][SLICES][RULE_COLUMNS];
+  __shared__ float o[D];
+  __shared__ float partial[32];
+  const int h = blockIdx.x, seq = blockIdx.y, tid = threadIdx.x;
+  const int channels = 3 * heads * D, span = taps - 1;
+  // the convolution: thread t < 3 D takes channel (t / D) (heads D) + h D + t % D
+  if (tid < 3 * D) {
+    const int c = (tid / D) * heads * D + h * D + tid % D;
+    float* state = conv_states + (long long)seq * span * channels;
+    float window[MAX_SPAN];
+#pragma unroll
+    for (int i = 0; i < MAX_SPAN; ++i) window[i] = i < span ? state[(long long)i * channels + c] : 0.0f;
+    const float* w = conv_weight + (long long)c * taps;
+    const float current = qkv[(long long)seq * channels + c];
+    float sum = 0.0f;
+    for (int i = 0; i < taps - 1; ++i) {
+      const int at = span - (taps - 1 - i);
+      float seen = 0.0f;
+#pragma unroll
+      for (int t = 0; t < MAX_SPAN; ++t)
+        if (t == at) seen = window[t];
+      sum = fmaf(w[i], seen, sum);
+    }
+    sum = fmaf(w[taps - 1], current, sum);
+    conv[tid] = sum / (1.0f + expf(-sum));
+#pragma unroll
+    for (int t = 0; t + 1 < MAX_SPAN; ++t)
+      if (t + 1 < span) window[t] = window[t + 1];
+#pragma unroll
+    for (int t = 0; t < MAX_SPAN; ++t)
+      if (t == span - 1) window[t] = current;
+#pragma unroll
+    for (int t = 0; t < MAX_SPAN; ++t)
+      if (t < span) state[(long long)t * channels + c] = window[t];
+  }
+  __syncthreads();
+  // the rule: q and k L2-normalised over the first 4 warps, as the rule
+  // kernel's 128 threads do
+  const int lane = tid % 32, warp = tid / 32;
+  const int slice = warp % SLICES, group = warp / SLICES;
+  float q_scale = 0.0f, k_scale = 0.0f;
+  {
+    float qq = 0.0f, kk = 0.0f;
+    if (tid < RULE_THREADS) {
+      const float qv = conv[tid], kv = conv[D + tid];
+      qq = fmaf(qv, qv, qq);
+      kk = fmaf(kv, kv, kk);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off /= 2) {
+      qq += __shfl_xor_sync(0xffffffffu, qq, off);
+      kk += __shfl_xor_sync(0xffffffffu, kk, off);
+    }
+    __shared__ float qk_parts[2][RULE_WARPS];
+    if (tid < RULE_THREADS && lane == 0) {
+      qk_parts[0][warp] = qq;
+      qk_parts[1][warp] = kk;
+    }
+    __syncthreads();
+    const float q_total = ((qk_parts[0][0] + qk_parts[0][1]) + qk_parts[0][2]) + qk_parts[0][3];
+    const float k_total = ((qk_parts[1][0] + qk_parts[1][1]) + qk_parts[1][2]) + qk_parts[1][3];
+    q_scale = 1.0f / sqrtf(q_total + 1e-6f) * (1.0f / sqrtf(float(D)));
+    k_scale = 1.0f / sqrtf(k_total + 1e-6f);
+  }
+  const int j = slice * RULE_COLUMNS + lane, i0 = group * ROWS;
+  float* column = states + (((long long)seq * heads + h) * D + i0) * D + j;
+  float sv[ROWS];
+#pragma unroll
+  for (int r = 0; r < ROWS; ++r) sv[r] = column[(long long)r * D];
+  const float v = conv[2 * D + j];
+  const float x = a[(long long)seq * heads + h] + dt_bias[h];
+  const float g = expf(decay[h] * (x > 20.0f ? x : log1pf(expf(x))));
+  const float beta = 1.0f / (1.0f + expf(-b[(long long)seq * heads + h]));
+  const float* qs = conv;
+  const float* ks = conv + D;
+  float part = 0.0f;
+#pragma unroll
+  for (int r = 0; r < ROWS; ++r) {
+    sv[r] *= g;
+    part = fmaf(sv[r], ks[i0 + r] * k_scale, part);
+  }
+  sums[group][slice][lane] = part;
+  __syncthreads();
+  const float kv = ((sums[0][slice][lane] + sums[1][slice][lane]) + sums[2][slice][lane]) +
+                   sums[3][slice][lane];
+  const float delta = (v - kv) * beta;
+  __syncthreads();  // sums is reused below
+  float acc = 0.0f;
+#pragma unroll
+  for (int r = 0; r < ROWS; ++r) {
+    sv[r] = fmaf(ks[i0 + r] * k_scale, delta, sv[r]);
+    acc = fmaf(sv[r], qs[i0 + r] * q_scale, acc);
+  }
+  sums[group][slice][lane] = acc;
+#pragma unroll
+  for (int r = 0; r < ROWS; ++r) column[(long long)r * D] = sv[r];
+  __syncthreads();
+  if (group == 0)
+    o[j] = ((sums[0][slice][lane] + sums[1][slice][lane]) + sums[2][slice][lane]) +
+           sums[3][slice][lane];
+  __syncthreads();
+  // the gated RMS norm of the head's output, over the first 4 warps as
+  // gated_rms_norm_kernel's 128 threads
+  if (tid < RULE_THREADS) {
+    const float value = o[tid];
+    float squares = fmaf(value, value, 0.0f);
+#pragma unroll
+    for (int off = 16; off > 0; off /= 2) squares += __shfl_xor_sync(0xffffffffu, squares, off);
+    if (lane == 0) partial[warp] = squares;
+    asm volatile("bar.sync 1, %0;" ::"r"(RULE_THREADS));
+    float total = 0.0f;
+    for (int w = 0; w < RULE_WARPS; ++w) total += partial[w];
+    const float scale = 1.0f / sqrtf(total / float(D) + epsilon);
+    const long long at = ((long long)seq * heads + h) * D + tid;
+    const float gv = z[at];
+    const float act = gv / (1.0f + expf(-gv));
+    const float normed = value * scale * norm_weight[tid] * act;
+    out[at] = normed;
+    if (records) x22_record_block(normed, records, seq, (h * D + tid) / 32, heads * D / 32);
+  }
+}
+
 DRIFT_REGISTER(causal_conv_batched, causal_conv_kernel)
+DRIFT_REGISTER(delta_decode_step_d128, delta_decode_step_kernel)
 DRIFT_REGISTER(delta_rule_d128, gated_delta_rule_kernel<128>)
 DRIFT_REGISTER(gated_rms_norm_records_f32, gated_rms_norm_kernel<1>)
 
@@ -313,6 +458,47 @@ int drift_gated_delta_rule_decode(const float* qkv, int sequences, int key_heads
     DRIFT_CUDA(launch_pdl(gated_delta_rule_kernel<128>, grid, RULE_THREADS, 0, s, qkv, 1,
                           key_heads, value_heads, tiled, a, b, decay, dt_bias, states, none, out));
   DRIFT_LAUNCHED("delta_rule");
+  return 0;
+}
+
+int drift_delta_decode_step(const float* qkv, const float* z, int sequences, int key_heads,
+                            int value_heads, int dim, int tiled, const float* conv_weight,
+                            int taps, float* conv_states, float* convolved, const float* a,
+                            const float* b, const float* decay, const float* dt_bias,
+                            float* states, const float* norm_weight, float epsilon, float* out,
+                            void* prepared, drift_stream_t stream) {
+  if (sequences < 0 || sequences > 65535 || key_heads <= 0 || value_heads <= 0 ||
+      value_heads % key_heads != 0)
+    return invalid("%d value heads over %d key heads (%d sequences)", value_heads, key_heads,
+                   sequences);
+  if (dim != 32 && dim != 64 && dim != 128)
+    return invalid("gatedDeltaRule: heads of %d (kernels take 32, 64, 128)", dim);
+  if (taps < 1 || taps > 9 || taps - 1 > MAX_SPAN)
+    return invalid("causalConv: %d taps (at most 9)", taps);
+  if (sequences == 0) return 0;
+  if (!qkv || !z || !conv_weight || (taps > 1 && !conv_states) || !a || !b || !decay ||
+      !dt_bias || !states || !norm_weight || !out)
+    return invalid("deltaDecodeStep: a null tensor");
+  if (prepared && dim % 32 != 0)
+    return invalid("gatedRmsNorm: prepared x needs rows of whole heads of 32-value blocks");
+  const int channels = (2 * key_heads + value_heads) * dim;
+  if (key_heads != value_heads || dim != STEP_D || taps < 2) {
+    // the three launches it stands for (the same bits): `convolved` holds
+    // the convolution's output between them
+    if (!convolved) return invalid("deltaDecodeStep: no room for the convolved channels");
+    DRIFT_TRY(drift_causal_conv_decode(qkv, sequences, channels, conv_weight, taps, 1, conv_states,
+                                       convolved, stream));
+    DRIFT_TRY(drift_gated_delta_rule_decode(convolved, sequences, key_heads, value_heads, dim,
+                                            tiled, a, b, decay, dt_bias, states, out, stream));
+    return drift_gated_rms_norm(out, norm_weight, z, DRIFT_SILU, epsilon, out,
+                                (int64_t)sequences * value_heads, dim, value_heads, prepared,
+                                stream);
+  }
+  DRIFT_CUDA(launch_pdl(delta_decode_step_kernel, dim3(unsigned(value_heads), unsigned(sequences)),
+                        STEP_THREADS, 0, cudaStream_t(stream), qkv, z, value_heads, conv_weight,
+                        taps, conv_states, a, b, decay, dt_bias, states, norm_weight, epsilon, out,
+                        static_cast<uint8_t*>(prepared)));
+  DRIFT_LAUNCHED("delta_decode_step");
   return 0;
 }
 

@@ -510,7 +510,7 @@ int drift_experts_linear_local(int x_dtype, const void* x, int64_t x_rows, int w
                                const void* weight, int64_t experts, int64_t first_expert,
                                int64_t n, int64_t k, const int32_t* ids, int64_t slots,
                                float* out, const void* prepared, drift_stream_t stream) {
-  if (first_expert < 0) return invalid("expertsLinear: experts from %lld", (long long)first_expert);
+  if (first_expert < -1) return invalid("expertsLinear: experts from %lld", (long long)first_expert);
   return experts_common(false, x_dtype, x, x_rows, weight_dtype, weight, nullptr, experts, n, k,
                         ids, slots, out, first_expert, 1, prepared, cudaStream_t(stream));
 }
@@ -529,7 +529,8 @@ int drift_experts_gated_linear_local(int x_dtype, const void* x, int64_t x_rows,
                                      const int32_t* ids, int64_t slots, float* out,
                                      const void* prepared, int shared_tail,
                                      drift_stream_t stream) {
-  if (first_expert < 0) return invalid("expertsGatedLinear: experts from %lld", (long long)first_expert);
+  if (first_expert < -1)
+    return invalid("expertsGatedLinear: experts from %lld", (long long)first_expert);
   return experts_common(true, x_dtype, x, x_rows, weight_dtype, gate, up, experts, n, k, ids,
                         slots, out, first_expert, 1, prepared, cudaStream_t(stream),
                         shared_tail != 0);

@@ -44,7 +44,7 @@ import torch
 
 from . import synthetic
 from ._lib import Q4_1, Q8_0
-from .ops import SIGMOID, SILU, Attention, CudaOps, KvCache, Rope, RowNorm, SharedExpert, Stored
+from .ops import SIGMOID, Attention, CudaOps, KvCache, Rope, RowNorm, SharedExpert, Stored
 
 
 @dataclass(frozen=True)
@@ -111,8 +111,9 @@ class MixtureLayer:
     shared_up: Stored
     shared_down: Stored          # [hidden, shared ffn]
     shared_router: torch.Tensor  # F32 [hidden]
-    # (gate, up, down) of experts + 1 experts, the last the shared expert,
-    # when the fields above are views of them (one launch serves both)
+    # (gate, up, down) of experts + 1 experts when the fields above are views
+    # of them (one launch serves both): on one GPU the shared expert last (id
+    # `experts`); under expert parallelism, on rank 0, first (id -1)
     fused: Optional[tuple] = None
 
 
@@ -156,6 +157,18 @@ class Partition:
         kv = (q[0] // group, (q[1] - 1) // group + 1)  # the key heads of the rank's query heads
         return Partition(rank, world, even(c.delta_key_heads), even(c.delta_value_heads), q, kv,
                          even(c.experts), (c.vocab * rank // world, c.vocab * (rank + 1) // world))
+
+
+def _shared_first(router, gate: Stored, up: Stored, down: Stored, experts: int, c, dtype: int,
+                  shared_router) -> "MixtureLayer":
+    """A mixture whose (gate, up, down) hold the shared expert first, then
+    `experts` routed experts (expert parallelism's rank 0)."""
+    first = _expert_range(down, 0, 1)
+    return MixtureLayer(router, _expert_range(gate, 1, experts + 1),
+                        _expert_range(up, 1, experts + 1), _expert_range(down, 1, experts + 1),
+                        _expert_range(gate, 0, 1), _expert_range(up, 0, 1),
+                        Stored(dtype, (c.hidden, c.shared_ffn), first.data), shared_router,
+                        (gate, up, down))
 
 
 def _rows(w: Stored, ranges, width: int) -> Stored:
@@ -222,7 +235,16 @@ class HybridWeights:
                                    f32(channels, c.conv_taps, scale=0.5),
                                    -torch.exp(torch.rand(dv, generator=g, device="cuda") * 2.5 - 1.0),
                                    f32(dv), norm(c.delta_dim), stored(c.hidden, value_width))
-            if world == 1 and c.shared_ffn == c.expert_ffn:
+            if world > 1 and rank == 0 and c.shared_ffn == c.expert_ffn:
+                # expert parallelism: the shared expert on rank 0, as expert
+                # 0 (id -1) of its weights, before its routed experts
+                router = f32(c.experts, c.hidden, scale=0.02)
+                gate, up, down = (stored(c.expert_ffn, c.hidden, experts + 1),
+                                  stored(c.expert_ffn, c.hidden, experts + 1),
+                                  stored(c.hidden, c.expert_ffn, experts + 1))
+                mixture = _shared_first(router, gate, up, down, experts, c, dtype,
+                                        f32(c.hidden, scale=0.02))
+            elif world == 1 and c.shared_ffn == c.expert_ffn:
                 # the shared expert as expert `experts` of the routed weights
                 router = f32(c.experts, c.hidden, scale=0.02)
                 gate, up, down = (stored(c.expert_ffn, c.hidden, experts + 1),
@@ -278,9 +300,21 @@ class HybridWeights:
                                    _columns(m.out, vh[0] * d, vh[1] * d))
             x = layer.mixture
             e0, e1 = part.experts
-            mixture = MixtureLayer(x.router, _expert_range(x.gate, e0, e1),
-                                   _expert_range(x.up, e0, e1), _expert_range(x.down, e0, e1),
-                                   x.shared_gate, x.shared_up, x.shared_down, x.shared_router)
+            if world > 1 and rank == 0 and c.shared_ffn == c.expert_ffn:
+                # the shared expert first, then the rank's routed experts
+                def joined(shared: Stored, routed: Stored) -> Stored:
+                    part_ = _expert_range(routed, e0, e1)
+                    data = torch.cat([shared.data.reshape(-1), part_.data.reshape(-1)])
+                    return Stored(routed.dtype, (e1 - e0 + 1,) + tuple(routed.shape[1:]), data)
+                shared_down = Stored(x.shared_down.dtype, (1,) + tuple(x.shared_down.shape),
+                                     x.shared_down.data)
+                mixture = _shared_first(x.router, joined(x.shared_gate, x.gate),
+                                        joined(x.shared_up, x.up), joined(shared_down, x.down),
+                                        e1 - e0, c, x.gate.dtype, x.shared_router)
+            else:
+                mixture = MixtureLayer(x.router, _expert_range(x.gate, e0, e1),
+                                       _expert_range(x.up, e0, e1), _expert_range(x.down, e0, e1),
+                                       x.shared_gate, x.shared_up, x.shared_down, x.shared_router)
             layers.append(HybridLayer(layer.input_norm, mixer, layer.post_norm, mixture))
         v0, v1 = part.vocab
         return HybridWeights(self.embedding, layers, self.final_norm,
@@ -366,7 +400,11 @@ class HybridDecoder:
         # shared ones the shared expert's index in fused weights), the SwiGLU
         # outputs and the down outputs as one buffer each, viewed per part
         routed = b * c.used
-        self.all_ids = torch.full((routed + b,), c.experts, dtype=torch.int32, device="cuda")
+        # the shared slots' id: `experts` on one GPU (the shared expert last
+        # in fused weights); -1 under expert parallelism (first on rank 0,
+        # another rank's -- zeros -- elsewhere)
+        shared_id = c.experts if part.world == 1 else -1
+        self.all_ids = torch.full((routed + b,), shared_id, dtype=torch.int32, device="cuda")
         self.route_ids = self.all_ids[:routed].view(b, c.used)
         self.route_weights = torch.zeros(b, c.used, **f32)
         self.all_gated = torch.zeros(routed + b, c.expert_ffn, **f32)
@@ -411,15 +449,13 @@ class HybridDecoder:
         # combine + norm, or the first norm)
         ops.linears(self.normed, [layer.qkv, layer.z, layer.a, layer.b],
                     [self.qkv, self.z, self.a, self.b], P)
-        ops.causal_conv_decode(self.qkv, layer.conv, 1, self.conv_states[index], self.convolved)
-        ops.gated_delta_rule_decode(self.convolved, self.a, self.b, layer.decay, layer.dt_bias,
-                                    self.delta_states[index],
-                                    (self.delta_key_heads, self.delta_value_heads, c.delta_dim,
-                                     False),
-                                    self.core)
-        core = self.core.view(b * self.delta_value_heads, c.delta_dim)
-        ops.gated_rms_norm(core, layer.norm, self.z.view(b * self.delta_value_heads, c.delta_dim),
-                           SILU, c.epsilon, core, P, self.delta_value_heads)
+        # the convolution, the delta rule and the gated norm (with the out
+        # projection's records): one launch
+        ops.delta_decode_step(self.qkv, self.z, layer.conv, self.conv_states[index],
+                              self.convolved, self.a, self.b, layer.decay, layer.dt_bias,
+                              self.delta_states[index],
+                              (self.delta_key_heads, self.delta_value_heads, c.delta_dim, False),
+                              layer.norm, c.epsilon, self.core, P)
         ops.linears(self.core.view(b, self.value_width), [layer.out], [self._block_out(0)], P)
 
     def _full(self, layer: FullLayer, index: int) -> None:
@@ -473,6 +509,20 @@ class HybridDecoder:
         # zeros), the shared expert on rank 0, the partial combine into the
         # exchange, summed over the ranks with the residual and normalised
         first = self.part.experts[0]
+        if mixture.fused is not None:
+            # rank 0: the shared expert (id -1) first in the fused weights,
+            # its slots in the routed experts' launches -- no launches of its
+            # own, so every rank runs the same ones
+            gate, up, down = mixture.fused
+            ops.experts_gated_linear(self.normed, gate, up, self.all_ids, self.all_gated,
+                                     first_expert=first - 1, prepared=P, shared_tail=True)
+            ops.experts_linear(self.all_gated, down, self.all_ids, self.all_out,
+                               first_expert=first - 1)
+            shared = SharedExpert(self.shared_out, self.normed, mixture.shared_router)
+            ops.moe_combine(self.expert_out, self.route_weights, shared, None,
+                            self.exchange.slots[1])
+            self.exchange.add_rms_norm(1, self.x, next_norm, P)
+            return
         ops.experts_gated_linear(self.normed, mixture.gate, mixture.up, self.route_ids.view(-1),
                                  self.expert_gated, first_expert=first, prepared=P)
         ops.experts_linear(self.expert_gated, mixture.down, self.route_ids.view(-1),

@@ -252,6 +252,26 @@ class CudaOps:
                                                      ns, m, k, self._stream())
         check("drift_linears", status)
 
+    def linears_gated(self, kind: int, x: torch.Tensor, gate: Stored, up: Stored,
+                      gate_out: torch.Tensor, up_out: torch.Tensor, out: torch.Tensor,
+                      prepared: torch.Tensor, out_prepared: Optional[torch.Tensor] = None) -> None:
+        """gate_out, up_out = x · gateᵀ, x · upᵀ; out = kind(gate_out) × up_out
+        (linears then gated, NormalisationOps.scala:24), the gating in the
+        products' launch below 32 rows; with `out_prepared` (not `prepared`),
+        out's records for the down product."""
+        m, n, k = self._check_linear(x, gate, gate_out)
+        _require(tuple(self._check_linear(x, up, up_out)) == (m, n, k),
+                 "gated linears: gate and up of one shape")
+        _require(isinstance(gate, Stored) and isinstance(up, Stored) and gate.dtype == up.dtype,
+                 "gated linears: quantized gate and up of one type")
+        _f32("gated", out)
+        _require(tuple(out.shape) == (m, n), f"gated: out {list(out.shape)} for [{m}, {n}]")
+        status = self.lib.drift_linears_gated_prepared(
+            kind, _x_dtype("linear", x), _ptr(x), _ptr(prepared), gate.dtype, _ptr(gate.data),
+            _ptr(up.data), _ptr(gate_out), _ptr(up_out), _ptr(out), m, n, k, _ptr(out_prepared),
+            self._stream())
+        check("drift_linears_gated_prepared", status)
+
     def embedding(self, table: Stored, ids: torch.Tensor, out: torch.Tensor) -> None:
         """out[t] = table[ids[t]] as F32 (LinearOps.scala:83-87; checks L163-177)."""
         _require(len(table.shape) == 2,
@@ -523,6 +543,34 @@ class CudaOps:
             _ptr(qkv), sequences, key_heads, value_heads, d, int(tiled), _ptr(a), _ptr(b),
             _ptr(decay), _ptr(dt_bias), _ptr(states), _ptr(out), self._stream())
         check("drift_gated_delta_rule_decode", status)
+
+    def delta_decode_step(self, qkv, z, conv_weight, conv_states, convolved, a, b, decay,
+                          dt_bias, states, rule, norm_weight, epsilon: float, out,
+                          prepared: Optional[torch.Tensor] = None) -> None:
+        """causal_conv_decode (dilation 1), gated_delta_rule_decode and the
+        SiLU-gated rms norm of the core by z, in one launch where it can
+        (every value head with a key head of its own, heads of 128): out
+        [S, value_heads, D]; `convolved` [S, channels] is used only when it
+        falls back to the three launches."""
+        key_heads, value_heads, d, tiled = rule
+        _f32("deltaDecodeStep", qkv, z, conv_weight, conv_states, convolved, a, b, decay,
+             dt_bias, states, norm_weight, out)
+        sequences, channels = qkv.shape
+        _require(channels == (2 * key_heads + value_heads) * d,
+                 f"deltaDecodeStep: qkv {list(qkv.shape)}")
+        taps = conv_weight.shape[-1]
+        _require(tuple(conv_states.shape) == (sequences, taps - 1, channels),
+                 f"deltaDecodeStep: conv states {list(conv_states.shape)}")
+        _require(tuple(states.shape) == (sequences, value_heads, d, d),
+                 f"deltaDecodeStep: states {list(states.shape)}")
+        _require(tuple(out.shape) == (sequences, value_heads, d) and z.numel() == out.numel(),
+                 f"deltaDecodeStep: out {list(out.shape)}")
+        status = self.lib.drift_delta_decode_step(
+            _ptr(qkv), _ptr(z), sequences, key_heads, value_heads, d, int(tiled),
+            _ptr(conv_weight), taps, _ptr(conv_states), _ptr(convolved), _ptr(a), _ptr(b),
+            _ptr(decay), _ptr(dt_bias), _ptr(states), _ptr(norm_weight), epsilon, _ptr(out),
+            _ptr(prepared), self._stream())
+        check("drift_delta_decode_step", status)
 
     def gated_rms_norm(self, x, weight, gate, kind: int, epsilon: float, out,
                        prepared: Optional[torch.Tensor] = None, heads: int = 0) -> None:

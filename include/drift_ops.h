@@ -258,6 +258,23 @@ int drift_gated_delta_rule_decode(const float* qkv, int sequences, int key_heads
                                   int dim, int tiled, const float* a, const float* b,
                                   const float* decay, const float* dt_bias, float* states,
                                   float* out, drift_stream_t stream);
+/* A DeltaNet layer's decode step after its input products (new; the
+ * hybrid decoder's causalConv, gatedDeltaRule and gatedRmsNorm of one token
+ * per sequence, models/HybridBlocks.scala): qkv [sequences][(2 key_heads +
+ * value_heads) dim] through the causal convolution (dilation 1, states
+ * [sequences][taps - 1][channels]), the gated delta rule on states
+ * [sequences][value_heads][dim][dim], and rmsNorm(core) * norm_weight *
+ * SiLU(z) into out [sequences][value_heads][dim] (z the same shape), with the
+ * out projection's records into `prepared` (NULL for none). One launch when
+ * key_heads == value_heads, dim 128 and taps >= 2; otherwise the three calls
+ * it stands for, with `convolved` [sequences][channels] between them. The
+ * same bits either way. */
+int drift_delta_decode_step(const float* qkv, const float* z, int sequences, int key_heads,
+                            int value_heads, int dim, int tiled, const float* conv_weight,
+                            int taps, float* conv_states, float* convolved, const float* a,
+                            const float* b, const float* decay, const float* dt_bias,
+                            float* states, const float* norm_weight, float epsilon, float* out,
+                            void* prepared, drift_stream_t stream);
 /* NormalisationOps.gatedRmsNorm (CpuNormalisation.scala:167-178): per row of
  * cols (<= 512) values, rmsNorm(x) * weight * act(gate), act DRIFT_SILU or
  * DRIFT_SIGMOID; out may be x. With `prepared` (rows = tokens x heads), the
@@ -269,7 +286,11 @@ int drift_gated_rms_norm(const float* x, const float* weight, const float* gate,
 /* Expert parallelism (new): a rank's weight holds experts [first_expert,
  * first_expert + experts) of the model's; `ids` are the model's; a slot whose
  * expert is another rank's gets a row of zeros (drift_experts_linear and
- * drift_experts_gated_linear flag such a slot as an error instead). */
+ * drift_experts_gated_linear flag such a slot as an error instead). Id -1
+ * names a mixture's shared expert: the rank that holds it puts it first and
+ * passes first_expert -1 (its routed experts then start at 0), so the shared
+ * expert's slots ride in the routed experts' launches on that rank and are
+ * zeros on the others. */
 int drift_experts_linear_local(int x_dtype, const void* x, int64_t x_rows, int weight_dtype,
                                const void* weight, int64_t experts, int64_t first_expert,
                                int64_t n, int64_t k, const int32_t* ids, int64_t slots,
@@ -325,6 +346,21 @@ int drift_linears_prepared(int x_dtype, const void* x, const void* prepared, int
                            const int* weight_dtypes, const void* const* weights,
                            float* const* outs, const int64_t* ns, int64_t m, int64_t k,
                            drift_stream_t stream);
+/* A dense feed-forward's gate and up products and its gating in one call:
+ * gate_out = x . gate^T, up_out = x . up^T (both [m, n]) and out = act(gate_out)
+ * x up_out (drift_gated's activation codes; out may alias gate_out), with
+ * out's records into `out_prepared` (NULL for none; n a multiple of 32) for
+ * the down product -- the runner's linears(gate, up) then gated(Silu, ...)
+ * (DenseDecoder.scala's feed-forward, ops/NormalisationOps.scala:24). For
+ * 1-2 rows of x whose two products share a balanced launch, the gating runs
+ * in that launch's epilogue (no launch of its own); otherwise the two calls
+ * it replaces, with the same bits either way. `out_prepared`
+ * must not overlap `prepared`: x's records are still read while out's are
+ * written. */
+int drift_linears_gated_prepared(int kind, int x_dtype, const void* x, const void* prepared,
+                                 int weight_dtype, const void* gate, const void* up,
+                                 float* gate_out, float* up_out, float* out, int64_t m, int64_t n,
+                                 int64_t k, void* out_prepared, drift_stream_t stream);
 
 /* ---- the tensor-parallel exchange over NVLink (new) --------------------------
  * The reference runs one device (native/HipRuntime.scala:40-43); a B200 box

@@ -134,6 +134,48 @@ def test_gated_rms_norm_records_feed_the_out_projection(ops):
     assert torch.equal(fused, alone)
 
 
+@pytest.mark.parametrize("sequences", [1, 3, 16])
+@pytest.mark.parametrize("key_heads,value_heads,dim,taps", [(4, 4, 128, 4), (16, 16, 128, 4),
+                                                             (2, 4, 128, 4), (4, 4, 64, 3)])
+def test_delta_decode_step_is_the_three_launches(ops, sequences, key_heads, value_heads, dim,
+                                                 taps):
+    """The fused decode step (one launch when each value head has its own key
+    head and heads are 128 wide) against causal_conv_decode, then
+    gated_delta_rule_decode, then the SiLU-gated rms norm with records: the
+    same outputs, states, convolution states and records, bit for bit."""
+    g = torch.Generator(device="cuda").manual_seed(sequences * 31 + key_heads + dim)
+    channels = (2 * key_heads + value_heads) * dim
+    f = lambda *shape, s=1.0: s * torch.randn(*shape, generator=g, device="cuda")
+    qkv, z = f(sequences, channels), f(sequences, value_heads, dim)
+    conv = f(channels, taps, s=0.5)
+    conv_states = f(sequences, taps - 1, channels)
+    a, b = f(sequences, value_heads), f(sequences, value_heads)
+    decay = -torch.exp(torch.rand(value_heads, generator=g, device="cuda") * 2.5 - 1.0)
+    dt_bias = f(value_heads)
+    states = f(sequences, value_heads, dim, dim, s=0.02)
+    norm = 1.0 + 0.02 * f(dim)
+    rule = (key_heads, value_heads, dim, False)
+    conv1, states1 = conv_states.clone(), states.clone()
+    out1 = torch.empty(sequences, value_heads, dim, device="cuda")
+    prepared1 = ops.prepared_x(sequences, value_heads * dim)
+    ops.delta_decode_step(qkv, z, conv, conv1, torch.empty_like(qkv), a, b, decay, dt_bias,
+                          states1, rule, norm, 1e-6, out1, prepared1)
+    conv2, states2 = conv_states.clone(), states.clone()
+    convolved = torch.empty_like(qkv)
+    ops.causal_conv_decode(qkv, conv, 1, conv2, convolved)
+    out2 = torch.empty_like(out1)
+    ops.gated_delta_rule_decode(convolved, a, b, decay, dt_bias, states2, rule, out2)
+    prepared2 = ops.prepared_x(sequences, value_heads * dim)
+    core = out2.view(sequences * value_heads, dim)
+    ops.gated_rms_norm(core, norm, z.view(sequences * value_heads, dim), SILU, 1e-6, core,
+                       prepared2, value_heads)
+    torch.cuda.synchronize()
+    assert torch.equal(conv1, conv2)
+    assert torch.equal(states1, states2)
+    assert torch.equal(out1, out2)
+    assert torch.equal(prepared1, prepared2)
+
+
 def test_refusals(ops):
     x = torch.zeros(1, 64, device="cuda")
     with pytest.raises(ValueError, match="state"):
