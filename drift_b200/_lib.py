@@ -93,8 +93,6 @@ SIGNATURES = {
     "drift_add_rms_norm_prepared": (_i32, [_p, _p, _p, _f32, _f32, _p, _i64, _i64, _p, _p]),
     "drift_gated_prepared": (_i32, [_i32, _p, _p, _p, _i64, _i64, _p, _p]),
     "drift_linears_prepared": (_i32, [_i32, _p, _p, _i32, _p, _p, _p, _p, _i64, _i64, _p]),
-    "drift_linears_gated_prepared": (_i32, [_i32, _i32, _p, _p, _i32, _p, _p, _p, _p, _p, _i64,
-                                            _i64, _i64, _p, _p]),
     "drift_attention_decode_prepared": (_i32, [_p, _i32, _i32, _p, _p, _i32, _i32, _i32, _i32, _p,
                                                _i32, _p, _i32, _f32, _i32, _f32, _p, _p, _p, _p]),
     "drift_rope": (_i32, [_p, _p, _p, _i32, _i32, _i32, _f32, _i32, _i32, _p]),

@@ -29,10 +29,6 @@ bool ring_many_fits(int weight_dtype, int count, const void* const* weights, con
 int matvec_ring_many(int weight_dtype, int count, const void* const* weights,
                      const uint8_t* records, float* const* ys, const int64_t* rows, int64_t cols,
                      int64_t vectors, cudaStream_t stream);
-int matvec_ring_gated(int weight_dtype, const void* gate, const void* up, const uint8_t* records,
-                      float* gate_out, float* up_out, float* out, uint8_t* out_records,
-                      int64_t rows, int64_t cols, int64_t vectors, int kind,
-                      cudaStream_t stream);
 size_t tc_workspace_bytes(int64_t m, int64_t k);
 int linear_tc(int x_dtype, const void* x, int weight_dtype, const void* weight, float* y,
               int64_t m, int64_t n, int64_t k, uint8_t* workspace, cudaStream_t stream);
@@ -199,49 +195,6 @@ int drift_linears_prepared(int x_dtype, const void* x, const void* prepared, int
   if (x_dtype != DRIFT_F32) return invalid("linears: prepared x comes from F32 x");
   return linears(x_dtype, x, prepared, count, weight_dtypes, weights, outs, ns, m, k,
                  cudaStream_t(stream));
-}
-
-int drift_linears_gated_prepared(int kind, int x_dtype, const void* x, const void* prepared,
-                                 int weight_dtype, const void* gate, const void* up,
-                                 float* gate_out, float* up_out, float* out, int64_t m, int64_t n,
-                                 int64_t k, void* out_prepared, drift_stream_t stream) {
-  if (kind < 0 || kind > 4) return invalid("gated: activation code %d", kind);
-  if (!prepared) return invalid("linears: no prepared x");
-  if (x_dtype != DRIFT_F32) return invalid("linears: prepared x comes from F32 x");
-  if (!gate_out || !up_out || !out) return invalid("gated linears: a null output");
-  if (out_prepared && n % 32 != 0)
-    return invalid("gated: prepared x needs rows of whole 32-value blocks");
-  if (out_prepared) {
-    // out's records are written while x's are still read
-    const uint8_t* a = static_cast<const uint8_t*>(prepared);
-    const uint8_t* b = static_cast<const uint8_t*>(out_prepared);
-    const size_t a_bytes = mma_workspace_bytes(m, k), b_bytes = mma_workspace_bytes(m, n);
-    if (a < b + b_bytes && b < a + a_bytes)
-      return invalid("gated linears: out's records overlap x's");
-  }
-  const cudaStream_t s = cudaStream_t(stream);
-  const void* weights[2] = {gate, up};
-  const int64_t ns[2] = {n, n};
-  const int dtypes[2] = {weight_dtype, weight_dtype};
-  // fused for 1-2 rows of x: there the gating's hand-off between the gate
-  // and the up tiles (a fence and an arrival count per tile) costs less than
-  // a launch of its own; with 3 or more rows (the MMA mode) it measured
-  // slower than the separate launch
-  if (m > 0 && m <= 2 && n > 0 && k > 0 && n % 32 == 0 && weight_dtype != DRIFT_F32 &&
-      ring_many_fits(weight_dtype, 2, weights, ns, k)) {
-    for (int i = 0; i < 2; ++i)
-      DRIFT_TRY(check_linear(x_dtype, x, weight_dtype, weights[i], i ? up_out : gate_out, m, n, k));
-    return matvec_ring_gated(weight_dtype, gate, up, static_cast<const uint8_t*>(prepared),
-                             gate_out, up_out, out, static_cast<uint8_t*>(out_prepared), n, k, m,
-                             kind, s);
-  }
-  // the same bits in two launches: the products, then the gating
-  float* outs[2] = {gate_out, up_out};
-  DRIFT_TRY(linears(x_dtype, x, prepared, 2, dtypes, weights, outs, ns, m, k, s));
-  if (m == 0 || n == 0) return 0;
-  if (out_prepared)
-    return drift_gated_prepared(kind, gate_out, up_out, out, m, n, out_prepared, stream);
-  return drift_gated(kind, gate_out, up_out, out, m * n, stream);
 }
 
 int drift_linear(int x_dtype, const void* x, int weight_dtype, const void* weight, float* out,

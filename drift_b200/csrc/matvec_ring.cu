@@ -29,10 +29,8 @@
 #include "mma_i8.cuh"
 #include "quant.cuh"
 #include "registry.cuh"
-#include "rowwise.cuh"
 #include "tc_common.cuh"
 #include "tma_host.cuh"
-#include "x22.cuh"
 
 namespace drift {
 
@@ -579,69 +577,17 @@ constexpr int SPLIT_UNITS = 8192;  // the most units a balanced launch takes
 
 struct SplitLaunch {
   CUtensorMap maps[MAX_MATRICES];
-  // the 1-2 vector modes: x's records as rows of 896 bytes, one per block,
-  // a box of a segment's 8 blocks x the launch's slots (112 bytes each)
-  CUtensorMap xmap;
   float* y[MAX_MATRICES];
   int rows[MAX_MATRICES];
   int tile_end[MAX_MATRICES];  // matrix m holds the launch's tiles [tile_end[m - 1], tile_end[m])
   int count, cols, vectors;
   const uint8_t* records;
   int* error;
-  // gate (matrix 0) and up (matrix 1) of the same rows, gated in the launch:
-  // gated_out = act(gate) x up, with its records when gated_records is set
-  int gated;  // 0, or 1 + the activation
-  float* gated_out;
-  uint8_t* gated_records;
 };
 
 // Groups arrived per tile of a balanced launch, zero between launches (the
 // completing warp clears its tile's).
 __device__ int split_arrivals[SPLIT_UNITS];
-
-// Gate and up tiles met per tile index of a gated launch, zero between
-// launches (the second to arrive clears its entry).
-__device__ int pair_arrivals[SPLIT_UNITS];
-
-// A warp that has written the last outputs of tile `local` of the gate or
-// the up matrix of a gated launch: the second of the two to get here writes
-// the tile's act(gate) x up (gated_kernel's arithmetic, so its bits) and, with
-// gated_records, the records of those outputs -- a tile's 64 rows are two
-// whole 32-value blocks of each vector's row (rows a multiple of 32).
-__device__ __forceinline__ void gate_pair(const SplitLaunch& L, int local, int lane) {
-  __threadfence();  // this warp's outputs, before its arrival
-  __syncwarp();
-  int second = 0;
-  if (lane == 0) second = atomicAdd(&pair_arrivals[local], 1) == 1;
-  if (!__shfl_sync(0xffffffffu, second, 0)) return;
-  __threadfence();  // the other tile's outputs, after its arrival
-  const int rows = L.rows[0], kind = L.gated - 1;
-  constexpr int B = ROWS / 32;
-  // every load in flight before the first is used: (vector, block) pairs of
-  // the tile, the whole warp taking each (rows are whole blocks)
-  float g[8][B], u[8][B];
-#pragma unroll
-  for (int v = 0; v < 8; ++v)
-#pragma unroll
-    for (int b = 0; b < B; ++b) {
-      const int row = local * ROWS + 32 * b + lane;
-      const bool in = v < L.vectors && local * ROWS + 32 * b < rows;
-      const long long at = (long long)v * rows + row;
-      g[v][b] = in ? __ldcg(L.y[0] + at) : 0.0f;
-      u[v][b] = in ? __ldcg(L.y[1] + at) : 0.0f;
-    }
-#pragma unroll
-  for (int v = 0; v < 8; ++v)
-#pragma unroll
-    for (int b = 0; b < B; ++b) {
-      const int row = local * ROWS + 32 * b + lane;
-      if (v >= L.vectors || local * ROWS + 32 * b >= rows) continue;  // warp-uniform
-      const float value = activate(g[v][b], kind) * gated_up(u[v][b], kind);
-      L.gated_out[(long long)v * rows + row] = value;
-      if (L.gated_records) x22_record_block(value, L.gated_records, v, row / 32, rows / 32);
-    }
-  if (lane == 0) pair_arrivals[local] = 0;
-}
 
 template <typename T, int MODE>
 __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
@@ -667,18 +613,6 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
     return int(u / groups.count) * segments + groups.begin(int(u % groups.count));
   };
   const int j0 = start(U * gw / G), jobs = start(U * (gw + 1) / G) - j0;
-  // The 1-2 vector modes bring each job's x -- its segment's 8 blocks of the
-  // records, the launch's slots of each -- by a second tensor copy onto the
-  // job's barrier, so a job's x is in shared memory when its weights are:
-  // read block by block from global memory, every block of a segment paid
-  // an L2 round trip of its own. The weights' copies of the first jobs go
-  // out before x exists (before the wait on the kernels before); their
-  // barriers expect the x bytes too, and the x copies follow the wait.
-  constexpr bool XSTAGED = MODE != MODE_MMA;
-  constexpr int XSTAGE = XSTAGED ? SEG_BLOCKS * MMA_SLOT_BYTES * VSLOTS : 0;
-  // (a tensor copy's destination: 128-byte aligned)
-  uint8_t* xring = smem + ((Shape::X_OFFSET + 127) & ~127) + warp * S * XSTAGE;
-
   if (threadIdx.x == 0) *abort = 0;
   if (lane < S) tc::mbar_init(&bars[lane], 1);
   tc::fence_barrier_init();
@@ -690,34 +624,24 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
     while (m + 1 < L.count && tile >= L.tile_end[m]) ++m;
     local = tile - (m > 0 ? L.tile_end[m - 1] : 0);
   };
-  // job j's x, once the kernels before have written it: staged by a tensor
-  // copy (1-2 vectors), or its records' lines (8 slots) into L1 ahead of use
-  bool x_ready = false;
-  auto issue_x = [&](int j) {
-    const int segment = (j0 + j) % segments;
-    if constexpr (XSTAGED) {
-      if (lane == 0)
-        tc::tma_load_2d(xring + (j % S) * XSTAGE, &L.xmap, &bars[j % S], 0, segment * SEG_BLOCKS);
-    } else {
-      for (int i = lane; i < SEG_BLOCKS * 7; i += WARP) {
-        const int b = segment * SEG_BLOCKS + i / 7;
-        if (b < blocks)
-          asm volatile("prefetch.global.L1 [%0];" ::"l"(L.records + (long long)b * MMA_RECORD_BYTES +
-                                                        128 * (i % 7)));
-      }
-    }
-  };
-  // job j: its weights by one 2-D tensor copy (and its x, when ready)
+  // job j: its weights by one 2-D tensor copy, and its x records' lines
+  // (the vectors' slots) into L1 ahead of use
   auto issue = [&](int j) {
     const int job = j0 + j, tile = job / segments, segment = job % segments;
     int m, local;
     locate(tile, m, local);
     if (lane == 0) {
-      tc::mbar_expect_tx(&bars[j % S], uint32_t(STAGE + XSTAGE));
+      tc::mbar_expect_tx(&bars[j % S], uint32_t(STAGE));
       tc::tma_load_2d(ring + (j % S) * STAGE, &L.maps[m], &bars[j % S],
                       segment * (Ring<T>::SEG / 4), local * ROWS);
     }
-    if (x_ready) issue_x(j);
+    constexpr int LINES = MODE == MODE_DP4A_1 ? 1 : MODE == MODE_DP4A_2 ? 2 : 7;
+    for (int i = lane; i < SEG_BLOCKS * LINES; i += WARP) {
+      const int b = segment * SEG_BLOCKS + i / LINES;
+      if (b < blocks)
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(L.records + (long long)b * MMA_RECORD_BYTES +
+                                                      128 * (i % LINES)));
+    }
     __syncwarp();
   };
 
@@ -726,9 +650,6 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
   while (issued < jobs && issued < S) issue(issued++);
   pdl_trigger();
   pdl_wait();  // the weights' first copies are in flight; x is now ready
-  x_ready = true;
-  for (int j = 0; j < issued; ++j) issue_x(j);
-  __syncwarp();
   Acc<MODE> part, total;
   part.zero();
   total.zero();
@@ -754,9 +675,8 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
       const int count = blocks - first < SEG_BLOCKS ? blocks - first : SEG_BLOCKS;
       if constexpr (MODE == MODE_MMA)
         segment_mma<T>(ring + (j % S) * STAGE, first, count, L.records, L.vectors, part.a);
-      else  // x staged from block `first` on
-        segment_dp4a<T, MODE, true>(ring + (j % S) * STAGE, 0, count, xring + (j % S) * XSTAGE,
-                                    part.a);
+      else
+        segment_dp4a<T, MODE, false>(ring + (j % S) * STAGE, first, count, L.records, part.a);
     }
     __syncwarp();
     if (ok && issued < jobs) issue(issued++);  // refill the freed stage
@@ -775,7 +695,6 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
             const int row = local * ROWS + r;
             if (row < L.rows[m] && v < L.vectors) L.y[m][(long long)v * L.rows[m] + row] = value;
           });
-          if (L.gated) gate_pair(L, local, lane);
         }
       } else {
         total.add(part);
@@ -785,7 +704,6 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
             if (row < L.rows[m] && v < L.vectors) L.y[m][(long long)v * L.rows[m] + row] = value;
           });
           total.zero();
-          if (L.gated) gate_pair(L, local, lane);
         }
       }
       part.zero();
@@ -813,7 +731,6 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
       if (row < L.rows[m] && v < L.vectors) L.y[m][(long long)v * L.rows[m] + row] = sum;
     });
     if (lane == 0) split_arrivals[tile] = 0;
-    if (L.gated) gate_pair(L, local, lane);
   }
   if (!ok) {
     // let the copies already issued land before the ring is left
@@ -864,16 +781,8 @@ int launch_split_mode(const SplitLaunch& launch, long long units, cudaStream_t s
   // batch 1 1.2 % slower); the MMA mode keeps 8 units to a CTA, faster there
   long long grid = MODE == MODE_MMA ? (units + Shape::WARPS - 1) / Shape::WARPS : units;
   if (grid > sm_count()) grid = sm_count();
-  // the MMA mode's chain, or the 1-2 vector modes' staged x (a segment's
-  // blocks x the mode's slots, per stage)
-  const int extra = MODE == MODE_MMA
-                        ? Shape::CHAIN_BYTES
-                        : 128 + Shape::WARPS * Shape::S * SEG_BLOCKS * MMA_SLOT_BYTES * MODE;
-  static_assert(Shape::BYTES + 128 + Shape::WARPS * Shape::S * SEG_BLOCKS * MMA_SLOT_BYTES * 2 <=
-                    MAX_SMEM,
-                "the staged x of two vectors fits beside the ring");
   DRIFT_CUDA(launch_pdl(matvec_split_kernel<T, MODE>, unsigned(grid), Shape::WARPS * 32,
-                        Shape::BYTES + extra, stream, launch));
+                        Shape::BYTES + (MODE == MODE_MMA ? Shape::CHAIN_BYTES : 0), stream, launch));
   return 0;
 }
 
@@ -887,12 +796,8 @@ long long split_units(int64_t rows, int64_t cols) {
 // 8 vectors, SPLIT_UNITS units together).
 template <typename T>
 int split_dispatch(int count, const uint8_t* const* weights, float* const* ys, const int64_t* rows,
-                   int cols, const uint8_t* records, int vectors, cudaStream_t stream,
-                   int gated = 0, float* gated_out = nullptr, uint8_t* gated_records = nullptr) {
+                   int cols, const uint8_t* records, int vectors, cudaStream_t stream) {
   SplitLaunch launch = {};
-  launch.gated = gated;
-  launch.gated_out = gated_out;
-  launch.gated_records = gated_records;
   int n = 0, tiles = 0;
   for (int i = 0; i < count; ++i) {
     if (rows[i] == 0) continue;
@@ -913,12 +818,6 @@ int split_dispatch(int count, const uint8_t* const* weights, float* const* ys, c
   const long long segments = (cols / 32 + SEG_BLOCKS - 1) / SEG_BLOCKS;
   const long long units = (long long)tiles * group_count(segments);
   if (units > SPLIT_UNITS) return invalid("a balanced launch of %lld units", units);
-  if (vectors <= 2) {
-    if ((reinterpret_cast<uintptr_t>(records) & 15) != 0)
-      return invalid("x's records do not start on a 16-byte boundary");
-    DRIFT_TRY(encode_word_rows(&launch.xmap, records, MMA_RECORD_BYTES / 4, cols / 32,
-                               MMA_SLOT_BYTES / 4 * vectors, SEG_BLOCKS));
-  }
   if (vectors == 1) return launch_split_mode<T, MODE_DP4A_1>(launch, units, stream);
   if (vectors == 2) return launch_split_mode<T, MODE_DP4A_2>(launch, units, stream);
   return launch_split_mode<T, MODE_MMA>(launch, units, stream);
@@ -1010,37 +909,6 @@ int matvec_ring_many(int weight_dtype, int count, const void* const* weights,
         break;
       default:
         DRIFT_TRY(split_dispatch<Q4_1T>(count, w, y, rows, int(cols), r, n, stream));
-    }
-  }
-  return 0;
-}
-
-// x . gate^T and x . up^T in one balanced launch per pass of 8 vectors, and
-// out = act(gate) x up with out's records (rows of `rows` values) -- gated
-// when both tiles of a row range are done, in the launch. The caller checks
-// ring_many_fits for the two and rows % 32 == 0.
-int matvec_ring_gated(int weight_dtype, const void* gate, const void* up, const uint8_t* records,
-                      float* gate_out, float* up_out, float* out, uint8_t* out_records,
-                      int64_t rows, int64_t cols, int64_t vectors, int kind,
-                      cudaStream_t stream) {
-  const int64_t blocks = cols / 32, out_blocks = rows / 32;
-  const int64_t both[2] = {rows, rows};
-  for (int64_t first = 0; first < vectors; first += 8) {
-    const int n = int(vectors - first < 8 ? vectors - first : 8);
-    const uint8_t* w[2] = {static_cast<const uint8_t*>(gate), static_cast<const uint8_t*>(up)};
-    float* y[2] = {gate_out + first * rows, up_out + first * rows};
-    const uint8_t* r = records + (first / 8) * blocks * MMA_RECORD_BYTES;
-    uint8_t* o = out_records ? out_records + (first / 8) * out_blocks * MMA_RECORD_BYTES : nullptr;
-    float* g = out + first * rows;
-    switch (weight_dtype) {
-      case DRIFT_Q8_0:
-        DRIFT_TRY(split_dispatch<Q8_0T>(2, w, y, both, int(cols), r, n, stream, 1 + kind, g, o));
-        break;
-      case DRIFT_Q4_0:
-        DRIFT_TRY(split_dispatch<Q4_0T>(2, w, y, both, int(cols), r, n, stream, 1 + kind, g, o));
-        break;
-      default:
-        DRIFT_TRY(split_dispatch<Q4_1T>(2, w, y, both, int(cols), r, n, stream, 1 + kind, g, o));
     }
   }
   return 0;

@@ -176,9 +176,6 @@ class DenseDecoder:
         # (the norms, the attention join, SwiGLU): one buffer, each product
         # reading it before the next producer writes it
         self.prepared = ops.prepared_x(b, max(c.hidden, self.q_heads * hd, self.ffn))
-        # the gated feed-forward's records, written while the gate and up
-        # products still read x's from `prepared`
-        self.prepared_ffn = ops.prepared_x(b, self.ffn)
         self.graph: Optional[torch.cuda.CUDAGraph] = None
         # the row-split products' exchange: peer memory over NVLink, fused
         # with the residual add and the norm ("peer"), or NCCL ("nccl")
@@ -235,17 +232,21 @@ class DenseDecoder:
                 # partials into the exchange's slots; every rank sums them
                 ops.linears(attended, [layer.o], [self.exchange.slots[0]], prepared)
                 self.exchange.add_rms_norm(0, self.x, mlp_norm, prepared)
-                ops.linears_gated(SILU, self.normed, layer.gate, layer.up, self.gate, self.up,
-                                  self.gate, prepared, self.prepared_ffn)
-                ops.linears(self.gate, [layer.down], [self.exchange.slots[1]], self.prepared_ffn)
+                ops.linears(self.normed, [layer.gate, layer.up], [self.gate, self.up], prepared)
+                ops.gated(SILU, self.gate, self.up, self.gate, prepared)
+                ops.linears(self.gate, [layer.down], [self.exchange.slots[1]], prepared)
                 self.exchange.add_rms_norm(1, self.x, next_norm, prepared)
                 continue
             ops.linears(attended, [layer.o], [self.projected], prepared)
             self._all_reduce(self.projected)
             ops.add_rms_norm(self.x, self.projected, mlp_norm, prepared)
-            ops.linears_gated(SILU, self.normed, layer.gate, layer.up, self.gate, self.up,
-                              self.gate, prepared, self.prepared_ffn)
-            ops.linears(self.gate, [layer.down], [self.projected], self.prepared_ffn)
+            # SwiGLU stays a launch of its own: fused into the gate/up
+            # launch's epilogue it held that launch's SMs to its end, and the
+            # down product's weight copies, which start during the short
+            # SwiGLU launch, lost more than the launch cost
+            ops.linears(self.normed, [layer.gate, layer.up], [self.gate, self.up], prepared)
+            ops.gated(SILU, self.gate, self.up, self.gate, prepared)
+            ops.linears(self.gate, [layer.down], [self.projected], prepared)
             self._all_reduce(self.projected)
             ops.add_rms_norm(self.x, self.projected, next_norm, prepared)
         ops.linears(self.normed, [w.lm_head], [self.logits], prepared)

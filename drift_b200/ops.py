@@ -252,26 +252,6 @@ class CudaOps:
                                                      ns, m, k, self._stream())
         check("drift_linears", status)
 
-    def linears_gated(self, kind: int, x: torch.Tensor, gate: Stored, up: Stored,
-                      gate_out: torch.Tensor, up_out: torch.Tensor, out: torch.Tensor,
-                      prepared: torch.Tensor, out_prepared: Optional[torch.Tensor] = None) -> None:
-        """gate_out, up_out = x · gateᵀ, x · upᵀ; out = kind(gate_out) × up_out
-        (linears then gated, NormalisationOps.scala:24), the gating in the
-        products' launch below 32 rows; with `out_prepared` (not `prepared`),
-        out's records for the down product."""
-        m, n, k = self._check_linear(x, gate, gate_out)
-        _require(tuple(self._check_linear(x, up, up_out)) == (m, n, k),
-                 "gated linears: gate and up of one shape")
-        _require(isinstance(gate, Stored) and isinstance(up, Stored) and gate.dtype == up.dtype,
-                 "gated linears: quantized gate and up of one type")
-        _f32("gated", out)
-        _require(tuple(out.shape) == (m, n), f"gated: out {list(out.shape)} for [{m}, {n}]")
-        status = self.lib.drift_linears_gated_prepared(
-            kind, _x_dtype("linear", x), _ptr(x), _ptr(prepared), gate.dtype, _ptr(gate.data),
-            _ptr(up.data), _ptr(gate_out), _ptr(up_out), _ptr(out), m, n, k, _ptr(out_prepared),
-            self._stream())
-        check("drift_linears_gated_prepared", status)
-
     def embedding(self, table: Stored, ids: torch.Tensor, out: torch.Tensor) -> None:
         """out[t] = table[ids[t]] as F32 (LinearOps.scala:83-87; checks L163-177)."""
         _require(len(table.shape) == 2,

@@ -346,21 +346,6 @@ int drift_linears_prepared(int x_dtype, const void* x, const void* prepared, int
                            const int* weight_dtypes, const void* const* weights,
                            float* const* outs, const int64_t* ns, int64_t m, int64_t k,
                            drift_stream_t stream);
-/* A dense feed-forward's gate and up products and its gating in one call:
- * gate_out = x . gate^T, up_out = x . up^T (both [m, n]) and out = act(gate_out)
- * x up_out (drift_gated's activation codes; out may alias gate_out), with
- * out's records into `out_prepared` (NULL for none; n a multiple of 32) for
- * the down product -- the runner's linears(gate, up) then gated(Silu, ...)
- * (DenseDecoder.scala's feed-forward, ops/NormalisationOps.scala:24). For
- * 1-2 rows of x whose two products share a balanced launch, the gating runs
- * in that launch's epilogue (no launch of its own); otherwise the two calls
- * it replaces, with the same bits either way. `out_prepared`
- * must not overlap `prepared`: x's records are still read while out's are
- * written. */
-int drift_linears_gated_prepared(int kind, int x_dtype, const void* x, const void* prepared,
-                                 int weight_dtype, const void* gate, const void* up,
-                                 float* gate_out, float* up_out, float* out, int64_t m, int64_t n,
-                                 int64_t k, void* out_prepared, drift_stream_t stream);
 
 /* ---- the tensor-parallel exchange over NVLink (new) --------------------------
  * The reference runs one device (native/HipRuntime.scala:40-43); a B200 box

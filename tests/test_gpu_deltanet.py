@@ -158,6 +158,7 @@ def test_delta_decode_step_is_the_three_launches(ops, sequences, key_heads, valu
     conv1, states1 = conv_states.clone(), states.clone()
     out1 = torch.empty(sequences, value_heads, dim, device="cuda")
     prepared1 = ops.prepared_x(sequences, value_heads * dim)
+    prepared1.fill_(0xA5)  # the slots past the sequences are left as they were
     ops.delta_decode_step(qkv, z, conv, conv1, torch.empty_like(qkv), a, b, decay, dt_bias,
                           states1, rule, norm, 1e-6, out1, prepared1)
     conv2, states2 = conv_states.clone(), states.clone()
@@ -166,6 +167,7 @@ def test_delta_decode_step_is_the_three_launches(ops, sequences, key_heads, valu
     out2 = torch.empty_like(out1)
     ops.gated_delta_rule_decode(convolved, a, b, decay, dt_bias, states2, rule, out2)
     prepared2 = ops.prepared_x(sequences, value_heads * dim)
+    prepared2.fill_(0xA5)
     core = out2.view(sequences * value_heads, dim)
     ops.gated_rms_norm(core, norm, z.view(sequences * value_heads, dim), SILU, 1e-6, core,
                        prepared2, value_heads)

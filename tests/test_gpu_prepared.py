@@ -88,58 +88,6 @@ def test_gated_records_feed_linear(ops, m):
     assert torch.equal(fused, alone)
 
 
-@pytest.mark.parametrize("dtype", [oracle.Q4_1, oracle.Q4_0, oracle.Q8_0])
-@pytest.mark.parametrize("m,ffn,hidden", [(1, 1536, 512), (2, 12288, 4096), (3, 1024, 2048),
-                                          (8, 3072, 1024), (16, 1536, 512), (31, 512, 256)])
-def test_gated_linears_are_linears_then_gated(ops, dtype, m, ffn, hidden):
-    """The feed-forward's gate and up products with the gating in their
-    launch: the same gate, up, SwiGLU and records, bit for bit, as linears,
-    then gated with records; and the down product over those records."""
-    rng = np.random.default_rng(m + ffn + dtype)
-    gate, up = weights(rng, [ffn, ffn], hidden, dtype)
-    (down,) = weights(rng, [hidden], ffn, dtype)
-    x = torch.from_numpy(rng.standard_normal((m, hidden)).astype(np.float32)).cuda()
-    weight = torch.from_numpy((1 + 0.02 * rng.standard_normal(hidden)).astype(np.float32)).cuda()
-    prepared = ops.prepared_x(m, hidden)
-    normed = torch.empty_like(x)
-    ops.add_rms_norm(x.clone(), None, RowNorm(weight, 1e-6, 0.0, normed), prepared)
-    g1, u1 = torch.empty(m, ffn, device="cuda"), torch.empty(m, ffn, device="cuda")
-    out_prepared = ops.prepared_x(m, ffn)
-    out_prepared.fill_(0xA5)
-    for _ in range(2):  # the pair counts are left at zero: a second call is the same
-        ops.linears_gated(SILU, normed, gate, up, g1, u1, g1, prepared, out_prepared)
-    y1 = torch.empty(m, hidden, device="cuda")
-    ops.linears(g1, [down], [y1], out_prepared)
-    g2, u2 = torch.empty_like(g1), torch.empty_like(u1)
-    ops.linears(normed, [gate, up], [g2, u2], prepared)
-    hidden2 = torch.empty_like(g2)
-    records2 = ops.prepared_x(m, ffn)
-    records2.fill_(0xA5)
-    ops.gated(SILU, g2, u2, hidden2, records2)
-    y2 = torch.empty_like(y1)
-    ops.linears(hidden2, [down], [y2], records2)
-    torch.cuda.synchronize()
-    assert torch.equal(u1, u2)
-    assert torch.equal(g1, hidden2)
-    assert torch.equal(out_prepared, records2)
-    assert torch.equal(y1, y2)
-    assert ops.take_device_error() == 0
-
-
-def test_gated_linears_refusals(ops):
-    rng = np.random.default_rng(1)
-    gate, up = weights(rng, [64, 64], 256)
-    x = torch.zeros(2, 256, device="cuda")
-    g, u = torch.empty(2, 64, device="cuda"), torch.empty(2, 64, device="cuda")
-    prepared = ops.prepared_x(2, 256)
-    with pytest.raises(ValueError, match="overlap"):
-        ops.linears_gated(SILU, x, gate, up, g, u, g, prepared, prepared)
-    (odd,) = weights(rng, [70], 256)
-    g70, u70 = torch.empty(2, 70, device="cuda"), torch.empty(2, 70, device="cuda")
-    with pytest.raises(ValueError, match="32-value blocks"):
-        ops.linears_gated(SILU, x, odd, odd, g70, u70, g70, prepared, ops.prepared_x(2, 96))
-
-
 @pytest.mark.parametrize("dim,q_heads,kv_heads", [(128, 8, 2), (64, 4, 4), (256, 4, 1)])
 def test_attention_records_feed_linear(ops, dim, q_heads, kv_heads):
     rng = np.random.default_rng(dim)
