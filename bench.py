@@ -871,6 +871,93 @@ def run_hybrid_case(batch: int, layers: int, steps: int) -> None:
     print(f"hybrid case b{batch} x {config.layers} layers: {steps} steps")
 
 
+def run_decode_groups(batch: int, layers: int, steps: int) -> None:
+    """`--decode-groups B`: per rank, the device time of each op group of the
+    C4 and C5 decode steps (`--decode-layers` layers, batch B): the step with
+    a CUDA event after each group, captured as a CUDA graph (the events as
+    record nodes, so no host launch time shows) and replayed `steps` times
+    after two warm-up replays -- which group limits a tensor- or
+    expert-parallel step. The event nodes stop each group's launches from
+    overlapping the next group's (programmatic dependent launch), so the sum
+    is above the plain step's time. An exchange's time on a rank includes its
+    wait for the slowest rank. Runs under torchrun like the bench; rank 0
+    prints one JSON line."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from drift_b200.decoder import DenseConfig, DenseDecoder, DenseWeights
+    from drift_b200.hybrid import HybridConfig, HybridDecoder, HybridWeights
+    from drift_b200.ops import CudaOps
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                timeout=datetime.timedelta(seconds=120))
+    group = dist.group.WORLD if world > 1 else None
+    ops = CudaOps(local)
+    result = {"batch": batch, "layers": layers, "ranks": world, "steps": steps,
+              "unit": "us per step"}
+
+    def profile(decoder) -> dict:
+        stream = torch.cuda.Stream()
+        with torch.cuda.stream(stream):
+            decoder.step()  # lazy state resolved outside the capture
+        torch.cuda.synchronize()
+        decoder.marks = []
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            decoder.step()
+        marks, decoder.marks = decoder.marks, None
+        for _ in range(2):
+            graph.replay()
+        torch.cuda.synchronize()
+        totals: dict = {}
+        for _ in range(steps):
+            if world > 1:
+                dist.barrier()
+            graph.replay()
+            torch.cuda.synchronize()
+            for (_, before), (name, after) in zip(marks, marks[1:]):
+                totals[name] = totals.get(name, 0.0) + before.elapsed_time(after) * 1000
+        del graph
+        return {name: round(t / steps, 1) for name, t in totals.items()}
+
+    dense = DenseConfig(layers=layers)
+    decoder = DenseDecoder(ops, dense, DenseWeights.random(dense, rank=rank, world=world), batch,
+                           DECODE_CONTEXT, group=group)
+    decoder.prefill_random(DECODE_CONTEXT - 1)
+    decoder.positions.fill_(DECODE_CONTEXT - 1)
+    decoder.reserve()
+    c4 = profile(decoder)
+    decoder.release()
+    del decoder
+    torch.cuda.empty_cache()
+    hybrid = HybridConfig(layers=layers)
+    decoder = HybridDecoder(ops, hybrid, HybridWeights.random(hybrid, rank=rank, world=world),
+                            batch, DECODE_CONTEXT, group=group)
+    decoder.prefill_random(DECODE_CONTEXT - 1)
+    decoder.positions.fill_(DECODE_CONTEXT - 1)
+    decoder.reserve()
+    c5 = profile(decoder)
+    decoder.release()
+    del decoder
+    per_rank = [(c4, c5)]
+    if world > 1:
+        per_rank = [None] * world
+        dist.all_gather_object(per_rank, (c4, c5))
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        result["c4"] = [p[0] for p in per_rank]
+        result["c5"] = [p[1] for p in per_rank]
+        print(json.dumps({"decode_groups": result}), flush=True)
+
+
 def run_decode_case(batch: int, layers: int, steps: int) -> None:
     """`--decode-case B`: eager decode steps of C4 (with `--decode-layers`
     layers), nothing timed -- the workload of a launch-list capture."""
@@ -906,6 +993,8 @@ def main() -> int:
                         help="tensor-parallel decode: the fused NVLink peer exchange, or NCCL")
     parser.add_argument("--decode-case", type=int, help="B: eager C4 decode steps (profiling)")
     parser.add_argument("--hybrid-case", type=int, help="B: eager C5 decode steps (profiling)")
+    parser.add_argument("--decode-groups", type=int,
+                        help="B: per-rank device time of each decode op group (profiling)")
     parser.add_argument("--decode-layers", type=int, default=36)
     parser.add_argument("--case", help="B,N,K: run one product --repeat times (profiling)")
     parser.add_argument("--case-dtype", type=int, default=Q4_1)
@@ -913,6 +1002,9 @@ def main() -> int:
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)
     args.decode_batches = [int(b) for b in str(args.decode_batches).split(",") if b]
+    if args.decode_groups:
+        run_decode_groups(args.decode_groups, args.decode_layers, args.repeat)
+        return 0
     if args.decode_case:
         run_decode_case(args.decode_case, args.decode_layers, args.repeat)
         return 0

@@ -184,6 +184,16 @@ class DenseDecoder:
             from .tensor_parallel import PeerExchange
             self.exchange = PeerExchange(ops, group, b, c.hidden)
         self._positions_host: list[int] = [0] * b
+        # (name, CUDA event) after each op group of an eager step, when a
+        # profiler sets it to a list
+        self.marks: Optional[list] = None
+
+    def _mark(self, name: str) -> None:
+        if self.marks is not None:
+            # (an event record node when the step is captured in a graph)
+            event = torch.cuda.Event(enable_timing=True, external=True)
+            event.record()
+            self.marks.append((name, event))
 
     def prefill_random(self, positions: int, seed: int = 1) -> None:
         """Every sequence's cache holds `positions` positions of N(0, 1) keys
@@ -211,11 +221,15 @@ class DenseDecoder:
         ops, c, w = self.ops, self.config, self.weights
         b, hd = self.batch, c.head_dim
         prepared = self.prepared
+        mark = self._mark
+        mark("start")
         ops.embedding(w.embedding, self.ids, self.x)
         ops.add_rms_norm(self.x, None, RowNorm(w.layers[0].attention_norm, c.epsilon, 0.0,
                                                self.normed), prepared)
+        mark("embed")
         for index, (layer, cache) in enumerate(zip(w.layers, self.caches)):
             ops.linears(self.normed, [layer.q, layer.k, layer.v], [self.q, self.k, self.v], prepared)
+            mark("qkv")
             # per-head q/k norms, rope, cache write: one launch for the batch;
             # then every sequence's attention in one launch
             ops.attention_inputs_decode(
@@ -224,6 +238,7 @@ class DenseDecoder:
                 self.positions, self.rope, self.q_turned, cache, self.page_tables)
             ops.attention_decode(self.q_turned, cache, self.page_tables, self.positions,
                                  self.context, self.attention, self.attended, prepared)
+            mark("attention")
             following = w.layers[index + 1].attention_norm if index + 1 < len(w.layers) else w.final_norm
             mlp_norm = RowNorm(layer.mlp_norm, c.epsilon, 0.0, self.normed)
             next_norm = RowNorm(following, c.epsilon, 0.0, self.normed)
@@ -231,26 +246,40 @@ class DenseDecoder:
             if self.exchange is not None:
                 # partials into the exchange's slots; every rank sums them
                 ops.linears(attended, [layer.o], [self.exchange.slots[0]], prepared)
+                mark("o")
                 self.exchange.add_rms_norm(0, self.x, mlp_norm, prepared)
+                mark("exchange")
                 ops.linears(self.normed, [layer.gate, layer.up], [self.gate, self.up], prepared)
+                mark("gate_up")
                 ops.gated(SILU, self.gate, self.up, self.gate, prepared)
+                mark("swiglu")
                 ops.linears(self.gate, [layer.down], [self.exchange.slots[1]], prepared)
+                mark("down")
                 self.exchange.add_rms_norm(1, self.x, next_norm, prepared)
+                mark("exchange")
                 continue
             ops.linears(attended, [layer.o], [self.projected], prepared)
+            mark("o")
             self._all_reduce(self.projected)
             ops.add_rms_norm(self.x, self.projected, mlp_norm, prepared)
+            mark("add_norm" if self.group is None else "exchange")
             # SwiGLU stays a launch of its own: fused into the gate/up
             # launch's epilogue it held that launch's SMs to its end, and the
             # down product's weight copies, which start during the short
             # SwiGLU launch, lost more than the launch cost
             ops.linears(self.normed, [layer.gate, layer.up], [self.gate, self.up], prepared)
+            mark("gate_up")
             ops.gated(SILU, self.gate, self.up, self.gate, prepared)
+            mark("swiglu")
             ops.linears(self.gate, [layer.down], [self.projected], prepared)
+            mark("down")
             self._all_reduce(self.projected)
             ops.add_rms_norm(self.x, self.projected, next_norm, prepared)
+            mark("add_norm" if self.group is None else "exchange")
         ops.linears(self.normed, [w.lm_head], [self.logits], prepared)
+        mark("lm_head")
         self.sampler(self.logits, self.next_ids)
+        mark("sample")
         return self.logits
 
     def reserve(self) -> None:

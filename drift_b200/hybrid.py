@@ -424,6 +424,16 @@ class HybridDecoder:
         widest = max(c.hidden, self.value_width, self.q_heads * c.head_dim, c.shared_ffn)
         self.prepared = ops.prepared_x(b, widest)
         self.graph: Optional[torch.cuda.CUDAGraph] = None
+        # (name, CUDA event) after each op group of an eager step, when a
+        # profiler sets it to a list
+        self.marks: Optional[list] = None
+
+    def _mark(self, name: str) -> None:
+        if self.marks is not None:
+            # (an event record node when the step is captured in a graph)
+            event = torch.cuda.Event(enable_timing=True, external=True)
+            event.record()
+            self.marks.append((name, event))
 
     def prefill_random(self, positions: int, seed: int = 1) -> None:
         """Caches holding `positions` positions of N(0, 1) keys and values;
@@ -449,6 +459,7 @@ class HybridDecoder:
         # combine + norm, or the first norm)
         ops.linears(self.normed, [layer.qkv, layer.z, layer.a, layer.b],
                     [self.qkv, self.z, self.a, self.b], P)
+        self._mark("mixer_in")
         # the convolution, the delta rule and the gated norm (with the out
         # projection's records): one launch
         ops.delta_decode_step(self.qkv, self.z, layer.conv, self.conv_states[index],
@@ -456,19 +467,24 @@ class HybridDecoder:
                               self.delta_states[index],
                               (self.delta_key_heads, self.delta_value_heads, c.delta_dim, False),
                               layer.norm, c.epsilon, self.core, P)
+        self._mark("delta_step")
         ops.linears(self.core.view(b, self.value_width), [layer.out], [self._block_out(0)], P)
+        self._mark("mixer_out")
 
     def _full(self, layer: FullLayer, index: int) -> None:
         ops, c, b, P = self.ops, self.config, self.batch, self.prepared
         ops.linears(self.normed, [layer.q, layer.k, layer.v],
                     [self.query_gate.view(b, -1), self.k.view(b, -1), self.v.view(b, -1)], P)
+        self._mark("mixer_in")
         ops.attention_inputs_decode(self.query_gate, self.k, self.v, layer.q_norm, layer.k_norm,
                                     c.epsilon, self.positions, self.rope, self.q_turned,
                                     self.caches[index], self.page_tables)
         ops.attention_decode(self.q_turned, self.caches[index], self.page_tables, self.positions,
                              self.context, self.attention, self.attended, P,
                              gate=self.query_gate[:, :, c.head_dim:])
+        self._mark("attention")
         ops.linears(self.attended.view(b, -1), [layer.o], [self._block_out(0)], P)
+        self._mark("mixer_out")
 
     def _block_out(self, slot: int) -> torch.Tensor:
         """Where a row-split output goes: the exchange's slot, or block_out."""
@@ -481,6 +497,7 @@ class HybridDecoder:
         # gate and up products (the weights hold every expert from 0 on)
         ops.route_linear(self.normed, mixture.router, self.logits_router, self.route_ids,
                          self.route_weights, P)
+        self._mark("route")
         next_norm = RowNorm(following, c.epsilon, 0.0, self.normed)
         if self.exchange is None and mixture.fused is not None:
             # routed and shared experts in one launch each: gate/up (the
@@ -488,10 +505,13 @@ class HybridDecoder:
             gate, up, down = mixture.fused
             ops.experts_gated_linear(self.normed, gate, up, self.all_ids, self.all_gated, 0, P,
                                      shared_tail=True)
+            self._mark("experts_gate_up")
             ops.experts_linear(self.all_gated, down, self.all_ids, self.all_out)
+            self._mark("experts_down")
             ops.moe_combine_norm(self.expert_out, self.route_weights,
                                  SharedExpert(self.shared_out, self.normed, mixture.shared_router),
                                  self.x, next_norm, P)
+            self._mark("combine_norm")
             return
         if self.exchange is None:
             ops.experts_gated_linear(self.normed, mixture.gate, mixture.up,
@@ -516,17 +536,23 @@ class HybridDecoder:
             gate, up, down = mixture.fused
             ops.experts_gated_linear(self.normed, gate, up, self.all_ids, self.all_gated,
                                      first_expert=first - 1, prepared=P, shared_tail=True)
+            self._mark("experts_gate_up")
             ops.experts_linear(self.all_gated, down, self.all_ids, self.all_out,
                                first_expert=first - 1)
+            self._mark("experts_down")
             shared = SharedExpert(self.shared_out, self.normed, mixture.shared_router)
             ops.moe_combine(self.expert_out, self.route_weights, shared, None,
                             self.exchange.slots[1])
+            self._mark("combine")
             self.exchange.add_rms_norm(1, self.x, next_norm, P)
+            self._mark("exchange")
             return
         ops.experts_gated_linear(self.normed, mixture.gate, mixture.up, self.route_ids.view(-1),
                                  self.expert_gated, first_expert=first, prepared=P)
+        self._mark("experts_gate_up")
         ops.experts_linear(self.expert_gated, mixture.down, self.route_ids.view(-1),
                            self.expert_out, first_expert=first)
+        self._mark("experts_down")
         shared = None
         if self.part.rank == 0:
             ops.experts_gated_linear(self.normed, mixture.shared_gate, mixture.shared_up,
@@ -534,16 +560,20 @@ class HybridDecoder:
             ops.linears(self.shared_gated, [mixture.shared_down], [self.shared_out])
             shared = SharedExpert(self.shared_out, self.normed, mixture.shared_router)
         ops.moe_combine(self.expert_out, self.route_weights, shared, None, self.exchange.slots[1])
+        self._mark("combine")
         self.exchange.add_rms_norm(1, self.x, next_norm, P)
+        self._mark("exchange")
 
     def step(self) -> torch.Tensor:
         """One decode step: self.ids at self.positions -> self.logits (this
         rank's vocabulary rows) and self.next_ids (each sequence's greedy next
         token over the whole vocabulary)."""
         ops, c, w, P = self.ops, self.config, self.weights, self.prepared
+        self._mark("start")
         ops.embedding(w.embedding, self.ids, self.x)
         ops.add_rms_norm(self.x, None, RowNorm(w.layers[0].input_norm, c.epsilon, 0.0, self.normed),
                          P)
+        self._mark("embed")
         for index, layer in enumerate(w.layers):
             if isinstance(layer.mixer, FullLayer):
                 self._full(layer.mixer, index)
@@ -552,13 +582,17 @@ class HybridDecoder:
             post = RowNorm(layer.post_norm, c.epsilon, 0.0, self.normed)
             if self.exchange is not None:
                 self.exchange.add_rms_norm(0, self.x, post, P)
+                self._mark("exchange")
             else:
                 ops.add_rms_norm(self.x, self.block_out, post, P)
+                self._mark("add_norm")
             following = (w.layers[index + 1].input_norm if index + 1 < len(w.layers)
                          else w.final_norm)
             self._mixture(layer.mixture, following)
         ops.linears(self.normed, [w.lm_head], [self.logits], P)
+        self._mark("lm_head")
         self.sampler(self.logits, self.next_ids)
+        self._mark("sample")
         return self.logits
 
     def reserve(self) -> None:
