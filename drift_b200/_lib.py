@@ -17,6 +17,7 @@ DRIFT_ERROR_TIMEOUT = 1002
 
 # Storage types: GGML type ids (runner/src/drift/runner/tensor/DType.scala:151-175).
 F32, F16, Q4_0, Q4_1, Q8_0, I32, BF16 = 0, 1, 2, 3, 8, 26, 30
+Q4_K, Q6_K = 12, 14  # the K-quants (tensor/KQuants.scala:99, 122)
 
 _p, _i32, _i64, _f32, _sz = (ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float,
                              ctypes.c_size_t)

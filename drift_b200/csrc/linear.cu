@@ -26,6 +26,8 @@ int matvec_f32_weights(int x_dtype, const void* x, const float* weight, float* y
 bool tc_supports(int weight_dtype, const void* weight, int64_t k);
 bool ring_many_fits(int weight_dtype, int count, const void* const* weights, const int64_t* rows,
                     int64_t cols);
+int kquant_linear(int x_dtype, const void* x, int weight_dtype, const void* weight, float* y,
+                  int64_t m, int64_t n, int64_t k, cudaStream_t stream);
 int matvec_ring_many(int weight_dtype, int count, const void* const* weights,
                      const uint8_t* records, float* const* ys, const int64_t* rows, int64_t cols,
                      int64_t vectors, cudaStream_t stream);
@@ -47,13 +49,13 @@ int check_linear(int x_dtype, const void* x, int weight_dtype, const void* weigh
                                                (long long)m, (long long)k, (long long)n,
                                                (long long)k);
   if (weight_dtype != DRIFT_Q8_0 && weight_dtype != DRIFT_Q4_0 && weight_dtype != DRIFT_Q4_1 &&
-      weight_dtype != DRIFT_F32)
+      weight_dtype != DRIFT_Q4_K && weight_dtype != DRIFT_Q6_K && weight_dtype != DRIFT_F32)
     return invalid("no kernels for %s weights yet", dtype_name(weight_dtype));
   const int64_t row = byte_size(weight_dtype, k);
   if (row < 0)
     return invalid("%lld elements are not whole %s blocks of %d", (long long)k,
                    dtype_name(weight_dtype), block_elements(weight_dtype));
-  if (weight_dtype != DRIFT_F32 && row % 4 != 0)
+  if (weight_dtype != DRIFT_F32 && weight_dtype != DRIFT_Q6_K && row % 4 != 0)
     return invalid("%s rows of %lld are not whole words", dtype_name(weight_dtype), (long long)k);
   if (k > (1ll << 30) || m * k > 0x7fffffffll || n > 0x7fffffffll)
     return invalid("linear over [%lld, %lld]", (long long)m, (long long)k);
@@ -100,13 +102,21 @@ static int linears(int x_dtype, const void* x, const void* prepared, int count,
         DRIFT_CUDA(cudaMemsetAsync(outs[i], 0, size_t(m * ns[i]) * 4, s));
     return 0;
   }
+  // the K-quants: their own products, on x as it is (F32 or BF16)
+  auto k_quant = [&](int i) {
+    return weight_dtypes[i] == DRIFT_Q4_K || weight_dtypes[i] == DRIFT_Q6_K;
+  };
   bool quantized = false, tensor_cores = false;
   for (int i = 0; i < count; ++i) {
+    if (k_quant(i)) continue;
     const bool tc = weight_dtypes[i] != DRIFT_F32 && m >= GEMM_MINIMUM_ROWS &&
                     tc_supports(weight_dtypes[i], weights[i], k);
     tensor_cores |= tc;
     quantized |= weight_dtypes[i] != DRIFT_F32 && !tc;
   }
+  for (int i = 0; i < count; ++i)
+    if (k_quant(i) && ns[i] > 0)
+      DRIFT_TRY(kquant_linear(x_dtype, x, weight_dtypes[i], weights[i], outs[i], m, ns[i], k, s));
   const size_t records_bytes = quantized && !prepared ? records_region(m, k) : 0;
   void* w = nullptr;
   if ((quantized && !prepared) || tensor_cores)
@@ -121,10 +131,11 @@ static int linears(int x_dtype, const void* x, const void* prepared, int count,
   // together, and the F32 products one launch (up to 4).
   constexpr int SHARED = 4;
   auto streamed = [&](int i) {
-    return weight_dtypes[i] != DRIFT_F32 &&
+    return weight_dtypes[i] != DRIFT_F32 && !k_quant(i) &&
            !(m >= GEMM_MINIMUM_ROWS && tc_supports(weight_dtypes[i], weights[i], k));
   };
   std::vector<char> done(size_t(count), 0);
+  for (int i = 0; i < count; ++i) done[i] = k_quant(i);
   for (int i = 0; i < count; ++i) {
     if (done[i] || ns[i] == 0 || !streamed(i)) continue;
     int which[SHARED], c = 0;

@@ -51,6 +51,8 @@ int block_elements(int dtype) {
     case DRIFT_Q4_0:
     case DRIFT_Q4_1:
     case DRIFT_Q8_0: return 32;
+    case DRIFT_Q4_K:
+    case DRIFT_Q6_K: return 256;
     default: return -1;
   }
 }
@@ -64,6 +66,8 @@ int block_bytes(int dtype) {
     case DRIFT_Q4_0: return 18;
     case DRIFT_Q4_1: return 20;
     case DRIFT_Q8_0: return 34;
+    case DRIFT_Q4_K: return 144;
+    case DRIFT_Q6_K: return 210;
     default: return -1;
   }
 }
@@ -77,6 +81,8 @@ const char* dtype_name(int dtype) {
     case DRIFT_Q4_0: return "Q4_0";
     case DRIFT_Q4_1: return "Q4_1";
     case DRIFT_Q8_0: return "Q8_0";
+    case DRIFT_Q4_K: return "Q4_K";
+    case DRIFT_Q6_K: return "Q6_K";
     default: return "an unknown type";
   }
 }

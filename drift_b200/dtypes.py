@@ -20,10 +20,12 @@ F16 = DType("F16", 1, 1, 2)
 Q4_0 = DType("Q4_0", 2, 32, 18)
 Q4_1 = DType("Q4_1", 3, 32, 20)
 Q8_0 = DType("Q8_0", 8, 32, 34)
+Q4_K = DType("Q4_K", 12, 256, 144)  # tensor/KQuants.scala:99
+Q6_K = DType("Q6_K", 14, 256, 210)  # tensor/KQuants.scala:122
 I32 = DType("I32", 26, 1, 4)
 BF16 = DType("BF16", 30, 1, 2)
 
-DTYPES = {t.ggml_id: t for t in (F32, F16, Q4_0, Q4_1, Q8_0, I32, BF16)}
+DTYPES = {t.ggml_id: t for t in (F32, F16, Q4_0, Q4_1, Q8_0, Q4_K, Q6_K, I32, BF16)}
 
 
 def byte_size(dtype: int, elements: int) -> int:

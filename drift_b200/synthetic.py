@@ -10,6 +10,9 @@ benchmarks also run on random weights, gpuTest/.../MatVecBenchmark.scala).
 - `random_blocks`: the reference tests' weights (TestData.quantized,
   runner/test/src/drift/runner/TestData.scala:33-51): random bytes, so every
   code occurs, with f16 scales ~ N(0, 0.01).
+- `k_quant_blocks`: Q4_K / Q6_K super-blocks as the reference's fixture
+  recipe draws them (runner/fixtures/generate.py: random bytes, every f16
+  field ~ N(0, 0.05)), scaled down to N(0, 0.005) so products stay in range.
 x ~ N(0, 1) (bf16 or f32).
 """
 
@@ -17,8 +20,10 @@ from __future__ import annotations
 
 import numpy as np
 
-F32, Q4_0, Q4_1, Q8_0 = 0, 2, 3, 8
+F32, Q4_0, Q4_1, Q8_0, Q4_K, Q6_K = 0, 2, 3, 8, 12, 14
 BLOCK_BYTES = {Q4_0: 18, Q4_1: 20, Q8_0: 34}
+# the K-quants: (bytes per 256-value super-block, offsets of the f16 fields)
+K_LAYOUT = {Q4_K: (144, [0, 2]), Q6_K: (210, [208])}
 
 
 def _scales(rng: np.random.Generator, count: int) -> np.ndarray:
@@ -99,4 +104,15 @@ def quantized_device(dtype: int, n: int, k: int, generator=None, device=None):
                                      dtype=torch.uint8)
     else:
         raise ValueError(f"no synthetic law for type {dtype}")
+    return out.reshape(-1)
+
+
+def k_quant_blocks(rng: np.random.Generator, dtype: int, n: int, k: int) -> np.ndarray:
+    """[n, k] weights of Q4_K or Q6_K as raw super-blocks (uint8)."""
+    size, fields = K_LAYOUT[dtype]
+    count = n * (k // 256)
+    out = rng.integers(0, 256, size=(count, size), dtype=np.uint8)
+    for at in fields:
+        halves = (rng.standard_normal(count) * 0.005).astype(np.float16)
+        out[:, at:at + 2] = halves.view(np.uint8).reshape(count, 2)
     return out.reshape(-1)

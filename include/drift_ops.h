@@ -44,6 +44,8 @@ extern "C" {
 #define DRIFT_Q4_0 2
 #define DRIFT_Q4_1 3
 #define DRIFT_Q8_0 8
+#define DRIFT_Q4_K 12 /* super-blocks of 256 (tensor/KQuants.scala:99) */
+#define DRIFT_Q6_K 14 /* (KQuants.scala:122) */
 #define DRIFT_I32 26
 #define DRIFT_BF16 30
 

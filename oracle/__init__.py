@@ -27,10 +27,11 @@ LIBRARY = os.path.join(HERE, "liboracle.so")
 
 # GGML type ids (runner/src/drift/runner/tensor/DType.scala:151-175).
 F32, F16, Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, BF16 = 0, 1, 2, 3, 6, 7, 8, 30
+Q4_K, Q6_K = 12, 14  # tensor/KQuants.scala:99, 122
 BLOCK = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q4_0: (32, 18), Q4_1: (32, 20),
-         Q5_0: (32, 22), Q5_1: (32, 24), Q8_0: (32, 34)}
+         Q5_0: (32, 22), Q5_1: (32, 24), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210)}
 NAMES = {F32: "F32", F16: "F16", BF16: "BF16", Q4_0: "Q4_0", Q4_1: "Q4_1",
-         Q5_0: "Q5_0", Q5_1: "Q5_1", Q8_0: "Q8_0"}
+         Q5_0: "Q5_0", Q5_1: "Q5_1", Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K"}
 
 
 def build() -> str:

@@ -4,7 +4,7 @@ The reference commits runner/test/resources/fixtures/quants/<type>.safetensors
 as Git LFS pointers only (sha256 + size); the bytes are not in its checkout.
 Its generator, runner/fixtures/generate.py:41-91, draws them from
 numpy.random.default_rng(42) -- 16 blocks per type in the order Q4_0, Q4_1,
-Q5_0, Q5_1, Q8_0, ..., block 0 all zeros, block 1 all 0xFF, the f16 scale
+Q5_0, Q5_1, Q8_0, Q2_K, Q3_K, Q4_K, Q5_K, Q6_K, ..., block 0 all zeros, block 1 all 0xFF, the f16 scale
 fields drawn as standard_normal * 0.05 -- and stores each block's decode by
 gguf-py's `dequantize` as "expected".
 
@@ -33,7 +33,15 @@ POINTERS = {
     "q5_0": ("8208b9cfc49aa08a690a54a0b7e341d7c797bcda14ea1c946035827738665ca0", 2544),
     "q5_1": ("fdcf6eea0ba8968d7e5c25a3136cdce9bf66cce3c6c64eb0322065e290172d95", 2576),
     "q8_0": ("344260c8b28001cb9b2e7e78ef61e5e0cd59c9a6a6c1d99b87b181325c9109e0", 2736),
+    "q2_k": ("bcc9580b7f5e838eb1958634d93e2a6119f1fde2f782232325f325509d28794a", 17880),
+    "q3_k": ("c6367bd2af93905fd5fb6e8255faec578489bea1c20a47df651cc5bb1b946392", 18296),
+    "q4_k": ("7f7f40d8244fb7b4918a075ecc6e1f58ecf257db487f3937a6a0130995e42912", 18840),
+    "q5_k": ("c0227321921d000b342e0efd747e6c9cdb861bb7b594a4d0f5d9b72591fda899", 19352),
+    "q6_k": ("073906d6b047810c6eff5d618bd43575357d57079973134db7024b18e5a188a4", 19896),
 }
+# the K-quants the library serves; the others are drawn only to keep the
+# generator's random sequence
+KEPT = {"q4_0", "q4_1", "q5_0", "q5_1", "q8_0", "q4_k", "q6_k"}
 
 
 def generate() -> dict:
@@ -50,6 +58,11 @@ def generate() -> dict:
         (T.Q5_0, 32, 22, [0]),
         (T.Q5_1, 32, 24, [0, 2]),
         (T.Q8_0, 32, 34, [0]),
+        (T.Q2_K, 256, 84, [80, 82]),
+        (T.Q3_K, 256, 110, [108]),
+        (T.Q4_K, 256, 144, [0, 2]),
+        (T.Q5_K, 256, 176, [0, 2]),
+        (T.Q6_K, 256, 210, [208]),
     ]
     count = 16
     files = {}
@@ -76,8 +89,9 @@ def main() -> int:
         bad += not ok
         print(f"{name}: {len(data)} bytes, sha256 {'matches' if ok else 'DIFFERS from'} "
               f"the reference's LFS pointer")
-        with open(os.path.join(HERE, "quants", f"{name}.safetensors"), "wb") as f:
-            f.write(data)
+        if name in KEPT:
+            with open(os.path.join(HERE, "quants", f"{name}.safetensors"), "wb") as f:
+                f.write(data)
     return 1 if bad else 0
 
 
