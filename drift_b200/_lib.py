@@ -114,6 +114,8 @@ SIGNATURES = {
     "drift_moe_combine": (_i32, [_p, _p, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p]),
     "drift_moe_combine_norm": (_i32, [_p, _p, _i64, _i64, _i64, _p, _p, _p, _p, _p, _f32, _f32,
                                       _p, _p]),
+    "drift_moe_decode": (_i32, [_i32, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
+                                _f32, _f32, _p, _p, _i64, _i64, _i64, _i64, _i64, _p]),
     "drift_moe_combine_norm_prepared": (_i32, [_p, _p, _i64, _i64, _i64, _p, _p, _p, _p, _p, _f32,
                                                _f32, _p, _p, _p]),
     "drift_workspace_reserve": (_i32, [_sz]),

@@ -14,6 +14,7 @@
 #include "quant.cuh"
 #include "registry.cuh"
 #include "rowwise.cuh"
+#include "tc_common.cuh"
 #include "x22.cuh"
 
 namespace drift {
@@ -28,14 +29,9 @@ int prepare_x_mma(int x_dtype, const void* x, int64_t m, int64_t k, uint8_t* rec
 // One warp per token: the k largest of `experts` <= 512 logits, the lower
 // expert first among equals, then their softmax among themselves in double
 // (as CpuExperts.route computes it), rounded once.
-__global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ logits,
-                                                    int* __restrict__ ids,
-                                                    float* __restrict__ weights, int tokens,
-                                                    int experts, int k) {
-  pdl_trigger();  // the next kernel may launch and wait for this one
-  pdl_wait();     // what the kernels before this one wrote is visible
-  const int t = blockIdx.x * (blockDim.x / WARP) + threadIdx.x / WARP;
-  if (t >= tokens) return;
+__device__ __forceinline__ void route_token(const float* __restrict__ logits,
+                                            int* __restrict__ ids, float* __restrict__ weights,
+                                            int t, int experts, int k) {
   const int lane = threadIdx.x % WARP;
   const float* row = logits + (long long)t * experts;
   float v[16];
@@ -104,6 +100,17 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
   }
 }
 
+__global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ logits,
+                                                    int* __restrict__ ids,
+                                                    float* __restrict__ weights, int tokens,
+                                                    int experts, int k) {
+  pdl_trigger();  // the next kernel may launch and wait for this one
+  pdl_wait();     // what the kernels before this one wrote is visible
+  const int t = blockIdx.x * (blockDim.x / WARP) + threadIdx.x / WARP;
+  if (t >= tokens) return;
+  route_token(logits, ids, weights, t, experts, k);
+}
+
 DRIFT_REGISTER(route_topk, route_kernel)
 
 // ---- experts' products ---------------------------------------------------------------------
@@ -121,28 +128,27 @@ DRIFT_REGISTER(route_topk, route_kernel)
 // (group, kw) takes 4 rows of its group and, lane l, blocks 32 kw + l,
 // 32 (kw + KS) + l, ...; the k-splits' sums meet in shared memory in a fixed
 // order.
-template <typename T, int KS, bool GATED, bool XQ = false>
-__global__ void __launch_bounds__(256) experts_x22_kernel(
+// One CTA's unit of the experts' products: row tile `tile` of slot `slot`
+// (the kernel's blockIdx.x, blockIdx.y). `x_slots`: XQ's x in shared memory.
+template <typename T, int KS, bool GATED, bool XQ>
+__device__ __forceinline__ void experts_unit(
     const uint8_t* __restrict__ gate, const uint8_t* __restrict__ up, long long expert_bytes,
     const int* __restrict__ ids, const uint8_t* __restrict__ records, int divisor,
     int routed_slots, float* __restrict__ y, int rows, int cols, long long experts,
-    long long first_expert, int others_zero, int* error, const float* __restrict__ x) {
-  pdl_trigger();  // the next kernel may launch and wait for this one
-  pdl_wait();     // what the kernels before this one wrote is visible
+    long long first_expert, int others_zero, int* error, const float* __restrict__ x,
+    int tile, int slot, uint8_t* x_slots) {
   constexpr int GROUPS = 8 / KS;
   constexpr int ROWS = 4;  // rows per warp
   __shared__ float partial[8][ROWS][2];
   const int warp = threadIdx.x / WARP, lane = threadIdx.x % WARP;
   const int kw = warp % KS, group = warp / KS;
-  const int slot = blockIdx.y;
   // the slot's expert in this weight (which holds experts [first_expert,
   // first_expert + experts)); with others_zero, a slot of another rank's
   // expert is zeros, not an error
   const long long expert = ids[slot] - first_expert;
-  const int row0 = (blockIdx.x * GROUPS + group) * ROWS;
+  const int row0 = (tile * GROUPS + group) * ROWS;
   const int blocks = cols / 32;
   const int v = slot < routed_slots ? slot / divisor : slot - routed_slots;
-  extern __shared__ __align__(16) uint8_t x_slots[];  // XQ: [blocks][112 bytes]
   const uint8_t* record =
       XQ ? x_slots
          : records + (long long)(v / 8) * blocks * MMA_RECORD_BYTES + MMA_SLOT_BYTES * (v % 8);
@@ -150,7 +156,7 @@ __global__ void __launch_bounds__(256) experts_x22_kernel(
   if (expert < 0 || expert >= experts) {
     if (!others_zero && threadIdx.x == 0 && blockIdx.x == 0 && error) atomicCAS(error, 0, 1);
     for (int r = threadIdx.x; r < GROUPS * ROWS; r += blockDim.x) {
-      const int row = blockIdx.x * GROUPS * ROWS + r;
+      const int row = tile * GROUPS * ROWS + r;
       if (row < rows) y[(long long)slot * rows + row] = others_zero ? 0.0f : __int_as_float(0x7fc00000);
     }
     return;
@@ -229,7 +235,7 @@ __global__ void __launch_bounds__(256) experts_x22_kernel(
   const int t = threadIdx.x;
   if (t < GROUPS * ROWS) {
     const int gi = t / ROWS, r = t % ROWS;
-    const int row = (blockIdx.x * GROUPS + gi) * ROWS + r;
+    const int row = (tile * GROUPS + gi) * ROWS + r;
     if (row < rows) {
       float gs = 0.0f, us = 0.0f;
 #pragma unroll
@@ -240,6 +246,20 @@ __global__ void __launch_bounds__(256) experts_x22_kernel(
       y[(long long)slot * rows + row] = GATED ? gs / (1.0f + expf(-gs)) * us : gs;
     }
   }
+}
+
+template <typename T, int KS, bool GATED, bool XQ = false>
+__global__ void __launch_bounds__(256) experts_x22_kernel(
+    const uint8_t* __restrict__ gate, const uint8_t* __restrict__ up, long long expert_bytes,
+    const int* __restrict__ ids, const uint8_t* __restrict__ records, int divisor,
+    int routed_slots, float* __restrict__ y, int rows, int cols, long long experts,
+    long long first_expert, int others_zero, int* error, const float* __restrict__ x) {
+  pdl_trigger();  // the next kernel may launch and wait for this one
+  pdl_wait();     // what the kernels before this one wrote is visible
+  extern __shared__ __align__(16) uint8_t x_slots[];  // XQ: [blocks][112 bytes]
+  experts_unit<T, KS, GATED, XQ>(gate, up, expert_bytes, ids, records, divisor, routed_slots, y,
+                                 rows, cols, experts, first_expert, others_zero, error, x,
+                                 blockIdx.x, blockIdx.y, x_slots);
 }
 
 #define DRIFT_EXPERTS_REGISTER(T, name)                                                   \
@@ -447,6 +467,237 @@ __global__ void __launch_bounds__(COMBINE_THREADS) combine_kernel(
 DRIFT_REGISTER(moe_combine_rows, (combine_kernel<false, 2>))
 DRIFT_REGISTER(moe_combine_norm_records, (combine_kernel<true, 2>))
 
+// ---- the whole mixture of a decode step in one launch ---------------------------------------
+// The router product, the top-k, the routed and shared experts' gate/up and
+// down products and the combine with the residual and the next norm -- five
+// launches' work -- in one cooperative launch: each phase is its launch's
+// work split into the same units (a (vector, row) of the router, a token's
+// top-k, a (row tile, slot) of the experts' products, a token's combine),
+// taken by the grid's CTAs in turn and computed by the same device code, so
+// the bits are the separate launches'; a grid barrier between phases. The
+// combine's 1024-thread block is stood in for by 256 threads, each holding
+// four of its threads' values, so its two reductions keep their order.
+constexpr int MOE_THREADS = 256;
+
+// A grid barrier: every CTA's writes before it are visible to every CTA
+// after it. Thread 0 of each CTA arrives on a count; the last to arrive
+// resets it and advances the generation the others wait on (at most about a
+// second, then device error 2 and false: the caller returns, its results
+// void).
+__device__ unsigned moe_arrivals, moe_generation;
+
+__device__ bool moe_grid_barrier(unsigned ctas, int* error) {
+  __shared__ int passed;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned generation = *reinterpret_cast<volatile unsigned*>(&moe_generation);
+    __threadfence();
+    passed = 1;
+    if (atomicAdd(&moe_arrivals, 1u) == ctas - 1) {
+      atomicExch(&moe_arrivals, 0u);
+      __threadfence();
+      atomicAdd(&moe_generation, 1u);
+    } else {
+      const uint64_t start = tc::global_ns();
+      while (*reinterpret_cast<volatile unsigned*>(&moe_generation) == generation) {
+        if (tc::global_ns() - start > 1000000000ull) {
+          atomicCAS(error, 0, 2);
+          passed = 0;
+          break;
+        }
+        __nanosleep(32);
+      }
+      __threadfence();
+    }
+  }
+  __syncthreads();
+  return passed != 0;
+}
+
+// combine_kernel<true, 2> for token t with 256 threads: thread (w, l) holds
+// the 1024-thread kernel's threads 32 (4 w + i) + l, i = 0..3, each with its
+// two columns c and c + 1024.
+__device__ void moe_combine_norm_token(
+    const float* __restrict__ expert_out, const float* __restrict__ weights,
+    const float* __restrict__ shared_out, const float* __restrict__ shared_input,
+    const float* __restrict__ shared_router, float* residual, int k, int hidden,
+    const float* __restrict__ norm_weight, float* __restrict__ normed, float epsilon,
+    float weight_offset, uint8_t* records, long long t) {
+  constexpr int V = 4, PER = 2, BIG = COMBINE_THREADS;
+  __shared__ float partial[32];
+  const int warp = threadIdx.x / WARP, lane = threadIdx.x % WARP;
+  // block_sum's order over the big block's 32 warps: virtual warp 4 w + i
+  // reduced by the same shuffle tree, then the 32 sums in order
+  auto big_sum = [&](float (&values)[V]) {
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+#pragma unroll
+      for (int o = 16; o > 0; o /= 2) values[i] += __shfl_xor_sync(0xffffffffu, values[i], o);
+      if (lane == 0) partial[4 * warp + i] = values[i];
+    }
+    __syncthreads();
+    float total = 0.0f;
+    for (int w = 0; w < BIG / WARP; ++w) total += partial[w];
+    __syncthreads();
+    return total;
+  };
+  float sum[V][PER], shared[V][PER], dot[V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int vt = WARP * (4 * warp + i) + lane;  // the big block's thread
+    float routed[PER];
+    dot[i] = 0.0f;
+#pragma unroll
+    for (int p = 0; p < PER; ++p) {
+      const int c = vt + p * BIG;
+      const bool in = c < hidden;
+      sum[i][p] = in ? residual[t * hidden + c] : 0.0f;
+      shared[i][p] = shared_out && in ? shared_out[t * hidden + c] : 0.0f;
+      if (shared_out && in) dot[i] = fmaf(shared_input[t * hidden + c], shared_router[c], dot[i]);
+      routed[p] = 0.0f;
+    }
+    // the routed experts' outputs, weighted, in slot order
+    for (int j = 0; j < k; ++j) {
+      const float wj = weights[t * k + j];
+#pragma unroll
+      for (int p = 0; p < PER; ++p) {
+        const int c = vt + p * BIG;
+        routed[p] = fmaf(wj, c < hidden ? expert_out[(t * k + j) * hidden + c] : 0.0f, routed[p]);
+      }
+    }
+#pragma unroll
+    for (int p = 0; p < PER; ++p) sum[i][p] = sum[i][p] + routed[p];  // residual + routed
+  }
+  // the shared expert's gate: sigmoid(x . router)
+  float gate = 0.0f;
+  if (shared_out) gate = 1.0f / (1.0f + expf(-big_sum(dot)));
+  float squares[V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int vt = WARP * (4 * warp + i) + lane;
+    squares[i] = 0.0f;
+#pragma unroll
+    for (int p = 0; p < PER; ++p) {
+      const int c = vt + p * BIG;
+      if (shared_out) sum[i][p] = fmaf(gate, shared[i][p], sum[i][p]);
+      if (c < hidden) residual[t * hidden + c] = sum[i][p];
+      squares[i] = fmaf(sum[i][p], sum[i][p], squares[i]);
+    }
+  }
+  const float total = big_sum(squares);
+  const float scale = 1.0f / sqrtf(total / float(hidden) + epsilon);
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int vt = WARP * (4 * warp + i) + lane;
+#pragma unroll
+    for (int p = 0; p < PER; ++p) {
+      const int c = vt + p * BIG;
+      if (c >= hidden) continue;  // whole warps: hidden is a multiple of 32
+      const float value = sum[i][p] * scale * (norm_weight[c] + weight_offset);
+      normed[t * hidden + c] = value;
+      if (records) x22_record_block(value, records, int(t), c / 32, hidden / 32);
+    }
+  }
+}
+
+struct MoeArgs {
+  // router: logits [tokens][experts] = x . router^T
+  const float* x;            // [tokens][hidden], the post norm's output (also the shared gate's input)
+  const uint8_t* x_records;  // its records, for the gate/up products
+  const float* router;       // [experts][hidden] F32
+  float* logits;
+  int* ids;                  // [tokens k + tokens]: routed slots, then one shared slot a token
+  float* route_weights;      // [tokens][k]
+  // experts: the shared expert is expert `experts` of the weights
+  const uint8_t* gate;
+  const uint8_t* up;
+  const uint8_t* down;
+  long long gate_bytes, down_bytes;  // one expert's bytes
+  float* gated;              // [slots][ffn]
+  float* out;                // [slots][hidden]
+  const float* shared_router;
+  float* residual;           // [tokens][hidden], updated
+  const float* norm_weight;
+  float* normed;             // the next norm's output (may be x)
+  uint8_t* records;          // its records (may be x_records)
+  float epsilon, weight_offset;
+  int tokens, experts, k, hidden, ffn;
+  int* error;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(MOE_THREADS) moe_decode_kernel(const __grid_constant__ MoeArgs a) {
+  pdl_trigger();  // the next kernel may launch and wait for this one
+  pdl_wait();     // what the kernels before this one wrote is visible
+  extern __shared__ __align__(16) uint8_t x_slots[];  // the down products' x
+  __shared__ float partial[32];
+  const unsigned G = gridDim.x;
+  const int slots = a.tokens * a.k + a.tokens;
+  // 1. the router's logits (matvec_f32_kernel: a (vector, row) a unit)
+  for (int u = blockIdx.x; u < a.tokens * a.experts; u += G) {
+    const int row = u % a.experts, vector = u / a.experts;
+    const float total = f32_row_dot<false>(a.x, a.router, a.router + (long long)row * a.hidden,
+                                           vector, a.hidden, partial);
+    if (threadIdx.x == 0) a.logits[(long long)vector * a.experts + row] = total;
+  }
+  if (!moe_grid_barrier(G, a.error)) return;
+  // 2. the top-k of each token (route_kernel: a warp a token)
+  {
+    const int t = blockIdx.x * (MOE_THREADS / WARP) + threadIdx.x / WARP;
+    if (t < a.tokens) {
+      route_token(a.logits, a.ids, a.route_weights, t, a.experts, a.k);
+      // the token's shared slot: the shared expert, expert `experts`
+      if (threadIdx.x % WARP == 0) a.ids[a.tokens * a.k + t] = a.experts;
+    }
+  }
+  if (!moe_grid_barrier(G, a.error)) return;
+  // 3. gate/up of every slot, the shared ones last (experts_x22_kernel, gated)
+  {
+    const int blocks = a.hidden / 32;
+    const int ks = blocks >= 128 ? 4 : (blocks >= 64 ? 2 : 1);
+    const int per_cta = 4 * (8 / ks);
+    const int tiles = (a.ffn + per_cta - 1) / per_cta;
+    for (int u = blockIdx.x; u < tiles * slots; u += G) {
+      const int tile = u % tiles, slot = u / tiles;
+#define DRIFT_MOE_GATE(KS)                                                                          experts_unit<T, KS, true, false>(a.gate, a.up, a.gate_bytes, a.ids, a.x_records, a.k,                                           a.tokens * a.k, a.gated, a.ffn, a.hidden, a.experts + 1, 0,                                     0, a.error, nullptr, tile, slot, x_slots)
+      if (ks == 4) DRIFT_MOE_GATE(4);
+      else if (ks == 2) DRIFT_MOE_GATE(2);
+      else DRIFT_MOE_GATE(1);
+#undef DRIFT_MOE_GATE
+      __syncthreads();  // the unit's shared memory is the next unit's
+    }
+  }
+  if (!moe_grid_barrier(G, a.error)) return;
+  // 4. down of every slot (experts_x22_kernel, x prepared in the CTA)
+  {
+    const int blocks = a.ffn / 32;
+    const int ks = blocks >= 128 ? 4 : (blocks >= 64 ? 2 : 1);
+    const int per_cta = 4 * (8 / ks);
+    const int tiles = (a.hidden + per_cta - 1) / per_cta;
+    for (int u = blockIdx.x; u < tiles * slots; u += G) {
+      const int tile = u % tiles, slot = u / tiles;
+#define DRIFT_MOE_DOWN(KS)                                                                            experts_unit<T, KS, false, true>(a.down, a.down, a.down_bytes, a.ids, nullptr, 1, slots, a.out,                                    a.hidden, a.ffn, a.experts + 1, 0, 0, a.error, a.gated, tile,                                     slot, x_slots)
+      if (ks == 4) DRIFT_MOE_DOWN(4);
+      else if (ks == 2) DRIFT_MOE_DOWN(2);
+      else DRIFT_MOE_DOWN(1);
+#undef DRIFT_MOE_DOWN
+      __syncthreads();
+    }
+  }
+  if (!moe_grid_barrier(G, a.error)) return;
+  // 5. the combine with the residual and the next norm (combine_kernel)
+  for (int t = blockIdx.x; t < a.tokens; t += G) {
+    moe_combine_norm_token(a.out, a.route_weights, a.out + (long long)a.tokens * a.k * a.hidden,
+                           a.x, a.shared_router, a.residual, a.k, a.hidden, a.norm_weight,
+                           a.normed, a.epsilon, a.weight_offset, a.records, t);
+    __syncthreads();
+  }
+}
+
+DRIFT_REGISTER(moe_decode_q8_0, moe_decode_kernel<Q8_0T>)
+DRIFT_REGISTER(moe_decode_q4_0, moe_decode_kernel<Q4_0T>)
+DRIFT_REGISTER(moe_decode_q4_1, moe_decode_kernel<Q4_1T>)
+
 template <bool NORM>
 static int launch_combine(const float* expert_out, const float* weights, int64_t tokens, int64_t k,
                           int64_t hidden, const float* shared_out, const float* shared_input,
@@ -560,6 +811,84 @@ int drift_moe_combine_norm(const float* expert_out, const float* weights, int64_
   return launch_combine<true>(expert_out, weights, tokens, k, hidden, shared_out, shared_input,
                               shared_router, residual, residual, norm_weight, normed, epsilon,
                               weight_offset, cudaStream_t(stream));
+}
+
+int drift_moe_decode(int weight_dtype, const float* x, const void* x_prepared, const float* router,
+                     float* logits, int32_t* ids, float* route_weights, const void* gate,
+                     const void* up, const void* down, float* gated, float* out,
+                     const float* shared_router, float* residual, const float* norm_weight,
+                     float epsilon, float weight_offset, float* normed, void* prepared,
+                     int64_t tokens, int64_t experts, int64_t k, int64_t hidden, int64_t ffn,
+                     drift_stream_t stream) {
+  if (weight_dtype != DRIFT_Q8_0 && weight_dtype != DRIFT_Q4_0 && weight_dtype != DRIFT_Q4_1)
+    return invalid("no kernels for %s experts yet", dtype_name(weight_dtype));
+  if (tokens < 0 || experts < 1 || experts > 512 || k < 1 || k > 16 || k > experts)
+    return invalid("moe: top-%lld of %lld experts", (long long)k, (long long)experts);
+  if (hidden <= 0 || hidden > 2 * COMBINE_THREADS || hidden % 32 != 0 || ffn <= 0 ||
+      ffn % 32 != 0 || ffn / 32 > 128)
+    return invalid("moe: hidden %lld (whole blocks, at most %d), expert rows of %lld (at most 4096)",
+                   (long long)hidden, 2 * COMBINE_THREADS, (long long)ffn);
+  const int64_t gate_row = byte_size(weight_dtype, hidden), down_row = byte_size(weight_dtype, ffn);
+  if (gate_row % 4 != 0 || down_row % 4 != 0)
+    return invalid("%s rows are not whole words", dtype_name(weight_dtype));
+  if (tokens == 0) return 0;
+  if (tokens * (k + 1) > 65535) return invalid("moe: %lld slots", (long long)(tokens * (k + 1)));
+  if (!x || !x_prepared || !router || !logits || !ids || !route_weights || !gate || !up ||
+      !down || !gated || !out || !shared_router || !residual || !norm_weight || !normed)
+    return invalid("moe: a null tensor");
+  MoeArgs a = {};
+  a.x = x;
+  a.x_records = static_cast<const uint8_t*>(x_prepared);
+  a.router = router;
+  a.logits = logits;
+  a.ids = ids;
+  a.route_weights = route_weights;
+  a.gate = static_cast<const uint8_t*>(gate);
+  a.up = static_cast<const uint8_t*>(up);
+  a.down = static_cast<const uint8_t*>(down);
+  a.gate_bytes = ffn * gate_row;
+  a.down_bytes = hidden * down_row;
+  a.gated = gated;
+  a.out = out;
+  a.shared_router = shared_router;
+  a.residual = residual;
+  a.norm_weight = norm_weight;
+  a.normed = normed;
+  a.records = static_cast<uint8_t*>(prepared);
+  a.epsilon = epsilon;
+  a.weight_offset = weight_offset;
+  a.tokens = int(tokens);
+  a.experts = int(experts);
+  a.k = int(k);
+  a.hidden = int(hidden);
+  a.ffn = int(ffn);
+  a.error = device_error_word();
+  const size_t smem = size_t(ffn / 32) * MMA_SLOT_BYTES;  // the down products' x
+  // every CTA resident at once (the grid barriers wait on all of them): the
+  // occupancy's count, launched cooperatively
+  auto launch = [&](auto kernel) -> int {
+    int per_sm = 0;
+    DRIFT_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, MOE_THREADS, smem));
+    if (per_sm < 1) return invalid("moe: the launch does not fit an SM");
+    cudaLaunchConfig_t config = {};
+    config.gridDim = dim3(unsigned(per_sm * sm_count()));
+    config.blockDim = dim3(MOE_THREADS);
+    config.dynamicSmemBytes = smem;
+    config.stream = cudaStream_t(stream);
+    cudaLaunchAttribute attribute[1];
+    attribute[0].id = cudaLaunchAttributeCooperative;
+    attribute[0].val.cooperative = 1;
+    config.attrs = attribute;
+    config.numAttrs = 1;
+    DRIFT_CUDA(cudaLaunchKernelEx(&config, kernel, a));
+    DRIFT_LAUNCHED("moe_decode");
+    return 0;
+  };
+  switch (weight_dtype) {
+    case DRIFT_Q8_0: return launch(moe_decode_kernel<Q8_0T>);
+    case DRIFT_Q4_0: return launch(moe_decode_kernel<Q4_0T>);
+    default: return launch(moe_decode_kernel<Q4_1T>);
+  }
 }
 
 int drift_moe_combine_norm_prepared(const float* expert_out, const float* weights, int64_t tokens,

@@ -1,6 +1,7 @@
-// Row-wise device helpers shared by the layer kernels (layers.cu) and the
-// fused attention inputs (attention.cu): the same arithmetic in both, so a
-// fused kernel gives the bits of the kernels it replaces.
+// Row-wise device helpers shared by the layer kernels (layers.cu), the
+// attention inputs (attention.cu) and the whole-mixture launch (experts.cu):
+// the same arithmetic everywhere, so a fused kernel gives the bits of the
+// kernels it replaces.
 #pragma once
 
 #include "common.cuh"
@@ -20,6 +21,53 @@ __device__ __forceinline__ float block_sum(float value, float* partial) {
   for (int w = 0; w < warps; ++w) total += partial[w];
   __syncthreads();  // partial is reused by the next reduction
   return total;
+}
+
+// ---- products with F32 weights -------------------------------------------------------------
+// (routers, DeltaNet's a and b; matvec_f32_kernel in layers.cu, and the
+// whole-mixture launch in experts.cu): a CTA of 256 threads per (row,
+// vector), the row in 16-byte loads, every load of a thread issued before
+// its first use (a 4096-value row is one round trip), summed per thread in
+// column order, then the block's fixed tree. `weight` is the matrix's first
+// row (whose alignment picks the path, so a row sums the same way in either
+// kernel), w the row's.
+template <bool BF16>
+__device__ __forceinline__ float f32_row_dot(const void* __restrict__ x,
+                                             const float* __restrict__ weight,
+                                             const float* __restrict__ w, int vector, int k,
+                                             float* partial) {
+  float sum = 0.0f;
+  if (!BF16 && k % 4 == 0 && (reinterpret_cast<uintptr_t>(weight) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+    const float4* x4 = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) +
+                                                       (long long)vector * k);
+    const int quads = k / 4;
+    for (int base = 0; base < quads; base += 4 * 256) {
+      float4 wv[4], xv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int q = base + u * 256 + threadIdx.x;
+        wv[u] = q < quads ? __ldg(w4 + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+        xv[u] = q < quads ? x4[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        sum = fmaf(wv[u].x, xv[u].x, sum);
+        sum = fmaf(wv[u].y, xv[u].y, sum);
+        sum = fmaf(wv[u].z, xv[u].z, sum);
+        sum = fmaf(wv[u].w, xv[u].w, sum);
+      }
+    }
+  } else {
+    for (int c = threadIdx.x; c < k; c += 256) {
+      const float xv =
+          BF16 ? __uint_as_float(uint32_t(reinterpret_cast<const uint16_t*>(x)[(long long)vector * k + c]) << 16)
+               : reinterpret_cast<const float*>(x)[(long long)vector * k + c];
+      sum = fmaf(w[c], xv, sum);
+    }
+  }
+  return block_sum(sum, partial);
 }
 
 // ---- activations ----------------------------------------------------------------------------

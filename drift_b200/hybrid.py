@@ -427,6 +427,14 @@ class HybridDecoder:
         # (name, CUDA event) after each op group of an eager step, when a
         # profiler sets it to a list
         self.marks: Optional[list] = None
+        # one GPU: the mixture in one launch (drift_moe_decode) rather than
+        # the router, top-k, experts and combine launches -- the same bits.
+        # Off for the captured step: its four grid barriers cost more than
+        # the four launches they replace (C5 batch 1: 4019 against 3181 us a
+        # step), which a graph replays with programmatic dependent launch;
+        # for a host launching every op itself the one launch saves four
+        # launches' host time
+        self.whole_mixture = False
 
     def _mark(self, name: str) -> None:
         if self.marks is not None:
@@ -492,13 +500,23 @@ class HybridDecoder:
 
     def _mixture(self, mixture: MixtureLayer, following: torch.Tensor) -> None:
         ops, c, P = self.ops, self.config, self.prepared
+        next_norm = RowNorm(following, c.epsilon, 0.0, self.normed)
+        if self.exchange is None and mixture.fused is not None and self.whole_mixture:
+            # the router, the top-k, the experts' SwiGLU and down products
+            # (the shared expert as the last expert) and the combine with
+            # the residual and the next norm: one launch
+            gate, up, down = mixture.fused
+            ops.moe_decode(self.normed, P, mixture.router, self.logits_router, self.all_ids,
+                           self.route_weights, gate, up, down, self.all_gated, self.all_out,
+                           mixture.shared_router, self.x, next_norm, P)
+            self._mark("moe")
+            return
         # routing is the same on every rank (the same x, the same router);
         # the post norm wrote normed's records into P for the router and the
         # gate and up products (the weights hold every expert from 0 on)
         ops.route_linear(self.normed, mixture.router, self.logits_router, self.route_ids,
                          self.route_weights, P)
         self._mark("route")
-        next_norm = RowNorm(following, c.epsilon, 0.0, self.normed)
         if self.exchange is None and mixture.fused is not None:
             # routed and shared experts in one launch each: gate/up (the
             # shared slots last, one per sequence), then down

@@ -684,6 +684,40 @@ class CudaOps:
                 _ptr(prepared), int(shared_tail), self._stream())
         check("drift_experts_gated_linear", status)
 
+    def moe_decode(self, x, x_prepared, router, logits, ids, route_weights, gate: Stored,
+                   up: Stored, down: Stored, gated, out, shared_router, residual, norm: RowNorm,
+                   prepared: Optional[torch.Tensor] = None) -> None:
+        """The mixture of a decode step in one launch (route_linear,
+        experts_gated_linear with the shared tail, experts_linear and
+        moe_combine_norm): x [b, H] with its records; router F32 [E, H];
+        gate/up [E + 1, F, H] and down [E + 1, H, F] with the shared expert
+        last; ids [b k + b], route_weights [b, k], gated [b k + b, F], out
+        [b k + b, H]; residual updated and norm.out (its records into
+        `prepared`) written last."""
+        _f32("moe", x, router, logits, route_weights, gated, out, shared_router, residual,
+             norm.weight, norm.out)
+        tokens, hidden = x.shape
+        experts = router.shape[0]
+        k = route_weights.shape[-1]
+        ffn = gate.shape[1]
+        _require(tuple(gate.shape) == (experts + 1, ffn, hidden) and tuple(up.shape) == tuple(gate.shape)
+                 and tuple(down.shape) == (experts + 1, hidden, ffn)
+                 and gate.dtype == up.dtype == down.dtype,
+                 f"moe: weights {list(gate.shape)}, {list(up.shape)}, {list(down.shape)} for "
+                 f"{experts} experts and a shared one")
+        _require(ids.dtype == torch.int32 and ids.numel() == tokens * k + tokens
+                 and tuple(gated.shape) == (tokens * k + tokens, ffn)
+                 and tuple(out.shape) == (tokens * k + tokens, hidden)
+                 and tuple(logits.shape) == (tokens, experts),
+                 "moe: slot buffers")
+        status = self.lib.drift_moe_decode(
+            gate.dtype, _ptr(x), _ptr(x_prepared), _ptr(router), _ptr(logits), _ptr(ids),
+            _ptr(route_weights), _ptr(gate.data), _ptr(up.data), _ptr(down.data), _ptr(gated),
+            _ptr(out), _ptr(shared_router), _ptr(residual), _ptr(norm.weight), norm.epsilon,
+            norm.weight_offset, _ptr(norm.out), _ptr(prepared), tokens, experts, k, hidden, ffn,
+            self._stream())
+        check("drift_moe_decode", status)
+
     @staticmethod
     def _check_combine(expert_out, weights, shared, residual, out):
         _f32("moeCombine", expert_out, weights, out)

@@ -322,6 +322,29 @@ size_t drift_prepared_x_bytes(int64_t m, int64_t k);
 int drift_add_rms_norm_prepared(float* x, const float* y, const float* weight, float epsilon,
                                 float weight_offset, float* out, int64_t rows, int64_t cols,
                                 void* prepared, drift_stream_t stream);
+/* A mixture's whole decode step in one launch (new; the reference's
+ * route + expertsGatedLinear + expertsLinear + moeCombineNorm of
+ * models/HybridBlocks.scala, its GPU `moe_group*` kernels,
+ * runner/kernels/matvec.hip:1816-1933): logits = x . router^T (F32 router
+ * [experts][hidden]), the top-k into ids [tokens][k] and route_weights, the
+ * routed and shared experts' SwiGLU (gate, up: [experts + 1][ffn][hidden],
+ * the shared expert last; x's records in x_prepared) into gated [tokens k +
+ * tokens][ffn], their down products (down [experts + 1][hidden][ffn]) into out
+ * [tokens k + tokens][hidden], and the combine with the shared expert's
+ * sigmoid(x . shared_router) gate into residual [tokens][hidden], then
+ * rmsNorm(residual) into normed and its records into prepared (either may be
+ * x / x_prepared: they are written last). ids gets tokens k + tokens entries,
+ * the shared slots `experts`. The bits of the five separate calls. A
+ * cooperative launch of as many CTAs as the device holds at once, its
+ * phases separated by grid barriers (each wait bounded: device error 2).
+ * hidden <= 2048, whole 32-value blocks; ffn <= 4096; k <= 16; experts <= 512. */
+int drift_moe_decode(int weight_dtype, const float* x, const void* x_prepared, const float* router,
+                     float* logits, int32_t* ids, float* route_weights, const void* gate,
+                     const void* up, const void* down, float* gated, float* out,
+                     const float* shared_router, float* residual, const float* norm_weight,
+                     float epsilon, float weight_offset, float* normed, void* prepared,
+                     int64_t tokens, int64_t experts, int64_t k, int64_t hidden, int64_t ffn,
+                     drift_stream_t stream);
 /* drift_moe_combine_norm (hidden a multiple of 32), also writing normed's
  * records: the next layer's input, as the reference's moe_combine_norm feeds
  * the next layer's products (norm.hip:43-59). */

@@ -51,7 +51,7 @@ def check(ops, dtype, blocks, n, k, m, bf16, seed):
 def test_golden_blocks_as_weights(ops, golden_dir, name, m):
     """The reference's 16 fixture super-blocks as a [4, 1024] weight."""
     fixture = read_safetensors(os.path.join(golden_dir, "quants", f"{name}.safetensors"))
-    blocks = fixture["blocks"].reshape(-1)
+    blocks = fixture["blocks"].reshape(-1).copy()
     # scales drawn ~ N(0, 0.05) by the recipe: products of 1024 values stay
     # finite; the all-ones block's f16 fields are NaN-free by construction
     check(ops, TYPES[name], blocks, 4, 1024, m, False, m)
