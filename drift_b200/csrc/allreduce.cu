@@ -55,7 +55,8 @@ struct Comm {
   size_t send_offset(int s) const { return s * slot_bytes; }
   size_t lane_offset(int s, int p) const { return 2 * slot_bytes + (s * MAX_RANKS + p) * 2 * slot_bytes; }
   size_t counts_offset() const { return 2 * slot_bytes + 2 * MAX_RANKS * 2 * slot_bytes; }
-  size_t total() const { return counts_offset() + MAX_ROWS * 4; }
+  // a call count per (row, CTA of a row's cluster)
+  size_t total() const { return counts_offset() + MAX_ROWS * 8 * 4; }
 };
 
 struct ExchangeArgs {
@@ -198,6 +199,155 @@ __global__ void __launch_bounds__(THREADS) add_rms_norm_allreduce_kernel(
 
 DRIFT_REGISTER(add_rms_norm_allreduce_f32, (add_rms_norm_allreduce_kernel<4, 1024>))
 
+// Rows of more than 1024 values, a cluster of SPLIT CTAs a row: the row's
+// exchange and norm spread over SPLIT SMs instead of one. The rms norm
+// kernel's 1024 threads (PER values each: columns t + 1024 i) are dealt out
+// 128 to a CTA -- CTA j holds threads [128 j, 128 j + 128) -- so each
+// thread's sum of squares and each warp's shuffle tree are that kernel's;
+// the 32 warp sums meet through distributed shared memory and are added in
+// warp order on every CTA: the bits of the one-CTA kernel (and of
+// add_rms_norm). Each CTA pushes and polls its own columns with its own call
+// count. A wait that runs out in any CTA leaves the whole row as it was:
+// the CTAs' outcomes meet at the same cluster barrier as the sums, which
+// every CTA reaches.
+constexpr int SPLIT = 8, SPLIT_THREADS = 1024 / SPLIT;
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+__device__ __forceinline__ float cluster_load(const float* local, unsigned rank) {
+  uint32_t address = static_cast<uint32_t>(__cvta_generic_to_shared(local)), remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(address), "r"(rank));
+  float value;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(value) : "r"(remote) : "memory");
+  return value;
+}
+
+template <int PER>
+__global__ void __launch_bounds__(SPLIT_THREADS) add_rms_norm_allreduce_cluster_kernel(
+    const __grid_constant__ ExchangeArgs e, float* __restrict__ x, const float* __restrict__ weight,
+    float* __restrict__ out, int cols, float epsilon, float weight_offset,
+    uint8_t* __restrict__ records) {
+  pdl_trigger();  // the next kernel may launch and wait for this one
+  pdl_wait();     // this rank's partials (the product before) are written
+  constexpr int BIG = SPLIT * SPLIT_THREADS;  // the one-CTA kernel's threads
+  __shared__ float sums[SPLIT_THREADS / 32];  // this CTA's four warp sums
+  __shared__ float failed;                    // 1 when a wait ran out here
+  __shared__ unsigned call;
+  unsigned j;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(j));
+  const int row_index = blockIdx.x / SPLIT;
+  const int t = int(j) * SPLIT_THREADS + threadIdx.x;  // the one-CTA kernel's thread
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  if (threadIdx.x == 0) {
+    unsigned* counter = e.counts + row_index * SPLIT + j;
+    call = *counter + 1;
+    *counter = call;
+    failed = 0.0f;
+  }
+  __syncthreads();
+  const unsigned long long count = (unsigned long long)call << 32;
+  static_assert(MAX_RANKS * PER <= 32, "a thread's words fit one bit mask");
+  {
+    const float* mine = e.send + (long long)row_index * cols;
+    unsigned long long own[PER];
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int c = t + i * BIG;
+      own[i] = count | (c < cols ? __float_as_uint(mine[c]) : 0u);
+    }
+    for (int p = 0; p < e.world; ++p) {
+      unsigned long long* to = e.pushes[p] + (long long)row_index * cols;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const int c = t + i * BIG;
+        if (c < cols) store_relaxed_sys(to + c, own[i]);
+      }
+    }
+  }
+  float part[MAX_RANKS][PER];
+  unsigned pending = 0;
+#pragma unroll
+  for (int p = 0; p < MAX_RANKS; ++p)
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      part[p][i] = 0.0f;
+      if (p < e.world && t + i * BIG < cols) pending |= 1u << (p * PER + i);
+    }
+  const uint64_t start = tc::global_ns();
+  while (pending) {
+#pragma unroll
+    for (int p = 0; p < MAX_RANKS; ++p) {
+      if (p >= e.world) break;
+      const unsigned long long* lane_words = e.lanes + p * e.lane_words + (long long)row_index * cols;
+      unsigned long long w[PER];
+#pragma unroll
+      for (int i = 0; i < PER; ++i)
+        w[i] = (pending >> (p * PER + i)) & 1u ? load_relaxed_sys(lane_words + t + i * BIG) : 0ull;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const unsigned bit = 1u << (p * PER + i);
+        if ((pending & bit) && unsigned(w[i] >> 32) == call) {
+          part[p][i] = __uint_as_float(unsigned(w[i]));
+          pending &= ~bit;
+        }
+      }
+    }
+    if (!pending) break;
+    if (tc::global_ns() - start > e.wait_ns) {
+      atomicCAS(e.error, 0, 3);
+      failed = 1.0f;
+      break;
+    }
+    __nanosleep(64);
+  }
+  float* row = x + (long long)row_index * cols;
+  float value[PER], w[PER], sum[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int c = t + i * BIG;
+    value[i] = c < cols ? row[c] : 0.0f;
+    w[i] = c < cols ? weight[c] : 0.0f;
+    sum[i] = 0.0f;
+  }
+#pragma unroll
+  for (int p = 0; p < MAX_RANKS; ++p)
+    if (p < e.world) {
+#pragma unroll
+      for (int i = 0; i < PER; ++i) sum[i] += part[p][i];
+    }
+  float squares = 0.0f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    value[i] = value[i] + sum[i];
+    squares = fmaf(value[i], value[i], squares);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o /= 2) squares += __shfl_xor_sync(0xffffffffu, squares, o);
+  if (lane == 0) sums[warp] = squares;
+  __syncthreads();
+  cluster_sync();  // every CTA's warp sums and outcome are in
+  float total = 0.0f, any_failed = 0.0f;
+  for (int w32 = 0; w32 < BIG / 32; ++w32)
+    total += cluster_load(&sums[w32 % (SPLIT_THREADS / 32)], unsigned(w32 / (SPLIT_THREADS / 32)));
+  for (unsigned r = 0; r < SPLIT; ++r) any_failed += cluster_load(&failed, r);
+  cluster_sync();  // every CTA has read the others' before any leaves
+  if (any_failed != 0.0f) return;
+  const float scale = 1.0f / sqrtf(total / float(cols) + epsilon);
+  float* target = out + (long long)row_index * cols;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int c = t + i * BIG;
+    if (c < cols) row[c] = value[i];
+    const float normed = value[i] * scale * (w[i] + weight_offset);
+    if (c < cols) target[c] = normed;
+    if (records && c < cols) x22_record_block(normed, records, row_index, c / 32, cols / 32);
+  }
+}
+
+DRIFT_REGISTER(add_rms_norm_allreduce_cluster_f32, (add_rms_norm_allreduce_cluster_kernel<4>))
+
 }  // namespace
 }  // namespace drift
 
@@ -302,6 +452,31 @@ int drift_add_rms_norm_allreduce(void* comm, int slot, float* x, const float* we
   const cudaStream_t s = cudaStream_t(stream);
   const unsigned grid = unsigned(rows);
   const int n = int(cols);
+  // rows of more than 1024 values: a cluster of SPLIT CTAs a row, the
+  // threads of launch_rms_norm's 1024-thread shape dealt out among them
+  if (cols > 1024) {
+    cudaLaunchConfig_t config = {};
+    config.gridDim = dim3(grid * SPLIT);
+    config.blockDim = dim3(SPLIT_THREADS);
+    config.stream = s;
+    cudaLaunchAttribute attribute[2];
+    attribute[0].id = cudaLaunchAttributeClusterDimension;
+    attribute[0].val.clusterDim.x = SPLIT;
+    attribute[0].val.clusterDim.y = 1;
+    attribute[0].val.clusterDim.z = 1;
+    attribute[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attribute[1].val.programmaticStreamSerializationAllowed = 1;
+    config.attrs = attribute;
+    config.numAttrs = 2;
+    if (cols <= 2048)
+      DRIFT_CUDA(cudaLaunchKernelEx(&config, add_rms_norm_allreduce_cluster_kernel<2>, e, x, weight,
+                                    out, n, epsilon, weight_offset, records));
+    else
+      DRIFT_CUDA(cudaLaunchKernelEx(&config, add_rms_norm_allreduce_cluster_kernel<4>, e, x, weight,
+                                    out, n, epsilon, weight_offset, records));
+    DRIFT_LAUNCHED("add_rms_norm_allreduce");
+    return 0;
+  }
   // the shapes of launch_rms_norm (layers.cu), so the norm's bits are its
 #define DRIFT_EXCHANGE(PER, THREADS)                                                           \
   DRIFT_CUDA(launch_pdl(add_rms_norm_allreduce_kernel<PER, THREADS>, grid, THREADS, 0, s, e, x, \

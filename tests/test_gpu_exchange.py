@@ -116,55 +116,61 @@ def _timeout_ranks(rank: int, world: int, port: int):
     """Rank 1 skips one exchange; rank 0's rows give up after the comm's 10 ms
     limit, device error 3, x and out untouched; both ranks then close the
     comm, and a new one works (the context is still usable)."""
-    import time
-
     dist = _init(rank, world, port)
-    from drift_b200.ops import CudaOps, RowNorm
-    from drift_b200.tensor_parallel import PeerExchange
     try:
-        ops = CudaOps()
-        rows, cols = 4, 1024
-        g = torch.Generator(device="cuda").manual_seed(2)
-        x0 = torch.randn(rows, cols, device="cuda", generator=g)
-        weight = 1 + 0.02 * torch.randn(cols, device="cuda", generator=g)
-        parts = [torch.randn(rows, cols, device="cuda", generator=g) for _ in range(world)]
-        exchange = PeerExchange(ops, dist.group.WORLD, rows, cols, wait_limit_ns=10_000_000)
-        exchange.slots[0].copy_(parts[rank])
-        torch.cuda.synchronize()
-        dist.barrier()
-        assert ops.take_device_error() == 0
-        if rank == 0:
-            x = x0.clone()
-            normed = torch.full_like(x, 7.0)
-            start = time.perf_counter()
-            exchange.add_rms_norm(0, x, RowNorm(weight, 1e-6, 0.0, normed))
-            torch.cuda.synchronize()
-            waited = time.perf_counter() - start
-            assert waited < 2.0, waited
-            assert ops.take_device_error() == 3
-            assert torch.equal(x, x0)
-            assert bool((normed == 7.0).all())
-        torch.cuda.synchronize()
-        dist.barrier()  # rank 0's pushes into rank 1's buffer have ended
-        exchange.close()
-        dist.barrier()
-        # a fresh exchange on the same context sums as before
-        exchange = PeerExchange(ops, dist.group.WORLD, rows, cols)
-        exchange.slots[0].copy_(parts[rank])
-        x = x0.clone()
-        normed = torch.empty_like(x)
-        exchange.add_rms_norm(0, x, RowNorm(weight, 1e-6, 0.0, normed))
-        expected_x = x0.clone()
-        expected = torch.empty_like(x)
-        ops.add_rms_norm(expected_x, parts[0] + parts[1], RowNorm(weight, 1e-6, 0.0, expected))
-        torch.cuda.synchronize()
-        assert torch.equal(x, expected_x)
-        assert torch.equal(normed, expected)
-        assert ops.take_device_error() == 0
-        dist.barrier()
-        exchange.close()
+        # the one-CTA exchange (rows of up to 1024) and the clustered one
+        for cols in (1024, 4096):
+            _timeout_case(rank, world, dist, 4, cols)
     finally:
         dist.destroy_process_group()
+
+
+def _timeout_case(rank, world, dist, rows, cols):
+    """One skipped exchange under a 10 ms limit, then a fresh comm."""
+    import time
+
+    from drift_b200.ops import CudaOps, RowNorm
+    from drift_b200.tensor_parallel import PeerExchange
+    ops = CudaOps()
+    g = torch.Generator(device="cuda").manual_seed(2)
+    x0 = torch.randn(rows, cols, device="cuda", generator=g)
+    weight = 1 + 0.02 * torch.randn(cols, device="cuda", generator=g)
+    parts = [torch.randn(rows, cols, device="cuda", generator=g) for _ in range(world)]
+    exchange = PeerExchange(ops, dist.group.WORLD, rows, cols, wait_limit_ns=10_000_000)
+    exchange.slots[0].copy_(parts[rank])
+    torch.cuda.synchronize()
+    dist.barrier()
+    assert ops.take_device_error() == 0
+    if rank == 0:
+        x = x0.clone()
+        normed = torch.full_like(x, 7.0)
+        start = time.perf_counter()
+        exchange.add_rms_norm(0, x, RowNorm(weight, 1e-6, 0.0, normed))
+        torch.cuda.synchronize()
+        waited = time.perf_counter() - start
+        assert waited < 2.0, waited
+        assert ops.take_device_error() == 3
+        assert torch.equal(x, x0)
+        assert bool((normed == 7.0).all())
+    torch.cuda.synchronize()
+    dist.barrier()  # rank 0's pushes into rank 1's buffer have ended
+    exchange.close()
+    dist.barrier()
+    # a fresh exchange on the same context sums as before
+    exchange = PeerExchange(ops, dist.group.WORLD, rows, cols)
+    exchange.slots[0].copy_(parts[rank])
+    x = x0.clone()
+    normed = torch.empty_like(x)
+    exchange.add_rms_norm(0, x, RowNorm(weight, 1e-6, 0.0, normed))
+    expected_x = x0.clone()
+    expected = torch.empty_like(x)
+    ops.add_rms_norm(expected_x, parts[0] + parts[1], RowNorm(weight, 1e-6, 0.0, expected))
+    torch.cuda.synchronize()
+    assert torch.equal(x, expected_x)
+    assert torch.equal(normed, expected)
+    assert ops.take_device_error() == 0
+    dist.barrier()
+    exchange.close()
 
 
 @needs_two
