@@ -161,6 +161,25 @@ __device__ __forceinline__ void experts_unit(
     }
     return;
   }
+  // the warp's rows side by side: each block of x is read once for all of
+  // them, and every row's weights of the block are in flight together; a
+  // row's sum is its lane's blocks in order, then the warp's lanes. A
+  // lane's first block's weights are asked for before x is prepared (XQ),
+  // so the two waits overlap.
+  const long long row_bytes = (long long)blocks * T::BYTES;
+  const uint8_t* gate_base = gate + expert * expert_bytes;
+  const uint8_t* up_base = up + expert * expert_bytes;
+  uint32_t wg[ROWS][T::WORDS], wu[ROWS][T::WORDS];
+  auto fetch = [&](int c) {
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) {
+      const long long row = row0 + r < rows ? row0 + r : row0;
+      load_block<T>(gate_base + row * row_bytes, c, wg[r]);
+      if (GATED) load_block<T>(up_base + row * row_bytes, c, wu[r]);
+    }
+  };
+  const int c0 = kw * WARP + lane;
+  if (c0 < blocks) fetch(c0);
   if constexpr (XQ) {
     for (int c = warp; c < blocks; c += 8)
       x22_record_slot(x[(long long)v * cols + 32 * c + lane], x_slots + c * MMA_SLOT_BYTES);
@@ -170,23 +189,11 @@ __device__ __forceinline__ void experts_unit(
     if constexpr (XQ) return *a;
     else return __ldg(a);
   };
-  // the warp's rows side by side: each block of x is read once for all of
-  // them, and every row's weights of the block are in flight together; a
-  // row's sum is its lane's blocks in order, then the warp's lanes
   float g[ROWS], u[ROWS];
 #pragma unroll
   for (int r = 0; r < ROWS; ++r) g[r] = u[r] = 0.0f;
-  const long long row_bytes = (long long)blocks * T::BYTES;
-  const uint8_t* gate_base = gate + expert * expert_bytes;
-  const uint8_t* up_base = up + expert * expert_bytes;
-  for (int c = kw * WARP + lane; c < blocks; c += WARP * KS) {
-    uint32_t wg[ROWS][T::WORDS], wu[ROWS][T::WORDS];
-#pragma unroll
-    for (int r = 0; r < ROWS; ++r) {
-      const long long row = row0 + r < rows ? row0 + r : row0;
-      load_block<T>(gate_base + row * row_bytes, c, wg[r]);
-      if (GATED) load_block<T>(up_base + row * row_bytes, c, wu[r]);
-    }
+  for (int c = c0; c < blocks; c += WARP * KS) {
+    if (c != c0) fetch(c);
     const uint4* rec = reinterpret_cast<const uint4*>(record + (long long)c * STRIDE);
     // stored words 0..7 of a plane hold words 0, 4, 1, 5, 2, 6, 3, 7
     uint32_t planes[24];
