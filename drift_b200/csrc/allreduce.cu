@@ -212,17 +212,6 @@ DRIFT_REGISTER(add_rms_norm_allreduce_f32, (add_rms_norm_allreduce_kernel<4, 102
 // every CTA reaches.
 constexpr int SPLIT = 8, SPLIT_THREADS = 1024 / SPLIT;
 
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
-               ::: "memory");
-}
-__device__ __forceinline__ float cluster_load(const float* local, unsigned rank) {
-  uint32_t address = static_cast<uint32_t>(__cvta_generic_to_shared(local)), remote;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(address), "r"(rank));
-  float value;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(value) : "r"(remote) : "memory");
-  return value;
-}
 
 template <int PER>
 __global__ void __launch_bounds__(SPLIT_THREADS) add_rms_norm_allreduce_cluster_kernel(
@@ -346,7 +335,7 @@ __global__ void __launch_bounds__(SPLIT_THREADS) add_rms_norm_allreduce_cluster_
   }
 }
 
-DRIFT_REGISTER(add_rms_norm_allreduce_cluster_f32, (add_rms_norm_allreduce_cluster_kernel<4>))
+// (not in the by-name table: it runs only as a cluster launch)
 
 }  // namespace
 }  // namespace drift

@@ -23,6 +23,27 @@ __device__ __forceinline__ float block_sum(float value, float* partial) {
   return total;
 }
 
+// ---- thread-block clusters ------------------------------------------------------------
+// Every CTA of the cluster past this point sees the others' shared memory
+// writes from before it.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+// `local`'s float in the shared memory of the cluster's CTA `rank`.
+__device__ __forceinline__ float cluster_load(const float* local, unsigned rank) {
+  uint32_t address = static_cast<uint32_t>(__cvta_generic_to_shared(local)), remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(address), "r"(rank));
+  float value;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(value) : "r"(remote) : "memory");
+  return value;
+}
+__device__ __forceinline__ unsigned cluster_rank() {
+  unsigned rank;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+  return rank;
+}
+
 // ---- products with F32 weights -------------------------------------------------------------
 // (routers, DeltaNet's a and b; matvec_f32_kernel in layers.cu, and the
 // whole-mixture launch in experts.cu): a CTA of 256 threads per (row,
