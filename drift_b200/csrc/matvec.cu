@@ -248,9 +248,10 @@ int matvec_ring(int weight_dtype, const void* weight, const uint8_t* records, fl
 int matvec_prepared(int weight_dtype, const void* weight, const uint8_t* records, float* y,
                     int64_t rows, int64_t cols, int64_t vectors, cudaStream_t stream) {
   if (ring_supports(weight_dtype, weight, cols)) {
+    // up to 16 vectors a launch (two passes' records met by each weight fragment)
     const int64_t blocks = cols / 32;
-    for (int64_t first = 0; first < vectors; first += 8) {
-      const int64_t count = vectors - first < 8 ? vectors - first : 8;
+    for (int64_t first = 0; first < vectors; first += 16) {
+      const int64_t count = vectors - first < 16 ? vectors - first : 16;
       DRIFT_TRY(matvec_ring(weight_dtype, weight, records + (first / 8) * blocks * MMA_RECORD_BYTES,
                             y + first * rows, rows, cols, count, stream));
     }

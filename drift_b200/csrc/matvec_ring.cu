@@ -40,10 +40,18 @@ namespace {
 
 constexpr int SEG_BLOCKS = 8;
 // Every tile is 64 rows: two rows per lane in the dp4a modes, four 16-row MMA
-// tiles in the MMA mode, so all modes share one schedule -- and one order of
+// tiles in the MMA modes, so all modes share one schedule -- and one order of
 // summation -- per matrix.
 constexpr int ROWS = 64;
-constexpr int MODE_DP4A_1 = 1, MODE_DP4A_2 = 2, MODE_MMA = 8;
+// 1 or 2 vectors (dp4a), 3-8 vectors (MMA, one pass of x records) and 9-16
+// vectors (MMA16: two passes' records met by each weight fragment, so the
+// weights stream once for 16 vectors)
+constexpr int MODE_DP4A_1 = 1, MODE_DP4A_2 = 2, MODE_MMA = 8, MODE_MMA16 = 16;
+__host__ __device__ constexpr bool mma_mode(int mode) { return mode >= MODE_MMA; }
+// 8-vector passes of x records a mode reads at once
+__host__ __device__ constexpr int mode_passes(int mode) { return mode == MODE_MMA16 ? 2 : 1; }
+// output slots per row of a tile (a pass's 8 in the MMA modes)
+__host__ __device__ constexpr int mode_slots(int mode) { return mma_mode(mode) ? 8 * mode_passes(mode) : mode; }
 
 template <typename T>
 struct Ring {
@@ -57,6 +65,8 @@ struct Ring {
   static constexpr int STAGE = ROWS * PITCH;
 };
 
+constexpr int MAX_SMEM = 232448;
+
 // Warps per CTA and stages per warp, by type: about 180-210 KB of ring.
 template <typename T>
 struct RingShape {
@@ -65,10 +75,15 @@ struct RingShape {
   static constexpr int BARS = WARPS * S * Ring<T>::STAGE;
   static constexpr int X_OFFSET = BARS + WARPS * S * 8 + 16;  // x staged for the dp4a modes
   static constexpr int BYTES = X_OFFSET + 1024;  // + room to align to 1024; + x when staged
-  // the MMA mode keeps a tile's chain of group sums here, not in registers
-  static constexpr int CHAIN_BYTES = WARPS * 16 * WARP * 4;
+  // the MMA modes keep a tile's chain of group sums here, not in registers
+  // (16 floats a lane a pass)
+  static constexpr int chain_bytes(int mode) {
+    return mma_mode(mode) ? WARPS * 16 * mode_passes(mode) * WARP * 4 : 0;
+  }
+  // whether the MMA16 chain fits beside the ring (Q4_0, Q4_1; Q8_0's larger
+  // ring leaves it two 8-vector passes)
+  static constexpr bool MMA16 = BYTES + chain_bytes(MODE_MMA16) <= MAX_SMEM;
 };
-constexpr int MAX_SMEM = 232448;
 
 // One vector's x for one block, as the dp4a modes use it.
 struct XBlock {
@@ -179,23 +194,29 @@ __device__ __forceinline__ void segment_dp4a(const uint8_t* stage, int first_blo
     segment_dp4a_blocks<T, V, SRC, STRIDE, false>(row0, row1, rec0, count, acc);
 }
 
-// ---- MMA mode: 3-8 vectors -------------------------------------------------------------------
-// acc[i][.] gains the segment's blocks for rows (16 i + g, 16 i + g + 8) and
-// vectors (2t, 2t + 1), each as acc = fmaf(s, value, acc); x is fetched one
-// block ahead.
-template <typename T, bool FULL>
+// ---- MMA modes: 3-16 vectors ----------------------------------------------------------------
+// acc[i][4 p + .] gains the segment's blocks for rows (16 i + g, 16 i + g + 8)
+// and vectors (8 p + 2t, 8 p + 2t + 1) of pass p (P passes, their records
+// `pass_bytes` apart), each as acc = fmaf(s, value, acc); a row's weight
+// fragment is unpacked once for every pass, and x is fetched one block ahead.
+// A vector's arithmetic is the same in either mode, so 16 vectors give the
+// bits of two 8-vector passes.
+template <typename T, int P, bool FULL>
 __device__ __forceinline__ void segment_mma_blocks(const uint8_t* row_g, const uint8_t* rec0,
-                                                   int count, bool have_vector,
-                                                   float (&acc)[4][4]) {
-  const int t = threadIdx.x % 4;
-  XFragment x[2];
-  load_fragment<T>(rec0, have_vector, x[0]);
+                                                   long long pass_bytes, int count, int vectors,
+                                                   float (&acc)[4][4 * P]) {
+  const int lane = threadIdx.x % WARP, g = lane / 4, t = lane % 4;
+  XFragment x[2][P];
+#pragma unroll
+  for (int p = 0; p < P; ++p) load_fragment<T>(rec0 + p * pass_bytes, g + 8 * p < vectors, x[0][p]);
 #pragma unroll
   for (int b = 0; b < SEG_BLOCKS; ++b) {
     if (FULL || b < count) {
       if (b + 1 < SEG_BLOCKS && (FULL || b + 1 < count))
-        load_fragment<T>(rec0 + (b + 1) * MMA_RECORD_BYTES, have_vector, x[(b + 1) & 1]);
-      const XFragment& xb = x[b & 1];
+#pragma unroll
+        for (int p = 0; p < P; ++p)
+          load_fragment<T>(rec0 + (b + 1) * MMA_RECORD_BYTES + p * pass_bytes, g + 8 * p < vectors,
+                           x[(b + 1) & 1][p]);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         uint32_t lo0, hi0, lo1, hi1;
@@ -203,51 +224,61 @@ __device__ __forceinline__ void segment_mma_blocks(const uint8_t* row_g, const u
         fragment_row<T, SharedWords>(row_g + 16 * i * Ring<T>::PITCH, b, t, lo0, hi0, d0, m0);
         fragment_row<T, SharedWords>(row_g + (16 * i + 8) * Ring<T>::PITCH, b, t, lo1, hi1, d1, m1);
         const uint32_t a[4] = {lo0, lo1, hi0, hi1};
-        int p0[4], p1[4], p2[4];
-        mma_i8_zero<T::SIGNED, false>(p0, a, xb.planes[0].x, xb.planes[0].y);
-        mma_i8_zero<T::SIGNED, false>(p1, a, xb.planes[1].x, xb.planes[1].y);
-        mma_i8_zero<T::SIGNED, true>(p2, a, xb.planes[2].x, xb.planes[2].y);
-        acc[i][0] = fmaf(xb.s.x, mma_block_value<T>(p0[0], p1[0], p2[0], d0, m0, xb.sum.x, xb.fsum.x), acc[i][0]);
-        acc[i][1] = fmaf(xb.s.y, mma_block_value<T>(p0[1], p1[1], p2[1], d0, m0, xb.sum.y, xb.fsum.y), acc[i][1]);
-        acc[i][2] = fmaf(xb.s.x, mma_block_value<T>(p0[2], p1[2], p2[2], d1, m1, xb.sum.x, xb.fsum.x), acc[i][2]);
-        acc[i][3] = fmaf(xb.s.y, mma_block_value<T>(p0[3], p1[3], p2[3], d1, m1, xb.sum.y, xb.fsum.y), acc[i][3]);
+#pragma unroll
+        for (int p = 0; p < P; ++p) {
+          const XFragment& xb = x[b & 1][p];
+          float* out = acc[i] + 4 * p;
+          int p0[4], p1[4], p2[4];
+          mma_i8_zero<T::SIGNED, false>(p0, a, xb.planes[0].x, xb.planes[0].y);
+          mma_i8_zero<T::SIGNED, false>(p1, a, xb.planes[1].x, xb.planes[1].y);
+          mma_i8_zero<T::SIGNED, true>(p2, a, xb.planes[2].x, xb.planes[2].y);
+          out[0] = fmaf(xb.s.x, mma_block_value<T>(p0[0], p1[0], p2[0], d0, m0, xb.sum.x, xb.fsum.x), out[0]);
+          out[1] = fmaf(xb.s.y, mma_block_value<T>(p0[1], p1[1], p2[1], d0, m0, xb.sum.y, xb.fsum.y), out[1]);
+          out[2] = fmaf(xb.s.x, mma_block_value<T>(p0[2], p1[2], p2[2], d1, m1, xb.sum.x, xb.fsum.x), out[2]);
+          out[3] = fmaf(xb.s.y, mma_block_value<T>(p0[3], p1[3], p2[3], d1, m1, xb.sum.y, xb.fsum.y), out[3]);
+        }
       }
     }
   }
 }
 
-template <typename T>
+template <typename T, int P>
 __device__ __forceinline__ void segment_mma(const uint8_t* stage, int first_block, int count,
-                                            const uint8_t* __restrict__ records, int vectors,
-                                            float (&acc)[4][4]) {
+                                            const uint8_t* __restrict__ records, int blocks,
+                                            int vectors, float (&acc)[4][4 * P]) {
   const int lane = threadIdx.x % WARP, g = lane / 4;
   const uint8_t* rec0 = records + (long long)first_block * MMA_RECORD_BYTES;
   const uint8_t* row_g = stage + g * Ring<T>::PITCH;
+  const long long pass_bytes = (long long)blocks * MMA_RECORD_BYTES;
   if (count == SEG_BLOCKS)
-    segment_mma_blocks<T, true>(row_g, rec0, SEG_BLOCKS, g < vectors, acc);
+    segment_mma_blocks<T, P, true>(row_g, rec0, pass_bytes, SEG_BLOCKS, vectors, acc);
   else
-    segment_mma_blocks<T, false>(row_g, rec0, count, g < vectors, acc);
+    segment_mma_blocks<T, P, false>(row_g, rec0, pass_bytes, count, vectors, acc);
 }
 
 // The accumulators of a warp: dp4a modes acc[r][v] for rows lane + 32 r;
-// MMA mode acc[i][e] for the fragment of rows 16 i + g (+8), vectors 2t (+1).
+// MMA modes acc[i][4 p + e] for the fragment of rows 16 i + g (+8), vectors
+// 8 p + 2t (+1) of pass p.
 template <int MODE>
 struct Acc {
-  float a[MODE == MODE_MMA ? 4 : 2][4];
+  static constexpr int I = mma_mode(MODE) ? 4 : 2, E = mma_mode(MODE) ? 4 * mode_passes(MODE) : 4;
+  float a[I][E];
   __device__ void zero() {
 #pragma unroll
-    for (int i = 0; i < (MODE == MODE_MMA ? 4 : 2); ++i) a[i][0] = a[i][1] = a[i][2] = a[i][3] = 0.0f;
+    for (int i = 0; i < I; ++i)
+#pragma unroll
+      for (int e = 0; e < E; ++e) a[i][e] = 0.0f;
   }
-  // the chain in shared memory (MMA mode), lane-major: slot (i, e) of lane l
-  // at chain[(4 i + e) 32 + l]. first: the tile's first group (the chain
+  // the chain in shared memory (MMA modes), lane-major: slot (i, e) of lane l
+  // at chain[(E i + e) 32 + l]. first: the tile's first group (the chain
   // starts as it); returns nothing -- the last group is added by `finish`.
   __device__ void chain_into(float* chain, bool first) const {
     const int lane = threadIdx.x % WARP;
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < I; ++i)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float* c = chain + (4 * i + e) * WARP + lane;
+      for (int e = 0; e < E; ++e) {
+        float* c = chain + (E * i + e) * WARP + lane;
         *c = first ? a[i][e] : *c + a[i][e];
       }
   }
@@ -255,28 +286,30 @@ struct Acc {
   __device__ void finish(const float* chain, bool first) {
     const int lane = threadIdx.x % WARP;
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < I; ++i)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) a[i][e] = first ? a[i][e] : chain[(4 * i + e) * WARP + lane] + a[i][e];
+      for (int e = 0; e < E; ++e) a[i][e] = first ? a[i][e] : chain[(E * i + e) * WARP + lane] + a[i][e];
   }
   __device__ void add(const Acc& o) {
 #pragma unroll
-    for (int i = 0; i < (MODE == MODE_MMA ? 4 : 2); ++i)
+    for (int i = 0; i < I; ++i)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) a[i][e] += o.a[i][e];
+      for (int e = 0; e < E; ++e) a[i][e] += o.a[i][e];
   }
   // call f(row within the tile, vector, value) for each output this lane holds
   template <typename F>
   __device__ void each(F f) const {
     const int lane = threadIdx.x % WARP, g = lane / 4, t = lane % 4;
-    if constexpr (MODE == MODE_MMA) {
+    if constexpr (mma_mode(MODE)) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        f(16 * i + g, 2 * t, a[i][0]);
-        f(16 * i + g, 2 * t + 1, a[i][1]);
-        f(16 * i + g + 8, 2 * t, a[i][2]);
-        f(16 * i + g + 8, 2 * t + 1, a[i][3]);
-      }
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int p = 0; p < mode_passes(MODE); ++p) {
+          f(16 * i + g, 8 * p + 2 * t, a[i][4 * p]);
+          f(16 * i + g, 8 * p + 2 * t + 1, a[i][4 * p + 1]);
+          f(16 * i + g + 8, 8 * p + 2 * t, a[i][4 * p + 2]);
+          f(16 * i + g + 8, 8 * p + 2 * t + 1, a[i][4 * p + 3]);
+        }
     } else {
 #pragma unroll
       for (int r = 0; r < 2; ++r)
@@ -359,7 +392,7 @@ struct Lanes<2> {
 template <int VSLOTS, typename OUT>
 __device__ __forceinline__ void chain_groups(const float* sums, long long stride, int count,
                                              int first, int step, OUT out) {
-  constexpr int N = VSLOTS == 8 ? 4 : 2, E = ROWS * VSLOTS, BATCH = VSLOTS == 2 ? 4 : 8;
+  constexpr int N = VSLOTS >= 8 ? 4 : 2, E = ROWS * VSLOTS, BATCH = VSLOTS == 2 ? 4 : 8;
   using V = typename Lanes<N>::type;
   for (int en = first; en < E / N; en += step) {
     V sum = {};
@@ -427,7 +460,7 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
                        int cols, int vectors, int* error) {
   using Shape = RingShape<T>;
   constexpr int W = Shape::WARPS, S = Shape::S, STAGE = Ring<T>::STAGE;
-  constexpr int VSLOTS = MODE == MODE_MMA ? 8 : MODE;
+  constexpr int VSLOTS = mode_slots(MODE);
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -469,7 +502,7 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
     // While the first copies fly: the vectors' slots of every block's record,
     // 112 V bytes a block, into shared memory, where every row of every tile
     // reads them.
-    static_assert(MODE != MODE_MMA, "the MMA mode reads x from global memory");
+    static_assert(!mma_mode(MODE), "the MMA modes read x from global memory");
     constexpr int SLOT = MMA_SLOT_BYTES * MODE;
     uint8_t* xs = smem + Shape::X_OFFSET;
     for (int i = threadIdx.x; i < blocks * (SLOT / 16); i += blockDim.x) {
@@ -479,7 +512,7 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
     }
     __syncthreads();
     x = xs;
-  } else if constexpr (MODE != MODE_MMA) {
+  } else if constexpr (!mma_mode(MODE)) {
     // x stays in global memory: bring the line or two of each record that the
     // vectors' slots occupy into L1 before the first rows need them.
     constexpr int LINES = MODE == MODE_DP4A_1 ? 1 : 2;
@@ -492,7 +525,7 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
   total.zero();
   const int whole = plan.rounds * segments;
   const Groups& groups = plan.groups;
-  float* chain = reinterpret_cast<float*>(smem + Shape::X_OFFSET) + warp * 16 * WARP;
+  float* chain = reinterpret_cast<float*>(smem + Shape::X_OFFSET) + warp * 16 * mode_passes(MODE) * WARP;
   float* shared_sums = group_partials + (long long)blockIdx.x * W * groups.count * ROWS * VSLOTS;
   while (consumed < issued) {
     const int j = consumed;
@@ -502,8 +535,9 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
     if (ok) {
       const int first = segment * SEG_BLOCKS;
       const int count = blocks - first < SEG_BLOCKS ? blocks - first : SEG_BLOCKS;
-      if constexpr (MODE == MODE_MMA)
-        segment_mma<T>(ring + (j % S) * STAGE, first, count, records, vectors, part.a);
+      if constexpr (mma_mode(MODE))
+        segment_mma<T, mode_passes(MODE)>(ring + (j % S) * STAGE, first, count, records, blocks,
+                                          vectors, part.a);
       else
         segment_dp4a<T, MODE, XSMEM>(ring + (j % S) * STAGE, first, count, x, part.a);
     }
@@ -513,7 +547,7 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
     if (!groups.last(segment)) continue;
     if (j < whole) {
       const bool first_group = groups.in_first(segment);
-      if constexpr (MODE == MODE_MMA) {
+      if constexpr (mma_mode(MODE)) {
         if (segment != segments - 1) {
           part.chain_into(chain, first_group);
         } else {
@@ -594,7 +628,7 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
     matvec_split_kernel(const __grid_constant__ SplitLaunch L) {
   using Shape = RingShape<T>;
   constexpr int W = Shape::WARPS, S = Shape::S, STAGE = Ring<T>::STAGE;
-  constexpr int VSLOTS = MODE == MODE_MMA ? 8 : MODE;
+  constexpr int VSLOTS = mode_slots(MODE);
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -636,11 +670,13 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
                       segment * (Ring<T>::SEG / 4), local * ROWS);
     }
     constexpr int LINES = MODE == MODE_DP4A_1 ? 1 : MODE == MODE_DP4A_2 ? 2 : 7;
-    for (int i = lane; i < SEG_BLOCKS * LINES; i += WARP) {
-      const int b = segment * SEG_BLOCKS + i / LINES;
+    for (int i = lane; i < SEG_BLOCKS * LINES * mode_passes(MODE); i += WARP) {
+      const int pass = i / (SEG_BLOCKS * LINES), at = i % (SEG_BLOCKS * LINES);
+      const int b = segment * SEG_BLOCKS + at / LINES;
       if (b < blocks)
-        asm volatile("prefetch.global.L1 [%0];" ::"l"(L.records + (long long)b * MMA_RECORD_BYTES +
-                                                      128 * (i % LINES)));
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(L.records +
+                                                      ((long long)pass * blocks + b) * MMA_RECORD_BYTES +
+                                                      128 * (at % LINES)));
     }
     __syncwarp();
   };
@@ -653,7 +689,7 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
   Acc<MODE> part, total;
   part.zero();
   total.zero();
-  float* chain = reinterpret_cast<float*>(smem + Shape::X_OFFSET) + warp * 16 * WARP;
+  float* chain = reinterpret_cast<float*>(smem + Shape::X_OFFSET) + warp * 16 * mode_passes(MODE) * WARP;
   bool whole = false;  // this warp holds the current tile whole
   int first_group = 0;
   // every job is walked, even after a failed wait (as zeros), so that the
@@ -673,8 +709,9 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
     if (ok && j < issued) {
       const int first = segment * SEG_BLOCKS;
       const int count = blocks - first < SEG_BLOCKS ? blocks - first : SEG_BLOCKS;
-      if constexpr (MODE == MODE_MMA)
-        segment_mma<T>(ring + (j % S) * STAGE, first, count, L.records, L.vectors, part.a);
+      if constexpr (mma_mode(MODE))
+        segment_mma<T, mode_passes(MODE)>(ring + (j % S) * STAGE, first, count, L.records, blocks,
+                                          L.vectors, part.a);
       else
         segment_dp4a<T, MODE, false>(ring + (j % S) * STAGE, first, count, L.records, part.a);
     }
@@ -686,7 +723,7 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
     locate(tile, m, local);
     if (whole) {
       const bool first_group = group == 0;
-      if constexpr (MODE == MODE_MMA) {
+      if constexpr (mma_mode(MODE)) {
         if (segment != segments - 1) {
           part.chain_into(chain, first_group);
         } else {
@@ -739,6 +776,17 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
   }
 }
 
+// Whether the tile schedule's leftover group sums fit group_partials: a CTA
+// per SM (or per tile), W warps' tiles of G groups, ROWS x slots floats each.
+template <typename T>
+bool ring_partials_fit(int rows, int cols, int mode) {
+  const long long tiles = (rows + ROWS - 1) / ROWS;
+  const long long grid = tiles < sm_count() ? tiles : sm_count();
+  const long long segments = (cols / 32 + SEG_BLOCKS - 1) / SEG_BLOCKS;
+  return grid * RingShape<T>::WARPS * group_count(segments) * ROWS * mode_slots(mode) <=
+         PARTIAL_FLOATS;
+}
+
 template <typename T, int MODE, bool XSMEM>
 int launch_mode(const CUtensorMap& wmap, const uint8_t* records, float* y, int rows, int cols,
                 int vectors, int smem, cudaStream_t stream) {
@@ -748,9 +796,9 @@ int launch_mode(const CUtensorMap& wmap, const uint8_t* records, float* y, int r
   const int tiles = (rows + ROWS - 1) / ROWS;
   const unsigned grid = unsigned(tiles < sm_count() ? tiles : sm_count());
   // each CTA's leftover tiles keep their group sums in group_partials
-  if ((long long)grid * Shape::WARPS * MAX_GROUPS * ROWS * 8 > PARTIAL_FLOATS)
+  if (!ring_partials_fit<T>(rows, cols, MODE))
     return invalid("%u CTAs of leftover sums (at most %lld)", grid,
-                   PARTIAL_FLOATS / (Shape::WARPS * MAX_GROUPS * ROWS * 8));
+                   PARTIAL_FLOATS / (Shape::WARPS * MAX_GROUPS * ROWS * mode_slots(MODE)));
   DRIFT_CUDA(launch_pdl(matvec_ring_kernel<T, MODE, XSMEM>, grid, Shape::WARPS * 32, smem, stream,
                         wmap, records, y, rows, cols, vectors, device_error_word()));
   return 0;
@@ -779,10 +827,10 @@ int launch_split_mode(const SplitLaunch& launch, long long units, cudaStream_t s
   // 1-2 vectors: a CTA per unit up to the SM count, so a few-unit product
   // streams through every SM (8 units to a CTA left SMs idle: the C4 step at
   // batch 1 1.2 % slower); the MMA mode keeps 8 units to a CTA, faster there
-  long long grid = MODE == MODE_MMA ? (units + Shape::WARPS - 1) / Shape::WARPS : units;
+  long long grid = mma_mode(MODE) ? (units + Shape::WARPS - 1) / Shape::WARPS : units;
   if (grid > sm_count()) grid = sm_count();
   DRIFT_CUDA(launch_pdl(matvec_split_kernel<T, MODE>, unsigned(grid), Shape::WARPS * 32,
-                        Shape::BYTES + (MODE == MODE_MMA ? Shape::CHAIN_BYTES : 0), stream, launch));
+                        Shape::BYTES + Shape::chain_bytes(MODE), stream, launch));
   return 0;
 }
 
@@ -793,7 +841,7 @@ long long split_units(int64_t rows, int64_t cols) {
 }
 
 // One balanced launch over `count` matrices of one type sharing x (at most
-// 8 vectors, SPLIT_UNITS units together).
+// 16 vectors, SPLIT_UNITS units together).
 template <typename T>
 int split_dispatch(int count, const uint8_t* const* weights, float* const* ys, const int64_t* rows,
                    int cols, const uint8_t* records, int vectors, cudaStream_t stream) {
@@ -820,7 +868,19 @@ int split_dispatch(int count, const uint8_t* const* weights, float* const* ys, c
   if (units > SPLIT_UNITS) return invalid("a balanced launch of %lld units", units);
   if (vectors == 1) return launch_split_mode<T, MODE_DP4A_1>(launch, units, stream);
   if (vectors == 2) return launch_split_mode<T, MODE_DP4A_2>(launch, units, stream);
-  return launch_split_mode<T, MODE_MMA>(launch, units, stream);
+  if (vectors <= 8) return launch_split_mode<T, MODE_MMA>(launch, units, stream);
+  if constexpr (RingShape<T>::MMA16) {
+    return launch_split_mode<T, MODE_MMA16>(launch, units, stream);
+  } else {
+    // two 8-vector passes, the second on the next pass's records
+    DRIFT_TRY((launch_split_mode<T, MODE_MMA>(launch, units, stream)));
+    launch.records = records + (long long)(cols / 32) * MMA_RECORD_BYTES;
+    launch.vectors = vectors - 8;
+    for (int i = 0; i < n; ++i) launch.y[i] += 8ll * launch.rows[i];
+    if (launch.vectors == 1) return launch_split_mode<T, MODE_DP4A_1>(launch, units, stream);
+    if (launch.vectors == 2) return launch_split_mode<T, MODE_DP4A_2>(launch, units, stream);
+    return launch_split_mode<T, MODE_MMA>(launch, units, stream);
+  }
 }
 
 // One configuration per matrix type, whatever the number of vectors (and the
@@ -828,11 +888,17 @@ int split_dispatch(int count, const uint8_t* const* weights, float* const* ys, c
 // fewer tiles than SMs takes the balanced schedule, whose (tile, group)
 // units reach every SM, for 1-2 vectors and for long rows; the MMA mode's
 // products of shorter rows keep the tile schedule, which leaves SMs free for
-// the next launch's early weight copies.
+// the next launch's early weight copies. 9-16 vectors take one MMA16 launch
+// (two 8-vector passes where its leftover sums would not fit).
 template <typename T>
 int ring_dispatch(const uint8_t* weight, const uint8_t* records, float* y, int rows, int cols,
                   int vectors, cudaStream_t stream) {
   const int64_t rows64 = rows;
+  if (vectors > 8 && (!RingShape<T>::MMA16 || !ring_partials_fit<T>(rows, cols, MODE_MMA16))) {
+    DRIFT_TRY(ring_dispatch<T>(weight, records, y, rows, cols, 8, stream));
+    return ring_dispatch<T>(weight, records + (long long)(cols / 32) * MMA_RECORD_BYTES,
+                            y + 8ll * rows, rows, cols, vectors - 8, stream);
+  }
   const bool few_tiles = (rows + ROWS - 1) / ROWS < sm_count();
   const bool long_rows = (cols / 32 + SEG_BLOCKS - 1) / SEG_BLOCKS >= LONG_SEGMENTS;
   if (few_tiles && (vectors <= 2 || long_rows) && split_units(rows64, cols) <= SPLIT_UNITS)
@@ -842,8 +908,15 @@ int ring_dispatch(const uint8_t* weight, const uint8_t* records, float* y, int r
                              Ring<T>::PITCH / 4, ROWS));
   if (vectors == 1) return launch_dp4a<T, MODE_DP4A_1>(wmap, records, y, rows, cols, vectors, stream);
   if (vectors == 2) return launch_dp4a<T, MODE_DP4A_2>(wmap, records, y, rows, cols, vectors, stream);
-  return launch_mode<T, MODE_MMA, false>(wmap, records, y, rows, cols, vectors,
-                                         RingShape<T>::BYTES + RingShape<T>::CHAIN_BYTES, stream);
+  if (vectors <= 8)
+    return launch_mode<T, MODE_MMA, false>(wmap, records, y, rows, cols, vectors,
+                                           RingShape<T>::BYTES + RingShape<T>::chain_bytes(MODE_MMA),
+                                           stream);
+  if constexpr (RingShape<T>::MMA16)
+    return launch_mode<T, MODE_MMA16, false>(wmap, records, y, rows, cols, vectors,
+                                             RingShape<T>::BYTES + RingShape<T>::chain_bytes(MODE_MMA16),
+                                             stream);
+  return invalid("%d vectors in one pass", vectors);  // (taken as two passes above)
 }
 
 #define DRIFT_RING_REGISTER(T, name)                                                        \
@@ -855,9 +928,16 @@ int ring_dispatch(const uint8_t* weight, const uint8_t* records, float* y, int r
   DRIFT_REGISTER(matvec_ring_##name##_dp4a2, (matvec_ring_kernel<T, MODE_DP4A_2, false>))    \
   DRIFT_REGISTER(matvec_ring_##name##_dp4a2_xs, (matvec_ring_kernel<T, MODE_DP4A_2, true>))  \
   DRIFT_REGISTER(matvec_ring_##name##_mma, (matvec_ring_kernel<T, MODE_MMA, false>))
+// the 16-vector kernels of the types whose chain fits beside the ring
+#define DRIFT_RING16_REGISTER(T, name)                                                      \
+  DRIFT_REGISTER(matvec_split_##name##_mma16, (matvec_split_kernel<T, MODE_MMA16>))           \
+  DRIFT_REGISTER(matvec_ring_##name##_mma16, (matvec_ring_kernel<T, MODE_MMA16, false>))
 DRIFT_RING_REGISTER(Q8_0T, q8_0)
 DRIFT_RING_REGISTER(Q4_0T, q4_0)
 DRIFT_RING_REGISTER(Q4_1T, q4_1)
+DRIFT_RING16_REGISTER(Q4_0T, q4_0)
+DRIFT_RING16_REGISTER(Q4_1T, q4_1)
+static_assert(RingShape<Q4_0T>::MMA16 && RingShape<Q4_1T>::MMA16, "the 16-vector chain fits");
 
 }  // namespace
 
@@ -885,14 +965,14 @@ bool ring_many_fits(int weight_dtype, int count, const void* const* weights, con
   return units <= SPLIT_UNITS;
 }
 
-// Products sharing x's records in balanced launches, 8 vectors at a time.
+// Products sharing x's records in balanced launches, 16 vectors at a time.
 int matvec_ring_many(int weight_dtype, int count, const void* const* weights,
                      const uint8_t* records, float* const* ys, const int64_t* rows, int64_t cols,
                      int64_t vectors, cudaStream_t stream) {
   if (count > MAX_MATRICES) return invalid("%d products in one launch", count);
   const int64_t blocks = cols / 32;
-  for (int64_t first = 0; first < vectors; first += 8) {
-    const int n = int(vectors - first < 8 ? vectors - first : 8);
+  for (int64_t first = 0; first < vectors; first += 16) {
+    const int n = int(vectors - first < 16 ? vectors - first : 16);
     const uint8_t* w[MAX_MATRICES];
     float* y[MAX_MATRICES];
     for (int i = 0; i < count; ++i) {

@@ -33,7 +33,8 @@ TYPES = [oracle.Q8_0, oracle.Q4_0, oracle.Q4_1]
 # (M, N, K) as LinearTests.cases (L33-58): one row, odd row counts, rows
 # shorter than a chunk, a model's width, several vectors, past 8 vectors.
 CASES = [(1, 1, 64), (1, 7, 512), (1, 33, 640), (1, 64, 2560), (2, 9, 4096), (3, 20, 1024),
-         (8, 16, 2560), (9, 24, 512), (40, 72, 2560), (1, 1030, 1024), (64, 130, 4096)]
+         (8, 16, 2560), (9, 24, 512), (40, 72, 2560), (1, 1030, 1024), (64, 130, 4096),
+         (16, 300, 4096), (31, 70, 2048)]
 
 
 @pytest.fixture(scope="module")
@@ -208,18 +209,60 @@ def test_pipelined_host_copies(ops):
         assert lib.drift_stream_destroy(handle) == 0
 
 
-def test_linear_rows_do_not_depend_on_batch(ops):
-    """A row's sum is the same whether it comes alone or with 7 others."""
+@pytest.mark.parametrize("m", [8, 16])
+def test_linear_rows_do_not_depend_on_batch(ops, m):
+    """A row's sum is the same whether it comes alone or with 7 (or 15) others."""
     rng = np.random.default_rng(12)
     n, k = 300, 4096
     w = Stored.upload(oracle.Q4_1, (n, k), synthetic.quantized(rng, oracle.Q4_1, n, k))
-    x = torch.from_numpy(synthetic.gaussian(rng, 8, k)).cuda()
-    batch = torch.empty(8, n, device="cuda")
+    x = torch.from_numpy(synthetic.gaussian(rng, m, k)).cuda()
+    batch = torch.empty(m, n, device="cuda")
     ops.linear(x, w, batch)
-    for i in range(8):
+    for i in range(m):
         one = torch.empty(1, n, device="cuda")
         ops.linear(x[i:i + 1].contiguous(), w, one)
         assert torch.equal(one[0], batch[i])
+
+
+# 9-16 vectors stream the weights once (the MMA16 mode): every schedule --
+# the tile schedule with and without leftover tiles, the balanced one for
+# long rows, and two 8-vector passes where the leftover sums would not fit
+# (20000 x 8192) -- against passes of at most 8 vectors, bit for bit.
+SIXTEEN_SHAPES = [(300, 4096), (20000, 4096), (4096, 12288), (20000, 8192)]
+
+
+@pytest.mark.parametrize("dtype", TYPES, ids=lambda t: oracle.NAMES[t])
+@pytest.mark.parametrize("shape", SIXTEEN_SHAPES, ids=lambda s: f"{s[0]}x{s[1]}")
+def test_sixteen_vectors_are_two_passes(ops, dtype, shape):
+    n, k = shape
+    rng = np.random.default_rng(n + k + dtype)
+    w = Stored.upload(dtype, (n, k), synthetic.quantized(rng, dtype, n, k))
+    x = torch.from_numpy(synthetic.gaussian(rng, 31, k)).cuda()
+    for m in (9, 16, 31):
+        together = torch.empty(m, n, device="cuda")
+        ops.linear(x[:m].contiguous(), w, together)
+        for first in range(0, m, 8):
+            count = min(8, m - first)
+            part = torch.empty(count, n, device="cuda")
+            ops.linear(x[first:first + count].contiguous(), w, part)
+            assert torch.equal(part, together[first:first + count]), (m, first)
+
+
+def test_sixteen_vectors_share_a_launch(ops):
+    """Two Q4_1 products of 16 vectors in one balanced launch: each equals its
+    8-vector passes alone."""
+    rng = np.random.default_rng(15)
+    k = 4096
+    ws = [Stored.upload(oracle.Q4_1, (n, k), synthetic.quantized(rng, oracle.Q4_1, n, k))
+          for n in (1024, 512)]
+    x = torch.from_numpy(synthetic.gaussian(rng, 16, k)).cuda()
+    together = [torch.empty(16, w.shape[0], device="cuda") for w in ws]
+    ops.linears(x, ws, together)
+    for w, t in zip(ws, together):
+        for first in (0, 8):
+            part = torch.empty(8, w.shape[0], device="cuda")
+            ops.linear(x[first:first + 8].contiguous(), w, part)
+            assert torch.equal(part, t[first:first + 8])
 
 
 # The benchmark config C2 shapes at full size: sampled rows against the oracle,
