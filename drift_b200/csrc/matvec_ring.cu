@@ -83,6 +83,22 @@ struct RingShape {
   // whether the MMA16 chain fits beside the ring (Q4_0, Q4_1; Q8_0's larger
   // ring leaves it two 8-vector passes)
   static constexpr bool MMA16 = BYTES + chain_bytes(MODE_MMA16) <= MAX_SMEM;
+  // The tile schedule's MMA mode shares each segment's x records among the
+  // CTA's warps: X_SLOTS slots of a segment's records (8 x 896 bytes) after
+  // the chain, filled by bulk copies, then a full and an empty barrier per
+  // slot. Up to 4 slots where they fit (Q4_0, Q4_1), else none (Q8_0: the
+  // warps read x from global memory, as the other modes do).
+  static constexpr int X_SLOT = SEG_BLOCKS * MMA_RECORD_BYTES;
+  static constexpr int XS_OFFSET = (X_OFFSET + chain_bytes(MODE_MMA) + 127) / 128 * 128;
+  static constexpr int X_ROOM = (MAX_SMEM - 1024 - XS_OFFSET) / (X_SLOT + 16);
+  static constexpr int X_SLOTS = X_ROOM >= 4 ? 4 : X_ROOM >= 2 ? X_ROOM : 0;
+  static constexpr int XBAR_OFFSET = XS_OFFSET + X_SLOTS * X_SLOT;
+  // dynamic shared memory of the tile schedule's MMA modes (`slots`: with
+  // the shared x slots)
+  static constexpr int mma_bytes(int mode, bool slots) {
+    return mode == MODE_MMA && slots && X_SLOTS ? XBAR_OFFSET + 16 * X_SLOTS + 1024
+                                                : BYTES + chain_bytes(mode);
+  }
 };
 
 // One vector's x for one block, as the dp4a modes use it.
@@ -195,28 +211,53 @@ __device__ __forceinline__ void segment_dp4a(const uint8_t* stage, int first_blo
 }
 
 // ---- MMA modes: 3-16 vectors ----------------------------------------------------------------
+// load_fragment's x fragment from records copied to shared memory.
+template <typename T>
+__device__ __forceinline__ void load_fragment_shared(const uint8_t* rec, bool have_vector,
+                                                     XFragment& x) {
+  const int lane = threadIdx.x % 32, g = lane / 4, t = lane % 4;
+#pragma unroll
+  for (int p = 0; p < 3; ++p)
+    x.planes[p] = have_vector ? *reinterpret_cast<const uint2*>(rec + mma_plane_byte(g, p, t))
+                              : make_uint2(0, 0);
+  const float* s0 = reinterpret_cast<const float*>(rec + mma_scale_byte(2 * t));
+  const float* s1 = reinterpret_cast<const float*>(rec + mma_scale_byte(2 * t + 1));
+  x.s = make_float2(s0[0], s1[0]);
+  x.sum = T::DTYPE == DRIFT_Q4_0 ? make_int2(reinterpret_cast<const int*>(s0)[1],
+                                             reinterpret_cast<const int*>(s1)[1])
+                                 : make_int2(0, 0);
+  x.fsum = T::DTYPE == DRIFT_Q4_1 ? make_float2(s0[2], s1[2]) : make_float2(0.0f, 0.0f);
+}
+
 // acc[i][4 p + .] gains the segment's blocks for rows (16 i + g, 16 i + g + 8)
 // and vectors (8 p + 2t, 8 p + 2t + 1) of pass p (P passes, their records
 // `pass_bytes` apart), each as acc = fmaf(s, value, acc); a row's weight
 // fragment is unpacked once for every pass, and x is fetched one block ahead.
 // A vector's arithmetic is the same in either mode, so 16 vectors give the
 // bits of two 8-vector passes.
-template <typename T, int P, bool FULL>
+// XS: rec0 is the segment's records in shared memory, not global.
+template <typename T, int P, bool FULL, bool XS>
 __device__ __forceinline__ void segment_mma_blocks(const uint8_t* row_g, const uint8_t* rec0,
                                                    long long pass_bytes, int count, int vectors,
                                                    float (&acc)[4][4 * P]) {
   const int lane = threadIdx.x % WARP, g = lane / 4, t = lane % 4;
+  auto fetch = [&](const uint8_t* rec, bool have, XFragment& x) {
+    if constexpr (XS)
+      load_fragment_shared<T>(rec, have, x);
+    else
+      load_fragment<T>(rec, have, x);
+  };
   XFragment x[2][P];
 #pragma unroll
-  for (int p = 0; p < P; ++p) load_fragment<T>(rec0 + p * pass_bytes, g + 8 * p < vectors, x[0][p]);
+  for (int p = 0; p < P; ++p) fetch(rec0 + p * pass_bytes, g + 8 * p < vectors, x[0][p]);
 #pragma unroll
   for (int b = 0; b < SEG_BLOCKS; ++b) {
     if (FULL || b < count) {
       if (b + 1 < SEG_BLOCKS && (FULL || b + 1 < count))
 #pragma unroll
         for (int p = 0; p < P; ++p)
-          load_fragment<T>(rec0 + (b + 1) * MMA_RECORD_BYTES + p * pass_bytes, g + 8 * p < vectors,
-                           x[(b + 1) & 1][p]);
+          fetch(rec0 + (b + 1) * MMA_RECORD_BYTES + p * pass_bytes, g + 8 * p < vectors,
+                x[(b + 1) & 1][p]);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         uint32_t lo0, hi0, lo1, hi1;
@@ -251,9 +292,22 @@ __device__ __forceinline__ void segment_mma(const uint8_t* stage, int first_bloc
   const uint8_t* row_g = stage + g * Ring<T>::PITCH;
   const long long pass_bytes = (long long)blocks * MMA_RECORD_BYTES;
   if (count == SEG_BLOCKS)
-    segment_mma_blocks<T, P, true>(row_g, rec0, pass_bytes, SEG_BLOCKS, vectors, acc);
+    segment_mma_blocks<T, P, true, false>(row_g, rec0, pass_bytes, SEG_BLOCKS, vectors, acc);
   else
-    segment_mma_blocks<T, P, false>(row_g, rec0, pass_bytes, count, vectors, acc);
+    segment_mma_blocks<T, P, false, false>(row_g, rec0, pass_bytes, count, vectors, acc);
+}
+
+// The same with the segment's records (one pass) in a shared-memory slot.
+template <typename T>
+__device__ __forceinline__ void segment_mma_staged(const uint8_t* stage, int count,
+                                                   const uint8_t* slot, int vectors,
+                                                   float (&acc)[4][4]) {
+  const int lane = threadIdx.x % WARP, g = lane / 4;
+  const uint8_t* row_g = stage + g * Ring<T>::PITCH;
+  if (count == SEG_BLOCKS)
+    segment_mma_blocks<T, 1, true, true>(row_g, slot, 0, SEG_BLOCKS, vectors, acc);
+  else
+    segment_mma_blocks<T, 1, false, true>(row_g, slot, 0, count, vectors, acc);
 }
 
 // The accumulators of a warp: dp4a modes acc[r][v] for rows lane + 32 r;
@@ -468,17 +522,63 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Shape::BARS) + warp * S;
   volatile int* abort = reinterpret_cast<int*>(smem + Shape::BARS + W * S * 8);
   uint8_t* ring = smem + warp * S * STAGE;
+  // The MMA mode's shared x: the warps' whole tiles walk the row's segments
+  // in step (job j of every warp is segment j mod segments), so one copy of
+  // a segment's records serves all W warps. Slot j mod NX holds job j's;
+  // x_full[slot] completes when they land, x_empty[slot] when all W warps
+  // are done with them. Thread 0 fills the slots NX - 1 jobs ahead of its
+  // own warp, each after every warp has left the job it held before.
+  // (XSMEM in the MMA mode: the launch takes the slots; a CTA of fewer
+  // tiles than warps has no whole tiles and launches without them)
+  constexpr int NX = MODE == MODE_MMA && XSMEM ? Shape::X_SLOTS : 0;
+  uint8_t* x_slots = smem + Shape::XS_OFFSET;
+  uint64_t* x_full = reinterpret_cast<uint64_t*>(smem + Shape::XBAR_OFFSET);
+  uint64_t* x_empty = x_full + NX;
 
   const int blocks = cols / 32;
   const int segments = (blocks + SEG_BLOCKS - 1) / SEG_BLOCKS;
   const Schedule plan((rows + ROWS - 1) / ROWS, segments, W);
   const int jobs = plan.jobs(warp);
+  const int whole = plan.rounds * segments;  // jobs of whole tiles (every warp the same)
 
   if (threadIdx.x == 0) *abort = 0;
   if (lane < S) tc::mbar_init(&bars[lane], 1);
+  if (NX > 0 && threadIdx.x < NX) {
+    tc::mbar_init(&x_full[threadIdx.x], 1);
+    tc::mbar_init(&x_empty[threadIdx.x], W);
+  }
   tc::fence_barrier_init();
   __syncthreads();
+  // job q's records (q < whole) into its slot, by thread 0
+  auto issue_x = [&](int q) {
+    const int first = (q % segments) * SEG_BLOCKS;
+    const int count = blocks - first < SEG_BLOCKS ? blocks - first : SEG_BLOCKS;
+    const uint32_t bytes = uint32_t(count * MMA_RECORD_BYTES);
+    tc::mbar_expect_tx(&x_full[q % NX], bytes);
+    tc::bulk_load(x_slots + (q % NX) * Shape::X_SLOT, records + (long long)first * MMA_RECORD_BYTES,
+                  bytes, &x_full[q % NX]);
+  };
+  int x_issued = 0;  // (thread 0's count)
 
+  // The MMA mode's jobs outside the shared slots (a leftover tile's
+  // groups) bring their segment's x records (7 lines a block) into L1
+  // ahead of use -- only once x is written, after pdl_wait, so that no line
+  // of the kernel before lands in L1 first.
+  bool x_ready = false;
+  auto prefetch_x = [&](int j) {
+    if constexpr (MODE == MODE_MMA) {
+      if (!x_ready || (NX > 0 && j < whole)) return;
+      int tile, segment;
+      plan.job(warp, j, tile, segment);
+      constexpr int LINES = MMA_RECORD_BYTES / 128;
+      for (int i = lane; i < SEG_BLOCKS * LINES; i += WARP) {
+        const int b = segment * SEG_BLOCKS + i / LINES;
+        if (b < blocks)
+          asm volatile("prefetch.global.L1 [%0];" ::"l"(records + (long long)b * MMA_RECORD_BYTES +
+                                                        128 * (i % LINES)));
+      }
+    }
+  };
   // job j: one 2-D tensor copy of 64 rows x PITCH bytes (rows past the
   // matrix, and columns past a row, arrive as zeros)
   auto issue = [&](int j) {
@@ -489,6 +589,7 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
       tc::tma_load_2d(ring + (j % S) * STAGE, &wmap, &bars[j % S], segment * (Ring<T>::SEG / 4),
                       tile * ROWS);
     }
+    prefetch_x(j);
     __syncwarp();
   };
 
@@ -497,12 +598,15 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
   while (issued < jobs && issued < S) issue(issued++);
   pdl_trigger();
   pdl_wait();  // the weights' first copies are in flight; x is now ready
+  x_ready = true;
+  for (int j = 0; j < issued; ++j) prefetch_x(j);
   const uint8_t* x = records;
-  if constexpr (XSMEM) {
+  if (NX > 0 && threadIdx.x == 0)
+    for (; x_issued < NX - 1 && x_issued < whole; ++x_issued) issue_x(x_issued);
+  if constexpr (XSMEM && !mma_mode(MODE)) {
     // While the first copies fly: the vectors' slots of every block's record,
     // 112 V bytes a block, into shared memory, where every row of every tile
     // reads them.
-    static_assert(!mma_mode(MODE), "the MMA modes read x from global memory");
     constexpr int SLOT = MMA_SLOT_BYTES * MODE;
     uint8_t* xs = smem + Shape::X_OFFSET;
     for (int i = threadIdx.x; i < blocks * (SLOT / 16); i += blockDim.x) {
@@ -523,7 +627,6 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
   Acc<MODE> part, total;  // the group being summed; the chain of the tile's groups
   part.zero();
   total.zero();
-  const int whole = plan.rounds * segments;
   const Groups& groups = plan.groups;
   float* chain = reinterpret_cast<float*>(smem + Shape::X_OFFSET) + warp * 16 * mode_passes(MODE) * WARP;
   float* shared_sums = group_partials + (long long)blockIdx.x * W * groups.count * ROWS * VSLOTS;
@@ -531,19 +634,45 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
     const int j = consumed;
     int tile, segment;
     plan.job(warp, j, tile, segment);
+    const bool staged = NX > 0 && j < whole;
     if (ok) ok = tc::mbar_wait_warp(&bars[j % S], (j / S) & 1, abort, error);
+    if (ok && staged) ok = tc::mbar_wait_warp(&x_full[j % NX], (j / NX) & 1, abort, error);
     if (ok) {
       const int first = segment * SEG_BLOCKS;
       const int count = blocks - first < SEG_BLOCKS ? blocks - first : SEG_BLOCKS;
-      if constexpr (mma_mode(MODE))
+      if constexpr (NX > 0) {
+        if (staged)
+          segment_mma_staged<T>(ring + (j % S) * STAGE, count, x_slots + (j % NX) * Shape::X_SLOT,
+                                vectors, part.a);
+        else
+          segment_mma<T, 1>(ring + (j % S) * STAGE, first, count, records, blocks, vectors, part.a);
+      } else if constexpr (mma_mode(MODE)) {
         segment_mma<T, mode_passes(MODE)>(ring + (j % S) * STAGE, first, count, records, blocks,
                                           vectors, part.a);
-      else
+      } else {
         segment_dp4a<T, MODE, XSMEM>(ring + (j % S) * STAGE, first, count, x, part.a);
+      }
     }
     __syncwarp();
     ++consumed;
     if (ok && issued < jobs) issue(issued++);  // refill the freed stage
+    if (NX > 0 && staged) {
+      if (ok && lane == 0) tc::mbar_arrive(&x_empty[j % NX]);
+      // thread 0: job j + NX - 1's records, into the slot of job j - 1 once
+      // every warp has left it
+      const int q = j + NX - 1;
+      if (warp == 0 && ok && q < whole) {
+        bool free = true;
+        if (lane == 0) {
+          if (q >= NX) free = tc::mbar_wait(&x_empty[q % NX], ((q / NX) - 1) & 1, abort, error);
+          if (free) {
+            issue_x(q);
+            x_issued = q + 1;
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, free, 0);
+      }
+    }
     if (!groups.last(segment)) continue;
     if (j < whole) {
       const bool first_group = groups.in_first(segment);
@@ -582,6 +711,12 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
     // let the copies already issued land before the ring is reused or left
     volatile int never = 0;
     for (int j = consumed; j < issued; ++j) tc::mbar_wait(&bars[j % S], (j / S) & 1, &never, nullptr);
+  }
+  if (NX > 0 && threadIdx.x == 0) {
+    // the x copies in flight (at most one a slot) land before the CTA is left
+    volatile int never = 0;
+    for (int q = x_issued - NX > 0 ? x_issued - NX : 0; q < x_issued; ++q)
+      tc::mbar_wait(&x_full[q % NX], (q / NX) & 1, &never, nullptr);
   }
   if (plan.left > 0) {
     // the leftover tiles: their group sums chained in group order, warp w
@@ -658,17 +793,13 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
     while (m + 1 < L.count && tile >= L.tile_end[m]) ++m;
     local = tile - (m > 0 ? L.tile_end[m - 1] : 0);
   };
-  // job j: its weights by one 2-D tensor copy, and its x records' lines
-  // (the vectors' slots) into L1 ahead of use
-  auto issue = [&](int j) {
-    const int job = j0 + j, tile = job / segments, segment = job % segments;
-    int m, local;
-    locate(tile, m, local);
-    if (lane == 0) {
-      tc::mbar_expect_tx(&bars[j % S], uint32_t(STAGE));
-      tc::tma_load_2d(ring + (j % S) * STAGE, &L.maps[m], &bars[j % S],
-                      segment * (Ring<T>::SEG / 4), local * ROWS);
-    }
+  // job j's x records' lines (the vectors' slots) into L1 ahead of use --
+  // only once x is written, after pdl_wait, so that no line of the kernel
+  // before lands in L1 first
+  bool x_ready = false;
+  auto prefetch_x = [&](int j) {
+    if (!x_ready) return;
+    const int segment = (j0 + j) % segments;
     constexpr int LINES = MODE == MODE_DP4A_1 ? 1 : MODE == MODE_DP4A_2 ? 2 : 7;
     for (int i = lane; i < SEG_BLOCKS * LINES * mode_passes(MODE); i += WARP) {
       const int pass = i / (SEG_BLOCKS * LINES), at = i % (SEG_BLOCKS * LINES);
@@ -678,6 +809,18 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
                                                       ((long long)pass * blocks + b) * MMA_RECORD_BYTES +
                                                       128 * (at % LINES)));
     }
+  };
+  // job j: its weights by one 2-D tensor copy, and its x lines
+  auto issue = [&](int j) {
+    const int job = j0 + j, tile = job / segments, segment = job % segments;
+    int m, local;
+    locate(tile, m, local);
+    if (lane == 0) {
+      tc::mbar_expect_tx(&bars[j % S], uint32_t(STAGE));
+      tc::tma_load_2d(ring + (j % S) * STAGE, &L.maps[m], &bars[j % S],
+                      segment * (Ring<T>::SEG / 4), local * ROWS);
+    }
+    prefetch_x(j);
     __syncwarp();
   };
 
@@ -686,6 +829,8 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
   while (issued < jobs && issued < S) issue(issued++);
   pdl_trigger();
   pdl_wait();  // the weights' first copies are in flight; x is now ready
+  x_ready = true;
+  for (int j = 0; j < issued; ++j) prefetch_x(j);
   Acc<MODE> part, total;
   part.zero();
   total.zero();
@@ -886,7 +1031,8 @@ int split_dispatch(int count, const uint8_t* const* weights, float* const* ys, c
 // One configuration per matrix type, whatever the number of vectors (and the
 // group chain makes a row's bits the same in any schedule). A matrix of
 // fewer tiles than SMs takes the balanced schedule, whose (tile, group)
-// units reach every SM, for 1-2 vectors and for long rows; the MMA mode's
+// units reach every SM, for 1-2 vectors, 9-16 vectors (C4's step at batch 16
+// 2.7 % faster than with the tile schedule) and for long rows; the MMA mode's
 // products of shorter rows keep the tile schedule, which leaves SMs free for
 // the next launch's early weight copies. 9-16 vectors take one MMA16 launch
 // (two 8-vector passes where its leftover sums would not fit).
@@ -901,21 +1047,25 @@ int ring_dispatch(const uint8_t* weight, const uint8_t* records, float* y, int r
   }
   const bool few_tiles = (rows + ROWS - 1) / ROWS < sm_count();
   const bool long_rows = (cols / 32 + SEG_BLOCKS - 1) / SEG_BLOCKS >= LONG_SEGMENTS;
-  if (few_tiles && (vectors <= 2 || long_rows) && split_units(rows64, cols) <= SPLIT_UNITS)
+  if (few_tiles && (vectors <= 2 || vectors > 8 || long_rows) && split_units(rows64, cols) <= SPLIT_UNITS)
     return split_dispatch<T>(1, &weight, &y, &rows64, cols, records, vectors, stream);
   CUtensorMap wmap;
   DRIFT_TRY(encode_word_rows(&wmap, weight, int64_t(cols / 32) * T::BYTES / 4, rows,
                              Ring<T>::PITCH / 4, ROWS));
   if (vectors == 1) return launch_dp4a<T, MODE_DP4A_1>(wmap, records, y, rows, cols, vectors, stream);
   if (vectors == 2) return launch_dp4a<T, MODE_DP4A_2>(wmap, records, y, rows, cols, vectors, stream);
-  if (vectors <= 8)
+  if (vectors <= 8) {
+    // the shared x slots where every CTA holds whole tiles (as many as its warps)
+    const long long tiles = (rows + ROWS - 1) / ROWS;
+    if (RingShape<T>::X_SLOTS && tiles >= (long long)RingShape<T>::WARPS * sm_count())
+      return launch_mode<T, MODE_MMA, true>(wmap, records, y, rows, cols, vectors,
+                                            RingShape<T>::mma_bytes(MODE_MMA, true), stream);
     return launch_mode<T, MODE_MMA, false>(wmap, records, y, rows, cols, vectors,
-                                           RingShape<T>::BYTES + RingShape<T>::chain_bytes(MODE_MMA),
-                                           stream);
+                                           RingShape<T>::mma_bytes(MODE_MMA, false), stream);
+  }
   if constexpr (RingShape<T>::MMA16)
     return launch_mode<T, MODE_MMA16, false>(wmap, records, y, rows, cols, vectors,
-                                             RingShape<T>::BYTES + RingShape<T>::chain_bytes(MODE_MMA16),
-                                             stream);
+                                             RingShape<T>::mma_bytes(MODE_MMA16, false), stream);
   return invalid("%d vectors in one pass", vectors);  // (taken as two passes above)
 }
 
@@ -927,7 +1077,8 @@ int ring_dispatch(const uint8_t* weight, const uint8_t* records, float* y, int r
   DRIFT_REGISTER(matvec_ring_##name##_dp4a1_xs, (matvec_ring_kernel<T, MODE_DP4A_1, true>))  \
   DRIFT_REGISTER(matvec_ring_##name##_dp4a2, (matvec_ring_kernel<T, MODE_DP4A_2, false>))    \
   DRIFT_REGISTER(matvec_ring_##name##_dp4a2_xs, (matvec_ring_kernel<T, MODE_DP4A_2, true>))  \
-  DRIFT_REGISTER(matvec_ring_##name##_mma, (matvec_ring_kernel<T, MODE_MMA, false>))
+  DRIFT_REGISTER(matvec_ring_##name##_mma, (matvec_ring_kernel<T, MODE_MMA, false>))          \
+  DRIFT_REGISTER(matvec_ring_##name##_mma_xs, (matvec_ring_kernel<T, MODE_MMA, true>))
 // the 16-vector kernels of the types whose chain fits beside the ring
 #define DRIFT_RING16_REGISTER(T, name)                                                      \
   DRIFT_REGISTER(matvec_split_##name##_mma16, (matvec_split_kernel<T, MODE_MMA16>))           \
