@@ -560,13 +560,14 @@ __global__ void __launch_bounds__(RingShape<T>::WARPS * 32, 1)
   };
   int x_issued = 0;  // (thread 0's count)
 
-  // The MMA mode's jobs outside the shared slots (a leftover tile's
+  // With the shared slots, the MMA mode's other jobs (a leftover tile's
   // groups) bring their segment's x records (7 lines a block) into L1
   // ahead of use -- only once x is written, after pdl_wait, so that no line
-  // of the kernel before lands in L1 first.
+  // of the kernel before lands in L1 first. (Without the slots, CTAs of a
+  // tile or two, the prefetch costs more than it saves.)
   bool x_ready = false;
   auto prefetch_x = [&](int j) {
-    if constexpr (MODE == MODE_MMA) {
+    if constexpr (NX > 0) {
       if (!x_ready || (NX > 0 && j < whole)) return;
       int tile, segment;
       plan.job(warp, j, tile, segment);
