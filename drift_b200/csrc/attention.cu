@@ -468,23 +468,42 @@ __global__ void __launch_bounds__(SPLIT_THREADS) attention_split_kernel(const At
   }
   __syncthreads();
 
-  // keys (an invisible key's row is left as it is: its score is never used)
+  // keys (an invisible key's row is left as it is: its score is never used).
+  // Where a row's chunks divide the threads, a thread's chunk column is the
+  // same for all its keys, and their starts are read before the copies.
+  if constexpr (SPLIT_THREADS % T::CH == 0) {
+    constexpr int STEP = SPLIT_THREADS / T::CH, PER = KEYS / STEP;
+    const int c = tid % T::CH, k0 = tid / T::CH;
+    unsigned at[PER];
+#pragma unroll
+    for (int j = 0; j < PER; ++j) at[j] = key_at[k0 + STEP * j];
+#pragma unroll
+    for (int j = 0; j < PER; ++j)
+      if (at[j] != NONE)
+        cp_async16(ks + T::key_chunk(k0 + STEP * j, c), a.keys + 8 * ((long long)at[j] + c));
+  } else {
 #pragma unroll 4
-  for (int i = tid; i < KEYS * T::CH; i += SPLIT_THREADS) {
-    const int k = i / T::CH, c = i % T::CH;
-    const unsigned at = key_at[k];
-    if (at != NONE) cp_async16(ks + T::key_chunk(k, c), a.keys + 8 * ((long long)at + c));
+    for (int i = tid; i < KEYS * T::CH; i += SPLIT_THREADS) {
+      const int k = i / T::CH, c = i % T::CH;
+      const unsigned at = key_at[k];
+      if (at != NONE) cp_async16(ks + T::key_chunk(k, c), a.keys + 8 * ((long long)at + c));
+    }
   }
   asm volatile("cp.async.commit_group;" ::: "memory");  // the keys: group 1
   // values, a 16-byte run of 8 positions of one dimension at a time (a run
-  // never crosses a page: pages are multiples of 16 positions)
+  // never crosses a page: pages are multiples of 16 positions); a thread's
+  // run r is the same for all its dimensions (RUNS divides the threads)
   const long long column = ps / 8;  // 16-byte units from one dimension to the next
+  static_assert(SPLIT_THREADS % T::RUNS == 0, "a thread's run is fixed");
+  constexpr int V_STEP = SPLIT_THREADS / T::RUNS;
+  const int r = tid % T::RUNS, d0 = tid / T::RUNS;
+  const bool whole_run = run_whole[r];
+  const unsigned run_start = run_at[r];
 #pragma unroll 4
-  for (int i = tid; i < D * T::RUNS; i += SPLIT_THREADS) {
-    const int d = i / T::RUNS, r = i % T::RUNS;
+  for (int d = d0; d < D; d += V_STEP) {
     uint8_t* to = vs + T::value_chunk(d, r);
-    if (run_whole[r]) {
-      cp_async16(to, a.values + 8 * (run_at[r] + d * column));
+    if (whole_run) {
+      cp_async16(to, a.values + 8 * (run_start + d * column));
     } else {
       // a run the visible range cuts or misses: its visible positions one
       // by one, zeros elsewhere (an invisible position's weight is 0, and
