@@ -28,17 +28,19 @@ int prepare_x_mma(int x_dtype, const void* x, int64_t m, int64_t k, uint8_t* rec
 // ---- routing ----------------------------------------------------------------------------
 // One warp per token: the k largest of `experts` <= 512 logits, the lower
 // expert first among equals, then their softmax among themselves in double
-// (as CpuExperts.route computes it), rounded once.
-__device__ __forceinline__ void route_token(const float* __restrict__ logits,
-                                            int* __restrict__ ids, float* __restrict__ weights,
-                                            int t, int experts, int k) {
+// (as CpuExperts.route computes it), rounded once. The logits are read
+// through L2: in the whole-mixture launch other CTAs of the same launch
+// wrote them.
+__device__ __forceinline__ void route_token(const float* logits, int* __restrict__ ids,
+                                            float* __restrict__ weights, int t, int experts,
+                                            int k) {
   const int lane = threadIdx.x % WARP;
   const float* row = logits + (long long)t * experts;
   float v[16];
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     const int e = lane + 32 * i;
-    v[i] = e < experts ? row[e] : -INFINITY;
+    v[i] = e < experts ? __ldcg(row + e) : -INFINITY;
   }
   float chosen[16];
   int chosen_id[16];
