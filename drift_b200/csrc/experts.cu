@@ -282,6 +282,231 @@ DRIFT_EXPERTS_REGISTER(Q8_0T, q8_0)
 DRIFT_EXPERTS_REGISTER(Q4_0T, q4_0)
 DRIFT_EXPERTS_REGISTER(Q4_1T, q4_1)
 
+// ---- the experts' products, streamed through shared memory ----------------------------------
+// The same products as experts_x22_kernel, bit for bit, for weights whose
+// rows are whole 16-byte units. A launch's units are (slot, tile of 64 / KS
+// rows), slot-major, a contiguous run of them a CTA (one CTA of 16 warps an
+// SM). Thread 0 brings each unit's rows of the slot's expert -- and, gated,
+// of its up weight -- into one of the stages by bulk copies (an expert's
+// rows are contiguous), as many units ahead as there are stages, refilling a
+// stage as soon as the CTA has left it. The 16 warps are 16 / KS row groups
+// of KS k-splits, as experts_unit's 8: warp (group, kw) takes 4 rows and,
+// lane l, blocks 32 kw + l, 32 (kw + KS) + l, ... (each block of x read once
+// for the 4 rows); a row's k-splits meet in shared memory in order -- the
+// arithmetic of experts_unit, so the bits are its. The copies keep bytes in
+// flight while the warps compute; experts_x22_kernel is one round trip of
+// 4-byte loads a CTA, then its sums.
+constexpr int ES_WARPS = 16;
+struct ExpertsStream {
+  const uint8_t* gate;
+  const uint8_t* up;
+  long long expert_bytes;
+  const int* ids;
+  const uint8_t* records;
+  int divisor, routed_slots;
+  float* y;
+  int rows, cols;
+  long long experts, first_expert;
+  int others_zero;
+  int* error;
+  const float* x;        // XQ: the slots' F32 x rows
+  int tiles;             // units a slot
+  int units, stage_bytes, stages;
+};
+
+__host__ __device__ constexpr int es_x_bytes(int blocks) { return (blocks * MMA_SLOT_BYTES + 127) / 128 * 128; }
+
+template <typename T, int KS, bool GATED, bool XQ>
+__global__ void __launch_bounds__(ES_WARPS * 32, 1) experts_stream_kernel(const __grid_constant__ ExpertsStream L) {
+  constexpr int GROUPS = ES_WARPS / KS, ROWS = 4, TILE = GROUPS * ROWS, MAX_STAGES = 4;
+  pdl_trigger();  // the next kernel may launch and wait for this one
+  pdl_wait();     // the ids and x are written (which weights to copy follows from the ids)
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
+                                             ~uintptr_t(127));
+  __shared__ float partial[2][ES_WARPS][ROWS][2];
+  const int warp = threadIdx.x / WARP, lane = threadIdx.x % WARP;
+  const int kw = warp % KS, group = warp / KS;
+  const int blocks = L.cols / 32, S = L.stages;
+  const long long row_bytes = (long long)blocks * T::BYTES;
+  uint8_t* x_slot = smem + S * L.stage_bytes;  // XQ: the slot's x records
+  uint64_t* full = reinterpret_cast<uint64_t*>(x_slot + (XQ ? es_x_bytes(blocks) : 0));
+  volatile int* abort = reinterpret_cast<volatile int*>(full + MAX_STAGES);
+  const int u0 = int((long long)L.units * blockIdx.x / gridDim.x);
+  const int count = int((long long)L.units * (blockIdx.x + 1) / gridDim.x) - u0;
+  if (threadIdx.x == 0) *abort = 0;
+  if (threadIdx.x < S) tc::mbar_init(&full[threadIdx.x], 1);
+  tc::fence_barrier_init();
+  __syncthreads();
+
+  auto expert_of = [&](int slot) { return (long long)L.ids[slot] - L.first_expert; };
+  // unit j's rows into stage j mod S (thread 0); a slot of no expert here
+  // copies nothing
+  auto issue = [&](int j) {
+    const int u = u0 + j, slot = u / L.tiles, tile = u % L.tiles, st = j % S;
+    const long long e = expert_of(slot);
+    if (e < 0 || e >= L.experts) {
+      tc::mbar_arrive(&full[st]);
+      return;
+    }
+    const int row0 = tile * TILE;
+    const int n = L.rows - row0 < TILE ? L.rows - row0 : TILE;
+    const uint32_t bytes = uint32_t(n * row_bytes);
+    const long long at = e * L.expert_bytes + row0 * row_bytes;
+    uint8_t* stage = smem + st * L.stage_bytes;
+    tc::mbar_expect_tx(&full[st], GATED ? 2 * bytes : bytes);
+    tc::bulk_load(stage, L.gate + at, bytes, &full[st]);
+    if (GATED) tc::bulk_load(stage + TILE * row_bytes, L.up + at, bytes, &full[st]);
+  };
+  bool ok = true;
+  int issued = 0;  // (thread 0's count)
+  if (threadIdx.x == 0)
+    for (; issued < S && issued < count; ++issued) issue(issued);
+  int x_of = -1;  // XQ: the x row in x_slot
+  for (int j = 0; j < count; ++j) {
+    const int u = u0 + j, slot = u / L.tiles, tile = u % L.tiles;
+    const int v = slot < L.routed_slots ? slot / L.divisor : slot - L.routed_slots;
+    if constexpr (XQ) {
+      if (v != x_of) {
+        // the slot's x row as records (x22_record_slot: the preparation
+        // launch's bytes); every warp has left the last unit's x (the
+        // barrier at the end of each unit)
+        for (int c = warp; c < blocks; c += ES_WARPS)
+          x22_record_slot(L.x[(long long)v * L.cols + 32 * c + lane], x_slot + c * MMA_SLOT_BYTES);
+        __syncthreads();
+        x_of = v;
+      }
+    }
+    const long long e = expert_of(slot);
+    const int row0 = tile * TILE;
+    if (ok) ok = tc::mbar_wait_warp(&full[j % S], (j / S) & 1, abort, L.error);
+    const bool valid = e >= 0 && e < L.experts;
+    if (ok && valid) {
+      const uint8_t* stage = smem + (j % S) * L.stage_bytes;
+      const uint8_t* record =
+          XQ ? x_slot
+             : L.records + (long long)(v / 8) * blocks * MMA_RECORD_BYTES + MMA_SLOT_BYTES * (v % 8);
+      constexpr int STRIDE = XQ ? MMA_SLOT_BYTES : MMA_RECORD_BYTES;
+      const uint8_t* wg = stage + group * ROWS * row_bytes;
+      const uint8_t* wu = stage + (TILE + group * ROWS) * row_bytes;
+      float g[ROWS], up[ROWS];
+#pragma unroll
+      for (int r = 0; r < ROWS; ++r) g[r] = up[r] = 0.0f;
+      for (int c = kw * WARP + lane; c < blocks; c += WARP * KS) {
+        const uint4* rec = reinterpret_cast<const uint4*>(record + (long long)c * STRIDE);
+        // stored words 0..7 of a plane hold words 0, 4, 1, 5, 2, 6, 3, 7
+        uint32_t planes[24];
+#pragma unroll
+        for (int p = 0; p < 3; ++p) {
+          const uint4 q0 = XQ ? rec[2 * p] : __ldg(rec + 2 * p);
+          const uint4 q1 = XQ ? rec[2 * p + 1] : __ldg(rec + 2 * p + 1);
+          planes[8 * p + 0] = q0.x;
+          planes[8 * p + 4] = q0.y;
+          planes[8 * p + 1] = q0.z;
+          planes[8 * p + 5] = q0.w;
+          planes[8 * p + 2] = q1.x;
+          planes[8 * p + 6] = q1.y;
+          planes[8 * p + 3] = q1.z;
+          planes[8 * p + 7] = q1.w;
+        }
+        const uint4 tail = XQ ? rec[6] : __ldg(rec + 6);  // s, sum X at bytes 96, 100
+        const int word0 = (c * T::BYTES) & ~3;
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) {
+          uint32_t w[T::WORDS];
+          const uint32_t* pg = reinterpret_cast<const uint32_t*>(wg + r * row_bytes + word0);
+#pragma unroll
+          for (int i = 0; i < T::WORDS; ++i) w[i] = pg[i];
+          int a0, a1, a2;
+          const Codes cg = T::decode(w, c);
+          plane_sums<T>(cg, planes, a0, a1, a2);
+          g[r] += block_dot<T>(cg, a0, a1, a2, __uint_as_float(tail.x), int(tail.y));
+          if (GATED) {
+            const uint32_t* pu = reinterpret_cast<const uint32_t*>(wu + r * row_bytes + word0);
+#pragma unroll
+            for (int i = 0; i < T::WORDS; ++i) w[i] = pu[i];
+            const Codes cu = T::decode(w, c);
+            plane_sums<T>(cu, planes, a0, a1, a2);
+            up[r] += block_dot<T>(cu, a0, a1, a2, __uint_as_float(tail.x), int(tail.y));
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < ROWS; ++r) {
+#pragma unroll
+        for (int o = 16; o > 0; o /= 2) {
+          g[r] += __shfl_xor_sync(0xffffffffu, g[r], o);
+          if (GATED) up[r] += __shfl_xor_sync(0xffffffffu, up[r], o);
+        }
+      }
+      if (lane == 0) {
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) {
+          partial[j & 1][warp][r][0] = g[r];
+          partial[j & 1][warp][r][1] = up[r];
+        }
+      }
+    }
+    __syncthreads();  // the stage is free; the partial sums are in
+    if (threadIdx.x == 0 && ok && issued < count) {
+      issue(issued);
+      ++issued;
+    }
+    const int t = threadIdx.x;
+    if (t < TILE && row0 + t < L.rows) {
+      const int gi = t / ROWS, r = t % ROWS;
+      float* out = L.y + (long long)slot * L.rows + row0 + t;
+      if (!valid) {
+        // another rank's expert (zeros), or an id outside the table
+        if (!L.others_zero && t == 0 && L.error) atomicCAS(L.error, 0, 1);
+        *out = L.others_zero ? 0.0f : __int_as_float(0x7fc00000);
+      } else if (ok) {
+        float gs = 0.0f, us = 0.0f;
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk) {
+          gs += partial[j & 1][gi * KS + kk][r][0];
+          us += partial[j & 1][gi * KS + kk][r][1];
+        }
+        *out = GATED ? gs / (1.0f + expf(-gs)) * us : gs;
+      }
+    }
+  }
+  if (threadIdx.x == 0) {
+    // the copies issued land before the CTA leaves (all of them, when every
+    // wait came through; the last of each stage otherwise)
+    volatile int never = 0;
+    for (int q = issued - S > 0 ? issued - S : 0; q < issued; ++q)
+      tc::mbar_wait(&full[q % S], (q / S) & 1, &never, nullptr);
+  }
+}
+
+// The stages of a launch: a stage holds a unit's rows (both weights when
+// gated), as many stages (up to 4) as fit.
+struct EsShape {
+  int tile_rows, stage_bytes, stages, smem;
+};
+inline EsShape es_shape(int ks, long long row_bytes, bool gated, int blocks, bool xq) {
+  EsShape s;
+  s.tile_rows = (ES_WARPS / ks) * 4;
+  s.stage_bytes = int((row_bytes * s.tile_rows * (gated ? 2 : 1) + 16 + 127) / 128 * 128);
+  const int fixed = (xq ? es_x_bytes(blocks) : 0) + 4 * 8 + 16 + 128;
+  s.stages = (232448 - 2048 - fixed) / s.stage_bytes;
+  if (s.stages > 4) s.stages = 4;
+  s.smem = s.stages * s.stage_bytes + fixed;
+  return s;
+}
+
+template <typename T, int KS, bool GATED, bool XQ>
+static int launch_stream(const ExpertsStream& L, const EsShape& shape, cudaStream_t stream) {
+  static PerDevice configured;
+  DRIFT_TRY(ensure_shared_memory(configured, experts_stream_kernel<T, KS, GATED, XQ>, 232448 - 2048));
+  const int grid = L.units < sm_count() ? L.units : sm_count();
+  DRIFT_CUDA(launch_pdl(experts_stream_kernel<T, KS, GATED, XQ>, unsigned(grid), ES_WARPS * 32,
+                        shape.smem, stream, L));
+  DRIFT_LAUNCHED("experts_stream");
+  return 0;
+}
+
 template <typename T, bool GATED>
 static int launch_experts(const uint8_t* gate, const uint8_t* up, long long expert_bytes,
                           const int* ids, const uint8_t* records, int divisor, int routed_slots,
@@ -290,6 +515,48 @@ static int launch_experts(const uint8_t* gate, const uint8_t* up, long long expe
                           int others_zero, cudaStream_t stream, const float* xq = nullptr) {
   const int blocks = cols / 32;
   const int ks = blocks >= 128 ? 4 : (blocks >= 64 ? 2 : 1);
+  const long long row_bytes = (long long)blocks * T::BYTES;
+  const bool with_xq = !GATED && xq != nullptr;
+  const EsShape shape = es_shape(ks, row_bytes, GATED, blocks, with_xq);
+  if (row_bytes % 16 == 0 && (reinterpret_cast<uintptr_t>(gate) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(up) & 15) == 0 && expert_bytes % 16 == 0 && rows > 0 &&
+      slots > 0 && shape.stages >= 2 &&
+      (long long)slots * ((rows + shape.tile_rows - 1) / shape.tile_rows) >= 4LL * sm_count()) {
+    // rows of whole 16-byte units, two units' rows in shared memory at once,
+    // and four units or more an SM (C5's step at batch 16 3.4 % faster; with
+    // a unit or two an SM, as at batch 1, the direct kernel's three CTAs an
+    // SM are faster): streamed
+    ExpertsStream L = {};
+    L.gate = gate;
+    L.up = up;
+    L.expert_bytes = expert_bytes;
+    L.ids = ids;
+    L.records = records;
+    L.divisor = divisor;
+    L.routed_slots = routed_slots;
+    L.y = y;
+    L.rows = rows;
+    L.cols = cols;
+    L.experts = experts;
+    L.first_expert = first_expert;
+    L.others_zero = others_zero;
+    L.error = device_error_word();
+    L.x = xq;
+    L.tiles = (rows + shape.tile_rows - 1) / shape.tile_rows;
+    L.stage_bytes = shape.stage_bytes;
+    L.stages = shape.stages;
+    const long long units = (long long)slots * L.tiles;
+    if (units > 0x7fffffffll) return invalid("%lld expert units", units);
+    L.units = int(units);
+    if (with_xq) {
+      if (ks == 4) return launch_stream<T, 4, false, true>(L, shape, stream);
+      if (ks == 2) return launch_stream<T, 2, false, true>(L, shape, stream);
+      return launch_stream<T, 1, false, true>(L, shape, stream);
+    }
+    if (ks == 4) return launch_stream<T, 4, GATED, false>(L, shape, stream);
+    if (ks == 2) return launch_stream<T, 2, GATED, false>(L, shape, stream);
+    return launch_stream<T, 1, GATED, false>(L, shape, stream);
+  }
   const int rows_per_cta = 4 * (8 / ks);
   const dim3 grid(unsigned((rows + rows_per_cta - 1) / rows_per_cta), unsigned(slots));
   int* error = device_error_word();

@@ -253,6 +253,62 @@ def test_experts_linear_and_gated(ops, dtype):
         assert ok, summary
 
 
+def _shifted(w: Stored) -> Stored:
+    """The same blocks 4 bytes into a buffer: rows no longer start on 16-byte
+    boundaries, so the products take the direct-load kernel."""
+    data = torch.zeros(w.data.numel() + 4, dtype=torch.uint8, device="cuda")
+    data[4:] = w.data
+    return Stored(w.dtype, w.shape, data[4:])
+
+
+@pytest.mark.parametrize("dtype", [oracle.Q8_0, oracle.Q4_0, oracle.Q4_1],
+                         ids=lambda t: oracle.NAMES[t])
+@pytest.mark.parametrize("tokens", [16, 40])
+def test_streamed_experts_are_the_direct_kernel(ops, dtype, tokens):
+    """Weights of whole 16-byte rows stream through shared memory
+    (experts_stream_kernel, at four units an SM or more: 16 tokens of 10
+    slots are); the same weights 4 bytes off take the direct-load kernel
+    (experts_x22_kernel). Bit for bit: the gated gate/up over records
+    of x, the plain product of x rows shared by 10 slots, the down product
+    with x prepared in the kernel, and an expert-parallel product whose other
+    ranks' slots are zeros."""
+    rng = np.random.default_rng(70 + dtype + tokens)
+    experts, ffn, hidden = 24, 512, 2048
+    gate = Stored.upload(dtype, (experts, ffn, hidden),
+                         synthetic.quantized(rng, dtype, experts * ffn, hidden))
+    up = Stored.upload(dtype, (experts, ffn, hidden),
+                       synthetic.quantized(rng, dtype, experts * ffn, hidden))
+    down = Stored.upload(dtype, (experts, hidden, ffn),
+                         synthetic.quantized(rng, dtype, experts * hidden, ffn))
+    x = dev((synthetic.gaussian(rng, tokens, hidden) * 0.02).astype(np.float32))
+    ids = dev(np.stack([rng.permutation(experts)[:10] for _ in range(tokens)])
+              .astype(np.int32).reshape(-1))
+    slots = tokens * 10
+
+    def both(run, n):
+        a = torch.full((slots, n), float("nan"), device="cuda")
+        b = torch.full((slots, n), float("nan"), device="cuda")
+        run(False, a)
+        run(True, b)
+        assert torch.equal(a, b)
+        return a
+
+    gated = both(lambda shift, out: ops.experts_gated_linear(
+        x, _shifted(gate) if shift else gate, _shifted(up) if shift else up, ids, out), ffn)
+    both(lambda shift, out: ops.experts_linear(x, _shifted(gate) if shift else gate, ids, out),
+         ffn)
+    act = (gated / gated.std()).contiguous()
+    both(lambda shift, out: ops.experts_linear(act, _shifted(down) if shift else down, ids, out),
+         hidden)
+    # expert parallelism: this rank holds experts 8..15; the other slots are zeros
+    per_expert = hidden * ffn // 32 * synthetic.BLOCK_BYTES[dtype]
+    local = Stored(dtype, (8, hidden, ffn), down.data[8 * per_expert:16 * per_expert].contiguous())
+    part = both(lambda shift, out: ops.experts_linear(act, _shifted(local) if shift else local,
+                                                       ids, out, first_expert=8), hidden)
+    outside = ((ids < 8) | (ids >= 16)).cpu().numpy()
+    assert (part.cpu().numpy()[outside] == 0).all()
+
+
 def test_shared_expert_rides_in_the_routed_launch(ops):
     """A shared tail: the routed slots, then one slot per row of x for the
     shared expert (one more expert of the weights), in one launch -- bit for
