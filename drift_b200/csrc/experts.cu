@@ -520,12 +520,14 @@ static int launch_experts(const uint8_t* gate, const uint8_t* up, long long expe
   const EsShape shape = es_shape(ks, row_bytes, GATED, blocks, with_xq);
   if (row_bytes % 16 == 0 && (reinterpret_cast<uintptr_t>(gate) & 15) == 0 &&
       (reinterpret_cast<uintptr_t>(up) & 15) == 0 && expert_bytes % 16 == 0 && rows > 0 &&
-      slots > 0 && shape.stages >= 2 &&
+      slots > 0 && shape.stages >= 2 && GATED &&
       (long long)slots * ((rows + shape.tile_rows - 1) / shape.tile_rows) >= 4LL * sm_count()) {
-    // rows of whole 16-byte units, two units' rows in shared memory at once,
-    // and four units or more an SM (C5's step at batch 16 3.4 % faster; with
-    // a unit or two an SM, as at batch 1, the direct kernel's three CTAs an
-    // SM are faster): streamed
+    // the gated products (gate/up) of rows of whole 16-byte units, two
+    // units' rows in shared memory at once, and four units or more an SM:
+    // streamed (C5's step at batch 16 6.4 % faster). With a unit or two an
+    // SM, as at batch 1, the direct kernel's three CTAs an SM are faster;
+    // so are they for the plain products, whose units are a quarter of the
+    // work (streaming C5's down products too: 3.3 % faster only).
     ExpertsStream L = {};
     L.gate = gate;
     L.up = up;

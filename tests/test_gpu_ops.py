@@ -265,13 +265,12 @@ def _shifted(w: Stored) -> Stored:
                          ids=lambda t: oracle.NAMES[t])
 @pytest.mark.parametrize("tokens", [16, 40])
 def test_streamed_experts_are_the_direct_kernel(ops, dtype, tokens):
-    """Weights of whole 16-byte rows stream through shared memory
+    """Gated weights of whole 16-byte rows stream through shared memory
     (experts_stream_kernel, at four units an SM or more: 16 tokens of 10
     slots are); the same weights 4 bytes off take the direct-load kernel
-    (experts_x22_kernel). Bit for bit: the gated gate/up over records
-    of x, the plain product of x rows shared by 10 slots, the down product
-    with x prepared in the kernel, and an expert-parallel product whose other
-    ranks' slots are zeros."""
+    (experts_x22_kernel). Bit for bit: the gated gate/up over records of x,
+    and an expert-parallel gate/up whose other ranks' slots are zeros; the
+    plain products (direct either way) alongside."""
     rng = np.random.default_rng(70 + dtype + tokens)
     experts, ffn, hidden = 24, 512, 2048
     gate = Stored.upload(dtype, (experts, ffn, hidden),
@@ -301,12 +300,16 @@ def test_streamed_experts_are_the_direct_kernel(ops, dtype, tokens):
     both(lambda shift, out: ops.experts_linear(act, _shifted(down) if shift else down, ids, out),
          hidden)
     # expert parallelism: this rank holds experts 8..15; the other slots are zeros
-    per_expert = hidden * ffn // 32 * synthetic.BLOCK_BYTES[dtype]
-    local = Stored(dtype, (8, hidden, ffn), down.data[8 * per_expert:16 * per_expert].contiguous())
-    part = both(lambda shift, out: ops.experts_linear(act, _shifted(local) if shift else local,
-                                                       ids, out, first_expert=8), hidden)
+    per_expert = ffn * hidden // 32 * synthetic.BLOCK_BYTES[dtype]
+    lg = Stored(dtype, (8, ffn, hidden), gate.data[8 * per_expert:16 * per_expert].contiguous())
+    lu = Stored(dtype, (8, ffn, hidden), up.data[8 * per_expert:16 * per_expert].contiguous())
+    part = both(lambda shift, out: ops.experts_gated_linear(
+        x, _shifted(lg) if shift else lg, _shifted(lu) if shift else lu, ids, out,
+        first_expert=8), ffn)
     outside = ((ids < 8) | (ids >= 16)).cpu().numpy()
     assert (part.cpu().numpy()[outside] == 0).all()
+    assert torch.equal(part[torch.from_numpy(~outside).cuda()],
+                       gated[torch.from_numpy(~outside).cuda()])
 
 
 def test_shared_expert_rides_in_the_routed_launch(ops):
