@@ -316,9 +316,15 @@ struct ExpertsStream {
 
 __host__ __device__ constexpr int es_x_bytes(int blocks) { return (blocks * MMA_SLOT_BYTES + 127) / 128 * 128; }
 
-template <typename T, int KS, bool GATED, bool XQ>
+// HALF (plain products of at most 16 blocks a row, KS = 1): a warp's two
+// half-warps take a row each, 8 rows a warp in four passes, and a row's
+// lanes meet by the tree of its half-warp -- the bits of the full warp's
+// tree, in which the other half's lanes hold zeros (a lane's sum, 0 plus its
+// block's, is never -0, so adding those zeros changes nothing).
+template <typename T, int KS, bool GATED, bool XQ, bool HALF = false>
 __global__ void __launch_bounds__(ES_WARPS * 32, 1) experts_stream_kernel(const __grid_constant__ ExpertsStream L) {
-  constexpr int GROUPS = ES_WARPS / KS, ROWS = 4, TILE = GROUPS * ROWS, MAX_STAGES = 4;
+  static_assert(!HALF || (KS == 1 && !GATED), "half-warp rows: plain products, one k-split");
+  constexpr int GROUPS = ES_WARPS / KS, ROWS = HALF ? 8 : 4, TILE = GROUPS * ROWS, MAX_STAGES = 4;
   pdl_trigger();  // the next kernel may launch and wait for this one
   pdl_wait();     // the ids and x are written (which weights to copy follows from the ids)
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -392,6 +398,53 @@ __global__ void __launch_bounds__(ES_WARPS * 32, 1) experts_stream_kernel(const 
       float g[ROWS], up[ROWS];
 #pragma unroll
       for (int r = 0; r < ROWS; ++r) g[r] = up[r] = 0.0f;
+      if constexpr (HALF) {
+        // pass p: half-warp h takes row 2 p + h, lane its block lane % 16
+        const int h = lane / 16, c = lane % 16;
+        if (c < blocks) {
+          const uint4* rec = reinterpret_cast<const uint4*>(record + (long long)c * STRIDE);
+          uint32_t planes[24];
+#pragma unroll
+          for (int p = 0; p < 3; ++p) {
+            const uint4 q0 = XQ ? rec[2 * p] : __ldg(rec + 2 * p);
+            const uint4 q1 = XQ ? rec[2 * p + 1] : __ldg(rec + 2 * p + 1);
+            planes[8 * p + 0] = q0.x;
+            planes[8 * p + 4] = q0.y;
+            planes[8 * p + 1] = q0.z;
+            planes[8 * p + 5] = q0.w;
+            planes[8 * p + 2] = q1.x;
+            planes[8 * p + 6] = q1.y;
+            planes[8 * p + 3] = q1.z;
+            planes[8 * p + 7] = q1.w;
+          }
+          const uint4 tail = XQ ? rec[6] : __ldg(rec + 6);
+          const int word0 = (c * T::BYTES) & ~3;
+#pragma unroll
+          for (int p = 0; p < ROWS / 2; ++p) {
+            uint32_t w[T::WORDS];
+            const uint32_t* pg =
+                reinterpret_cast<const uint32_t*>(wg + (2 * p + h) * row_bytes + word0);
+#pragma unroll
+            for (int i = 0; i < T::WORDS; ++i) w[i] = pg[i];
+            int a0, a1, a2;
+            const Codes cg = T::decode(w, c);
+            plane_sums<T>(cg, planes, a0, a1, a2);
+            g[p] += block_dot<T>(cg, a0, a1, a2, __uint_as_float(tail.x), int(tail.y));
+          }
+        }
+#pragma unroll
+        for (int p = 0; p < ROWS / 2; ++p) {
+#pragma unroll
+          for (int o = 8; o > 0; o /= 2) g[p] += __shfl_xor_sync(0xffffffffu, g[p], o);
+        }
+        if (lane % 16 == 0) {
+#pragma unroll
+          for (int p = 0; p < ROWS / 2; ++p) {
+            partial[j & 1][warp][2 * p + h][0] = g[p];
+            partial[j & 1][warp][2 * p + h][1] = 0.0f;
+          }
+        }
+      } else {
       for (int c = kw * WARP + lane; c < blocks; c += WARP * KS) {
         const uint4* rec = reinterpret_cast<const uint4*>(record + (long long)c * STRIDE);
         // stored words 0..7 of a plane hold words 0, 4, 1, 5, 2, 6, 3, 7
@@ -446,6 +499,7 @@ __global__ void __launch_bounds__(ES_WARPS * 32, 1) experts_stream_kernel(const 
           partial[j & 1][warp][r][1] = up[r];
         }
       }
+      }
     }
     __syncthreads();  // the stage is free; the partial sums are in
     if (threadIdx.x == 0 && ok && issued < count) {
@@ -485,9 +539,10 @@ __global__ void __launch_bounds__(ES_WARPS * 32, 1) experts_stream_kernel(const 
 struct EsShape {
   int tile_rows, stage_bytes, stages, smem;
 };
-inline EsShape es_shape(int ks, long long row_bytes, bool gated, int blocks, bool xq) {
+inline EsShape es_shape(int ks, long long row_bytes, bool gated, int blocks, bool xq,
+                        bool half = false) {
   EsShape s;
-  s.tile_rows = (ES_WARPS / ks) * 4;
+  s.tile_rows = (ES_WARPS / ks) * (half ? 8 : 4);
   s.stage_bytes = int((row_bytes * s.tile_rows * (gated ? 2 : 1) + 16 + 127) / 128 * 128);
   const int fixed = (xq ? es_x_bytes(blocks) : 0) + 4 * 8 + 16 + 128;
   s.stages = (232448 - 2048 - fixed) / s.stage_bytes;
@@ -496,13 +551,14 @@ inline EsShape es_shape(int ks, long long row_bytes, bool gated, int blocks, boo
   return s;
 }
 
-template <typename T, int KS, bool GATED, bool XQ>
+template <typename T, int KS, bool GATED, bool XQ, bool HALF = false>
 static int launch_stream(const ExpertsStream& L, const EsShape& shape, cudaStream_t stream) {
   static PerDevice configured;
-  DRIFT_TRY(ensure_shared_memory(configured, experts_stream_kernel<T, KS, GATED, XQ>, 232448 - 2048));
+  DRIFT_TRY(ensure_shared_memory(configured, experts_stream_kernel<T, KS, GATED, XQ, HALF>,
+                                 232448 - 2048));
   const int grid = L.units < sm_count() ? L.units : sm_count();
-  DRIFT_CUDA(launch_pdl(experts_stream_kernel<T, KS, GATED, XQ>, unsigned(grid), ES_WARPS * 32,
-                        shape.smem, stream, L));
+  DRIFT_CUDA(launch_pdl(experts_stream_kernel<T, KS, GATED, XQ, HALF>, unsigned(grid),
+                        ES_WARPS * 32, shape.smem, stream, L));
   DRIFT_LAUNCHED("experts_stream");
   return 0;
 }
@@ -517,10 +573,11 @@ static int launch_experts(const uint8_t* gate, const uint8_t* up, long long expe
   const int ks = blocks >= 128 ? 4 : (blocks >= 64 ? 2 : 1);
   const long long row_bytes = (long long)blocks * T::BYTES;
   const bool with_xq = !GATED && xq != nullptr;
-  const EsShape shape = es_shape(ks, row_bytes, GATED, blocks, with_xq);
+  const bool half = !GATED && blocks <= 16;  // plain products of short rows: HALF
+  const EsShape shape = es_shape(ks, row_bytes, GATED, blocks, with_xq, half);
   if (row_bytes % 16 == 0 && (reinterpret_cast<uintptr_t>(gate) & 15) == 0 &&
       (reinterpret_cast<uintptr_t>(up) & 15) == 0 && expert_bytes % 16 == 0 && rows > 0 &&
-      slots > 0 && shape.stages >= 2 && GATED &&
+      slots > 0 && shape.stages >= 2 && (GATED || half) &&
       (long long)slots * ((rows + shape.tile_rows - 1) / shape.tile_rows) >= 4LL * sm_count()) {
     // the gated products (gate/up) of rows of whole 16-byte units, two
     // units' rows in shared memory at once, and four units or more an SM:
@@ -550,14 +607,15 @@ static int launch_experts(const uint8_t* gate, const uint8_t* up, long long expe
     const long long units = (long long)slots * L.tiles;
     if (units > 0x7fffffffll) return invalid("%lld expert units", units);
     L.units = int(units);
-    if (with_xq) {
-      if (ks == 4) return launch_stream<T, 4, false, true>(L, shape, stream);
-      if (ks == 2) return launch_stream<T, 2, false, true>(L, shape, stream);
-      return launch_stream<T, 1, false, true>(L, shape, stream);
+    if constexpr (!GATED) {
+      // (half: blocks <= 16, so ks is 1)
+      if (with_xq) return launch_stream<T, 1, false, true, true>(L, shape, stream);
+      return launch_stream<T, 1, false, false, true>(L, shape, stream);
+    } else {
+      if (ks == 4) return launch_stream<T, 4, true, false>(L, shape, stream);
+      if (ks == 2) return launch_stream<T, 2, true, false>(L, shape, stream);
+      return launch_stream<T, 1, true, false>(L, shape, stream);
     }
-    if (ks == 4) return launch_stream<T, 4, GATED, false>(L, shape, stream);
-    if (ks == 2) return launch_stream<T, 2, GATED, false>(L, shape, stream);
-    return launch_stream<T, 1, GATED, false>(L, shape, stream);
   }
   const int rows_per_cta = 4 * (8 / ks);
   const dim3 grid(unsigned((rows + rows_per_cta - 1) / rows_per_cta), unsigned(slots));

@@ -265,12 +265,14 @@ def _shifted(w: Stored) -> Stored:
                          ids=lambda t: oracle.NAMES[t])
 @pytest.mark.parametrize("tokens", [16, 40])
 def test_streamed_experts_are_the_direct_kernel(ops, dtype, tokens):
-    """Gated weights of whole 16-byte rows stream through shared memory
+    """Weights of whole 16-byte rows stream through shared memory
     (experts_stream_kernel, at four units an SM or more: 16 tokens of 10
-    slots are); the same weights 4 bytes off take the direct-load kernel
-    (experts_x22_kernel). Bit for bit: the gated gate/up over records of x,
-    and an expert-parallel gate/up whose other ranks' slots are zeros; the
-    plain products (direct either way) alongside."""
+    slots are) -- the gated products, and plain products of rows of at most
+    16 blocks (the down product, x prepared in the kernel, a row to each
+    half-warp); the same weights 4 bytes off take the direct-load kernel
+    (experts_x22_kernel). Bit for bit, and for expert-parallel products whose
+    other ranks' slots are zeros; the plain gate product (direct either way)
+    alongside."""
     rng = np.random.default_rng(70 + dtype + tokens)
     experts, ffn, hidden = 24, 512, 2048
     gate = Stored.upload(dtype, (experts, ffn, hidden),
@@ -297,8 +299,8 @@ def test_streamed_experts_are_the_direct_kernel(ops, dtype, tokens):
     both(lambda shift, out: ops.experts_linear(x, _shifted(gate) if shift else gate, ids, out),
          ffn)
     act = (gated / gated.std()).contiguous()
-    both(lambda shift, out: ops.experts_linear(act, _shifted(down) if shift else down, ids, out),
-         hidden)
+    full = both(lambda shift, out: ops.experts_linear(act, _shifted(down) if shift else down,
+                                                       ids, out), hidden)
     # expert parallelism: this rank holds experts 8..15; the other slots are zeros
     per_expert = ffn * hidden // 32 * synthetic.BLOCK_BYTES[dtype]
     lg = Stored(dtype, (8, ffn, hidden), gate.data[8 * per_expert:16 * per_expert].contiguous())
@@ -308,8 +310,13 @@ def test_streamed_experts_are_the_direct_kernel(ops, dtype, tokens):
         first_expert=8), ffn)
     outside = ((ids < 8) | (ids >= 16)).cpu().numpy()
     assert (part.cpu().numpy()[outside] == 0).all()
-    assert torch.equal(part[torch.from_numpy(~outside).cuda()],
-                       gated[torch.from_numpy(~outside).cuda()])
+    inside = torch.from_numpy(~outside).cuda()
+    assert torch.equal(part[inside], gated[inside])
+    ld = Stored(dtype, (8, hidden, ffn), down.data[8 * per_expert:16 * per_expert].contiguous())
+    part = both(lambda shift, out: ops.experts_linear(act, _shifted(ld) if shift else ld, ids,
+                                                       out, first_expert=8), hidden)
+    assert (part.cpu().numpy()[outside] == 0).all()
+    assert torch.equal(part[inside], full[inside])
 
 
 def test_shared_expert_rides_in_the_routed_launch(ops):
