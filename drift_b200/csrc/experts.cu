@@ -335,8 +335,8 @@ __global__ void __launch_bounds__(ES_WARPS * 32, 1) experts_stream_kernel(const 
   const int kw = warp % KS, group = warp / KS;
   const int blocks = L.cols / 32, S = L.stages;
   const long long row_bytes = (long long)blocks * T::BYTES;
-  uint8_t* x_slot = smem + S * L.stage_bytes;  // XQ: the slot's x records
-  uint64_t* full = reinterpret_cast<uint64_t*>(x_slot + (XQ ? es_x_bytes(blocks) : 0));
+  uint8_t* x_slot = smem + S * L.stage_bytes;  // the slot's x records
+  uint64_t* full = reinterpret_cast<uint64_t*>(x_slot + es_x_bytes(blocks));
   volatile int* abort = reinterpret_cast<volatile int*>(full + MAX_STAGES);
   const int u0 = int((long long)L.units * blockIdx.x / gridDim.x);
   const int count = int((long long)L.units * (blockIdx.x + 1) / gridDim.x) - u0;
@@ -368,20 +368,31 @@ __global__ void __launch_bounds__(ES_WARPS * 32, 1) experts_stream_kernel(const 
   int issued = 0;  // (thread 0's count)
   if (threadIdx.x == 0)
     for (; issued < S && issued < count; ++issued) issue(issued);
-  int x_of = -1;  // XQ: the x row in x_slot
+  int x_of = -1;  // the x row in x_slot
   for (int j = 0; j < count; ++j) {
     const int u = u0 + j, slot = u / L.tiles, tile = u % L.tiles;
     const int v = slot < L.routed_slots ? slot / L.divisor : slot - L.routed_slots;
-    if constexpr (XQ) {
-      if (v != x_of) {
-        // the slot's x row as records (x22_record_slot: the preparation
-        // launch's bytes); every warp has left the last unit's x (the
-        // barrier at the end of each unit)
+    if (v != x_of) {
+      // the slot's x records into shared memory, where every warp reads
+      // them (read from global memory by every k-split's warps, they kept
+      // the load queue full): XQ makes them from the F32 row
+      // (x22_record_slot: the preparation launch's bytes), else they are
+      // copied from the prepared records. Every warp has left the last
+      // unit's x (the barrier at the end of each unit).
+      if constexpr (XQ) {
         for (int c = warp; c < blocks; c += ES_WARPS)
           x22_record_slot(L.x[(long long)v * L.cols + 32 * c + lane], x_slot + c * MMA_SLOT_BYTES);
-        __syncthreads();
-        x_of = v;
+      } else {
+        const uint8_t* from =
+            L.records + (long long)(v / 8) * blocks * MMA_RECORD_BYTES + MMA_SLOT_BYTES * (v % 8);
+        for (int i = threadIdx.x; i < blocks * (MMA_SLOT_BYTES / 16); i += blockDim.x) {
+          const int c = i / (MMA_SLOT_BYTES / 16), part = i % (MMA_SLOT_BYTES / 16);
+          *reinterpret_cast<uint4*>(x_slot + c * MMA_SLOT_BYTES + 16 * part) = __ldg(
+              reinterpret_cast<const uint4*>(from + (long long)c * MMA_RECORD_BYTES + 16 * part));
+        }
       }
+      __syncthreads();
+      x_of = v;
     }
     const long long e = expert_of(slot);
     const int row0 = tile * TILE;
@@ -389,10 +400,8 @@ __global__ void __launch_bounds__(ES_WARPS * 32, 1) experts_stream_kernel(const 
     const bool valid = e >= 0 && e < L.experts;
     if (ok && valid) {
       const uint8_t* stage = smem + (j % S) * L.stage_bytes;
-      const uint8_t* record =
-          XQ ? x_slot
-             : L.records + (long long)(v / 8) * blocks * MMA_RECORD_BYTES + MMA_SLOT_BYTES * (v % 8);
-      constexpr int STRIDE = XQ ? MMA_SLOT_BYTES : MMA_RECORD_BYTES;
+      const uint8_t* record = x_slot;
+      constexpr int STRIDE = MMA_SLOT_BYTES;
       const uint8_t* wg = stage + group * ROWS * row_bytes;
       const uint8_t* wu = stage + (TILE + group * ROWS) * row_bytes;
       float g[ROWS], up[ROWS];
@@ -406,8 +415,8 @@ __global__ void __launch_bounds__(ES_WARPS * 32, 1) experts_stream_kernel(const 
           uint32_t planes[24];
 #pragma unroll
           for (int p = 0; p < 3; ++p) {
-            const uint4 q0 = XQ ? rec[2 * p] : __ldg(rec + 2 * p);
-            const uint4 q1 = XQ ? rec[2 * p + 1] : __ldg(rec + 2 * p + 1);
+            const uint4 q0 = rec[2 * p];
+            const uint4 q1 = rec[2 * p + 1];
             planes[8 * p + 0] = q0.x;
             planes[8 * p + 4] = q0.y;
             planes[8 * p + 1] = q0.z;
@@ -417,7 +426,7 @@ __global__ void __launch_bounds__(ES_WARPS * 32, 1) experts_stream_kernel(const 
             planes[8 * p + 3] = q1.z;
             planes[8 * p + 7] = q1.w;
           }
-          const uint4 tail = XQ ? rec[6] : __ldg(rec + 6);
+          const uint4 tail = rec[6];
           const int word0 = (c * T::BYTES) & ~3;
 #pragma unroll
           for (int p = 0; p < ROWS / 2; ++p) {
@@ -451,8 +460,8 @@ __global__ void __launch_bounds__(ES_WARPS * 32, 1) experts_stream_kernel(const 
         uint32_t planes[24];
 #pragma unroll
         for (int p = 0; p < 3; ++p) {
-          const uint4 q0 = XQ ? rec[2 * p] : __ldg(rec + 2 * p);
-          const uint4 q1 = XQ ? rec[2 * p + 1] : __ldg(rec + 2 * p + 1);
+          const uint4 q0 = rec[2 * p];
+          const uint4 q1 = rec[2 * p + 1];
           planes[8 * p + 0] = q0.x;
           planes[8 * p + 4] = q0.y;
           planes[8 * p + 1] = q0.z;
@@ -462,7 +471,7 @@ __global__ void __launch_bounds__(ES_WARPS * 32, 1) experts_stream_kernel(const 
           planes[8 * p + 3] = q1.z;
           planes[8 * p + 7] = q1.w;
         }
-        const uint4 tail = XQ ? rec[6] : __ldg(rec + 6);  // s, sum X at bytes 96, 100
+        const uint4 tail = rec[6];  // s, sum X at bytes 96, 100
         const int word0 = (c * T::BYTES) & ~3;
 #pragma unroll
         for (int r = 0; r < ROWS; ++r) {
@@ -539,12 +548,11 @@ __global__ void __launch_bounds__(ES_WARPS * 32, 1) experts_stream_kernel(const 
 struct EsShape {
   int tile_rows, stage_bytes, stages, smem;
 };
-inline EsShape es_shape(int ks, long long row_bytes, bool gated, int blocks, bool xq,
-                        bool half = false) {
+inline EsShape es_shape(int ks, long long row_bytes, bool gated, int blocks, bool half) {
   EsShape s;
   s.tile_rows = (ES_WARPS / ks) * (half ? 8 : 4);
   s.stage_bytes = int((row_bytes * s.tile_rows * (gated ? 2 : 1) + 16 + 127) / 128 * 128);
-  const int fixed = (xq ? es_x_bytes(blocks) : 0) + 4 * 8 + 16 + 128;
+  const int fixed = es_x_bytes(blocks) + 4 * 8 + 16 + 128;  // + the slot's x records
   s.stages = (232448 - 2048 - fixed) / s.stage_bytes;
   if (s.stages > 4) s.stages = 4;
   s.smem = s.stages * s.stage_bytes + fixed;
@@ -574,7 +582,7 @@ static int launch_experts(const uint8_t* gate, const uint8_t* up, long long expe
   const long long row_bytes = (long long)blocks * T::BYTES;
   const bool with_xq = !GATED && xq != nullptr;
   const bool half = !GATED && blocks <= 16;  // plain products of short rows: HALF
-  const EsShape shape = es_shape(ks, row_bytes, GATED, blocks, with_xq, half);
+  const EsShape shape = es_shape(ks, row_bytes, GATED, blocks, half);
   if (row_bytes % 16 == 0 && (reinterpret_cast<uintptr_t>(gate) & 15) == 0 &&
       (reinterpret_cast<uintptr_t>(up) & 15) == 0 && expert_bytes % 16 == 0 && rows > 0 &&
       slots > 0 && shape.stages >= 2 && (GATED || half) &&
