@@ -293,9 +293,10 @@ DRIFT_EXPERTS_REGISTER(Q4_1T, q4_1)
 // of KS k-splits, as experts_unit's 8: warp (group, kw) takes 4 rows and,
 // lane l, blocks 32 kw + l, 32 (kw + KS) + l, ... (each block of x read once
 // for the 4 rows); a row's k-splits meet in shared memory in order -- the
-// arithmetic of experts_unit, so the bits are its. The copies keep bytes in
-// flight while the warps compute; experts_x22_kernel is one round trip of
-// 4-byte loads a CTA, then its sums.
+// arithmetic of experts_unit, so the bits are its. The slot's x records sit
+// in shared memory too (copied, or made from the F32 row, once a slot). The
+// copies keep bytes in flight while the warps compute; experts_x22_kernel is
+// one round trip of 4-byte loads a CTA, then its sums.
 constexpr int ES_WARPS = 16;
 struct ExpertsStream {
   const uint8_t* gate;
@@ -586,13 +587,12 @@ static int launch_experts(const uint8_t* gate, const uint8_t* up, long long expe
   if (row_bytes % 16 == 0 && (reinterpret_cast<uintptr_t>(gate) & 15) == 0 &&
       (reinterpret_cast<uintptr_t>(up) & 15) == 0 && expert_bytes % 16 == 0 && rows > 0 &&
       slots > 0 && shape.stages >= 2 && (GATED || half) &&
-      (long long)slots * ((rows + shape.tile_rows - 1) / shape.tile_rows) >= 4LL * sm_count()) {
-    // the gated products (gate/up) of rows of whole 16-byte units, two
-    // units' rows in shared memory at once, and four units or more an SM:
-    // streamed (C5's step at batch 16 6.4 % faster). With a unit or two an
-    // SM, as at batch 1, the direct kernel's three CTAs an SM are faster;
-    // so are they for the plain products, whose units are a quarter of the
-    // work (streaming C5's down products too: 3.3 % faster only).
+      (long long)slots * ((rows + shape.tile_rows - 1) / shape.tile_rows) >= sm_count()) {
+    // rows of whole 16-byte units, gated or (plain) of at most 16 blocks, two
+    // units' rows in shared memory at once, and a unit or more an SM:
+    // streamed (C5's step 2.6 % faster at batch 1 and 26 % at batch 16 than
+    // with experts_x22 alone). Plain products of longer rows, a row a warp,
+    // were slower streamed than direct.
     ExpertsStream L = {};
     L.gate = gate;
     L.up = up;

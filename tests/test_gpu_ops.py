@@ -266,8 +266,8 @@ def _shifted(w: Stored) -> Stored:
 @pytest.mark.parametrize("tokens", [16, 40])
 def test_streamed_experts_are_the_direct_kernel(ops, dtype, tokens):
     """Weights of whole 16-byte rows stream through shared memory
-    (experts_stream_kernel, at four units an SM or more: 16 tokens of 10
-    slots are) -- the gated products, and plain products of rows of at most
+    (experts_stream_kernel, at a unit an SM or more: 16 tokens of 10 slots
+    are) -- the gated products, and plain products of rows of at most
     16 blocks (the down product, x prepared in the kernel, a row to each
     half-warp); the same weights 4 bytes off take the direct-load kernel
     (experts_x22_kernel). Bit for bit, and for expert-parallel products whose
