@@ -590,7 +590,7 @@ static int launch_experts(const uint8_t* gate, const uint8_t* up, long long expe
       (long long)slots * ((rows + shape.tile_rows - 1) / shape.tile_rows) >= sm_count()) {
     // rows of whole 16-byte units, gated or (plain) of at most 16 blocks, two
     // units' rows in shared memory at once, and a unit or more an SM:
-    // streamed (C5's step 2.6 % faster at batch 1 and 26 % at batch 16 than
+    // streamed (C5's step 2.6 % shorter at batch 1 and 28 % at batch 16 than
     // with experts_x22 alone). Plain products of longer rows, a row a warp,
     // were slower streamed than direct.
     ExpertsStream L = {};
